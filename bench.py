@@ -1,0 +1,353 @@
+"""Benchmark of the ternary hot path (one JSON line on stdout from rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (the metric's "ternary GEMV HBM GB/s"):
+dense ternary GEMV, x f32 [1, 2048] ~ N(0,1), W [5632, 2048] ternary with
+P(-1)=P(0)=P(+1)=1/3 packed in the reference's 2-bit layout, per-row scales
+~ U(0.01, 0.1).  One step = one GEMV y = scale * (W x) on one weight copy.
+The steps rotate over R distinct weight copies whose total size exceeds 2x
+the 126 MB L2, so every step streams its weights from HBM.  Inputs are made
+on the device from a seeded generator (synthetic data; no dataset exists for
+this path).
+
+value: algorithmic GB/s over all ranks = steps * ranks * 2,936,832 B / max
+over ranks of the device time of the K timed steps (CUDA events on the
+launching stream; launches replayed from CUDA graphs).
+
+Multi-GPU: the GEMV does not shard; each rank runs its own replica stream
+(weak scaling, no collective on the data path).  Rank 0 prints the line.
+
+--impl reference times the reference's CPU algorithm for the same workload:
+the C restatement of ternary_matmul_packed_parallel (src/model/ternary.rs:
+471-529) with per-row scales, on all host cores (the reference itself is Rust
+and cannot be built on this image; see oracle/).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+ROWS, COLS = 5632, 2048
+ALGO_BYTES = ROWS * COLS // 4 + ROWS * 4 + COLS * 4 + ROWS * 4  # W + scales + x + y
+METRIC = "ternary GEMV HBM GB/s"
+UNIT = "GB/s"
+L2_BYTES = 126 * 1024 * 1024
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def load_traffic():
+    p = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    try:
+        return json.load(open(p))
+    except Exception:
+        return {}
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks / throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "50", "-i", str(self.dev)], stdout=subprocess.PIPE,
+                stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        time.sleep(0.1)
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        sms, maxs, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sms.append(float(f[1]))
+                maxs.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() in ("active", "1"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sms) if sms else None,
+                "sm_max_mhz": max(maxs) if maxs else None, "reasons": sorted(reasons),
+                "samples": len(sms)}
+
+
+# ------------------------------------------------------------------ ours --
+def make_weights(gpu, torch, n_copies, device):
+    """n_copies ternary [ROWS, COLS] matrices with row scales, made on the device."""
+    weights = []
+    g = torch.Generator(device=device)
+    for i in range(n_copies):
+        g.manual_seed(i)
+        codes = torch.randint(0, 3, (ROWS * COLS,), generator=g, device=device, dtype=torch.int32)
+        c = codes.view(-1, 16)
+        shifts = torch.arange(0, 32, 2, device=device, dtype=torch.int64)
+        words = (c.to(torch.int64) << shifts).sum(dim=1)  # 16 codes per u32, LSB first
+        words = torch.where(words >= 2**31, words - 2**32, words).to(torch.int32).contiguous()
+        scales = (torch.rand(ROWS, generator=g, device=device) * 0.09 + 0.01).contiguous()
+        import ctypes as C
+        h = C.c_void_p()
+        ctx = gpu.get_context(device.index)
+        from ferrisres_b200._lib import call
+        call("ft_weight_from_device_u32", ctx.handle, C.c_void_p(words.data_ptr()), ROWS, COLS,
+             C.c_void_p(scales.data_ptr()), C.c_void_p(torch.cuda.current_stream().cuda_stream),
+             C.byref(h))
+        torch.cuda.synchronize()
+        weights.append(gpu.DeviceTernaryWeight(h, ROWS, COLS, ctx))
+        del codes, words
+    return weights
+
+
+def run_ours(args, ws, rank, local):
+    import torch
+    import torch.distributed as dist
+
+    from ferrisres_b200 import _lib, gpu
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if ws > 1 and not dist.is_initialized():
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+
+    n_copies = max(8, -(-2 * L2_BYTES // (ROWS * COLS // 4)))  # > 2x L2 of weights
+    weights = make_weights(gpu, torch, n_copies, device)
+    g = torch.Generator(device=device).manual_seed(1000 + rank)
+    x = torch.randn(1, COLS, generator=g, device=device)
+    ys = [torch.empty(1, ROWS, device=device) for _ in range(2)]
+
+    stream = torch.cuda.Stream(device=device)
+    # warm-up (also sizes the context workspace before capture)
+    with torch.cuda.stream(stream):
+        for i in range(max(args.warmup, 3)):
+            weights[i % n_copies].matmul_f32(x, out=ys[i & 1])
+    stream.synchronize()
+
+    def capture(nsteps, offset=0):
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(nsteps):
+                weights[(offset + i) % n_copies].matmul_f32(x, out=ys[i & 1])
+        return graph
+
+    launches0 = _lib.lib().ft_launch_counter()
+    g_full = capture(n_copies)
+    per_sweep = _lib.lib().ft_launch_counter() - launches0
+    full, rem = divmod(args.steps, n_copies)
+    launches0 = _lib.lib().ft_launch_counter()
+    g_rem = capture(rem) if rem else None
+    rem_launches = _lib.lib().ft_launch_counter() - launches0
+    gpu_launches = full * per_sweep + rem_launches
+
+    # graph warm-up
+    g_full.replay()
+    stream.synchronize()
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(full):
+        g_full.replay()
+    if g_rem is not None:
+        g_rem.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    if ws > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1)
+    t_max = torch.tensor([ms], device=device, dtype=torch.float64)
+    if ws > 1:
+        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+    ms = float(t_max.item())
+    sec = ms / 1e3
+    value = args.steps * ws * ALGO_BYTES / sec / 1e9
+
+    # isolated single launch (latency-bound), for context
+    iso = []
+    with torch.cuda.stream(stream):
+        for i in range(20):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            weights[i % n_copies].matmul_f32(x, out=ys[0])
+            b.record(stream)
+            b.synchronize()
+            iso.append(a.elapsed_time(b))
+
+    # end to end through the host-buffer accelerator call (pinned host memory)
+    import numpy as np
+    acc = gpu.GpuMatmulAccelerator(local)
+    xh = torch.empty(COLS, dtype=torch.float32, pin_memory=True)
+    xh.copy_(x.view(-1).cpu())
+    n_e2e = min(args.steps, 2000)
+    t0 = time.perf_counter()
+    for i in range(n_e2e):
+        acc.gpu_ternary_matmul_vram(weights[i % n_copies], xh.numpy(), 1, COLS, ROWS)
+    e2e_sec = time.perf_counter() - t0
+    e2e_local = torch.tensor([e2e_sec / n_e2e], device=device, dtype=torch.float64)
+    if ws > 1:
+        dist.all_reduce(e2e_local, op=dist.ReduceOp.MAX)
+    e2e_value = ws * ALGO_BYTES / float(e2e_local.item()) / 1e9
+
+    peak, peak_kind = load_peaks()
+    traffic = load_traffic().get("gemv_cfg0", {}).get("dram_bytes_per_launch")
+    result = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": ws,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded, generated on device)",
+        "config": {"workload": "cfg0 dense ternary GEMV x f32 [1,2048] . W [5632,2048]^T, "
+                               "per-row scales", "rows": ROWS, "cols": COLS, "seq": 1,
+                   "weight_copies": n_copies,
+                   "l2": f"weights rotate over {n_copies} copies "
+                         f"({n_copies * ROWS * COLS // 4 / 2**20:.0f} MiB > 2x L2)",
+                   "parallelism": f"replicas x{ws}", "graph": "CUDA graph replay"},
+        "roofline": {"bound": "hbm", "achieved": round(ALGO_BYTES / (sec / args.steps) / 1e9, 2),
+                     "peak": peak, "unit": "GB/s",
+                     "frac": round(ALGO_BYTES / (sec / args.steps) / 1e9 / peak, 4),
+                     "peak_source": peak_kind, "traffic": traffic,
+                     "algorithmic_bytes_per_launch": ALGO_BYTES,
+                     "note": "achieved = algorithmic bytes per step / per-step device time"},
+        "isolated_launch_us": round(statistics.median(iso) * 1e3, 2),
+        "e2e": {"value": round(e2e_value, 3), "unit": UNIT, "h2d_bytes_per_step": COLS * 4,
+                "d2h_bytes_per_step": ROWS * 4, "steps": n_e2e,
+                "api": "ft_gpu_ternary_matmul_vram (GpuMatmulAccelerator::gpu_ternary_matmul_vram)"},
+        "gpu_launches": int(gpu_launches),
+        "clocks": clocks,
+    }
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+    del g_full, g_rem
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return result
+
+
+# ------------------------------------------------------------- CPU side --
+def cpu_setup():
+    import numpy as np
+
+    from oracle import oracle as fo
+    rng = np.random.default_rng(0)
+    t = rng.integers(-1, 2, size=ROWS * COLS).astype(np.int8)
+    packed = fo.pack_ternary(t)
+    rs = rng.uniform(0.01, 0.1, ROWS).astype(np.float32)
+    x = rng.standard_normal(COLS).astype(np.float32)
+    return fo, packed, rs, x
+
+
+def cpu_baseline(seconds):
+    """Oracle restatement of ternary_matmul_packed_parallel timed on all host cores."""
+    fo, packed, rs, x = cpu_setup()
+    threads = fo.num_threads(0)
+    fo.ternary_matmul_packed_parallel_rows(packed, rs, x, ROWS, COLS, threads)  # warm
+    n, t0 = 0, time.perf_counter()
+    while True:
+        fo.ternary_matmul_packed_parallel_rows(packed, rs, x, ROWS, COLS, threads)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds and n >= 3:
+            break
+    return {"value": round(n * ALGO_BYTES / el / 1e9, 3), "unit": UNIT, "cores": threads,
+            "kind": "port",
+            "sample": f"{n} GEMVs [5632x2048] in {el:.1f} s (ternary_matmul_packed_parallel, "
+                      f"per-row scales, 32 row batches over {threads} threads)"}
+
+
+def run_reference(args, ws, rank):
+    if rank != 0:
+        return None
+    fo, packed, rs, x = cpu_setup()
+    threads = fo.num_threads(0)
+    for _ in range(args.warmup):
+        fo.ternary_matmul_packed_parallel_rows(packed, rs, x, ROWS, COLS, threads)
+    steps = args.steps if args.steps <= 2000 else 2000  # bounded sample
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        fo.ternary_matmul_packed_parallel_rows(packed, rs, x, ROWS, COLS, threads)
+    el = time.perf_counter() - t0
+    value = steps * ALGO_BYTES / el / 1e9
+    return {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT,
+        "n_gpus": ws, "steps": steps, "warmup": args.warmup, "ms_per_step": el * 1e3 / steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded)",
+        "config": {"workload": "cfg0 dense ternary GEMV x f32 [1,2048] . W [5632,2048]^T, "
+                               "per-row scales", "rows": ROWS, "cols": COLS, "seq": 1},
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{steps} GEMVs (requested {args.steps}); C restatement of "
+                                   "ternary_matmul_packed_parallel, src/model/ternary.rs:471-529"},
+        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--warmup", type=int, default=200)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    ws, rank, local = dist_env()
+    if args.gpus != ws and ws > 1:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE={ws}", file=sys.stderr)
+    if args.impl == "reference":
+        res = run_reference(args, ws, rank)
+    else:
+        res = run_ours(args, ws, rank, local)
+    if rank == 0 and res is not None:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,329 @@
+// C ABI of libferris_ternary.so: context, errors, weight upload and the
+// dense entry points.  Declarations and reference citations are in
+// include/ferris_ternary.h.
+#include <cstdlib>
+#include <cstring>
+#include <new>
+#include <vector>
+
+#include "ft_internal.cuh"
+
+namespace ft {
+
+static thread_local std::string g_last_error;
+std::atomic<uint64_t> g_launches{0};
+
+void set_error(const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+}
+
+int fail(int status, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return status;
+}
+
+int workspace_reserve(ft_ctx* ctx, size_t bytes, cudaStream_t stream) {
+  if (ctx->ws.bytes >= bytes) return FT_OK;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (stream != nullptr) cudaStreamIsCapturing(stream, &cs);
+  FT_CHECK(cs == cudaStreamCaptureStatusNone, FT_ERR_UNSUPPORTED,
+           "workspace must grow to %zu bytes but the stream is being captured; run the call "
+           "once before capture",
+           bytes);
+  // Growing frees the old buffer: wait for work that may still read it.
+  if (ctx->ws.ptr) {
+    FT_CUDA(cudaDeviceSynchronize());
+    FT_CUDA(cudaFree(ctx->ws.ptr));
+    ctx->ws.ptr = nullptr;
+    ctx->ws.bytes = 0;
+  }
+  size_t grow = bytes + bytes / 4 + (1 << 20);
+  FT_CUDA(cudaMalloc(&ctx->ws.ptr, grow));
+  ctx->ws.bytes = grow;
+  return FT_OK;
+}
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+static int alloc_weight(ft_ctx* ctx, int64_t rows, int64_t cols, ft_weight** out) {
+  FT_CHECK(ctx && out, FT_ERR_SHAPE, "null argument");
+  FT_CHECK(rows > 0 && cols > 0, FT_ERR_SHAPE, "weight shape [%lld, %lld] must be positive",
+           (long long)rows, (long long)cols);
+  ft_weight* w = new (std::nothrow) ft_weight();
+  FT_CHECK(w, FT_ERR_OOM, "host allocation failed");
+  w->device = ctx->device;
+  w->rows = rows;
+  w->cols = cols;
+  w->n_tiles = ceil_div(rows, kTileRows);
+  w->n_chunks = ceil_div(cols, kChunkK);
+  size_t code_bytes = (size_t)(w->n_tiles * w->n_chunks) * kBlockBytes;
+  size_t scale_bytes = (size_t)(w->n_tiles * kTileRows) * sizeof(float);
+  cudaError_t e = cudaMalloc(&w->codes, code_bytes);
+  if (e == cudaSuccess) e = cudaMalloc(&w->row_scales, scale_bytes);
+  if (e != cudaSuccess) {
+    if (w->codes) cudaFree(w->codes);
+    delete w;
+    return fail(e == cudaErrorMemoryAllocation ? FT_ERR_OOM : FT_ERR_GPU,
+                "weight allocation (%zu bytes) failed: %s", code_bytes + scale_bytes,
+                cudaGetErrorString(e));
+  }
+  *out = w;
+  return FT_OK;
+}
+
+static int finish_scales(ft_weight* w, const float* scales, bool host, cudaStream_t s) {
+  size_t scale_bytes = (size_t)(w->n_tiles * kTileRows) * sizeof(float);
+  FT_CUDA(cudaMemsetAsync(w->row_scales, 0, scale_bytes, s));
+  FT_CUDA(cudaMemcpyAsync(w->row_scales, scales, (size_t)w->rows * sizeof(float),
+                          host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice, s));
+  return FT_OK;
+}
+
+}  // namespace ft
+
+using namespace ft;
+
+extern "C" {
+
+const char* ft_version(void) { return "ferris-ternary-b200 0.1.0 (sm_100a)"; }
+
+const char* ft_last_error_string(void) { return g_last_error.c_str(); }
+
+uint64_t ft_launch_counter(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int ft_ctx_create(int device, ft_ctx** out) {
+  FT_CHECK(out, FT_ERR_SHAPE, "null out pointer");
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  FT_CHECK(e == cudaSuccess && n > 0, FT_ERR_DEVICE, "no CUDA device available (%s)",
+           cudaGetErrorString(e));
+  FT_CHECK(device >= 0 && device < n, FT_ERR_DEVICE, "device %d out of range [0, %d)", device, n);
+  cudaDeviceProp prop;
+  FT_CUDA(cudaGetDeviceProperties(&prop, device));
+  FT_CHECK(prop.major == 10 && prop.minor == 0, FT_ERR_UNSUPPORTED,
+           "device %d is sm_%d%d; this library is built for sm_100a (B200)", device, prop.major,
+           prop.minor);
+  DeviceGuard g(device);
+  ft_ctx* c = new (std::nothrow) ft_ctx();
+  FT_CHECK(c, FT_ERR_OOM, "host allocation failed");
+  c->device = device;
+  c->num_sms = prop.multiProcessorCount;
+  cudaError_t se = cudaStreamCreateWithFlags(&c->host_stream, cudaStreamNonBlocking);
+  if (se != cudaSuccess) {
+    delete c;
+    return fail(FT_ERR_GPU, "stream creation failed: %s", cudaGetErrorString(se));
+  }
+  *out = c;
+  return FT_OK;
+}
+
+int ft_ctx_destroy(ft_ctx* ctx) {
+  if (!ctx) return FT_OK;
+  DeviceGuard g(ctx->device);
+  cudaDeviceSynchronize();
+  if (ctx->ws.ptr) cudaFree(ctx->ws.ptr);
+  if (ctx->host_stream) cudaStreamDestroy(ctx->host_stream);
+  delete ctx;
+  return FT_OK;
+}
+
+int ft_weight_upload_packed_u8(ft_ctx* ctx, const uint8_t* packed_host, int64_t rows,
+                               int64_t cols, const float* row_scales_host, ft_weight** out) {
+  FT_CHECK(packed_host && row_scales_host, FT_ERR_SHAPE, "null host buffer");
+  DeviceGuard g(ctx ? ctx->device : 0);
+  ft_weight* w = nullptr;
+  int st = alloc_weight(ctx, rows, cols, &w);
+  if (st != FT_OK) return st;
+  size_t nbytes = (size_t)((rows * cols + 3) / 4);
+  uint8_t* staging = nullptr;
+  cudaStream_t s = ctx->host_stream;
+  cudaError_t e = cudaMalloc(&staging, nbytes);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(staging, packed_host, nbytes, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess) st = launch_repack_u8(staging, rows, cols, w, s);
+  if (e == cudaSuccess && st == FT_OK) st = finish_scales(w, row_scales_host, true, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (staging) cudaFree(staging);
+  if (e != cudaSuccess || st != FT_OK) {
+    ft_weight_destroy(w);
+    if (e != cudaSuccess) return fail(FT_ERR_GPU, "weight upload failed: %s", cudaGetErrorString(e));
+    return st;
+  }
+  *out = w;
+  return FT_OK;
+}
+
+int ft_weight_upload_packed_u32(ft_ctx* ctx, const uint32_t* words_host, int64_t rows,
+                                int64_t cols, const float* row_scales_host, ft_weight** out) {
+  FT_CHECK(words_host && row_scales_host, FT_ERR_SHAPE, "null host buffer");
+  DeviceGuard g(ctx ? ctx->device : 0);
+  ft_weight* w = nullptr;
+  int st = alloc_weight(ctx, rows, cols, &w);
+  if (st != FT_OK) return st;
+  size_t nbytes = (size_t)rows * (size_t)ceil_div(cols, 16) * 4;
+  uint32_t* staging = nullptr;
+  cudaStream_t s = ctx->host_stream;
+  cudaError_t e = cudaMalloc(&staging, nbytes);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(staging, words_host, nbytes, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess) st = launch_repack_u32(staging, rows, cols, w, s);
+  if (e == cudaSuccess && st == FT_OK) st = finish_scales(w, row_scales_host, true, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (staging) cudaFree(staging);
+  if (e != cudaSuccess || st != FT_OK) {
+    ft_weight_destroy(w);
+    if (e != cudaSuccess) return fail(FT_ERR_GPU, "weight upload failed: %s", cudaGetErrorString(e));
+    return st;
+  }
+  *out = w;
+  return FT_OK;
+}
+
+int ft_weight_from_device_u32(ft_ctx* ctx, const uint32_t* words_dev, int64_t rows, int64_t cols,
+                              const float* row_scales_dev, void* stream, ft_weight** out) {
+  FT_CHECK(words_dev && row_scales_dev, FT_ERR_SHAPE, "null device buffer");
+  DeviceGuard g(ctx ? ctx->device : 0);
+  ft_weight* w = nullptr;
+  int st = alloc_weight(ctx, rows, cols, &w);
+  if (st != FT_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  st = launch_repack_u32(words_dev, rows, cols, w, s);
+  if (st == FT_OK) st = finish_scales(w, row_scales_dev, false, s);
+  if (st != FT_OK) {
+    cudaStreamSynchronize(s);
+    ft_weight_destroy(w);
+    return st;
+  }
+  *out = w;
+  return FT_OK;
+}
+
+int ft_weight_destroy(ft_weight* w) {
+  if (!w) return FT_OK;
+  DeviceGuard g(w->device);
+  if (w->codes) cudaFree(w->codes);
+  if (w->row_scales) cudaFree(w->row_scales);
+  delete w;
+  return FT_OK;
+}
+
+int ft_weight_info(const ft_weight* w, int64_t* rows, int64_t* cols, int64_t* device_bytes) {
+  FT_CHECK(w, FT_ERR_SHAPE, "null weight");
+  if (rows) *rows = w->rows;
+  if (cols) *cols = w->cols;
+  if (device_bytes) *device_bytes = w->n_tiles * w->n_chunks * kBlockBytes + w->n_tiles * kTileRows * 4;
+  return FT_OK;
+}
+
+int ft_ternary_matmul_f32(ft_ctx* ctx, const ft_weight* w, int64_t seq, const float* x_dev,
+                          float* y_dev, void* stream) {
+  FT_CHECK(ctx && w, FT_ERR_SHAPE, "null context or weight");
+  FT_CHECK(seq >= 0, FT_ERR_SHAPE, "seq must be >= 0");
+  FT_CHECK(seq == 0 || (x_dev && y_dev), FT_ERR_SHAPE, "null activation/output pointer");
+  FT_CHECK(w->device == ctx->device, FT_ERR_DEVICE, "weight lives on device %d, context on %d",
+           w->device, ctx->device);
+  DeviceGuard g(ctx->device);
+  return launch_dense_f32(ctx, w, seq, x_dev, y_dev, static_cast<cudaStream_t>(stream));
+}
+
+int ft_quantize_absmax_i8_f32(ft_ctx* ctx, int64_t seq, int64_t cols, const float* x_dev,
+                              int8_t* q_dev, float* sx_dev, void* stream) {
+  FT_CHECK(ctx, FT_ERR_SHAPE, "null context");
+  FT_CHECK(seq >= 0 && cols > 0, FT_ERR_SHAPE, "bad shape [%lld, %lld]", (long long)seq,
+           (long long)cols);
+  DeviceGuard g(ctx->device);
+  return launch_quantize_i8(x_dev, false, seq, cols, q_dev, sx_dev, static_cast<cudaStream_t>(stream));
+}
+
+int ft_quantize_absmax_i8_bf16(ft_ctx* ctx, int64_t seq, int64_t cols, const uint16_t* x_dev,
+                               int8_t* q_dev, float* sx_dev, void* stream) {
+  FT_CHECK(ctx, FT_ERR_SHAPE, "null context");
+  FT_CHECK(seq >= 0 && cols > 0, FT_ERR_SHAPE, "bad shape [%lld, %lld]", (long long)seq,
+           (long long)cols);
+  DeviceGuard g(ctx->device);
+  return launch_quantize_i8(x_dev, true, seq, cols, q_dev, sx_dev, static_cast<cudaStream_t>(stream));
+}
+
+int ft_ternary_matmul_i8(ft_ctx* ctx, const ft_weight* w, int64_t seq, const int8_t* q_dev,
+                         const float* sx_dev, float* y_dev, void* stream) {
+  FT_CHECK(ctx && w, FT_ERR_SHAPE, "null context or weight");
+  FT_CHECK(seq >= 0, FT_ERR_SHAPE, "seq must be >= 0");
+  FT_CHECK(seq == 0 || (q_dev && sx_dev && y_dev), FT_ERR_SHAPE, "null activation/output pointer");
+  FT_CHECK(w->device == ctx->device, FT_ERR_DEVICE, "weight lives on device %d, context on %d",
+           w->device, ctx->device);
+  DeviceGuard g(ctx->device);
+  return launch_dense_i8(ctx, w, seq, q_dev, sx_dev, y_dev, static_cast<cudaStream_t>(stream));
+}
+
+int ft_ternary_matmul_op_dispatch(ft_ctx* ctx, const uint32_t* ternary_dev,
+                                  const float* scales_dev, const float* input_dev,
+                                  float* output_dev, uint32_t seq_len, uint32_t in_cols,
+                                  uint32_t out_rows, void* stream) {
+  FT_CHECK(ctx, FT_ERR_SHAPE, "null context");
+  FT_CHECK(ternary_dev && scales_dev && input_dev && output_dev, FT_ERR_SHAPE, "null buffer");
+  DeviceGuard g(ctx->device);
+  return launch_wgsl_op(ternary_dev, scales_dev, input_dev, output_dev, seq_len, in_cols, out_rows,
+                        static_cast<cudaStream_t>(stream));
+}
+
+int ft_gpu_ternary_matmul(ft_ctx* ctx, const uint32_t* packed_weights_host,
+                          const float* scales_host, const float* input_host, size_t seq_len,
+                          size_t in_cols, size_t out_rows, float* output_host) {
+  FT_CHECK(ctx, FT_ERR_SHAPE, "null context");
+  FT_CHECK(packed_weights_host && scales_host && input_host && output_host, FT_ERR_SHAPE,
+           "null host buffer");
+  if (seq_len == 0 || out_rows == 0) return FT_OK;
+  ft_weight* w = nullptr;
+  int st = ft_weight_upload_packed_u32(ctx, packed_weights_host, (int64_t)out_rows,
+                                       (int64_t)in_cols, scales_host, &w);
+  if (st != FT_OK) return st;
+  st = ft_gpu_ternary_matmul_vram(ctx, w, input_host, seq_len, output_host);
+  ft_weight_destroy(w);
+  return st;
+}
+
+int ft_gpu_ternary_matmul_vram(ft_ctx* ctx, const ft_weight* w, const float* input_host,
+                               size_t seq_len, float* output_host) {
+  FT_CHECK(ctx && w, FT_ERR_SHAPE, "null context or weight");
+  FT_CHECK(input_host && output_host, FT_ERR_SHAPE, "null host buffer");
+  if (seq_len == 0) return FT_OK;
+  DeviceGuard g(ctx->device);
+  cudaStream_t s = ctx->host_stream;
+  size_t in_bytes = seq_len * (size_t)w->cols * sizeof(float);
+  size_t out_bytes = seq_len * (size_t)w->rows * sizeof(float);
+  float* dx = nullptr;
+  float* dy = nullptr;
+  FT_CUDA(cudaMallocAsync(&dx, in_bytes, s));
+  cudaError_t e = cudaMallocAsync(&dy, out_bytes, s);
+  int st = FT_OK;
+  if (e == cudaSuccess) e = cudaMemcpyAsync(dx, input_host, in_bytes, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess) st = launch_dense_f32(ctx, w, (int64_t)seq_len, dx, dy, s);
+  if (e == cudaSuccess && st == FT_OK)
+    e = cudaMemcpyAsync(output_host, dy, out_bytes, cudaMemcpyDeviceToHost, s);
+  if (dx) cudaFreeAsync(dx, s);
+  if (dy) cudaFreeAsync(dy, s);
+  cudaError_t e2 = cudaStreamSynchronize(s);
+  if (e == cudaSuccess) e = e2;
+  if (e != cudaSuccess) return fail(FT_ERR_GPU, "gpu_ternary_matmul_vram failed: %s", cudaGetErrorString(e));
+  return st;
+}
+
+}  // extern "C"

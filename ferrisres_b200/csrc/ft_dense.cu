@@ -1,0 +1,377 @@
+// Dense ternary kernels on CUDA cores: weight repack, int8 quantizer, the
+// split-K fp32 / int8 matmuls over the tiled T128 layout, and the raw
+// WGSL-layout op.  The tensor-core (tcgen05) path lives in ft_tc.cu.
+#include "ft_internal.cuh"
+
+namespace ft {
+namespace {
+
+// ---------------------------------------------------------------- repack --
+// One thread per output u32 word of the tiled layout (see ft_internal.cuh).
+template <bool kU32Src>
+__global__ void repack_kernel(const void* __restrict__ src, int64_t rows, int64_t cols,
+                              int64_t n_chunks, int64_t total_words, uint32_t* __restrict__ dst) {
+  int64_t gw = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (gw >= total_words) return;
+  int64_t block = gw >> 10;  // 1024 words per 4096-byte block
+  int within = (int)(gw & 1023);
+  int half = within >> 9;
+  int rem = within & 511;
+  int row = rem >> 2, w = rem & 3;
+  int64_t tile = block / n_chunks, chunk = block % n_chunks;
+  int64_t R = tile * kTileRows + row;
+  int64_t base = chunk * kChunkK + half * 64 + w * 16;
+  uint32_t out = 0;
+  int64_t cp = (cols + 15) >> 4;
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      int64_t k = base + 4 * q + b;
+      uint32_t code = 1u;
+      if (R < rows && k < cols) {
+        if (kU32Src) {
+          uint32_t word = static_cast<const uint32_t*>(src)[R * cp + (k >> 4)];
+          code = (word >> ((k & 15) * 2)) & 3u;
+        } else {
+          int64_t idx = R * cols + k;  // flat pack_ternary stream
+          uint8_t byte = static_cast<const uint8_t*>(src)[idx >> 2];
+          code = (byte >> ((idx & 3) * 2)) & 3u;
+        }
+        if (code == 3u) code = 1u;  // 0b11 decodes to 0 in the reference
+      }
+      out |= code << (8 * b + 2 * q);
+    }
+  dst[gw] = out;
+}
+
+// ------------------------------------------------------------- quantizer --
+__device__ __forceinline__ float load_act(const void* x, bool bf16, int64_t i) {
+  if (bf16) {
+    uint32_t b = static_cast<const uint16_t*>(x)[i];
+    return __uint_as_float(b << 16);
+  }
+  return static_cast<const float*>(x)[i];
+}
+
+__global__ void quantize_i8_kernel(const void* __restrict__ x, bool bf16, int64_t cols,
+                                   int8_t* __restrict__ q, float* __restrict__ sx) {
+  int64_t s = blockIdx.x;
+  const int64_t off = s * cols;
+  float amax = 0.0f;
+  for (int64_t j = threadIdx.x; j < cols; j += blockDim.x) amax = fmaxf(amax, fabsf(load_act(x, bf16, off + j)));
+  __shared__ float red[32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  amax = red[0];
+  if (amax == 0.0f) {
+    for (int64_t j = threadIdx.x; j < cols; j += blockDim.x) q[off + j] = 0;
+    if (threadIdx.x == 0) sx[s] = 1.0f;
+    return;
+  }
+  const float inv = 127.0f / amax;  // IEEE division (no fast-math in this build)
+  for (int64_t j = threadIdx.x; j < cols; j += blockDim.x) {
+    float r = roundf(__fmul_rn(load_act(x, bf16, off + j), inv));
+    r = fminf(fmaxf(r, -127.0f), 127.0f);
+    q[off + j] = (int8_t)(int)r;
+  }
+  if (threadIdx.x == 0) sx[s] = __fdiv_rn(amax, 127.0f);
+}
+
+// ------------------------------------------------- split-K CUDA-core GEMM --
+// grid (n_tiles, ksplit, ceil(seq/TOK)); 128 threads, thread = row of tile.
+// Each CTA covers chunks [c0, c1) and TOK tokens; partial sums go to
+// part[ks][s][row] (or straight to y when ksplit == 1).
+constexpr int kTok = 4;
+
+template <int TOK>
+__global__ void __launch_bounds__(128) dense_f32_kernel(
+    const uint8_t* __restrict__ codes, const float* __restrict__ rscale, int64_t rows,
+    int64_t cols, int64_t n_chunks, int chunks_per_split, int64_t seq,
+    const float* __restrict__ x, float* __restrict__ out, int64_t rows_pad, bool direct) {
+  __shared__ float xs[TOK][kChunkK];
+  const int r = threadIdx.x;
+  const int64_t tile = blockIdx.x;
+  const int ks = blockIdx.y;
+  const int64_t s0 = (int64_t)blockIdx.z * TOK;
+  const int64_t c0 = (int64_t)ks * chunks_per_split;
+  int64_t c1 = c0 + chunks_per_split;
+  if (c1 > n_chunks) c1 = n_chunks;
+  float acc[TOK];
+#pragma unroll
+  for (int t = 0; t < TOK; ++t) acc[t] = 0.0f;
+  for (int64_t c = c0; c < c1; ++c) {
+    __syncthreads();
+#pragma unroll
+    for (int t = 0; t < TOK; ++t) {
+      int64_t s = s0 + t, k = c * kChunkK + r;
+      xs[t][r] = (s < seq && k < cols) ? x[s * cols + k] : 0.0f;
+    }
+    __syncthreads();
+    const uint8_t* blk = codes + (tile * n_chunks + c) * kBlockBytes;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint4 v = *reinterpret_cast<const uint4*>(blk + h * 2048 + r * 16);
+      uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint32_t u = (wv[w] >> (2 * q)) & 0x03030303u;
+#pragma unroll
+          for (int b = 0; b < 4; ++b) {
+            float wt = (float)((u >> (8 * b)) & 0xFFu) - 1.0f;
+            int kk = h * 64 + w * 16 + 4 * q + b;
+#pragma unroll
+            for (int t = 0; t < TOK; ++t) acc[t] = fmaf(wt, xs[t][kk], acc[t]);
+          }
+        }
+      }
+    }
+  }
+  const int64_t R = tile * kTileRows + r;
+#pragma unroll
+  for (int t = 0; t < TOK; ++t) {
+    int64_t s = s0 + t;
+    if (s >= seq) break;
+    if (direct) {
+      if (R < rows) out[s * rows + R] = acc[t] * rscale[R];
+    } else {
+      out[((int64_t)ks * seq + s) * rows_pad + R] = acc[t];
+    }
+  }
+}
+
+__global__ void reduce_f32_kernel(const float* __restrict__ part, int ksplit, int64_t seq,
+                                  int64_t rows, int64_t rows_pad, const float* __restrict__ rscale,
+                                  float* __restrict__ y) {
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= seq * rows) return;
+  int64_t s = i / rows, R = i % rows;
+  float a = 0.0f;
+  for (int k = 0; k < ksplit; ++k) a += part[((int64_t)k * seq + s) * rows_pad + R];
+  y[i] = a * rscale[R];
+}
+
+// int8 activations: unsigned codes u = w+1 dotted with signed q by dp4a, the
+// chunk's sum of q subtracted once, so the int32 result is exact.
+template <int TOK>
+__global__ void __launch_bounds__(128) dense_i8_kernel(
+    const uint8_t* __restrict__ codes, int64_t rows, int64_t cols, int64_t n_chunks,
+    int chunks_per_split, int64_t seq, const int8_t* __restrict__ q, int32_t* __restrict__ part,
+    int64_t rows_pad) {
+  __shared__ int32_t qs[TOK][kChunkK / 4];
+  __shared__ int32_t qsum[TOK];
+  const int r = threadIdx.x;
+  const int64_t tile = blockIdx.x;
+  const int ks = blockIdx.y;
+  const int64_t s0 = (int64_t)blockIdx.z * TOK;
+  const int64_t c0 = (int64_t)ks * chunks_per_split;
+  int64_t c1 = c0 + chunks_per_split;
+  if (c1 > n_chunks) c1 = n_chunks;
+  int32_t acc[TOK];
+#pragma unroll
+  for (int t = 0; t < TOK; ++t) acc[t] = 0;
+  for (int64_t c = c0; c < c1; ++c) {
+    __syncthreads();
+    if (r < 32) {
+#pragma unroll
+      for (int t = 0; t < TOK; ++t) {
+        int64_t s = s0 + t;
+        uint32_t word = 0;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          int64_t k = c * kChunkK + r * 4 + b;
+          uint32_t v = (s < seq && k < cols) ? (uint8_t)q[s * cols + k] : 0u;
+          word |= v << (8 * b);
+        }
+        qs[t][r] = (int32_t)word;
+        int sum = __dp4a((int)word, 0x01010101, 0);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if (r == 0) qsum[t] = sum;
+      }
+    }
+    __syncthreads();
+    const uint8_t* blk = codes + (tile * n_chunks + c) * kBlockBytes;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint4 v = *reinterpret_cast<const uint4*>(blk + h * 2048 + r * 16);
+      uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int w = 0; w < 4; ++w)
+#pragma unroll
+        for (int qq = 0; qq < 4; ++qq) {
+          int u = (int)((wv[w] >> (2 * qq)) & 0x03030303u);
+          int widx = h * 16 + w * 4 + qq;
+#pragma unroll
+          for (int t = 0; t < TOK; ++t) acc[t] = __dp4a(u, qs[t][widx], acc[t]);
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < TOK; ++t) acc[t] -= qsum[t];
+  }
+  const int64_t R = tile * kTileRows + r;
+#pragma unroll
+  for (int t = 0; t < TOK; ++t) {
+    int64_t s = s0 + t;
+    if (s >= seq) break;
+    part[((int64_t)ks * seq + s) * rows_pad + R] = acc[t];
+  }
+}
+
+__global__ void reduce_i8_kernel(const int32_t* __restrict__ part, int ksplit, int64_t seq,
+                                 int64_t rows, int64_t rows_pad, const float* __restrict__ sx,
+                                 const float* __restrict__ rscale, float* __restrict__ y) {
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= seq * rows) return;
+  int64_t s = i / rows, R = i % rows;
+  int32_t a = 0;
+  for (int k = 0; k < ksplit; ++k) a += part[((int64_t)k * seq + s) * rows_pad + R];
+  y[i] = __fmul_rn(__fmul_rn((float)a, sx[s]), rscale[R]);
+}
+
+// ------------------------------------------------------------ WGSL op ------
+// One warp per (token, row) over the raw u32 layout; lanes take words
+// round-robin, then a shuffle reduction; result * scales[row].
+__global__ void wgsl_op_kernel(const uint32_t* __restrict__ words, const float* __restrict__ scales,
+                               const float* __restrict__ x, float* __restrict__ y, uint32_t seq,
+                               uint32_t in_cols, uint32_t out_rows) {
+  int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  int lane = threadIdx.x & 31;
+  if (warp >= (int64_t)seq * out_rows) return;
+  uint32_t s = (uint32_t)(warp / out_rows), row = (uint32_t)(warp % out_rows);
+  uint32_t cp = (in_cols + 15) / 16;
+  const uint32_t* wr = words + (int64_t)row * cp;
+  const float* xr = x + (int64_t)s * in_cols;
+  float sum = 0.0f;
+  for (uint32_t p = lane; p < cp; p += 32) {
+    uint32_t word = wr[p];
+#pragma unroll
+    for (uint32_t b = 0; b < 16; ++b) {
+      uint32_t col = p * 16 + b;
+      if (col >= in_cols) break;
+      uint32_t code = (word >> (b * 2)) & 3u;
+      float v = xr[col];
+      if (code == 0u) sum -= v;
+      else if (code == 2u) sum += v;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  if (lane == 0) y[(int64_t)s * out_rows + row] = sum * scales[row];
+}
+
+int pick_ksplit(const ft_ctx* ctx, const ft_weight* w, int64_t token_groups) {
+  int64_t ctas = w->n_tiles * token_groups;
+  int64_t target = (int64_t)ctx->num_sms * 8;
+  int64_t ks = (target + ctas - 1) / ctas;
+  if (ks > w->n_chunks) ks = w->n_chunks;
+  if (ks < 1) ks = 1;
+  return (int)ks;
+}
+
+}  // namespace
+
+int launch_repack_u8(const uint8_t* packed, int64_t rows, int64_t cols, ft_weight* w,
+                     cudaStream_t s) {
+  int64_t total = w->n_tiles * w->n_chunks * (kBlockBytes / 4);
+  repack_kernel<false><<<(unsigned)ceil_div(total, 256), 256, 0, s>>>(
+      packed, rows, cols, w->n_chunks, total, reinterpret_cast<uint32_t*>(w->codes));
+  FT_LAUNCH_CHECK();
+  return FT_OK;
+}
+
+int launch_repack_u32(const uint32_t* words, int64_t rows, int64_t cols, ft_weight* w,
+                      cudaStream_t s) {
+  int64_t total = w->n_tiles * w->n_chunks * (kBlockBytes / 4);
+  repack_kernel<true><<<(unsigned)ceil_div(total, 256), 256, 0, s>>>(
+      words, rows, cols, w->n_chunks, total, reinterpret_cast<uint32_t*>(w->codes));
+  FT_LAUNCH_CHECK();
+  return FT_OK;
+}
+
+int launch_quantize_i8(const void* x, bool bf16, int64_t seq, int64_t cols, int8_t* q, float* sx,
+                       cudaStream_t s) {
+  if (seq == 0) return FT_OK;
+  quantize_i8_kernel<<<(unsigned)seq, 256, 0, s>>>(x, bf16, cols, q, sx);
+  FT_LAUNCH_CHECK();
+  return FT_OK;
+}
+
+int launch_dense_f32(ft_ctx* ctx, const ft_weight* w, int64_t seq, const float* x, float* y,
+                     cudaStream_t s) {
+  if (seq == 0) return FT_OK;
+  int64_t groups = ceil_div(seq, kTok);
+  FT_CHECK(groups <= 65535, FT_ERR_UNSUPPORTED, "seq %lld too large for the CUDA-core path",
+           (long long)seq);
+  int ks = pick_ksplit(ctx, w, groups);
+  int cps = (int)ceil_div(w->n_chunks, ks);
+  ks = (int)ceil_div(w->n_chunks, cps);
+  int64_t rows_pad = w->n_tiles * kTileRows;
+  dim3 grid((unsigned)w->n_tiles, (unsigned)ks, (unsigned)groups);
+  if (ks == 1) {
+    dense_f32_kernel<kTok><<<grid, 128, 0, s>>>(w->codes, w->row_scales, w->rows, w->cols,
+                                                w->n_chunks, cps, seq, x, y, rows_pad, true);
+    FT_LAUNCH_CHECK();
+    return FT_OK;
+  }
+  size_t need = (size_t)ks * seq * rows_pad * sizeof(float);
+  int st = workspace_reserve(ctx, need, s);
+  if (st != FT_OK) return st;
+  float* part = static_cast<float*>(ctx->ws.ptr);
+  dense_f32_kernel<kTok><<<grid, 128, 0, s>>>(w->codes, w->row_scales, w->rows, w->cols,
+                                              w->n_chunks, cps, seq, x, part, rows_pad, false);
+  FT_LAUNCH_CHECK();
+  int64_t n = seq * w->rows;
+  reduce_f32_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(part, ks, seq, w->rows, rows_pad,
+                                                               w->row_scales, y);
+  FT_LAUNCH_CHECK();
+  return FT_OK;
+}
+
+int launch_dense_i8(ft_ctx* ctx, const ft_weight* w, int64_t seq, const int8_t* q,
+                    const float* sx, float* y, cudaStream_t s) {
+  if (seq == 0) return FT_OK;
+  int64_t groups = ceil_div(seq, kTok);
+  FT_CHECK(groups <= 65535, FT_ERR_UNSUPPORTED, "seq %lld too large for the CUDA-core path",
+           (long long)seq);
+  int ks = pick_ksplit(ctx, w, groups);
+  int cps = (int)ceil_div(w->n_chunks, ks);
+  ks = (int)ceil_div(w->n_chunks, cps);
+  int64_t rows_pad = w->n_tiles * kTileRows;
+  size_t need = (size_t)ks * seq * rows_pad * sizeof(int32_t);
+  int st = workspace_reserve(ctx, need, s);
+  if (st != FT_OK) return st;
+  int32_t* part = static_cast<int32_t*>(ctx->ws.ptr);
+  dim3 grid((unsigned)w->n_tiles, (unsigned)ks, (unsigned)groups);
+  dense_i8_kernel<kTok><<<grid, 128, 0, s>>>(w->codes, w->rows, w->cols, w->n_chunks, cps, seq, q,
+                                             part, rows_pad);
+  FT_LAUNCH_CHECK();
+  int64_t n = seq * w->rows;
+  reduce_i8_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(part, ks, seq, w->rows, rows_pad, sx,
+                                                              w->row_scales, y);
+  FT_LAUNCH_CHECK();
+  return FT_OK;
+}
+
+int launch_wgsl_op(const uint32_t* words, const float* scales, const float* x, float* y,
+                   uint32_t seq, uint32_t in_cols, uint32_t out_rows, cudaStream_t s) {
+  int64_t warps = (int64_t)seq * out_rows;
+  if (warps == 0) return FT_OK;
+  wgsl_op_kernel<<<(unsigned)ceil_div(warps * 32, 256), 256, 0, s>>>(words, scales, x, y, seq,
+                                                                    in_cols, out_rows);
+  FT_LAUNCH_CHECK();
+  return FT_OK;
+}
+
+}  // namespace ft

@@ -1,0 +1,107 @@
+// Internal definitions shared by the translation units of libferris_ternary.so.
+//
+// Device layout of a dense ternary weight ("tiled T128"):
+//   rows are grouped into tiles of 128 output channels, K into chunks of 128
+//   codes.  Block (tile t, chunk c) is 4096 contiguous bytes at offset
+//   (t * n_chunks + c) * 4096:
+//       [half h in 0..1][row r in 0..127][16 bytes]
+//   The 16 bytes of (h, r) are four u32 words w = 0..3; word w holds the 16
+//   codes of K positions base + 0..15, base = c*128 + h*64 + w*16, arranged so
+//   that byte b, bits 2q..2q+1 hold the code of K position base + 4q + b.
+//   Shifting a word right by 2q and masking with 0x03030303 therefore yields
+//   four unsigned bytes {0,1,2} = (w+1) for K positions base+4q .. base+4q+3,
+//   in K order: the int8 operand the tensor-core path stores in TMEM.
+//   Codes: 0 -> -1, 1 -> 0, 2 -> +1 (same as the reference).  Padding rows and
+//   padding K positions hold code 1 (weight 0).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "../../include/ferris_ternary.h"
+
+namespace ft {
+
+constexpr int kTileRows = 128;  // output channels per tile
+constexpr int kChunkK = 128;    // K codes per chunk
+constexpr int kBlockBytes = kTileRows * kChunkK / 4;  // 4096
+
+void set_error(const char* fmt, ...);
+extern std::atomic<uint64_t> g_launches;  // kernels launched by this library
+int fail(int status, const char* fmt, ...);
+
+#define FT_CUDA(call)                                                                    \
+  do {                                                                                   \
+    cudaError_t e_ = (call);                                                             \
+    if (e_ != cudaSuccess)                                                               \
+      return ::ft::fail(e_ == cudaErrorMemoryAllocation ? FT_ERR_OOM : FT_ERR_GPU,       \
+                        "%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_), __FILE__, \
+                        __LINE__);                                                       \
+  } while (0)
+
+#define FT_CHECK(cond, status, ...)                 \
+  do {                                              \
+    if (!(cond)) return ::ft::fail(status, __VA_ARGS__); \
+  } while (0)
+
+// Kernel launch check: reports launch-configuration errors without syncing,
+// and counts the launch.
+#define FT_LAUNCH_CHECK()                                                                  \
+  do {                                                                                     \
+    ::ft::g_launches.fetch_add(1, std::memory_order_relaxed);                              \
+    cudaError_t e_ = cudaGetLastError();                                                   \
+    if (e_ != cudaSuccess)                                                                 \
+      return ::ft::fail(FT_ERR_GPU, "kernel launch failed: %s (%s:%d)",                    \
+                        cudaGetErrorString(e_), __FILE__, __LINE__);                        \
+  } while (0)
+
+inline int64_t round_up(int64_t a, int64_t b) { return (a + b - 1) / b * b; }
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// Per-context device workspace (grown on demand, freed with the context).
+struct Workspace {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+};
+
+}  // namespace ft
+
+struct ft_ctx {
+  int device = 0;
+  int num_sms = 0;
+  ft::Workspace ws;
+  cudaStream_t host_stream = nullptr;  // used by the synchronous host-buffer calls
+};
+
+struct ft_weight {
+  int device = 0;
+  int64_t rows = 0, cols = 0;
+  int64_t n_tiles = 0, n_chunks = 0;
+  uint8_t* codes = nullptr;   // tiled T128 layout, n_tiles*n_chunks*4096 bytes
+  float* row_scales = nullptr;  // [n_tiles*128], zero on padding rows
+};
+
+namespace ft {
+// Ensures ctx->ws holds at least `bytes` (must not be called during stream
+// capture; it may cudaMalloc).  Returns FT_OK or a status.
+int workspace_reserve(ft_ctx* ctx, size_t bytes, cudaStream_t stream);
+
+// Kernels launched by ft_api.cu (defined in ft_dense.cu).
+int launch_repack_u8(const uint8_t* packed, int64_t rows, int64_t cols, ft_weight* w,
+                     cudaStream_t s);
+int launch_repack_u32(const uint32_t* words, int64_t rows, int64_t cols, ft_weight* w,
+                      cudaStream_t s);
+int launch_quantize_i8(const void* x, bool bf16, int64_t seq, int64_t cols, int8_t* q, float* sx,
+                       cudaStream_t s);
+int launch_dense_f32(ft_ctx* ctx, const ft_weight* w, int64_t seq, const float* x, float* y,
+                     cudaStream_t s);
+int launch_dense_i8(ft_ctx* ctx, const ft_weight* w, int64_t seq, const int8_t* q,
+                    const float* sx, float* y, cudaStream_t s);
+int launch_wgsl_op(const uint32_t* words, const float* scales, const float* x, float* y,
+                   uint32_t seq, uint32_t in_cols, uint32_t out_rows, cudaStream_t s);
+}  // namespace ft

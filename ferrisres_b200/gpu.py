@@ -1,0 +1,224 @@
+"""GPU-side mirror of the reference's ternary compute API.
+
+Classes keep the reference names and argument meanings:
+
+* ``TernaryMatMulOp`` -- src/compute/kernels/ternary_matmul.rs:78-225
+  (``new`` + ``dispatch`` over raw u32 buffers).
+* ``GpuMatmulAccelerator`` -- src/model/gpu_forward.rs:1154-1297
+  (``gpu_ternary_matmul`` host slices in, host vector out; ``_vram`` variant).
+* ``DeviceTernaryWeight`` -- an uploaded weight (the role of the reference's
+  ``GpuVramCache`` entries, src/model/cpu_block_attn_res.rs:3072-3120).
+
+Device buffers are torch CUDA tensors; every call goes through the C ABI of
+libferris_ternary.so on the caller's current torch stream.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import threading
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import ShapeError, call
+
+_ctxs: dict[int, "Context"] = {}
+_ctx_lock = threading.Lock()
+
+
+class Context:
+    """One CUDA device bound to the library (ft_ctx)."""
+
+    def __init__(self, device: int = 0):
+        h = C.c_void_p()
+        call("ft_ctx_create", int(device), C.byref(h))
+        self.handle = h
+        self.device = int(device)
+
+    def close(self):
+        if self.handle:
+            _lib.lib().ft_ctx_destroy(self.handle)
+            self.handle = None
+
+
+def get_context(device: int | None = None) -> Context:
+    if device is None:
+        device = torch.cuda.current_device()
+    with _ctx_lock:
+        c = _ctxs.get(device)
+        if c is None:
+            c = _ctxs[device] = Context(device)
+        return c
+
+
+def _stream_ptr(stream=None):
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return C.c_void_p(s.cuda_stream)
+
+
+def _dptr(t: torch.Tensor):
+    if not t.is_cuda:
+        raise ShapeError("expected a CUDA tensor")
+    if not t.is_contiguous():
+        raise ShapeError("expected a contiguous tensor")
+    return C.c_void_p(t.data_ptr())
+
+
+def _host(a, dtype):
+    return np.ascontiguousarray(np.asarray(a), dtype=dtype)
+
+
+class DeviceTernaryWeight:
+    """A dense ternary matrix [rows, cols] resident in HBM with per-row scales."""
+
+    def __init__(self, handle, rows: int, cols: int, ctx: Context):
+        self.handle = handle
+        self.rows, self.cols = int(rows), int(cols)
+        self.ctx = ctx
+
+    @classmethod
+    def from_packed_u8(cls, packed, rows, cols, row_scales, device=None):
+        """Reference pack_ternary byte stream (src/model/ternary.rs:141-163)."""
+        ctx = get_context(device)
+        p = _host(packed, np.uint8)
+        s = _host(row_scales, np.float32)
+        if p.size < (rows * cols + 3) // 4 or s.size < rows:
+            raise ShapeError("packed/scales too short for the given shape")
+        h = C.c_void_p()
+        call("ft_weight_upload_packed_u8", ctx.handle, p.ctypes.data_as(C.c_void_p), int(rows),
+             int(cols), s.ctypes.data_as(C.c_void_p), C.byref(h))
+        return cls(h, rows, cols, ctx)
+
+    @classmethod
+    def from_packed_u32(cls, words, rows, cols, row_scales, device=None):
+        """pack_ternary_u32 / WGSL layout (src/model/ternary.rs:1317-1328)."""
+        ctx = get_context(device)
+        w = _host(words, np.uint32)
+        s = _host(row_scales, np.float32)
+        if w.size < rows * ((cols + 15) // 16) or s.size < rows:
+            raise ShapeError("words/scales too short for the given shape")
+        h = C.c_void_p()
+        call("ft_weight_upload_packed_u32", ctx.handle, w.ctypes.data_as(C.c_void_p), int(rows),
+             int(cols), s.ctypes.data_as(C.c_void_p), C.byref(h))
+        return cls(h, rows, cols, ctx)
+
+    @classmethod
+    def from_ternary(cls, values, rows, cols, row_scales, device=None):
+        from .ternary import pack_ternary
+        return cls.from_packed_u8(pack_ternary(values), rows, cols, row_scales, device)
+
+    def device_bytes(self) -> int:
+        b = C.c_int64()
+        call("ft_weight_info", self.handle, None, None, C.byref(b))
+        return b.value
+
+    def matmul_f32(self, x: torch.Tensor, out: torch.Tensor | None = None, stream=None):
+        """y[s, r] = scale[r] * sum_k W[r, k] x[s, k]; x float32 [seq, cols]."""
+        if x.dtype != torch.float32 or x.shape[-1] != self.cols:
+            raise ShapeError(f"x must be float32 [..., {self.cols}], got {tuple(x.shape)} {x.dtype}")
+        seq = x.numel() // self.cols
+        if out is None:
+            out = torch.empty(seq, self.rows, dtype=torch.float32, device=x.device)
+        call("ft_ternary_matmul_f32", self.ctx.handle, self.handle, seq, _dptr(x), _dptr(out),
+             _stream_ptr(stream))
+        return out
+
+    def matmul_i8(self, q: torch.Tensor, sx: torch.Tensor, out: torch.Tensor | None = None,
+                  stream=None):
+        """Bit-exact int8-activation path: ((float)acc * sx[s]) * scale[r]."""
+        if q.dtype != torch.int8 or q.shape[-1] != self.cols:
+            raise ShapeError(f"q must be int8 [..., {self.cols}]")
+        seq = q.numel() // self.cols
+        if sx.dtype != torch.float32 or sx.numel() != seq:
+            raise ShapeError("sx must be float32 [seq]")
+        if out is None:
+            out = torch.empty(seq, self.rows, dtype=torch.float32, device=q.device)
+        call("ft_ternary_matmul_i8", self.ctx.handle, self.handle, seq, _dptr(q), _dptr(sx),
+             _dptr(out), _stream_ptr(stream))
+        return out
+
+    def close(self):
+        if self.handle:
+            _lib.lib().ft_weight_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def quantize_absmax_i8(x: torch.Tensor, stream=None):
+    """Per-token absmax int8 (pinned formula; see include/ferris_ternary.h)."""
+    if x.dim() != 2:
+        raise ShapeError("x must be [seq, cols]")
+    seq, cols = x.shape
+    q = torch.empty(seq, cols, dtype=torch.int8, device=x.device)
+    sx = torch.empty(seq, dtype=torch.float32, device=x.device)
+    ctx = get_context(x.device.index)
+    if x.dtype == torch.bfloat16:
+        call("ft_quantize_absmax_i8_bf16", ctx.handle, seq, cols, _dptr(x), _dptr(q), _dptr(sx),
+             _stream_ptr(stream))
+    elif x.dtype == torch.float32:
+        call("ft_quantize_absmax_i8_f32", ctx.handle, seq, cols, _dptr(x), _dptr(q), _dptr(sx),
+             _stream_ptr(stream))
+    else:
+        raise ShapeError("x must be float32 or bfloat16")
+    return q, sx
+
+
+class TernaryMatMulOp:
+    """src/compute/kernels/ternary_matmul.rs:78-225 on raw device u32 buffers."""
+
+    def __init__(self, device=None):
+        self.ctx = get_context(device)
+
+    @classmethod
+    def new(cls, device=None):
+        return cls(device)
+
+    def dispatch(self, ternary: torch.Tensor, scales: torch.Tensor, input: torch.Tensor,
+                 output: torch.Tensor, seq_len: int, in_cols: int, out_rows: int, stream=None):
+        cp = (in_cols + 15) // 16
+        if ternary.dtype not in (torch.int32, torch.uint32) or ternary.numel() < out_rows * cp:
+            raise ShapeError("ternary must hold out_rows*ceil(in_cols/16) u32 words")
+        if scales.numel() < out_rows or input.numel() < seq_len * in_cols or \
+                output.numel() < seq_len * out_rows:
+            raise ShapeError("buffer too small for the given dims")
+        call("ft_ternary_matmul_op_dispatch", self.ctx.handle, _dptr(ternary), _dptr(scales),
+             _dptr(input), _dptr(output), int(seq_len), int(in_cols), int(out_rows),
+             _stream_ptr(stream))
+
+
+class GpuMatmulAccelerator:
+    """src/model/gpu_forward.rs:1154-1297: host slices in, host vector out."""
+
+    def __init__(self, device=None):
+        self.ctx = get_context(device)
+
+    def gpu_ternary_matmul(self, packed_weights, scales, input, seq_len, in_cols, out_rows):
+        w = _host(packed_weights, np.uint32)
+        s = _host(scales, np.float32)
+        x = _host(input, np.float32)
+        if w.size < out_rows * ((in_cols + 15) // 16) or s.size < out_rows or \
+                x.size < seq_len * in_cols:
+            raise ShapeError("buffer too small for the given dims")
+        y = np.empty(seq_len * out_rows, np.float32)
+        call("ft_gpu_ternary_matmul", self.ctx.handle, w.ctypes.data_as(C.c_void_p),
+             s.ctypes.data_as(C.c_void_p), x.ctypes.data_as(C.c_void_p), int(seq_len),
+             int(in_cols), int(out_rows), y.ctypes.data_as(C.c_void_p))
+        return y
+
+    def gpu_ternary_matmul_vram(self, weight: DeviceTernaryWeight, input, seq_len, in_cols,
+                                out_rows):
+        if weight.cols != in_cols or weight.rows != out_rows:
+            raise ShapeError("weight shape does not match in_cols/out_rows")
+        x = _host(input, np.float32)
+        if x.size < seq_len * in_cols:
+            raise ShapeError("input too small")
+        y = np.empty(seq_len * out_rows, np.float32)
+        call("ft_gpu_ternary_matmul_vram", self.ctx.handle, weight.handle,
+             x.ctypes.data_as(C.c_void_p), int(seq_len), y.ctypes.data_as(C.c_void_p))
+        return y

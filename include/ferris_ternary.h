@@ -1,0 +1,131 @@
+/*
+ * ferris_ternary.h -- C ABI of libferris_ternary.so, the B200 (sm_100a) ternary
+ * matmul hot path of FerrisRes.
+ *
+ * Conventions
+ *   - Every entry point returns an int status (ft_status).  On failure the
+ *     per-thread message is available from ft_last_error_string().  Nothing
+ *     throws or aborts across this boundary.
+ *   - Shapes follow the reference: a weight is [rows = out_features,
+ *     cols = in_features] row-major ("row" = output channel); activations
+ *     are [seq, cols]; outputs are [seq, rows].
+ *   - Pointers documented as "device" are CUDA device pointers; "host" are
+ *     ordinary host memory.  Device-pointer calls are asynchronous on the
+ *     caller's stream (a cudaStream_t passed as void*, NULL = legacy default
+ *     stream) and never synchronise.  Host-buffer calls are synchronous.
+ *   - Reference interfaces replaced are cited as path:line within
+ *     shift/FerrisRes v0.2.3.
+ *
+ * Status codes map onto FerrisResError (src/error.rs:3-36):
+ *   1 Shape, 2 Gpu, 3 OOM, 4 Unsupported, 5 Timeout/Comm, 6 Device.
+ */
+#ifndef FERRIS_TERNARY_H
+#define FERRIS_TERNARY_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+typedef enum ft_status {
+  FT_OK = 0,
+  FT_ERR_SHAPE = 1,       /* FerrisResError::Shape */
+  FT_ERR_GPU = 2,         /* FerrisResError::Gpu */
+  FT_ERR_OOM = 3,         /* FerrisResError::OOM */
+  FT_ERR_UNSUPPORTED = 4, /* FerrisResError::Unsupported */
+  FT_ERR_TIMEOUT = 5,     /* collective / wait timed out */
+  FT_ERR_DEVICE = 6       /* FerrisResError::Device (bad device, no GPU) */
+} ft_status;
+
+typedef struct ft_ctx ft_ctx;       /* one CUDA device + workspace */
+typedef struct ft_weight ft_weight; /* one dense ternary matrix resident in HBM */
+typedef struct ft_sparse ft_sparse; /* one 2:4 sparse ternary matrix resident in HBM */
+
+/* ---- library / context ------------------------------------------------ */
+const char* ft_version(void);
+const char* ft_last_error_string(void);
+/* Number of CUDA kernels this library has launched in this process (a
+ * diagnostic; launches replayed from a captured CUDA graph are not counted
+ * again).  No reference counterpart. */
+uint64_t ft_launch_counter(void);
+/* Replaces TernaryMatMulOp::new(&Arc<Device>, &Arc<Queue>)
+ * (src/compute/kernels/ternary_matmul.rs:84); the kernels are compiled ahead
+ * of time, so creation only binds a device. */
+int ft_ctx_create(int device, ft_ctx** out);
+int ft_ctx_destroy(ft_ctx* ctx);
+
+/* ---- dense weights ----------------------------------------------------- */
+/* Upload from the reference host layout produced by pack_ternary
+ * (src/model/ternary.rs:136-163): (rows*cols+3)/4 bytes, 4 codes per byte,
+ * LSB first, code -1->0b00, 0->0b01, +1->0b10, 0b11->0.  row_scales: [rows]
+ * host floats (the per-output-channel scale; pass the broadcast scalar for
+ * the reference's single-alpha types, src/model/cpu_moe.rs:73-78).  The
+ * matrix is repacked on the device into the tiled layout the kernels read. */
+int ft_weight_upload_packed_u8(ft_ctx* ctx, const uint8_t* packed_host, int64_t rows,
+                               int64_t cols, const float* row_scales_host, ft_weight** out);
+/* Upload from the GPU layout of pack_ternary_u32 / the WGSL op
+ * (src/model/ternary.rs:1317-1328, src/compute/kernels/ternary_matmul.rs:7-8):
+ * rows * ceil(cols/16) u32 words, 16 codes per word, LSB first.  Replaces
+ * GpuVramCache::upload (src/model/cpu_block_attn_res.rs:3072). */
+int ft_weight_upload_packed_u32(ft_ctx* ctx, const uint32_t* words_host, int64_t rows,
+                                int64_t cols, const float* row_scales_host, ft_weight** out);
+/* Same layout already in device memory (e.g. a buffer the caller owns). */
+int ft_weight_from_device_u32(ft_ctx* ctx, const uint32_t* words_dev, int64_t rows, int64_t cols,
+                              const float* row_scales_dev, void* stream, ft_weight** out);
+int ft_weight_destroy(ft_weight* w);
+int ft_weight_info(const ft_weight* w, int64_t* rows, int64_t* cols, int64_t* device_bytes);
+
+/* ---- dense compute (device pointers, caller stream) -------------------- */
+/* y[s, r] = row_scale[r] * sum_k W[r, k] * x[s, k], fp32 activations.
+ * Replaces TernaryMatMulOp::dispatch (src/compute/kernels/ternary_matmul.rs:167-225)
+ * for weights held as ft_weight.  Any seq >= 1 (decode GEMV and prefill GEMM). */
+int ft_ternary_matmul_f32(ft_ctx* ctx, const ft_weight* w, int64_t seq, const float* x_dev,
+                          float* y_dev, void* stream);
+/* Per-token absmax int8 quantizer: sx[s] = absmax/127 (1 when absmax == 0),
+ * q = clamp(round_half_away(x * (127/absmax)), -127, 127).  No reference
+ * counterpart (the reference has no int8 activation path); the formula is
+ * pinned so the int8 matmul below is bit-exact against the reference's own
+ * ternary_matmul run on the same int8 codes. */
+int ft_quantize_absmax_i8_f32(ft_ctx* ctx, int64_t seq, int64_t cols, const float* x_dev,
+                              int8_t* q_dev, float* sx_dev, void* stream);
+int ft_quantize_absmax_i8_bf16(ft_ctx* ctx, int64_t seq, int64_t cols, const uint16_t* x_dev,
+                               int8_t* q_dev, float* sx_dev, void* stream);
+/* y[s, r] = ((float)acc[s, r] * sx[s]) * row_scale[r], acc = exact int32
+ * sum_k W[r, k] * q[s, k].  Bit-exact against the reference ternary_matmul
+ * (src/model/ternary.rs:292-328) fed the int8 codes as f32. */
+int ft_ternary_matmul_i8(ft_ctx* ctx, const ft_weight* w, int64_t seq, const int8_t* q_dev,
+                         const float* sx_dev, float* y_dev, void* stream);
+
+/* Raw WGSL-op form: same arguments as TernaryMatMulOp::dispatch
+ * (src/compute/kernels/ternary_matmul.rs:167-177): ternary = rows*ceil(in_cols/16)
+ * u32 words in device memory, scales [out_rows], input [seq_len, in_cols],
+ * output [seq_len, out_rows], all device pointers; sequential-in-K fp32 sum
+ * then * scales[row], as the shader does. */
+int ft_ternary_matmul_op_dispatch(ft_ctx* ctx, const uint32_t* ternary_dev,
+                                  const float* scales_dev, const float* input_dev,
+                                  float* output_dev, uint32_t seq_len, uint32_t in_cols,
+                                  uint32_t out_rows, void* stream);
+
+/* ---- host-buffer accelerator calls (synchronous) ----------------------- */
+/* GpuMatmulAccelerator::gpu_ternary_matmul (src/model/gpu_forward.rs:1154-1237):
+ * uploads weights, runs, reads back into output_host [seq_len*out_rows]. */
+int ft_gpu_ternary_matmul(ft_ctx* ctx, const uint32_t* packed_weights_host,
+                          const float* scales_host, const float* input_host, size_t seq_len,
+                          size_t in_cols, size_t out_rows, float* output_host);
+/* GpuMatmulAccelerator::gpu_ternary_matmul_vram (src/model/gpu_forward.rs:1245-1297):
+ * weights already resident (ft_weight); host activations in, host output out. */
+int ft_gpu_ternary_matmul_vram(ft_ctx* ctx, const ft_weight* w, const float* input_host,
+                               size_t seq_len, float* output_host);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+#ifdef __cplusplus
+}
+#endif
+#endif /* FERRIS_TERNARY_H */
