@@ -181,8 +181,9 @@ def run_ours(args, ws, rank, local):
     rem_launches = _lib.lib().ft_launch_counter() - launches0
     gpu_launches = full * per_sweep + rem_launches
 
-    # graph warm-up
-    g_full.replay()
+    # graph warm-up (replay() launches on torch's current stream: keep it `stream`)
+    with torch.cuda.stream(stream):
+        g_full.replay()
     stream.synchronize()
 
     sampler = ClockSampler(local)
@@ -191,12 +192,13 @@ def run_ours(args, ws, rank, local):
         dist.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(full):
-        g_full.replay()
-    if g_rem is not None:
-        g_rem.replay()
-    e1.record(stream)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(full):
+            g_full.replay()
+        if g_rem is not None:
+            g_rem.replay()
+        e1.record(stream)
     torch.cuda.synchronize()
     if ws > 1:
         dist.barrier()
@@ -209,16 +211,18 @@ def run_ours(args, ws, rank, local):
     sec = ms / 1e3
     value = args.steps * ws * ALGO_BYTES / sec / 1e9
 
-    # isolated single launch (latency-bound), for context
+    # one step alone (a 1-step graph after an idle GPU: launch + latency bound), for context
     iso = []
+    g_one = capture(1)
     with torch.cuda.stream(stream):
         for i in range(20):
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record(stream)
-            weights[i % n_copies].matmul_f32(x, out=ys[0])
+            g_one.replay()
             b.record(stream)
             b.synchronize()
             iso.append(a.elapsed_time(b))
+    del g_one
 
     # end to end through the host-buffer accelerator call (pinned host memory)
     import numpy as np

@@ -62,12 +62,14 @@ SIGNATURES = {
     "ft_launch_counter": [],
     "ft_ctx_create": [_i, _p],
     "ft_ctx_destroy": [_p],
+    "ft_ctx_check": [_p],
     "ft_weight_upload_packed_u8": [_p, _p, _i64, _i64, _p, _p],
     "ft_weight_upload_packed_u32": [_p, _p, _i64, _i64, _p, _p],
     "ft_weight_from_device_u32": [_p, _p, _i64, _i64, _p, _p, _p],
     "ft_weight_destroy": [_p],
     "ft_weight_info": [_p, _p, _p, _p],
     "ft_ternary_matmul_f32": [_p, _p, _i64, _p, _p, _p],
+    "ft_ternary_matmul_bf16": [_p, _p, _i64, _p, _p, _p],
     "ft_quantize_absmax_i8_f32": [_p, _i64, _i64, _p, _p, _p, _p],
     "ft_quantize_absmax_i8_bf16": [_p, _i64, _i64, _p, _p, _p, _p],
     "ft_ternary_matmul_i8": [_p, _p, _i64, _p, _p, _p, _p],

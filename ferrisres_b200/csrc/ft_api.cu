@@ -53,6 +53,28 @@ int workspace_reserve(ft_ctx* ctx, size_t bytes, cudaStream_t stream) {
   return FT_OK;
 }
 
+int zero_scratch_reserve(ft_ctx* ctx, size_t bytes, cudaStream_t stream) {
+  if (ctx->zs.bytes >= bytes) return FT_OK;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (stream != nullptr) cudaStreamIsCapturing(stream, &cs);
+  FT_CHECK(cs == cudaStreamCaptureStatusNone, FT_ERR_UNSUPPORTED,
+           "scratch must grow to %zu bytes but the stream is being captured; run the call "
+           "once before capture",
+           bytes);
+  if (ctx->zs.ptr) {
+    FT_CUDA(cudaDeviceSynchronize());
+    FT_CUDA(cudaFree(ctx->zs.ptr));
+    ctx->zs.ptr = nullptr;
+    ctx->zs.bytes = 0;
+    ctx->err_flag = nullptr;
+  }
+  size_t grow = bytes + bytes / 4 + (1 << 20);
+  FT_CUDA(cudaMalloc(&ctx->zs.ptr, grow));
+  ctx->zs.bytes = grow;
+  FT_CUDA(cudaMemsetAsync(ctx->zs.ptr, 0, grow, stream));
+  return FT_OK;
+}
+
 struct DeviceGuard {
   int prev = -1;
   explicit DeviceGuard(int dev) {
@@ -142,6 +164,8 @@ int ft_ctx_destroy(ft_ctx* ctx) {
   DeviceGuard g(ctx->device);
   cudaDeviceSynchronize();
   if (ctx->ws.ptr) cudaFree(ctx->ws.ptr);
+  if (ctx->io.ptr) cudaFree(ctx->io.ptr);
+  if (ctx->zs.ptr) cudaFree(ctx->zs.ptr);
   if (ctx->host_stream) cudaStreamDestroy(ctx->host_stream);
   delete ctx;
   return FT_OK;
@@ -241,7 +265,35 @@ int ft_ternary_matmul_f32(ft_ctx* ctx, const ft_weight* w, int64_t seq, const fl
   FT_CHECK(w->device == ctx->device, FT_ERR_DEVICE, "weight lives on device %d, context on %d",
            w->device, ctx->device);
   DeviceGuard g(ctx->device);
-  return launch_dense_f32(ctx, w, seq, x_dev, y_dev, static_cast<cudaStream_t>(stream));
+  return launch_tc_matmul(ctx, w, seq, x_dev, 0, nullptr, y_dev, static_cast<cudaStream_t>(stream));
+}
+
+int ft_ternary_matmul_bf16(ft_ctx* ctx, const ft_weight* w, int64_t seq, const uint16_t* x_dev,
+                           float* y_dev, void* stream) {
+  FT_CHECK(ctx && w, FT_ERR_SHAPE, "null context or weight");
+  FT_CHECK(seq >= 0, FT_ERR_SHAPE, "seq must be >= 0");
+  FT_CHECK(seq == 0 || (x_dev && y_dev), FT_ERR_SHAPE, "null activation/output pointer");
+  FT_CHECK(w->device == ctx->device, FT_ERR_DEVICE, "weight lives on device %d, context on %d",
+           w->device, ctx->device);
+  DeviceGuard g(ctx->device);
+  return launch_tc_matmul(ctx, w, seq, x_dev, 1, nullptr, y_dev, static_cast<cudaStream_t>(stream));
+}
+
+int ft_ctx_check(ft_ctx* ctx) {
+  FT_CHECK(ctx, FT_ERR_SHAPE, "null context");
+  DeviceGuard g(ctx->device);
+  FT_CUDA(cudaDeviceSynchronize());
+  if (ctx->err_flag) {
+    int code = 0;
+    FT_CUDA(cudaMemcpy(&code, ctx->err_flag, sizeof(int), cudaMemcpyDeviceToHost));
+    if (code != 0) {
+      int zero = 0;
+      FT_CUDA(cudaMemcpy(ctx->err_flag, &zero, sizeof(int), cudaMemcpyHostToDevice));
+      return fail(FT_ERR_TIMEOUT, "a kernel's bounded wait gave up (site %d); results of that "
+                  "launch are invalid", code);
+    }
+  }
+  return FT_OK;
 }
 
 int ft_quantize_absmax_i8_f32(ft_ctx* ctx, int64_t seq, int64_t cols, const float* x_dev,
@@ -270,7 +322,7 @@ int ft_ternary_matmul_i8(ft_ctx* ctx, const ft_weight* w, int64_t seq, const int
   FT_CHECK(w->device == ctx->device, FT_ERR_DEVICE, "weight lives on device %d, context on %d",
            w->device, ctx->device);
   DeviceGuard g(ctx->device);
-  return launch_dense_i8(ctx, w, seq, q_dev, sx_dev, y_dev, static_cast<cudaStream_t>(stream));
+  return launch_tc_matmul(ctx, w, seq, q_dev, 2, sx_dev, y_dev, static_cast<cudaStream_t>(stream));
 }
 
 int ft_ternary_matmul_op_dispatch(ft_ctx* ctx, const uint32_t* ternary_dev,
@@ -307,23 +359,29 @@ int ft_gpu_ternary_matmul_vram(ft_ctx* ctx, const ft_weight* w, const float* inp
   if (seq_len == 0) return FT_OK;
   DeviceGuard g(ctx->device);
   cudaStream_t s = ctx->host_stream;
-  size_t in_bytes = seq_len * (size_t)w->cols * sizeof(float);
+  size_t in_bytes = round_up(seq_len * (size_t)w->cols * sizeof(float), 256);
   size_t out_bytes = seq_len * (size_t)w->rows * sizeof(float);
-  float* dx = nullptr;
-  float* dy = nullptr;
-  FT_CUDA(cudaMallocAsync(&dx, in_bytes, s));
-  cudaError_t e = cudaMallocAsync(&dy, out_bytes, s);
-  int st = FT_OK;
-  if (e == cudaSuccess) e = cudaMemcpyAsync(dx, input_host, in_bytes, cudaMemcpyHostToDevice, s);
-  if (e == cudaSuccess) st = launch_dense_f32(ctx, w, (int64_t)seq_len, dx, dy, s);
-  if (e == cudaSuccess && st == FT_OK)
-    e = cudaMemcpyAsync(output_host, dy, out_bytes, cudaMemcpyDeviceToHost, s);
-  if (dx) cudaFreeAsync(dx, s);
-  if (dy) cudaFreeAsync(dy, s);
-  cudaError_t e2 = cudaStreamSynchronize(s);
-  if (e == cudaSuccess) e = e2;
-  if (e != cudaSuccess) return fail(FT_ERR_GPU, "gpu_ternary_matmul_vram failed: %s", cudaGetErrorString(e));
-  return st;
+  // Device staging is kept in the context and only grows (no per-call malloc).
+  if (ctx->io.bytes < in_bytes + out_bytes) {
+    FT_CUDA(cudaStreamSynchronize(s));
+    if (ctx->io.ptr) FT_CUDA(cudaFree(ctx->io.ptr));
+    ctx->io.ptr = nullptr;
+    ctx->io.bytes = 0;
+    FT_CUDA(cudaMalloc(&ctx->io.ptr, in_bytes + out_bytes));
+    ctx->io.bytes = in_bytes + out_bytes;
+  }
+  float* dx = static_cast<float*>(ctx->io.ptr);
+  float* dy = reinterpret_cast<float*>(static_cast<char*>(ctx->io.ptr) + in_bytes);
+  FT_CUDA(cudaMemcpyAsync(dx, input_host, seq_len * (size_t)w->cols * sizeof(float),
+                          cudaMemcpyHostToDevice, s));
+  int st = launch_tc_matmul(ctx, w, (int64_t)seq_len, dx, 0, nullptr, dy, s);
+  if (st != FT_OK) {
+    cudaStreamSynchronize(s);
+    return st;
+  }
+  FT_CUDA(cudaMemcpyAsync(output_host, dy, out_bytes, cudaMemcpyDeviceToHost, s));
+  FT_CUDA(cudaStreamSynchronize(s));
+  return FT_OK;
 }
 
 }  // extern "C"

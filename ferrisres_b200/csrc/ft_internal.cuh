@@ -76,6 +76,9 @@ struct ft_ctx {
   int num_sms = 0;
   ft::Workspace ws;
   cudaStream_t host_stream = nullptr;  // used by the synchronous host-buffer calls
+  ft::Workspace io;                    // device staging for the host-buffer calls
+  ft::Workspace zs;                    // zero-initialised scratch (split-K sums, tickets)
+  int* err_flag = nullptr;             // device word set by a kernel whose bounded wait gave up
 };
 
 struct ft_weight {
@@ -90,6 +93,9 @@ namespace ft {
 // Ensures ctx->ws holds at least `bytes` (must not be called during stream
 // capture; it may cudaMalloc).  Returns FT_OK or a status.
 int workspace_reserve(ft_ctx* ctx, size_t bytes, cudaStream_t stream);
+// Same for ctx->zs; new memory is zeroed on `stream`.  Kernels that use it
+// leave it zeroed again when they finish.
+int zero_scratch_reserve(ft_ctx* ctx, size_t bytes, cudaStream_t stream);
 
 // Kernels launched by ft_api.cu (defined in ft_dense.cu).
 int launch_repack_u8(const uint8_t* packed, int64_t rows, int64_t cols, ft_weight* w,
@@ -102,6 +108,10 @@ int launch_dense_f32(ft_ctx* ctx, const ft_weight* w, int64_t seq, const float* 
                      cudaStream_t s);
 int launch_dense_i8(ft_ctx* ctx, const ft_weight* w, int64_t seq, const int8_t* q,
                     const float* sx, float* y, cudaStream_t s);
+// Tensor-core path (ft_tc.cu).  xkind: 0 f32, 1 bf16, 2 int8 codes (then sx
+// is the per-token scale).
+int launch_tc_matmul(ft_ctx* ctx, const ft_weight* w, int64_t seq, const void* x, int xkind,
+                     const float* sx, float* y, cudaStream_t s);
 int launch_wgsl_op(const uint32_t* words, const float* scales, const float* x, float* y,
                    uint32_t seq, uint32_t in_cols, uint32_t out_rows, cudaStream_t s);
 }  // namespace ft

@@ -36,6 +36,10 @@ class Context:
         self.handle = h
         self.device = int(device)
 
+    def check(self):
+        """Synchronise and raise CommTimeoutError if a kernel's bounded wait gave up."""
+        call("ft_ctx_check", self.handle)
+
     def close(self):
         if self.handle:
             _lib.lib().ft_ctx_destroy(self.handle)
@@ -121,6 +125,17 @@ class DeviceTernaryWeight:
         if out is None:
             out = torch.empty(seq, self.rows, dtype=torch.float32, device=x.device)
         call("ft_ternary_matmul_f32", self.ctx.handle, self.handle, seq, _dptr(x), _dptr(out),
+             _stream_ptr(stream))
+        return out
+
+    def matmul_bf16(self, x: torch.Tensor, out: torch.Tensor | None = None, stream=None):
+        """Same as matmul_f32 with bf16 activations."""
+        if x.dtype != torch.bfloat16 or x.shape[-1] != self.cols:
+            raise ShapeError(f"x must be bfloat16 [..., {self.cols}]")
+        seq = x.numel() // self.cols
+        if out is None:
+            out = torch.empty(seq, self.rows, dtype=torch.float32, device=x.device)
+        call("ft_ternary_matmul_bf16", self.ctx.handle, self.handle, seq, _dptr(x), _dptr(out),
              _stream_ptr(stream))
         return out
 

@@ -58,6 +58,13 @@ uint64_t ft_launch_counter(void);
  * of time, so creation only binds a device. */
 int ft_ctx_create(int device, ft_ctx** out);
 int ft_ctx_destroy(ft_ctx* ctx);
+/* Synchronises the device and reports whether any kernel launched through
+ * this context gave up a bounded internal wait (FT_ERR_TIMEOUT; the flag is
+ * then cleared).  Kernels never spin unboundedly: a wait that exceeds 2 s
+ * records its site here and the launch finishes with invalid results.
+ * Note: a context's scratch is shared by its calls, so calls through one
+ * context must be ordered (same stream, or synchronised). */
+int ft_ctx_check(ft_ctx* ctx);
 
 /* ---- dense weights ----------------------------------------------------- */
 /* Upload from the reference host layout produced by pack_ternary
@@ -86,6 +93,9 @@ int ft_weight_info(const ft_weight* w, int64_t* rows, int64_t* cols, int64_t* de
  * for weights held as ft_weight.  Any seq >= 1 (decode GEMV and prefill GEMM). */
 int ft_ternary_matmul_f32(ft_ctx* ctx, const ft_weight* w, int64_t seq, const float* x_dev,
                           float* y_dev, void* stream);
+/* Same with bf16 activations (bit patterns as uint16). */
+int ft_ternary_matmul_bf16(ft_ctx* ctx, const ft_weight* w, int64_t seq, const uint16_t* x_dev,
+                           float* y_dev, void* stream);
 /* Per-token absmax int8 quantizer: sx[s] = absmax/127 (1 when absmax == 0),
  * q = clamp(round_half_away(x * (127/absmax)), -127, 127).  No reference
  * counterpart (the reference has no int8 activation path); the formula is

@@ -54,6 +54,26 @@ def test_i8_bit_exact(gpu, rows, cols, seq):
     assert_bits_equal(y.cpu().numpy(), ref, what=f"{rows}x{cols}x{seq}")
 
 
+@pytest.mark.parametrize("seq", [1, 4, 5, 64, 65, 300])
+def test_bf16_activations(gpu, seq):
+    rng = np.random.default_rng(seq)
+    rows, cols = 384, 1408
+    t = ternary_matrix(rng, rows, cols)
+    rs = rng.uniform(0.01, 0.1, rows).astype(np.float32)
+    xb = torch.from_numpy(rng.standard_normal((seq, cols)).astype(np.float32)).to(torch.bfloat16)
+    x = xb.float().numpy().ravel()
+    w = gpu.DeviceTernaryWeight.from_packed_u8(fo.pack_ternary(t), rows, cols, rs)
+    y = w.matmul_bf16(xb.cuda()).cpu().numpy()
+    ref = np.concatenate([fo.ternary_matmul(t, 1.0, x[s * cols:(s + 1) * cols], rows, cols, 1) * rs
+                          for s in range(seq)])
+    assert_fp32_close(y, ref, condition(t, x, rows, cols, seq, rs), what=f"bf16 seq={seq}")
+
+
+def test_no_kernel_timeouts(gpu):
+    """Run after the others in this module: no bounded wait inside a kernel gave up."""
+    gpu.get_context().check()
+
+
 def test_quantizer_bit_exact(gpu):
     rng = np.random.default_rng(0)
     x = rng.standard_normal((9, 1000)).astype(np.float32)
