@@ -152,77 +152,81 @@ def run_ours(args, ws, rank, local):
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
 
+    group = args.group
     n_copies = max(8, -(-2 * L2_BYTES // (ROWS * COLS // 4)))  # > 2x L2 of weights
+    n_copies = -(-n_copies // group) * group
     weights = make_weights(gpu, torch, n_copies, device)
     g = torch.Generator(device=device).manual_seed(1000 + rank)
     x = torch.randn(1, COLS, generator=g, device=device)
-    ys = [torch.empty(1, ROWS, device=device) for _ in range(2)]
+    ys = [torch.empty(1, ROWS, device=device) for _ in range(n_copies)]
+    # one grouped call per G consecutive weight copies, all reading the token x
+    calls = [gpu.GroupCall(weights[i:i + group], [x] * group, ys[i:i + group])
+             for i in range(0, n_copies, group)]
+    singles = [gpu.GroupCall([weights[i]], [x], [ys[i]]) for i in range(n_copies)]
 
     stream = torch.cuda.Stream(device=device)
-    # warm-up (also sizes the context workspace before capture)
-    with torch.cuda.stream(stream):
-        for i in range(max(args.warmup, 3)):
-            weights[i % n_copies].matmul_f32(x, out=ys[i & 1])
+    with torch.cuda.stream(stream):  # warm-up; also sizes workspaces before capture
+        for i in range(max(args.warmup // group, 3)):
+            calls[i % len(calls)]()
+        for i in range(3):
+            singles[i]()
     stream.synchronize()
 
-    def capture(nsteps, offset=0):
+    def capture(fns):
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=stream):
-            for i in range(nsteps):
-                weights[(offset + i) % n_copies].matmul_f32(x, out=ys[i & 1])
+            for f in fns:
+                f()
         return graph
 
+    steps = args.steps
     launches0 = _lib.lib().ft_launch_counter()
-    g_full = capture(n_copies)
+    g_full = capture(calls)  # one sweep = n_copies steps
     per_sweep = _lib.lib().ft_launch_counter() - launches0
-    full, rem = divmod(args.steps, n_copies)
+    full, rem = divmod(steps, n_copies)
+    rem_groups, rem_single = divmod(rem, group)
     launches0 = _lib.lib().ft_launch_counter()
-    g_rem = capture(rem) if rem else None
+    g_rem = capture(calls[:rem_groups] + singles[rem_groups * group:rem_groups * group + rem_single]) \
+        if rem else None
     rem_launches = _lib.lib().ft_launch_counter() - launches0
     gpu_launches = full * per_sweep + rem_launches
 
-    # graph warm-up (replay() launches on torch's current stream: keep it `stream`)
-    with torch.cuda.stream(stream):
-        g_full.replay()
-    stream.synchronize()
+    def timed(graph_list):
+        with torch.cuda.stream(stream):
+            graph_list[0][0].replay()  # warm
+        stream.synchronize()
+        if ws > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for gr, reps in graph_list:
+                for _ in range(reps):
+                    gr.replay()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        t = torch.tensor([ms], device=device, dtype=torch.float64)
+        if ws > 1:
+            dist.barrier()
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
 
     sampler = ClockSampler(local)
     sampler.start()
-    if ws > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        e0.record(stream)
-        for _ in range(full):
-            g_full.replay()
-        if g_rem is not None:
-            g_rem.replay()
-        e1.record(stream)
-    torch.cuda.synchronize()
-    if ws > 1:
-        dist.barrier()
+    plan = [(g_full, full)] + ([(g_rem, 1)] if g_rem is not None else [])
+    ms = timed(plan)
     clocks = sampler.stop()
-    ms = e0.elapsed_time(e1)
-    t_max = torch.tensor([ms], device=device, dtype=torch.float64)
-    if ws > 1:
-        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
-    ms = float(t_max.item())
     sec = ms / 1e3
-    value = args.steps * ws * ALGO_BYTES / sec / 1e9
+    value = steps * ws * ALGO_BYTES / sec / 1e9
 
-    # one step alone (a 1-step graph after an idle GPU: launch + latency bound), for context
-    iso = []
-    g_one = capture(1)
-    with torch.cuda.stream(stream):
-        for i in range(20):
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record(stream)
-            g_one.replay()
-            b.record(stream)
-            b.synchronize()
-            iso.append(a.elapsed_time(b))
-    del g_one
+    # dependent-chain reference: the same steps as single-GEMV launches
+    g_chain = capture(singles)
+    chain_reps = max(1, min(full, 20))
+    ms_chain = timed([(g_chain, chain_reps)])
+    chain_step_s = ms_chain / 1e3 / (chain_reps * n_copies)
+    del g_chain
 
     # end to end through the host-buffer accelerator call (pinned host memory)
     import numpy as np
@@ -251,14 +255,21 @@ def run_ours(args, ws, rank, local):
                    "weight_copies": n_copies,
                    "l2": f"weights rotate over {n_copies} copies "
                          f"({n_copies * ROWS * COLS // 4 / 2**20:.0f} MiB > 2x L2)",
-                   "parallelism": f"replicas x{ws}", "graph": "CUDA graph replay"},
-        "roofline": {"bound": "hbm", "achieved": round(ALGO_BYTES / (sec / args.steps) / 1e9, 2),
+                   "parallelism": f"replicas x{ws}", "graph": "CUDA graph replay",
+                   "launch_group": f"{group} GEMVs (shared token x) per launch"},
+        "roofline": {"bound": "hbm", "achieved": round(ALGO_BYTES * group / (sec * group / steps) / 1e9, 2),
                      "peak": peak, "unit": "GB/s",
-                     "frac": round(ALGO_BYTES / (sec / args.steps) / 1e9 / peak, 4),
+                     "frac": round(ALGO_BYTES * group / (sec * group / steps) / 1e9 / peak, 4),
                      "peak_source": peak_kind, "traffic": traffic,
-                     "algorithmic_bytes_per_launch": ALGO_BYTES,
-                     "note": "achieved = algorithmic bytes per step / per-step device time"},
-        "isolated_launch_us": round(statistics.median(iso) * 1e3, 2),
+                     "kernel": "tq_grouped_kernel<16> (+ prep_b_kernel)",
+                     "algorithmic_bytes_per_launch": ALGO_BYTES * group,
+                     "note": f"one launch = {group} GEMVs; achieved = algorithmic bytes per "
+                             "launch / per-launch device time (CUDA events over the timed region)"},
+        "single_gemv_chain": {"us_per_gemv": round(chain_step_s * 1e6, 3),
+                              "GBps": round(ALGO_BYTES / chain_step_s / 1e9, 2),
+                              "frac": round(ALGO_BYTES / chain_step_s / 1e9 / peak, 4),
+                              "note": "each GEMV its own launch (prep + matmul), back to back "
+                                      "in a CUDA graph with programmatic dependent launch"},
         "e2e": {"value": round(e2e_value, 3), "unit": UNIT, "h2d_bytes_per_step": COLS * 4,
                 "d2h_bytes_per_step": ROWS * 4, "steps": n_e2e,
                 "api": "ft_gpu_ternary_matmul_vram (GpuMatmulAccelerator::gpu_ternary_matmul_vram)"},
@@ -340,6 +351,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=200)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--group", type=int, default=16, help="GEMVs per launch (1..64)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()
     ws, rank, local = dist_env()

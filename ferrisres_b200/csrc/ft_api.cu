@@ -279,6 +279,25 @@ int ft_ternary_matmul_bf16(ft_ctx* ctx, const ft_weight* w, int64_t seq, const u
   return launch_tc_matmul(ctx, w, seq, x_dev, 1, nullptr, y_dev, static_cast<cudaStream_t>(stream));
 }
 
+int ft_ternary_matmul_f32_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t seq,
+                                  const float* const* xs_dev, float* const* ys_dev, void* stream) {
+  FT_CHECK(ctx && ws && xs_dev && ys_dev, FT_ERR_SHAPE, "null argument");
+  FT_CHECK(seq >= 0, FT_ERR_SHAPE, "seq must be >= 0");
+  DeviceGuard g(ctx->device);
+  return launch_tc_grouped(ctx, n, ws, seq, reinterpret_cast<const void* const*>(xs_dev), 0,
+                           nullptr, ys_dev, nullptr, static_cast<cudaStream_t>(stream));
+}
+
+int ft_ternary_matmul_i8_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t seq,
+                                 const int8_t* const* qs_dev, const float* const* sxs_dev,
+                                 float* const* ys_dev, void* stream) {
+  FT_CHECK(ctx && ws && qs_dev && sxs_dev && ys_dev, FT_ERR_SHAPE, "null argument");
+  FT_CHECK(seq >= 0, FT_ERR_SHAPE, "seq must be >= 0");
+  DeviceGuard g(ctx->device);
+  return launch_tc_grouped(ctx, n, ws, seq, reinterpret_cast<const void* const*>(qs_dev), 2,
+                           sxs_dev, ys_dev, nullptr, static_cast<cudaStream_t>(stream));
+}
+
 int ft_ctx_check(ft_ctx* ctx) {
   FT_CHECK(ctx, FT_ERR_SHAPE, "null context");
   DeviceGuard g(ctx->device);

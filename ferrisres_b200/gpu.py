@@ -165,6 +165,42 @@ class DeviceTernaryWeight:
             pass
 
 
+class GroupCall:
+    """A prepared grouped call: n weights with the same seq in one launch.
+
+    Pointer arrays are built once, so repeated calls (and CUDA-graph capture)
+    cost one C call each."""
+
+    def __init__(self, weights, xs, ys, qs_sx=None):
+        n = len(weights)
+        if not (1 <= n <= 64) or len(xs) != n or len(ys) != n:
+            raise ShapeError("group needs 1..64 weights with matching activations/outputs")
+        self.ctx = weights[0].ctx
+        self.weights, self.xs, self.ys = list(weights), list(xs), list(ys)
+        self.seq = xs[0].numel() // weights[0].cols
+        for w, x, y in zip(weights, xs, ys):
+            if x.shape[-1] != w.cols or x.numel() // w.cols != self.seq:
+                raise ShapeError("all group members need [seq, cols] activations, same seq")
+            if y.numel() < self.seq * w.rows:
+                raise ShapeError("output too small")
+            _dptr(x), _dptr(y)
+        self._w = (C.c_void_p * n)(*[w.handle.value for w in weights])
+        self._x = (C.c_void_p * n)(*[x.data_ptr() for x in xs])
+        self._y = (C.c_void_p * n)(*[y.data_ptr() for y in ys])
+        self.n = n
+        self.i8 = qs_sx is not None
+        if self.i8:
+            self._sx = (C.c_void_p * n)(*[sx.data_ptr() for sx in qs_sx])
+
+    def __call__(self, stream=None):
+        if self.i8:
+            call("ft_ternary_matmul_i8_grouped", self.ctx.handle, self.n, self._w, self.seq,
+                 self._x, self._sx, self._y, _stream_ptr(stream))
+        else:
+            call("ft_ternary_matmul_f32_grouped", self.ctx.handle, self.n, self._w, self.seq,
+                 self._x, self._y, _stream_ptr(stream))
+
+
 def quantize_absmax_i8(x: torch.Tensor, stream=None):
     """Per-token absmax int8 (pinned formula; see include/ferris_ternary.h)."""
     if x.dim() != 2:

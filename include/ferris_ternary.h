@@ -96,6 +96,17 @@ int ft_ternary_matmul_f32(ft_ctx* ctx, const ft_weight* w, int64_t seq, const fl
 /* Same with bf16 activations (bit patterns as uint16). */
 int ft_ternary_matmul_bf16(ft_ctx* ctx, const ft_weight* w, int64_t seq, const uint16_t* x_dev,
                            float* y_dev, void* stream);
+/* Grouped form: n (1..64) independent matmuls with the same seq in one
+ * persistent launch -- e.g. the q/k/v projections of a decode step, or the
+ * gate and up projections of the experts a token selected (the reference runs
+ * these as separate dispatches: src/model/cpu_block_attn_res.rs:2254-2316).
+ * ws[i] : weight i; xs_dev[i] : [seq, ws[i].cols]; ys_dev[i] : [seq, ws[i].rows].
+ * Entries that pass the same activation pointer share its preparation. */
+int ft_ternary_matmul_f32_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t seq,
+                                  const float* const* xs_dev, float* const* ys_dev, void* stream);
+int ft_ternary_matmul_i8_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t seq,
+                                 const int8_t* const* qs_dev, const float* const* sxs_dev,
+                                 float* const* ys_dev, void* stream);
 /* Per-token absmax int8 quantizer: sx[s] = absmax/127 (1 when absmax == 0),
  * q = clamp(round_half_away(x * (127/absmax)), -127, 127).  No reference
  * counterpart (the reference has no int8 activation path); the formula is

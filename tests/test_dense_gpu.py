@@ -69,6 +69,59 @@ def test_bf16_activations(gpu, seq):
     assert_fp32_close(y, ref, condition(t, x, rows, cols, seq, rs), what=f"bf16 seq={seq}")
 
 
+@pytest.mark.parametrize("seq", [1, 3])
+def test_grouped_f32(gpu, seq):
+    """One launch over several weights of different shapes; two share x."""
+    rng = np.random.default_rng(40 + seq)
+    shapes = [(5632, 2048), (2048, 2048), (300, 2048), (1408, 512), (129, 70)]
+    ws, xs, ys, refs, conds = [], [], [], [], []
+    x_shared = rng.standard_normal(seq * 2048).astype(np.float32)
+    xt_shared = torch.from_numpy(x_shared).cuda().view(seq, 2048)
+    for i, (rows, cols) in enumerate(shapes):
+        t = ternary_matrix(rng, rows, cols)
+        rs = rng.uniform(0.01, 0.1, rows).astype(np.float32)
+        if cols == 2048 and i < 3:
+            x, xt = x_shared, xt_shared
+        else:
+            x = rng.standard_normal(seq * cols).astype(np.float32)
+            xt = torch.from_numpy(x).cuda().view(seq, cols)
+        ws.append(gpu.DeviceTernaryWeight.from_packed_u8(fo.pack_ternary(t), rows, cols, rs))
+        xs.append(xt)
+        ys.append(torch.full((seq, rows), float("nan"), device="cuda"))
+        refs.append(np.concatenate([fo.ternary_matmul(t, 1.0, x[s * cols:(s + 1) * cols], rows,
+                                                      cols, 1) * rs for s in range(seq)]))
+        conds.append(condition(t, x, rows, cols, seq, rs))
+    gpu.GroupCall(ws, xs, ys)()
+    for y, ref, cond in zip(ys, refs, conds):
+        assert_fp32_close(y.cpu().numpy(), ref, cond, what="grouped")
+    # same call again: scratch left clean by the first call
+    for y in ys:
+        y.fill_(float("nan"))
+    gpu.GroupCall(ws, xs, ys)()
+    for y, ref, cond in zip(ys, refs, conds):
+        assert_fp32_close(y.cpu().numpy(), ref, cond, what="grouped again")
+
+
+def test_grouped_i8_bit_exact(gpu):
+    rng = np.random.default_rng(77)
+    seq = 40
+    shapes = [(1408, 2048), (1408, 2048), (2048, 1408)]
+    ws, qs, sxs, ys, refs = [], [], [], [], []
+    for rows, cols in shapes:
+        t = ternary_matrix(rng, rows, cols)
+        rs = rng.uniform(0.01, 0.1, rows).astype(np.float32)
+        x = rng.standard_normal(seq * cols).astype(np.float32)
+        q, sx = fo.quantize_absmax_i8(x, seq, cols)
+        ws.append(gpu.DeviceTernaryWeight.from_packed_u8(fo.pack_ternary(t), rows, cols, rs))
+        qs.append(torch.from_numpy(q).cuda().view(seq, cols))
+        sxs.append(torch.from_numpy(sx).cuda())
+        ys.append(torch.empty(seq, rows, device="cuda"))
+        refs.append(fo.ternary_matmul_i8(t, q, sx, rs, seq, cols, rows))
+    gpu.GroupCall(ws, qs, ys, qs_sx=sxs)()
+    for y, ref in zip(ys, refs):
+        assert_bits_equal(y.cpu().numpy(), ref, what="grouped i8")
+
+
 def test_no_kernel_timeouts(gpu):
     """Run after the others in this module: no bounded wait inside a kernel gave up."""
     gpu.get_context().check()
