@@ -20,16 +20,18 @@
 //
 // Work items.  A problem (one weight, its activations and output) is cut
 // into items = (column pass, 128-row tile, K range).  The launch is persistent:
-// CTA b takes items b, b + grid, b + 2*grid, ...  Warp roles (320 threads):
-//   warps 0-3  converters: thread r loads row r's 32 bytes per 128-K chunk
-//              straight from HBM (512 contiguous bytes per warp instruction),
-//              kPrefetch chunks in flight across item boundaries, unpacks,
-//              tcgen05.st into A stage s.
-//   warp 4     producer: 1-D bulk copies of the B chunk into smem stage s.
-//   warp 5     MMA issuer: 4 x tcgen05.mma (K = 32 each) per chunk into one of
+// CTA b takes items b, b + grid, b + 2*grid, ...  Warp roles (352 threads):
+//   warp 4     weight producer: 1-D bulk copies of the 4 KB (tile, chunk)
+//              blocks into a 16-deep smem ring (64 KB in flight per CTA),
+//              running ahead across item boundaries.
+//   warp 5     B producer: bulk copies of the B chunks into their own ring.
+//   warps 0-3  converters: thread r reads row r's 32 bytes of the block
+//              (conflict-free: the block is [half][row][16 B]), unpacks,
+//              tcgen05.st into TMEM A stage s.
+//   warp 6     MMA issuer: 4 x tcgen05.mma (K = 32 each) per chunk into one of
 //              two TMEM accumulators; tcgen05.commit frees stages / signals D.
 //              Also owns the TMEM allocation.
-//   warps 6-9  epilogue: tcgen05.ld of the finished accumulator, release it,
+//   warps 7-10 epilogue: tcgen05.ld of the finished accumulator, release it,
 //              then scale and store (or add split-K partials).
 // Split-K partials are combined with exact int32 atomics in a zero-initialised
 // scratch area; the last CTA of a tile (atomic ticket) runs the final
@@ -42,9 +44,10 @@
 namespace ft {
 namespace {
 
-constexpr int kStages = 4;
-constexpr int kPrefetch = 4;
-constexpr int kThreads = 320;
+constexpr int kStages = 4;   // TMEM A stages
+constexpr int kSA = 16;      // smem ring of 4 KB weight blocks (64 KB in flight per CTA)
+constexpr int kWarpLoadA = 4, kWarpLoadB = 5, kWarpMma = 6;  // warps 7-10: epilogue
+constexpr int kThreads = 352;
 constexpr int kMaxProblems = 64;
 
 struct TqProblem {
@@ -120,6 +123,13 @@ struct Cursor {
 };
 
 __host__ __device__ constexpr int dbufs_for(int npad) { return npad <= 128 ? 2 : 1; }
+// B-operand smem stages: about 96 KB, between 2 and 16 stages.
+__host__ __device__ constexpr int b_stages_for(int npad) {
+  return (98304 / (npad * 128)) < 2 ? 2 : (98304 / (npad * 128)) > 16 ? 16 : (98304 / (npad * 128));
+}
+__host__ __device__ constexpr size_t smem_bytes_for(int npad) {
+  return (size_t)kSA * 4096 + (size_t)b_stages_for(npad) * npad * 128;
+}
 __host__ __device__ constexpr uint32_t dstride_for(int npad) { return (uint32_t)((npad + 31) / 32 * 32); }
 __host__ __device__ constexpr uint32_t acol0_for(int npad) { return dbufs_for(npad) * dstride_for(npad); }
 __host__ __device__ constexpr uint32_t tmem_cols_for(int npad) {
@@ -163,17 +173,24 @@ __device__ __forceinline__ void epilogue_group(const TqProblem& p, int digits, i
 }
 
 template <int NPAD>
-__global__ void __launch_bounds__(kThreads, 2) tq_grouped_kernel(const __grid_constant__ TqBatch b) {
-  extern __shared__ __align__(128) uint8_t smem_b[];  // kStages x NPAD*128 bytes
-  __shared__ __align__(8) uint64_t bar_bfull[kStages];
-  __shared__ __align__(8) uint64_t bar_afull[kStages];
-  __shared__ __align__(8) uint64_t bar_free[kStages];
+__global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_constant__ TqBatch b) {
+  // dynamic smem: [SA weight blocks of 4096 B][SB B-operand stages of NPAD*128 B]
+  extern __shared__ __align__(1024) uint8_t smem_dyn[];
+  constexpr uint32_t kBStage = NPAD * 128;
+  constexpr int kSB = b_stages_for(NPAD);
+  uint8_t* const smem_a = smem_dyn;
+  uint8_t* const smem_b = smem_dyn + kSA * kBlockBytes;
+  __shared__ __align__(8) uint64_t bar_sa_full[kSA];   // weight block landed (tx)
+  __shared__ __align__(8) uint64_t bar_sa_empty[kSA];  // converters done reading it (4)
+  __shared__ __align__(8) uint64_t bar_sb_full[kSB];   // B stage landed (tx)
+  __shared__ __align__(8) uint64_t bar_sb_empty[kSB];  // MMA done with it (commit)
+  __shared__ __align__(8) uint64_t bar_afull[kStages];  // TMEM A stage written (4)
+  __shared__ __align__(8) uint64_t bar_free[kStages];   // TMEM A stage consumed (commit)
   __shared__ __align__(8) uint64_t bar_dfull[2];
   __shared__ __align__(8) uint64_t bar_dfree[2];
   __shared__ uint32_t tmem_base_sh;
   __shared__ int last_flag;
 
-  constexpr uint32_t kBStage = NPAD * 128;
   constexpr uint32_t kLBO = (NPAD / 8) * 128;  // K-direction core-matrix stride
   constexpr uint32_t kSBO = 128;               // N-direction 8-row group stride
   constexpr int kDBufs = dbufs_for(NPAD);
@@ -185,8 +202,15 @@ __global__ void __launch_bounds__(kThreads, 2) tq_grouped_kernel(const __grid_co
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
+    for (int s = 0; s < kSA; ++s) {
+      tc::mbar_init(tc::smem_u32(&bar_sa_full[s]), 1);
+      tc::mbar_init(tc::smem_u32(&bar_sa_empty[s]), 4);
+    }
+    for (int s = 0; s < kSB; ++s) {
+      tc::mbar_init(tc::smem_u32(&bar_sb_full[s]), 1);
+      tc::mbar_init(tc::smem_u32(&bar_sb_empty[s]), 1);
+    }
     for (int s = 0; s < kStages; ++s) {
-      tc::mbar_init(tc::smem_u32(&bar_bfull[s]), 1);
       tc::mbar_init(tc::smem_u32(&bar_afull[s]), 4);
       tc::mbar_init(tc::smem_u32(&bar_free[s]), 1);
     }
@@ -196,7 +220,7 @@ __global__ void __launch_bounds__(kThreads, 2) tq_grouped_kernel(const __grid_co
     }
     tc::fence_barrier_init();
   }
-  if (warp == 5) tc::tmem_alloc(tc::smem_u32(&tmem_base_sh), kTmemCols);
+  if (warp == kWarpMma) tc::tmem_alloc(tc::smem_u32(&tmem_base_sh), kTmemCols);
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
@@ -208,60 +232,64 @@ __global__ void __launch_bounds__(kThreads, 2) tq_grouped_kernel(const __grid_co
     // ------------------------------------------------------ converters --
     const int r = threadIdx.x;
     const uint32_t lane_off = (uint32_t)(32 * warp) << 16;
-    Cursor ld, cs;
-    ld.start(b);
+    Cursor cs;
     cs.start(b);
-    uint4 buf[kPrefetch][2];
-#pragma unroll
-    for (int j = 0; j < kPrefetch; ++j) {
-      if (ld.valid(b)) {
-        const TqProblem& p = b.p[ld.it.prob];
-        const uint8_t* src =
-            p.codes + (ld.it.tile * p.n_chunks + ld.it.c0 + ld.chunk) * kBlockBytes + r * 16;
-        buf[j][0] = __ldg(reinterpret_cast<const uint4*>(src));
-        buf[j][1] = __ldg(reinterpret_cast<const uint4*>(src + 2048));
-        ld.advance(b);
-      }
-    }
     uint32_t gc = 0;
     while (cs.valid(b)) {
+      const uint32_t sa = gc % kSA;
+      ok = ok && tc::mbar_wait(tc::smem_u32(&bar_sa_full[sa]), (gc / kSA) & 1, b.err, 10);
+      uint4 v0 = make_uint4(0, 0, 0, 0), v1 = make_uint4(0, 0, 0, 0);
+      if (ok) {
+        const uint8_t* blk = smem_a + sa * kBlockBytes + r * 16;
+        v0 = *reinterpret_cast<const uint4*>(blk);
+        v1 = *reinterpret_cast<const uint4*>(blk + 2048);
+      }
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(tc::smem_u32(&bar_sa_empty[sa]));
+      const uint32_t wv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+      const uint32_t s = gc % kStages;
+      if (ok && gc >= kStages)
+        ok = tc::mbar_wait(tc::smem_u32(&bar_free[s]), ((gc / kStages) + 1) & 1, b.err, 11);
+      ok = __all_sync(0xffffffffu, ok);  // tcgen05.st below is warp-collective
+      tc::tc_fence_after();
 #pragma unroll
-      for (int j = 0; j < kPrefetch; ++j) {
-        if (!cs.valid(b)) break;
-        const uint32_t wv[8] = {buf[j][0].x, buf[j][0].y, buf[j][0].z, buf[j][0].w,
-                                buf[j][1].x, buf[j][1].y, buf[j][1].z, buf[j][1].w};
-        if (ld.valid(b)) {
-          const TqProblem& p = b.p[ld.it.prob];
-          const uint8_t* src =
-              p.codes + (ld.it.tile * p.n_chunks + ld.it.c0 + ld.chunk) * kBlockBytes + r * 16;
-          buf[j][0] = __ldg(reinterpret_cast<const uint4*>(src));
-          buf[j][1] = __ldg(reinterpret_cast<const uint4*>(src + 2048));
-          ld.advance(b);
-        }
-        const uint32_t s = gc % kStages;
-        if (ok && gc >= kStages)
-          ok = tc::mbar_wait(tc::smem_u32(&bar_free[s]), ((gc / kStages) + 1) & 1, b.err, 11);
-        ok = __all_sync(0xffffffffu, ok);  // tcgen05.st below is warp-collective
-        tc::tc_fence_after();
+      for (int h = 0; h < 2; ++h) {  // two halves of 64 codes: 16 TMEM columns each
+        uint32_t a[16];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {  // two halves of 64 codes: 16 TMEM columns each
-          uint32_t a[16];
+        for (int w = 0; w < 4; ++w)
 #pragma unroll
-          for (int w = 0; w < 4; ++w)
-#pragma unroll
-            for (int q = 0; q < 4; ++q) a[w * 4 + q] = (wv[h * 4 + w] >> (2 * q)) & 0x03030303u;
-          if (ok) tc::tmem_st_x16(tmem + lane_off + kACol0 + 32 * s + 16 * h, a);
-        }
-        tc::tmem_wait_st();
-        tc::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) tc::mbar_arrive(tc::smem_u32(&bar_afull[s]));
+          for (int q = 0; q < 4; ++q) a[w * 4 + q] = (wv[h * 4 + w] >> (2 * q)) & 0x03030303u;
+        if (ok) tc::tmem_st_x16(tmem + lane_off + kACol0 + 32 * s + 16 * h, a);
+      }
+      tc::tmem_wait_st();
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(tc::smem_u32(&bar_afull[s]));
+      ++gc;
+      cs.advance(b);
+    }
+  } else if (warp == kWarpLoadA) {
+    // ------------------------------------------- weight-block producer --
+    if (lane == 0) {
+      Cursor cs;
+      cs.start(b);
+      uint32_t gc = 0;
+      while (cs.valid(b) && ok) {
+        const TqProblem& p = b.p[cs.it.prob];
+        const uint32_t sa = gc % kSA;
+        if (gc >= kSA)
+          ok = tc::mbar_wait(tc::smem_u32(&bar_sa_empty[sa]), ((gc / kSA) + 1) & 1, b.err, 17);
+        if (!ok) break;
+        const uint32_t bar = tc::smem_u32(&bar_sa_full[sa]);
+        tc::mbar_arrive_expect_tx(bar, kBlockBytes);
+        const uint8_t* src = p.codes + (cs.it.tile * p.n_chunks + cs.it.c0 + cs.chunk) * kBlockBytes;
+        tc::bulk_g2s(tc::smem_u32(smem_a + sa * kBlockBytes), src, kBlockBytes, bar);
         ++gc;
         cs.advance(b);
       }
     }
-  } else if (warp == 4) {
-    // -------------------------------------------------------- producer --
+  } else if (warp == kWarpLoadB) {
+    // ------------------------------------------------ B-stage producer --
     if (lane == 0) {
       tc::pdl_wait();  // B is written by the preceding prep kernel
       Cursor cs;
@@ -269,20 +297,20 @@ __global__ void __launch_bounds__(kThreads, 2) tq_grouped_kernel(const __grid_co
       uint32_t gc = 0;
       while (cs.valid(b) && ok) {
         const TqProblem& p = b.p[cs.it.prob];
-        const uint32_t s = gc % kStages;
-        if (gc >= kStages)
-          ok = tc::mbar_wait(tc::smem_u32(&bar_free[s]), ((gc / kStages) + 1) & 1, b.err, 12);
+        const uint32_t sb = gc % kSB;
+        if (gc >= (uint32_t)kSB)
+          ok = tc::mbar_wait(tc::smem_u32(&bar_sb_empty[sb]), ((gc / kSB) + 1) & 1, b.err, 12);
         if (!ok) break;
-        const uint32_t bar = tc::smem_u32(&bar_bfull[s]);
+        const uint32_t bar = tc::smem_u32(&bar_sb_full[sb]);
         tc::mbar_arrive_expect_tx(bar, kBStage);
         const int8_t* src =
             p.bmat + ((int64_t)cs.it.pass * p.n_chunks + cs.it.c0 + cs.chunk) * kBStage;
-        tc::bulk_g2s(tc::smem_u32(smem_b + s * kBStage), src, kBStage, bar);
+        tc::bulk_g2s(tc::smem_u32(smem_b + sb * kBStage), src, kBStage, bar);
         ++gc;
         cs.advance(b);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == kWarpMma) {
     // ------------------------------------------------------ MMA issuer --
     if (lane == 0) {
       Cursor cs;
@@ -299,12 +327,12 @@ __global__ void __launch_bounds__(kThreads, 2) tq_grouped_kernel(const __grid_co
         bool item_done = false;
         while (!item_done) {
           const uint32_t s = gc % kStages;
-          const uint32_t par = (gc / kStages) & 1;
-          ok = tc::mbar_wait(tc::smem_u32(&bar_afull[s]), par, b.err, 14) &&
-               tc::mbar_wait(tc::smem_u32(&bar_bfull[s]), par, b.err, 15);
+          const uint32_t sb = gc % kSB;
+          ok = tc::mbar_wait(tc::smem_u32(&bar_afull[s]), (gc / kStages) & 1, b.err, 14) &&
+               tc::mbar_wait(tc::smem_u32(&bar_sb_full[sb]), (gc / kSB) & 1, b.err, 15);
           if (!ok) break;
           tc::tc_fence_after();
-          const uint32_t bst = tc::smem_u32(smem_b + s * kBStage);
+          const uint32_t bst = tc::smem_u32(smem_b + sb * kBStage);
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const uint64_t bd = tc::smem_desc(bst + j * 2 * kLBO, kLBO, kSBO);
@@ -312,6 +340,7 @@ __global__ void __launch_bounds__(kThreads, 2) tq_grouped_kernel(const __grid_co
             first = false;
           }
           tc::mma_commit(tc::smem_u32(&bar_free[s]));
+          tc::mma_commit(tc::smem_u32(&bar_sb_empty[sb]));
           ++gc;
           item_done = cs.advance(b);
         }
@@ -320,6 +349,7 @@ __global__ void __launch_bounds__(kThreads, 2) tq_grouped_kernel(const __grid_co
       }
     }
   } else {
+
     // -------------------------------------------------------- epilogue --
     const int sub = warp & 3;  // TMEM sub-partition this warp may access
     const int r = sub * 32 + lane;
@@ -405,7 +435,7 @@ __global__ void __launch_bounds__(kThreads, 2) tq_grouped_kernel(const __grid_co
 
   tc::tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kWarpMma) {
     tc::tc_fence_after();
     tc::tmem_dealloc(tmem, kTmemCols);
   }
@@ -525,12 +555,7 @@ int pick_npad(int64_t ncols) {
 
 template <int NPAD>
 int launch_grouped_t(const TqBatch& batch, int64_t grid, cudaStream_t s) {
-  // A CTA that takes all 512 TMEM columns asks for enough shared memory that
-  // a second one cannot be placed on its SM (it would wait in tcgen05.alloc).
-  const size_t smem = tmem_cols_for(NPAD) >= 512 ? (size_t)(120 * 1024) > (size_t)kStages * NPAD * 128
-                                                      ? (size_t)(120 * 1024)
-                                                      : (size_t)kStages * NPAD * 128
-                                                : (size_t)kStages * NPAD * 128;
+  const size_t smem = smem_bytes_for(NPAD);
   static bool attr_set = false;  // per template instance
   if (!attr_set) {
     FT_CUDA(cudaFuncSetAttribute(tq_grouped_kernel<NPAD>,
