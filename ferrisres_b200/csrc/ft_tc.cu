@@ -44,10 +44,24 @@
 namespace ft {
 namespace {
 
-constexpr int kStages = 4;   // TMEM A stages
+#ifndef FT_TMEM_STAGES
+#define FT_TMEM_STAGES 4
+#endif
+#ifndef FT_CONV_SETS
+#define FT_CONV_SETS 1
+#endif
+#ifndef FT_CONV_WAITS_B
+#define FT_CONV_WAITS_B 0
+#endif
+constexpr int kStagesMax = FT_TMEM_STAGES;  // TMEM A stages (at most; see a_stages_for)
 constexpr int kSA = 16;      // smem ring of 4 KB weight blocks (64 KB in flight per CTA)
-constexpr int kWarpLoadA = 4, kWarpLoadB = 5, kWarpMma = 6;  // warps 7-10: epilogue
-constexpr int kThreads = 352;
+// Converter warps come in sets of four (one warp per TMEM sub-partition);
+// set c converts the blocks gc with gc % kConvSets == c, so several blocks are
+// in conversion at once.
+constexpr int kConvSets = FT_CONV_SETS;
+constexpr int kConvWarps = 4 * kConvSets;
+constexpr int kWarpLoadA = kConvWarps, kWarpLoadB = kConvWarps + 1, kWarpMma = kConvWarps + 2;
+constexpr int kThreads = (kConvWarps + 7) * 32;
 constexpr int kMaxProblems = 64;
 
 struct TqProblem {
@@ -132,8 +146,12 @@ __host__ __device__ constexpr size_t smem_bytes_for(int npad) {
 }
 __host__ __device__ constexpr uint32_t dstride_for(int npad) { return (uint32_t)((npad + 31) / 32 * 32); }
 __host__ __device__ constexpr uint32_t acol0_for(int npad) { return dbufs_for(npad) * dstride_for(npad); }
+__host__ __device__ constexpr int a_stages_for(int npad) {
+  return (int)((512 - acol0_for(npad)) / 32) < kStagesMax ? (int)((512 - acol0_for(npad)) / 32)
+                                                           : kStagesMax;
+}
 __host__ __device__ constexpr uint32_t tmem_cols_for(int npad) {
-  uint32_t need = acol0_for(npad) + kStages * 32;
+  uint32_t need = acol0_for(npad) + a_stages_for(npad) * 32;
   uint32_t c = 32;
   while (c < need) c <<= 1;
   return c;
@@ -184,6 +202,7 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
   __shared__ __align__(8) uint64_t bar_sa_empty[kSA];  // converters done reading it (4)
   __shared__ __align__(8) uint64_t bar_sb_full[kSB];   // B stage landed (tx)
   __shared__ __align__(8) uint64_t bar_sb_empty[kSB];  // MMA done with it (commit)
+  constexpr int kStages = a_stages_for(NPAD);
   __shared__ __align__(8) uint64_t bar_afull[kStages];  // TMEM A stage written (4)
   __shared__ __align__(8) uint64_t bar_free[kStages];   // TMEM A stage consumed (commit)
   __shared__ __align__(8) uint64_t bar_dfull[2];
@@ -228,14 +247,20 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
   const uint32_t tmem = tmem_base_sh;
   bool ok = true;
 
-  if (warp < 4) {
+  if (warp < kConvWarps) {
     // ------------------------------------------------------ converters --
-    const int r = threadIdx.x;
-    const uint32_t lane_off = (uint32_t)(32 * warp) << 16;
+    const int set = warp >> 2, sub = warp & 3;
+    const int r = sub * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(32 * sub) << 16;
     Cursor cs;
     cs.start(b);
     uint32_t gc = 0;
     while (cs.valid(b)) {
+      if ((int)(gc % kConvSets) != set) {  // another set converts this block
+        ++gc;
+        cs.advance(b);
+        continue;
+      }
       const uint32_t sa = gc % kSA;
       ok = ok && tc::mbar_wait(tc::smem_u32(&bar_sa_full[sa]), (gc / kSA) & 1, b.err, 10);
       uint4 v0 = make_uint4(0, 0, 0, 0), v1 = make_uint4(0, 0, 0, 0);
@@ -262,6 +287,11 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
         if (ok) tc::tmem_st_x16(tmem + lane_off + kACol0 + 32 * s + 16 * h, a);
       }
       tc::tmem_wait_st();
+#if FT_CONV_WAITS_B
+      // Fold the B-stage wait into the converters: the MMA thread then waits
+      // on one barrier per block.
+      ok = ok && tc::mbar_wait(tc::smem_u32(&bar_sb_full[gc % kSB]), (gc / kSB) & 1, b.err, 18);
+#endif
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(tc::smem_u32(&bar_afull[s]));
@@ -313,6 +343,7 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
   } else if (warp == kWarpMma) {
     // ------------------------------------------------------ MMA issuer --
     if (lane == 0) {
+      const uint64_t bdesc0 = tc::smem_desc(tc::smem_u32(smem_b), kLBO, kSBO);
       Cursor cs;
       cs.start(b);
       uint32_t gc = 0, ic = 0;
@@ -328,15 +359,19 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
         while (!item_done) {
           const uint32_t s = gc % kStages;
           const uint32_t sb = gc % kSB;
-          ok = tc::mbar_wait(tc::smem_u32(&bar_afull[s]), (gc / kStages) & 1, b.err, 14) &&
-               tc::mbar_wait(tc::smem_u32(&bar_sb_full[sb]), (gc / kSB) & 1, b.err, 15);
+          ok = tc::mbar_wait(tc::smem_u32(&bar_afull[s]), (gc / kStages) & 1, b.err, 14);
+#if !FT_CONV_WAITS_B
+          ok = ok && tc::mbar_wait(tc::smem_u32(&bar_sb_full[sb]), (gc / kSB) & 1, b.err, 15);
+#endif
           if (!ok) break;
           tc::tc_fence_after();
-          const uint32_t bst = tc::smem_u32(smem_b + sb * kBStage);
+          // descriptor start address advances by 2*LBO bytes (>> 4) per K step
+          const uint64_t bd0 = bdesc0 + (uint64_t)((sb * kBStage) >> 4);
+          const uint32_t a0 = tmem + kACol0 + 32 * s;
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            const uint64_t bd = tc::smem_desc(bst + j * 2 * kLBO, kLBO, kSBO);
-            tc::mma_i8_ts(dcol, tmem + kACol0 + 32 * s + 8 * j, bd, kIdesc, first ? 0u : 1u);
+            tc::mma_i8_ts(dcol, a0 + 8 * j, bd0 + (uint64_t)((j * 2 * kLBO) >> 4), kIdesc,
+                          first ? 0u : 1u);
             first = false;
           }
           tc::mma_commit(tc::smem_u32(&bar_free[s]));
@@ -351,7 +386,8 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
   } else {
 
     // -------------------------------------------------------- epilogue --
-    const int sub = warp & 3;  // TMEM sub-partition this warp may access
+    // A warp may only touch the TMEM lanes of its sub-partition, warp id % 4.
+    const int sub = warp & 3;
     const int r = sub * 32 + lane;
     const uint32_t lane_off = (uint32_t)(32 * sub) << 16;
     bool waited_pdl = false;
@@ -631,7 +667,9 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
   char* wsb = static_cast<char*>(ctx->ws.ptr);
 
   // work decomposition and zero-initialised split-K scratch
-  const int64_t grid_target = ctx->num_sms;
+  // Two CTAs per SM when both fit in TMEM (each has its own MMA-issuing
+  // thread, which is what limits a small-N launch); one otherwise.
+  const int64_t grid_target = (int64_t)ctx->num_sms * (tmem_cols_for(npad) <= 256 ? 2 : 1);
   int64_t tiles_total = 0;
   for (int i = 0; i < n; ++i) tiles_total += ws[i]->n_tiles * passes;
   size_t zoff = 0;
