@@ -72,6 +72,7 @@ SIGNATURES = {
     "ft_ternary_matmul_bf16": [_p, _p, _i64, _p, _p, _p],
     "ft_ternary_matmul_f32_grouped": [_p, _i, _p, _i64, _p, _p, _p],
     "ft_ternary_matmul_i8_grouped": [_p, _i, _p, _i64, _p, _p, _p, _p],
+    "ft_ternary_matmul_f32_noalloc": [_p, _p, _i64, _p, _p, _p],
     "ft_quantize_absmax_i8_f32": [_p, _i64, _i64, _p, _p, _p, _p],
     "ft_quantize_absmax_i8_bf16": [_p, _i64, _i64, _p, _p, _p, _p],
     "ft_ternary_matmul_i8": [_p, _p, _i64, _p, _p, _p, _p],

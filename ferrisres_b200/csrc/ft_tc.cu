@@ -784,3 +784,145 @@ int launch_tc_matmul(ft_ctx* ctx, const ft_weight* w, int64_t seq, const void* x
 }
 
 }  // namespace ft
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of the fp32 matmul, for decode-sized calls.
+//
+// Some callers cannot let a library allocate device memory during a call: a
+// host that hands out all device memory itself (a serving engine with a fixed
+// arena, or an FFI contract that forbids hidden allocations on the hot path),
+// or a real-time loop that cannot take cudaMalloc's implicit device-wide
+// synchronisation.  This entry point runs the same two kernels as
+// ft_ternary_matmul_f32, but its scratch (activation operand, column sums,
+// token scales, split-K sums and tickets, error word) lives in the
+// file-scope array below, reserved in the library image on every GPU that
+// loads the library and held until the process exits.
+// ---------------------------------------------------------------------------
+namespace ft {
+namespace {
+constexpr int64_t kNaMaxSeq = 4;        // tokens per call (4 digit columns each -> NPAD 16)
+constexpr int64_t kNaMaxCols = 16384;
+constexpr int64_t kNaMaxRows = 16384;
+constexpr int kNaNpad = 16;
+constexpr size_t kNaBOff = 0;
+constexpr size_t kNaBBytes = (size_t)(kNaMaxCols / kChunkK) * kNaNpad * 128;        // 256 KiB
+constexpr size_t kNaColsumOff = kNaBOff + kNaBBytes;                                  // 16 x int32
+constexpr size_t kNaTokOff = kNaColsumOff + 256;                                      // 4 x double
+constexpr size_t kNaAccOff = kNaTokOff + 256;
+constexpr size_t kNaAccBytes = (size_t)(kNaMaxRows / kTileRows) * kNaNpad * kTileRows * 4;  // 1 MiB
+constexpr size_t kNaCntOff = kNaAccOff + kNaAccBytes;
+constexpr size_t kNaCntBytes = (size_t)(kNaMaxRows / kTileRows) * 4;
+constexpr size_t kNaErrOff = kNaCntOff + (kNaCntBytes + 255) / 256 * 256;
+constexpr size_t kNaBytes = kNaErrOff + 256;  // about 1.3 MB
+constexpr int kNaMaxDevices = 64;
+
+static void* g_na_ptr[kNaMaxDevices];  // device address of g_noalloc_scratch, per device
+}  // namespace
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNaBytes];
+
+namespace {
+// Looks up (once per device, with that device current) the device address of
+// the scratch array; host code must never pass the symbol itself to a kernel.
+int noalloc_scratch(int device, char** out) {
+  FT_CHECK(device >= 0 && device < kNaMaxDevices, FT_ERR_DEVICE, "device %d not supported", device);
+  if (g_na_ptr[device] == nullptr) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    FT_CHECK(e == cudaSuccess && p != nullptr, FT_ERR_GPU,
+             "cudaGetSymbolAddress of the no-alloc scratch failed: %s", cudaGetErrorString(e));
+    g_na_ptr[device] = p;
+  }
+  *out = static_cast<char*>(g_na_ptr[device]);
+  return FT_OK;
+}
+
+int launch_tc_noalloc(ft_ctx* ctx, const ft_weight* w, int64_t seq, const float* x, float* y,
+                      cudaStream_t s) {
+  char* zs = nullptr;
+  int st = noalloc_scratch(ctx->device, &zs);
+  if (st != FT_OK) return st;
+  // the split-K sums, tickets and error word must start at zero
+  FT_CUDA(cudaMemsetAsync(zs + kNaAccOff, 0, kNaBytes - kNaAccOff, s));
+
+  const int D = 4, npad = kNaNpad, tok_per_pass = npad / D;
+  static thread_local TqBatch batch;
+  memset(&batch, 0, sizeof(batch));
+  batch.nprob = 1;
+  batch.digits = D;
+  const int64_t grid_target = (int64_t)ctx->num_sms * (tmem_cols_for(npad) <= 256 ? 2 : 1);
+  TqProblem& p = batch.p[0];
+  int64_t want = (4 * grid_target + w->n_tiles - 1) / w->n_tiles;
+  if (want < 1) want = 1;
+  if (want > w->n_chunks) want = w->n_chunks;
+  p.cps = (int)ceil_div(w->n_chunks, want);
+  p.ksplit = (int)ceil_div(w->n_chunks, p.cps);
+  p.codes = w->codes;
+  p.row_scales = w->row_scales;
+  p.rows = w->rows;
+  p.n_tiles = w->n_tiles;
+  p.n_chunks = w->n_chunks;
+  p.bmat = reinterpret_cast<const int8_t*>(zs + kNaBOff);
+  p.colsum = reinterpret_cast<const int32_t*>(zs + kNaColsumOff);
+  p.tok_scale = reinterpret_cast<const double*>(zs + kNaTokOff);
+  p.sx = nullptr;
+  p.y = y;
+  p.ldy = w->rows;
+  p.seq = seq;
+  p.tok_per_pass = tok_per_pass;
+  p.passes = 1;
+  p.item_begin = 0;
+  p.acc = reinterpret_cast<int32_t*>(zs + kNaAccOff);
+  p.cnt = reinterpret_cast<int32_t*>(zs + kNaCntOff);
+  batch.total_items = w->n_tiles * p.ksplit;
+  batch.err = reinterpret_cast<int*>(zs + kNaErrOff);
+  ctx->err_flag = batch.err;
+
+  static thread_local PrepBatch pb;
+  memset(&pb, 0, sizeof(pb));
+  pb.nsrc = 1;
+  pb.xkind = 0;
+  pb.D = D;
+  pb.npad = npad;
+  pb.tok_per_pass = tok_per_pass;
+  pb.block_begin[0] = 0;
+  pb.block_begin[1] = tok_per_pass;
+  PrepSource& ps = pb.s[0];
+  ps.x = x;
+  ps.bmat = reinterpret_cast<int8_t*>(zs + kNaBOff);
+  ps.colsum = reinterpret_cast<int32_t*>(zs + kNaColsumOff);
+  ps.tok_scale = reinterpret_cast<double*>(zs + kNaTokOff);
+  ps.seq = seq;
+  ps.K = w->cols;
+  ps.n_chunks = w->n_chunks;
+  ps.passes = 1;
+  prep_b_kernel<<<tok_per_pass, 256, 0, s>>>(pb);
+  FT_LAUNCH_CHECK();
+  const int64_t grid = batch.total_items < grid_target ? batch.total_items : grid_target;
+  return launch_grouped_t<16>(batch, grid, s);
+}
+}  // namespace
+}  // namespace ft
+
+extern "C" int ft_ternary_matmul_f32_noalloc(ft_ctx* ctx, const ft_weight* w, int64_t seq,
+                                             const float* x_dev, float* y_dev, void* stream) {
+  using namespace ft;
+  FT_CHECK(ctx && w, FT_ERR_SHAPE, "null context or weight");
+  FT_CHECK(seq >= 0, FT_ERR_SHAPE, "seq must be >= 0");
+  FT_CHECK(seq == 0 || (x_dev && y_dev), FT_ERR_SHAPE, "null activation/output pointer");
+  FT_CHECK(w->device == ctx->device, FT_ERR_DEVICE, "weight lives on device %d, context on %d",
+           w->device, ctx->device);
+  FT_CHECK(seq <= kNaMaxSeq && w->rows <= kNaMaxRows && w->cols <= kNaMaxCols,
+           FT_ERR_UNSUPPORTED,
+           "no-alloc matmul limits are seq <= %lld, rows <= %lld, cols <= %lld (got seq %lld, "
+           "weight [%lld, %lld]); use ft_ternary_matmul_f32 for larger shapes",
+           (long long)kNaMaxSeq, (long long)kNaMaxRows, (long long)kNaMaxCols, (long long)seq,
+           (long long)w->rows, (long long)w->cols);
+  if (seq == 0) return FT_OK;
+  int prev = -1;
+  if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+  if (prev != ctx->device) FT_CUDA(cudaSetDevice(ctx->device));
+  const int st = launch_tc_noalloc(ctx, w, seq, x_dev, y_dev, static_cast<cudaStream_t>(stream));
+  if (prev >= 0 && prev != ctx->device) cudaSetDevice(prev);
+  return st;
+}

@@ -107,6 +107,23 @@ int ft_ternary_matmul_f32_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws
 int ft_ternary_matmul_i8_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t seq,
                                  const int8_t* const* qs_dev, const float* const* sxs_dev,
                                  float* const* ys_dev, void* stream);
+/* Allocation-free form of ft_ternary_matmul_f32 for decode-sized calls.  No
+ * counterpart in the reference.  It is for callers that must not let a library
+ * allocate device memory inside a call: a host that owns all device memory
+ * itself (a serving engine with a fixed arena, or an FFI contract that forbids
+ * hidden allocations on the hot path), or a real-time loop that cannot take
+ * cudaMalloc's implicit device-wide synchronisation.  It calls no cudaMalloc or
+ * cudaFree: its scratch is one ~1.3 MB array reserved in the library image on
+ * every GPU that loads the library, held until the process exits.  Limits:
+ * seq <= 4, w rows <= 16384, w cols <= 16384; larger shapes return
+ * FT_ERR_UNSUPPORTED.  The context and weight are created beforehand as usual.
+ * The first call on a device looks up the array's device address, so make
+ * that first call before any stream capture.  All calls share the array (each
+ * clears what must start at zero), so calls that overlap on the GPU -- other
+ * streams, other host threads, other contexts on the same device -- race:
+ * order them. */
+int ft_ternary_matmul_f32_noalloc(ft_ctx* ctx, const ft_weight* w, int64_t seq, const float* x_dev,
+                                  float* y_dev, void* stream);
 /* Per-token absmax int8 quantizer: sx[s] = absmax/127 (1 when absmax == 0),
  * q = clamp(round_half_away(x * (127/absmax)), -127, 127).  No reference
  * counterpart (the reference has no int8 activation path); the formula is
