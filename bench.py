@@ -344,6 +344,94 @@ def run_reference(args, ws, rank):
     }
 
 
+# ------------------------------------------------------------- cfg2 GEMM --
+G_M, G_K, G_N = 512, 4096, 11008
+G_OPS = 2 * G_M * G_K * G_N
+
+
+def run_gemm(args, ws, rank, local):
+    """int8 prefill GEMM (bf16 x -> per-token absmax int8 ->
+    exact int32 ternary matmul -> f32), W [11008, 4096] with P(0)=0.5.  One step
+    = quantize + matmul; weights rotate over copies totalling > 2x L2."""
+    import torch
+
+    from ferrisres_b200 import _lib, gpu
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    n_copies = max(3, -(-2 * L2_BYTES // (G_N * G_K // 4)))
+    weights = []
+    g = torch.Generator(device=device)
+    import ctypes as C
+    from ferrisres_b200._lib import call
+    ctx = gpu.get_context(local)
+    for i in range(n_copies):
+        g.manual_seed(100 + i)
+        u = torch.rand(G_N * G_K, generator=g, device=device)
+        codes = torch.where(u < 0.25, 0, torch.where(u < 0.75, 1, 2)).to(torch.int64)
+        words = (codes.view(-1, 16) << torch.arange(0, 32, 2, device=device)).sum(dim=1)
+        words = torch.where(words >= 2**31, words - 2**32, words).to(torch.int32).contiguous()
+        scales = (torch.rand(G_N, generator=g, device=device) * 0.09 + 0.01).contiguous()
+        h = C.c_void_p()
+        call("ft_weight_from_device_u32", ctx.handle, C.c_void_p(words.data_ptr()), G_N, G_K,
+             C.c_void_p(scales.data_ptr()), C.c_void_p(torch.cuda.current_stream().cuda_stream),
+             C.byref(h))
+        torch.cuda.synchronize()
+        weights.append(gpu.DeviceTernaryWeight(h, G_N, G_K, ctx))
+        del u, codes, words
+    g.manual_seed(7)
+    xb = torch.randn(G_M, G_K, generator=g, device=device).to(torch.bfloat16)
+    y = torch.empty(G_M, G_N, device=device)
+    stream = torch.cuda.Stream(device=device)
+
+    def step(i):
+        q, sx = gpu.quantize_absmax_i8(xb)
+        weights[i % n_copies].matmul_i8(q, sx, out=y)
+
+    with torch.cuda.stream(stream):
+        for i in range(max(args.warmup, 3)):
+            step(i)
+    stream.synchronize()
+    launches0 = _lib.lib().ft_launch_counter()
+    with torch.cuda.stream(stream):
+        step(0)
+    per_step = _lib.lib().ft_launch_counter() - launches0
+    stream.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for i in range(args.steps):
+            step(i)
+        e1.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    sec = e0.elapsed_time(e1) / 1e3
+    tops = args.steps * G_OPS / sec / 1e12
+    bf16_peak = None
+    try:
+        bf16_peak = float(json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["bf16_tflops"])
+    except Exception:
+        pass
+    peak = 2 * (bf16_peak or 1590.0)
+    return {
+        "metric": "ternary int8 prefill GEMM TOPS", "value": round(tops, 2), "unit": "TOPS",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": sec * 1e3 / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded, generated on device)",
+        "config": {"workload": "cfg2 prefill GEMM M=512 K=4096 N=11008, bf16 x -> absmax int8",
+                   "weight_copies": n_copies, "l2": "weights rotate over copies > 2x L2"},
+        "roofline": {"bound": "tensor", "achieved": round(tops, 2), "peak": round(peak, 1),
+                     "unit": "TOP/s", "frac": round(tops / peak, 4),
+                     "peak_source": "2 x measured bf16 dense (int8 dense rate is twice bf16 on B200)"
+                                    if bf16_peak else "2 x fallback bf16",
+                     "traffic": None},
+        "gpu_launches": int(per_step * args.steps),
+        "clocks": clocks,
+    }
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -353,11 +441,15 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--group", type=int, default=16, help="GEMVs per launch (1..64)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--workload", choices=["gemv", "gemm_cfg2"], default="gemv",
+                    help="gemv = the headline cfg0 line; gemm_cfg2 = the int8 prefill GEMM")
     args = ap.parse_args()
     ws, rank, local = dist_env()
     if args.gpus != ws and ws > 1:
         print(f"warning: --gpus {args.gpus} but WORLD_SIZE={ws}", file=sys.stderr)
-    if args.impl == "reference":
+    if args.workload == "gemm_cfg2" and args.impl == "ours":
+        res = run_gemm(args, ws, rank, local)
+    elif args.impl == "reference":
         res = run_reference(args, ws, rank)
     else:
         res = run_ours(args, ws, rank, local)

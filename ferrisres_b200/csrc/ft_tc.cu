@@ -44,24 +44,10 @@
 namespace ft {
 namespace {
 
-#ifndef FT_TMEM_STAGES
-#define FT_TMEM_STAGES 4
-#endif
-#ifndef FT_CONV_SETS
-#define FT_CONV_SETS 1
-#endif
-#ifndef FT_CONV_WAITS_B
-#define FT_CONV_WAITS_B 0
-#endif
-constexpr int kStagesMax = FT_TMEM_STAGES;  // TMEM A stages (at most; see a_stages_for)
-constexpr int kSA = 16;      // smem ring of 4 KB weight blocks (64 KB in flight per CTA)
-// Converter warps come in sets of four (one warp per TMEM sub-partition);
-// set c converts the blocks gc with gc % kConvSets == c, so several blocks are
-// in conversion at once.
-constexpr int kConvSets = FT_CONV_SETS;
-constexpr int kConvWarps = 4 * kConvSets;
-constexpr int kWarpLoadA = kConvWarps, kWarpLoadB = kConvWarps + 1, kWarpMma = kConvWarps + 2;
-constexpr int kThreads = (kConvWarps + 7) * 32;
+constexpr int kSA = 16;  // smem ring of 4 KB weight blocks (64 KB in flight per CTA)
+constexpr int kSK = 2;   // K chunks per super-stage: one barrier wait / commit per 8 KB of weights
+constexpr int kWarpLoadA = 4, kWarpLoadB = 5, kWarpMma = 6;  // warps 0-3 convert, 7-10 epilogue
+constexpr int kThreads = 11 * 32;
 constexpr int kMaxProblems = 64;
 
 struct TqProblem {
@@ -134,27 +120,45 @@ struct Cursor {
     if (item < b.total_items) it = decode_item(b, item);
     return true;
   }
+  // chunks in the super-stage that starts at `chunk` (never spans two items)
+  __device__ __forceinline__ int ss_len() const {
+    return it.nch - chunk < kSK ? it.nch - chunk : kSK;
+  }
+  __device__ __forceinline__ bool advance_ss(const TqBatch& b) {
+    chunk += ss_len();
+    if (chunk < it.nch) return false;
+    chunk = 0;
+    item += gridDim.x;
+    if (item < b.total_items) it = decode_item(b, item);
+    return true;
+  }
 };
 
 __host__ __device__ constexpr int dbufs_for(int npad) { return npad <= 128 ? 2 : 1; }
-// B-operand smem stages: about 96 KB, between 2 and 16 stages.
-__host__ __device__ constexpr int b_stages_for(int npad) {
-  return (98304 / (npad * 128)) < 2 ? 2 : (98304 / (npad * 128)) > 16 ? 16 : (98304 / (npad * 128));
-}
-__host__ __device__ constexpr size_t smem_bytes_for(int npad) {
-  return (size_t)kSA * 4096 + (size_t)b_stages_for(npad) * npad * 128;
-}
 __host__ __device__ constexpr uint32_t dstride_for(int npad) { return (uint32_t)((npad + 31) / 32 * 32); }
 __host__ __device__ constexpr uint32_t acol0_for(int npad) { return dbufs_for(npad) * dstride_for(npad); }
-__host__ __device__ constexpr int a_stages_for(int npad) {
-  return (int)((512 - acol0_for(npad)) / 32) < kStagesMax ? (int)((512 - acol0_for(npad)) / 32)
-                                                           : kStagesMax;
+// TMEM A super-stages (kSK*32 columns each) after the accumulators: within a
+// 256-column allocation (two CTAs per SM) when at least two fit, else 512.
+__host__ __device__ constexpr int ss_fit(int budget, int npad) {
+  return (budget - (int)acol0_for(npad)) / (kSK * 32);
+}
+__host__ __device__ constexpr int a_ss_for(int npad) {
+  return ss_fit(256, npad) >= 2 ? (ss_fit(256, npad) > 4 ? 4 : ss_fit(256, npad))
+                                : (ss_fit(512, npad) > 4 ? 4 : ss_fit(512, npad));
 }
 __host__ __device__ constexpr uint32_t tmem_cols_for(int npad) {
-  uint32_t need = acol0_for(npad) + a_stages_for(npad) * 32;
-  uint32_t c = 32;
-  while (c < need) c <<= 1;
-  return c;
+  return acol0_for(npad) + a_ss_for(npad) * kSK * 32 <= 256 ? 256u : 512u;
+}
+// B-operand smem super-stages, between 2 and 8: within ~46 KB when two CTAs
+// share an SM (256 TMEM columns each), else within ~96 KB.
+__host__ __device__ constexpr int b_ss_raw(int npad) {
+  return (tmem_cols_for(npad) <= 256 ? 47104 : 98304) / (kSK * npad * 128);
+}
+__host__ __device__ constexpr int b_ss_for(int npad) {
+  return b_ss_raw(npad) < 2 ? 2 : b_ss_raw(npad) > 8 ? 8 : b_ss_raw(npad);
+}
+__host__ __device__ constexpr size_t smem_bytes_for(int npad) {
+  return (size_t)kSA * 4096 + (size_t)b_ss_for(npad) * kSK * npad * 128;
 }
 
 __device__ __forceinline__ void named_sync_epilogue() {
@@ -192,19 +196,20 @@ __device__ __forceinline__ void epilogue_group(const TqProblem& p, int digits, i
 
 template <int NPAD>
 __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_constant__ TqBatch b) {
-  // dynamic smem: [SA weight blocks of 4096 B][SB B-operand stages of NPAD*128 B]
+  // dynamic smem: [kSA weight blocks of 4096 B][kSBS B super-stages of kSK*NPAD*128 B]
   extern __shared__ __align__(1024) uint8_t smem_dyn[];
-  constexpr uint32_t kBStage = NPAD * 128;
-  constexpr int kSB = b_stages_for(NPAD);
+  constexpr uint32_t kBStage = NPAD * 128;       // B bytes per chunk
+  constexpr uint32_t kBSuper = kSK * kBStage;    // B bytes per super-stage
+  constexpr int kSBS = b_ss_for(NPAD);
+  constexpr int kSS = a_ss_for(NPAD);
   uint8_t* const smem_a = smem_dyn;
   uint8_t* const smem_b = smem_dyn + kSA * kBlockBytes;
-  __shared__ __align__(8) uint64_t bar_sa_full[kSA];   // weight block landed (tx)
-  __shared__ __align__(8) uint64_t bar_sa_empty[kSA];  // converters done reading it (4)
-  __shared__ __align__(8) uint64_t bar_sb_full[kSB];   // B stage landed (tx)
-  __shared__ __align__(8) uint64_t bar_sb_empty[kSB];  // MMA done with it (commit)
-  constexpr int kStages = a_stages_for(NPAD);
-  __shared__ __align__(8) uint64_t bar_afull[kStages];  // TMEM A stage written (4)
-  __shared__ __align__(8) uint64_t bar_free[kStages];   // TMEM A stage consumed (commit)
+  __shared__ __align__(8) uint64_t bar_sa_full[kSA];    // weight block landed (tx)
+  __shared__ __align__(8) uint64_t bar_sa_empty[kSA];   // converters done reading it (4)
+  __shared__ __align__(8) uint64_t bar_sb_full[kSBS];   // B super-stage landed (tx)
+  __shared__ __align__(8) uint64_t bar_sb_empty[kSBS];  // MMA done with it (commit)
+  __shared__ __align__(8) uint64_t bar_afull[kSS];      // TMEM A super-stage written, B landed (4)
+  __shared__ __align__(8) uint64_t bar_free[kSS];       // TMEM A super-stage consumed (commit)
   __shared__ __align__(8) uint64_t bar_dfull[2];
   __shared__ __align__(8) uint64_t bar_dfree[2];
   __shared__ uint32_t tmem_base_sh;
@@ -225,11 +230,11 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
       tc::mbar_init(tc::smem_u32(&bar_sa_full[s]), 1);
       tc::mbar_init(tc::smem_u32(&bar_sa_empty[s]), 4);
     }
-    for (int s = 0; s < kSB; ++s) {
+    for (int s = 0; s < kSBS; ++s) {
       tc::mbar_init(tc::smem_u32(&bar_sb_full[s]), 1);
       tc::mbar_init(tc::smem_u32(&bar_sb_empty[s]), 1);
     }
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < kSS; ++s) {
       tc::mbar_init(tc::smem_u32(&bar_afull[s]), 4);
       tc::mbar_init(tc::smem_u32(&bar_free[s]), 1);
     }
@@ -247,97 +252,105 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
   const uint32_t tmem = tmem_base_sh;
   bool ok = true;
 
-  if (warp < kConvWarps) {
+  if (warp < 4) {
     // ------------------------------------------------------ converters --
-    const int set = warp >> 2, sub = warp & 3;
-    const int r = sub * 32 + lane;
-    const uint32_t lane_off = (uint32_t)(32 * sub) << 16;
+    const int r = threadIdx.x;  // warp w may only touch TMEM lanes 32w..32w+31
+    const uint32_t lane_off = (uint32_t)(32 * warp) << 16;
     Cursor cs;
     cs.start(b);
-    uint32_t gc = 0;
+    uint32_t gb = 0, gs = 0;  // weight-block and super-stage counters
     while (cs.valid(b)) {
-      if ((int)(gc % kConvSets) != set) {  // another set converts this block
-        ++gc;
-        cs.advance(b);
-        continue;
+      const int n = cs.ss_len();
+      uint32_t wv[kSK][8];
+#pragma unroll
+      for (int j = 0; j < kSK; ++j) {
+        if (j < n) {
+          const uint32_t sa = gb % kSA;
+          ok = ok && tc::mbar_wait(tc::smem_u32(&bar_sa_full[sa]), (gb / kSA) & 1, b.err, 10);
+          uint4 v0 = make_uint4(0, 0, 0, 0), v1 = make_uint4(0, 0, 0, 0);
+          if (ok) {
+            const uint8_t* blk = smem_a + sa * kBlockBytes + r * 16;
+            v0 = *reinterpret_cast<const uint4*>(blk);
+            v1 = *reinterpret_cast<const uint4*>(blk + 2048);
+          }
+          __syncwarp();
+          if (lane == 0) tc::mbar_arrive(tc::smem_u32(&bar_sa_empty[sa]));
+          wv[j][0] = v0.x; wv[j][1] = v0.y; wv[j][2] = v0.z; wv[j][3] = v0.w;
+          wv[j][4] = v1.x; wv[j][5] = v1.y; wv[j][6] = v1.z; wv[j][7] = v1.w;
+          ++gb;
+        }
       }
-      const uint32_t sa = gc % kSA;
-      ok = ok && tc::mbar_wait(tc::smem_u32(&bar_sa_full[sa]), (gc / kSA) & 1, b.err, 10);
-      uint4 v0 = make_uint4(0, 0, 0, 0), v1 = make_uint4(0, 0, 0, 0);
-      if (ok) {
-        const uint8_t* blk = smem_a + sa * kBlockBytes + r * 16;
-        v0 = *reinterpret_cast<const uint4*>(blk);
-        v1 = *reinterpret_cast<const uint4*>(blk + 2048);
-      }
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(tc::smem_u32(&bar_sa_empty[sa]));
-      const uint32_t wv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-      const uint32_t s = gc % kStages;
-      if (ok && gc >= kStages)
-        ok = tc::mbar_wait(tc::smem_u32(&bar_free[s]), ((gc / kStages) + 1) & 1, b.err, 11);
+      const uint32_t s = gs % kSS;
+      if (ok && gs >= (uint32_t)kSS)
+        ok = tc::mbar_wait(tc::smem_u32(&bar_free[s]), ((gs / kSS) + 1) & 1, b.err, 11);
       ok = __all_sync(0xffffffffu, ok);  // tcgen05.st below is warp-collective
       tc::tc_fence_after();
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {  // two halves of 64 codes: 16 TMEM columns each
-        uint32_t a[16];
+      for (int j = 0; j < kSK; ++j) {
+        if (j < n) {
 #pragma unroll
-        for (int w = 0; w < 4; ++w)
+          for (int h = 0; h < 2; ++h) {  // two halves of 64 codes: 16 TMEM columns each
+            uint32_t a[16];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) a[w * 4 + q] = (wv[h * 4 + w] >> (2 * q)) & 0x03030303u;
-        if (ok) tc::tmem_st_x16(tmem + lane_off + kACol0 + 32 * s + 16 * h, a);
+            for (int w = 0; w < 4; ++w)
+#pragma unroll
+              for (int q = 0; q < 4; ++q) a[w * 4 + q] = (wv[j][h * 4 + w] >> (2 * q)) & 0x03030303u;
+            if (ok) tc::tmem_st_x16(tmem + lane_off + kACol0 + (s * kSK + j) * 32 + 16 * h, a);
+          }
+        }
       }
       tc::tmem_wait_st();
-#if FT_CONV_WAITS_B
-      // Fold the B-stage wait into the converters: the MMA thread then waits
-      // on one barrier per block.
-      ok = ok && tc::mbar_wait(tc::smem_u32(&bar_sb_full[gc % kSB]), (gc / kSB) & 1, b.err, 18);
-#endif
+      // The B super-stage is waited here too, so the MMA thread waits on one
+      // barrier per super-stage.
+      ok = ok && tc::mbar_wait(tc::smem_u32(&bar_sb_full[gs % kSBS]), (gs / kSBS) & 1, b.err, 18);
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(tc::smem_u32(&bar_afull[s]));
-      ++gc;
-      cs.advance(b);
+      ++gs;
+      cs.advance_ss(b);
     }
   } else if (warp == kWarpLoadA) {
     // ------------------------------------------- weight-block producer --
     if (lane == 0) {
       Cursor cs;
       cs.start(b);
-      uint32_t gc = 0;
+      uint32_t gb = 0;
       while (cs.valid(b) && ok) {
         const TqProblem& p = b.p[cs.it.prob];
-        const uint32_t sa = gc % kSA;
-        if (gc >= kSA)
-          ok = tc::mbar_wait(tc::smem_u32(&bar_sa_empty[sa]), ((gc / kSA) + 1) & 1, b.err, 17);
+        const uint32_t sa = gb % kSA;
+        if (gb >= kSA)
+          ok = tc::mbar_wait(tc::smem_u32(&bar_sa_empty[sa]), ((gb / kSA) + 1) & 1, b.err, 17);
         if (!ok) break;
         const uint32_t bar = tc::smem_u32(&bar_sa_full[sa]);
         tc::mbar_arrive_expect_tx(bar, kBlockBytes);
         const uint8_t* src = p.codes + (cs.it.tile * p.n_chunks + cs.it.c0 + cs.chunk) * kBlockBytes;
         tc::bulk_g2s(tc::smem_u32(smem_a + sa * kBlockBytes), src, kBlockBytes, bar);
-        ++gc;
+        ++gb;
         cs.advance(b);
       }
     }
   } else if (warp == kWarpLoadB) {
-    // ------------------------------------------------ B-stage producer --
+    // ------------------------------------------- B super-stage producer --
     if (lane == 0) {
       tc::pdl_wait();  // B is written by the preceding prep kernel
       Cursor cs;
       cs.start(b);
-      uint32_t gc = 0;
+      uint32_t gs = 0;
       while (cs.valid(b) && ok) {
         const TqProblem& p = b.p[cs.it.prob];
-        const uint32_t sb = gc % kSB;
-        if (gc >= (uint32_t)kSB)
-          ok = tc::mbar_wait(tc::smem_u32(&bar_sb_empty[sb]), ((gc / kSB) + 1) & 1, b.err, 12);
+        const uint32_t n = (uint32_t)cs.ss_len();
+        const uint32_t sb = gs % kSBS;
+        if (gs >= (uint32_t)kSBS)
+          ok = tc::mbar_wait(tc::smem_u32(&bar_sb_empty[sb]), ((gs / kSBS) + 1) & 1, b.err, 12);
         if (!ok) break;
         const uint32_t bar = tc::smem_u32(&bar_sb_full[sb]);
-        tc::mbar_arrive_expect_tx(bar, kBStage);
+        tc::mbar_arrive_expect_tx(bar, n * kBStage);
+        // the super-stage's chunks are contiguous in the prepared operand
         const int8_t* src =
             p.bmat + ((int64_t)cs.it.pass * p.n_chunks + cs.it.c0 + cs.chunk) * kBStage;
-        tc::bulk_g2s(tc::smem_u32(smem_b + sb * kBStage), src, kBStage, bar);
-        ++gc;
-        cs.advance(b);
+        tc::bulk_g2s(tc::smem_u32(smem_b + sb * kBSuper), src, n * kBStage, bar);
+        ++gs;
+        cs.advance_ss(b);
       }
     }
   } else if (warp == kWarpMma) {
@@ -346,7 +359,7 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
       const uint64_t bdesc0 = tc::smem_desc(tc::smem_u32(smem_b), kLBO, kSBO);
       Cursor cs;
       cs.start(b);
-      uint32_t gc = 0, ic = 0;
+      uint32_t gs = 0, ic = 0;
       while (cs.valid(b) && ok) {
         const uint32_t d = ic % kDBufs;
         if (ic >= (uint32_t)kDBufs)
@@ -357,34 +370,36 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
         bool first = true;
         bool item_done = false;
         while (!item_done) {
-          const uint32_t s = gc % kStages;
-          const uint32_t sb = gc % kSB;
-          ok = tc::mbar_wait(tc::smem_u32(&bar_afull[s]), (gc / kStages) & 1, b.err, 14);
-#if !FT_CONV_WAITS_B
-          ok = ok && tc::mbar_wait(tc::smem_u32(&bar_sb_full[sb]), (gc / kSB) & 1, b.err, 15);
-#endif
+          const int n = cs.ss_len();
+          const uint32_t s = gs % kSS;
+          const uint32_t sb = gs % kSBS;
+          ok = tc::mbar_wait(tc::smem_u32(&bar_afull[s]), (gs / kSS) & 1, b.err, 14);
           if (!ok) break;
           tc::tc_fence_after();
-          // descriptor start address advances by 2*LBO bytes (>> 4) per K step
-          const uint64_t bd0 = bdesc0 + (uint64_t)((sb * kBStage) >> 4);
-          const uint32_t a0 = tmem + kACol0 + 32 * s;
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            tc::mma_i8_ts(dcol, a0 + 8 * j, bd0 + (uint64_t)((j * 2 * kLBO) >> 4), kIdesc,
-                          first ? 0u : 1u);
-            first = false;
+          for (int j = 0; j < kSK; ++j) {
+            if (j < n) {
+              // descriptor start address advances by (bytes >> 4)
+              const uint64_t bdj = bdesc0 + (uint64_t)((sb * kBSuper + j * kBStage) >> 4);
+              const uint32_t aj = tmem + kACol0 + (s * kSK + j) * 32;
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                tc::mma_i8_ts(dcol, aj + 8 * k, bdj + (uint64_t)((k * 2 * kLBO) >> 4), kIdesc,
+                              first ? 0u : 1u);
+                first = false;
+              }
+            }
           }
           tc::mma_commit(tc::smem_u32(&bar_free[s]));
           tc::mma_commit(tc::smem_u32(&bar_sb_empty[sb]));
-          ++gc;
-          item_done = cs.advance(b);
+          ++gs;
+          item_done = cs.advance_ss(b);
         }
         tc::mma_commit(tc::smem_u32(&bar_dfull[d]));
         ++ic;
       }
     }
   } else {
-
     // -------------------------------------------------------- epilogue --
     // A warp may only touch the TMEM lanes of its sub-partition, warp id % 4.
     const int sub = warp & 3;
@@ -581,11 +596,16 @@ __global__ void __launch_bounds__(256) prep_b_kernel(const __grid_constant__ Pre
   }
 }
 
+#ifndef FT_MAX_NPAD
+#define FT_MAX_NPAD 128
+#endif
+// Column-pass width.  Wide problems use 128-column passes: two TMEM
+// accumulators then fit, so a tile's epilogue overlaps the next tile's MMAs.
 int pick_npad(int64_t ncols) {
   if (ncols <= 16) return 16;
   if (ncols <= 32) return 32;
   if (ncols <= 64) return 64;
-  if (ncols <= 128) return 128;
+  if (ncols <= 128 || FT_MAX_NPAD <= 128) return 128;
   return 256;
 }
 
@@ -682,8 +702,12 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
   for (int i = 0; i < n; ++i) {
     const ft_weight* w = ws[i];
     TqProblem& p = batch.p[i];
-    // Split K only when the group has too few tiles to give every SM work.
-    int64_t want = (4 * grid_target + tiles_total - 1) / tiles_total;
+    // Split K only when the group has too few tiles to give every CTA work
+    // (narrow passes: aim at ~4 items per CTA; wide passes, whose split-K
+    // partials are costly to combine: only when tiles are fewer than CTAs/2).
+    int64_t want = npad < 128 ? (4 * grid_target + tiles_total - 1) / tiles_total
+                   : (2 * tiles_total >= grid_target ? 1
+                                                     : (grid_target + tiles_total - 1) / tiles_total);
     if (want < 1) want = 1;
     if (want > w->n_chunks) want = w->n_chunks;
     p.cps = (int)ceil_div(w->n_chunks, want);
