@@ -67,6 +67,9 @@ SIGNATURES = {
     "ft_weight_upload_packed_u32": [_p, _p, _i64, _i64, _p, _p],
     "ft_weight_from_device_u32": [_p, _p, _i64, _i64, _p, _p, _p],
     "ft_weight_destroy": [_p],
+    "ft_sparse_upload_host": [_p, _p, _p, _i64, _i64, _p, _p],
+    "ft_sparse_upload_wgsl": [_p, _p, _i64, _i64, _p, _p],
+    "ft_gpu_sparse_ternary_matmul": [_p, _p, C.c_float, _p, _sz, _sz, _sz, _p],
     "ft_weight_info": [_p, _p, _p, _p],
     "ft_ternary_matmul_f32": [_p, _p, _i64, _p, _p, _p],
     "ft_ternary_matmul_bf16": [_p, _p, _i64, _p, _p, _p],

@@ -87,18 +87,21 @@ struct DeviceGuard {
   }
 };
 
-static int alloc_weight(ft_ctx* ctx, int64_t rows, int64_t cols, ft_weight** out) {
+static int alloc_weight(ft_ctx* ctx, int64_t rows, int64_t cols, ft_weight** out,
+                        int format = 0) {
   FT_CHECK(ctx && out, FT_ERR_SHAPE, "null argument");
   FT_CHECK(rows > 0 && cols > 0, FT_ERR_SHAPE, "weight shape [%lld, %lld] must be positive",
            (long long)rows, (long long)cols);
   ft_weight* w = new (std::nothrow) ft_weight();
   FT_CHECK(w, FT_ERR_OOM, "host allocation failed");
   w->device = ctx->device;
+  w->format = format;
   w->rows = rows;
   w->cols = cols;
   w->n_tiles = ceil_div(rows, kTileRows);
   w->n_chunks = ceil_div(cols, kChunkK);
-  size_t code_bytes = (size_t)(w->n_tiles * w->n_chunks) * kBlockBytes;
+  size_t code_bytes =
+      (size_t)(w->n_tiles * w->n_chunks) * (format == 1 ? kSparseBlockBytes : kBlockBytes);
   size_t scale_bytes = (size_t)(w->n_tiles * kTileRows) * sizeof(float);
   cudaError_t e = cudaMalloc(&w->codes, code_bytes);
   if (e == cudaSuccess) e = cudaMalloc(&w->row_scales, scale_bytes);
@@ -240,6 +243,79 @@ int ft_weight_from_device_u32(ft_ctx* ctx, const uint32_t* words_dev, int64_t ro
   return FT_OK;
 }
 
+int ft_sparse_upload_host(ft_ctx* ctx, const uint8_t* patterns_host, const uint8_t* signs_host,
+                          int64_t rows, int64_t cols, const float* row_scales_host,
+                          ft_weight** out) {
+  FT_CHECK(patterns_host && signs_host && row_scales_host, FT_ERR_SHAPE, "null host buffer");
+  FT_CHECK(cols > 0 && cols % 4 == 0, FT_ERR_SHAPE,
+           "cols must be a positive multiple of 4 for 2:4 sparsity, got %lld", (long long)cols);
+  DeviceGuard g(ctx ? ctx->device : 0);
+  ft_weight* w = nullptr;
+  int st = alloc_weight(ctx, rows, cols, &w, 1);
+  if (st != FT_OK) return st;
+  const size_t ng = (size_t)(rows * cols / 4);
+  const size_t pb = (ng + 1) / 2, sb = (ng + 3) / 4;
+  uint8_t* staging = nullptr;
+  cudaStream_t s = ctx->host_stream;
+  cudaError_t e = cudaMalloc(&staging, pb + sb);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(staging, patterns_host, pb, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(staging + pb, signs_host, sb, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess) st = launch_repack_sparse_host(staging, staging + pb, rows, cols, w, s);
+  if (e == cudaSuccess && st == FT_OK) st = finish_scales(w, row_scales_host, true, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (staging) cudaFree(staging);
+  if (e != cudaSuccess || st != FT_OK) {
+    ft_weight_destroy(w);
+    if (e != cudaSuccess) return fail(FT_ERR_GPU, "sparse upload failed: %s", cudaGetErrorString(e));
+    return st;
+  }
+  *out = w;
+  return FT_OK;
+}
+
+int ft_sparse_upload_wgsl(ft_ctx* ctx, const uint32_t* words_host, int64_t rows, int64_t cols,
+                          const float* row_scales_host, ft_weight** out) {
+  FT_CHECK(words_host && row_scales_host, FT_ERR_SHAPE, "null host buffer");
+  FT_CHECK(cols > 0 && cols % 4 == 0, FT_ERR_SHAPE,
+           "cols must be a positive multiple of 4 for 2:4 sparsity, got %lld", (long long)cols);
+  DeviceGuard g(ctx ? ctx->device : 0);
+  ft_weight* w = nullptr;
+  int st = alloc_weight(ctx, rows, cols, &w, 1);
+  if (st != FT_OK) return st;
+  const size_t nbytes = (size_t)rows * (size_t)ceil_div(cols / 4, 6) * 4;
+  uint32_t* staging = nullptr;
+  cudaStream_t s = ctx->host_stream;
+  cudaError_t e = cudaMalloc(&staging, nbytes);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(staging, words_host, nbytes, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess) st = launch_repack_sparse_wgsl(staging, rows, cols, w, s);
+  if (e == cudaSuccess && st == FT_OK) st = finish_scales(w, row_scales_host, true, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (staging) cudaFree(staging);
+  if (e != cudaSuccess || st != FT_OK) {
+    ft_weight_destroy(w);
+    if (e != cudaSuccess) return fail(FT_ERR_GPU, "sparse upload failed: %s", cudaGetErrorString(e));
+    return st;
+  }
+  *out = w;
+  return FT_OK;
+}
+
+int ft_gpu_sparse_ternary_matmul(ft_ctx* ctx, const uint32_t* sparse_words_host, float scale,
+                                 const float* input_host, size_t seq_len, size_t in_cols,
+                                 size_t out_rows, float* output_host) {
+  FT_CHECK(ctx, FT_ERR_SHAPE, "null context");
+  FT_CHECK(sparse_words_host && input_host && output_host, FT_ERR_SHAPE, "null host buffer");
+  if (seq_len == 0 || out_rows == 0) return FT_OK;
+  std::vector<float> scales(out_rows, scale);  // the reference passes one global scale
+  ft_weight* w = nullptr;
+  int st = ft_sparse_upload_wgsl(ctx, sparse_words_host, (int64_t)out_rows, (int64_t)in_cols,
+                                 scales.data(), &w);
+  if (st != FT_OK) return st;
+  st = ft_gpu_ternary_matmul_vram(ctx, w, input_host, seq_len, output_host);
+  ft_weight_destroy(w);
+  return st;
+}
+
 int ft_weight_destroy(ft_weight* w) {
   if (!w) return FT_OK;
   DeviceGuard g(w->device);
@@ -253,7 +329,9 @@ int ft_weight_info(const ft_weight* w, int64_t* rows, int64_t* cols, int64_t* de
   FT_CHECK(w, FT_ERR_SHAPE, "null weight");
   if (rows) *rows = w->rows;
   if (cols) *cols = w->cols;
-  if (device_bytes) *device_bytes = w->n_tiles * w->n_chunks * kBlockBytes + w->n_tiles * kTileRows * 4;
+  if (device_bytes)
+    *device_bytes = w->n_tiles * w->n_chunks * (w->format == 1 ? kSparseBlockBytes : kBlockBytes) +
+                    w->n_tiles * kTileRows * 4;
   return FT_OK;
 }
 

@@ -45,6 +45,52 @@ __global__ void repack_kernel(const void* __restrict__ src, int64_t rows, int64_
   dst[gw] = out;
 }
 
+// -------------------------------------------------------- sparse repack --
+// One thread per (tile, chunk, row): decodes the row's 32 groups of this chunk
+// from the reference layout and writes 32 x 5-bit codes (160 bits, LSB first)
+// = 5 words.  Code = pattern * 4 + signs (bit 0/1: first/second nonzero is
+// negative); 24 = all-zero group (padding rows or K).
+template <bool kWgsl>
+__global__ void repack_sparse_kernel(const uint8_t* __restrict__ pat, const uint8_t* __restrict__ sgn,
+                                     const uint32_t* __restrict__ words, int64_t rows, int64_t cols,
+                                     int64_t n_chunks, int64_t total, uint32_t* __restrict__ dst) {
+  int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= total) return;
+  const int64_t block = idx >> 7;
+  const int row = (int)(idx & 127);
+  const int64_t tile = block / n_chunks, chunk = block % n_chunks;
+  const int64_t R = tile * kTileRows + row;
+  const int64_t gpr = cols / 4;  // groups per row (cols % 4 == 0)
+  const int64_t wpr = (gpr + 5) / 6;
+  uint32_t out[5] = {0, 0, 0, 0, 0};
+#pragma unroll 4
+  for (int g = 0; g < 32; ++g) {
+    const int64_t kg = chunk * 32 + g;
+    uint32_t code = 24;
+    if (R < rows && kg < gpr) {
+      uint32_t p, sbits;
+      if (kWgsl) {
+        const uint32_t v = (words[R * wpr + kg / 6] >> ((kg % 6) * 5)) & 31u;
+        p = v & 7u;
+        if (p > 5) p = 5;          // the WGSL shader clamps the pattern
+        sbits = (v >> 3) & 3u;     // 1 = negative
+      } else {
+        const int64_t gi = R * gpr + kg;  // flat group index of the host matrix
+        p = (gi % 2 == 0) ? (pat[gi / 2] & 7u) : ((pat[gi / 2] >> 4) & 7u);
+        if (p > 5) p = 0;          // to_ternary's fallback for an invalid pattern
+        sbits = (~(uint32_t)(sgn[gi / 4] >> ((gi % 4) * 2))) & 3u;  // host: 1 = positive
+      }
+      code = p * 4 + sbits;
+    }
+    const int bit = 5 * g;
+    out[bit >> 5] |= code << (bit & 31);
+    if ((bit & 31) > 27) out[(bit >> 5) + 1] |= code >> (32 - (bit & 31));
+  }
+  uint32_t* d = dst + block * (kSparseBlockBytes / 4) + row * 5;
+#pragma unroll
+  for (int i = 0; i < 5; ++i) d[i] = out[i];
+}
+
 // ------------------------------------------------------------- quantizer --
 __device__ __forceinline__ float load_act(const void* x, bool bf16, int64_t i) {
   if (bf16) {
@@ -296,6 +342,24 @@ int launch_repack_u32(const uint32_t* words, int64_t rows, int64_t cols, ft_weig
   int64_t total = w->n_tiles * w->n_chunks * (kBlockBytes / 4);
   repack_kernel<true><<<(unsigned)ceil_div(total, 256), 256, 0, s>>>(
       words, rows, cols, w->n_chunks, total, reinterpret_cast<uint32_t*>(w->codes));
+  FT_LAUNCH_CHECK();
+  return FT_OK;
+}
+
+int launch_repack_sparse_host(const uint8_t* patterns, const uint8_t* signs, int64_t rows,
+                              int64_t cols, ft_weight* w, cudaStream_t s) {
+  int64_t total = w->n_tiles * w->n_chunks * kTileRows;
+  repack_sparse_kernel<false><<<(unsigned)ceil_div(total, 128), 128, 0, s>>>(
+      patterns, signs, nullptr, rows, cols, w->n_chunks, total, reinterpret_cast<uint32_t*>(w->codes));
+  FT_LAUNCH_CHECK();
+  return FT_OK;
+}
+
+int launch_repack_sparse_wgsl(const uint32_t* words, int64_t rows, int64_t cols, ft_weight* w,
+                              cudaStream_t s) {
+  int64_t total = w->n_tiles * w->n_chunks * kTileRows;
+  repack_sparse_kernel<true><<<(unsigned)ceil_div(total, 128), 128, 0, s>>>(
+      nullptr, nullptr, words, rows, cols, w->n_chunks, total, reinterpret_cast<uint32_t*>(w->codes));
   FT_LAUNCH_CHECK();
   return FT_OK;
 }

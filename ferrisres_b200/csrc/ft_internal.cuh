@@ -29,7 +29,10 @@ namespace ft {
 
 constexpr int kTileRows = 128;  // output channels per tile
 constexpr int kChunkK = 128;    // K codes per chunk
-constexpr int kBlockBytes = kTileRows * kChunkK / 4;  // 4096
+constexpr int kBlockBytes = kTileRows * kChunkK / 4;  // 4096 (dense 2-bit block)
+// 2:4 sparse block: each row's 32 groups of 4 codes as 5-bit group codes
+// (pattern * 4 + signs, 24 = all-zero padding group), 20 bytes per row.
+constexpr int kSparseBlockBytes = kTileRows * 20;      // 2560
 
 void set_error(const char* fmt, ...);
 extern std::atomic<uint64_t> g_launches;  // kernels launched by this library
@@ -83,9 +86,10 @@ struct ft_ctx {
 
 struct ft_weight {
   int device = 0;
+  int format = 0;             // 0: dense 2-bit (T128 tiles), 1: 2:4 sparse (5-bit groups)
   int64_t rows = 0, cols = 0;
   int64_t n_tiles = 0, n_chunks = 0;
-  uint8_t* codes = nullptr;   // tiled T128 layout, n_tiles*n_chunks*4096 bytes
+  uint8_t* codes = nullptr;   // n_tiles*n_chunks blocks of 4096 (dense) or 2560 (sparse) bytes
   float* row_scales = nullptr;  // [n_tiles*128], zero on padding rows
 };
 
@@ -102,6 +106,12 @@ int launch_repack_u8(const uint8_t* packed, int64_t rows, int64_t cols, ft_weigh
                      cudaStream_t s);
 int launch_repack_u32(const uint32_t* words, int64_t rows, int64_t cols, ft_weight* w,
                       cudaStream_t s);
+// 2:4 sparse repack from the reference host layout (patterns + signs) or from
+// the WGSL layout (5-bit groups, 6 per u32).
+int launch_repack_sparse_host(const uint8_t* patterns, const uint8_t* signs, int64_t rows,
+                              int64_t cols, ft_weight* w, cudaStream_t s);
+int launch_repack_sparse_wgsl(const uint32_t* words, int64_t rows, int64_t cols, ft_weight* w,
+                              cudaStream_t s);
 int launch_quantize_i8(const void* x, bool bf16, int64_t seq, int64_t cols, int8_t* q, float* sx,
                        cudaStream_t s);
 int launch_dense_f32(ft_ctx* ctx, const ft_weight* w, int64_t seq, const float* x, float* y,

@@ -194,8 +194,12 @@ __device__ __forceinline__ void epilogue_group(const TqProblem& p, int digits, i
   }
 }
 
-template <int NPAD>
+template <int NPAD, bool kSparse>
 __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_constant__ TqBatch b) {
+  // weight block bytes in HBM and in the smem ring (2:4 blocks use the first 2560 bytes)
+  constexpr uint32_t kBlk = kSparse ? kSparseBlockBytes : kBlockBytes;
+  // 2:4 group code -> four unsigned codes w+1 (bytes in K order); 24..31 = zero group
+  __shared__ uint32_t s_lut[32];
   // dynamic smem: [kSA weight blocks of 4096 B][kSBS B super-stages of kSK*NPAD*128 B]
   extern __shared__ __align__(1024) uint8_t smem_dyn[];
   constexpr uint32_t kBStage = NPAD * 128;       // B bytes per chunk
@@ -225,6 +229,20 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
+  if (kSparse && threadIdx.x < 32) {
+    const int c = threadIdx.x;
+    uint32_t v = 0x01010101u;
+    if (c < 24) {
+      const int pat = c >> 2, sg = c & 3;
+      // pattern -> positions (0,1),(0,2),(0,3),(1,2),(1,3),(2,3)
+      const int p0 = pat < 3 ? 0 : (pat < 5 ? 1 : 2);
+      const int p1 = pat == 0 ? 1 : (pat == 1 || pat == 3) ? 2 : 3;
+      v &= ~(0xFFu << (8 * p0)) & ~(0xFFu << (8 * p1));
+      v |= (uint32_t)((sg & 1) ? 0 : 2) << (8 * p0);
+      v |= (uint32_t)((sg & 2) ? 0 : 2) << (8 * p1);
+    }
+    s_lut[c] = v;
+  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < kSA; ++s) {
       tc::mbar_init(tc::smem_u32(&bar_sa_full[s]), 1);
@@ -267,16 +285,24 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
         if (j < n) {
           const uint32_t sa = gb % kSA;
           ok = ok && tc::mbar_wait(tc::smem_u32(&bar_sa_full[sa]), (gb / kSA) & 1, b.err, 10);
-          uint4 v0 = make_uint4(0, 0, 0, 0), v1 = make_uint4(0, 0, 0, 0);
-          if (ok) {
-            const uint8_t* blk = smem_a + sa * kBlockBytes + r * 16;
-            v0 = *reinterpret_cast<const uint4*>(blk);
-            v1 = *reinterpret_cast<const uint4*>(blk + 2048);
+          if (kSparse) {
+            // row r's 20 bytes: stride 5 words -> conflict-free across the warp
+            const uint32_t* rw = reinterpret_cast<const uint32_t*>(smem_a + sa * kBlockBytes) + r * 5;
+#pragma unroll
+            for (int i = 0; i < 5; ++i) wv[j][i] = ok ? rw[i] : 0u;
+            wv[j][5] = wv[j][6] = wv[j][7] = 0u;
+          } else {
+            uint4 v0 = make_uint4(0, 0, 0, 0), v1 = make_uint4(0, 0, 0, 0);
+            if (ok) {
+              const uint8_t* blk = smem_a + sa * kBlockBytes + r * 16;
+              v0 = *reinterpret_cast<const uint4*>(blk);
+              v1 = *reinterpret_cast<const uint4*>(blk + 2048);
+            }
+            wv[j][0] = v0.x; wv[j][1] = v0.y; wv[j][2] = v0.z; wv[j][3] = v0.w;
+            wv[j][4] = v1.x; wv[j][5] = v1.y; wv[j][6] = v1.z; wv[j][7] = v1.w;
           }
           __syncwarp();
           if (lane == 0) tc::mbar_arrive(tc::smem_u32(&bar_sa_empty[sa]));
-          wv[j][0] = v0.x; wv[j][1] = v0.y; wv[j][2] = v0.z; wv[j][3] = v0.w;
-          wv[j][4] = v1.x; wv[j][5] = v1.y; wv[j][6] = v1.z; wv[j][7] = v1.w;
           ++gb;
         }
       }
@@ -291,10 +317,21 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
 #pragma unroll
           for (int h = 0; h < 2; ++h) {  // two halves of 64 codes: 16 TMEM columns each
             uint32_t a[16];
+            if (kSparse) {
 #pragma unroll
-            for (int w = 0; w < 4; ++w)
+              for (int gg = 0; gg < 16; ++gg) {  // group g covers K 4g..4g+3 = TMEM column g
+                const int bit = 5 * (h * 16 + gg);
+                const int wi = bit >> 5, sh = bit & 31;
+                const uint32_t v = sh <= 27 ? (wv[j][wi] >> sh) & 31u
+                                            : __funnelshift_r(wv[j][wi], wv[j][wi + 1], sh) & 31u;
+                a[gg] = s_lut[v];
+              }
+            } else {
 #pragma unroll
-              for (int q = 0; q < 4; ++q) a[w * 4 + q] = (wv[j][h * 4 + w] >> (2 * q)) & 0x03030303u;
+              for (int w = 0; w < 4; ++w)
+#pragma unroll
+                for (int q = 0; q < 4; ++q) a[w * 4 + q] = (wv[j][h * 4 + w] >> (2 * q)) & 0x03030303u;
+            }
             if (ok) tc::tmem_st_x16(tmem + lane_off + kACol0 + (s * kSK + j) * 32 + 16 * h, a);
           }
         }
@@ -322,9 +359,9 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
           ok = tc::mbar_wait(tc::smem_u32(&bar_sa_empty[sa]), ((gb / kSA) + 1) & 1, b.err, 17);
         if (!ok) break;
         const uint32_t bar = tc::smem_u32(&bar_sa_full[sa]);
-        tc::mbar_arrive_expect_tx(bar, kBlockBytes);
-        const uint8_t* src = p.codes + (cs.it.tile * p.n_chunks + cs.it.c0 + cs.chunk) * kBlockBytes;
-        tc::bulk_g2s(tc::smem_u32(smem_a + sa * kBlockBytes), src, kBlockBytes, bar);
+        tc::mbar_arrive_expect_tx(bar, kBlk);
+        const uint8_t* src = p.codes + (cs.it.tile * p.n_chunks + cs.it.c0 + cs.chunk) * kBlk;
+        tc::bulk_g2s(tc::smem_u32(smem_a + sa * kBlockBytes), src, kBlk, bar);
         ++gb;
         cs.advance(b);
       }
@@ -609,12 +646,12 @@ int pick_npad(int64_t ncols) {
   return 256;
 }
 
-template <int NPAD>
+template <int NPAD, bool kSparse = false>
 int launch_grouped_t(const TqBatch& batch, int64_t grid, cudaStream_t s) {
   const size_t smem = smem_bytes_for(NPAD);
   static bool attr_set = false;  // per template instance
   if (!attr_set) {
-    FT_CUDA(cudaFuncSetAttribute(tq_grouped_kernel<NPAD>,
+    FT_CUDA(cudaFuncSetAttribute(tq_grouped_kernel<NPAD, kSparse>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     attr_set = true;
   }
@@ -628,7 +665,7 @@ int launch_grouped_t(const TqBatch& batch, int64_t grid, cudaStream_t s) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  FT_CUDA(cudaLaunchKernelEx(&cfg, tq_grouped_kernel<NPAD>, batch));
+  FT_CUDA(cudaLaunchKernelEx(&cfg, tq_grouped_kernel<NPAD, kSparse>, batch));
   FT_LAUNCH_CHECK();
   return FT_OK;
 }
@@ -657,6 +694,8 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
   for (int i = 0; i < n; ++i) {
     FT_CHECK(ws[i] && xs[i] && ys[i], FT_ERR_SHAPE, "null pointer in group entry %d", i);
     FT_CHECK(ws[i]->device == ctx->device, FT_ERR_DEVICE, "weight %d on another device", i);
+    FT_CHECK(ws[i]->format == ws[0]->format, FT_ERR_UNSUPPORTED,
+             "group mixes dense and 2:4 sparse weights (entry %d)", i);
     FT_CHECK(xkind != 2 || (sxs && sxs[i]), FT_ERR_SHAPE, "null sx in group entry %d", i);
     int j = 0;
     while (j < nsrc && !(src_x[j] == xs[i] && src_k[j] == ws[i]->cols)) ++j;
@@ -789,6 +828,15 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
   }
 
   const int64_t grid = items < grid_target ? items : grid_target;
+  if (ws[0]->format == 1) {
+    switch (npad) {
+      case 16: return launch_grouped_t<16, true>(batch, grid, s);
+      case 32: return launch_grouped_t<32, true>(batch, grid, s);
+      case 64: return launch_grouped_t<64, true>(batch, grid, s);
+      case 128: return launch_grouped_t<128, true>(batch, grid, s);
+      default: return launch_grouped_t<256, true>(batch, grid, s);
+    }
+  }
   switch (npad) {
     case 16: return launch_grouped_t<16>(batch, grid, s);
     case 32: return launch_grouped_t<32>(batch, grid, s);
@@ -936,6 +984,7 @@ extern "C" int ft_ternary_matmul_f32_noalloc(ft_ctx* ctx, const ft_weight* w, in
   FT_CHECK(seq == 0 || (x_dev && y_dev), FT_ERR_SHAPE, "null activation/output pointer");
   FT_CHECK(w->device == ctx->device, FT_ERR_DEVICE, "weight lives on device %d, context on %d",
            w->device, ctx->device);
+  FT_CHECK(w->format == 0, FT_ERR_UNSUPPORTED, "the no-alloc matmul takes dense weights only");
   FT_CHECK(seq <= kNaMaxSeq && w->rows <= kNaMaxRows && w->cols <= kNaMaxCols,
            FT_ERR_UNSUPPORTED,
            "no-alloc matmul limits are seq <= %lld, rows <= %lld, cols <= %lld (got seq %lld, "

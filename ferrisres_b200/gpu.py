@@ -108,6 +108,36 @@ class DeviceTernaryWeight:
         return cls(h, rows, cols, ctx)
 
     @classmethod
+    def from_sparse_host(cls, patterns, signs, rows, cols, row_scales, device=None):
+        """2:4 weights in the reference SparseTernaryMatrix layout
+        (src/model/sparse_ternary.rs:52-70); stored at 1.25 bits/weight."""
+        ctx = get_context(device)
+        ng = rows * cols // 4
+        pt, sg = _host(patterns, np.uint8), _host(signs, np.uint8)
+        s = _host(row_scales, np.float32)
+        if cols % 4 or pt.size < (ng + 1) // 2 or sg.size < (ng + 3) // 4 or s.size < rows:
+            raise ShapeError("bad 2:4 sparse buffers for the given shape")
+        h = C.c_void_p()
+        call("ft_sparse_upload_host", ctx.handle, pt.ctypes.data_as(C.c_void_p),
+             sg.ctypes.data_as(C.c_void_p), int(rows), int(cols), s.ctypes.data_as(C.c_void_p),
+             C.byref(h))
+        return cls(h, rows, cols, ctx)
+
+    @classmethod
+    def from_sparse_wgsl(cls, words, rows, cols, row_scales, device=None):
+        """2:4 weights in the WGSL SparseTernaryMatMulOp layout
+        (src/compute/kernels/sparse_ternary.rs:71-100)."""
+        ctx = get_context(device)
+        w = _host(words, np.uint32)
+        s = _host(row_scales, np.float32)
+        if cols % 4 or w.size < rows * ((cols // 4 + 5) // 6) or s.size < rows:
+            raise ShapeError("bad 2:4 sparse buffers for the given shape")
+        h = C.c_void_p()
+        call("ft_sparse_upload_wgsl", ctx.handle, w.ctypes.data_as(C.c_void_p), int(rows),
+             int(cols), s.ctypes.data_as(C.c_void_p), C.byref(h))
+        return cls(h, rows, cols, ctx)
+
+    @classmethod
     def from_ternary(cls, values, rows, cols, row_scales, device=None):
         from .ternary import pack_ternary
         return cls.from_packed_u8(pack_ternary(values), rows, cols, row_scales, device)
@@ -260,6 +290,19 @@ class GpuMatmulAccelerator:
         call("ft_gpu_ternary_matmul", self.ctx.handle, w.ctypes.data_as(C.c_void_p),
              s.ctypes.data_as(C.c_void_p), x.ctypes.data_as(C.c_void_p), int(seq_len),
              int(in_cols), int(out_rows), y.ctypes.data_as(C.c_void_p))
+        return y
+
+    def gpu_sparse_ternary_matmul(self, sparse_data, scale, input, seq_len, in_cols, out_rows):
+        """src/model/gpu_forward.rs:1299 (a zero-returning stub in the reference)."""
+        w = _host(sparse_data, np.uint32)
+        x = _host(input, np.float32)
+        if in_cols % 4 or w.size < out_rows * ((in_cols // 4 + 5) // 6) or \
+                x.size < seq_len * in_cols:
+            raise ShapeError("buffer too small for the given dims")
+        y = np.empty(seq_len * out_rows, np.float32)
+        call("ft_gpu_sparse_ternary_matmul", self.ctx.handle, w.ctypes.data_as(C.c_void_p),
+             float(scale), x.ctypes.data_as(C.c_void_p), int(seq_len), int(in_cols),
+             int(out_rows), y.ctypes.data_as(C.c_void_p))
         return y
 
     def gpu_ternary_matmul_vram(self, weight: DeviceTernaryWeight, input, seq_len, in_cols,

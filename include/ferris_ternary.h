@@ -84,6 +84,20 @@ int ft_weight_upload_packed_u32(ft_ctx* ctx, const uint32_t* words_host, int64_t
 /* Same layout already in device memory (e.g. a buffer the caller owns). */
 int ft_weight_from_device_u32(ft_ctx* ctx, const uint32_t* words_dev, int64_t rows, int64_t cols,
                               const float* row_scales_dev, void* stream, ft_weight** out);
+/* 2:4 sparse weights (every group of 4 codes along K holds exactly two +-1).
+ * From the reference host type SparseTernaryMatrix (src/model/sparse_ternary.rs:52-70):
+ * patterns = ceil(groups/2) bytes (3-bit pattern, even group in the low nibble),
+ * signs = ceil(groups/4) bytes (2 bits per group, 1 = +1); groups = rows*cols/4,
+ * cols % 4 == 0.  Stored on the device at 1.25 bits per weight (5-bit group
+ * codes) and usable with every ft_ternary_matmul_* entry point. */
+int ft_sparse_upload_host(ft_ctx* ctx, const uint8_t* patterns_host, const uint8_t* signs_host,
+                          int64_t rows, int64_t cols, const float* row_scales_host,
+                          ft_weight** out);
+/* From the WGSL SparseTernaryMatMulOp layout (src/compute/kernels/sparse_ternary.rs:71-100):
+ * rows * ceil(ceil(cols/4)/6) u32 words, 6 groups of 5 bits (3 pattern + 2 sign,
+ * 1 = -1) per word. */
+int ft_sparse_upload_wgsl(ft_ctx* ctx, const uint32_t* words_host, int64_t rows, int64_t cols,
+                          const float* row_scales_host, ft_weight** out);
 int ft_weight_destroy(ft_weight* w);
 int ft_weight_info(const ft_weight* w, int64_t* rows, int64_t* cols, int64_t* device_bytes);
 
@@ -155,6 +169,11 @@ int ft_ternary_matmul_op_dispatch(ft_ctx* ctx, const uint32_t* ternary_dev,
 int ft_gpu_ternary_matmul(ft_ctx* ctx, const uint32_t* packed_weights_host,
                           const float* scales_host, const float* input_host, size_t seq_len,
                           size_t in_cols, size_t out_rows, float* output_host);
+/* GpuMatmulAccelerator::gpu_sparse_ternary_matmul (src/model/gpu_forward.rs:1299-1327,
+ * a stub returning zeros in the reference): WGSL-layout words, one global scale. */
+int ft_gpu_sparse_ternary_matmul(ft_ctx* ctx, const uint32_t* sparse_words_host, float scale,
+                                 const float* input_host, size_t seq_len, size_t in_cols,
+                                 size_t out_rows, float* output_host);
 /* GpuMatmulAccelerator::gpu_ternary_matmul_vram (src/model/gpu_forward.rs:1245-1297):
  * weights already resident (ft_weight); host activations in, host output out. */
 int ft_gpu_ternary_matmul_vram(ft_ctx* ctx, const ft_weight* w, const float* input_host,
