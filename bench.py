@@ -432,6 +432,95 @@ def run_gemm(args, ws, rank, local):
     }
 
 
+# ------------------------------------------------------------ cfg3 2:4 ---
+S_N, S_K = 14336, 4096
+
+
+def run_sparse(args, ws, rank, local):
+    """2:4 sparse ternary matmul, K=4096, N=14336, fp32 x,
+    at M=1 (bandwidth-bound GEMV, grouped launches of --group) and M=64.
+    Weights enter in the reference SparseTernaryMatrix layout and are stored
+    at 1.25 bits/weight; copies rotate beyond 2x L2."""
+    import numpy as np
+    import torch
+
+    from ferrisres_b200 import _lib, gpu
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    dev_bytes = (S_N // 128) * (S_K // 128) * 2560
+    algo = dev_bytes + S_N * 4 + S_K * 4 + S_N * 4  # weights + scales + x + y per GEMV
+    group = args.group
+    n_copies = -(-max(4, -(-2 * L2_BYTES // dev_bytes)) // group) * group
+    rng = np.random.default_rng(0)
+    ng = S_N * S_K // 4
+    weights = []
+    for i in range(n_copies):
+        lo = rng.integers(0, 6, size=(ng + 1) // 2, dtype=np.uint8)
+        hi = rng.integers(0, 6, size=(ng + 1) // 2, dtype=np.uint8)
+        pat = (lo | (hi << 4)).astype(np.uint8)
+        sg = rng.integers(0, 256, size=(ng + 3) // 4, dtype=np.uint8)
+        rs = rng.uniform(0.01, 0.1, S_N).astype(np.float32)
+        weights.append(gpu.DeviceTernaryWeight.from_sparse_host(pat, sg, S_N, S_K, rs, local))
+    assert weights[0].device_bytes() == dev_bytes + S_N * 4
+    x1 = torch.randn(1, S_K, device=device)
+    x64 = torch.randn(64, S_K, device=device)
+    ys = [torch.empty(1, S_N, device=device) for _ in range(n_copies)]
+    y64 = torch.empty(64, S_N, device=device)
+    calls = [gpu.GroupCall(weights[i:i + group], [x1] * group, ys[i:i + group])
+             for i in range(0, n_copies, group)]
+    stream = torch.cuda.Stream(device=device)
+    with torch.cuda.stream(stream):
+        for c in calls:
+            c()
+        weights[0].matmul_f32(x64, out=y64)
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for c in calls:
+            c()
+    reps = max(1, args.steps // n_copies)
+    sampler = ClockSampler(local)
+    sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        graph.replay()
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    sec = e0.elapsed_time(e1) / 1e3
+    gbps = reps * n_copies * algo / sec / 1e9
+    # M = 64 (one matmul per step, weights rotating)
+    m64_steps = max(4, min(args.steps, 200))
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for i in range(m64_steps):
+            weights[i % n_copies].matmul_f32(x64, out=y64)
+        e1.record(stream)
+    torch.cuda.synchronize()
+    sec64 = e0.elapsed_time(e1) / 1e3 / m64_steps
+    peak, peak_kind = load_peaks()
+    return {
+        "metric": "2:4 sparse ternary GEMV HBM GB/s", "value": round(gbps, 2), "unit": "GB/s",
+        "n_gpus": 1, "steps": reps * n_copies, "warmup": n_copies,
+        "ms_per_step": sec * 1e3 / (reps * n_copies), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded 2:4 patterns and signs)",
+        "config": {"workload": "cfg3 2:4 sparse K=4096 N=14336, M=1 (grouped) and M=64",
+                   "device_bytes_per_weight": dev_bytes, "bits_per_weight": 1.25,
+                   "launch_group": group, "weight_copies": n_copies},
+        "roofline": {"bound": "hbm", "achieved": round(gbps, 2), "peak": peak, "unit": "GB/s",
+                     "frac": round(gbps / peak, 4), "peak_source": peak_kind,
+                     "algorithmic_bytes_per_gemv": algo, "traffic": None},
+        "m64": {"ms": round(sec64 * 1e3, 4), "TOPS_nonzero": round(2 * 64 * S_N * S_K / 2 / sec64 / 1e12, 2),
+                "GBps_weights": round(dev_bytes / sec64 / 1e9, 1)},
+        "gpu_launches": int(reps * len(calls) * 2),
+        "clocks": clocks,
+    }
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -441,7 +530,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--group", type=int, default=16, help="GEMVs per launch (1..64)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--workload", choices=["gemv", "gemm_cfg2"], default="gemv",
+    ap.add_argument("--workload", choices=["gemv", "gemm_cfg2", "sparse_cfg3"], default="gemv",
                     help="gemv = the headline cfg0 line; gemm_cfg2 = the int8 prefill GEMM")
     args = ap.parse_args()
     ws, rank, local = dist_env()
@@ -449,6 +538,8 @@ def main():
         print(f"warning: --gpus {args.gpus} but WORLD_SIZE={ws}", file=sys.stderr)
     if args.workload == "gemm_cfg2" and args.impl == "ours":
         res = run_gemm(args, ws, rank, local)
+    elif args.workload == "sparse_cfg3" and args.impl == "ours":
+        res = run_sparse(args, ws, rank, local)
     elif args.impl == "reference":
         res = run_reference(args, ws, rank)
     else:
