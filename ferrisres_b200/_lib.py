@@ -82,6 +82,15 @@ SIGNATURES = {
     "ft_ternary_matmul_op_dispatch": [_p, _p, _p, _p, _p, _u32, _u32, _u32, _p],
     "ft_gpu_ternary_matmul": [_p, _p, _p, _p, _sz, _sz, _sz, _p],
     "ft_gpu_ternary_matmul_vram": [_p, _p, _p, _sz, _p],
+    "ft_moe_create": [_p, _i64, _i64, _i64, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p],
+    "ft_moe_destroy": [_p],
+    "ft_moe_forward": [_p, _p, _i64, _p, _i, _p, _p, _p],
+    "ft_moe_forward_host": [_p, _p, _p, _sz, _p],
+    "ft_moe_route": [_p, _p, _i64, _p, _i, _p, _p, _p, _p, _p],
+    "ft_moe_dispatch_layout": [_p, _p, _i64, _p, _p, _p, _p, _p, _p, _p],
+    "ft_moe_gather_rows": [_p, _p, _i, _i64, _p, _i64, _p, _p],
+    "ft_moe_expert_ffn": [_p, _p, _i, _p, _p, _p, _i, _p, _p],
+    "ft_moe_combine": [_p, _p, _i64, _p, _p, _p, _p, _p],
 }
 _RESTYPE = {"ft_version": C.c_char_p, "ft_last_error_string": C.c_char_p,
             "ft_launch_counter": C.c_uint64}

@@ -126,7 +126,7 @@ int launch_tc_matmul(ft_ctx* ctx, const ft_weight* w, int64_t seq, const void* x
 // one persistent launch; identical activation pointers share one operand.
 int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t seq,
                       const void* const* xs, int xkind, const float* const* sxs, float* const* ys,
-                      const int64_t* ldys, cudaStream_t s);
+                      const int64_t* ldys, cudaStream_t s, const int64_t* seqs = nullptr);
 int launch_wgsl_op(const uint32_t* words, const float* scales, const float* x, float* y,
                    uint32_t seq, uint32_t in_cols, uint32_t out_rows, cudaStream_t s);
 }  // namespace ft

@@ -1,0 +1,511 @@
+// Ternary MoE FFN layer (TernaryMoELayer::forward, src/model/ternary_moe.rs:145-223)
+// on the B200 path:
+//   router  : scores[t, e] = sum_j R[e, j] x[t, j]  (fp32, sequential in j, no FMA
+//             contraction -- the reference loop's rounding), softmax, stable
+//             descending top-k, gates renormalised by their sum;
+//   dispatch: per-expert counts -> offsets -> expert-major slots (one slot per
+//             (token, k)) -> gathered activation rows;
+//   experts : one grouped tcgen05 launch for every expert's [gate; up]
+//             projection, SwiGLU (or GeLU-tanh) on CUDA cores, one grouped launch
+//             for the down projections;
+//   combine : y[t] = (0 + w_0 * o_0) + w_1 * o_1 ... in top-k order, the
+//             reference's accumulation order.
+// The stages are exported separately so an expert-parallel host can put its
+// all-to-all exchanges between them.
+#include <cstring>
+#include <vector>
+
+#include "ft_internal.cuh"
+
+struct ft_moe {
+  int device = 0;
+  int64_t E = 0, H = 0, F = 0;
+  int top_k = 2;
+  int use_gelu = 0;
+  float* router = nullptr;  // [E, H] fp32 (row e = expert e)
+  std::vector<ft_weight*> gate_up;  // [2F, H] each: gate rows then up rows
+  std::vector<ft_weight*> down;     // [H, F] each
+  ft::Workspace buf;                // forward intermediates (grown on demand)
+  std::vector<int32_t> counts_host;
+};
+
+namespace ft {
+namespace {
+
+constexpr int kRouterTok = 16;  // tokens per router block
+constexpr int kRouterKc = 64;   // K chunk staged in shared memory
+constexpr int kMaxExperts = 64;
+
+__device__ __forceinline__ float load_act(const void* x, int bf16, int64_t i) {
+  return bf16 ? __uint_as_float((uint32_t) static_cast<const uint16_t*>(x)[i] << 16)
+              : static_cast<const float*>(x)[i];
+}
+
+// One block = 16 tokens x all experts (E <= 64); thread t owns token t/16 and
+// experts t%16 + 16m.  Then one thread per token does softmax and top-k in the
+// reference's sequential order.
+__global__ void __launch_bounds__(256) moe_router_kernel(
+    const void* __restrict__ x, int bf16, int64_t T, int64_t H, int E, int K,
+    const float* __restrict__ R, int32_t* __restrict__ topk_idx, float* __restrict__ topk_w,
+    float* __restrict__ probs_out, int32_t* __restrict__ counts) {
+  __shared__ float xs[kRouterTok][kRouterKc];
+  __shared__ float rs[kRouterKc][kMaxExperts + 1];
+  __shared__ float sc[kRouterTok][kMaxExperts];
+  const int tt = threadIdx.x >> 4, el = threadIdx.x & 15;
+  const int64_t t0 = (int64_t)blockIdx.x * kRouterTok;
+  float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  for (int64_t k0 = 0; k0 < H; k0 += kRouterKc) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < kRouterTok * kRouterKc; i += blockDim.x) {
+      const int a = i / kRouterKc, kk = i % kRouterKc;
+      const int64_t t = t0 + a, k = k0 + kk;
+      xs[a][kk] = (t < T && k < H) ? load_act(x, bf16, t * H + k) : 0.0f;
+    }
+    for (int i = threadIdx.x; i < E * kRouterKc; i += blockDim.x) {
+      const int e = i / kRouterKc, kk = i % kRouterKc;
+      const int64_t k = k0 + kk;
+      rs[kk][e] = k < H ? R[(int64_t)e * H + k] : 0.0f;
+    }
+    __syncthreads();
+    const int kn = (int)((H - k0) < kRouterKc ? (H - k0) : kRouterKc);
+    for (int kk = 0; kk < kn; ++kk) {
+      const float xv = xs[tt][kk];
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        const int e = el + 16 * m;
+        if (e < E) acc[m] = __fadd_rn(acc[m], __fmul_rn(rs[kk][e], xv));
+      }
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < 4; ++m)
+    if (el + 16 * m < E) sc[tt][el + 16 * m] = acc[m];
+  __syncthreads();
+  const int64_t t = t0 + tt;
+  if (el != 0 || t >= T) return;
+  float* s = sc[tt];
+  float mx = -INFINITY;
+  for (int e = 0; e < E; ++e) mx = fmaxf(mx, s[e]);
+  float se = 0.0f;
+  for (int e = 0; e < E; ++e) {
+    s[e] = expf(s[e] - mx);
+    se += s[e];
+  }
+  for (int e = 0; e < E; ++e) s[e] = s[e] / se;
+  if (probs_out)
+    for (int e = 0; e < E; ++e) probs_out[t * E + e] = s[e];
+  // stable descending top-k: the largest remaining, lowest index first on ties
+  uint64_t taken = 0;
+  int idx[8];
+  float wsum = 0.0f;
+  for (int k = 0; k < K; ++k) {
+    int best = -1;
+    for (int e = 0; e < E; ++e)
+      if (!((taken >> e) & 1ull) && (best < 0 || s[e] > s[best])) best = e;
+    taken |= 1ull << best;
+    idx[k] = best;
+    wsum += s[best];
+  }
+  for (int k = 0; k < K; ++k) {
+    topk_idx[t * K + k] = idx[k];
+    topk_w[t * K + k] = wsum > 0.0f ? s[idx[k]] / wsum : s[idx[k]];
+    atomicAdd(&counts[idx[k]], 1);
+  }
+}
+
+__global__ void moe_offsets_kernel(const int32_t* __restrict__ counts, int E,
+                                   int32_t* __restrict__ offsets, int32_t* __restrict__ fill) {
+  if (threadIdx.x == 0) {
+    int32_t o = 0;
+    for (int e = 0; e < E; ++e) {
+      offsets[e] = o;
+      o += counts[e];
+      fill[e] = 0;
+    }
+    offsets[E] = o;
+  }
+}
+
+// slot_of[t*K+k] = expert-major slot of (t, k); token_of[slot] = t.
+__global__ void moe_scatter_kernel(const int32_t* __restrict__ topk_idx, int64_t n_entries, int K,
+                                   const int32_t* __restrict__ offsets, int32_t* __restrict__ fill,
+                                   int32_t* __restrict__ slot_of, int32_t* __restrict__ token_of) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n_entries) return;
+  const int e = topk_idx[i];
+  const int32_t slot = offsets[e] + atomicAdd(&fill[e], 1);
+  slot_of[i] = slot;
+  token_of[slot] = (int32_t)(i / K);
+}
+
+// xg[slot, :] = x[token_of[slot], :] (element type preserved)
+__global__ void moe_gather_kernel(const void* __restrict__ x, int elem_bytes, int64_t H,
+                                  const int32_t* __restrict__ token_of, int64_t n_slots,
+                                  void* __restrict__ xg) {
+  const int64_t row = blockIdx.x;
+  if (row >= n_slots) return;
+  const int64_t src = token_of[row];
+  const int64_t nb = H * elem_bytes;
+  const char* s = static_cast<const char*>(x) + src * nb;
+  char* d = static_cast<char*>(xg) + row * nb;
+  if ((nb & 15) == 0) {
+    for (int64_t i = threadIdx.x * 16; i < nb; i += blockDim.x * 16)
+      *reinterpret_cast<uint4*>(d + i) = *reinterpret_cast<const uint4*>(s + i);
+  } else {
+    for (int64_t i = threadIdx.x; i < nb; i += blockDim.x) d[i] = s[i];
+  }
+}
+
+// h[r, i] = silu(g) * u with silu(g) = g / (1 + exp(-g))  (ternary_moe.rs:206-209),
+// or gelu_tanh(g) (ternary_moe.rs:199-204); gu rows are [gate (F) | up (F)].
+__global__ void moe_act_kernel(const float* __restrict__ gu, int64_t rows, int64_t F, int use_gelu,
+                               float* __restrict__ h) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= rows * F) return;
+  const int64_t r = i / F, c = i % F;
+  const float g = gu[r * 2 * F + c];
+  float out;
+  if (use_gelu) {
+    const float ta = __fmul_rn(0.7978845608f,
+                               __fadd_rn(g, __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, g), g), g)));
+    out = __fmul_rn(__fmul_rn(0.5f, g), __fadd_rn(1.0f, tanhf(ta)));
+  } else {
+    const float silu = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
+    out = __fmul_rn(silu, gu[r * 2 * F + F + c]);
+  }
+  h[i] = out;
+}
+
+// y[t, j] = sum_k w[t, k] * o[slot_of[t, k], j], accumulated from 0 in k order
+__global__ void moe_combine_kernel(const float* __restrict__ o, const int32_t* __restrict__ slot_of,
+                                   const float* __restrict__ topk_w, int64_t T, int K, int64_t H,
+                                   float* __restrict__ y) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= T * H) return;
+  const int64_t t = i / H, j = i % H;
+  float acc = 0.0f;
+  for (int k = 0; k < K; ++k) {
+    const float w = topk_w[t * K + k];
+    acc = __fadd_rn(acc, __fmul_rn(w, o[(int64_t)slot_of[t * K + k] * H + j]));
+  }
+  y[i] = acc;
+}
+
+int moe_reserve(ft_moe* m, size_t bytes, cudaStream_t s) {
+  if (m->buf.bytes >= bytes) return FT_OK;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (s != nullptr) cudaStreamIsCapturing(s, &cs);
+  FT_CHECK(cs == cudaStreamCaptureStatusNone, FT_ERR_UNSUPPORTED,
+           "MoE buffers must grow but the stream is being captured");
+  if (m->buf.ptr) {
+    FT_CUDA(cudaDeviceSynchronize());
+    FT_CUDA(cudaFree(m->buf.ptr));
+    m->buf.ptr = nullptr;
+    m->buf.bytes = 0;
+  }
+  const size_t grow = bytes + bytes / 8 + (1 << 20);
+  FT_CUDA(cudaMalloc(&m->buf.ptr, grow));
+  m->buf.bytes = grow;
+  return FT_OK;
+}
+
+struct MoeBufs {
+  int32_t* topk_idx;
+  float* topk_w;
+  int32_t* counts;
+  int32_t* offsets;
+  int32_t* fill;
+  int32_t* slot_of;
+  int32_t* token_of;
+  void* xg;
+  float* gu;
+  float* h;
+  float* o;
+};
+
+// Layout of the forward intermediates for T tokens.
+size_t moe_layout(const ft_moe* m, int64_t T, int x_bytes, char* base, MoeBufs* b) {
+  const int64_t n = T * m->top_k;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    char* p = base ? base + off : nullptr;
+    off = round_up((int64_t)(off + bytes), 256);
+    return p;
+  };
+  b->topk_idx = reinterpret_cast<int32_t*>(take(n * 4));
+  b->topk_w = reinterpret_cast<float*>(take(n * 4));
+  b->counts = reinterpret_cast<int32_t*>(take((m->E + 1) * 4));
+  b->offsets = reinterpret_cast<int32_t*>(take((m->E + 1) * 4));
+  b->fill = reinterpret_cast<int32_t*>(take((m->E + 1) * 4));
+  b->slot_of = reinterpret_cast<int32_t*>(take(n * 4));
+  b->token_of = reinterpret_cast<int32_t*>(take(n * 4));
+  b->xg = take((size_t)n * m->H * x_bytes);
+  b->gu = reinterpret_cast<float*>(take((size_t)n * 2 * m->F * 4));
+  b->h = reinterpret_cast<float*>(take((size_t)n * m->F * 4));
+  b->o = reinterpret_cast<float*>(take((size_t)n * m->H * 4));
+  return off;
+}
+
+}  // namespace
+
+int moe_route(ft_ctx* ctx, ft_moe* m, int64_t T, const void* x, int bf16, int32_t* topk_idx,
+              float* topk_w, float* probs, int32_t* counts, cudaStream_t s) {
+  FT_CUDA(cudaMemsetAsync(counts, 0, m->E * sizeof(int32_t), s));
+  if (T == 0) return FT_OK;
+  moe_router_kernel<<<(unsigned)ceil_div(T, kRouterTok), 256, 0, s>>>(
+      x, bf16, T, m->H, (int)m->E, m->top_k, m->router, topk_idx, topk_w, probs, counts);
+  FT_LAUNCH_CHECK();
+  return FT_OK;
+}
+
+// Expert FFN over rows grouped in segments: segment i has seg_rows[i] rows for
+// expert seg_expert[i], stored consecutively in x_rows / y_rows.
+int moe_expert_segments(ft_ctx* ctx, ft_moe* m, int nseg, const int32_t* seg_expert,
+                        const int64_t* seg_rows, const void* x_rows, int bf16, float* gu,
+                        float* h, float* y_rows, cudaStream_t s) {
+  FT_CHECK(nseg >= 0 && nseg <= 64, FT_ERR_UNSUPPORTED, "at most 64 segments per call");
+  int64_t total = 0;
+  std::vector<const ft_weight*> wgu(nseg), wd(nseg);
+  std::vector<const void*> xs(nseg), hs(nseg);
+  std::vector<float*> gus(nseg), ys(nseg);
+  const int xb = bf16 ? 2 : 4;
+  for (int i = 0; i < nseg; ++i) {
+    FT_CHECK(seg_expert[i] >= 0 && seg_expert[i] < m->E, FT_ERR_SHAPE, "segment %d: bad expert %d",
+             i, seg_expert[i]);
+    FT_CHECK(seg_rows[i] >= 0, FT_ERR_SHAPE, "segment %d: negative rows", i);
+    wgu[i] = m->gate_up[seg_expert[i]];
+    wd[i] = m->down[seg_expert[i]];
+    xs[i] = static_cast<const char*>(x_rows) + total * m->H * xb;
+    gus[i] = gu + total * 2 * m->F;
+    hs[i] = h + total * m->F;
+    ys[i] = y_rows + total * m->H;
+    total += seg_rows[i];
+  }
+  if (total == 0) return FT_OK;
+  int st = launch_tc_grouped(ctx, nseg, wgu.data(), 0, xs.data(), bf16 ? 1 : 0, nullptr, gus.data(),
+                             nullptr, s, seg_rows);
+  if (st != FT_OK) return st;
+  moe_act_kernel<<<(unsigned)ceil_div(total * m->F, 256), 256, 0, s>>>(gu, total, m->F, m->use_gelu,
+                                                                       h);
+  FT_LAUNCH_CHECK();
+  return launch_tc_grouped(ctx, nseg, wd.data(), 0, hs.data(), 0, nullptr, ys.data(), nullptr, s,
+                           seg_rows);
+}
+
+}  // namespace ft
+
+using namespace ft;
+
+extern "C" {
+
+int ft_moe_create(ft_ctx* ctx, int64_t n_experts, int64_t hidden, int64_t inter, int top_k,
+                  int use_gelu, const float* router_host, const uint8_t* const* gate_packed,
+                  const float* const* gate_scales, const uint8_t* const* up_packed,
+                  const float* const* up_scales, const uint8_t* const* down_packed,
+                  const float* const* down_scales, ft_moe** out) {
+  FT_CHECK(ctx && out && router_host && gate_packed && gate_scales && up_packed && up_scales &&
+               down_packed && down_scales,
+           FT_ERR_SHAPE, "null argument");
+  FT_CHECK(n_experts >= 1 && n_experts <= kMaxExperts, FT_ERR_UNSUPPORTED,
+           "n_experts must be in [1, %d]", kMaxExperts);
+  FT_CHECK(top_k >= 1 && top_k <= 8 && top_k <= n_experts, FT_ERR_UNSUPPORTED,
+           "top_k must be in [1, min(8, n_experts)]");
+  FT_CHECK(hidden > 0 && inter > 0 && (inter * hidden) % 4 == 0, FT_ERR_SHAPE,
+           "hidden*inter must be a positive multiple of 4");
+  int prev = -1;
+  cudaGetDevice(&prev);
+  if (prev != ctx->device) cudaSetDevice(ctx->device);
+  ft_moe* m = new ft_moe();
+  m->device = ctx->device;
+  m->E = n_experts;
+  m->H = hidden;
+  m->F = inter;
+  m->top_k = top_k;
+  m->use_gelu = use_gelu;
+  m->counts_host.assign(n_experts + 1, 0);
+  int st = FT_OK;
+  cudaError_t e = cudaMalloc(&m->router, (size_t)n_experts * hidden * 4);
+  if (e == cudaSuccess)
+    e = cudaMemcpy(m->router, router_host, (size_t)n_experts * hidden * 4, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) st = fail(FT_ERR_GPU, "router upload failed: %s", cudaGetErrorString(e));
+  const size_t mat_bytes = (size_t)(inter * hidden) / 4;
+  std::vector<uint8_t> gu_bytes(2 * mat_bytes);
+  std::vector<float> gu_scales(2 * inter);
+  for (int64_t x = 0; x < n_experts && st == FT_OK; ++x) {
+    // [gate; up] stacked: the flat code streams of two row-major matrices
+    // concatenate into one [2F, H] matrix (F*H % 4 == 0 keeps bytes aligned).
+    memcpy(gu_bytes.data(), gate_packed[x], mat_bytes);
+    memcpy(gu_bytes.data() + mat_bytes, up_packed[x], mat_bytes);
+    memcpy(gu_scales.data(), gate_scales[x], inter * 4);
+    memcpy(gu_scales.data() + inter, up_scales[x], inter * 4);
+    ft_weight* w = nullptr;
+    st = ft_weight_upload_packed_u8(ctx, gu_bytes.data(), 2 * inter, hidden, gu_scales.data(), &w);
+    if (st != FT_OK) break;
+    m->gate_up.push_back(w);
+    st = ft_weight_upload_packed_u8(ctx, down_packed[x], hidden, inter, down_scales[x], &w);
+    if (st != FT_OK) break;
+    m->down.push_back(w);
+  }
+  if (prev >= 0 && prev != ctx->device) cudaSetDevice(prev);
+  if (st != FT_OK) {
+    for (auto* w : m->gate_up) ft_weight_destroy(w);
+    for (auto* w : m->down) ft_weight_destroy(w);
+    if (m->router) cudaFree(m->router);
+    delete m;
+    return st;
+  }
+  *out = m;
+  return FT_OK;
+}
+
+int ft_moe_destroy(ft_moe* m) {
+  if (!m) return FT_OK;
+  int prev = -1;
+  cudaGetDevice(&prev);
+  if (prev != m->device) cudaSetDevice(m->device);
+  cudaDeviceSynchronize();
+  for (auto* w : m->gate_up) ft_weight_destroy(w);
+  for (auto* w : m->down) ft_weight_destroy(w);
+  if (m->router) cudaFree(m->router);
+  if (m->buf.ptr) cudaFree(m->buf.ptr);
+  if (prev >= 0 && prev != m->device) cudaSetDevice(prev);
+  delete m;
+  return FT_OK;
+}
+
+int ft_moe_route(ft_ctx* ctx, ft_moe* m, int64_t T, const void* x_dev, int x_is_bf16,
+                 int32_t* topk_idx_dev, float* topk_w_dev, float* probs_dev, int32_t* counts_dev,
+                 void* stream) {
+  FT_CHECK(ctx && m && counts_dev && (T == 0 || (x_dev && topk_idx_dev && topk_w_dev)),
+           FT_ERR_SHAPE, "null argument");
+  return moe_route(ctx, m, T, x_dev, x_is_bf16, topk_idx_dev, topk_w_dev, probs_dev, counts_dev,
+                   static_cast<cudaStream_t>(stream));
+}
+
+int ft_moe_dispatch_layout(ft_ctx* ctx, ft_moe* m, int64_t T, const int32_t* topk_idx_dev,
+                           const int32_t* counts_dev, int32_t* offsets_dev, int32_t* fill_dev,
+                           int32_t* slot_of_dev, int32_t* token_of_dev, void* stream) {
+  FT_CHECK(ctx && m && counts_dev && offsets_dev && fill_dev, FT_ERR_SHAPE, "null argument");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  moe_offsets_kernel<<<1, 32, 0, s>>>(counts_dev, (int)m->E, offsets_dev, fill_dev);
+  FT_LAUNCH_CHECK();
+  const int64_t n = T * m->top_k;
+  if (n == 0) return FT_OK;
+  moe_scatter_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(topk_idx_dev, n, m->top_k,
+                                                                offsets_dev, fill_dev, slot_of_dev,
+                                                                token_of_dev);
+  FT_LAUNCH_CHECK();
+  return FT_OK;
+}
+
+int ft_moe_gather_rows(ft_ctx* ctx, const void* x_dev, int elem_bytes, int64_t H,
+                       const int32_t* token_of_dev, int64_t n_rows, void* out_dev, void* stream) {
+  FT_CHECK(ctx && (n_rows == 0 || (x_dev && token_of_dev && out_dev)), FT_ERR_SHAPE,
+           "null argument");
+  FT_CHECK(elem_bytes == 2 || elem_bytes == 4, FT_ERR_SHAPE, "elem_bytes must be 2 or 4");
+  if (n_rows == 0) return FT_OK;
+  moe_gather_kernel<<<(unsigned)n_rows, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+      x_dev, elem_bytes, H, token_of_dev, n_rows, out_dev);
+  FT_LAUNCH_CHECK();
+  return FT_OK;
+}
+
+int ft_moe_expert_ffn(ft_ctx* ctx, ft_moe* m, int nseg, const int32_t* seg_expert_host,
+                      const int64_t* seg_rows_host, const void* x_rows_dev, int x_is_bf16,
+                      float* y_rows_dev, void* stream) {
+  FT_CHECK(ctx && m && (nseg == 0 || (seg_expert_host && seg_rows_host && x_rows_dev && y_rows_dev)),
+           FT_ERR_SHAPE, "null argument");
+  int64_t total = 0;
+  for (int i = 0; i < nseg; ++i) total += seg_rows_host[i] > 0 ? seg_rows_host[i] : 0;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // gate/up and activation scratch: 3F floats per row
+  int st = moe_reserve(m, (size_t)total * 3 * m->F * 4 + 512, s);
+  if (st != FT_OK) return st;
+  float* gu = static_cast<float*>(m->buf.ptr);
+  float* h = gu + round_up(total * 2 * m->F, 64);
+  return moe_expert_segments(ctx, m, nseg, seg_expert_host, seg_rows_host, x_rows_dev, x_is_bf16,
+                             gu, h, y_rows_dev, s);
+}
+
+int ft_moe_combine(ft_ctx* ctx, ft_moe* m, int64_t T, const float* o_rows_dev,
+                   const int32_t* slot_of_dev, const float* topk_w_dev, float* y_dev, void* stream) {
+  FT_CHECK(ctx && m && (T == 0 || (o_rows_dev && slot_of_dev && topk_w_dev && y_dev)),
+           FT_ERR_SHAPE, "null argument");
+  if (T == 0) return FT_OK;
+  moe_combine_kernel<<<(unsigned)ceil_div(T * m->H, 256), 256, 0,
+                       static_cast<cudaStream_t>(stream)>>>(o_rows_dev, slot_of_dev, topk_w_dev, T,
+                                                            m->top_k, m->H, y_dev);
+  FT_LAUNCH_CHECK();
+  return FT_OK;
+}
+
+int ft_moe_forward(ft_ctx* ctx, ft_moe* m, int64_t T, const void* x_dev, int x_is_bf16,
+                   float* y_dev, float* probs_dev, void* stream) {
+  FT_CHECK(ctx && m && (T == 0 || (x_dev && y_dev)), FT_ERR_SHAPE, "null argument");
+  if (T == 0) return FT_OK;
+  int prev = -1;
+  cudaGetDevice(&prev);
+  if (prev != ctx->device) FT_CUDA(cudaSetDevice(ctx->device));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int xb = x_is_bf16 ? 2 : 4;
+  MoeBufs b;
+  const size_t need = moe_layout(m, T, xb, nullptr, &b);
+  int st = moe_reserve(m, need, s);
+  if (st == FT_OK) {
+    moe_layout(m, T, xb, static_cast<char*>(m->buf.ptr), &b);
+    st = moe_route(ctx, m, T, x_dev, x_is_bf16, b.topk_idx, b.topk_w, probs_dev, b.counts, s);
+  }
+  if (st == FT_OK)
+    st = ft_moe_dispatch_layout(ctx, m, T, b.topk_idx, b.counts, b.offsets, b.fill, b.slot_of,
+                                b.token_of, s);
+  if (st == FT_OK)
+    st = ft_moe_gather_rows(ctx, x_dev, xb, m->H, b.token_of, T * m->top_k, b.xg, s);
+  // The per-expert row counts size the grouped launches: one small read-back.
+  if (st == FT_OK) {
+    cudaError_t e = cudaMemcpyAsync(m->counts_host.data(), b.counts, m->E * 4,
+                                    cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) st = fail(FT_ERR_GPU, "expert counts read-back failed: %s", cudaGetErrorString(e));
+  }
+  if (st == FT_OK) {
+    std::vector<int32_t> ex(m->E);
+    std::vector<int64_t> rows(m->E);
+    for (int64_t e = 0; e < m->E; ++e) {
+      ex[e] = (int32_t)e;
+      rows[e] = m->counts_host[e];
+    }
+    st = moe_expert_segments(ctx, m, (int)m->E, ex.data(), rows.data(), b.xg, x_is_bf16, b.gu, b.h,
+                             b.o, s);
+  }
+  if (st == FT_OK) st = ft_moe_combine(ctx, m, T, b.o, b.slot_of, b.topk_w, y_dev, s);
+  if (prev >= 0 && prev != ctx->device) cudaSetDevice(prev);
+  return st;
+}
+
+int ft_moe_forward_host(ft_ctx* ctx, ft_moe* m, const float* input_host, size_t seq,
+                        float* output_host) {
+  FT_CHECK(ctx && m && input_host && output_host, FT_ERR_SHAPE, "null argument");
+  if (seq == 0) return FT_OK;
+  int prev = -1;
+  cudaGetDevice(&prev);
+  if (prev != ctx->device) FT_CUDA(cudaSetDevice(ctx->device));
+  cudaStream_t s = ctx->host_stream;
+  const size_t in_b = seq * (size_t)m->H * 4;
+  float* dx = nullptr;
+  float* dy = nullptr;
+  int st = FT_OK;
+  cudaError_t e = cudaMalloc(&dx, in_b);
+  if (e == cudaSuccess) e = cudaMalloc(&dy, in_b);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(dx, input_host, in_b, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess) st = ft_moe_forward(ctx, m, (int64_t)seq, dx, 0, dy, nullptr, s);
+  if (e == cudaSuccess && st == FT_OK)
+    e = cudaMemcpyAsync(output_host, dy, in_b, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (dx) cudaFree(dx);
+  if (dy) cudaFree(dy);
+  if (prev >= 0 && prev != ctx->device) cudaSetDevice(prev);
+  if (e != cudaSuccess) return fail(FT_ERR_GPU, "moe forward (host) failed: %s", cudaGetErrorString(e));
+  return st;
+}
+
+}  // extern "C"

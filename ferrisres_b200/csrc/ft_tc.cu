@@ -541,7 +541,7 @@ struct PrepSource {
   int64_t seq, K, n_chunks;
   int passes;
 };
-constexpr int kMaxSources = 16;
+constexpr int kMaxSources = 64;
 struct PrepBatch {
   int nsrc;
   int xkind;  // 0 f32, 1 bf16, 2 int8 codes
@@ -672,41 +672,56 @@ int launch_grouped_t(const TqBatch& batch, int64_t grid, cudaStream_t s) {
 
 }  // namespace
 
-// Grouped tensor-core matmul.  All problems share seq and the activation
-// kind; xs[i] may repeat (identical pointers share one prepared B operand).
+// Grouped tensor-core matmul over up to 64 independent problems sharing the
+// activation kind.  Problem i has seqs[i] tokens (or `seq` when seqs is null;
+// problems with 0 tokens are skipped); activations xs[i] [seq_i, cols_i],
+// output ys[i] rows of length ldys[i] (default rows_i).  Entries with the same
+// activation pointer, K and seq share one prepared B operand.
 int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t seq,
                       const void* const* xs, int xkind, const float* const* sxs, float* const* ys,
-                      const int64_t* ldys, cudaStream_t s) {
+                      const int64_t* ldys, cudaStream_t s, const int64_t* seqs) {
   FT_CHECK(n >= 1 && n <= kMaxProblems, FT_ERR_UNSUPPORTED, "group size %d not in [1, %d]", n,
            kMaxProblems);
-  if (seq == 0) return FT_OK;
   const int D = xkind == 2 ? 1 : 4;
-  const int npad = pick_npad(seq * D);
+  int64_t max_seq = 0;
+  for (int i = 0; i < n; ++i) {
+    const int64_t si = seqs ? seqs[i] : seq;
+    FT_CHECK(si >= 0, FT_ERR_SHAPE, "negative seq in group entry %d", i);
+    max_seq = si > max_seq ? si : max_seq;
+  }
+  if (max_seq == 0) return FT_OK;
+  const int npad = pick_npad(max_seq * D);
   const int tok_per_pass = npad / D;
-  const int64_t passes = ceil_div(seq, tok_per_pass);
-  FT_CHECK(passes <= (1 << 20), FT_ERR_UNSUPPORTED, "seq %lld too large", (long long)seq);
+  FT_CHECK(ceil_div(max_seq, tok_per_pass) <= (1 << 20), FT_ERR_UNSUPPORTED, "seq %lld too large",
+           (long long)max_seq);
 
-  // distinct activation sources (by pointer and K)
+  // live problems and their distinct activation sources (pointer, K, seq)
+  int live[kMaxProblems];
+  int nlive = 0;
   int src_of[kMaxProblems];
   int nsrc = 0;
   const void* src_x[kMaxSources];
-  int64_t src_k[kMaxSources];
+  int64_t src_k[kMaxSources], src_seq[kMaxSources];
   for (int i = 0; i < n; ++i) {
+    const int64_t si = seqs ? seqs[i] : seq;
+    if (si == 0) continue;
     FT_CHECK(ws[i] && xs[i] && ys[i], FT_ERR_SHAPE, "null pointer in group entry %d", i);
     FT_CHECK(ws[i]->device == ctx->device, FT_ERR_DEVICE, "weight %d on another device", i);
     FT_CHECK(ws[i]->format == ws[0]->format, FT_ERR_UNSUPPORTED,
              "group mixes dense and 2:4 sparse weights (entry %d)", i);
     FT_CHECK(xkind != 2 || (sxs && sxs[i]), FT_ERR_SHAPE, "null sx in group entry %d", i);
     int j = 0;
-    while (j < nsrc && !(src_x[j] == xs[i] && src_k[j] == ws[i]->cols)) ++j;
+    while (j < nsrc && !(src_x[j] == xs[i] && src_k[j] == ws[i]->cols && src_seq[j] == si)) ++j;
     if (j == nsrc) {
       FT_CHECK(nsrc < kMaxSources, FT_ERR_UNSUPPORTED, "more than %d distinct activations",
                kMaxSources);
       src_x[nsrc] = xs[i];
       src_k[nsrc] = ws[i]->cols;
+      src_seq[nsrc] = si;
       ++nsrc;
     }
-    src_of[i] = j;
+    src_of[nlive] = j;
+    live[nlive++] = i;
   }
 
   // workspace: per source B operand, column sums, token scales
@@ -714,12 +729,13 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
   size_t b_off[kMaxSources], cs_off[kMaxSources], ts_off[kMaxSources];
   for (int j = 0; j < nsrc; ++j) {
     const int64_t nch = ceil_div(src_k[j], kChunkK);
+    const int64_t passes = ceil_div(src_seq[j], tok_per_pass);
     b_off[j] = off;
     off = round_up((int64_t)(off + (size_t)(passes * nch) * npad * 128), 256);
     cs_off[j] = off;
     off = round_up((int64_t)(off + passes * npad * 4), 256);
     ts_off[j] = off;
-    off = round_up((int64_t)(off + seq * 8), 256);
+    off = round_up((int64_t)(off + src_seq[j] * 8), 256);
   }
   int st = workspace_reserve(ctx, off, s);
   if (st != FT_OK) return st;
@@ -730,17 +746,21 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
   // thread, which is what limits a small-N launch); one otherwise.
   const int64_t grid_target = (int64_t)ctx->num_sms * (tmem_cols_for(npad) <= 256 ? 2 : 1);
   int64_t tiles_total = 0;
-  for (int i = 0; i < n; ++i) tiles_total += ws[i]->n_tiles * passes;
+  for (int q = 0; q < nlive; ++q)
+    tiles_total += ws[live[q]]->n_tiles * ceil_div(src_seq[src_of[q]], tok_per_pass);
   size_t zoff = 0;
   size_t acc_off[kMaxProblems], cnt_off[kMaxProblems];
   static thread_local TqBatch batch;  // host staging; the launch copies it as the parameter
   memset(&batch, 0, sizeof(batch));
-  batch.nprob = n;
+  batch.nprob = nlive;
   batch.digits = D;
   int64_t items = 0;
-  for (int i = 0; i < n; ++i) {
+  for (int q = 0; q < nlive; ++q) {
+    const int i = live[q];
     const ft_weight* w = ws[i];
-    TqProblem& p = batch.p[i];
+    const int j = src_of[q];
+    const int64_t passes = ceil_div(src_seq[j], tok_per_pass);
+    TqProblem& p = batch.p[q];
     // Split K only when the group has too few tiles to give every CTA work
     // (narrow passes: aim at ~4 items per CTA; wide passes, whose split-K
     // partials are costly to combine: only when tiles are fewer than CTAs/2).
@@ -756,23 +776,22 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
     p.rows = w->rows;
     p.n_tiles = w->n_tiles;
     p.n_chunks = w->n_chunks;
-    const int j = src_of[i];
     p.bmat = reinterpret_cast<const int8_t*>(wsb + b_off[j]);
     p.colsum = reinterpret_cast<const int32_t*>(wsb + cs_off[j]);
     p.tok_scale = reinterpret_cast<const double*>(wsb + ts_off[j]);
     p.sx = sxs ? sxs[i] : nullptr;
     p.y = ys[i];
     p.ldy = ldys ? ldys[i] : w->rows;
-    p.seq = seq;
+    p.seq = src_seq[j];
     p.tok_per_pass = tok_per_pass;
     p.passes = (int)passes;
     p.item_begin = items;
     items += passes * w->n_tiles * p.ksplit;
-    acc_off[i] = cnt_off[i] = 0;
+    acc_off[q] = cnt_off[q] = 0;
     if (p.ksplit > 1) {
-      acc_off[i] = zoff;
+      acc_off[q] = zoff;
       zoff = round_up((int64_t)(zoff + (size_t)(passes * w->n_tiles) * npad * kTileRows * 4), 256);
-      cnt_off[i] = zoff;
+      cnt_off[q] = zoff;
       zoff = round_up((int64_t)(zoff + passes * w->n_tiles * 4), 256);
     }
   }
@@ -781,10 +800,10 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
   st = zero_scratch_reserve(ctx, err_off + 256, s);
   if (st != FT_OK) return st;
   char* zs = static_cast<char*>(ctx->zs.ptr);
-  for (int i = 0; i < n; ++i)
-    if (batch.p[i].ksplit > 1) {
-      batch.p[i].acc = reinterpret_cast<int32_t*>(zs + acc_off[i]);
-      batch.p[i].cnt = reinterpret_cast<int32_t*>(zs + cnt_off[i]);
+  for (int q = 0; q < nlive; ++q)
+    if (batch.p[q].ksplit > 1) {
+      batch.p[q].acc = reinterpret_cast<int32_t*>(zs + acc_off[q]);
+      batch.p[q].cnt = reinterpret_cast<int32_t*>(zs + cnt_off[q]);
     }
   batch.err = reinterpret_cast<int*>(zs + err_off);
   ctx->err_flag = batch.err;
@@ -800,13 +819,14 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
     pb.tok_per_pass = tok_per_pass;
     int64_t blocks = 0;
     for (int j = 0; j < nsrc; ++j) {
+      const int64_t passes = ceil_div(src_seq[j], tok_per_pass);
       pb.block_begin[j] = blocks;
       PrepSource& ps = pb.s[j];
       ps.x = src_x[j];
       ps.bmat = reinterpret_cast<int8_t*>(wsb + b_off[j]);
       ps.colsum = reinterpret_cast<int32_t*>(wsb + cs_off[j]);
       ps.tok_scale = reinterpret_cast<double*>(wsb + ts_off[j]);
-      ps.seq = seq;
+      ps.seq = src_seq[j];
       ps.K = src_k[j];
       ps.n_chunks = ceil_div(src_k[j], kChunkK);
       ps.passes = (int)passes;
@@ -828,7 +848,7 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
   }
 
   const int64_t grid = items < grid_target ? items : grid_target;
-  if (ws[0]->format == 1) {
+  if (ws[live[0]]->format == 1) {
     switch (npad) {
       case 16: return launch_grouped_t<16, true>(batch, grid, s);
       case 32: return launch_grouped_t<32, true>(batch, grid, s);
@@ -852,7 +872,8 @@ int launch_tc_matmul(ft_ctx* ctx, const ft_weight* w, int64_t seq, const void* x
   const void* xs[1] = {x};
   const float* sxs[1] = {sx};
   float* ys[1] = {y};
-  return launch_tc_grouped(ctx, 1, ws, seq, xs, xkind, xkind == 2 ? sxs : nullptr, ys, nullptr, s);
+  return launch_tc_grouped(ctx, 1, ws, seq, xs, xkind, xkind == 2 ? sxs : nullptr, ys, nullptr, s,
+                           nullptr);
 }
 
 }  // namespace ft

@@ -44,7 +44,7 @@ typedef enum ft_status {
 
 typedef struct ft_ctx ft_ctx;       /* one CUDA device + workspace */
 typedef struct ft_weight ft_weight; /* one dense ternary matrix resident in HBM */
-typedef struct ft_sparse ft_sparse; /* one 2:4 sparse ternary matrix resident in HBM */
+typedef struct ft_moe ft_moe;       /* one ternary MoE FFN layer resident in HBM */
 
 /* ---- library / context ------------------------------------------------ */
 const char* ft_version(void);
@@ -178,6 +178,54 @@ int ft_gpu_sparse_ternary_matmul(ft_ctx* ctx, const uint32_t* sparse_words_host,
  * weights already resident (ft_weight); host activations in, host output out. */
 int ft_gpu_ternary_matmul_vram(ft_ctx* ctx, const ft_weight* w, const float* input_host,
                                size_t seq_len, float* output_host);
+
+/* ---- MoE FFN layer: TernaryMoELayer (src/model/ternary_moe.rs:77-223) ------
+ * router_host: [n_experts, hidden] fp32, row e = expert e (the layout
+ * TernaryMoELayer::forward indexes, ternary_moe.rs:157).  Per expert e:
+ * gate/up [inter, hidden] and down [hidden, inter] in the reference pack_ternary
+ * byte layout with per-row scales.  top_k <= 8, n_experts <= 64, SwiGLU
+ * (use_gelu = 0) or GeLU-tanh (use_gelu = 1). */
+int ft_moe_create(ft_ctx* ctx, int64_t n_experts, int64_t hidden, int64_t inter, int top_k,
+                  int use_gelu, const float* router_host, const uint8_t* const* gate_packed,
+                  const float* const* gate_scales, const uint8_t* const* up_packed,
+                  const float* const* up_scales, const uint8_t* const* down_packed,
+                  const float* const* down_scales, ft_moe** out);
+int ft_moe_destroy(ft_moe* m);
+/* Whole layer on one GPU: y [T, hidden] fp32 from x [T, hidden] (fp32, or bf16
+ * bit patterns when x_is_bf16).  probs_dev (optional, [T, n_experts]) receives
+ * the router softmax.  Reads back the per-expert token counts once (a stream
+ * synchronisation) to size the expert launches.  Replaces
+ * TernaryMoELayer::forward (src/model/ternary_moe.rs:145). */
+int ft_moe_forward(ft_ctx* ctx, ft_moe* m, int64_t T, const void* x_dev, int x_is_bf16,
+                   float* y_dev, float* probs_dev, void* stream);
+/* Same with host buffers (fp32), the reference's &[f32] -> Vec<f32> form. */
+int ft_moe_forward_host(ft_ctx* ctx, ft_moe* m, const float* input_host, size_t seq,
+                        float* output_host);
+/* Stages, for expert-parallel hosts that exchange tokens between them:
+ * route: top-k experts and gates per token ([T, top_k]) and per-expert counts
+ * ([n_experts], zeroed first); probs_dev optional. */
+int ft_moe_route(ft_ctx* ctx, ft_moe* m, int64_t T, const void* x_dev, int x_is_bf16,
+                 int32_t* topk_idx_dev, float* topk_w_dev, float* probs_dev, int32_t* counts_dev,
+                 void* stream);
+/* Expert-major slots: offsets [n_experts + 1] (exclusive scan of counts), fill
+ * [n_experts] scratch, slot_of [T*top_k] (slot of entry t*top_k + k), token_of
+ * [T*top_k] (token of each slot). */
+int ft_moe_dispatch_layout(ft_ctx* ctx, ft_moe* m, int64_t T, const int32_t* topk_idx_dev,
+                           const int32_t* counts_dev, int32_t* offsets_dev, int32_t* fill_dev,
+                           int32_t* slot_of_dev, int32_t* token_of_dev, void* stream);
+/* out[r, :] = x[token_of[r], :] for r < n_rows (elem_bytes 2 or 4). */
+int ft_moe_gather_rows(ft_ctx* ctx, const void* x_dev, int elem_bytes, int64_t H,
+                       const int32_t* token_of_dev, int64_t n_rows, void* out_dev, void* stream);
+/* Expert FFN (gate/up, activation, down) over rows stored in segments: segment
+ * i holds seg_rows[i] consecutive rows for expert seg_expert[i] (host arrays,
+ * at most 64 segments).  y_rows [sum rows, hidden] fp32. */
+int ft_moe_expert_ffn(ft_ctx* ctx, ft_moe* m, int nseg, const int32_t* seg_expert_host,
+                      const int64_t* seg_rows_host, const void* x_rows_dev, int x_is_bf16,
+                      float* y_rows_dev, void* stream);
+/* y[t] = sum_k w[t, k] * o[slot_of[t*top_k + k]] in top-k order (the
+ * reference's accumulation order, ternary_moe.rs:217-221). */
+int ft_moe_combine(ft_ctx* ctx, ft_moe* m, int64_t T, const float* o_rows_dev,
+                   const int32_t* slot_of_dev, const float* topk_w_dev, float* y_dev, void* stream);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop
