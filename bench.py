@@ -33,6 +33,8 @@ import subprocess
 import sys
 import time
 
+import numpy as np
+
 ROOT = os.path.dirname(os.path.abspath(__file__))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
@@ -521,6 +523,94 @@ def run_sparse(args, ws, rank, local):
     }
 
 
+# ------------------------------------------------------------- cfg4 MoE ---
+M_E, M_H, M_F, M_T, M_K = 64, 2048, 1408, 4096, 2
+M_OPS = M_T * M_K * (3 * 2 * M_H * M_F) + 2 * M_T * M_E * M_H
+
+
+def _rand_packed(rng, rows, cols):
+    """Reference pack_ternary bytes of a matrix with P(-1)=P(0)=P(+1)=1/3."""
+    c = rng.integers(0, 3, size=(rows * cols // 4, 4), dtype=np.uint8)
+    return (c[:, 0] | (c[:, 1] << 2) | (c[:, 2] << 4) | (c[:, 3] << 6)).astype(np.uint8)
+
+
+def run_moe(args, ws, rank, local):
+    """ternary MoE FFN layer, 64 experts, H=2048, F=1408,
+    SwiGLU, top-2, 4096 bf16 tokens; expert-parallel over the ranks (rank r
+    holds experts [r*64/N, (r+1)*64/N) and routes 4096/N tokens).  One step = one
+    layer forward over the global batch.  value = 4096 tokens / max-over-ranks
+    device time (strong scaling: the layer and batch are fixed)."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from ferrisres_b200 import moe, moe_ep
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if ws > 1 and not dist.is_initialized():
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    rng = np.random.default_rng(4)
+    router = (rng.standard_normal(M_E * M_H) * 0.02).astype(np.float32)
+    router = torch.from_numpy(router).to(torch.bfloat16).float().numpy()  # bf16 router weights
+    per = M_E // ws
+    mine = range(rank * per, (rank + 1) * per)
+    g, u, d, gs, us, ds = [], [], [], [], [], []
+    for e in range(M_E):
+        wrng = np.random.default_rng(1000 + e)
+        if e in mine:
+            g.append(_rand_packed(wrng, M_F, M_H)); u.append(_rand_packed(wrng, M_F, M_H))
+            d.append(_rand_packed(wrng, M_H, M_F))
+            gs.append(wrng.uniform(0.01, 0.1, M_F).astype(np.float32))
+            us.append(wrng.uniform(0.01, 0.1, M_F).astype(np.float32))
+            ds.append(wrng.uniform(0.01, 0.1, M_H).astype(np.float32))
+        else:
+            for lst in (g, u, d, gs, us, ds):
+                lst.append(None)
+    layer = moe.TernaryMoELayer(router, g, gs, u, us, d, ds, M_H, M_F, M_K, device=local)
+    be = moe_ep.GpuMoEBackend(layer)
+    gx = torch.Generator(device=device).manual_seed(99)
+    x = torch.randn(M_T, M_H, generator=gx, device=device).to(torch.bfloat16)
+    shard = x.chunk(ws)[rank].contiguous()
+    stream = torch.cuda.Stream(device=device)
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            moe_ep.ep_forward(shard, be, M_E, rank, ws)
+    torch.cuda.synchronize()
+    if ws > 1:
+        dist.barrier()
+    sampler = ClockSampler(local)
+    sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(args.steps):
+            moe_ep.ep_forward(shard, be, M_E, rank, ws)
+        e1.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    t = torch.tensor([e0.elapsed_time(e1) / 1e3], device=device, dtype=torch.float64)
+    if ws > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    sec = float(t.item()) / args.steps
+    res = {
+        "metric": "MoE-layer tokens/s", "value": round(M_T / sec, 1), "unit": "tokens/s",
+        "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded ternary experts, bf16 router and tokens)",
+        "config": {"workload": "cfg4 ternary MoE FFN: 64 experts, H=2048, F=1408, SwiGLU, top-2, "
+                               "4096 tokens", "parallelism": f"ep{ws}",
+                   "experts_per_gpu": per, "tokens_per_gpu": M_T // ws},
+        "algorithmic_TOPS": round(M_OPS / sec / 1e12, 2),
+        "clocks": clocks,
+    }
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -530,7 +620,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--group", type=int, default=16, help="GEMVs per launch (1..64)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--workload", choices=["gemv", "gemm_cfg2", "sparse_cfg3"], default="gemv",
+    ap.add_argument("--workload", choices=["gemv", "gemm_cfg2", "sparse_cfg3", "moe_cfg4"], default="gemv",
                     help="gemv = the headline cfg0 line; gemm_cfg2 = the int8 prefill GEMM")
     args = ap.parse_args()
     ws, rank, local = dist_env()
@@ -540,6 +630,8 @@ def main():
         res = run_gemm(args, ws, rank, local)
     elif args.workload == "sparse_cfg3" and args.impl == "ours":
         res = run_sparse(args, ws, rank, local)
+    elif args.workload == "moe_cfg4" and args.impl == "ours":
+        res = run_moe(args, ws, rank, local)
     elif args.impl == "reference":
         res = run_reference(args, ws, rank)
     else:

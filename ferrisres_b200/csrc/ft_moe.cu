@@ -273,6 +273,8 @@ int moe_expert_segments(ft_ctx* ctx, ft_moe* m, int nseg, const int32_t* seg_exp
     FT_CHECK(seg_expert[i] >= 0 && seg_expert[i] < m->E, FT_ERR_SHAPE, "segment %d: bad expert %d",
              i, seg_expert[i]);
     FT_CHECK(seg_rows[i] >= 0, FT_ERR_SHAPE, "segment %d: negative rows", i);
+    FT_CHECK(m->gate_up[seg_expert[i]] && m->down[seg_expert[i]], FT_ERR_SHAPE,
+             "segment %d: expert %d is not held by this layer", i, seg_expert[i]);
     wgu[i] = m->gate_up[seg_expert[i]];
     wd[i] = m->down[seg_expert[i]];
     xs[i] = static_cast<const char*>(x_rows) + total * m->H * xb;
@@ -332,6 +334,13 @@ int ft_moe_create(ft_ctx* ctx, int64_t n_experts, int64_t hidden, int64_t inter,
   std::vector<uint8_t> gu_bytes(2 * mat_bytes);
   std::vector<float> gu_scales(2 * inter);
   for (int64_t x = 0; x < n_experts && st == FT_OK; ++x) {
+    if (!gate_packed[x]) {  // expert held by another rank (expert parallelism)
+      m->gate_up.push_back(nullptr);
+      m->down.push_back(nullptr);
+      continue;
+    }
+    FT_CHECK(up_packed[x] && down_packed[x] && gate_scales[x] && up_scales[x] && down_scales[x],
+             FT_ERR_SHAPE, "expert %lld: gate given but up/down/scales missing", (long long)x);
     // [gate; up] stacked: the flat code streams of two row-major matrices
     // concatenate into one [2F, H] matrix (F*H % 4 == 0 keeps bytes aligned).
     memcpy(gu_bytes.data(), gate_packed[x], mat_bytes);

@@ -33,14 +33,17 @@ class TernaryMoELayer:
         keep = [r]
 
         def arr(lst, dt, n):
-            out = []
+            ptrs = []
             for a in lst:
+                if a is None:  # expert held by another rank
+                    ptrs.append(None)
+                    continue
                 a = _host(a, dt)
                 if a.size < n:
                     raise ShapeError("per-expert buffer too small")
-                out.append(a)
-            keep.extend(out)
-            return (C.c_void_p * E)(*[a.ctypes.data for a in out])
+                keep.append(a)
+                ptrs.append(a.ctypes.data)
+            return (C.c_void_p * E)(*ptrs)
 
         mb = inter * hidden // 4
         h = C.c_void_p()
@@ -57,9 +60,9 @@ class TernaryMoELayer:
     def from_ternary(cls, router, gate, gate_scales, up, up_scales, down, down_scales, hidden,
                      inter, top_k=2, use_gelu=False, device=None):
         """Per-expert int8 {-1,0,1} value arrays (reference TernaryWeight::from_ternary)."""
-        return cls(router, [pack_ternary(g) for g in gate], gate_scales,
-                   [pack_ternary(u) for u in up], up_scales, [pack_ternary(d) for d in down],
-                   down_scales, hidden, inter, top_k, use_gelu, device)
+        pk = lambda a: None if a is None else pack_ternary(a)
+        return cls(router, [pk(g) for g in gate], gate_scales, [pk(u) for u in up], up_scales,
+                   [pk(d) for d in down], down_scales, hidden, inter, top_k, use_gelu, device)
 
     def forward_device(self, x: torch.Tensor, probs: bool = False, stream=None):
         """x [T, H] float32 or bfloat16 CUDA tensor -> y [T, H] float32 (and softmax probs)."""

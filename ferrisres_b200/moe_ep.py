@@ -1,0 +1,129 @@
+"""Expert-parallel MoE layer: experts sharded over the ranks of a process group.
+
+Rank r holds experts [r*E/W, (r+1)*E/W) and routes its own tokens.  One layer
+forward is:
+  1. route (router GEMV + softmax + top-k, on the GPU) and build the
+     expert-major layout of this rank's (token, k) entries;
+  2. exchange the per-expert counts (all_gather of E int32 per rank);
+  3. dispatch: all_to_all_single of the gathered activation rows to the
+     experts' owners (uneven splits from the counts);
+  4. every owner runs ONE grouped expert launch over its (source rank,
+     local expert) segments;
+  5. combine: the reverse all_to_all_single brings the expert outputs back in
+     the order they were sent, then the top-k weighted sum per token.
+The reference has no expert parallelism (its distributed transports are
+simulated, src/compute/distributed.rs:167-174); this is new.  Collectives run
+on torch.distributed (NCCL over NVLink on B200, gloo in the CPU tests).  The
+compute stages come from a backend: ``GpuMoEBackend`` calls
+libferris_ternary.so; the tests plug in a CPU backend to check the exchange
+bookkeeping on gloo ranks.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from ._lib import ShapeError, call
+
+
+def _p(t):
+    return C.c_void_p(t.data_ptr()) if t is not None else None
+
+
+class GpuMoEBackend:
+    """Stages of ft_moe_* on the current CUDA stream."""
+
+    def __init__(self, layer):
+        self.layer = layer
+        self.E, self.K, self.H = layer.n_experts, layer.top_k, layer.hidden_dim
+
+    def _s(self):
+        return C.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+    def route(self, x):
+        T = x.shape[0]
+        dev = x.device
+        idx = torch.empty(T, self.K, dtype=torch.int32, device=dev)
+        w = torch.empty(T, self.K, dtype=torch.float32, device=dev)
+        counts = torch.empty(self.E, dtype=torch.int32, device=dev)
+        call("ft_moe_route", self.layer.ctx.handle, self.layer.handle, T, _p(x),
+             int(x.dtype == torch.bfloat16), _p(idx), _p(w), None, _p(counts), self._s())
+        return idx, w, counts
+
+    def layout(self, idx, counts):
+        T = idx.shape[0]
+        dev = idx.device
+        offs = torch.empty(self.E + 1, dtype=torch.int32, device=dev)
+        fill = torch.empty(self.E, dtype=torch.int32, device=dev)
+        slot_of = torch.empty(T * self.K, dtype=torch.int32, device=dev)
+        token_of = torch.empty(T * self.K, dtype=torch.int32, device=dev)
+        call("ft_moe_dispatch_layout", self.layer.ctx.handle, self.layer.handle, T, _p(idx),
+             _p(counts), _p(offs), _p(fill), _p(slot_of), _p(token_of), self._s())
+        return slot_of, token_of
+
+    def gather(self, x, token_of):
+        n = token_of.numel()
+        out = torch.empty(n, self.H, dtype=x.dtype, device=x.device)
+        call("ft_moe_gather_rows", self.layer.ctx.handle, _p(x), x.element_size(), self.H,
+             _p(token_of), n, _p(out), self._s())
+        return out
+
+    def experts(self, seg_experts, seg_rows, x_rows):
+        total = int(sum(seg_rows))
+        out = torch.empty(total, self.H, dtype=torch.float32, device=x_rows.device)
+        if len(seg_experts):
+            e = np.ascontiguousarray(seg_experts, np.int32)
+            r = np.ascontiguousarray(seg_rows, np.int64)
+            call("ft_moe_expert_ffn", self.layer.ctx.handle, self.layer.handle, len(e),
+                 e.ctypes.data_as(C.c_void_p), r.ctypes.data_as(C.c_void_p), _p(x_rows),
+                 int(x_rows.dtype == torch.bfloat16), _p(out), self._s())
+        return out
+
+    def combine(self, o_rows, slot_of, w):
+        T = w.shape[0]
+        y = torch.empty(T, self.H, dtype=torch.float32, device=o_rows.device)
+        call("ft_moe_combine", self.layer.ctx.handle, self.layer.handle, T, _p(o_rows),
+             _p(slot_of), _p(w), _p(y), self._s())
+        return y
+
+
+def ep_forward(x, backend, n_experts, rank=0, world=1, group=None):
+    """One expert-parallel MoE forward of this rank's tokens x [T, H]."""
+    E = n_experts
+    if E % world:
+        raise ShapeError(f"{E} experts do not split over {world} ranks")
+    per = E // world
+    H = x.shape[1]
+    idx, w, counts = backend.route(x)
+    slot_of, token_of = backend.layout(idx, counts)
+    xg = backend.gather(x, token_of)  # [T*K, H], expert-major
+    if world == 1:
+        ac = counts.cpu().numpy().reshape(1, E).astype(np.int64)
+    else:
+        parts = [torch.empty_like(counts) for _ in range(world)]
+        dist.all_gather(parts, counts, group=group)
+        ac = torch.stack(parts).cpu().numpy().astype(np.int64)  # [src rank, expert]
+    send_rows = [int(ac[rank, d * per:(d + 1) * per].sum()) for d in range(world)]
+    recv_rows = [int(ac[s, rank * per:(rank + 1) * per].sum()) for s in range(world)]
+    if world == 1:
+        recv = xg
+    else:
+        recv = torch.empty(sum(recv_rows), H, dtype=xg.dtype, device=xg.device)
+        dist.all_to_all_single(recv.view(-1), xg.reshape(-1), [r * H for r in recv_rows],
+                               [r * H for r in send_rows], group=group)
+    seg_e, seg_n = [], []
+    for s in range(world):
+        for e in range(rank * per, (rank + 1) * per):
+            seg_e.append(e)
+            seg_n.append(int(ac[s, e]))
+    o_recv = backend.experts(seg_e, seg_n, recv)
+    if world == 1:
+        o_send = o_recv
+    else:
+        o_send = torch.empty(xg.shape[0], H, dtype=o_recv.dtype, device=xg.device)
+        dist.all_to_all_single(o_send.view(-1), o_recv.view(-1), [r * H for r in send_rows],
+                               [r * H for r in recv_rows], group=group)
+    return backend.combine(o_send, slot_of, w)

@@ -184,7 +184,9 @@ int ft_gpu_ternary_matmul_vram(ft_ctx* ctx, const ft_weight* w, const float* inp
  * TernaryMoELayer::forward indexes, ternary_moe.rs:157).  Per expert e:
  * gate/up [inter, hidden] and down [hidden, inter] in the reference pack_ternary
  * byte layout with per-row scales.  top_k <= 8, n_experts <= 64, SwiGLU
- * (use_gelu = 0) or GeLU-tanh (use_gelu = 1). */
+ * (use_gelu = 0) or GeLU-tanh (use_gelu = 1).  For expert parallelism a rank
+ * passes NULL gate/up/down pointers for the experts it does not hold; the
+ * router is always complete. */
 int ft_moe_create(ft_ctx* ctx, int64_t n_experts, int64_t hidden, int64_t inter, int top_k,
                   int use_gelu, const float* router_host, const uint8_t* const* gate_packed,
                   const float* const* gate_scales, const uint8_t* const* up_packed,

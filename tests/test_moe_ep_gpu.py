@@ -1,0 +1,87 @@
+"""Expert-parallel MoE layer on 2 GPUs (NCCL over NVLink): every rank holds
+only its experts and routes its own tokens; the gathered result must equal
+the single-GPU layer bit for bit (same kernels, same per-token arithmetic).
+Skipped with fewer than 2 GPUs."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def build_params(E, H, F, seed=0):
+    rng = np.random.default_rng(seed)
+    router = torch.from_numpy((rng.standard_normal(E * H) * 0.02).astype(np.float32)) \
+        .to(torch.bfloat16).float().numpy()
+    g = [rng.integers(-1, 2, size=F * H).astype(np.int8) for _ in range(E)]
+    u = [rng.integers(-1, 2, size=F * H).astype(np.int8) for _ in range(E)]
+    d = [rng.integers(-1, 2, size=H * F).astype(np.int8) for _ in range(E)]
+    gs = [rng.uniform(0.01, 0.1, F).astype(np.float32) for _ in range(E)]
+    us = [rng.uniform(0.01, 0.1, F).astype(np.float32) for _ in range(E)]
+    ds = [rng.uniform(0.01, 0.1, H).astype(np.float32) for _ in range(E)]
+    x = torch.from_numpy(rng.standard_normal((256, H)).astype(np.float32)).to(torch.bfloat16)
+    return router, g, gs, u, us, d, ds, x
+
+
+def _worker(rank, world, port, E, H, F, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    from ferrisres_b200 import moe, moe_ep
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        router, g, gs, u, us, d, ds, x = build_params(E, H, F)
+        per = E // world
+        mine = range(rank * per, (rank + 1) * per)
+        keep = lambda lst: [a if e in mine else None for e, a in enumerate(lst)]
+        layer = moe.TernaryMoELayer.from_ternary(router, keep(g), keep(gs), keep(u), keep(us),
+                                                 keep(d), keep(ds), H, F, 2, device=rank)
+        shard = x.chunk(world)[rank].cuda()
+        y = moe_ep.ep_forward(shard, moe_ep.GpuMoEBackend(layer), E, rank, world)
+        torch.cuda.synchronize()
+        q.put((rank, y.cpu().numpy()))
+    except Exception as e:  # surface the failure to the parent instead of a queue timeout
+        q.put((rank, repr(e)))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep_two_gpus_equals_single_gpu():
+    import torch.multiprocessing as mp
+
+    from ferrisres_b200 import moe
+    E, H, F, world = 8, 512, 256, 2
+    router, g, gs, u, us, d, ds, x = build_params(E, H, F)
+    layer = moe.TernaryMoELayer.from_ternary(router, g, gs, u, us, d, ds, H, F, 2, device=0)
+    ref = layer.forward_device(x.cuda()).cpu().numpy()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, E, H, F, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=300) for _ in range(world))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for r in range(world):
+        assert not isinstance(got[r], str), f"rank {r} failed: {got[r]}"
+    y = np.concatenate([got[r] for r in range(world)])
+    assert (y.view(np.uint32) == ref.view(np.uint32)).all()
