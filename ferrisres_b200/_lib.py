@@ -91,6 +91,17 @@ SIGNATURES = {
     "ft_moe_gather_rows": [_p, _p, _i, _i64, _p, _i64, _p, _p],
     "ft_moe_expert_ffn": [_p, _p, _i, _p, _p, _p, _i, _p, _p],
     "ft_moe_combine": [_p, _p, _i64, _p, _p, _p, _p, _p],
+    "ft_kv3_create": [_p, _i64, _i64, _i64, _i64, _p],
+    "ft_kv3_destroy": [_p],
+    "ft_kv3_append": [_p, _p, _i64, _p, _p, _i, _p],
+    "ft_kv3_append_packed": [_p, _p, _i64, _p, _p, _p, _p, _p],
+    "ft_kv3_len": [_p, _p],
+    "ft_kv3_capacity": [_p, _p],
+    "ft_kv3_evict_front": [_p, _i64],
+    "ft_kv3_reset": [_p],
+    "ft_kv3_get_range": [_p, _p, _i64, _i64, _p, _p, _p],
+    "ft_kv3_export_range": [_p, _p, _i64, _i64, _p, _p, _p, _p, _p],
+    "ft_flash_decode_3bit": [_p, _p, _p, _i64, C.c_float, _p, _p],
 }
 _RESTYPE = {"ft_version": C.c_char_p, "ft_last_error_string": C.c_char_p,
             "ft_launch_counter": C.c_uint64}

@@ -1,0 +1,1049 @@
+// 3-bit KV cache (TurboQuantKVCache, src/inference/turboquant_kv.rs:173-411) and
+// the split-S flash-decode that reads it (math of flash_decode_ref,
+// tests/kernel_tests.rs:1073-1110, with the GQA head map kv_h = h / (Hq/Hkv) of
+// src/model/cpu_block_attn_res.rs:471-472).
+//
+// Quantisation, per head vector of 128 values (the reference's group of 128 at
+// kv_dim = Hkv * 128; turboquant_kv.rs:83-117): min, max, range = max - min,
+// scale = 7 / range, code = clamp(round((v - min) * scale), 0, 7) (0 when
+// range == 0); dequant = min + code * ((max - min) / 7).  The append kernel
+// reproduces those roundings, so the stored codes and (min, max) equal the
+// reference's bit for bit; the export kernel rebuilds the reference byte stream
+// (8 codes -> 3 bytes, LSB first, :35-74) from them.
+//
+// Device layout.  Positions live in a ring of `cap` slots (cap a multiple of
+// 32); logical position p of the cache is slot (head + p) % cap, so evicting
+// the oldest positions only moves `head`.  Per (sequence, kv head) "row":
+//   K records  [row][cap][48 B]: one record per slot, in "quad-major" order
+//              so that the tensor-core operand of a lane group comes out of
+//              three words: for lane group r in 0..3, words 3r, 3r+1 hold the
+//              low 2 bits and word 3r+2 the high bit of the codes of the 32
+//              dims {4(r + 4i) + b : i in 0..7, b in 0..3}: the low bits of
+//              dim 4(r+4i)+b sit in word 3r + i/4 at bit 8b + 2(i%4), its
+//              high bit in word 3r+2 at bit 8b + i.
+//   V blocks   [row][cap/32][128 dims][3 words]: the codes of 32 consecutive
+//              slots of one dim; slot u of the block (quad i = u/4, b = u%4)
+//              keeps its low bits in word i/4 at bit 8b + 2(i%4) and its high
+//              bit in word 2 at bit 8b + i.
+//   min/max    [row][cap] float2 for K and for V.
+// 3 bits per code either way: 48 B of codes + 8 B of (min, max) per vector,
+// the reference's footprint.  Shifting a word by 2(i%4) and masking with
+// 0x03030303, and the high word by i and masking with 0x01010101, yields the 4
+// codes of a quad as 4 bytes: the int8 operand of a tensor-core MMA.
+//
+// Decode, per (sequence, kv head, group of <=4 q heads, split of the slots):
+// four compute warps each take one 32-slot block of every 128-slot tile; a
+// producer warp streams tiles into a 4-stage shared-memory ring with 1-D bulk
+// copies.  Scores: mma.m16n8k32 with A = K codes (16 slots x 32 dims) and B =
+// the q heads as 4 signed base-256 digits of round(q * 2^30 / absmax(q)),
+// accumulated exactly in int32; q.k = min * sum(q) + (max-min)/7 * sum(q_i c_i).
+// Online softmax in base 2.  P.V: mma.m16n8k32 with A = V codes (16 dims x 32
+// slots) and B = the weights w = p * (max-min)/7 as 4 unsigned base-256 digits
+// of round(w * 2^E); the digit sums stay exact in int32 and fold into fp32 only
+// when the running max or the scale 2^E changes, and at the end.  The
+// min * p term is a per-head scalar added to every dim.  Each split writes
+// (m, l, numerator) partials; a combine kernel merges the splits.
+#include <cmath>
+#include <cstring>
+
+#include "ft_internal.cuh"
+#include "ft_tc.cuh"
+
+struct ft_kv3 {
+  int device = 0;
+  int64_t batch = 0, kv_heads = 0, cap = 0;  // cap: slots per row, multiple of 32
+  int64_t head = 0, len = 0;                   // ring start slot, live positions
+  uint8_t* kc = nullptr;   // K records
+  uint32_t* vc = nullptr;  // V blocks
+  float2* kmm = nullptr;
+  float2* vmm = nullptr;
+  ft::Workspace part;  // split partials
+};
+
+namespace ft {
+namespace {
+
+constexpr int kD = 128;                  // head dim = quantisation group
+constexpr int kRec = 48;                 // bytes of codes per vector
+constexpr int kBlk = 32;                 // slots per V block
+constexpr int kBlkBytes = kBlk * kRec;   // 1536 (both K and V)
+constexpr int kMmBlkBytes = kBlk * 8;    // 256
+constexpr int kDecWarps = 4;             // compute warps = blocks per tile
+constexpr int kStages = 4;
+constexpr int kStageBytes = kDecWarps * (2 * kBlkBytes + 2 * kMmBlkBytes);  // 14336
+constexpr int kOffV = kDecWarps * kBlkBytes;
+constexpr int kOffKmm = 2 * kDecWarps * kBlkBytes;
+constexpr int kOffVmm = kOffKmm + kDecWarps * kMmBlkBytes;
+constexpr int kWsmBytes = kDecWarps * 4 * 4 * kBlk;  // [warp][head][digit][32 slots]
+constexpr int kQdBytes = 4 * 4 * kD;                 // [head][digit][128 dims] int8
+constexpr int kDecSmem = kStages * kStageBytes + kWsmBytes + kQdBytes + 64 + 16 * kStages;
+constexpr int kPart = 2 + kD;  // partial record: m (log2 domain), l, numerator[128]
+
+__device__ __forceinline__ float load_act(const void* p, int64_t i, int bf16) {
+  return bf16 ? __uint_as_float((uint32_t) static_cast<const uint16_t*>(p)[i] << 16)
+              : static_cast<const float*>(p)[i];
+}
+
+// code of dim d in a K record
+__device__ __forceinline__ uint32_t krec_code(const uint32_t* w, int d) {
+  const int qd = d >> 2, b = d & 3, r = qd & 3, i = qd >> 2;
+  const uint32_t lo = (w[3 * r + (i >> 2)] >> (8 * b + 2 * (i & 3))) & 3u;
+  const uint32_t hi = (w[3 * r + 2] >> (8 * b + i)) & 1u;
+  return lo | (hi << 2);
+}
+
+// code of slot u (0..31) in a V (block, dim) triple
+__device__ __forceinline__ uint32_t vtri_code(const uint32_t* w, int u) {
+  const int i = u >> 2, b = u & 3;
+  const uint32_t lo = (w[i >> 2] >> (8 * b + 2 * (i & 3))) & 3u;
+  const uint32_t hi = (w[2] >> (8 * b + i)) & 1u;
+  return lo | (hi << 2);
+}
+
+// ---------------------------------------------------------------- append --
+struct AppendParams {
+  const void* k;  // kPacked: reference bytes [B][n][Hkv*48]; else values [B][n][Hkv][128]
+  const void* v;
+  const float* kmm_in;  // kPacked only: [B][n][Hkv][2]
+  const float* vmm_in;
+  int bf16;
+  int64_t n_pos, Hkv, cap, nbc, s0;
+  uint8_t* kc;
+  uint32_t* vc;
+  float2* kmm;
+  float2* vmm;
+};
+
+// code idx of a reference LSB-first 3-bit stream (the next byte is read only
+// when the code straddles it)
+__device__ __forceinline__ uint32_t ref_stream_code(const uint8_t* bytes, int64_t idx) {
+  const int64_t bit = 3 * idx;
+  const int64_t by = bit >> 3;
+  uint32_t w = bytes[by];
+  if ((bit & 7) > 5) w |= (uint32_t)bytes[by + 1] << 8;
+  return (w >> (bit & 7)) & 7u;
+}
+
+// One CTA per (32-slot block touched, row); thread = dim.  Quantises each new
+// position of the block (or takes its codes from a reference byte stream),
+// writes the K record and min/max, and rewrites the dim's V triple once.
+template <bool kPacked>
+__global__ void __launch_bounds__(kD) kv3_append_kernel(AppendParams p) {
+  const int64_t x = blockIdx.x, row = blockIdx.y;
+  const int64_t b = row / p.Hkv, h = row % p.Hkv;
+  const int d = threadIdx.x, warp = d >> 5, lane = d & 31;
+  const int64_t off0 = p.s0 % kBlk;
+  const int64_t pb = (p.s0 / kBlk + x) % p.nbc;
+  const int64_t u_begin = x == 0 ? off0 : 0;
+  int64_t u_end = p.n_pos + off0 - x * kBlk;
+  if (u_end > kBlk) u_end = kBlk;
+  __shared__ float red[kDecWarps][4];
+  __shared__ uint32_t rec[12];
+  uint32_t* vw = p.vc + ((row * p.nbc + pb) * kD + d) * 3;
+  uint32_t v0 = vw[0], v1 = vw[1], v2 = vw[2];
+  for (int64_t u = u_begin; u < u_end; ++u) {
+    const int64_t pi = x * kBlk + u - off0;  // input position
+    const int64_t slot = pb * kBlk + u;
+    const int64_t vec = (b * p.n_pos + pi) * p.Hkv + h;
+    uint32_t ck, cv;
+    float kmin, kmax, vmin, vmax;
+    if (kPacked) {
+      const int64_t rowbytes = p.Hkv * kRec;
+      const uint8_t* kb = static_cast<const uint8_t*>(p.k) + (b * p.n_pos + pi) * rowbytes;
+      const uint8_t* vb = static_cast<const uint8_t*>(p.v) + (b * p.n_pos + pi) * rowbytes;
+      ck = ref_stream_code(kb, h * kD + d);
+      cv = ref_stream_code(vb, h * kD + d);
+      kmin = p.kmm_in[vec * 2];
+      kmax = p.kmm_in[vec * 2 + 1];
+      vmin = p.vmm_in[vec * 2];
+      vmax = p.vmm_in[vec * 2 + 1];
+    } else {
+      const float xk = load_act(p.k, vec * kD + d, p.bf16);
+      const float xv = load_act(p.v, vec * kD + d, p.bf16);
+      float a0 = xk, a1 = xk, a2 = xv, a3 = xv;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        a0 = fminf(a0, __shfl_xor_sync(0xffffffffu, a0, o));
+        a1 = fmaxf(a1, __shfl_xor_sync(0xffffffffu, a1, o));
+        a2 = fminf(a2, __shfl_xor_sync(0xffffffffu, a2, o));
+        a3 = fmaxf(a3, __shfl_xor_sync(0xffffffffu, a3, o));
+      }
+      if (lane == 0) {
+        red[warp][0] = a0;
+        red[warp][1] = a1;
+        red[warp][2] = a2;
+        red[warp][3] = a3;
+      }
+      __syncthreads();
+      kmin = fminf(fminf(red[0][0], red[1][0]), fminf(red[2][0], red[3][0]));
+      kmax = fmaxf(fmaxf(red[0][1], red[1][1]), fmaxf(red[2][1], red[3][1]));
+      vmin = fminf(fminf(red[0][2], red[1][2]), fminf(red[2][2], red[3][2]));
+      vmax = fmaxf(fmaxf(red[0][3], red[1][3]), fmaxf(red[2][3], red[3][3]));
+      // quantize_3bit (turboquant_kv.rs:83-107), same roundings
+      const float kr = __fsub_rn(kmax, kmin), vr = __fsub_rn(vmax, vmin);
+      ck = 0;
+      if (kr > 0.0f) {
+        const float q = roundf(__fmul_rn(__fsub_rn(xk, kmin), __fdiv_rn(7.0f, kr)));
+        ck = q <= 0.0f ? 0u : (q >= 7.0f ? 7u : (uint32_t)q);
+      }
+      cv = 0;
+      if (vr > 0.0f) {
+        const float q = roundf(__fmul_rn(__fsub_rn(xv, vmin), __fdiv_rn(7.0f, vr)));
+        cv = q <= 0.0f ? 0u : (q >= 7.0f ? 7u : (uint32_t)q);
+      }
+    }
+    if (d < 12) rec[d] = 0u;
+    __syncthreads();
+    {
+      const int qd = d >> 2, bb = d & 3, r = qd & 3, i = qd >> 2;
+      atomicOr(&rec[3 * r + (i >> 2)], (ck & 3u) << (8 * bb + 2 * (i & 3)));
+      atomicOr(&rec[3 * r + 2], ((ck >> 2) & 1u) << (8 * bb + i));
+    }
+    {
+      const int i = (int)(u >> 2), bb = (int)(u & 3);
+      const int sl = 8 * bb + 2 * (i & 3), sh = 8 * bb + i;
+      const uint32_t lo_mask = 3u << sl, lo_bits = (cv & 3u) << sl;
+      if ((i >> 2) == 0)
+        v0 = (v0 & ~lo_mask) | lo_bits;
+      else
+        v1 = (v1 & ~lo_mask) | lo_bits;
+      v2 = (v2 & ~(1u << sh)) | (((cv >> 2) & 1u) << sh);
+    }
+    __syncthreads();
+    if (d < 12)
+      reinterpret_cast<uint32_t*>(p.kc + (row * p.cap + slot) * kRec)[d] = rec[d];
+    if (d == 0) p.kmm[row * p.cap + slot] = make_float2(kmin, kmax);
+    if (d == 1) p.vmm[row * p.cap + slot] = make_float2(vmin, vmax);
+    __syncthreads();
+  }
+  vw[0] = v0;
+  vw[1] = v1;
+  vw[2] = v2;
+}
+
+// ------------------------------------------------------- read-back kernels --
+struct RangeParams {
+  int64_t B, Hkv, cap, nbc, head, start, n;
+  const uint8_t* kc;
+  const uint32_t* vc;
+  const float2* kmm;
+  const float2* vmm;
+};
+
+// get_range (turboquant_kv.rs:271-291): out [B][n][Hkv][128] f32, dequantised
+// with the reference's roundings (dequantize_3bit :110-117).
+__global__ void kv3_dequant_kernel(RangeParams p, float* __restrict__ kout,
+                                   float* __restrict__ vout) {
+  const int64_t vec = blockIdx.x;  // (b, pos, h)
+  const int d = threadIdx.x;
+  const int64_t h = vec % p.Hkv;
+  const int64_t pos = (vec / p.Hkv) % p.n;
+  const int64_t b = vec / (p.Hkv * p.n);
+  const int64_t row = b * p.Hkv + h;
+  const int64_t slot = (p.head + p.start + pos) % p.cap;
+  const uint32_t* kr = reinterpret_cast<const uint32_t*>(p.kc + (row * p.cap + slot) * kRec);
+  const uint32_t* vt = p.vc + ((row * p.nbc + slot / kBlk) * kD + d) * 3;
+  const uint32_t ck = krec_code(kr, d), cv = vtri_code(vt, (int)(slot % kBlk));
+  const float2 km = p.kmm[row * p.cap + slot], vm = p.vmm[row * p.cap + slot];
+  float kv, vv;
+  if (km.y == km.x) {
+    kv = km.x;
+  } else {
+    kv = __fadd_rn(km.x, __fmul_rn((float)ck, __fdiv_rn(__fsub_rn(km.y, km.x), 7.0f)));
+  }
+  if (vm.y == vm.x) {
+    vv = vm.x;
+  } else {
+    vv = __fadd_rn(vm.x, __fmul_rn((float)cv, __fdiv_rn(__fsub_rn(vm.y, vm.x), 7.0f)));
+  }
+  kout[vec * kD + d] = kv;
+  vout[vec * kD + d] = vv;
+}
+
+// The reference's stored form: codes [B][n][Hkv*48] bytes (pack_3bit over the
+// whole kv_dim vector) and (min, max) [B][n][Hkv][2].  Thread = 8 codes.
+__global__ void kv3_export_kernel(RangeParams p, uint8_t* __restrict__ kbytes,
+                                  float* __restrict__ kmm_out, uint8_t* __restrict__ vbytes,
+                                  float* __restrict__ vmm_out) {
+  const int64_t vec = blockIdx.x;  // (b, pos, h)
+  const int m = threadIdx.x;       // 0..15: codes 8m..8m+7
+  const int64_t h = vec % p.Hkv;
+  const int64_t pos = (vec / p.Hkv) % p.n;
+  const int64_t b = vec / (p.Hkv * p.n);
+  const int64_t row = b * p.Hkv + h;
+  const int64_t slot = (p.head + p.start + pos) % p.cap;
+  const uint32_t* kr = reinterpret_cast<const uint32_t*>(p.kc + (row * p.cap + slot) * kRec);
+  const uint32_t* vbase = p.vc + ((row * p.nbc + slot / kBlk) * kD) * 3;
+  const int u = (int)(slot % kBlk);
+  uint32_t kbits = 0, vbits = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int d = 8 * m + j;
+    kbits |= krec_code(kr, d) << (3 * j);
+    vbits |= vtri_code(vbase + d * 3, u) << (3 * j);
+  }
+  const int64_t o = vec * kRec + 3 * m;  // [B][n][Hkv][48] == [B][n][Hkv*48]
+  kbytes[o] = (uint8_t)(kbits & 0xFF);
+  kbytes[o + 1] = (uint8_t)((kbits >> 8) & 0xFF);
+  kbytes[o + 2] = (uint8_t)((kbits >> 16) & 0xFF);
+  vbytes[o] = (uint8_t)(vbits & 0xFF);
+  vbytes[o + 1] = (uint8_t)((vbits >> 8) & 0xFF);
+  vbytes[o + 2] = (uint8_t)((vbits >> 16) & 0xFF);
+  if (m == 0) {
+    const float2 km = p.kmm[row * p.cap + slot], vm = p.vmm[row * p.cap + slot];
+    kmm_out[vec * 2] = km.x;
+    kmm_out[vec * 2 + 1] = km.y;
+    vmm_out[vec * 2] = vm.x;
+    vmm_out[vec * 2 + 1] = vm.y;
+  }
+}
+
+// ---------------------------------------------------------------- decode --
+struct DecodeParams {
+  const float* q;  // [B][Hq][128]
+  int64_t Hq, Hkv;
+  int G, hgroups;  // q heads per kv head, CTAs (groups of <=4 q heads) per kv head
+  int64_t cap, nbc, head_off, head_blk, len;
+  int64_t nlb;        // logical 32-slot blocks covering the live range
+  int64_t tiles_per;  // 128-slot tiles per split
+  float qk_log2;      // softmax scale * log2(e)
+  const uint8_t* kc;
+  const uint32_t* vc;
+  const float2* kmm;
+  const float2* vmm;
+  float* part;  // [B][Hq][nsplit][kPart]
+  int* err;
+};
+
+__device__ __forceinline__ void mma_u8s8(int (&c)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+      "{%8, %9}, {%0, %1, %2, %3};"
+      : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void mma_u8u8(int (&c)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+      "{%8, %9}, {%0, %1, %2, %3};"
+      : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// 4 codes of a quad as bytes: low bits from `lo` at `lo_shift`, high bit
+// already moved to bit 2 of each byte in `hi_sh`.
+__device__ __forceinline__ uint32_t quad_bytes(uint32_t lo, int lo_shift, uint32_t hi_sh) {
+  return ((lo >> lo_shift) & 0x03030303u) | (hi_sh & 0x04040404u);
+}
+
+// exact int32 digit sums -> float: sum_j 256^j d_j
+__device__ __forceinline__ float digits4(int d0, int d1, int d2, int d3) {
+  const long long v = (long long)d0 + ((long long)d1 << 8) + ((long long)d2 << 16) +
+                      ((long long)d3 << 24);
+  return (float)v;
+}
+
+__global__ void __launch_bounds__((kDecWarps + 1) * 32)
+    kv3_decode_kernel(const __grid_constant__ DecodeParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* wsm = smem + kStages * kStageBytes;                          // W digits
+  int8_t* qd = reinterpret_cast<int8_t*>(wsm + kWsmBytes);              // q digits
+  float* qinfo = reinterpret_cast<float*>(wsm + kWsmBytes + kQdBytes);  // qsum[4], qscale[4]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(wsm + kWsmBytes + kQdBytes + 64);
+  const uint32_t full0 = tc::smem_u32(bars), empty0 = full0 + 8 * kStages;
+
+  const int split = blockIdx.x;
+  const int64_t kvh = blockIdx.y / p.hgroups;
+  const int hg = blockIdx.y % p.hgroups;
+  const int64_t b = blockIdx.z;
+  const int64_t row = b * p.Hkv + kvh;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, r = lane & 3;
+  int nheads = p.G - 4 * hg;
+  if (nheads > 4) nheads = 4;
+  const int64_t qh0 = kvh * p.G + 4 * hg;  // first q head of this CTA
+
+  const int64_t ntiles_all = (p.nlb + kDecWarps - 1) / kDecWarps;
+  const int64_t t_begin = (int64_t)split * p.tiles_per;
+  int64_t t_end = t_begin + p.tiles_per;
+  if (t_end > ntiles_all) t_end = ntiles_all;
+  const int ntiles = t_end > t_begin ? (int)(t_end - t_begin) : 0;
+
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      tc::mbar_init(full0 + 8 * s, 1);
+      tc::mbar_init(empty0 + 8 * s, kDecWarps);
+    }
+    tc::fence_barrier_init();
+  }
+  // q prep: warp w < 4 turns head w of the group (zeros past nheads) into
+  // 4 signed base-256 digits of round(q * 2^30 / absmax)
+  if (warp < 4) {
+    float qv[4];
+    const bool valid = warp < nheads;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      qv[j] = valid ? p.q[((b * p.Hq) + qh0 + warp) * kD + 4 * lane + j] : 0.0f;
+    float amax = fmaxf(fmaxf(fabsf(qv[0]), fabsf(qv[1])), fmaxf(fabsf(qv[2]), fabsf(qv[3])));
+    float sum = (qv[0] + qv[1]) + (qv[2] + qv[3]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    }
+    const float mul = amax > 0.0f ? __fdiv_rn(1073741824.0f, amax) : 0.0f;  // 2^30 / amax
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      int X = __float2int_rn(qv[j] * mul);
+      const int dim = 4 * lane + j;
+#pragma unroll
+      for (int dg = 0; dg < 3; ++dg) {
+        const int lo = ((X & 255) ^ 128) - 128;  // signed digit in [-128, 127]
+        qd[(warp * 4 + dg) * kD + dim] = (int8_t)lo;
+        X = (X - lo) >> 8;
+      }
+      qd[(warp * 4 + 3) * kD + dim] = (int8_t)X;  // |X| <= 65 here
+    }
+    if (lane == 0) {
+      qinfo[warp] = sum;
+      qinfo[4 + warp] = amax * 9.313225746154785e-10f;  // amax / 2^30
+    }
+  }
+  __syncthreads();
+
+  const uint32_t stage_base = tc::smem_u32(smem);
+  if (warp == kDecWarps) {
+    // ------------------------------------------------------ producer warp --
+    if (lane == 0) {
+      bool ok = true;
+      int issued = 0;
+      for (int it = 0; it < ntiles && ok; ++it) {
+        const int s = it % kStages;
+        if (it >= kStages)
+          ok = tc::mbar_wait(empty0 + 8 * s, ((it / kStages) - 1) & 1, p.err, 31);
+        if (!ok) break;
+        const int64_t j0 = (t_begin + it) * kDecWarps;
+        uint32_t bytes = 0;
+        for (int w = 0; w < kDecWarps; ++w)
+          if (j0 + w < p.nlb) bytes += 2 * kBlkBytes + 2 * kMmBlkBytes;
+        tc::mbar_arrive_expect_tx(full0 + 8 * s, bytes);
+        const uint32_t sb = stage_base + s * kStageBytes;
+        for (int w = 0; w < kDecWarps; ++w) {
+          const int64_t j = j0 + w;
+          if (j >= p.nlb) break;
+          const int64_t pb = (p.head_blk + j) % p.nbc;
+          tc::bulk_g2s(sb + w * kBlkBytes, p.kc + (row * p.cap + pb * kBlk) * kRec, kBlkBytes,
+                       full0 + 8 * s);
+          tc::bulk_g2s(sb + kOffV + w * kBlkBytes, p.vc + (row * p.nbc + pb) * (kD * 3),
+                       kBlkBytes, full0 + 8 * s);
+          tc::bulk_g2s(sb + kOffKmm + w * kMmBlkBytes, p.kmm + row * p.cap + pb * kBlk,
+                       kMmBlkBytes, full0 + 8 * s);
+          tc::bulk_g2s(sb + kOffVmm + w * kMmBlkBytes, p.vmm + row * p.cap + pb * kBlk,
+                       kMmBlkBytes, full0 + 8 * s);
+        }
+        ++issued;
+      }
+      // the copies of the last stages must land before the CTA may exit
+      for (int it = issued - kStages < 0 ? 0 : issued - kStages; it < issued; ++it)
+        tc::mbar_wait(full0 + 8 * (it % kStages), (it / kStages) & 1, p.err, 32);
+    }
+    return;
+  }
+
+  // -------------------------------------------------------- compute warps --
+  // B fragments of q: column n = g <-> (head g/2, digit g%2 + 2*nb)
+  uint32_t bq[4][2][2];
+#pragma unroll
+  for (int ks = 0; ks < 4; ++ks)
+#pragma unroll
+    for (int nb = 0; nb < 2; ++nb) {
+      const int8_t* src = qd + ((g >> 1) * 4 + (g & 1) + 2 * nb) * kD + 32 * ks + 4 * r;
+      bq[ks][nb][0] = *reinterpret_cast<const uint32_t*>(src);
+      bq[ks][nb][1] = *reinterpret_cast<const uint32_t*>(src + 16);
+    }
+  const float qsum = qinfo[r], qscale = qinfo[4 + r];
+
+  float m_run = -INFINITY, l_part = 0.0f, vmin_part = 0.0f;
+  float o[16];  // head r, dims 16*mb + g + 8*h at o[2*mb + h]
+#pragma unroll
+  for (int i = 0; i < 16; ++i) o[i] = 0.0f;
+  int pv[8][2][4];
+#pragma unroll
+  for (int mb = 0; mb < 8; ++mb)
+#pragma unroll
+    for (int nb = 0; nb < 2; ++nb)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) pv[mb][nb][c] = 0;
+  float wmul = 0.0f, wbound = 0.0f;  // W = p * vs * wmul, valid while vs < wbound
+  uint8_t* my_w = wsm + warp * (4 * 4 * kBlk);
+  bool ok = true;
+
+  auto fold = [&](float inv) {
+#pragma unroll
+    for (int mb = 0; mb < 8; ++mb)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const float v =
+            digits4(pv[mb][0][2 * h], pv[mb][0][2 * h + 1], pv[mb][1][2 * h], pv[mb][1][2 * h + 1]);
+        o[2 * mb + h] = fmaf(v, inv, o[2 * mb + h]);
+      }
+#pragma unroll
+    for (int mb = 0; mb < 8; ++mb)
+#pragma unroll
+      for (int nb = 0; nb < 2; ++nb)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) pv[mb][nb][c] = 0;
+  };
+
+  for (int it = 0; it < ntiles; ++it) {
+    const int s = it % kStages;
+    if (ok) ok = tc::mbar_wait(full0 + 8 * s, (it / kStages) & 1, p.err, 33);
+    const int64_t j = (t_begin + it) * kDecWarps + warp;
+    if (ok && j < p.nlb) {
+      const uint8_t* sb = smem + s * kStageBytes;
+      const uint8_t* kb = sb + warp * kBlkBytes;
+      const uint32_t* vb = reinterpret_cast<const uint32_t*>(sb + kOffV + warp * kBlkBytes);
+      const float2* kmt = reinterpret_cast<const float2*>(sb + kOffKmm) + warp * kBlk;
+      const float2* vmt = reinterpret_cast<const float2*>(sb + kOffVmm) + warp * kBlk;
+      // ---- scores: slots u = 16*mb + g + 8*h
+      float s2[4], vsv[4], vmn[4];
+#pragma unroll
+      for (int mb = 0; mb < 2; ++mb) {
+        int acc[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+        const uint32_t* k0 = reinterpret_cast<const uint32_t*>(kb + (16 * mb + g) * kRec) + 3 * r;
+        const uint32_t* k1 = k0 + 8 * (kRec / 4);
+        const uint32_t l00 = k0[0], l01 = k0[1], h0 = k0[2];
+        const uint32_t l10 = k1[0], l11 = k1[1], h1 = k1[2];
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+          const int i0 = 2 * ks, i1 = 2 * ks + 1;
+          const uint32_t la = ks < 2 ? l00 : l01, lb = ks < 2 ? l10 : l11;
+          // high bit of quad i to bit 2 of each byte: shift right by i-2 (left for i < 2)
+          const uint32_t ha0 = i0 >= 2 ? (h0 >> (i0 - 2)) : (h0 << (2 - i0));
+          const uint32_t hb0 = i0 >= 2 ? (h1 >> (i0 - 2)) : (h1 << (2 - i0));
+          const uint32_t ha1 = i1 >= 2 ? (h0 >> (i1 - 2)) : (h0 << (2 - i1));
+          const uint32_t hb1 = i1 >= 2 ? (h1 >> (i1 - 2)) : (h1 << (2 - i1));
+          uint32_t a[4];
+          a[0] = quad_bytes(la, 2 * (i0 & 3), ha0);
+          a[1] = quad_bytes(lb, 2 * (i0 & 3), hb0);
+          a[2] = quad_bytes(la, 2 * (i1 & 3), ha1);
+          a[3] = quad_bytes(lb, 2 * (i1 & 3), hb1);
+          mma_u8s8(acc[0], a, bq[ks][0][0], bq[ks][0][1]);
+          mma_u8s8(acc[1], a, bq[ks][1][0], bq[ks][1][1]);
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int u = 16 * mb + g + 8 * h;
+          const float S =
+              digits4(acc[0][2 * h], acc[0][2 * h + 1], acc[1][2 * h], acc[1][2 * h + 1]);
+          const float2 km = kmt[u];
+          const float ksc = km.y == km.x ? 0.0f : __fdiv_rn(km.y - km.x, 7.0f);
+          const float dot = fmaf(km.x, qsum, ksc * (S * qscale));
+          const int64_t logical = j * kBlk + u - p.head_off;
+          const bool live = logical >= 0 && logical < p.len;
+          s2[2 * mb + h] = live ? dot * p.qk_log2 : -INFINITY;
+          const float2 vm = vmt[u];
+          vsv[2 * mb + h] = live && vm.y != vm.x ? __fdiv_rn(vm.y - vm.x, 7.0f) : 0.0f;
+          vmn[2 * mb + h] = live ? vm.x : 0.0f;
+        }
+      }
+      // ---- online softmax (head r): max over the block's 32 slots
+      float mt = fmaxf(fmaxf(s2[0], s2[1]), fmaxf(s2[2], s2[3]));
+      float vsmax = fmaxf(fmaxf(vsv[0], vsv[1]), fmaxf(vsv[2], vsv[3]));
+#pragma unroll
+      for (int o2 = 4; o2 < 32; o2 <<= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, o2));
+#pragma unroll
+      for (int o2 = 1; o2 < 32; o2 <<= 1)
+        vsmax = fmaxf(vsmax, __shfl_xor_sync(0xffffffffu, vsmax, o2));
+      const float m_new = fmaxf(m_run, mt);
+      const bool rescale = vsmax >= wbound && vsmax > 0.0f;  // warp-uniform
+      if (m_new > m_run || rescale) {
+        if (wmul > 0.0f) fold(1.0f / wmul);
+        if (rescale) {
+          int e;
+          frexpf(vsmax, &e);  // vsmax < 2^e
+          wbound = ldexpf(1.0f, e);
+          wmul = ldexpf(1.0f, 31 - e);
+        }
+        const float alpha = m_run == -INFINITY ? 0.0f : exp2f(m_run - m_new);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) o[i] *= alpha;
+        l_part *= alpha;
+        vmin_part *= alpha;
+        m_run = m_new;
+      }
+      // ---- probabilities -> W digits in shared memory: my_w[head][digit][slot]
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int u = 16 * (k >> 1) + g + 8 * (k & 1);
+        const float pr = s2[k] == -INFINITY ? 0.0f : exp2f(s2[k] - m_run);
+        l_part += pr;
+        vmin_part = fmaf(pr, vmn[k], vmin_part);
+        const uint32_t W = __float2uint_rn(pr * vsv[k] * wmul);
+#pragma unroll
+        for (int dg = 0; dg < 4; ++dg) my_w[(r * 4 + dg) * kBlk + u] = (uint8_t)(W >> (8 * dg));
+      }
+      __syncwarp();
+      // ---- P.V: B fragments of W, column n = g <-> (head g/2, digit g%2 + 2*nb)
+      uint32_t bw[2][2];
+#pragma unroll
+      for (int nb = 0; nb < 2; ++nb) {
+        const uint8_t* src = my_w + ((g >> 1) * 4 + (g & 1) + 2 * nb) * kBlk + 4 * r;
+        bw[nb][0] = *reinterpret_cast<const uint32_t*>(src);
+        bw[nb][1] = *reinterpret_cast<const uint32_t*>(src + 16);
+      }
+#pragma unroll
+      for (int mb = 0; mb < 8; ++mb) {
+        const uint32_t* v0 = vb + (16 * mb + g) * 3;
+        const uint32_t* v1 = v0 + 8 * 3;
+        const uint32_t a_lo0 = v0[0], a_lo1 = v0[1], a_hi = v0[2];
+        const uint32_t b_lo0 = v1[0], b_lo1 = v1[1], b_hi = v1[2];
+        uint32_t a[4];
+        // quad r: high bit r -> bit 2 via (hi << 2) >> r (bits 30-31 belong to quads 6-7)
+        a[0] = quad_bytes(a_lo0, 2 * r, (a_hi << 2) >> r);
+        a[1] = quad_bytes(b_lo0, 2 * r, (b_hi << 2) >> r);
+        // quad r + 4: low bits in word 1 at 2r, high bit r+4 -> bit 2 via >> (r + 2)
+        a[2] = quad_bytes(a_lo1, 2 * r, a_hi >> (r + 2));
+        a[3] = quad_bytes(b_lo1, 2 * r, b_hi >> (r + 2));
+        mma_u8u8(pv[mb][0], a, bw[0][0], bw[0][1]);
+        mma_u8u8(pv[mb][1], a, bw[1][0], bw[1][1]);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) tc::mbar_arrive(empty0 + 8 * s);
+  }
+  if (wmul > 0.0f) fold(1.0f / wmul);
+#pragma unroll
+  for (int o2 = 4; o2 < 32; o2 <<= 1) {
+    l_part += __shfl_xor_sync(0xffffffffu, l_part, o2);
+    vmin_part += __shfl_xor_sync(0xffffffffu, vmin_part, o2);
+  }
+  // ---- combine the 4 warps in shared memory; the stage buffers are free
+  // (every issued copy has been consumed)
+  asm volatile("bar.sync 1, %0;" ::"r"(kDecWarps * 32) : "memory");
+  float* red = reinterpret_cast<float*>(smem);  // [warp][head][4]
+  float* ored = red + kDecWarps * 4 * 4;        // [warp][head][128]
+  if (g == 0) {
+    red[(warp * 4 + r) * 4 + 0] = m_run;
+    red[(warp * 4 + r) * 4 + 1] = l_part;
+    red[(warp * 4 + r) * 4 + 2] = vmin_part;
+  }
+#pragma unroll
+  for (int mb = 0; mb < 8; ++mb)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) ored[(warp * 4 + r) * kD + 16 * mb + g + 8 * h] = o[2 * mb + h];
+  asm volatile("bar.sync 1, %0;" ::"r"(kDecWarps * 32) : "memory");
+  {
+    const int hh = warp;  // head written by this warp; dims 4*lane..4*lane+3
+    if (hh < nheads) {
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < kDecWarps; ++w) M = fmaxf(M, red[(w * 4 + hh) * 4]);
+      float l = 0.0f, vm = 0.0f, num[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+      for (int w = 0; w < kDecWarps; ++w) {
+        const float mw = red[(w * 4 + hh) * 4];
+        const float f = mw == -INFINITY ? 0.0f : exp2f(mw - M);
+        l = fmaf(f, red[(w * 4 + hh) * 4 + 1], l);
+        vm = fmaf(f, red[(w * 4 + hh) * 4 + 2], vm);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          num[k] = fmaf(f, ored[(w * 4 + hh) * kD + 4 * lane + k], num[k]);
+      }
+      const int nsplit = gridDim.x;
+      float* pp = p.part + (((b * p.Hq) + qh0 + hh) * nsplit + split) * kPart;
+      if (lane == 0) {
+        pp[0] = M;
+        pp[1] = l;
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) pp[2 + 4 * lane + k] = num[k] + vm;
+    }
+  }
+}
+
+// Merges the split partials of one (sequence, q head): thread = dim.
+__global__ void kv3_combine_kernel(const float* __restrict__ part, int nsplit,
+                                   float* __restrict__ out) {
+  const int64_t bh = blockIdx.x;
+  const int d = threadIdx.x;
+  const float* pp = part + bh * nsplit * kPart;
+  float M = -INFINITY;
+  for (int s = 0; s < nsplit; ++s) M = fmaxf(M, pp[s * kPart]);
+  float l = 0.0f, a = 0.0f;
+  for (int s = 0; s < nsplit; ++s) {
+    const float m = pp[s * kPart];
+    if (m == -INFINITY) continue;
+    const float f = exp2f(m - M);
+    l = fmaf(pp[s * kPart + 1], f, l);
+    a = fmaf(pp[s * kPart + 2 + d], f, a);
+  }
+  out[bh * kD + d] = a / l;
+}
+
+// Opts the decode kernel into its dynamic shared memory (once per device) and
+// returns its resident CTAs per SM.
+int decode_occupancy(int device) {
+  static int cached[64] = {0};
+  if (device >= 0 && device < 64 && cached[device]) return cached[device];
+  cudaFuncSetAttribute(kv3_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDecSmem);
+  int occ = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kv3_decode_kernel,
+                                                    (kDecWarps + 1) * 32, kDecSmem) != cudaSuccess ||
+      occ < 1)
+    occ = 1;
+  if (device >= 0 && device < 64) cached[device] = occ;
+  return occ;
+}
+
+// New ring of at least `need` slots; the live blocks are copied in logical
+// order, so the new head is head % 32.
+int grow(ft_kv3* c, int64_t need, cudaStream_t s) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (s) cudaStreamIsCapturing(s, &cs);
+  FT_CHECK(cs == cudaStreamCaptureStatusNone, FT_ERR_UNSUPPORTED,
+           "the 3-bit KV cache must grow but the stream is being captured");
+  int64_t ncap = c->cap * 2;
+  if (ncap < need + kBlk) ncap = need + kBlk;  // room for the head offset
+  ncap = round_up(ncap, kBlk);
+  const int64_t rows = c->batch * c->kv_heads, nbc = c->cap / kBlk, nnbc = ncap / kBlk;
+  uint8_t* kc = nullptr;
+  uint32_t* vc = nullptr;
+  float2 *kmm = nullptr, *vmm = nullptr;
+  cudaError_t e = cudaMalloc(&kc, (size_t)(rows * ncap * kRec));
+  if (e == cudaSuccess) e = cudaMalloc(&vc, (size_t)(rows * ncap * kRec));
+  if (e == cudaSuccess) e = cudaMalloc(&kmm, (size_t)(rows * ncap * 8));
+  if (e == cudaSuccess) e = cudaMalloc(&vmm, (size_t)(rows * ncap * 8));
+  if (e == cudaSuccess) e = cudaMemsetAsync(vc, 0, (size_t)(rows * ncap * kRec), s);
+  if (e != cudaSuccess) {
+    cudaFree(kc);
+    cudaFree(vc);
+    cudaFree(kmm);
+    cudaFree(vmm);
+    return fail(e == cudaErrorMemoryAllocation ? FT_ERR_OOM : FT_ERR_GPU,
+                "3-bit KV cache growth to %lld slots failed: %s", (long long)ncap,
+                cudaGetErrorString(e));
+  }
+  const int64_t hb = c->head / kBlk;
+  const int64_t nlb = c->len == 0 ? 0 : (c->head % kBlk + c->len + kBlk - 1) / kBlk;
+  // runs of physical blocks: [hb, hb + n1) then [0, nlb - n1)
+  const int64_t n1 = nlb < nbc - hb ? nlb : nbc - hb;
+  const int64_t runs[2][3] = {{hb, 0, n1}, {0, n1, nlb - n1}};  // src block, dst block, count
+  const size_t kb = (size_t)kBlkBytes, mb = (size_t)kMmBlkBytes;
+  for (const auto& run : runs) {
+    if (run[2] <= 0) continue;
+    FT_CUDA(cudaMemcpy2DAsync(kc + run[1] * kb, nnbc * kb, c->kc + run[0] * kb, nbc * kb,
+                              run[2] * kb, rows, cudaMemcpyDeviceToDevice, s));
+    FT_CUDA(cudaMemcpy2DAsync(reinterpret_cast<uint8_t*>(vc) + run[1] * kb, nnbc * kb,
+                              reinterpret_cast<uint8_t*>(c->vc) + run[0] * kb, nbc * kb,
+                              run[2] * kb, rows, cudaMemcpyDeviceToDevice, s));
+    FT_CUDA(cudaMemcpy2DAsync(reinterpret_cast<uint8_t*>(kmm) + run[1] * mb, nnbc * mb,
+                              reinterpret_cast<uint8_t*>(c->kmm) + run[0] * mb, nbc * mb,
+                              run[2] * mb, rows, cudaMemcpyDeviceToDevice, s));
+    FT_CUDA(cudaMemcpy2DAsync(reinterpret_cast<uint8_t*>(vmm) + run[1] * mb, nnbc * mb,
+                              reinterpret_cast<uint8_t*>(c->vmm) + run[0] * mb, nbc * mb,
+                              run[2] * mb, rows, cudaMemcpyDeviceToDevice, s));
+  }
+  FT_CUDA(cudaStreamSynchronize(s));
+  cudaFree(c->kc);
+  cudaFree(c->vc);
+  cudaFree(c->kmm);
+  cudaFree(c->vmm);
+  c->kc = kc;
+  c->vc = vc;
+  c->kmm = kmm;
+  c->vmm = vmm;
+  c->cap = ncap;
+  c->head = c->head % kBlk;
+  return FT_OK;
+}
+
+class DeviceScope {
+ public:
+  explicit DeviceScope(int dev) : dev_(dev) {
+    cudaGetDevice(&prev_);
+    if (prev_ != dev) cudaSetDevice(dev);
+  }
+  ~DeviceScope() {
+    if (prev_ >= 0 && prev_ != dev_) cudaSetDevice(prev_);
+  }
+
+ private:
+  int dev_ = 0, prev_ = -1;
+};
+
+int append_common(ft_kv3* c, int64_t n_pos, const AppendParams& proto, bool packed,
+                  cudaStream_t s) {
+  FT_CHECK(n_pos >= 0, FT_ERR_SHAPE, "negative position count");
+  if (n_pos == 0) return FT_OK;
+  {
+    // the new slots must fit the ring, and their blocks must be distinct (one
+    // CTA per block): a range that wraps onto its own first block grows too
+    const int64_t s0 = (c->head + c->len) % c->cap;
+    const int64_t nblk = (s0 % kBlk + n_pos + kBlk - 1) / kBlk;
+    if (c->len + n_pos > c->cap || nblk > c->cap / kBlk) {
+      const int rc = grow(c, c->len + n_pos, s);
+      if (rc != FT_OK) return rc;
+    }
+  }
+  AppendParams p = proto;
+  p.n_pos = n_pos;
+  p.Hkv = c->kv_heads;
+  p.cap = c->cap;
+  p.nbc = c->cap / kBlk;
+  p.s0 = (c->head + c->len) % c->cap;
+  p.kc = c->kc;
+  p.vc = c->vc;
+  p.kmm = c->kmm;
+  p.vmm = c->vmm;
+  const int64_t nblk = (p.s0 % kBlk + n_pos + kBlk - 1) / kBlk;
+  // a block is touched by one CTA only: the new slots never wrap onto a block
+  // that an earlier CTA of this launch also writes
+  FT_CHECK(nblk <= p.nbc, FT_ERR_SHAPE, "append spans more blocks than the ring holds");
+  dim3 grid((unsigned)nblk, (unsigned)(c->batch * c->kv_heads));
+  if (packed)
+    kv3_append_kernel<true><<<grid, kD, 0, s>>>(p);
+  else
+    kv3_append_kernel<false><<<grid, kD, 0, s>>>(p);
+  FT_LAUNCH_CHECK();
+  c->len += n_pos;
+  return FT_OK;
+}
+
+RangeParams range_params(const ft_kv3* c, int64_t start, int64_t n) {
+  RangeParams p;
+  p.B = c->batch;
+  p.Hkv = c->kv_heads;
+  p.cap = c->cap;
+  p.nbc = c->cap / kBlk;
+  p.head = c->head;
+  p.start = start;
+  p.n = n;
+  p.kc = c->kc;
+  p.vc = c->vc;
+  p.kmm = c->kmm;
+  p.vmm = c->vmm;
+  return p;
+}
+
+}  // namespace
+}  // namespace ft
+
+using namespace ft;
+
+extern "C" {
+
+int ft_kv3_create(ft_ctx* ctx, int64_t batch, int64_t kv_heads, int64_t head_dim, int64_t max_seq,
+                  ft_kv3** out) {
+  FT_CHECK(ctx && out, FT_ERR_SHAPE, "null argument");
+  FT_CHECK(head_dim == kD, FT_ERR_UNSUPPORTED,
+           "head_dim must be %d (one quantisation group per head vector)", kD);
+  FT_CHECK(batch > 0 && kv_heads > 0 && max_seq > 0, FT_ERR_SHAPE, "bad cache shape");
+  DeviceScope scope(ctx->device);
+  ft_kv3* c = new ft_kv3();
+  c->device = ctx->device;
+  c->batch = batch;
+  c->kv_heads = kv_heads;
+  c->cap = round_up(max_seq, kBlk);
+  const size_t slots = (size_t)(batch * kv_heads * c->cap);
+  cudaError_t e = cudaMalloc(&c->kc, slots * kRec);
+  if (e == cudaSuccess) e = cudaMalloc(&c->vc, slots * kRec);
+  if (e == cudaSuccess) e = cudaMalloc(&c->kmm, slots * 8);
+  if (e == cudaSuccess) e = cudaMalloc(&c->vmm, slots * 8);
+  // the V blocks start zeroed: append rewrites whole triples, and the decode
+  // reads whole blocks (slots outside the live range get zero weight)
+  if (e == cudaSuccess) e = cudaMemset(c->vc, 0, slots * kRec);
+  if (e != cudaSuccess) {
+    cudaFree(c->kc);
+    cudaFree(c->vc);
+    cudaFree(c->kmm);
+    cudaFree(c->vmm);
+    delete c;
+    return fail(e == cudaErrorMemoryAllocation ? FT_ERR_OOM : FT_ERR_GPU,
+                "3-bit KV cache allocation failed: %s", cudaGetErrorString(e));
+  }
+  *out = c;
+  return FT_OK;
+}
+
+int ft_kv3_destroy(ft_kv3* c) {
+  if (!c) return FT_OK;
+  DeviceScope scope(c->device);
+  cudaDeviceSynchronize();
+  cudaFree(c->kc);
+  cudaFree(c->vc);
+  cudaFree(c->kmm);
+  cudaFree(c->vmm);
+  if (c->part.ptr) cudaFree(c->part.ptr);
+  delete c;
+  return FT_OK;
+}
+
+int ft_kv3_append(ft_ctx* ctx, ft_kv3* c, int64_t n_pos, const void* k_dev, const void* v_dev,
+                  int is_bf16, void* stream) {
+  FT_CHECK(ctx && c && (n_pos == 0 || (k_dev && v_dev)), FT_ERR_SHAPE, "null argument");
+  DeviceScope scope(c->device);
+  AppendParams p{};
+  p.k = k_dev;
+  p.v = v_dev;
+  p.bf16 = is_bf16 ? 1 : 0;
+  return append_common(c, n_pos, p, false, static_cast<cudaStream_t>(stream));
+}
+
+int ft_kv3_append_packed(ft_ctx* ctx, ft_kv3* c, int64_t n_pos, const uint8_t* k_codes_dev,
+                         const float* k_minmax_dev, const uint8_t* v_codes_dev,
+                         const float* v_minmax_dev, void* stream) {
+  FT_CHECK(ctx && c &&
+               (n_pos == 0 || (k_codes_dev && k_minmax_dev && v_codes_dev && v_minmax_dev)),
+           FT_ERR_SHAPE, "null argument");
+  DeviceScope scope(c->device);
+  AppendParams p{};
+  p.k = k_codes_dev;
+  p.v = v_codes_dev;
+  p.kmm_in = k_minmax_dev;
+  p.vmm_in = v_minmax_dev;
+  return append_common(c, n_pos, p, true, static_cast<cudaStream_t>(stream));
+}
+
+int ft_kv3_len(const ft_kv3* c, int64_t* len) {
+  FT_CHECK(c && len, FT_ERR_SHAPE, "null argument");
+  *len = c->len;
+  return FT_OK;
+}
+
+int ft_kv3_capacity(const ft_kv3* c, int64_t* cap) {
+  FT_CHECK(c && cap, FT_ERR_SHAPE, "null argument");
+  *cap = c->cap;
+  return FT_OK;
+}
+
+int ft_kv3_evict_front(ft_kv3* c, int64_t n) {
+  FT_CHECK(c, FT_ERR_SHAPE, "null argument");
+  FT_CHECK(n >= 0, FT_ERR_SHAPE, "negative eviction count");
+  if (n > c->len) n = c->len;
+  c->head = (c->head + n) % c->cap;
+  c->len -= n;
+  return FT_OK;
+}
+
+int ft_kv3_reset(ft_kv3* c) {
+  FT_CHECK(c, FT_ERR_SHAPE, "null argument");
+  c->len = 0;
+  c->head = 0;
+  return FT_OK;
+}
+
+int ft_kv3_get_range(ft_ctx* ctx, const ft_kv3* c, int64_t start, int64_t end, float* k_out_dev,
+                     float* v_out_dev, void* stream) {
+  FT_CHECK(ctx && c && k_out_dev && v_out_dev, FT_ERR_SHAPE, "null argument");
+  FT_CHECK(0 <= start && start <= end && end <= c->len, FT_ERR_SHAPE,
+           "range [%lld, %lld) outside the cache length %lld", (long long)start, (long long)end,
+           (long long)c->len);
+  const int64_t n = end - start;
+  if (n == 0) return FT_OK;
+  DeviceScope scope(c->device);
+  kv3_dequant_kernel<<<(unsigned)(c->batch * n * c->kv_heads), kD, 0,
+                       static_cast<cudaStream_t>(stream)>>>(range_params(c, start, n), k_out_dev,
+                                                            v_out_dev);
+  FT_LAUNCH_CHECK();
+  return FT_OK;
+}
+
+int ft_kv3_export_range(ft_ctx* ctx, const ft_kv3* c, int64_t start, int64_t end,
+                        uint8_t* k_codes_dev, float* k_minmax_dev, uint8_t* v_codes_dev,
+                        float* v_minmax_dev, void* stream) {
+  FT_CHECK(ctx && c && k_codes_dev && k_minmax_dev && v_codes_dev && v_minmax_dev, FT_ERR_SHAPE,
+           "null argument");
+  FT_CHECK(0 <= start && start <= end && end <= c->len, FT_ERR_SHAPE,
+           "range [%lld, %lld) outside the cache length %lld", (long long)start, (long long)end,
+           (long long)c->len);
+  const int64_t n = end - start;
+  if (n == 0) return FT_OK;
+  DeviceScope scope(c->device);
+  kv3_export_kernel<<<(unsigned)(c->batch * n * c->kv_heads), 16, 0,
+                      static_cast<cudaStream_t>(stream)>>>(range_params(c, start, n), k_codes_dev,
+                                                           k_minmax_dev, v_codes_dev,
+                                                           v_minmax_dev);
+  FT_LAUNCH_CHECK();
+  return FT_OK;
+}
+
+int ft_flash_decode_3bit(ft_ctx* ctx, ft_kv3* c, const float* q_dev, int64_t q_heads, float scale,
+                         float* out_dev, void* stream) {
+  FT_CHECK(ctx && c && q_dev && out_dev, FT_ERR_SHAPE, "null argument");
+  FT_CHECK(q_heads > 0 && q_heads % c->kv_heads == 0, FT_ERR_SHAPE,
+           "q_heads (%lld) must be a multiple of kv_heads (%lld)", (long long)q_heads,
+           (long long)c->kv_heads);
+  FT_CHECK(c->len > 0, FT_ERR_SHAPE, "flash decode over an empty cache");
+  DeviceScope scope(c->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  DecodeParams p{};
+  p.q = q_dev;
+  p.Hq = q_heads;
+  p.Hkv = c->kv_heads;
+  p.G = (int)(q_heads / c->kv_heads);
+  p.hgroups = (p.G + 3) / 4;
+  p.cap = c->cap;
+  p.nbc = c->cap / kBlk;
+  p.head_off = c->head % kBlk;
+  p.head_blk = c->head / kBlk;
+  p.len = c->len;
+  p.nlb = (p.head_off + c->len + kBlk - 1) / kBlk;
+  const float sc = scale > 0.0f ? scale : 1.0f / sqrtf((float)kD);
+  p.qk_log2 = sc * 1.4426950408889634f;
+  p.kc = c->kc;
+  p.vc = c->vc;
+  p.kmm = c->kmm;
+  p.vmm = c->vmm;
+  p.err = ctx->err_flag;
+  // split choice: minimise waves x (tiles per CTA + per-CTA overhead); at most
+  // 2^15 tiles (2^20 slots, 2^18 per warp) per CTA keeps every int32 digit sum
+  // exact (7 * 255 * 2^18 < 2^31)
+  const int64_t units = c->batch * c->kv_heads * p.hgroups;
+  const int64_t ntiles = (p.nlb + kDecWarps - 1) / kDecWarps;
+  const int64_t resident = (int64_t)decode_occupancy(ctx->device) * ctx->num_sms;
+  int64_t best_cost = INT64_MAX, best_per = ntiles;
+  for (int64_t sp = 1; sp <= 256 && sp <= ntiles; ++sp) {
+    const int64_t per = ceil_div(ntiles, sp);
+    if (per > 32768) continue;
+    const int64_t nsp = ceil_div(ntiles, per);
+    const int64_t waves = ceil_div(units * nsp, resident);
+    const int64_t cost = waves * (per + 2);
+    if (cost < best_cost) {
+      best_cost = cost;
+      best_per = per;
+    }
+  }
+  FT_CHECK(best_per <= 32768, FT_ERR_UNSUPPORTED, "cache too long for one decode launch");
+  p.tiles_per = best_per;
+  const int64_t nsplit = ceil_div(ntiles, best_per);
+  FT_CHECK(nsplit <= 65535 && c->kv_heads * p.hgroups <= 65535 && c->batch <= 65535,
+           FT_ERR_UNSUPPORTED, "decode grid too large");
+  const size_t need = (size_t)(c->batch * q_heads * nsplit * kPart) * 4;
+  if (c->part.bytes < need) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (s) cudaStreamIsCapturing(s, &cs);
+    FT_CHECK(cs == cudaStreamCaptureStatusNone, FT_ERR_UNSUPPORTED,
+             "the decode partials buffer must grow but the stream is being captured");
+    if (c->part.ptr) {
+      FT_CUDA(cudaStreamSynchronize(s));
+      FT_CUDA(cudaFree(c->part.ptr));
+      c->part.ptr = nullptr;
+      c->part.bytes = 0;
+    }
+    FT_CUDA(cudaMalloc(&c->part.ptr, need));
+    c->part.bytes = need;
+  }
+  p.part = static_cast<float*>(c->part.ptr);
+  dim3 grid((unsigned)nsplit, (unsigned)(c->kv_heads * p.hgroups), (unsigned)c->batch);
+  kv3_decode_kernel<<<grid, (kDecWarps + 1) * 32, kDecSmem, s>>>(p);
+  FT_LAUNCH_CHECK();
+  kv3_combine_kernel<<<(unsigned)(c->batch * q_heads), kD, 0, s>>>(p.part, (int)nsplit, out_dev);
+  FT_LAUNCH_CHECK();
+  return FT_OK;
+}
+
+}  // extern "C"

@@ -45,6 +45,7 @@ typedef enum ft_status {
 typedef struct ft_ctx ft_ctx;       /* one CUDA device + workspace */
 typedef struct ft_weight ft_weight; /* one dense ternary matrix resident in HBM */
 typedef struct ft_moe ft_moe;       /* one ternary MoE FFN layer resident in HBM */
+typedef struct ft_kv3 ft_kv3;       /* one layer's 3-bit KV cache resident in HBM */
 
 /* ---- library / context ------------------------------------------------ */
 const char* ft_version(void);
@@ -228,6 +229,47 @@ int ft_moe_expert_ffn(ft_ctx* ctx, ft_moe* m, int nseg, const int32_t* seg_exper
  * reference's accumulation order, ternary_moe.rs:217-221). */
 int ft_moe_combine(ft_ctx* ctx, ft_moe* m, int64_t T, const float* o_rows_dev,
                    const int32_t* slot_of_dev, const float* topk_w_dev, float* y_dev, void* stream);
+
+/* ---- 3-bit KV cache: TurboQuantKVCache (src/inference/turboquant_kv.rs:173-411)
+ * One layer of the cache for `batch` sequences with kv_heads heads of head_dim
+ * 128 (kv_dim = kv_heads * 128, quantisation group 128 = one head vector, the
+ * reference's group_size 128).  max_seq is the initial capacity; an append past
+ * it grows the cache (a reallocation, not allowed during stream capture), as
+ * the reference's Vec storage grows.  Replaces TurboQuantKVCache::new (:211). */
+int ft_kv3_create(ft_ctx* ctx, int64_t batch, int64_t kv_heads, int64_t head_dim,
+                  int64_t max_seq, ft_kv3** out);
+int ft_kv3_destroy(ft_kv3* c);
+/* Appends n_pos positions per sequence: k, v [batch, n_pos, kv_heads, 128]
+ * fp32 (bf16 bit patterns when is_bf16), quantised exactly as append /
+ * quantize_vector / quantize_3bit do (:240-266, :370-389, :83-107). */
+int ft_kv3_append(ft_ctx* ctx, ft_kv3* c, int64_t n_pos, const void* k_dev, const void* v_dev,
+                  int is_bf16, void* stream);
+/* Appends positions already in the reference's stored form: codes
+ * [batch, n_pos, kv_heads*48] bytes (pack_3bit of the kv_dim codes, :121-137)
+ * and (min, max) [batch, n_pos, kv_heads, 2]. */
+int ft_kv3_append_packed(ft_ctx* ctx, ft_kv3* c, int64_t n_pos, const uint8_t* k_codes_dev,
+                         const float* k_minmax_dev, const uint8_t* v_codes_dev,
+                         const float* v_minmax_dev, void* stream);
+/* seq_len (:345) and the current capacity in positions. */
+int ft_kv3_len(const ft_kv3* c, int64_t* len);
+int ft_kv3_capacity(const ft_kv3* c, int64_t* cap);
+/* Drops the n oldest positions (evict_oldest / evict_to, :308-328). */
+int ft_kv3_evict_front(ft_kv3* c, int64_t n);
+int ft_kv3_reset(ft_kv3* c); /* reset (:360) */
+/* get_range (:271-291): dequantised K, V [batch, end-start, kv_heads, 128] fp32. */
+int ft_kv3_get_range(ft_ctx* ctx, const ft_kv3* c, int64_t start, int64_t end, float* k_out_dev,
+                     float* v_out_dev, void* stream);
+/* Positions [start, end) in the reference's stored form (see append_packed). */
+int ft_kv3_export_range(ft_ctx* ctx, const ft_kv3* c, int64_t start, int64_t end,
+                        uint8_t* k_codes_dev, float* k_minmax_dev, uint8_t* v_codes_dev,
+                        float* v_minmax_dev, void* stream);
+/* Flash decode over the whole cache: out[b, h] = sum_s softmax_s(scale *
+ * q[b, h] . K[b, s, h / (q_heads / kv_heads)]) V[b, s, ...] with q, out
+ * [batch, q_heads, 128] fp32; scale <= 0 selects 1/sqrt(128).  The math of
+ * flash_decode_ref (tests/kernel_tests.rs:1073-1110) on the dequantised cache
+ * with the GQA head map of cpu_attention_raw (src/model/cpu_block_attn_res.rs:471-472). */
+int ft_flash_decode_3bit(ft_ctx* ctx, ft_kv3* c, const float* q_dev, int64_t q_heads, float scale,
+                         float* out_dev, void* stream);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop
