@@ -13,23 +13,26 @@
 //
 // Device layout.  Positions live in a ring of `cap` slots (cap a multiple of
 // 32); logical position p of the cache is slot (head + p) % cap, so evicting
-// the oldest positions only moves `head`.  Per (sequence, kv head) "row":
-//   K records  [row][cap][48 B]: one record per slot, in "quad-major" order
-//              so that the tensor-core operand of a lane group comes out of
-//              three words: for lane group r in 0..3, words 3r, 3r+1 hold the
-//              low 2 bits and word 3r+2 the high bit of the codes of the 32
-//              dims {4(r + 4i) + b : i in 0..7, b in 0..3}: the low bits of
-//              dim 4(r+4i)+b sit in word 3r + i/4 at bit 8b + 2(i%4), its
-//              high bit in word 3r+2 at bit 8b + i.
-//   V blocks   [row][cap/32][128 dims][3 words]: the codes of 32 consecutive
-//              slots of one dim; slot u of the block (quad i = u/4, b = u%4)
-//              keeps its low bits in word i/4 at bit 8b + 2(i%4) and its high
-//              bit in word 2 at bit 8b + i.
-//   min/max    [row][cap] float2 for K and for V.
-// 3 bits per code either way: 48 B of codes + 8 B of (min, max) per vector,
-// the reference's footprint.  Shifting a word by 2(i%4) and masking with
-// 0x03030303, and the high word by i and masking with 0x01010101, yields the 4
-// codes of a quad as 4 bytes: the int8 operand of a tensor-core MMA.
+// the oldest positions only moves `head`.  Per (sequence, kv head) "row" the
+// slots are grouped in blocks of 32, and each block is stored "lane-major":
+// the 12 words that lane L = 4g + r (g = L/4, r = L%4) of a decode warp feeds
+// into its tensor-core fragments are contiguous (48 bytes at L*48), so a lane
+// reads them with three 128-bit shared loads and extracts 4 codes per
+// fragment register with compile-time shifts and masks.  Codes are split into
+// their low 2 bits and high bit: shifting a word by 2j and masking with
+// 0x03030303 gives 4 low parts as bytes, shifting the high word and masking
+// with 0x04040404 puts the 4 high bits at bit 2 of each byte.
+//   K block (1536 B): slot s = g + 8e (e in 0..3) sits in lane group g; lane
+//     4g + r, words 3e + {0,1,2} hold the codes of slot s for the 32 dims
+//     {4(r + 4i) + b : i in 0..7, b in 0..3}: low bits of dim 4(r+4i)+b in
+//     word 3e + i/4 at bit 8b + 2(i%4), its high bit in word 3e+2 at bit 8b + i.
+//   V block (1536 B): lane 4g + r, words 3m + {0,1,2} (m in 0..3) hold the
+//     codes of the 4 dims j = 0..3 -> d = 16(2m + j/2) + g + 8(j%2) for the 8
+//     slots r + 4a + 8e (a in 0..1, e in 0..3): low bits in word 3m + a at bit
+//     8e + 2j, high bit in word 3m+2 at bit 8e + 4a + j.
+//   min/max: per block 32 float2 (K and V separately), slot s at (s%8)*4 + s/8.
+// 3 bits per code: 48 B of codes + 8 B of (min, max) per vector, the
+// reference's footprint.
 //
 // Decode, per (sequence, kv head, group of <=4 q heads, split of the slots):
 // four compute warps each take one 32-slot block of every 128-slot tile; a
@@ -53,7 +56,7 @@ struct ft_kv3 {
   int device = 0;
   int64_t batch = 0, kv_heads = 0, cap = 0;  // cap: slots per row, multiple of 32
   int64_t head = 0, len = 0;                   // ring start slot, live positions
-  uint8_t* kc = nullptr;   // K records
+  uint32_t* kc = nullptr;  // K blocks
   uint32_t* vc = nullptr;  // V blocks
   float2* kmm = nullptr;
   float2* vmm = nullptr;
@@ -65,7 +68,8 @@ namespace {
 
 constexpr int kD = 128;                  // head dim = quantisation group
 constexpr int kRec = 48;                 // bytes of codes per vector
-constexpr int kBlk = 32;                 // slots per V block
+constexpr int kBlk = 32;                 // slots per block
+constexpr int kBlkWords = kBlk * kRec / 4;  // 384
 constexpr int kBlkBytes = kBlk * kRec;   // 1536 (both K and V)
 constexpr int kMmBlkBytes = kBlk * 8;    // 256
 constexpr int kDecWarps = 4;             // compute warps = blocks per tile
@@ -74,30 +78,58 @@ constexpr int kStageBytes = kDecWarps * (2 * kBlkBytes + 2 * kMmBlkBytes);  // 1
 constexpr int kOffV = kDecWarps * kBlkBytes;
 constexpr int kOffKmm = 2 * kDecWarps * kBlkBytes;
 constexpr int kOffVmm = kOffKmm + kDecWarps * kMmBlkBytes;
-constexpr int kWsmBytes = kDecWarps * 4 * 4 * kBlk;  // [warp][head][digit][32 slots]
-constexpr int kQdBytes = 4 * 4 * kD;                 // [head][digit][128 dims] int8
-constexpr int kDecSmem = kStages * kStageBytes + kWsmBytes + kQdBytes + 64 + 16 * kStages;
+constexpr int kWsmBytes = kDecWarps * 4 * 4 * kBlk;      // [warp][digit][head][8 words]
+constexpr int kQfBytes = 4 * 32 * 16;                    // q fragments [chunk][lane][16 B]
+constexpr int kOsmBytes = kDecWarps * 4 * kD * 4;        // fp32 numerators [warp][head][128]
+constexpr int kQdBytes = 4 * 4 * kD;  // q digits [head][digit][128], staged in the numerator area
+constexpr int kOffW = kStages * kStageBytes;
+constexpr int kOffQf = kOffW + kWsmBytes;
+constexpr int kOffO = kOffQf + kQfBytes;
+constexpr int kOffQinfo = kOffO + kOsmBytes;
+constexpr int kOffBars = kOffQinfo + 64;
+constexpr int kDecSmem = kOffBars + 16 * kStages;
 constexpr int kPart = 2 + kD;  // partial record: m (log2 domain), l, numerator[128]
+static_assert(kQdBytes <= kOsmBytes, "q digits are staged in the numerator area");
+#ifndef FT_KV_MIN_BLOCKS
+#define FT_KV_MIN_BLOCKS 3
+#endif
 
 __device__ __forceinline__ float load_act(const void* p, int64_t i, int bf16) {
   return bf16 ? __uint_as_float((uint32_t) static_cast<const uint16_t*>(p)[i] << 16)
               : static_cast<const float*>(p)[i];
 }
 
-// code of dim d in a K record
-__device__ __forceinline__ uint32_t krec_code(const uint32_t* w, int d) {
-  const int qd = d >> 2, b = d & 3, r = qd & 3, i = qd >> 2;
-  const uint32_t lo = (w[3 * r + (i >> 2)] >> (8 * b + 2 * (i & 3))) & 3u;
-  const uint32_t hi = (w[3 * r + 2] >> (8 * b + i)) & 1u;
-  return lo | (hi << 2);
+// ---- layout maps (word indices within a 384-word block) ----
+__device__ __forceinline__ int k_lo_word(int s, int d) {
+  const int qd = d >> 2, r = qd & 3, i = qd >> 2;
+  return (4 * (s & 7) + r) * 12 + 3 * (s >> 3) + (i >> 2);
 }
+__device__ __forceinline__ int k_hi_word(int s, int d) {
+  const int r = (d >> 2) & 3;
+  return (4 * (s & 7) + r) * 12 + 3 * (s >> 3) + 2;
+}
+__device__ __forceinline__ int k_lo_bit(int d) { return 8 * (d & 3) + 2 * ((d >> 4) & 3); }
+__device__ __forceinline__ int k_hi_bit(int d) { return 8 * (d & 3) + (d >> 4); }
+// V: dim d -> (g, m, j); slot s -> (r, a, e)
+__device__ __forceinline__ int v_lane(int s, int d) { return 4 * (d & 7) + (s & 3); }
+__device__ __forceinline__ int v_j(int d) { return 2 * ((d >> 4) & 1) + ((d >> 3) & 1); }
+__device__ __forceinline__ int v_lo_word(int s, int d) {
+  return v_lane(s, d) * 12 + 3 * (d >> 5) + ((s >> 2) & 1);
+}
+__device__ __forceinline__ int v_hi_word(int s, int d) { return v_lane(s, d) * 12 + 3 * (d >> 5) + 2; }
+__device__ __forceinline__ int v_lo_bit(int s, int d) { return 8 * (s >> 3) + 2 * v_j(d); }
+__device__ __forceinline__ int v_hi_bit(int s, int d) {
+  return 8 * (s >> 3) + 4 * ((s >> 2) & 1) + v_j(d);
+}
+__device__ __forceinline__ int mm_index(int s) { return (s & 7) * 4 + (s >> 3); }
 
-// code of slot u (0..31) in a V (block, dim) triple
-__device__ __forceinline__ uint32_t vtri_code(const uint32_t* w, int u) {
-  const int i = u >> 2, b = u & 3;
-  const uint32_t lo = (w[i >> 2] >> (8 * b + 2 * (i & 3))) & 3u;
-  const uint32_t hi = (w[2] >> (8 * b + i)) & 1u;
-  return lo | (hi << 2);
+__device__ __forceinline__ uint32_t k_code(const uint32_t* blk, int s, int d) {
+  return ((blk[k_lo_word(s, d)] >> k_lo_bit(d)) & 3u) |
+         (((blk[k_hi_word(s, d)] >> k_hi_bit(d)) & 1u) << 2);
+}
+__device__ __forceinline__ uint32_t v_code(const uint32_t* blk, int s, int d) {
+  return ((blk[v_lo_word(s, d)] >> v_lo_bit(s, d)) & 3u) |
+         (((blk[v_hi_word(s, d)] >> v_hi_bit(s, d)) & 1u) << 2);
 }
 
 // ---------------------------------------------------------------- append --
@@ -108,7 +140,7 @@ struct AppendParams {
   const float* vmm_in;
   int bf16;
   int64_t n_pos, Hkv, cap, nbc, s0;
-  uint8_t* kc;
+  uint32_t* kc;
   uint32_t* vc;
   float2* kmm;
   float2* vmm;
@@ -126,7 +158,7 @@ __device__ __forceinline__ uint32_t ref_stream_code(const uint8_t* bytes, int64_
 
 // One CTA per (32-slot block touched, row); thread = dim.  Quantises each new
 // position of the block (or takes its codes from a reference byte stream),
-// writes the K record and min/max, and rewrites the dim's V triple once.
+// and rewrites the block's K and V words and min/max.
 template <bool kPacked>
 __global__ void __launch_bounds__(kD) kv3_append_kernel(AppendParams p) {
   const int64_t x = blockIdx.x, row = blockIdx.y;
@@ -134,16 +166,20 @@ __global__ void __launch_bounds__(kD) kv3_append_kernel(AppendParams p) {
   const int d = threadIdx.x, warp = d >> 5, lane = d & 31;
   const int64_t off0 = p.s0 % kBlk;
   const int64_t pb = (p.s0 / kBlk + x) % p.nbc;
-  const int64_t u_begin = x == 0 ? off0 : 0;
-  int64_t u_end = p.n_pos + off0 - x * kBlk;
-  if (u_end > kBlk) u_end = kBlk;
-  __shared__ float red[kDecWarps][4];
-  __shared__ uint32_t rec[12];
-  uint32_t* vw = p.vc + ((row * p.nbc + pb) * kD + d) * 3;
-  uint32_t v0 = vw[0], v1 = vw[1], v2 = vw[2];
-  for (int64_t u = u_begin; u < u_end; ++u) {
+  const int u_begin = x == 0 ? (int)off0 : 0;
+  int64_t u_end64 = p.n_pos + off0 - x * kBlk;
+  const int u_end = u_end64 > kBlk ? kBlk : (int)u_end64;
+  __shared__ float red[4][4];
+  __shared__ uint32_t kw[kBlkWords], vw[kBlkWords];
+  uint32_t* kg = p.kc + (row * p.nbc + pb) * kBlkWords;
+  uint32_t* vg = p.vc + (row * p.nbc + pb) * kBlkWords;
+  for (int i = d; i < kBlkWords; i += kD) {
+    kw[i] = kg[i];
+    vw[i] = vg[i];
+  }
+  __syncthreads();
+  for (int u = u_begin; u < u_end; ++u) {
     const int64_t pi = x * kBlk + u - off0;  // input position
-    const int64_t slot = pb * kBlk + u;
     const int64_t vec = (b * p.n_pos + pi) * p.Hkv + h;
     uint32_t ck, cv;
     float kmin, kmax, vmin, vmax;
@@ -192,39 +228,29 @@ __global__ void __launch_bounds__(kD) kv3_append_kernel(AppendParams p) {
         cv = q <= 0.0f ? 0u : (q >= 7.0f ? 7u : (uint32_t)q);
       }
     }
-    if (d < 12) rec[d] = 0u;
-    __syncthreads();
-    {
-      const int qd = d >> 2, bb = d & 3, r = qd & 3, i = qd >> 2;
-      atomicOr(&rec[3 * r + (i >> 2)], (ck & 3u) << (8 * bb + 2 * (i & 3)));
-      atomicOr(&rec[3 * r + 2], ((ck >> 2) & 1u) << (8 * bb + i));
-    }
-    {
-      const int i = (int)(u >> 2), bb = (int)(u & 3);
-      const int sl = 8 * bb + 2 * (i & 3), sh = 8 * bb + i;
-      const uint32_t lo_mask = 3u << sl, lo_bits = (cv & 3u) << sl;
-      if ((i >> 2) == 0)
-        v0 = (v0 & ~lo_mask) | lo_bits;
-      else
-        v1 = (v1 & ~lo_mask) | lo_bits;
-      v2 = (v2 & ~(1u << sh)) | (((cv >> 2) & 1u) << sh);
-    }
-    __syncthreads();
-    if (d < 12)
-      reinterpret_cast<uint32_t*>(p.kc + (row * p.cap + slot) * kRec)[d] = rec[d];
-    if (d == 0) p.kmm[row * p.cap + slot] = make_float2(kmin, kmax);
-    if (d == 1) p.vmm[row * p.cap + slot] = make_float2(vmin, vmax);
-    __syncthreads();
+    // the slot's bits: clear, then set (threads touch disjoint bits)
+    atomicAnd(&kw[k_lo_word(u, d)], ~(3u << k_lo_bit(d)));
+    atomicAnd(&kw[k_hi_word(u, d)], ~(1u << k_hi_bit(d)));
+    atomicAnd(&vw[v_lo_word(u, d)], ~(3u << v_lo_bit(u, d)));
+    atomicAnd(&vw[v_hi_word(u, d)], ~(1u << v_hi_bit(u, d)));
+    atomicOr(&kw[k_lo_word(u, d)], (ck & 3u) << k_lo_bit(d));
+    atomicOr(&kw[k_hi_word(u, d)], ((ck >> 2) & 1u) << k_hi_bit(d));
+    atomicOr(&vw[v_lo_word(u, d)], (cv & 3u) << v_lo_bit(u, d));
+    atomicOr(&vw[v_hi_word(u, d)], ((cv >> 2) & 1u) << v_hi_bit(u, d));
+    if (d == 0) p.kmm[(row * p.nbc + pb) * kBlk + mm_index(u)] = make_float2(kmin, kmax);
+    if (d == 1) p.vmm[(row * p.nbc + pb) * kBlk + mm_index(u)] = make_float2(vmin, vmax);
+    __syncthreads();  // red is reused by the next position
   }
-  vw[0] = v0;
-  vw[1] = v1;
-  vw[2] = v2;
+  for (int i = d; i < kBlkWords; i += kD) {
+    kg[i] = kw[i];
+    vg[i] = vw[i];
+  }
 }
 
 // ------------------------------------------------------- read-back kernels --
 struct RangeParams {
   int64_t B, Hkv, cap, nbc, head, start, n;
-  const uint8_t* kc;
+  const uint32_t* kc;
   const uint32_t* vc;
   const float2* kmm;
   const float2* vmm;
@@ -241,10 +267,11 @@ __global__ void kv3_dequant_kernel(RangeParams p, float* __restrict__ kout,
   const int64_t b = vec / (p.Hkv * p.n);
   const int64_t row = b * p.Hkv + h;
   const int64_t slot = (p.head + p.start + pos) % p.cap;
-  const uint32_t* kr = reinterpret_cast<const uint32_t*>(p.kc + (row * p.cap + slot) * kRec);
-  const uint32_t* vt = p.vc + ((row * p.nbc + slot / kBlk) * kD + d) * 3;
-  const uint32_t ck = krec_code(kr, d), cv = vtri_code(vt, (int)(slot % kBlk));
-  const float2 km = p.kmm[row * p.cap + slot], vm = p.vmm[row * p.cap + slot];
+  const int64_t blk = row * p.nbc + slot / kBlk;
+  const int s = (int)(slot % kBlk);
+  const uint32_t ck = k_code(p.kc + blk * kBlkWords, s, d);
+  const uint32_t cv = v_code(p.vc + blk * kBlkWords, s, d);
+  const float2 km = p.kmm[blk * kBlk + mm_index(s)], vm = p.vmm[blk * kBlk + mm_index(s)];
   float kv, vv;
   if (km.y == km.x) {
     kv = km.x;
@@ -272,15 +299,15 @@ __global__ void kv3_export_kernel(RangeParams p, uint8_t* __restrict__ kbytes,
   const int64_t b = vec / (p.Hkv * p.n);
   const int64_t row = b * p.Hkv + h;
   const int64_t slot = (p.head + p.start + pos) % p.cap;
-  const uint32_t* kr = reinterpret_cast<const uint32_t*>(p.kc + (row * p.cap + slot) * kRec);
-  const uint32_t* vbase = p.vc + ((row * p.nbc + slot / kBlk) * kD) * 3;
-  const int u = (int)(slot % kBlk);
+  const int64_t blk = row * p.nbc + slot / kBlk;
+  const int s = (int)(slot % kBlk);
+  const uint32_t* kb = p.kc + blk * kBlkWords;
+  const uint32_t* vb = p.vc + blk * kBlkWords;
   uint32_t kbits = 0, vbits = 0;
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    const int d = 8 * m + j;
-    kbits |= krec_code(kr, d) << (3 * j);
-    vbits |= vtri_code(vbase + d * 3, u) << (3 * j);
+    kbits |= k_code(kb, s, 8 * m + j) << (3 * j);
+    vbits |= v_code(vb, s, 8 * m + j) << (3 * j);
   }
   const int64_t o = vec * kRec + 3 * m;  // [B][n][Hkv][48] == [B][n][Hkv*48]
   kbytes[o] = (uint8_t)(kbits & 0xFF);
@@ -290,7 +317,7 @@ __global__ void kv3_export_kernel(RangeParams p, uint8_t* __restrict__ kbytes,
   vbytes[o + 1] = (uint8_t)((vbits >> 8) & 0xFF);
   vbytes[o + 2] = (uint8_t)((vbits >> 16) & 0xFF);
   if (m == 0) {
-    const float2 km = p.kmm[row * p.cap + slot], vm = p.vmm[row * p.cap + slot];
+    const float2 km = p.kmm[blk * kBlk + mm_index(s)], vm = p.vmm[blk * kBlk + mm_index(s)];
     kmm_out[vec * 2] = km.x;
     kmm_out[vec * 2 + 1] = km.y;
     vmm_out[vec * 2] = vm.x;
@@ -303,11 +330,11 @@ struct DecodeParams {
   const float* q;  // [B][Hq][128]
   int64_t Hq, Hkv;
   int G, hgroups;  // q heads per kv head, CTAs (groups of <=4 q heads) per kv head
-  int64_t cap, nbc, head_off, head_blk, len;
+  int64_t nbc, head_off, head_blk, len;
   int64_t nlb;        // logical 32-slot blocks covering the live range
   int64_t tiles_per;  // 128-slot tiles per split
   float qk_log2;      // softmax scale * log2(e)
-  const uint8_t* kc;
+  const uint32_t* kc;
   const uint32_t* vc;
   const float2* kmm;
   const float2* vmm;
@@ -315,44 +342,52 @@ struct DecodeParams {
   int* err;
 };
 
-__device__ __forceinline__ void mma_u8s8(int (&c)[4], const uint32_t (&a)[4], uint32_t b0,
-                                         uint32_t b1) {
+__device__ __forceinline__ void mma_u8s8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
   asm volatile(
       "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
       "{%8, %9}, {%0, %1, %2, %3};"
       : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ void mma_u8u8(int (&c)[4], const uint32_t (&a)[4], uint32_t b0,
-                                         uint32_t b1) {
+__device__ __forceinline__ void mma_u8u8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
   asm volatile(
       "mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
       "{%8, %9}, {%0, %1, %2, %3};"
       : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// 4 codes of a quad as bytes: low bits from `lo` at `lo_shift`, high bit
-// already moved to bit 2 of each byte in `hi_sh`.
-__device__ __forceinline__ uint32_t quad_bytes(uint32_t lo, int lo_shift, uint32_t hi_sh) {
-  return ((lo >> lo_shift) & 0x03030303u) | (hi_sh & 0x04040404u);
+// 4 codes as bytes: low parts from `lo` shifted by LS, high bits from `hi`
+// moved from bit HB of each byte to bit 2 (compile-time shifts).
+template <int LS, int HB>
+__device__ __forceinline__ uint32_t quad(uint32_t lo, uint32_t hi) {
+  const uint32_t h = HB >= 2 ? (hi >> (HB - 2)) : (hi << (2 - HB));
+  return ((lo >> LS) & 0x03030303u) | (h & 0x04040404u);
 }
 
-// exact int32 digit sums -> float: sum_j 256^j d_j
+// exact for |d| < 2^22
+__device__ __forceinline__ float small_int_to_float(int d) {
+  return __int_as_float(0x4B400000 + d) - 12582912.0f;
+}
+
+// exact int32 digit sums -> float: sum_j 256^j d_j (any magnitude)
 __device__ __forceinline__ float digits4(int d0, int d1, int d2, int d3) {
   const long long v = (long long)d0 + ((long long)d1 << 8) + ((long long)d2 << 16) +
                       ((long long)d3 << 24);
   return (float)v;
 }
 
-__global__ void __launch_bounds__((kDecWarps + 1) * 32)
+__global__ void __launch_bounds__((kDecWarps + 1) * 32, FT_KV_MIN_BLOCKS)
     kv3_decode_kernel(const __grid_constant__ DecodeParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
-  uint8_t* wsm = smem + kStages * kStageBytes;                          // W digits
-  int8_t* qd = reinterpret_cast<int8_t*>(wsm + kWsmBytes);              // q digits
-  float* qinfo = reinterpret_cast<float*>(wsm + kWsmBytes + kQdBytes);  // qsum[4], qscale[4]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(wsm + kWsmBytes + kQdBytes + 64);
+  uint32_t* wsm = reinterpret_cast<uint32_t*>(smem + kOffW);        // W digit words
+  const uint4* qf = reinterpret_cast<const uint4*>(smem + kOffQf);   // q fragments
+  float* osm = reinterpret_cast<float*>(smem + kOffO);               // fp32 numerators
+  float* qinfo = reinterpret_cast<float*>(smem + kOffQinfo);         // qsum*, qscale*
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBars);
   const uint32_t full0 = tc::smem_u32(bars), empty0 = full0 + 8 * kStages;
 
   const int split = blockIdx.x;
@@ -380,7 +415,8 @@ __global__ void __launch_bounds__((kDecWarps + 1) * 32)
     tc::fence_barrier_init();
   }
   // q prep: warp w < 4 turns head w of the group (zeros past nheads) into
-  // 4 signed base-256 digits of round(q * 2^30 / absmax)
+  // 4 signed base-256 digits of round(q * 2^30 / absmax), staged in the W area
+  int8_t* qd = reinterpret_cast<int8_t*>(smem + kOffO);  // [head][digit][128], reused below
   if (warp < 4) {
     float qv[4];
     const bool valid = warp < nheads;
@@ -408,10 +444,28 @@ __global__ void __launch_bounds__((kDecWarps + 1) * 32)
       qd[(warp * 4 + 3) * kD + dim] = (int8_t)X;  // |X| <= 65 here
     }
     if (lane == 0) {
-      qinfo[warp] = sum;
-      qinfo[4 + warp] = amax * 9.313225746154785e-10f;  // amax / 2^30
+      qinfo[warp] = sum * p.qk_log2;                                // sum(q) in score units
+      qinfo[4 + warp] = amax * 9.313225746154785e-10f * p.qk_log2;  // amax / 2^30, same
     }
   }
+  __syncthreads();
+  // q B fragments, chunk c = ks (k-step of 32 dims): words {nb0 b0, nb0 b1, nb1 b0, nb1 b1};
+  // column n = g <-> (head g/2, digit g%2 + 2*nb)
+  if (warp < 4) {
+    const int ks = warp;
+    uint32_t w4[4];
+#pragma unroll
+    for (int nb = 0; nb < 2; ++nb) {
+      const int8_t* src = qd + ((g >> 1) * 4 + (g & 1) + 2 * nb) * kD + 32 * ks + 4 * r;
+      w4[2 * nb] = *reinterpret_cast<const uint32_t*>(src);
+      w4[2 * nb + 1] = *reinterpret_cast<const uint32_t*>(src + 16);
+    }
+    reinterpret_cast<uint4*>(smem + kOffQf)[ks * 32 + lane] =
+        make_uint4(w4[0], w4[1], w4[2], w4[3]);
+  }
+  __syncthreads();
+  // the numerators start at zero (the q digits there are no longer needed)
+  for (int i = tid; i < kDecWarps * 4 * kD; i += blockDim.x) osm[i] = 0.0f;
   __syncthreads();
 
   const uint32_t stage_base = tc::smem_u32(smem);
@@ -420,29 +474,26 @@ __global__ void __launch_bounds__((kDecWarps + 1) * 32)
     if (lane == 0) {
       bool ok = true;
       int issued = 0;
+      int64_t pb = (p.head_blk + t_begin * kDecWarps) % p.nbc;
       for (int it = 0; it < ntiles && ok; ++it) {
         const int s = it % kStages;
         if (it >= kStages)
           ok = tc::mbar_wait(empty0 + 8 * s, ((it / kStages) - 1) & 1, p.err, 31);
         if (!ok) break;
         const int64_t j0 = (t_begin + it) * kDecWarps;
-        uint32_t bytes = 0;
-        for (int w = 0; w < kDecWarps; ++w)
-          if (j0 + w < p.nlb) bytes += 2 * kBlkBytes + 2 * kMmBlkBytes;
-        tc::mbar_arrive_expect_tx(full0 + 8 * s, bytes);
+        const int nb = p.nlb - j0 < kDecWarps ? (int)(p.nlb - j0) : kDecWarps;
+        tc::mbar_arrive_expect_tx(full0 + 8 * s, nb * (2 * kBlkBytes + 2 * kMmBlkBytes));
         const uint32_t sb = stage_base + s * kStageBytes;
-        for (int w = 0; w < kDecWarps; ++w) {
-          const int64_t j = j0 + w;
-          if (j >= p.nlb) break;
-          const int64_t pb = (p.head_blk + j) % p.nbc;
-          tc::bulk_g2s(sb + w * kBlkBytes, p.kc + (row * p.cap + pb * kBlk) * kRec, kBlkBytes,
+        for (int w = 0; w < nb; ++w) {
+          const int64_t blk = row * p.nbc + pb;
+          tc::bulk_g2s(sb + w * kBlkBytes, p.kc + blk * kBlkWords, kBlkBytes, full0 + 8 * s);
+          tc::bulk_g2s(sb + kOffV + w * kBlkBytes, p.vc + blk * kBlkWords, kBlkBytes,
                        full0 + 8 * s);
-          tc::bulk_g2s(sb + kOffV + w * kBlkBytes, p.vc + (row * p.nbc + pb) * (kD * 3),
-                       kBlkBytes, full0 + 8 * s);
-          tc::bulk_g2s(sb + kOffKmm + w * kMmBlkBytes, p.kmm + row * p.cap + pb * kBlk,
-                       kMmBlkBytes, full0 + 8 * s);
-          tc::bulk_g2s(sb + kOffVmm + w * kMmBlkBytes, p.vmm + row * p.cap + pb * kBlk,
-                       kMmBlkBytes, full0 + 8 * s);
+          tc::bulk_g2s(sb + kOffKmm + w * kMmBlkBytes, p.kmm + blk * kBlk, kMmBlkBytes,
+                       full0 + 8 * s);
+          tc::bulk_g2s(sb + kOffVmm + w * kMmBlkBytes, p.vmm + blk * kBlk, kMmBlkBytes,
+                       full0 + 8 * s);
+          if (++pb == p.nbc) pb = 0;
         }
         ++issued;
       }
@@ -454,22 +505,8 @@ __global__ void __launch_bounds__((kDecWarps + 1) * 32)
   }
 
   // -------------------------------------------------------- compute warps --
-  // B fragments of q: column n = g <-> (head g/2, digit g%2 + 2*nb)
-  uint32_t bq[4][2][2];
-#pragma unroll
-  for (int ks = 0; ks < 4; ++ks)
-#pragma unroll
-    for (int nb = 0; nb < 2; ++nb) {
-      const int8_t* src = qd + ((g >> 1) * 4 + (g & 1) + 2 * nb) * kD + 32 * ks + 4 * r;
-      bq[ks][nb][0] = *reinterpret_cast<const uint32_t*>(src);
-      bq[ks][nb][1] = *reinterpret_cast<const uint32_t*>(src + 16);
-    }
   const float qsum = qinfo[r], qscale = qinfo[4 + r];
-
   float m_run = -INFINITY, l_part = 0.0f, vmin_part = 0.0f;
-  float o[16];  // head r, dims 16*mb + g + 8*h at o[2*mb + h]
-#pragma unroll
-  for (int i = 0; i < 16; ++i) o[i] = 0.0f;
   int pv[8][2][4];
 #pragma unroll
   for (int mb = 0; mb < 8; ++mb)
@@ -478,17 +515,21 @@ __global__ void __launch_bounds__((kDecWarps + 1) * 32)
 #pragma unroll
       for (int c = 0; c < 4; ++c) pv[mb][nb][c] = 0;
   float wmul = 0.0f, wbound = 0.0f;  // W = p * vs * wmul, valid while vs < wbound
-  uint8_t* my_w = wsm + warp * (4 * 4 * kBlk);
+  uint32_t* my_w = wsm + warp * (4 * 4 * 8);
+  float* my_o = osm + (warp * 4 + r) * kD;  // head r
   bool ok = true;
 
-  auto fold = [&](float inv) {
+  // adds the digit sums times `inv` to the numerators and clears them; then
+  // scales the numerators by alpha
+  auto fold_scale = [&](float inv, float alpha) {
 #pragma unroll
     for (int mb = 0; mb < 8; ++mb)
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const float v =
             digits4(pv[mb][0][2 * h], pv[mb][0][2 * h + 1], pv[mb][1][2 * h], pv[mb][1][2 * h + 1]);
-        o[2 * mb + h] = fmaf(v, inv, o[2 * mb + h]);
+        float* o = my_o + 16 * mb + g + 8 * h;
+        *o = fmaf(v, inv, *o) * alpha;
       }
 #pragma unroll
     for (int mb = 0; mb < 8; ++mb)
@@ -504,137 +545,170 @@ __global__ void __launch_bounds__((kDecWarps + 1) * 32)
     const int64_t j = (t_begin + it) * kDecWarps + warp;
     if (ok && j < p.nlb) {
       const uint8_t* sb = smem + s * kStageBytes;
-      const uint8_t* kb = sb + warp * kBlkBytes;
-      const uint32_t* vb = reinterpret_cast<const uint32_t*>(sb + kOffV + warp * kBlkBytes);
-      const float2* kmt = reinterpret_cast<const float2*>(sb + kOffKmm) + warp * kBlk;
-      const float2* vmt = reinterpret_cast<const float2*>(sb + kOffVmm) + warp * kBlk;
-      // ---- scores: slots u = 16*mb + g + 8*h
+      const uint4* kb4 = reinterpret_cast<const uint4*>(sb + warp * kBlkBytes) + lane * 3;
+      const uint4* vb4 = reinterpret_cast<const uint4*>(sb + kOffV + warp * kBlkBytes) + lane * 3;
+      const float4* km4 =
+          reinterpret_cast<const float4*>(sb + kOffKmm + warp * kMmBlkBytes) + g * 2;
+      const float4* vm4 =
+          reinterpret_cast<const float4*>(sb + kOffVmm + warp * kMmBlkBytes) + g * 2;
+      // live slots of this block: u in [lo_live, hi_live)
+      const int64_t base = j * kBlk - p.head_off;
+      const int lo_live = base >= 0 ? 0 : (int)(-base);
+      const int64_t hl = p.len - base;
+      const int hi_live = hl >= kBlk ? kBlk : (int)hl;
+      // ---- scores: this lane's slots u = g + 8e, e = 2*mb + h
       float s2[4], vsv[4], vmn[4];
+      {
+        const uint4 k0 = kb4[0], k1 = kb4[1], k2 = kb4[2];
+        // slot e = 0: k0.x k0.y k0.z | e = 1: k0.w k1.x k1.y | e = 2: k1.z k1.w k2.x | e = 3: k2.y..
+        const uint32_t lo0[4] = {k0.x, k0.w, k1.z, k2.y};
+        const uint32_t lo1[4] = {k0.y, k1.x, k1.w, k2.z};
+        const uint32_t hiw[4] = {k0.z, k1.y, k2.x, k2.w};
 #pragma unroll
-      for (int mb = 0; mb < 2; ++mb) {
-        int acc[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
-        const uint32_t* k0 = reinterpret_cast<const uint32_t*>(kb + (16 * mb + g) * kRec) + 3 * r;
-        const uint32_t* k1 = k0 + 8 * (kRec / 4);
-        const uint32_t l00 = k0[0], l01 = k0[1], h0 = k0[2];
-        const uint32_t l10 = k1[0], l11 = k1[1], h1 = k1[2];
+        for (int mb = 0; mb < 2; ++mb) {
+          int acc[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+          const int ea = 2 * mb, eb = 2 * mb + 1;  // rows g, g+8
 #pragma unroll
-        for (int ks = 0; ks < 4; ++ks) {
-          const int i0 = 2 * ks, i1 = 2 * ks + 1;
-          const uint32_t la = ks < 2 ? l00 : l01, lb = ks < 2 ? l10 : l11;
-          // high bit of quad i to bit 2 of each byte: shift right by i-2 (left for i < 2)
-          const uint32_t ha0 = i0 >= 2 ? (h0 >> (i0 - 2)) : (h0 << (2 - i0));
-          const uint32_t hb0 = i0 >= 2 ? (h1 >> (i0 - 2)) : (h1 << (2 - i0));
-          const uint32_t ha1 = i1 >= 2 ? (h0 >> (i1 - 2)) : (h0 << (2 - i1));
-          const uint32_t hb1 = i1 >= 2 ? (h1 >> (i1 - 2)) : (h1 << (2 - i1));
-          uint32_t a[4];
-          a[0] = quad_bytes(la, 2 * (i0 & 3), ha0);
-          a[1] = quad_bytes(lb, 2 * (i0 & 3), hb0);
-          a[2] = quad_bytes(la, 2 * (i1 & 3), ha1);
-          a[3] = quad_bytes(lb, 2 * (i1 & 3), hb1);
-          mma_u8s8(acc[0], a, bq[ks][0][0], bq[ks][0][1]);
-          mma_u8s8(acc[1], a, bq[ks][1][0], bq[ks][1][1]);
-        }
+          for (int ks = 0; ks < 4; ++ks) {
+            const uint4 bq = qf[ks * 32 + lane];
+            uint32_t a0, a1, a2, a3;
+            // quad index i0 = 2ks (a0, a1) and i1 = 2ks + 1 (a2, a3)
+#define FT_KQ(I, LOA, HIA) quad<2 * ((I) & 3), (I)>(LOA, HIA)
+            if (ks == 0) {
+              a0 = FT_KQ(0, lo0[ea], hiw[ea]); a1 = FT_KQ(0, lo0[eb], hiw[eb]);
+              a2 = FT_KQ(1, lo0[ea], hiw[ea]); a3 = FT_KQ(1, lo0[eb], hiw[eb]);
+            } else if (ks == 1) {
+              a0 = FT_KQ(2, lo0[ea], hiw[ea]); a1 = FT_KQ(2, lo0[eb], hiw[eb]);
+              a2 = FT_KQ(3, lo0[ea], hiw[ea]); a3 = FT_KQ(3, lo0[eb], hiw[eb]);
+            } else if (ks == 2) {
+              a0 = FT_KQ(4, lo1[ea], hiw[ea]); a1 = FT_KQ(4, lo1[eb], hiw[eb]);
+              a2 = FT_KQ(5, lo1[ea], hiw[ea]); a3 = FT_KQ(5, lo1[eb], hiw[eb]);
+            } else {
+              a0 = FT_KQ(6, lo1[ea], hiw[ea]); a1 = FT_KQ(6, lo1[eb], hiw[eb]);
+              a2 = FT_KQ(7, lo1[ea], hiw[ea]); a3 = FT_KQ(7, lo1[eb], hiw[eb]);
+            }
+#undef FT_KQ
+            mma_u8s8(acc[0], a0, a1, a2, a3, bq.x, bq.y);
+            mma_u8s8(acc[1], a0, a1, a2, a3, bq.z, bq.w);
+          }
+          const float4 kmA = km4[mb];  // (min, max) of slots e = 2mb, 2mb + 1
+          const float4 vmA = vm4[mb];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int u = 16 * mb + g + 8 * h;
-          const float S =
-              digits4(acc[0][2 * h], acc[0][2 * h + 1], acc[1][2 * h], acc[1][2 * h + 1]);
-          const float2 km = kmt[u];
-          const float ksc = km.y == km.x ? 0.0f : __fdiv_rn(km.y - km.x, 7.0f);
-          const float dot = fmaf(km.x, qsum, ksc * (S * qscale));
-          const int64_t logical = j * kBlk + u - p.head_off;
-          const bool live = logical >= 0 && logical < p.len;
-          s2[2 * mb + h] = live ? dot * p.qk_log2 : -INFINITY;
-          const float2 vm = vmt[u];
-          vsv[2 * mb + h] = live && vm.y != vm.x ? __fdiv_rn(vm.y - vm.x, 7.0f) : 0.0f;
-          vmn[2 * mb + h] = live ? vm.x : 0.0f;
+          for (int h = 0; h < 2; ++h) {
+            const int e = 2 * mb + h, u = g + 8 * e;
+            const float S = fmaf(
+                fmaf(fmaf(small_int_to_float(acc[1][2 * h + 1]), 256.0f,
+                          small_int_to_float(acc[1][2 * h])),
+                     256.0f, small_int_to_float(acc[0][2 * h + 1])),
+                256.0f, small_int_to_float(acc[0][2 * h]));
+            const float kmin = h ? kmA.z : kmA.x, kmax = h ? kmA.w : kmA.y;
+            const float vmin = h ? vmA.z : vmA.x, vmax = h ? vmA.w : vmA.y;
+            const bool live = u >= lo_live && u < hi_live;
+            const float ksc = (kmax - kmin) * 0.14285714285714285f;
+            s2[e] = live ? fmaf(kmin, qsum, ksc * (S * qscale)) : -INFINITY;
+            vsv[e] = live ? (vmax - vmin) * 0.14285714285714285f : 0.0f;
+            vmn[e] = live ? vmin : 0.0f;
+          }
         }
       }
       // ---- online softmax (head r): max over the block's 32 slots
       float mt = fmaxf(fmaxf(s2[0], s2[1]), fmaxf(s2[2], s2[3]));
-      float vsmax = fmaxf(fmaxf(vsv[0], vsv[1]), fmaxf(vsv[2], vsv[3]));
 #pragma unroll
       for (int o2 = 4; o2 < 32; o2 <<= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, o2));
-#pragma unroll
-      for (int o2 = 1; o2 < 32; o2 <<= 1)
-        vsmax = fmaxf(vsmax, __shfl_xor_sync(0xffffffffu, vsmax, o2));
+      const float vloc = fmaxf(fmaxf(vsv[0], vsv[1]), fmaxf(vsv[2], vsv[3]));
+      const bool rescale = __any_sync(0xffffffffu, vloc >= wbound && vloc > 0.0f);
       const float m_new = fmaxf(m_run, mt);
-      const bool rescale = vsmax >= wbound && vsmax > 0.0f;  // warp-uniform
       if (m_new > m_run || rescale) {
-        if (wmul > 0.0f) fold(1.0f / wmul);
+        const float alpha = m_run == -INFINITY ? 0.0f : exp2f(m_run - m_new);
+        if (wmul > 0.0f) fold_scale(1.0f / wmul, alpha);
+        else {
+#pragma unroll
+          for (int mb = 0; mb < 8; ++mb)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) my_o[16 * mb + g + 8 * h] *= alpha;
+        }
         if (rescale) {
+          float vsmax = vloc;
+#pragma unroll
+          for (int o2 = 1; o2 < 32; o2 <<= 1)
+            vsmax = fmaxf(vsmax, __shfl_xor_sync(0xffffffffu, vsmax, o2));
           int e;
           frexpf(vsmax, &e);  // vsmax < 2^e
           wbound = ldexpf(1.0f, e);
           wmul = ldexpf(1.0f, 31 - e);
         }
-        const float alpha = m_run == -INFINITY ? 0.0f : exp2f(m_run - m_new);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) o[i] *= alpha;
         l_part *= alpha;
         vmin_part *= alpha;
         m_run = m_new;
       }
-      // ---- probabilities -> W digits in shared memory: my_w[head][digit][slot]
+      // ---- probabilities -> W digit words: word (digit, head r, g) holds the
+      // digit of the W of slots g + 8e as byte e
+      uint32_t W[4];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int u = 16 * (k >> 1) + g + 8 * (k & 1);
-        const float pr = s2[k] == -INFINITY ? 0.0f : exp2f(s2[k] - m_run);
+      for (int e = 0; e < 4; ++e) {
+        const float pr = s2[e] == -INFINITY ? 0.0f : exp2f(s2[e] - m_run);
         l_part += pr;
-        vmin_part = fmaf(pr, vmn[k], vmin_part);
-        const uint32_t W = __float2uint_rn(pr * vsv[k] * wmul);
-#pragma unroll
-        for (int dg = 0; dg < 4; ++dg) my_w[(r * 4 + dg) * kBlk + u] = (uint8_t)(W >> (8 * dg));
+        vmin_part = fmaf(pr, vmn[e], vmin_part);
+        W[e] = __float2uint_rn(pr * vsv[e] * wmul);
+      }
+      {
+        const uint32_t t0 = __byte_perm(W[0], W[1], 0x5140), t1 = __byte_perm(W[2], W[3], 0x5140);
+        const uint32_t t2 = __byte_perm(W[0], W[1], 0x7362), t3 = __byte_perm(W[2], W[3], 0x7362);
+        my_w[0 * 32 + r * 8 + g] = __byte_perm(t0, t1, 0x5410);
+        my_w[1 * 32 + r * 8 + g] = __byte_perm(t0, t1, 0x7632);
+        my_w[2 * 32 + r * 8 + g] = __byte_perm(t2, t3, 0x5410);
+        my_w[3 * 32 + r * 8 + g] = __byte_perm(t2, t3, 0x7632);
       }
       __syncwarp();
-      // ---- P.V: B fragments of W, column n = g <-> (head g/2, digit g%2 + 2*nb)
+      // ---- P.V: B column n = g <-> (head g/2, digit g%2 + 2*nb); k = 4r + e <->
+      // slot r + 8e (score lane g_s = r), k = 16 + 4r + e <-> slot r + 4 + 8e
       uint32_t bw[2][2];
 #pragma unroll
       for (int nb = 0; nb < 2; ++nb) {
-        const uint8_t* src = my_w + ((g >> 1) * 4 + (g & 1) + 2 * nb) * kBlk + 4 * r;
-        bw[nb][0] = *reinterpret_cast<const uint32_t*>(src);
-        bw[nb][1] = *reinterpret_cast<const uint32_t*>(src + 16);
+        const uint32_t* src = my_w + ((g & 1) + 2 * nb) * 32 + (g >> 1) * 8;
+        bw[nb][0] = src[r];
+        bw[nb][1] = src[r + 4];
       }
+      {
+        const uint4 v0 = vb4[0], v1 = vb4[1], v2 = vb4[2];
+        const uint32_t vlo0[4] = {v0.x, v0.w, v1.z, v2.y};
+        const uint32_t vlo1[4] = {v0.y, v1.x, v1.w, v2.z};
+        const uint32_t vhi[4] = {v0.z, v1.y, v2.x, v2.w};
 #pragma unroll
-      for (int mb = 0; mb < 8; ++mb) {
-        const uint32_t* v0 = vb + (16 * mb + g) * 3;
-        const uint32_t* v1 = v0 + 8 * 3;
-        const uint32_t a_lo0 = v0[0], a_lo1 = v0[1], a_hi = v0[2];
-        const uint32_t b_lo0 = v1[0], b_lo1 = v1[1], b_hi = v1[2];
-        uint32_t a[4];
-        // quad r: high bit r -> bit 2 via (hi << 2) >> r (bits 30-31 belong to quads 6-7)
-        a[0] = quad_bytes(a_lo0, 2 * r, (a_hi << 2) >> r);
-        a[1] = quad_bytes(b_lo0, 2 * r, (b_hi << 2) >> r);
-        // quad r + 4: low bits in word 1 at 2r, high bit r+4 -> bit 2 via >> (r + 2)
-        a[2] = quad_bytes(a_lo1, 2 * r, a_hi >> (r + 2));
-        a[3] = quad_bytes(b_lo1, 2 * r, b_hi >> (r + 2));
-        mma_u8u8(pv[mb][0], a, bw[0][0], bw[0][1]);
-        mma_u8u8(pv[mb][1], a, bw[1][0], bw[1][1]);
+        for (int m = 0; m < 4; ++m) {
+          // dims j = 0, 1: mb = 2m (rows g, g+8); j = 2, 3: mb = 2m + 1
+          uint32_t a0 = quad<0, 0>(vlo0[m], vhi[m]);
+          uint32_t a1 = quad<2, 1>(vlo0[m], vhi[m]);
+          uint32_t a2 = quad<0, 4>(vlo1[m], vhi[m]);
+          uint32_t a3 = quad<2, 5>(vlo1[m], vhi[m]);
+          mma_u8u8(pv[2 * m][0], a0, a1, a2, a3, bw[0][0], bw[0][1]);
+          mma_u8u8(pv[2 * m][1], a0, a1, a2, a3, bw[1][0], bw[1][1]);
+          a0 = quad<4, 2>(vlo0[m], vhi[m]);
+          a1 = quad<6, 3>(vlo0[m], vhi[m]);
+          a2 = quad<4, 6>(vlo1[m], vhi[m]);
+          a3 = quad<6, 7>(vlo1[m], vhi[m]);
+          mma_u8u8(pv[2 * m + 1][0], a0, a1, a2, a3, bw[0][0], bw[0][1]);
+          mma_u8u8(pv[2 * m + 1][1], a0, a1, a2, a3, bw[1][0], bw[1][1]);
+        }
       }
     }
     __syncwarp();
     if (lane == 0) tc::mbar_arrive(empty0 + 8 * s);
   }
-  if (wmul > 0.0f) fold(1.0f / wmul);
+  if (wmul > 0.0f) fold_scale(1.0f / wmul, 1.0f);
 #pragma unroll
   for (int o2 = 4; o2 < 32; o2 <<= 1) {
     l_part += __shfl_xor_sync(0xffffffffu, l_part, o2);
     vmin_part += __shfl_xor_sync(0xffffffffu, vmin_part, o2);
   }
-  // ---- combine the 4 warps in shared memory; the stage buffers are free
-  // (every issued copy has been consumed)
-  asm volatile("bar.sync 1, %0;" ::"r"(kDecWarps * 32) : "memory");
+  // ---- combine the 4 warps through shared memory (the stage buffers are
+  // free: every issued copy has been consumed)
   float* red = reinterpret_cast<float*>(smem);  // [warp][head][4]
-  float* ored = red + kDecWarps * 4 * 4;        // [warp][head][128]
   if (g == 0) {
     red[(warp * 4 + r) * 4 + 0] = m_run;
     red[(warp * 4 + r) * 4 + 1] = l_part;
     red[(warp * 4 + r) * 4 + 2] = vmin_part;
   }
-#pragma unroll
-  for (int mb = 0; mb < 8; ++mb)
-#pragma unroll
-    for (int h = 0; h < 2; ++h) ored[(warp * 4 + r) * kD + 16 * mb + g + 8 * h] = o[2 * mb + h];
   asm volatile("bar.sync 1, %0;" ::"r"(kDecWarps * 32) : "memory");
   {
     const int hh = warp;  // head written by this warp; dims 4*lane..4*lane+3
@@ -649,9 +723,11 @@ __global__ void __launch_bounds__((kDecWarps + 1) * 32)
         const float f = mw == -INFINITY ? 0.0f : exp2f(mw - M);
         l = fmaf(f, red[(w * 4 + hh) * 4 + 1], l);
         vm = fmaf(f, red[(w * 4 + hh) * 4 + 2], vm);
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-          num[k] = fmaf(f, ored[(w * 4 + hh) * kD + 4 * lane + k], num[k]);
+        const float4 o4 = reinterpret_cast<const float4*>(osm + (w * 4 + hh) * kD)[lane];
+        num[0] = fmaf(f, o4.x, num[0]);
+        num[1] = fmaf(f, o4.y, num[1]);
+        num[2] = fmaf(f, o4.z, num[2]);
+        num[3] = fmaf(f, o4.w, num[3]);
       }
       const int nsplit = gridDim.x;
       float* pp = p.part + (((b * p.Hq) + qh0 + hh) * nsplit + split) * kPart;
@@ -710,13 +786,14 @@ int grow(ft_kv3* c, int64_t need, cudaStream_t s) {
   if (ncap < need + kBlk) ncap = need + kBlk;  // room for the head offset
   ncap = round_up(ncap, kBlk);
   const int64_t rows = c->batch * c->kv_heads, nbc = c->cap / kBlk, nnbc = ncap / kBlk;
-  uint8_t* kc = nullptr;
+  uint32_t* kc = nullptr;
   uint32_t* vc = nullptr;
   float2 *kmm = nullptr, *vmm = nullptr;
   cudaError_t e = cudaMalloc(&kc, (size_t)(rows * ncap * kRec));
   if (e == cudaSuccess) e = cudaMalloc(&vc, (size_t)(rows * ncap * kRec));
   if (e == cudaSuccess) e = cudaMalloc(&kmm, (size_t)(rows * ncap * 8));
   if (e == cudaSuccess) e = cudaMalloc(&vmm, (size_t)(rows * ncap * 8));
+  if (e == cudaSuccess) e = cudaMemsetAsync(kc, 0, (size_t)(rows * ncap * kRec), s);
   if (e == cudaSuccess) e = cudaMemsetAsync(vc, 0, (size_t)(rows * ncap * kRec), s);
   if (e != cudaSuccess) {
     cudaFree(kc);
@@ -735,7 +812,8 @@ int grow(ft_kv3* c, int64_t need, cudaStream_t s) {
   const size_t kb = (size_t)kBlkBytes, mb = (size_t)kMmBlkBytes;
   for (const auto& run : runs) {
     if (run[2] <= 0) continue;
-    FT_CUDA(cudaMemcpy2DAsync(kc + run[1] * kb, nnbc * kb, c->kc + run[0] * kb, nbc * kb,
+    FT_CUDA(cudaMemcpy2DAsync(reinterpret_cast<uint8_t*>(kc) + run[1] * kb, nnbc * kb,
+                              reinterpret_cast<uint8_t*>(c->kc) + run[0] * kb, nbc * kb,
                               run[2] * kb, rows, cudaMemcpyDeviceToDevice, s));
     FT_CUDA(cudaMemcpy2DAsync(reinterpret_cast<uint8_t*>(vc) + run[1] * kb, nnbc * kb,
                               reinterpret_cast<uint8_t*>(c->vc) + run[0] * kb, nbc * kb,
@@ -853,8 +931,9 @@ int ft_kv3_create(ft_ctx* ctx, int64_t batch, int64_t kv_heads, int64_t head_dim
   if (e == cudaSuccess) e = cudaMalloc(&c->vc, slots * kRec);
   if (e == cudaSuccess) e = cudaMalloc(&c->kmm, slots * 8);
   if (e == cudaSuccess) e = cudaMalloc(&c->vmm, slots * 8);
-  // the V blocks start zeroed: append rewrites whole triples, and the decode
-  // reads whole blocks (slots outside the live range get zero weight)
+  // blocks start zeroed (the decode reads whole blocks; slots outside the
+  // live range get zero weight whatever they hold)
+  if (e == cudaSuccess) e = cudaMemset(c->kc, 0, slots * kRec);
   if (e == cudaSuccess) e = cudaMemset(c->vc, 0, slots * kRec);
   if (e != cudaSuccess) {
     cudaFree(c->kc);
@@ -986,7 +1065,6 @@ int ft_flash_decode_3bit(ft_ctx* ctx, ft_kv3* c, const float* q_dev, int64_t q_h
   p.Hkv = c->kv_heads;
   p.G = (int)(q_heads / c->kv_heads);
   p.hgroups = (p.G + 3) / 4;
-  p.cap = c->cap;
   p.nbc = c->cap / kBlk;
   p.head_off = c->head % kBlk;
   p.head_blk = c->head / kBlk;
