@@ -17,19 +17,18 @@
 // slots are grouped in blocks of 32, and each block is stored "lane-major":
 // the 12 words that lane L = 4g + r (g = L/4, r = L%4) of a decode warp feeds
 // into its tensor-core fragments are contiguous (48 bytes at L*48), so a lane
-// reads them with three 128-bit shared loads and extracts 4 codes per
-// fragment register with compile-time shifts and masks.  Codes are split into
-// their low 2 bits and high bit: shifting a word by 2j and masking with
-// 0x03030303 gives 4 low parts as bytes, shifting the high word and masking
-// with 0x04040404 puts the 4 high bits at bit 2 of each byte.
+// reads them with three 128-bit shared loads.
+// The unit of storage is a "triple": 3 words holding 8 quads Q = 0..7 of 4
+// codes each, byte b of every word belonging to element b of each quad.
+// Quads 0..5 are whole 3-bit fields (word Q/2, bits 8b + 3(Q%2) .. +2), so a
+// quad becomes the 4 bytes of an int8 fragment register with one shift and
+// one mask; quads 6 and 7 keep their low 2 bits in bits 8b+6..7 of word 0 and
+// word 1 and their high bit in word 2 at bit 8b + Q.
 //   K block (1536 B): slot s = g + 8e (e in 0..3) sits in lane group g; lane
-//     4g + r, words 3e + {0,1,2} hold the codes of slot s for the 32 dims
-//     {4(r + 4i) + b : i in 0..7, b in 0..3}: low bits of dim 4(r+4i)+b in
-//     word 3e + i/4 at bit 8b + 2(i%4), its high bit in word 3e+2 at bit 8b + i.
-//   V block (1536 B): lane 4g + r, words 3m + {0,1,2} (m in 0..3) hold the
-//     codes of the 4 dims j = 0..3 -> d = 16(2m + j/2) + g + 8(j%2) for the 8
-//     slots r + 4a + 8e (a in 0..1, e in 0..3): low bits in word 3m + a at bit
-//     8e + 2j, high bit in word 3m+2 at bit 8e + 4a + j.
+//     4g + r, triple e holds slot s's codes of dims 4(r + 4Q) + b.
+//   V block (1536 B): lane 4g + r, triple m (0..3) holds, for j = 0..3 and
+//     a = 0..1, quad Q = 2j + a: the codes of dim 16(2m + j/2) + g + 8(j%2) at
+//     slots r + 4a + 8b.
 //   min/max: per block 32 float2 (K and V separately), slot s at (s%8)*4 + s/8.
 // 3 bits per code: 48 B of codes + 8 B of (min, max) per vector, the
 // reference's footprint.
@@ -100,36 +99,44 @@ __device__ __forceinline__ float load_act(const void* p, int64_t i, int bf16) {
 }
 
 // ---- layout maps (word indices within a 384-word block) ----
-__device__ __forceinline__ int k_lo_word(int s, int d) {
-  const int qd = d >> 2, r = qd & 3, i = qd >> 2;
-  return (4 * (s & 7) + r) * 12 + 3 * (s >> 3) + (i >> 2);
+// triple base word and quad of K code (slot s, dim d) / V code (slot s, dim d)
+__device__ __forceinline__ int k_triple(int s, int d) {
+  return (4 * (s & 7) + ((d >> 2) & 3)) * 12 + 3 * (s >> 3);
 }
-__device__ __forceinline__ int k_hi_word(int s, int d) {
-  const int r = (d >> 2) & 3;
-  return (4 * (s & 7) + r) * 12 + 3 * (s >> 3) + 2;
+__device__ __forceinline__ int k_quad(int d) { return d >> 4; }
+__device__ __forceinline__ int k_elem(int s, int d) { return d & 3; }
+__device__ __forceinline__ int v_triple(int s, int d) {
+  return (4 * (d & 7) + (s & 3)) * 12 + 3 * (d >> 5);
 }
-__device__ __forceinline__ int k_lo_bit(int d) { return 8 * (d & 3) + 2 * ((d >> 4) & 3); }
-__device__ __forceinline__ int k_hi_bit(int d) { return 8 * (d & 3) + (d >> 4); }
-// V: dim d -> (g, m, j); slot s -> (r, a, e)
-__device__ __forceinline__ int v_lane(int s, int d) { return 4 * (d & 7) + (s & 3); }
-__device__ __forceinline__ int v_j(int d) { return 2 * ((d >> 4) & 1) + ((d >> 3) & 1); }
-__device__ __forceinline__ int v_lo_word(int s, int d) {
-  return v_lane(s, d) * 12 + 3 * (d >> 5) + ((s >> 2) & 1);
+__device__ __forceinline__ int v_quad(int s, int d) {
+  return 2 * (2 * ((d >> 4) & 1) + ((d >> 3) & 1)) + ((s >> 2) & 1);
 }
-__device__ __forceinline__ int v_hi_word(int s, int d) { return v_lane(s, d) * 12 + 3 * (d >> 5) + 2; }
-__device__ __forceinline__ int v_lo_bit(int s, int d) { return 8 * (s >> 3) + 2 * v_j(d); }
-__device__ __forceinline__ int v_hi_bit(int s, int d) {
-  return 8 * (s >> 3) + 4 * ((s >> 2) & 1) + v_j(d);
-}
+__device__ __forceinline__ int v_elem(int s) { return s >> 3; }
 __device__ __forceinline__ int mm_index(int s) { return (s & 7) * 4 + (s >> 3); }
 
+__device__ __forceinline__ uint32_t triple_get(const uint32_t* t, int Q, int b) {
+  if (Q < 6) return (t[Q >> 1] >> (8 * b + 3 * (Q & 1))) & 7u;
+  return ((t[Q - 6] >> (8 * b + 6)) & 3u) | (((t[2] >> (8 * b + Q)) & 1u) << 2);
+}
+// writes code c at (Q, b) of a shared-memory triple; concurrent writers touch
+// disjoint bits
+__device__ __forceinline__ void triple_put(uint32_t* t, int Q, int b, uint32_t c) {
+  if (Q < 6) {
+    const int sh = 8 * b + 3 * (Q & 1);
+    atomicAnd(&t[Q >> 1], ~(7u << sh));
+    atomicOr(&t[Q >> 1], c << sh);
+  } else {
+    atomicAnd(&t[Q - 6], ~(3u << (8 * b + 6)));
+    atomicOr(&t[Q - 6], (c & 3u) << (8 * b + 6));
+    atomicAnd(&t[2], ~(1u << (8 * b + Q)));
+    atomicOr(&t[2], (c >> 2) << (8 * b + Q));
+  }
+}
 __device__ __forceinline__ uint32_t k_code(const uint32_t* blk, int s, int d) {
-  return ((blk[k_lo_word(s, d)] >> k_lo_bit(d)) & 3u) |
-         (((blk[k_hi_word(s, d)] >> k_hi_bit(d)) & 1u) << 2);
+  return triple_get(blk + k_triple(s, d), k_quad(d), k_elem(s, d));
 }
 __device__ __forceinline__ uint32_t v_code(const uint32_t* blk, int s, int d) {
-  return ((blk[v_lo_word(s, d)] >> v_lo_bit(s, d)) & 3u) |
-         (((blk[v_hi_word(s, d)] >> v_hi_bit(s, d)) & 1u) << 2);
+  return triple_get(blk + v_triple(s, d), v_quad(s, d), v_elem(s));
 }
 
 // ---------------------------------------------------------------- append --
@@ -228,15 +235,8 @@ __global__ void __launch_bounds__(kD) kv3_append_kernel(AppendParams p) {
         cv = q <= 0.0f ? 0u : (q >= 7.0f ? 7u : (uint32_t)q);
       }
     }
-    // the slot's bits: clear, then set (threads touch disjoint bits)
-    atomicAnd(&kw[k_lo_word(u, d)], ~(3u << k_lo_bit(d)));
-    atomicAnd(&kw[k_hi_word(u, d)], ~(1u << k_hi_bit(d)));
-    atomicAnd(&vw[v_lo_word(u, d)], ~(3u << v_lo_bit(u, d)));
-    atomicAnd(&vw[v_hi_word(u, d)], ~(1u << v_hi_bit(u, d)));
-    atomicOr(&kw[k_lo_word(u, d)], (ck & 3u) << k_lo_bit(d));
-    atomicOr(&kw[k_hi_word(u, d)], ((ck >> 2) & 1u) << k_hi_bit(d));
-    atomicOr(&vw[v_lo_word(u, d)], (cv & 3u) << v_lo_bit(u, d));
-    atomicOr(&vw[v_hi_word(u, d)], ((cv >> 2) & 1u) << v_hi_bit(u, d));
+    triple_put(kw + k_triple(u, d), k_quad(d), k_elem(u, d), ck);
+    triple_put(vw + v_triple(u, d), v_quad(u, d), v_elem(u), cv);
     if (d == 0) p.kmm[(row * p.nbc + pb) * kBlk + mm_index(u)] = make_float2(kmin, kmax);
     if (d == 1) p.vmm[(row * p.nbc + pb) * kBlk + mm_index(u)] = make_float2(vmin, vmax);
     __syncthreads();  // red is reused by the next position
@@ -360,12 +360,18 @@ __device__ __forceinline__ void mma_u8u8(int (&c)[4], uint32_t a0, uint32_t a1, 
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// 4 codes as bytes: low parts from `lo` shifted by LS, high bits from `hi`
-// moved from bit HB of each byte to bit 2 (compile-time shifts).
-template <int LS, int HB>
-__device__ __forceinline__ uint32_t quad(uint32_t lo, uint32_t hi) {
-  const uint32_t h = HB >= 2 ? (hi >> (HB - 2)) : (hi << (2 - HB));
-  return ((lo >> LS) & 0x03030303u) | (h & 0x04040404u);
+// quad Q of a triple as the 4 bytes of an int8 fragment register
+template <int Q>
+__device__ __forceinline__ uint32_t tquad(uint32_t w0, uint32_t w1, uint32_t w2) {
+  constexpr uint32_t M3 = 0x07070707u;
+  if (Q == 0) return w0 & M3;
+  if (Q == 1) return (w0 >> 3) & M3;
+  if (Q == 2) return w1 & M3;
+  if (Q == 3) return (w1 >> 3) & M3;
+  if (Q == 4) return w2 & M3;
+  if (Q == 5) return (w2 >> 3) & M3;
+  if (Q == 6) return ((w0 >> 6) & 0x03030303u) | ((w2 >> 4) & 0x04040404u);
+  return ((w1 >> 6) & 0x03030303u) | ((w2 >> 5) & 0x04040404u);
 }
 
 // exact for |d| < 2^22
@@ -560,42 +566,32 @@ __global__ void __launch_bounds__((kDecWarps + 1) * 32, FT_KV_MIN_BLOCKS)
       float s2[4], vsv[4], vmn[4];
       {
         const uint4 k0 = kb4[0], k1 = kb4[1], k2 = kb4[2];
-        // slot e = 0: k0.x k0.y k0.z | e = 1: k0.w k1.x k1.y | e = 2: k1.z k1.w k2.x | e = 3: k2.y..
-        const uint32_t lo0[4] = {k0.x, k0.w, k1.z, k2.y};
-        const uint32_t lo1[4] = {k0.y, k1.x, k1.w, k2.z};
-        const uint32_t hiw[4] = {k0.z, k1.y, k2.x, k2.w};
+        // triple of slot e: (kw0[e], kw1[e], kw2[e])
+        const uint32_t kw0[4] = {k0.x, k0.w, k1.z, k2.y};
+        const uint32_t kw1[4] = {k0.y, k1.x, k1.w, k2.z};
+        const uint32_t kw2[4] = {k0.z, k1.y, k2.x, k2.w};
 #pragma unroll
         for (int mb = 0; mb < 2; ++mb) {
           int acc[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
           const int ea = 2 * mb, eb = 2 * mb + 1;  // rows g, g+8
-#pragma unroll
-          for (int ks = 0; ks < 4; ++ks) {
-            const uint4 bq = qf[ks * 32 + lane];
-            uint32_t a0, a1, a2, a3;
-            // quad index i0 = 2ks (a0, a1) and i1 = 2ks + 1 (a2, a3)
-#define FT_KQ(I, LOA, HIA) quad<2 * ((I) & 3), (I)>(LOA, HIA)
-            if (ks == 0) {
-              a0 = FT_KQ(0, lo0[ea], hiw[ea]); a1 = FT_KQ(0, lo0[eb], hiw[eb]);
-              a2 = FT_KQ(1, lo0[ea], hiw[ea]); a3 = FT_KQ(1, lo0[eb], hiw[eb]);
-            } else if (ks == 1) {
-              a0 = FT_KQ(2, lo0[ea], hiw[ea]); a1 = FT_KQ(2, lo0[eb], hiw[eb]);
-              a2 = FT_KQ(3, lo0[ea], hiw[ea]); a3 = FT_KQ(3, lo0[eb], hiw[eb]);
-            } else if (ks == 2) {
-              a0 = FT_KQ(4, lo1[ea], hiw[ea]); a1 = FT_KQ(4, lo1[eb], hiw[eb]);
-              a2 = FT_KQ(5, lo1[ea], hiw[ea]); a3 = FT_KQ(5, lo1[eb], hiw[eb]);
-            } else {
-              a0 = FT_KQ(6, lo1[ea], hiw[ea]); a1 = FT_KQ(6, lo1[eb], hiw[eb]);
-              a2 = FT_KQ(7, lo1[ea], hiw[ea]); a3 = FT_KQ(7, lo1[eb], hiw[eb]);
-            }
-#undef FT_KQ
-            mma_u8s8(acc[0], a0, a1, a2, a3, bq.x, bq.y);
-            mma_u8s8(acc[1], a0, a1, a2, a3, bq.z, bq.w);
-          }
+          // k-step ks covers quads 2ks (a0, a1) and 2ks + 1 (a2, a3)
+#define FT_KSTEP(KS)                                                                      \
+  {                                                                                       \
+    const uint4 bq = qf[(KS) * 32 + lane];                                                \
+    const uint32_t a0 = tquad<2 * (KS)>(kw0[ea], kw1[ea], kw2[ea]);                       \
+    const uint32_t a1 = tquad<2 * (KS)>(kw0[eb], kw1[eb], kw2[eb]);                       \
+    const uint32_t a2 = tquad<2 * (KS) + 1>(kw0[ea], kw1[ea], kw2[ea]);                   \
+    const uint32_t a3 = tquad<2 * (KS) + 1>(kw0[eb], kw1[eb], kw2[eb]);                   \
+    mma_u8s8(acc[0], a0, a1, a2, a3, bq.x, bq.y);                                         \
+    mma_u8s8(acc[1], a0, a1, a2, a3, bq.z, bq.w);                                         \
+  }
+          FT_KSTEP(0) FT_KSTEP(1) FT_KSTEP(2) FT_KSTEP(3)
+#undef FT_KSTEP
           const float4 kmA = km4[mb];  // (min, max) of slots e = 2mb, 2mb + 1
           const float4 vmA = vm4[mb];
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            const int e = 2 * mb + h, u = g + 8 * e;
+            const int e = 2 * mb + h;
             const float S = fmaf(
                 fmaf(fmaf(small_int_to_float(acc[1][2 * h + 1]), 256.0f,
                           small_int_to_float(acc[1][2 * h])),
@@ -603,11 +599,21 @@ __global__ void __launch_bounds__((kDecWarps + 1) * 32, FT_KV_MIN_BLOCKS)
                 256.0f, small_int_to_float(acc[0][2 * h]));
             const float kmin = h ? kmA.z : kmA.x, kmax = h ? kmA.w : kmA.y;
             const float vmin = h ? vmA.z : vmA.x, vmax = h ? vmA.w : vmA.y;
-            const bool live = u >= lo_live && u < hi_live;
             const float ksc = (kmax - kmin) * 0.14285714285714285f;
-            s2[e] = live ? fmaf(kmin, qsum, ksc * (S * qscale)) : -INFINITY;
-            vsv[e] = live ? (vmax - vmin) * 0.14285714285714285f : 0.0f;
-            vmn[e] = live ? vmin : 0.0f;
+            s2[e] = fmaf(kmin, qsum, ksc * (S * qscale));
+            vsv[e] = (vmax - vmin) * 0.14285714285714285f;
+            vmn[e] = vmin;
+          }
+        }
+      }
+      if (lo_live > 0 || hi_live < kBlk) {  // a partial block (warp-uniform)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int u = g + 8 * e;
+          if (u < lo_live || u >= hi_live) {
+            s2[e] = -INFINITY;
+            vsv[e] = 0.0f;
+            vmn[e] = 0.0f;
           }
         }
       }
@@ -671,22 +677,23 @@ __global__ void __launch_bounds__((kDecWarps + 1) * 32, FT_KV_MIN_BLOCKS)
       }
       {
         const uint4 v0 = vb4[0], v1 = vb4[1], v2 = vb4[2];
-        const uint32_t vlo0[4] = {v0.x, v0.w, v1.z, v2.y};
-        const uint32_t vlo1[4] = {v0.y, v1.x, v1.w, v2.z};
-        const uint32_t vhi[4] = {v0.z, v1.y, v2.x, v2.w};
+        const uint32_t vw0[4] = {v0.x, v0.w, v1.z, v2.y};
+        const uint32_t vw1[4] = {v0.y, v1.x, v1.w, v2.z};
+        const uint32_t vw2[4] = {v0.z, v1.y, v2.x, v2.w};
 #pragma unroll
         for (int m = 0; m < 4; ++m) {
-          // dims j = 0, 1: mb = 2m (rows g, g+8); j = 2, 3: mb = 2m + 1
-          uint32_t a0 = quad<0, 0>(vlo0[m], vhi[m]);
-          uint32_t a1 = quad<2, 1>(vlo0[m], vhi[m]);
-          uint32_t a2 = quad<0, 4>(vlo1[m], vhi[m]);
-          uint32_t a3 = quad<2, 5>(vlo1[m], vhi[m]);
+          // quad Q = 2j + a: dims j = 0, 1 are rows g, g+8 of mb = 2m, j = 2, 3 of
+          // mb = 2m + 1; a = 0 is k 4r..4r+3, a = 1 is k 16+4r..
+          uint32_t a0 = tquad<0>(vw0[m], vw1[m], vw2[m]);
+          uint32_t a1 = tquad<2>(vw0[m], vw1[m], vw2[m]);
+          uint32_t a2 = tquad<1>(vw0[m], vw1[m], vw2[m]);
+          uint32_t a3 = tquad<3>(vw0[m], vw1[m], vw2[m]);
           mma_u8u8(pv[2 * m][0], a0, a1, a2, a3, bw[0][0], bw[0][1]);
           mma_u8u8(pv[2 * m][1], a0, a1, a2, a3, bw[1][0], bw[1][1]);
-          a0 = quad<4, 2>(vlo0[m], vhi[m]);
-          a1 = quad<6, 3>(vlo0[m], vhi[m]);
-          a2 = quad<4, 6>(vlo1[m], vhi[m]);
-          a3 = quad<6, 7>(vlo1[m], vhi[m]);
+          a0 = tquad<4>(vw0[m], vw1[m], vw2[m]);
+          a1 = tquad<6>(vw0[m], vw1[m], vw2[m]);
+          a2 = tquad<5>(vw0[m], vw1[m], vw2[m]);
+          a3 = tquad<7>(vw0[m], vw1[m], vw2[m]);
           mma_u8u8(pv[2 * m + 1][0], a0, a1, a2, a3, bw[0][0], bw[0][1]);
           mma_u8u8(pv[2 * m + 1][1], a0, a1, a2, a3, bw[1][0], bw[1][1]);
         }
