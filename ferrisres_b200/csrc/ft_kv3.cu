@@ -30,6 +30,9 @@
 //     a = 0..1, quad Q = 2j + a: the codes of dim 16(2m + j/2) + g + 8(j%2) at
 //     slots r + 4a + 8b.
 //   min/max: per block 32 float2 (K and V separately), slot s at (s%8)*4 + s/8.
+// A block's K words, V words, K min/max and V min/max form one 3584-byte
+// record, and consecutive blocks of a row are contiguous, so a tile of 4
+// blocks is one bulk copy.
 // 3 bits per code: 48 B of codes + 8 B of (min, max) per vector, the
 // reference's footprint.
 //
@@ -55,10 +58,7 @@ struct ft_kv3 {
   int device = 0;
   int64_t batch = 0, kv_heads = 0, cap = 0;  // cap: slots per row, multiple of 32
   int64_t head = 0, len = 0;                   // ring start slot, live positions
-  uint32_t* kc = nullptr;  // K blocks
-  uint32_t* vc = nullptr;  // V blocks
-  float2* kmm = nullptr;
-  float2* vmm = nullptr;
+  uint32_t* blocks = nullptr;  // [row][cap/32] block records
   ft::Workspace part;  // split partials
 };
 
@@ -73,10 +73,10 @@ constexpr int kBlkBytes = kBlk * kRec;   // 1536 (both K and V)
 constexpr int kMmBlkBytes = kBlk * 8;    // 256
 constexpr int kDecWarps = 4;             // compute warps = blocks per tile
 constexpr int kStages = 4;
-constexpr int kStageBytes = kDecWarps * (2 * kBlkBytes + 2 * kMmBlkBytes);  // 14336
-constexpr int kOffV = kDecWarps * kBlkBytes;
-constexpr int kOffKmm = 2 * kDecWarps * kBlkBytes;
-constexpr int kOffVmm = kOffKmm + kDecWarps * kMmBlkBytes;
+constexpr int kRecBytes = 2 * kBlkBytes + 2 * kMmBlkBytes;  // 3584: K | V | K min/max | V min/max
+constexpr int kRecWords = kRecBytes / 4;
+constexpr int kRecV = kBlkWords, kRecKmm = 2 * kBlkWords, kRecVmm = 2 * kBlkWords + 2 * kBlk;
+constexpr int kStageBytes = kDecWarps * kRecBytes;  // 14336
 constexpr int kWsmBytes = kDecWarps * 4 * 4 * kBlk;      // [warp][digit][head][8 words]
 constexpr int kQfBytes = 4 * 32 * 16;                    // q fragments [chunk][lane][16 B]
 constexpr int kOsmBytes = kDecWarps * 4 * kD * 4;        // fp32 numerators [warp][head][128]
@@ -147,10 +147,7 @@ struct AppendParams {
   const float* vmm_in;
   int bf16;
   int64_t n_pos, Hkv, cap, nbc, s0;
-  uint32_t* kc;
-  uint32_t* vc;
-  float2* kmm;
-  float2* vmm;
+  uint32_t* blocks;
 };
 
 // code idx of a reference LSB-first 3-bit stream (the next byte is read only
@@ -178,8 +175,10 @@ __global__ void __launch_bounds__(kD) kv3_append_kernel(AppendParams p) {
   const int u_end = u_end64 > kBlk ? kBlk : (int)u_end64;
   __shared__ float red[4][4];
   __shared__ uint32_t kw[kBlkWords], vw[kBlkWords];
-  uint32_t* kg = p.kc + (row * p.nbc + pb) * kBlkWords;
-  uint32_t* vg = p.vc + (row * p.nbc + pb) * kBlkWords;
+  uint32_t* kg = p.blocks + (row * p.nbc + pb) * kRecWords;
+  uint32_t* vg = kg + kRecV;
+  float2* kmm = reinterpret_cast<float2*>(kg + kRecKmm);
+  float2* vmm = reinterpret_cast<float2*>(kg + kRecVmm);
   for (int i = d; i < kBlkWords; i += kD) {
     kw[i] = kg[i];
     vw[i] = vg[i];
@@ -237,8 +236,8 @@ __global__ void __launch_bounds__(kD) kv3_append_kernel(AppendParams p) {
     }
     triple_put(kw + k_triple(u, d), k_quad(d), k_elem(u, d), ck);
     triple_put(vw + v_triple(u, d), v_quad(u, d), v_elem(u), cv);
-    if (d == 0) p.kmm[(row * p.nbc + pb) * kBlk + mm_index(u)] = make_float2(kmin, kmax);
-    if (d == 1) p.vmm[(row * p.nbc + pb) * kBlk + mm_index(u)] = make_float2(vmin, vmax);
+    if (d == 0) kmm[mm_index(u)] = make_float2(kmin, kmax);
+    if (d == 1) vmm[mm_index(u)] = make_float2(vmin, vmax);
     __syncthreads();  // red is reused by the next position
   }
   for (int i = d; i < kBlkWords; i += kD) {
@@ -250,10 +249,7 @@ __global__ void __launch_bounds__(kD) kv3_append_kernel(AppendParams p) {
 // ------------------------------------------------------- read-back kernels --
 struct RangeParams {
   int64_t B, Hkv, cap, nbc, head, start, n;
-  const uint32_t* kc;
-  const uint32_t* vc;
-  const float2* kmm;
-  const float2* vmm;
+  const uint32_t* blocks;
 };
 
 // get_range (turboquant_kv.rs:271-291): out [B][n][Hkv][128] f32, dequantised
@@ -269,9 +265,11 @@ __global__ void kv3_dequant_kernel(RangeParams p, float* __restrict__ kout,
   const int64_t slot = (p.head + p.start + pos) % p.cap;
   const int64_t blk = row * p.nbc + slot / kBlk;
   const int s = (int)(slot % kBlk);
-  const uint32_t ck = k_code(p.kc + blk * kBlkWords, s, d);
-  const uint32_t cv = v_code(p.vc + blk * kBlkWords, s, d);
-  const float2 km = p.kmm[blk * kBlk + mm_index(s)], vm = p.vmm[blk * kBlk + mm_index(s)];
+  const uint32_t* rec = p.blocks + blk * kRecWords;
+  const uint32_t ck = k_code(rec, s, d);
+  const uint32_t cv = v_code(rec + kRecV, s, d);
+  const float2 km = reinterpret_cast<const float2*>(rec + kRecKmm)[mm_index(s)];
+  const float2 vm = reinterpret_cast<const float2*>(rec + kRecVmm)[mm_index(s)];
   float kv, vv;
   if (km.y == km.x) {
     kv = km.x;
@@ -301,8 +299,8 @@ __global__ void kv3_export_kernel(RangeParams p, uint8_t* __restrict__ kbytes,
   const int64_t slot = (p.head + p.start + pos) % p.cap;
   const int64_t blk = row * p.nbc + slot / kBlk;
   const int s = (int)(slot % kBlk);
-  const uint32_t* kb = p.kc + blk * kBlkWords;
-  const uint32_t* vb = p.vc + blk * kBlkWords;
+  const uint32_t* kb = p.blocks + blk * kRecWords;
+  const uint32_t* vb = kb + kRecV;
   uint32_t kbits = 0, vbits = 0;
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
@@ -317,7 +315,8 @@ __global__ void kv3_export_kernel(RangeParams p, uint8_t* __restrict__ kbytes,
   vbytes[o + 1] = (uint8_t)((vbits >> 8) & 0xFF);
   vbytes[o + 2] = (uint8_t)((vbits >> 16) & 0xFF);
   if (m == 0) {
-    const float2 km = p.kmm[blk * kBlk + mm_index(s)], vm = p.vmm[blk * kBlk + mm_index(s)];
+    const float2 km = reinterpret_cast<const float2*>(kb + kRecKmm)[mm_index(s)];
+    const float2 vm = reinterpret_cast<const float2*>(kb + kRecVmm)[mm_index(s)];
     kmm_out[vec * 2] = km.x;
     kmm_out[vec * 2 + 1] = km.y;
     vmm_out[vec * 2] = vm.x;
@@ -334,10 +333,7 @@ struct DecodeParams {
   int64_t nlb;        // logical 32-slot blocks covering the live range
   int64_t tiles_per;  // 128-slot tiles per split
   float qk_log2;      // softmax scale * log2(e)
-  const uint32_t* kc;
-  const uint32_t* vc;
-  const float2* kmm;
-  const float2* vmm;
+  const uint32_t* blocks;
   float* part;  // [B][Hq][nsplit][kPart]
   int* err;
 };
@@ -488,19 +484,17 @@ __global__ void __launch_bounds__((kDecWarps + 1) * 32, FT_KV_MIN_BLOCKS)
         if (!ok) break;
         const int64_t j0 = (t_begin + it) * kDecWarps;
         const int nb = p.nlb - j0 < kDecWarps ? (int)(p.nlb - j0) : kDecWarps;
-        tc::mbar_arrive_expect_tx(full0 + 8 * s, nb * (2 * kBlkBytes + 2 * kMmBlkBytes));
+        tc::mbar_arrive_expect_tx(full0 + 8 * s, nb * kRecBytes);
         const uint32_t sb = stage_base + s * kStageBytes;
-        for (int w = 0; w < nb; ++w) {
-          const int64_t blk = row * p.nbc + pb;
-          tc::bulk_g2s(sb + w * kBlkBytes, p.kc + blk * kBlkWords, kBlkBytes, full0 + 8 * s);
-          tc::bulk_g2s(sb + kOffV + w * kBlkBytes, p.vc + blk * kBlkWords, kBlkBytes,
-                       full0 + 8 * s);
-          tc::bulk_g2s(sb + kOffKmm + w * kMmBlkBytes, p.kmm + blk * kBlk, kMmBlkBytes,
-                       full0 + 8 * s);
-          tc::bulk_g2s(sb + kOffVmm + w * kMmBlkBytes, p.vmm + blk * kBlk, kMmBlkBytes,
-                       full0 + 8 * s);
-          if (++pb == p.nbc) pb = 0;
-        }
+        // nb consecutive records from physical block pb, wrapping at most once
+        const int n1 = pb + nb <= p.nbc ? nb : (int)(p.nbc - pb);
+        tc::bulk_g2s(sb, p.blocks + (row * p.nbc + pb) * kRecWords, n1 * kRecBytes,
+                     full0 + 8 * s);
+        if (n1 < nb)
+          tc::bulk_g2s(sb + n1 * kRecBytes, p.blocks + row * p.nbc * kRecWords,
+                       (nb - n1) * kRecBytes, full0 + 8 * s);
+        pb += nb;
+        if (pb >= p.nbc) pb -= p.nbc;
         ++issued;
       }
       // the copies of the last stages must land before the CTA may exit
@@ -545,23 +539,23 @@ __global__ void __launch_bounds__((kDecWarps + 1) * 32, FT_KV_MIN_BLOCKS)
         for (int c = 0; c < 4; ++c) pv[mb][nb][c] = 0;
   };
 
-  for (int it = 0; it < ntiles; ++it) {
+  // 32-bit block arithmetic: the host keeps head_off + len below 2^31 - 64
+  const int nlb32 = (int)p.nlb, hoff = (int)p.head_off, len32 = (int)p.len;
+  int j = (int)(t_begin * kDecWarps) + warp;  // logical block of this warp in tile `it`
+  for (int it = 0; it < ntiles; ++it, j += kDecWarps) {
     const int s = it % kStages;
     if (ok) ok = tc::mbar_wait(full0 + 8 * s, (it / kStages) & 1, p.err, 33);
-    const int64_t j = (t_begin + it) * kDecWarps + warp;
-    if (ok && j < p.nlb) {
-      const uint8_t* sb = smem + s * kStageBytes;
-      const uint4* kb4 = reinterpret_cast<const uint4*>(sb + warp * kBlkBytes) + lane * 3;
-      const uint4* vb4 = reinterpret_cast<const uint4*>(sb + kOffV + warp * kBlkBytes) + lane * 3;
-      const float4* km4 =
-          reinterpret_cast<const float4*>(sb + kOffKmm + warp * kMmBlkBytes) + g * 2;
-      const float4* vm4 =
-          reinterpret_cast<const float4*>(sb + kOffVmm + warp * kMmBlkBytes) + g * 2;
+    if (ok && j < nlb32) {
+      const uint8_t* sb = smem + s * kStageBytes + warp * kRecBytes;
+      const uint4* kb4 = reinterpret_cast<const uint4*>(sb) + lane * 3;
+      const uint4* vb4 = reinterpret_cast<const uint4*>(sb + 4 * kRecV) + lane * 3;
+      const float4* km4 = reinterpret_cast<const float4*>(sb + 4 * kRecKmm) + g * 2;
+      const float4* vm4 = reinterpret_cast<const float4*>(sb + 4 * kRecVmm) + g * 2;
       // live slots of this block: u in [lo_live, hi_live)
-      const int64_t base = j * kBlk - p.head_off;
-      const int lo_live = base >= 0 ? 0 : (int)(-base);
-      const int64_t hl = p.len - base;
-      const int hi_live = hl >= kBlk ? kBlk : (int)hl;
+      const int base = j * kBlk - hoff;
+      const int lo_live = base >= 0 ? 0 : -base;
+      const int hl = len32 - base;
+      const int hi_live = hl >= kBlk ? kBlk : hl;
       // ---- scores: this lane's slots u = g + 8e, e = 2*mb + h
       float s2[4], vsv[4], vmn[4];
       {
@@ -793,20 +787,11 @@ int grow(ft_kv3* c, int64_t need, cudaStream_t s) {
   if (ncap < need + kBlk) ncap = need + kBlk;  // room for the head offset
   ncap = round_up(ncap, kBlk);
   const int64_t rows = c->batch * c->kv_heads, nbc = c->cap / kBlk, nnbc = ncap / kBlk;
-  uint32_t* kc = nullptr;
-  uint32_t* vc = nullptr;
-  float2 *kmm = nullptr, *vmm = nullptr;
-  cudaError_t e = cudaMalloc(&kc, (size_t)(rows * ncap * kRec));
-  if (e == cudaSuccess) e = cudaMalloc(&vc, (size_t)(rows * ncap * kRec));
-  if (e == cudaSuccess) e = cudaMalloc(&kmm, (size_t)(rows * ncap * 8));
-  if (e == cudaSuccess) e = cudaMalloc(&vmm, (size_t)(rows * ncap * 8));
-  if (e == cudaSuccess) e = cudaMemsetAsync(kc, 0, (size_t)(rows * ncap * kRec), s);
-  if (e == cudaSuccess) e = cudaMemsetAsync(vc, 0, (size_t)(rows * ncap * kRec), s);
+  uint32_t* blocks = nullptr;
+  cudaError_t e = cudaMalloc(&blocks, (size_t)(rows * nnbc) * kRecBytes);
+  if (e == cudaSuccess) e = cudaMemsetAsync(blocks, 0, (size_t)(rows * nnbc) * kRecBytes, s);
   if (e != cudaSuccess) {
-    cudaFree(kc);
-    cudaFree(vc);
-    cudaFree(kmm);
-    cudaFree(vmm);
+    cudaFree(blocks);
     return fail(e == cudaErrorMemoryAllocation ? FT_ERR_OOM : FT_ERR_GPU,
                 "3-bit KV cache growth to %lld slots failed: %s", (long long)ncap,
                 cudaGetErrorString(e));
@@ -816,31 +801,16 @@ int grow(ft_kv3* c, int64_t need, cudaStream_t s) {
   // runs of physical blocks: [hb, hb + n1) then [0, nlb - n1)
   const int64_t n1 = nlb < nbc - hb ? nlb : nbc - hb;
   const int64_t runs[2][3] = {{hb, 0, n1}, {0, n1, nlb - n1}};  // src block, dst block, count
-  const size_t kb = (size_t)kBlkBytes, mb = (size_t)kMmBlkBytes;
+  const size_t rb = (size_t)kRecBytes;
   for (const auto& run : runs) {
     if (run[2] <= 0) continue;
-    FT_CUDA(cudaMemcpy2DAsync(reinterpret_cast<uint8_t*>(kc) + run[1] * kb, nnbc * kb,
-                              reinterpret_cast<uint8_t*>(c->kc) + run[0] * kb, nbc * kb,
-                              run[2] * kb, rows, cudaMemcpyDeviceToDevice, s));
-    FT_CUDA(cudaMemcpy2DAsync(reinterpret_cast<uint8_t*>(vc) + run[1] * kb, nnbc * kb,
-                              reinterpret_cast<uint8_t*>(c->vc) + run[0] * kb, nbc * kb,
-                              run[2] * kb, rows, cudaMemcpyDeviceToDevice, s));
-    FT_CUDA(cudaMemcpy2DAsync(reinterpret_cast<uint8_t*>(kmm) + run[1] * mb, nnbc * mb,
-                              reinterpret_cast<uint8_t*>(c->kmm) + run[0] * mb, nbc * mb,
-                              run[2] * mb, rows, cudaMemcpyDeviceToDevice, s));
-    FT_CUDA(cudaMemcpy2DAsync(reinterpret_cast<uint8_t*>(vmm) + run[1] * mb, nnbc * mb,
-                              reinterpret_cast<uint8_t*>(c->vmm) + run[0] * mb, nbc * mb,
-                              run[2] * mb, rows, cudaMemcpyDeviceToDevice, s));
+    FT_CUDA(cudaMemcpy2DAsync(reinterpret_cast<uint8_t*>(blocks) + run[1] * rb, nnbc * rb,
+                              reinterpret_cast<uint8_t*>(c->blocks) + run[0] * rb, nbc * rb,
+                              run[2] * rb, rows, cudaMemcpyDeviceToDevice, s));
   }
   FT_CUDA(cudaStreamSynchronize(s));
-  cudaFree(c->kc);
-  cudaFree(c->vc);
-  cudaFree(c->kmm);
-  cudaFree(c->vmm);
-  c->kc = kc;
-  c->vc = vc;
-  c->kmm = kmm;
-  c->vmm = vmm;
+  cudaFree(c->blocks);
+  c->blocks = blocks;
   c->cap = ncap;
   c->head = c->head % kBlk;
   return FT_OK;
@@ -880,10 +850,7 @@ int append_common(ft_kv3* c, int64_t n_pos, const AppendParams& proto, bool pack
   p.cap = c->cap;
   p.nbc = c->cap / kBlk;
   p.s0 = (c->head + c->len) % c->cap;
-  p.kc = c->kc;
-  p.vc = c->vc;
-  p.kmm = c->kmm;
-  p.vmm = c->vmm;
+  p.blocks = c->blocks;
   const int64_t nblk = (p.s0 % kBlk + n_pos + kBlk - 1) / kBlk;
   // a block is touched by one CTA only: the new slots never wrap onto a block
   // that an earlier CTA of this launch also writes
@@ -907,10 +874,7 @@ RangeParams range_params(const ft_kv3* c, int64_t start, int64_t n) {
   p.head = c->head;
   p.start = start;
   p.n = n;
-  p.kc = c->kc;
-  p.vc = c->vc;
-  p.kmm = c->kmm;
-  p.vmm = c->vmm;
+  p.blocks = c->blocks;
   return p;
 }
 
@@ -933,20 +897,13 @@ int ft_kv3_create(ft_ctx* ctx, int64_t batch, int64_t kv_heads, int64_t head_dim
   c->batch = batch;
   c->kv_heads = kv_heads;
   c->cap = round_up(max_seq, kBlk);
-  const size_t slots = (size_t)(batch * kv_heads * c->cap);
-  cudaError_t e = cudaMalloc(&c->kc, slots * kRec);
-  if (e == cudaSuccess) e = cudaMalloc(&c->vc, slots * kRec);
-  if (e == cudaSuccess) e = cudaMalloc(&c->kmm, slots * 8);
-  if (e == cudaSuccess) e = cudaMalloc(&c->vmm, slots * 8);
+  const size_t recs = (size_t)(batch * kv_heads * (c->cap / kBlk));
+  cudaError_t e = cudaMalloc(&c->blocks, recs * kRecBytes);
   // blocks start zeroed (the decode reads whole blocks; slots outside the
   // live range get zero weight whatever they hold)
-  if (e == cudaSuccess) e = cudaMemset(c->kc, 0, slots * kRec);
-  if (e == cudaSuccess) e = cudaMemset(c->vc, 0, slots * kRec);
+  if (e == cudaSuccess) e = cudaMemset(c->blocks, 0, recs * kRecBytes);
   if (e != cudaSuccess) {
-    cudaFree(c->kc);
-    cudaFree(c->vc);
-    cudaFree(c->kmm);
-    cudaFree(c->vmm);
+    cudaFree(c->blocks);
     delete c;
     return fail(e == cudaErrorMemoryAllocation ? FT_ERR_OOM : FT_ERR_GPU,
                 "3-bit KV cache allocation failed: %s", cudaGetErrorString(e));
@@ -959,10 +916,7 @@ int ft_kv3_destroy(ft_kv3* c) {
   if (!c) return FT_OK;
   DeviceScope scope(c->device);
   cudaDeviceSynchronize();
-  cudaFree(c->kc);
-  cudaFree(c->vc);
-  cudaFree(c->kmm);
-  cudaFree(c->vmm);
+  cudaFree(c->blocks);
   if (c->part.ptr) cudaFree(c->part.ptr);
   delete c;
   return FT_OK;
@@ -1064,6 +1018,8 @@ int ft_flash_decode_3bit(ft_ctx* ctx, ft_kv3* c, const float* q_dev, int64_t q_h
            "q_heads (%lld) must be a multiple of kv_heads (%lld)", (long long)q_heads,
            (long long)c->kv_heads);
   FT_CHECK(c->len > 0, FT_ERR_SHAPE, "flash decode over an empty cache");
+  FT_CHECK(c->len + kBlk < (int64_t)INT32_MAX - 64, FT_ERR_UNSUPPORTED,
+           "cache too long for the decode's 32-bit slot arithmetic");
   DeviceScope scope(c->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   DecodeParams p{};
@@ -1079,10 +1035,7 @@ int ft_flash_decode_3bit(ft_ctx* ctx, ft_kv3* c, const float* q_dev, int64_t q_h
   p.nlb = (p.head_off + c->len + kBlk - 1) / kBlk;
   const float sc = scale > 0.0f ? scale : 1.0f / sqrtf((float)kD);
   p.qk_log2 = sc * 1.4426950408889634f;
-  p.kc = c->kc;
-  p.vc = c->vc;
-  p.kmm = c->kmm;
-  p.vmm = c->vmm;
+  p.blocks = c->blocks;
   p.err = ctx->err_flag;
   // split choice: minimise waves x (tiles per CTA + per-CTA overhead); at most
   // 2^15 tiles (2^20 slots, 2^18 per warp) per CTA keeps every int32 digit sum
