@@ -375,13 +375,6 @@ __device__ __forceinline__ float small_int_to_float(int d) {
   return __int_as_float(0x4B400000 + d) - 12582912.0f;
 }
 
-// exact int32 digit sums -> float: sum_j 256^j d_j (any magnitude)
-__device__ __forceinline__ float digits4(int d0, int d1, int d2, int d3) {
-  const long long v = (long long)d0 + ((long long)d1 << 8) + ((long long)d2 << 16) +
-                      ((long long)d3 << 24);
-  return (float)v;
-}
-
 __global__ void __launch_bounds__((kDecWarps + 1) * 32, FT_KV_MIN_BLOCKS)
     kv3_decode_kernel(const __grid_constant__ DecodeParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -526,8 +519,10 @@ __global__ void __launch_bounds__((kDecWarps + 1) * 32, FT_KV_MIN_BLOCKS)
     for (int mb = 0; mb < 8; ++mb)
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        const float v =
-            digits4(pv[mb][0][2 * h], pv[mb][0][2 * h + 1], pv[mb][1][2 * h], pv[mb][1][2 * h + 1]);
+        // sum_j 256^j d_j in fp32 (relative error a few 2^-24)
+        const float v = fmaf(fmaf(fmaf((float)pv[mb][1][2 * h + 1], 256.0f, (float)pv[mb][1][2 * h]),
+                                  256.0f, (float)pv[mb][0][2 * h + 1]),
+                             256.0f, (float)pv[mb][0][2 * h]);
         float* o = my_o + 16 * mb + g + 8 * h;
         *o = fmaf(v, inv, *o) * alpha;
       }
@@ -559,15 +554,22 @@ __global__ void __launch_bounds__((kDecWarps + 1) * 32, FT_KV_MIN_BLOCKS)
       // ---- scores: this lane's slots u = g + 8e, e = 2*mb + h
       float s2[4], vsv[4], vmn[4];
       {
-        const uint4 k0 = kb4[0], k1 = kb4[1], k2 = kb4[2];
-        // triple of slot e: (kw0[e], kw1[e], kw2[e])
-        const uint32_t kw0[4] = {k0.x, k0.w, k1.z, k2.y};
-        const uint32_t kw1[4] = {k0.y, k1.x, k1.w, k2.z};
-        const uint32_t kw2[4] = {k0.z, k1.y, k2.x, k2.w};
 #pragma unroll
         for (int mb = 0; mb < 2; ++mb) {
           int acc[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
-          const int ea = 2 * mb, eb = 2 * mb + 1;  // rows g, g+8
+          // triples of slots e = 2mb (row g) and 2mb + 1 (row g + 8): words 6mb .. 6mb+5
+          uint32_t kw0[2], kw1[2], kw2[2];
+          const uint32_t* kwp = reinterpret_cast<const uint32_t*>(kb4) + 6 * mb;
+          if (mb == 0) {
+            const uint4 x = *reinterpret_cast<const uint4*>(kwp);
+            const uint2 y = *reinterpret_cast<const uint2*>(kwp + 4);
+            kw0[0] = x.x; kw1[0] = x.y; kw2[0] = x.z; kw0[1] = x.w; kw1[1] = y.x; kw2[1] = y.y;
+          } else {
+            const uint2 x = *reinterpret_cast<const uint2*>(kwp);
+            const uint4 y = *reinterpret_cast<const uint4*>(kwp + 2);
+            kw0[0] = x.x; kw1[0] = x.y; kw2[0] = y.x; kw0[1] = y.y; kw1[1] = y.z; kw2[1] = y.w;
+          }
+          const int ea = 0, eb = 1;
           // k-step ks covers quads 2ks (a0, a1) and 2ks + 1 (a2, a3)
 #define FT_KSTEP(KS)                                                                      \
   {                                                                                       \
@@ -670,12 +672,25 @@ __global__ void __launch_bounds__((kDecWarps + 1) * 32, FT_KV_MIN_BLOCKS)
         bw[nb][1] = src[r + 4];
       }
       {
-        const uint4 v0 = vb4[0], v1 = vb4[1], v2 = vb4[2];
-        const uint32_t vw0[4] = {v0.x, v0.w, v1.z, v2.y};
-        const uint32_t vw1[4] = {v0.y, v1.x, v1.w, v2.z};
-        const uint32_t vw2[4] = {v0.z, v1.y, v2.x, v2.w};
 #pragma unroll
         for (int m = 0; m < 4; ++m) {
+          // triple m: words 3m .. 3m+2, loaded in pairs of triples (uint4 + uint2
+          // for m = 0, 1; uint2 + uint4 for m = 2, 3)
+          const uint32_t* vwp = reinterpret_cast<const uint32_t*>(vb4) + 6 * (m >> 1);
+          uint32_t t6[6];
+          if ((m >> 1) == 0) {
+            const uint4 x = *reinterpret_cast<const uint4*>(vwp);
+            const uint2 y = *reinterpret_cast<const uint2*>(vwp + 4);
+            t6[0] = x.x; t6[1] = x.y; t6[2] = x.z; t6[3] = x.w; t6[4] = y.x; t6[5] = y.y;
+          } else {
+            const uint2 x = *reinterpret_cast<const uint2*>(vwp);
+            const uint4 y = *reinterpret_cast<const uint4*>(vwp + 2);
+            t6[0] = x.x; t6[1] = x.y; t6[2] = y.x; t6[3] = y.y; t6[4] = y.z; t6[5] = y.w;
+          }
+          uint32_t vw0[4], vw1[4], vw2[4];
+          vw0[m] = t6[3 * (m & 1)];
+          vw1[m] = t6[3 * (m & 1) + 1];
+          vw2[m] = t6[3 * (m & 1) + 2];
           // quad Q = 2j + a: dims j = 0, 1 are rows g, g+8 of mb = 2m, j = 2, 3 of
           // mb = 2m + 1; a = 0 is k 4r..4r+3, a = 1 is k 16+4r..
           uint32_t a0 = tquad<0>(vw0[m], vw1[m], vw2[m]);
