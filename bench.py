@@ -611,6 +611,171 @@ def run_moe(args, ws, rank, local):
     return res
 
 
+# ---------------------------------------------------------- cfg5 3-bit KV --
+KV_B, KV_HQ, KV_HKV, KV_D, KV_S = 32, 32, 8, 128, 32768
+KV_CACHE_BYTES = KV_B * KV_HKV * KV_S * (48 + 48 + 8 + 8)  # codes + (min, max), K and V
+KV_IO_BYTES = 2 * KV_B * KV_HQ * KV_D * 4                  # q in, out
+KV_ALGO_BYTES = KV_CACHE_BYTES + KV_IO_BYTES
+
+
+def run_kv(args, ws, rank, local):
+    """TurboQuant 3-bit KV flash decode, B=32, Hq=32, Hkv=8,
+    d=128, context 32768 (reference scheme: per-vector min/max, 3-bit codes).
+    One step = append one position per sequence (bf16 K, V) + evict the oldest
+    (the context stays at 32768) + flash decode over the cache.  value = the
+    step's algorithmic bytes (cache read + q/out) / device time, over all ranks
+    (replicas: each rank decodes its own batch)."""
+    import torch
+    import torch.distributed as dist
+
+    from ferrisres_b200 import _lib, kv
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if ws > 1 and not dist.is_initialized():
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    cache = kv.Kv3Cache(KV_B, KV_HKV, KV_S + 64, device=local)
+    gen = torch.Generator(device=device).manual_seed(5 + rank)
+    chunk = 4096
+    for _ in range(KV_S // chunk):
+        kk = torch.randn((KV_B, chunk, KV_HKV, KV_D), device=device, generator=gen).to(torch.bfloat16)
+        vv = torch.randn((KV_B, chunk, KV_HKV, KV_D), device=device, generator=gen).to(torch.bfloat16)
+        cache.append(kk, vv)
+        del kk, vv
+    q = torch.randn((KV_B, KV_HQ, KV_D), device=device, generator=gen)
+    out = torch.empty_like(q)
+    k1 = torch.randn((KV_B, 1, KV_HKV, KV_D), device=device, generator=gen).to(torch.bfloat16)
+    v1 = torch.randn((KV_B, 1, KV_HKV, KV_D), device=device, generator=gen).to(torch.bfloat16)
+    stream = torch.cuda.Stream(device=device)
+
+    def step():
+        cache.append(k1, v1, stream=stream)
+        cache.evict_front(1)
+        cache.flash_decode(q, out=out, stream=stream)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    stream.synchronize()
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+    def timed(fn, n):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(n):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / 1e3], device=device, dtype=torch.float64)
+        if ws > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    launches0 = _lib.lib().ft_launch_counter()
+    sampler = ClockSampler(local)
+    sampler.start()
+    sec = timed(step, args.steps)
+    clocks = sampler.stop()
+    gpu_launches = _lib.lib().ft_launch_counter() - launches0
+    # the dominant kernel alone (decode + split combine), for the roofline
+    n_dec = max(5, min(args.steps, 50))
+    dec_sec = timed(lambda: cache.flash_decode(q, out=out, stream=stream), n_dec) / n_dec
+    step_s = sec / args.steps
+    value = ws * KV_ALGO_BYTES / step_s / 1e9
+
+    # end to end through the public API with host buffers: q and the new K/V
+    # from pinned host memory, the output read back every step
+    qh = torch.empty_like(q, device="cpu").pin_memory()
+    qh.copy_(q.cpu())
+    kh = torch.empty_like(k1, device="cpu").pin_memory()
+    kh.copy_(k1.cpu())
+    oh = torch.empty_like(out, device="cpu").pin_memory()
+    qd, kd, vd = torch.empty_like(q), torch.empty_like(k1), torch.empty_like(v1)
+    n_e2e = max(3, min(args.steps, 50))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(n_e2e):
+            qd.copy_(qh, non_blocking=True)
+            kd.copy_(kh, non_blocking=True)
+            vd.copy_(kh, non_blocking=True)
+            cache.append(kd, vd, stream=stream)
+            cache.evict_front(1)
+            cache.flash_decode(qd, out=out, stream=stream)
+            oh.copy_(out, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / 1e3 / n_e2e], device=device, dtype=torch.float64)
+    if ws > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_value = ws * KV_ALGO_BYTES / float(t.item()) / 1e9
+    cache.ctx.check()
+
+    peak, peak_kind = load_peaks()
+    traffic = load_traffic().get("kv_cfg5", {}).get("dram_bytes_per_launch")
+    dec_gbs = KV_ALGO_BYTES / dec_sec / 1e9
+    res = {
+        "metric": "3-bit KV flash-decode HBM GB/s", "value": round(value, 2), "unit": "GB/s",
+        "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8 codes / f32",
+        "data": "synthetic (K, V ~ N(0,1) bf16 quantised to 3 bits; q ~ N(0,1))",
+        "config": {"workload": "cfg5 3-bit KV flash decode: B=32, Hq=32, Hkv=8, d=128, ctx 32768, "
+                               "reference TurboQuantKVCache scheme (min/max per 128-vector)",
+                   "step": "append 1 position + evict oldest + decode",
+                   "l2": f"cache {KV_CACHE_BYTES / 2**20:.0f} MiB > L2",
+                   "parallelism": f"replicas x{ws}",
+                   "decode_tokens_per_s": round(ws * KV_B / step_s, 1)},
+        "roofline": {"bound": "hbm", "achieved": round(dec_gbs, 2), "peak": peak, "unit": "GB/s",
+                     "frac": round(dec_gbs / peak, 4), "peak_source": peak_kind,
+                     "traffic": traffic, "kernel": "kv3_decode_kernel (+ kv3_combine_kernel)",
+                     "algorithmic_bytes_per_launch": KV_ALGO_BYTES,
+                     "note": "112 B per (sequence, position, kv head) + q/out; decode launch "
+                             "timed alone with CUDA events"},
+        "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
+                "h2d_bytes_per_step": q.numel() * 4 + 2 * k1.numel() * 2,
+                "d2h_bytes_per_step": out.numel() * 4, "steps": n_e2e,
+                "api": "Kv3Cache.append + flash_decode (ft_kv3_append, ft_flash_decode_3bit)"},
+        "gpu_launches": int(gpu_launches),
+        "clocks": clocks,
+    }
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = kv_cpu_baseline(args.cpu_seconds)
+    cache.close()
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return res
+
+
+def kv_cpu_baseline(seconds):
+    """Oracle restatement of get_range dequant + flash_decode_ref with GQA, on all host
+    cores, over a bounded sample: one sequence (of 32) at the full 32768 context."""
+    from oracle import oracle as fo
+    rng = np.random.default_rng(0)
+    S = KV_S
+    kc = rng.integers(0, 256, size=(1, S, KV_HKV * 48), dtype=np.uint8)
+    vc = rng.integers(0, 256, size=(1, S, KV_HKV * 48), dtype=np.uint8)
+    mn = rng.standard_normal((1, S, KV_HKV, 1)).astype(np.float32) - 2.5
+    km = np.concatenate([mn, mn + 5.0], axis=-1).astype(np.float32)
+    vm = km.copy()
+    q = rng.standard_normal((1, KV_HQ, KV_D)).astype(np.float32)
+    threads = fo.num_threads(0)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        fo.flash_decode_3bit(q, kc, km, vc, vm, 1, S, KV_HQ, KV_HKV, KV_D, threads)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds and n >= 3:
+            break
+    per_seq = KV_ALGO_BYTES / KV_B
+    return {"value": round(n * per_seq / el / 1e9, 3), "unit": "GB/s", "cores": threads,
+            "kind": "port",
+            "sample": f"{n} decodes of 1 sequence x 32 q heads over 32768 positions in {el:.1f} s "
+                      f"(get_range dequant + flash_decode_ref, parallel over heads)"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -620,7 +785,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--group", type=int, default=16, help="GEMVs per launch (1..64)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--workload", choices=["gemv", "gemm_cfg2", "sparse_cfg3", "moe_cfg4"], default="gemv",
+    ap.add_argument("--workload", choices=["gemv", "gemm_cfg2", "sparse_cfg3", "moe_cfg4", "kv_cfg5"],
+                    default="gemv",
                     help="gemv = the headline cfg0 line; gemm_cfg2 = the int8 prefill GEMM")
     args = ap.parse_args()
     ws, rank, local = dist_env()
@@ -632,6 +798,8 @@ def main():
         res = run_sparse(args, ws, rank, local)
     elif args.workload == "moe_cfg4" and args.impl == "ours":
         res = run_moe(args, ws, rank, local)
+    elif args.workload == "kv_cfg5" and args.impl == "ours":
+        res = run_kv(args, ws, rank, local)
     elif args.impl == "reference":
         res = run_reference(args, ws, rank)
     else:
