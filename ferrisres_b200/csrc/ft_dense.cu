@@ -11,23 +11,22 @@ namespace {
 template <bool kU32Src>
 __global__ void repack_kernel(const void* __restrict__ src, int64_t rows, int64_t cols,
                               int64_t n_chunks, int64_t total_words, uint32_t* __restrict__ dst) {
+  // one thread per output word; block = 1024 words = [m-block][lane][word ks]
   int64_t gw = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (gw >= total_words) return;
-  int64_t block = gw >> 10;  // 1024 words per 4096-byte block
-  int within = (int)(gw & 1023);
-  int half = within >> 9;
-  int rem = within & 511;
-  int row = rem >> 2, w = rem & 3;
+  int64_t block = gw >> 10;
+  const int within = (int)(gw & 1023);
+  const int mb = within >> 7, lane = (within >> 2) & 31, ks = within & 3;
+  const int g = lane >> 2, r = lane & 3;
   int64_t tile = block / n_chunks, chunk = block % n_chunks;
-  int64_t R = tile * kTileRows + row;
-  int64_t base = chunk * kChunkK + half * 64 + w * 16;
-  uint32_t out = 0;
   int64_t cp = (cols + 15) >> 4;
+  uint32_t out = 0;
 #pragma unroll
-  for (int q = 0; q < 4; ++q)
+  for (int j = 0; j < 4; ++j)
 #pragma unroll
     for (int b = 0; b < 4; ++b) {
-      int64_t k = base + 4 * q + b;
+      const int64_t R = tile * kTileRows + 16 * mb + g + 8 * (j & 1);
+      const int64_t k = chunk * kChunkK + 32 * ks + 16 * (j >> 1) + 4 * r + b;
       uint32_t code = 1u;
       if (R < rows && k < cols) {
         if (kU32Src) {
@@ -40,7 +39,7 @@ __global__ void repack_kernel(const void* __restrict__ src, int64_t rows, int64_
         }
         if (code == 3u) code = 1u;  // 0b11 decodes to 0 in the reference
       }
-      out |= code << (8 * b + 2 * q);
+      out |= code << (8 * b + 2 * j);
     }
   dst[gw] = out;
 }
@@ -133,159 +132,6 @@ __global__ void quantize_i8_kernel(const void* __restrict__ x, bool bf16, int64_
   if (threadIdx.x == 0) sx[s] = __fdiv_rn(amax, 127.0f);
 }
 
-// ------------------------------------------------- split-K CUDA-core GEMM --
-// grid (n_tiles, ksplit, ceil(seq/TOK)); 128 threads, thread = row of tile.
-// Each CTA covers chunks [c0, c1) and TOK tokens; partial sums go to
-// part[ks][s][row] (or straight to y when ksplit == 1).
-constexpr int kTok = 4;
-
-template <int TOK>
-__global__ void __launch_bounds__(128) dense_f32_kernel(
-    const uint8_t* __restrict__ codes, const float* __restrict__ rscale, int64_t rows,
-    int64_t cols, int64_t n_chunks, int chunks_per_split, int64_t seq,
-    const float* __restrict__ x, float* __restrict__ out, int64_t rows_pad, bool direct) {
-  __shared__ float xs[TOK][kChunkK];
-  const int r = threadIdx.x;
-  const int64_t tile = blockIdx.x;
-  const int ks = blockIdx.y;
-  const int64_t s0 = (int64_t)blockIdx.z * TOK;
-  const int64_t c0 = (int64_t)ks * chunks_per_split;
-  int64_t c1 = c0 + chunks_per_split;
-  if (c1 > n_chunks) c1 = n_chunks;
-  float acc[TOK];
-#pragma unroll
-  for (int t = 0; t < TOK; ++t) acc[t] = 0.0f;
-  for (int64_t c = c0; c < c1; ++c) {
-    __syncthreads();
-#pragma unroll
-    for (int t = 0; t < TOK; ++t) {
-      int64_t s = s0 + t, k = c * kChunkK + r;
-      xs[t][r] = (s < seq && k < cols) ? x[s * cols + k] : 0.0f;
-    }
-    __syncthreads();
-    const uint8_t* blk = codes + (tile * n_chunks + c) * kBlockBytes;
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      uint4 v = *reinterpret_cast<const uint4*>(blk + h * 2048 + r * 16);
-      uint32_t wv[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-      for (int w = 0; w < 4; ++w) {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint32_t u = (wv[w] >> (2 * q)) & 0x03030303u;
-#pragma unroll
-          for (int b = 0; b < 4; ++b) {
-            float wt = (float)((u >> (8 * b)) & 0xFFu) - 1.0f;
-            int kk = h * 64 + w * 16 + 4 * q + b;
-#pragma unroll
-            for (int t = 0; t < TOK; ++t) acc[t] = fmaf(wt, xs[t][kk], acc[t]);
-          }
-        }
-      }
-    }
-  }
-  const int64_t R = tile * kTileRows + r;
-#pragma unroll
-  for (int t = 0; t < TOK; ++t) {
-    int64_t s = s0 + t;
-    if (s >= seq) break;
-    if (direct) {
-      if (R < rows) out[s * rows + R] = acc[t] * rscale[R];
-    } else {
-      out[((int64_t)ks * seq + s) * rows_pad + R] = acc[t];
-    }
-  }
-}
-
-__global__ void reduce_f32_kernel(const float* __restrict__ part, int ksplit, int64_t seq,
-                                  int64_t rows, int64_t rows_pad, const float* __restrict__ rscale,
-                                  float* __restrict__ y) {
-  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= seq * rows) return;
-  int64_t s = i / rows, R = i % rows;
-  float a = 0.0f;
-  for (int k = 0; k < ksplit; ++k) a += part[((int64_t)k * seq + s) * rows_pad + R];
-  y[i] = a * rscale[R];
-}
-
-// int8 activations: unsigned codes u = w+1 dotted with signed q by dp4a, the
-// chunk's sum of q subtracted once, so the int32 result is exact.
-template <int TOK>
-__global__ void __launch_bounds__(128) dense_i8_kernel(
-    const uint8_t* __restrict__ codes, int64_t rows, int64_t cols, int64_t n_chunks,
-    int chunks_per_split, int64_t seq, const int8_t* __restrict__ q, int32_t* __restrict__ part,
-    int64_t rows_pad) {
-  __shared__ int32_t qs[TOK][kChunkK / 4];
-  __shared__ int32_t qsum[TOK];
-  const int r = threadIdx.x;
-  const int64_t tile = blockIdx.x;
-  const int ks = blockIdx.y;
-  const int64_t s0 = (int64_t)blockIdx.z * TOK;
-  const int64_t c0 = (int64_t)ks * chunks_per_split;
-  int64_t c1 = c0 + chunks_per_split;
-  if (c1 > n_chunks) c1 = n_chunks;
-  int32_t acc[TOK];
-#pragma unroll
-  for (int t = 0; t < TOK; ++t) acc[t] = 0;
-  for (int64_t c = c0; c < c1; ++c) {
-    __syncthreads();
-    if (r < 32) {
-#pragma unroll
-      for (int t = 0; t < TOK; ++t) {
-        int64_t s = s0 + t;
-        uint32_t word = 0;
-#pragma unroll
-        for (int b = 0; b < 4; ++b) {
-          int64_t k = c * kChunkK + r * 4 + b;
-          uint32_t v = (s < seq && k < cols) ? (uint8_t)q[s * cols + k] : 0u;
-          word |= v << (8 * b);
-        }
-        qs[t][r] = (int32_t)word;
-        int sum = __dp4a((int)word, 0x01010101, 0);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        if (r == 0) qsum[t] = sum;
-      }
-    }
-    __syncthreads();
-    const uint8_t* blk = codes + (tile * n_chunks + c) * kBlockBytes;
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      uint4 v = *reinterpret_cast<const uint4*>(blk + h * 2048 + r * 16);
-      uint32_t wv[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-      for (int w = 0; w < 4; ++w)
-#pragma unroll
-        for (int qq = 0; qq < 4; ++qq) {
-          int u = (int)((wv[w] >> (2 * qq)) & 0x03030303u);
-          int widx = h * 16 + w * 4 + qq;
-#pragma unroll
-          for (int t = 0; t < TOK; ++t) acc[t] = __dp4a(u, qs[t][widx], acc[t]);
-        }
-    }
-#pragma unroll
-    for (int t = 0; t < TOK; ++t) acc[t] -= qsum[t];
-  }
-  const int64_t R = tile * kTileRows + r;
-#pragma unroll
-  for (int t = 0; t < TOK; ++t) {
-    int64_t s = s0 + t;
-    if (s >= seq) break;
-    part[((int64_t)ks * seq + s) * rows_pad + R] = acc[t];
-  }
-}
-
-__global__ void reduce_i8_kernel(const int32_t* __restrict__ part, int ksplit, int64_t seq,
-                                 int64_t rows, int64_t rows_pad, const float* __restrict__ sx,
-                                 const float* __restrict__ rscale, float* __restrict__ y) {
-  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= seq * rows) return;
-  int64_t s = i / rows, R = i % rows;
-  int32_t a = 0;
-  for (int k = 0; k < ksplit; ++k) a += part[((int64_t)k * seq + s) * rows_pad + R];
-  y[i] = __fmul_rn(__fmul_rn((float)a, sx[s]), rscale[R]);
-}
-
 // ------------------------------------------------------------ WGSL op ------
 // One warp per (token, row) over the raw u32 layout; lanes take words
 // round-robin, then a shuffle reduction; result * scales[row].
@@ -315,15 +161,6 @@ __global__ void wgsl_op_kernel(const uint32_t* __restrict__ words, const float* 
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
   if (lane == 0) y[(int64_t)s * out_rows + row] = sum * scales[row];
-}
-
-int pick_ksplit(const ft_ctx* ctx, const ft_weight* w, int64_t token_groups) {
-  int64_t ctas = w->n_tiles * token_groups;
-  int64_t target = (int64_t)ctx->num_sms * 8;
-  int64_t ks = (target + ctas - 1) / ctas;
-  if (ks > w->n_chunks) ks = w->n_chunks;
-  if (ks < 1) ks = 1;
-  return (int)ks;
 }
 
 }  // namespace
@@ -368,62 +205,6 @@ int launch_quantize_i8(const void* x, bool bf16, int64_t seq, int64_t cols, int8
                        cudaStream_t s) {
   if (seq == 0) return FT_OK;
   quantize_i8_kernel<<<(unsigned)seq, 256, 0, s>>>(x, bf16, cols, q, sx);
-  FT_LAUNCH_CHECK();
-  return FT_OK;
-}
-
-int launch_dense_f32(ft_ctx* ctx, const ft_weight* w, int64_t seq, const float* x, float* y,
-                     cudaStream_t s) {
-  if (seq == 0) return FT_OK;
-  int64_t groups = ceil_div(seq, kTok);
-  FT_CHECK(groups <= 65535, FT_ERR_UNSUPPORTED, "seq %lld too large for the CUDA-core path",
-           (long long)seq);
-  int ks = pick_ksplit(ctx, w, groups);
-  int cps = (int)ceil_div(w->n_chunks, ks);
-  ks = (int)ceil_div(w->n_chunks, cps);
-  int64_t rows_pad = w->n_tiles * kTileRows;
-  dim3 grid((unsigned)w->n_tiles, (unsigned)ks, (unsigned)groups);
-  if (ks == 1) {
-    dense_f32_kernel<kTok><<<grid, 128, 0, s>>>(w->codes, w->row_scales, w->rows, w->cols,
-                                                w->n_chunks, cps, seq, x, y, rows_pad, true);
-    FT_LAUNCH_CHECK();
-    return FT_OK;
-  }
-  size_t need = (size_t)ks * seq * rows_pad * sizeof(float);
-  int st = workspace_reserve(ctx, need, s);
-  if (st != FT_OK) return st;
-  float* part = static_cast<float*>(ctx->ws.ptr);
-  dense_f32_kernel<kTok><<<grid, 128, 0, s>>>(w->codes, w->row_scales, w->rows, w->cols,
-                                              w->n_chunks, cps, seq, x, part, rows_pad, false);
-  FT_LAUNCH_CHECK();
-  int64_t n = seq * w->rows;
-  reduce_f32_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(part, ks, seq, w->rows, rows_pad,
-                                                               w->row_scales, y);
-  FT_LAUNCH_CHECK();
-  return FT_OK;
-}
-
-int launch_dense_i8(ft_ctx* ctx, const ft_weight* w, int64_t seq, const int8_t* q,
-                    const float* sx, float* y, cudaStream_t s) {
-  if (seq == 0) return FT_OK;
-  int64_t groups = ceil_div(seq, kTok);
-  FT_CHECK(groups <= 65535, FT_ERR_UNSUPPORTED, "seq %lld too large for the CUDA-core path",
-           (long long)seq);
-  int ks = pick_ksplit(ctx, w, groups);
-  int cps = (int)ceil_div(w->n_chunks, ks);
-  ks = (int)ceil_div(w->n_chunks, cps);
-  int64_t rows_pad = w->n_tiles * kTileRows;
-  size_t need = (size_t)ks * seq * rows_pad * sizeof(int32_t);
-  int st = workspace_reserve(ctx, need, s);
-  if (st != FT_OK) return st;
-  int32_t* part = static_cast<int32_t*>(ctx->ws.ptr);
-  dim3 grid((unsigned)w->n_tiles, (unsigned)ks, (unsigned)groups);
-  dense_i8_kernel<kTok><<<grid, 128, 0, s>>>(w->codes, w->rows, w->cols, w->n_chunks, cps, seq, q,
-                                             part, rows_pad);
-  FT_LAUNCH_CHECK();
-  int64_t n = seq * w->rows;
-  reduce_i8_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(part, ks, seq, w->rows, rows_pad, sx,
-                                                              w->row_scales, y);
   FT_LAUNCH_CHECK();
   return FT_OK;
 }

@@ -1,18 +1,21 @@
 // Internal definitions shared by the translation units of libferris_ternary.so.
 //
-// Device layout of a dense ternary weight ("tiled T128"):
+// Device layout of a dense ternary weight ("tiled T128", lane-major blocks):
 //   rows are grouped into tiles of 128 output channels, K into chunks of 128
 //   codes.  Block (tile t, chunk c) is 4096 contiguous bytes at offset
-//   (t * n_chunks + c) * 4096:
-//       [half h in 0..1][row r in 0..127][16 bytes]
-//   The 16 bytes of (h, r) are four u32 words w = 0..3; word w holds the 16
-//   codes of K positions base + 0..15, base = c*128 + h*64 + w*16, arranged so
-//   that byte b, bits 2q..2q+1 hold the code of K position base + 4q + b.
-//   Shifting a word right by 2q and masking with 0x03030303 therefore yields
-//   four unsigned bytes {0,1,2} = (w+1) for K positions base+4q .. base+4q+3,
-//   in K order: the int8 operand the tensor-core path stores in TMEM.
-//   Codes: 0 -> -1, 1 -> 0, 2 -> +1 (same as the reference).  Padding rows and
-//   padding K positions hold code 1 (weight 0).
+//   (t * n_chunks + c) * 4096, arranged for the int8 MMA fragments of a warp:
+//       [m-block mb in 0..7][lane L in 0..31][word ks in 0..3]
+//   with L = 4g + r.  Word ks of lane (g, r) in m-block mb holds 4 quads
+//   j = 0..3 of 4 codes: byte b, bits 2j..2j+1 = code of
+//       row 16*mb + g + 8*(j & 1),  K position 32*ks + 16*(j >> 1) + 4*r + b.
+//   Shifting a word right by 2j and masking with 0x03030303 yields four
+//   unsigned bytes {0,1,2} = (w+1): exactly the A fragment register aj of an
+//   m16n8k32 MMA for k-step ks (a0/a1: rows g / g+8, k 4r..4r+3; a2/a3: the
+//   same rows, k 16+4r..16+4r+3), so one 128-bit load per lane feeds four
+//   MMAs.  A row's 128 codes of a chunk are spread over the 4 lanes (g, 0..3)
+//   of its m-block: 64 contiguous bytes.  Codes: 0 -> -1, 1 -> 0, 2 -> +1
+//   (same as the reference).  Padding rows and padding K positions hold code
+//   1 (weight 0).
 #pragma once
 
 #include <cuda_runtime.h>
@@ -114,10 +117,6 @@ int launch_repack_sparse_wgsl(const uint32_t* words, int64_t rows, int64_t cols,
                               cudaStream_t s);
 int launch_quantize_i8(const void* x, bool bf16, int64_t seq, int64_t cols, int8_t* q, float* sx,
                        cudaStream_t s);
-int launch_dense_f32(ft_ctx* ctx, const ft_weight* w, int64_t seq, const float* x, float* y,
-                     cudaStream_t s);
-int launch_dense_i8(ft_ctx* ctx, const ft_weight* w, int64_t seq, const int8_t* q,
-                    const float* sx, float* y, cudaStream_t s);
 // Tensor-core path (ft_tc.cu).  xkind: 0 f32, 1 bf16, 2 int8 codes (then sx
 // is the per-token scale).
 int launch_tc_matmul(ft_ctx* ctx, const ft_weight* w, int64_t seq, const void* x, int xkind,
@@ -127,6 +126,20 @@ int launch_tc_matmul(ft_ctx* ctx, const ft_weight* w, int64_t seq, const void* x
 int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t seq,
                       const void* const* xs, int xkind, const float* const* sxs, float* const* ys,
                       const int64_t* ldys, cudaStream_t s, const int64_t* seqs = nullptr);
+// Decode-shape kernel (ft_gemv.cu) over prep_b_kernel's 16-column operand.
+struct GvLaunchProblem {
+  const uint8_t* codes;
+  const float* row_scales;
+  int64_t rows, n_tiles, n_chunks;
+  const int8_t* bmat;
+  const int32_t* colsum;
+  const double* tok_scale;
+  const float* sx;
+  float* y;
+  int64_t ldy, seq;
+};
+int launch_gemv(ft_ctx* ctx, int nprob, const GvLaunchProblem* probs, int digits,
+                cudaStream_t s);
 int launch_wgsl_op(const uint32_t* words, const float* scales, const float* x, float* y,
                    uint32_t seq, uint32_t in_cols, uint32_t out_rows, cudaStream_t s);
 }  // namespace ft

@@ -72,7 +72,10 @@ constexpr int kBlkWords = kBlk * kRec / 4;  // 384
 constexpr int kBlkBytes = kBlk * kRec;   // 1536 (both K and V)
 constexpr int kMmBlkBytes = kBlk * 8;    // 256
 constexpr int kDecWarps = 4;             // compute warps = blocks per tile
-constexpr int kStages = 4;
+#ifndef FT_KV_STAGES
+#define FT_KV_STAGES 4
+#endif
+constexpr int kStages = FT_KV_STAGES;
 constexpr int kRecBytes = 2 * kBlkBytes + 2 * kMmBlkBytes;  // 3584: K | V | K min/max | V min/max
 constexpr int kRecWords = kRecBytes / 4;
 constexpr int kRecV = kBlkWords, kRecKmm = 2 * kBlkWords, kRecVmm = 2 * kBlkWords + 2 * kBlk;

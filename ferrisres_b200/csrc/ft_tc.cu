@@ -2,8 +2,8 @@
 // group of independent problems in one persistent launch.
 //
 // Formulation.  The packed 2-bit codes u = w + 1 in {0, 1, 2} are unpacked
-// in registers (one shift + one mask per 4 codes, thanks to the tiled T128
-// layout) and written to tensor memory as the 8-bit A operand (M = 128
+// in registers (one shift + one mask per 4 codes, thanks to the lane-major
+// T128 layout) and written to tensor memory as the 8-bit A operand (M = 128
 // output channels of one tile).  The activations are the signed 8-bit B
 // operand, K-major in shared memory, N = NPAD columns:
 //   * int8 mode: one column per token, the caller's int8 codes q;
@@ -25,8 +25,8 @@
 //              blocks into a 16-deep smem ring (64 KB in flight per CTA),
 //              running ahead across item boundaries.
 //   warp 5     B producer: bulk copies of the B chunks into their own ring.
-//   warps 0-3  converters: thread r reads row r's 32 bytes of the block
-//              (conflict-free: the block is [half][row][16 B]), unpacks,
+//   warps 0-3  converters: thread r reads row r's 64 bytes of the
+//              lane-major block (lanes (g, 0..3) of its m-block), unpacks,
 //              tcgen05.st into TMEM A stage s.
 //   warp 6     MMA issuer: 4 x tcgen05.mma (K = 32 each) per chunk into one of
 //              two TMEM accumulators; tcgen05.commit frees stages / signals D.
@@ -279,7 +279,7 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
     uint32_t gb = 0, gs = 0;  // weight-block and super-stage counters
     while (cs.valid(b)) {
       const int n = cs.ss_len();
-      uint32_t wv[kSK][8];
+      uint32_t wv[kSK][16];
 #pragma unroll
       for (int j = 0; j < kSK; ++j) {
         if (j < n) {
@@ -292,17 +292,16 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
             for (int i = 0; i < 5; ++i) wv[j][i] = ok ? rw[i] : 0u;
             wv[j][5] = wv[j][6] = wv[j][7] = 0u;
           } else {
-            uint4 v0 = make_uint4(0, 0, 0, 0), v1 = make_uint4(0, 0, 0, 0);
-            if (ok) {
-              const uint8_t* blk = smem_a + sa * kBlockBytes + r * 16;
-              v0 = *reinterpret_cast<const uint4*>(blk);
-              v1 = *reinterpret_cast<const uint4*>(blk + 2048);
+            // row r = 16*mb + g + 8*par: lanes (g, 0..3) of m-block mb, 64 contiguous bytes
+            const uint4* blk = reinterpret_cast<const uint4*>(smem_a + sa * kBlockBytes) +
+                               (r >> 4) * 32 + 4 * (r & 7);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const uint4 v = ok ? blk[i] : make_uint4(0, 0, 0, 0);
+              wv[j][4 * i + 0] = v.x; wv[j][4 * i + 1] = v.y;
+              wv[j][4 * i + 2] = v.z; wv[j][4 * i + 3] = v.w;
             }
-            wv[j][0] = v0.x; wv[j][1] = v0.y; wv[j][2] = v0.z; wv[j][3] = v0.w;
-            wv[j][4] = v1.x; wv[j][5] = v1.y; wv[j][6] = v1.z; wv[j][7] = v1.w;
           }
-          __syncwarp();
-          if (lane == 0) tc::mbar_arrive(tc::smem_u32(&bar_sa_empty[sa]));
           ++gb;
         }
       }
@@ -327,16 +326,29 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
                 a[gg] = s_lut[v];
               }
             } else {
+              // column 8*ks' + 4*a + i (ks = 2h + ks') = word ks of lane i, quad par + 2a
+              const int par = (r >> 3) & 1;
 #pragma unroll
-              for (int w = 0; w < 4; ++w)
+              for (int kk = 0; kk < 2; ++kk)
 #pragma unroll
-                for (int q = 0; q < 4; ++q) a[w * 4 + q] = (wv[j][h * 4 + w] >> (2 * q)) & 0x03030303u;
+                for (int aa = 0; aa < 2; ++aa)
+#pragma unroll
+                  for (int i = 0; i < 4; ++i)
+                    a[8 * kk + 4 * aa + i] =
+                        (wv[j][4 * i + 2 * h + kk] >> (2 * par + 4 * aa)) & 0x03030303u;
             }
             if (ok) tc::tmem_st_x16(tmem + lane_off + kACol0 + (s * kSK + j) * 32 + 16 * h, a);
           }
         }
       }
       tc::tmem_wait_st();
+      // Release the weight slots only now: the TMEM stores above consumed the
+      // registers the shared loads filled, so those loads have completed and
+      // the producer's next bulk copy cannot overwrite a slot still being read.
+      __syncwarp();
+      if (lane == 0)
+        for (int j = 0; j < n; ++j)
+          tc::mbar_arrive(tc::smem_u32(&bar_sa_empty[(gb - n + j) % kSA]));
       // The B super-stage is waited here too, so the MMA thread waits on one
       // barrier per super-stage.
       ok = ok && tc::mbar_wait(tc::smem_u32(&bar_sb_full[gs % kSBS]), (gs / kSBS) & 1, b.err, 18);
@@ -847,6 +859,16 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
     FT_LAUNCH_CHECK();
   }
 
+  if (ws[live[0]]->format == 0 && npad == 16) {
+    // decode shapes: the warp-level kernel streams the weights at memory pace
+    GvLaunchProblem gp[kMaxProblems];
+    for (int q = 0; q < nlive; ++q) {
+      const TqProblem& p = batch.p[q];
+      gp[q] = GvLaunchProblem{p.codes, p.row_scales, p.rows, p.n_tiles, p.n_chunks, p.bmat,
+                              p.colsum, p.tok_scale, p.sx, p.y, p.ldy, p.seq};
+    }
+    return launch_gemv(ctx, nlive, gp, D, s);
+  }
   const int64_t grid = items < grid_target ? items : grid_target;
   if (ws[live[0]]->format == 1) {
     switch (npad) {
