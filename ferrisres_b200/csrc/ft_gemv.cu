@@ -1,17 +1,22 @@
 // Decode-shape ternary matmul (GEMV and small M): y = scale * (W . x) for a
-// group of independent problems whose activations fit one 16-column operand
+// group of independent problems whose activations fit 16 operand columns
 // (fp32/bf16: <= 4 tokens as 4 base-256 digits each; int8: <= 16 tokens).
 //
 // Same exact formulation as the tensor-core engine (ft_tc.cu): the A operand
 // is the unsigned codes u = w + 1, the B operand the int8 activation columns
-// written by prep_b_kernel, int32 sums are exact, the epilogue subtracts the
+// (fp32/bf16: the signed base-256 digits of X = round(x * 2^30 / absmax(x)),
+// int8: the caller's codes), int32 sums are exact, the epilogue subtracts the
 // column sums and scales.  Here the MMAs are warp-level (mma.sync m16n8k32):
 // every lane loads its 16 bytes of a 4 KB weight block straight from global
 // memory with one coalesced 128-bit load (the lane-major block layout puts a
 // warp's 512 bytes of an m-block contiguous), unpacks each word with one shift
-// and one mask per fragment register, and issues 4 MMAs per n-block.  The
-// weight stream needs no shared memory, barriers or TMEM, so a decode GEMV
-// runs at the memory system's pace.
+// and one mask per fragment register, and issues 4 MMAs per n8 block.  The
+// weight stream needs no shared memory staging, barriers or TMEM.
+//
+// prep_b_kernel (ft_tc.cu) writes the activation operand in this kernel's
+// fragment order; the kernel is launched as its programmatic dependent, so
+// each warp starts its weight stream before waiting for the prep, then the
+// CTA copies its fragments into shared memory.
 //
 // Work: a CTA of 8 warps covers 8/S m-blocks (16 rows each) of one problem,
 // each split S ways along K (S in {1, 2, 4, 8}, chosen so the launch has
@@ -24,26 +29,33 @@ namespace {
 
 constexpr int kGvWarps = 8;
 constexpr int kGvMaxProblems = 64;
-constexpr int kNpad = 16;  // activation columns (two n8 blocks)
-constexpr int kUnroll = 4;  // weight loads in flight per lane
+#ifndef FT_GV_DEPTH
+#define FT_GV_DEPTH 6
+#endif
+#ifndef FT_GV_MIN_BLOCKS
+#define FT_GV_MIN_BLOCKS 5
+#endif
+constexpr int kDepth = FT_GV_DEPTH;  // weight chunks in flight per warp (cp.async ring)
+constexpr int kRingBytes = kGvWarps * kDepth * 512;
 
 struct GvProblem {
   const uint4* codes;  // lane-major blocks, 256 uint4 per (tile, chunk)
   const float* row_scales;
   int64_t rows, n_tiles, n_chunks;
-  const int8_t* bmat;      // [n_chunks][kNpad * 128] (prep_b_kernel, one pass)
-  const int32_t* colsum;   // [kNpad]
-  const double* tok_scale; // fp32 mode: absmax * 2^-30 per token
-  const float* sx;         // int8 mode: per-token scale
+  const uint4* bfrag;       // [n_chunks][2][32 lanes][2 uint4] (prep_b_kernel)
+  const int32_t* colsum;    // [16]
+  const double* tok_scale;  // fp32 mode: absmax * 2^-30 per token
+  const float* sx;          // int8 mode: per-token scale
   float* y;
   int64_t ldy, seq;
-  int64_t cta_begin;       // first CTA of this problem
-  int ksplit, cps, nb;     // K splits, chunks per split, live n8 blocks (1 or 2)
+  int64_t cta_begin;  // first CTA of this problem
+  int ksplit, cps;    // K splits, chunks per split
 };
 
 struct GvBatch {
   int nprob;
-  int digits;
+  int digits;  // 4 (fp32/bf16) or 1 (int8)
+  int nb;      // n8 blocks of B (1 or 2)
   GvProblem p[kGvMaxProblems];
 };
 
@@ -56,42 +68,49 @@ __device__ __forceinline__ void mma_u8s8(int (&c)[4], uint32_t a0, uint32_t a1, 
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ uint4 ldg_stream(const uint4* p) {
-  uint4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
-  return v;
+// 16-byte asynchronous copy global -> shared (bypasses L1 and registers)
+__device__ __forceinline__ void cp_async16(const void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                   (uint32_t)__cvta_generic_to_shared(smem_dst)),
+               "l"(gsrc)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// the 4 MMAs of one 128-K chunk for n8 blocks 0 .. NB-1
-template <int NB>
-__device__ __forceinline__ void chunk_mma(int (&acc)[2][4], const uint4 w, const int8_t* bchunk,
-                                          int g, int r) {
+// the 4 k-steps of one 128-K chunk against the 8 fragment words of one n8 block
+__device__ __forceinline__ void chunk_mma(int (&acc)[4], const uint4 w, const uint4 b0,
+                                          const uint4 b1) {
   const uint32_t wk[4] = {w.x, w.y, w.z, w.w};
+  const uint32_t bw[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
   for (int ks = 0; ks < 4; ++ks) {
     const uint32_t a0 = wk[ks] & 0x03030303u;
     const uint32_t a1 = (wk[ks] >> 2) & 0x03030303u;
     const uint32_t a2 = (wk[ks] >> 4) & 0x03030303u;
     const uint32_t a3 = (wk[ks] >> 6) & 0x03030303u;
-#pragma unroll
-    for (int nb = 0; nb < NB; ++nb) {
-      // B column n = g of n8 block nb; k 4r..4r+3 (k16 group 2ks) and 16+4r.. (2ks+1)
-      const int8_t* bp = bchunk + ((2 * ks) * (kNpad / 8) + nb) * 128 + g * 16 + 4 * r;
-      const uint32_t b0 = __ldg(reinterpret_cast<const uint32_t*>(bp));
-      const uint32_t b1 = __ldg(reinterpret_cast<const uint32_t*>(bp + (kNpad / 8) * 128));
-      mma_u8s8(acc[nb], a0, a1, a2, a3, b0, b1);
-    }
+    mma_u8s8(acc, a0, a1, a2, a3, bw[2 * ks], bw[2 * ks + 1]);
   }
 }
 
 template <int NB>
-__global__ void __launch_bounds__(kGvWarps * 32) gemv_kernel(const __grid_constant__ GvBatch b) {
+__global__ void __launch_bounds__(kGvWarps * 32, FT_GV_MIN_BLOCKS) gemv_kernel(const __grid_constant__ GvBatch b) {
+  // dynamic: [warp][kDepth][32 lanes] uint4 weight ring, then the B fragments
+  // [n_chunks][NB][32 lanes][8 words]
+  extern __shared__ __align__(16) uint4 dyn[];
+  uint32_t* frag = reinterpret_cast<uint32_t*>(dyn + kRingBytes / 16);
+  __shared__ int colsum[16];
+  __shared__ double tok_scale[4];
+
   int pi = 0;
   while (pi + 1 < b.nprob && b.p[pi + 1].cta_begin <= (int64_t)blockIdx.x) ++pi;
   const GvProblem& p = b.p[pi];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, r = lane & 3;
   const int S = p.ksplit;
   const int64_t mblock = (blockIdx.x - p.cta_begin) * (kGvWarps / S) + warp / S;
@@ -103,29 +122,59 @@ __global__ void __launch_bounds__(kGvWarps * 32) gemv_kernel(const __grid_consta
   if (c1 > p.n_chunks) c1 = p.n_chunks;
   if (!active) c1 = c0;
 
-  int acc[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+  // ---- start the weight stream: each lane copies (and later reads) only its
+  // own 16 bytes of each chunk, so the ring needs no barriers
   const uint4* wp = p.codes + (tile * p.n_chunks) * 256 + mb * 32 + lane;
-  // the first weights do not depend on the previous launch: start them before
-  // waiting for the prep kernel that writes the activation operand
-  uint4 w[kUnroll];
+  uint4* ring = dyn + warp * (kDepth * 32) + lane;
 #pragma unroll
-  for (int u = 0; u < kUnroll; ++u)
-    if (c0 + u < c1) w[u] = ldg_stream(wp + (c0 + u) * 256);
-  tc::pdl_wait();
-  for (int64_t c = c0; c < c1; c += kUnroll) {
-#pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      if (c + u < c1) {
-        const uint4 cur = w[u];
-        if (c + u + kUnroll < c1) w[u] = ldg_stream(wp + (c + u + kUnroll) * 256);
-        chunk_mma<NB>(acc, cur, p.bmat + (c + u) * (kNpad * 128), g, r);
-      }
-    }
+  for (int d = 0; d < kDepth; ++d) {
+    if (c0 + d < c1) cp_async16(ring + d * 32, wp + (c0 + d) * 256);
+    cp_async_commit();  // one group per chunk slot, empty past the range
   }
 
-  // ---- combine the K splits of each m-block in shared memory
-  __shared__ int red[kGvWarps][32][8];
+  // ---- the activation operand, column sums and token scales of the prep
+  tc::pdl_wait();
+  const int D = b.digits;
+  const int seq = (int)p.seq;
+  {
+    uint4* f4 = reinterpret_cast<uint4*>(frag);
+    const int n16 = (int)(p.n_chunks * NB * 64);  // 16-byte pieces
+    for (int i = tid; i < n16; i += blockDim.x) {
+      const int64_t chunk = i / (NB * 64);
+      const int rem = i % (NB * 64);  // (nb, lane, half)
+      cp_async16(f4 + i, p.bfrag + chunk * 128 + rem);
+    }
+    cp_async_commit();
+    if (tid < 16) colsum[tid] = p.colsum[tid];
+    if (tid < 4 && D == 4) tok_scale[tid] = p.tok_scale[tid];
+    // the weight ring's groups are older, so waiting for all is waiting for this one too
+    cp_async_wait<0>();
+  }
+  __syncthreads();
+
+  // ---- the weight stream against the fragments
+  int acc[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+  const uint4* fq = reinterpret_cast<const uint4*>(frag);
+  int slot = 0;
+  for (int64_t ch = c0; ch < c1; ++ch) {
+    cp_async_wait<kDepth - 1>();  // this lane's copy of chunk ch has landed
+    const uint4 cur = ring[slot * 32];
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb) {
+      const uint4* f = fq + ((ch * NB + nb) * 32 + lane) * 2;
+      chunk_mma(acc[nb], cur, f[0], f[1]);
+    }
+    // the MMAs consumed `cur`, so the slot can be refilled
+    if (ch + kDepth < c1) cp_async16(ring + slot * 32, wp + (ch + kDepth) * 256);
+    cp_async_commit();
+    slot = slot + 1 == kDepth ? 0 : slot + 1;
+  }
+  cp_async_wait<0>();
+  __syncthreads();  // the ring is reused for the split sums below
+
+  // ---- combine the K splits of each m-block
   if (S > 1) {
+    int(*red)[32][8] = reinterpret_cast<int(*)[32][8]>(dyn);  // [warp][lane][8], in the ring
 #pragma unroll
     for (int nb = 0; nb < 2; ++nb)
 #pragma unroll
@@ -142,15 +191,15 @@ __global__ void __launch_bounds__(kGvWarps * 32) gemv_kernel(const __grid_consta
 
   // ---- epilogue: acc[nb][0..1] = row g, columns 8nb + 2r, +1; [2..3] = row g + 8
   const int64_t R0 = tile * kTileRows + 16 * mb + g;
-  if (b.digits == 1) {
+  if (D == 1) {
 #pragma unroll
     for (int nb = 0; nb < NB; ++nb)
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int n = 8 * nb + 2 * r + (i & 1);
         const int64_t R = R0 + 8 * (i >> 1);
-        if (n < p.seq && R < p.rows) {
-          const int32_t a = acc[nb][i] - p.colsum[n];
+        if (n < seq && R < p.rows) {
+          const int32_t a = acc[nb][i] - colsum[n];
           p.y[n * p.ldy + R] = __fmul_rn(__fmul_rn((float)a, p.sx[n]), p.row_scales[R]);
         }
       }
@@ -165,18 +214,17 @@ __global__ void __launch_bounds__(kGvWarps * 32) gemv_kernel(const __grid_consta
       if ((r & 1) == 0) {
         const int t = 2 * nb + (r >> 1);
         const int n0 = 4 * t;
-        if (t < p.seq) {
+        if (t < seq) {
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             const int64_t R = R0 + 8 * h;
             if (R >= p.rows) continue;
-            const long long d0 = acc[nb][2 * h] - p.colsum[n0];
-            const long long d1 = acc[nb][2 * h + 1] - p.colsum[n0 + 1];
-            const long long d2 = (h ? hi2 : hi0) - p.colsum[n0 + 2];
-            const long long d3 = (h ? hi3 : hi1) - p.colsum[n0 + 3];
+            const long long d0 = acc[nb][2 * h] - colsum[n0];
+            const long long d1 = acc[nb][2 * h + 1] - colsum[n0 + 1];
+            const long long d2 = (h ? hi2 : hi0) - colsum[n0 + 2];
+            const long long d3 = (h ? hi3 : hi1) - colsum[n0 + 3];
             const long long S4 = d0 + d1 * 256 + d2 * 65536 + d3 * 16777216;
-            p.y[t * p.ldy + R] =
-                (float)((double)S4 * p.tok_scale[t] * (double)p.row_scales[R]);
+            p.y[t * p.ldy + R] = (float)((double)S4 * tok_scale[t] * (double)p.row_scales[R]);
           }
         }
       }
@@ -184,34 +232,67 @@ __global__ void __launch_bounds__(kGvWarps * 32) gemv_kernel(const __grid_consta
   }
 }
 
+template <int NB>
+int launch_nb(const GvBatch& batch, int64_t ctas, size_t smem, cudaStream_t s) {
+  static int attr_smem = 0;  // per template instance
+  if ((int)smem > attr_smem) {
+    FT_CUDA(cudaFuncSetAttribute(gemv_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem));
+    attr_smem = (int)smem;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)ctas);
+  cfg.blockDim = dim3(kGvWarps * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  FT_CUDA(cudaLaunchKernelEx(&cfg, gemv_kernel<NB>, batch));
+  FT_LAUNCH_CHECK();
+  return FT_OK;
+}
+
 }  // namespace
 
-// Launches the decode-shape kernel for problems whose prep output (npad 16,
-// one pass) is ready in the workspace.  `probs` carries everything but the
-// work split, which is chosen here.
-int launch_gemv(ft_ctx* ctx, int nprob, const GvLaunchProblem* probs, int digits,
+bool gemv_fits(const ft_weight* w, int64_t seq, int xkind) {
+  const int digits = xkind == 2 ? 1 : 4;
+  const int64_t ncols = seq * digits;
+  if (w->format != 0 || ncols > 16) return false;
+  const int64_t nb = ncols > 8 ? 2 : 1;
+  return kRingBytes + w->n_chunks * nb * 1024 <= kGemvMaxSmem;
+}
+
+int launch_gemv(ft_ctx* ctx, int nprob, const GvLaunchProblem* probs, int xkind,
                 cudaStream_t s) {
   FT_CHECK(nprob > 0 && nprob <= kGvMaxProblems, FT_ERR_UNSUPPORTED, "bad GEMV group size");
   static thread_local GvBatch batch;
   batch.nprob = nprob;
-  batch.digits = digits;
-  int64_t mblocks = 0;
-  int nbmax = 1;
-  for (int i = 0; i < nprob; ++i) mblocks += probs[i].n_tiles * 8;
-  // K splits: enough warps for ~32 per SM, but a split keeps >= 2 chunks
+  batch.digits = xkind == 2 ? 1 : 4;
+  int64_t mblocks = 0, max_nch = 0, max_cols = 0;
+  for (int i = 0; i < nprob; ++i) {
+    mblocks += probs[i].n_tiles * 8;
+    max_nch = probs[i].n_chunks > max_nch ? probs[i].n_chunks : max_nch;
+    const int64_t nc = probs[i].seq * batch.digits;
+    max_cols = nc > max_cols ? nc : max_cols;
+  }
+  batch.nb = max_cols > 8 ? 2 : 1;
+  // K splits: enough warps for ~32 per SM, but a split keeps >= 8 chunks
   const int64_t want_warps = (int64_t)ctx->num_sms * 32;
   int64_t ctas = 0;
   for (int i = 0; i < nprob; ++i) {
     const GvLaunchProblem& q = probs[i];
     GvProblem& p = batch.p[i];
     int S = 1;
-    while (S < 8 && mblocks * S < want_warps && q.n_chunks >= 4 * S) S *= 2;
+    while (S < 8 && mblocks * S < want_warps && q.n_chunks >= 8 * S) S *= 2;
     p.codes = reinterpret_cast<const uint4*>(q.codes);
     p.row_scales = q.row_scales;
     p.rows = q.rows;
     p.n_tiles = q.n_tiles;
     p.n_chunks = q.n_chunks;
-    p.bmat = q.bmat;
+    p.bfrag = reinterpret_cast<const uint4*>(q.bmat);
     p.colsum = q.colsum;
     p.tok_scale = q.tok_scale;
     p.sx = q.sx;
@@ -220,27 +301,14 @@ int launch_gemv(ft_ctx* ctx, int nprob, const GvLaunchProblem* probs, int digits
     p.seq = q.seq;
     p.ksplit = S;
     p.cps = (int)ceil_div(q.n_chunks, S);
-    p.nb = (int)((q.seq * digits + 7) / 8);
-    if (p.nb > nbmax) nbmax = p.nb;
     p.cta_begin = ctas;
     ctas += ceil_div(q.n_tiles * 8, kGvWarps / S);
   }
   FT_CHECK(ctas <= 0x7FFFFFFF, FT_ERR_UNSUPPORTED, "GEMV grid too large");
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)ctas);
-  cfg.blockDim = dim3(kGvWarps * 32);
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  if (nbmax == 1)
-    FT_CUDA(cudaLaunchKernelEx(&cfg, gemv_kernel<1>, batch));
-  else
-    FT_CUDA(cudaLaunchKernelEx(&cfg, gemv_kernel<2>, batch));
-  FT_LAUNCH_CHECK();
-  return FT_OK;
+  const size_t smem = (size_t)kRingBytes + (size_t)max_nch * batch.nb * 1024;
+  FT_CHECK(smem <= (size_t)kGemvMaxSmem, FT_ERR_UNSUPPORTED, "GEMV operand too large");
+  static_assert(kRingBytes >= kGvWarps * 32 * 8 * 4, "split sums reuse the ring");
+  return batch.nb == 1 ? launch_nb<1>(batch, ctas, smem, s) : launch_nb<2>(batch, ctas, smem, s);
 }
 
 }  // namespace ft

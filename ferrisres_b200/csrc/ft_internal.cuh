@@ -126,19 +126,22 @@ int launch_tc_matmul(ft_ctx* ctx, const ft_weight* w, int64_t seq, const void* x
 int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t seq,
                       const void* const* xs, int xkind, const float* const* sxs, float* const* ys,
                       const int64_t* ldys, cudaStream_t s, const int64_t* seqs = nullptr);
-// Decode-shape kernel (ft_gemv.cu) over prep_b_kernel's 16-column operand.
+// Decode-shape kernel (ft_gemv.cu): dense problems whose activations fit 16
+// operand columns; prep_b_kernel writes their operand in fragment order.
+constexpr int kGemvMaxSmem = 64 * 1024;
 struct GvLaunchProblem {
   const uint8_t* codes;
   const float* row_scales;
   int64_t rows, n_tiles, n_chunks;
-  const int8_t* bmat;
+  const int8_t* bmat;  // [n_chunks][2][32 lanes][8 words]
   const int32_t* colsum;
   const double* tok_scale;
   const float* sx;
   float* y;
   int64_t ldy, seq;
 };
-int launch_gemv(ft_ctx* ctx, int nprob, const GvLaunchProblem* probs, int digits,
+bool gemv_fits(const ft_weight* w, int64_t seq, int xkind);
+int launch_gemv(ft_ctx* ctx, int nprob, const GvLaunchProblem* probs, int xkind,
                 cudaStream_t s);
 int launch_wgsl_op(const uint32_t* words, const float* scales, const float* x, float* y,
                    uint32_t seq, uint32_t in_cols, uint32_t out_rows, cudaStream_t s);

@@ -558,6 +558,7 @@ struct PrepBatch {
   int nsrc;
   int xkind;  // 0 f32, 1 bf16, 2 int8 codes
   int D, npad, tok_per_pass;
+  int frag_layout;  // 1: the decode kernel's per-lane fragment order (npad 16, one pass)
   int64_t block_begin[kMaxSources + 1];
   PrepSource s[kMaxSources];
 };
@@ -566,6 +567,14 @@ __device__ __forceinline__ int64_t b_offset(int64_t pass, int64_t chunk, int n, 
                                             int64_t n_chunks) {
   return ((pass * n_chunks + chunk) * npad) * 128 + ((kin >> 4) * (npad >> 3) + (n >> 3)) * 128 +
          (n & 7) * 16 + (kin & 15);
+}
+
+// Fragment order for the decode-shape kernel (ft_gemv.cu): per chunk, per n8
+// block nb, per lane L = 4g + r, 8 words: word 2ks + kk holds column 8nb + g
+// at K = 32ks + 16kk + 4r .. +3 (one mma.m16n8k32 B fragment register).
+__device__ __forceinline__ int64_t frag_offset(int64_t chunk, int n, int kin) {
+  const int nb = n >> 3, g = n & 7, ks = kin >> 5, kk = (kin >> 4) & 1, r = (kin >> 2) & 3;
+  return (((chunk * 2 + nb) * 32 + 4 * g + r) * 8 + 2 * ks + kk) * 4 + (kin & 3);
 }
 
 __device__ __forceinline__ float load_x(const void* x, int xkind, int64_t i) {
@@ -627,7 +636,9 @@ __global__ void __launch_bounds__(256) prep_b_kernel(const __grid_constant__ Pre
     const int64_t chunk = k >> 7;
     const int kin = (int)(k & 127);
     for (int d = 0; d < D; ++d) {
-      src.bmat[b_offset(pass, chunk, lt * D + d, kin, npad, src.n_chunks)] = (int8_t)dg[d];
+      const int64_t o = pb.frag_layout ? frag_offset(chunk, lt * D + d, kin)
+                                       : b_offset(pass, chunk, lt * D + d, kin, npad, src.n_chunks);
+      src.bmat[o] = (int8_t)dg[d];
       csum[d] += dg[d];
     }
   }
@@ -736,6 +747,10 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
     live[nlive++] = i;
   }
 
+  // decode shapes run on the warp-level kernel (ft_gemv.cu)
+  bool gemv = true;
+  for (int q = 0; q < nlive && gemv; ++q) gemv = gemv_fits(ws[live[q]], src_seq[src_of[q]], xkind);
+
   // workspace: per source B operand, column sums, token scales
   size_t off = 0;
   size_t b_off[kMaxSources], cs_off[kMaxSources], ts_off[kMaxSources];
@@ -829,6 +844,7 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
     pb.D = D;
     pb.npad = npad;
     pb.tok_per_pass = tok_per_pass;
+    pb.frag_layout = gemv ? 1 : 0;
     int64_t blocks = 0;
     for (int j = 0; j < nsrc; ++j) {
       const int64_t passes = ceil_div(src_seq[j], tok_per_pass);
@@ -859,15 +875,14 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
     FT_LAUNCH_CHECK();
   }
 
-  if (ws[live[0]]->format == 0 && npad == 16) {
-    // decode shapes: the warp-level kernel streams the weights at memory pace
+  if (gemv) {
     GvLaunchProblem gp[kMaxProblems];
     for (int q = 0; q < nlive; ++q) {
       const TqProblem& p = batch.p[q];
       gp[q] = GvLaunchProblem{p.codes, p.row_scales, p.rows, p.n_tiles, p.n_chunks, p.bmat,
                               p.colsum, p.tok_scale, p.sx, p.y, p.ldy, p.seq};
     }
-    return launch_gemv(ctx, nlive, gp, D, s);
+    return launch_gemv(ctx, nlive, gp, xkind, s);
   }
   const int64_t grid = items < grid_target ? items : grid_target;
   if (ws[live[0]]->format == 1) {
