@@ -158,6 +158,15 @@ int ft_ctx_create(int device, ft_ctx** out) {
     delete c;
     return fail(FT_ERR_GPU, "stream creation failed: %s", cudaGetErrorString(se));
   }
+  se = cudaMalloc(&c->err_word, 256);
+  if (se == cudaSuccess) se = cudaMemset(c->err_word, 0, 256);
+  if (se != cudaSuccess) {
+    cudaStreamDestroy(c->host_stream);
+    if (c->err_word) cudaFree(c->err_word);
+    delete c;
+    return fail(FT_ERR_GPU, "error word allocation failed: %s", cudaGetErrorString(se));
+  }
+  c->err_flag = c->err_word;
   *out = c;
   return FT_OK;
 }
@@ -169,6 +178,7 @@ int ft_ctx_destroy(ft_ctx* ctx) {
   if (ctx->ws.ptr) cudaFree(ctx->ws.ptr);
   if (ctx->io.ptr) cudaFree(ctx->io.ptr);
   if (ctx->zs.ptr) cudaFree(ctx->zs.ptr);
+  if (ctx->err_word) cudaFree(ctx->err_word);
   if (ctx->host_stream) cudaStreamDestroy(ctx->host_stream);
   delete ctx;
   return FT_OK;
@@ -380,12 +390,14 @@ int ft_ctx_check(ft_ctx* ctx) {
   FT_CHECK(ctx, FT_ERR_SHAPE, "null context");
   DeviceGuard g(ctx->device);
   FT_CUDA(cudaDeviceSynchronize());
-  if (ctx->err_flag) {
+  int* words[2] = {ctx->err_word, ctx->err_flag != ctx->err_word ? ctx->err_flag : nullptr};
+  for (int* wd : words) {
+    if (!wd) continue;
     int code = 0;
-    FT_CUDA(cudaMemcpy(&code, ctx->err_flag, sizeof(int), cudaMemcpyDeviceToHost));
+    FT_CUDA(cudaMemcpy(&code, wd, sizeof(int), cudaMemcpyDeviceToHost));
     if (code != 0) {
       int zero = 0;
-      FT_CUDA(cudaMemcpy(ctx->err_flag, &zero, sizeof(int), cudaMemcpyHostToDevice));
+      FT_CUDA(cudaMemcpy(wd, &zero, sizeof(int), cudaMemcpyHostToDevice));
       return fail(FT_ERR_TIMEOUT, "a kernel's bounded wait gave up (site %d); results of that "
                   "launch are invalid", code);
     }

@@ -232,6 +232,152 @@ __global__ void __launch_bounds__(kGvWarps * 32, FT_GV_MIN_BLOCKS) gemv_kernel(c
   }
 }
 
+// ---------------------------------------------------------------- prep --
+// Activation operand in fragment order for the kernel above, one CTA per
+// (source, token slot): column n = slot*D + d of chunk c sits in lane
+// 4(n%8) + r, word 2ks + kk of n8 block n/8 for K = c*128 + 32ks + 16kk + 4r
+// .. +3.  fp32/bf16: the signed base-256 digits of X = round(x * 2^30 /
+// absmax(x)) (|X| <= 2^30 fits 32 bits); int8: the caller's codes.  Slots
+// past the token count write zeros.  Column sums and token scales as in
+// prep_b_kernel.
+struct FragSource {
+  const void* x;
+  uint32_t* frag;          // [n_chunks][2][32][8] words
+  int32_t* colsum;         // [16]
+  double* tok_scale;       // [4]
+  int64_t K, n_chunks, seq;
+};
+constexpr int kMaxFragSources = 64;
+constexpr int kPrepThreads = 512;
+struct FragBatch {
+  int nsrc, xkind, D, slots;  // token slots per source (8*nb / D)
+  FragSource s[kMaxFragSources];
+};
+
+__device__ __forceinline__ float4 load_x4(const void* x, int xkind, int64_t row, int64_t k,
+                                          int64_t K) {
+  // elements k .. k+3 of row `row` (zero past K)
+  float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  const int64_t i = row * K + k;
+  if (xkind == 0) {
+    const float* f = static_cast<const float*>(x);
+    if (k + 3 < K && ((reinterpret_cast<uintptr_t>(f + i) & 15) == 0)) {
+      v = __ldg(reinterpret_cast<const float4*>(f + i));
+    } else {
+      if (k < K) v.x = f[i];
+      if (k + 1 < K) v.y = f[i + 1];
+      if (k + 2 < K) v.z = f[i + 2];
+      if (k + 3 < K) v.w = f[i + 3];
+    }
+  } else {
+    const uint16_t* h = static_cast<const uint16_t*>(x);
+    if (k < K) v.x = __uint_as_float((uint32_t)h[i] << 16);
+    if (k + 1 < K) v.y = __uint_as_float((uint32_t)h[i + 1] << 16);
+    if (k + 2 < K) v.z = __uint_as_float((uint32_t)h[i + 2] << 16);
+    if (k + 3 < K) v.w = __uint_as_float((uint32_t)h[i + 3] << 16);
+  }
+  return v;
+}
+
+__global__ void __launch_bounds__(kPrepThreads) prep_frag_kernel(const __grid_constant__ FragBatch fb) {
+  // let the matmul start streaming its weights, then wait for the producer of x
+  tc::pdl_launch_dependents();
+  tc::pdl_wait();
+  const int si = blockIdx.x / fb.slots, t = blockIdx.x % fb.slots;
+  const FragSource& src = fb.s[si];
+  const int D = fb.D, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const bool live = t < src.seq;
+  const int nquads = (int)(src.n_chunks * 32);
+  constexpr int kQ = 4;  // quads per thread kept in registers (K <= 8192)
+  __shared__ float red_f[kPrepThreads / 32];
+  __shared__ int red_i[kPrepThreads / 32][4];
+  uint32_t word[kQ][4];
+  int cs[4] = {0, 0, 0, 0};
+  if (D == 4) {
+    float4 xv[kQ];
+    float amax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kQ; ++j) {
+      const int qi = tid + j * kPrepThreads;
+      xv[j] = live && qi < nquads ? load_x4(src.x, fb.xkind, t, 4 * (int64_t)qi, src.K)
+                                  : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      amax = fmaxf(amax, fmaxf(fmaxf(fabsf(xv[j].x), fabsf(xv[j].y)),
+                               fmaxf(fabsf(xv[j].z), fabsf(xv[j].w))));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if (lane == 0) red_f[warp] = amax;
+    __syncthreads();
+    amax = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kPrepThreads / 32; ++w) amax = fmaxf(amax, red_f[w]);
+    const double mult = amax > 0.0f ? 1073741824.0 / (double)amax : 0.0;  // 2^30 / absmax
+    if (tid == 0 && live) src.tok_scale[t] = (double)amax / 1073741824.0;
+#pragma unroll
+    for (int j = 0; j < kQ; ++j) {
+      const float e4[4] = {xv[j].x, xv[j].y, xv[j].z, xv[j].w};
+      word[j][0] = word[j][1] = word[j][2] = word[j][3] = 0u;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        int X = __double2int_rn((double)e4[e] * mult);
+#pragma unroll
+        for (int d = 0; d < 3; ++d) {
+          const int lo = ((X & 0xFF) ^ 0x80) - 0x80;  // signed low digit
+          word[j][d] |= (uint32_t)(lo & 0xFF) << (8 * e);
+          cs[d] += lo;
+          X = (X - lo) >> 8;
+        }
+        word[j][3] |= (uint32_t)(X & 0xFF) << (8 * e);  // |X| <= 65 here
+        cs[3] += X;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < kQ; ++j) {
+      const int qi = tid + j * kPrepThreads;
+      uint32_t wv = 0u;
+      if (live && qi < nquads) {
+        const int8_t* q = static_cast<const int8_t*>(src.x) + (int64_t)t * src.K;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int64_t k = 4 * (int64_t)qi + e;
+          const int v = k < src.K ? q[k] : 0;
+          wv |= (uint32_t)(v & 0xFF) << (8 * e);
+          cs[0] += v;
+        }
+      }
+      word[j][0] = wv;
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < kQ; ++j) {
+    const int qi = tid + j * kPrepThreads;
+    if (qi >= nquads) break;
+    const int64_t chunk = qi >> 5;
+    const int kin = (qi & 31) * 4;
+    const int rr = (kin >> 2) & 3, ks = kin >> 5, kk = (kin >> 4) & 1;
+    for (int d = 0; d < D; ++d) {
+      const int n = t * D + d;
+      src.frag[((chunk * 2 + (n >> 3)) * 32 + 4 * (n & 7) + rr) * 8 + 2 * ks + kk] = word[j][d];
+    }
+  }
+  // column sums
+#pragma unroll
+  for (int d = 0; d < 4; ++d) {
+    int v = cs[d];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) red_i[warp][d] = v;
+  }
+  __syncthreads();
+  if (tid < D) {
+    int v = 0;
+#pragma unroll
+    for (int w = 0; w < kPrepThreads / 32; ++w) v += red_i[w][tid];
+    src.colsum[t * D + tid] = v;
+  }
+}
+
 template <int NB>
 int launch_nb(const GvBatch& batch, int64_t ctas, size_t smem, cudaStream_t s) {
   static int attr_smem = 0;  // per template instance
@@ -309,6 +455,33 @@ int launch_gemv(ft_ctx* ctx, int nprob, const GvLaunchProblem* probs, int xkind,
   FT_CHECK(smem <= (size_t)kGemvMaxSmem, FT_ERR_UNSUPPORTED, "GEMV operand too large");
   static_assert(kRingBytes >= kGvWarps * 32 * 8 * 4, "split sums reuse the ring");
   return batch.nb == 1 ? launch_nb<1>(batch, ctas, smem, s) : launch_nb<2>(batch, ctas, smem, s);
+}
+
+int launch_gemv_prep(int nsrc, const GvPrepSource* srcs, int xkind, int nb, cudaStream_t s) {
+  FT_CHECK(nsrc > 0 && nsrc <= kMaxFragSources, FT_ERR_UNSUPPORTED, "bad source count");
+  static thread_local FragBatch fb;
+  fb.nsrc = nsrc;
+  fb.xkind = xkind;
+  fb.D = xkind == 2 ? 1 : 4;
+  fb.slots = 8 * nb / fb.D;
+  for (int i = 0; i < nsrc; ++i) {
+    FT_CHECK(srcs[i].n_chunks * 32 <= 4 * kPrepThreads, FT_ERR_UNSUPPORTED,
+             "K too large for the decode prep");
+    fb.s[i] = FragSource{srcs[i].x, reinterpret_cast<uint32_t*>(srcs[i].frag), srcs[i].colsum,
+                         srcs[i].tok_scale, srcs[i].K, srcs[i].n_chunks, srcs[i].seq};
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(nsrc * fb.slots));
+  cfg.blockDim = dim3(kPrepThreads);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  FT_CUDA(cudaLaunchKernelEx(&cfg, prep_frag_kernel, fb));
+  FT_LAUNCH_CHECK();
+  return FT_OK;
 }
 
 }  // namespace ft

@@ -84,7 +84,9 @@ struct ft_ctx {
   cudaStream_t host_stream = nullptr;  // used by the synchronous host-buffer calls
   ft::Workspace io;                    // device staging for the host-buffer calls
   ft::Workspace zs;                    // zero-initialised scratch (split-K sums, tickets)
-  int* err_flag = nullptr;             // device word set by a kernel whose bounded wait gave up
+  int* err_word = nullptr;             // device word set by a kernel whose bounded wait gave up
+  int* err_flag = nullptr;             // word of the latest launch (err_word, or the static
+                                       // word of the allocation-free entry point)
 };
 
 struct ft_weight {
@@ -141,6 +143,14 @@ struct GvLaunchProblem {
   int64_t ldy, seq;
 };
 bool gemv_fits(const ft_weight* w, int64_t seq, int xkind);
+struct GvPrepSource {
+  const void* x;
+  int8_t* frag;  // [n_chunks][2][32][32 B]
+  int32_t* colsum;
+  double* tok_scale;
+  int64_t K, n_chunks, seq;
+};
+int launch_gemv_prep(int nsrc, const GvPrepSource* srcs, int xkind, int nb, cudaStream_t s);
 int launch_gemv(ft_ctx* ctx, int nprob, const GvLaunchProblem* probs, int xkind,
                 cudaStream_t s);
 int launch_wgsl_op(const uint32_t* words, const float* scales, const float* x, float* y,

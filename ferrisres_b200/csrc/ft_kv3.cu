@@ -1054,7 +1054,7 @@ int ft_flash_decode_3bit(ft_ctx* ctx, ft_kv3* c, const float* q_dev, int64_t q_h
   const float sc = scale > 0.0f ? scale : 1.0f / sqrtf((float)kD);
   p.qk_log2 = sc * 1.4426950408889634f;
   p.blocks = c->blocks;
-  p.err = ctx->err_flag;
+  p.err = ctx->err_word;
   // split choice: minimise waves x (tiles per CTA + per-CTA overhead); at most
   // 2^15 tiles (2^20 slots, 2^18 per warp) per CTA keeps every int32 digit sum
   // exact (7 * 255 * 2^18 < 2^31)

@@ -558,7 +558,6 @@ struct PrepBatch {
   int nsrc;
   int xkind;  // 0 f32, 1 bf16, 2 int8 codes
   int D, npad, tok_per_pass;
-  int frag_layout;  // 1: the decode kernel's per-lane fragment order (npad 16, one pass)
   int64_t block_begin[kMaxSources + 1];
   PrepSource s[kMaxSources];
 };
@@ -567,14 +566,6 @@ __device__ __forceinline__ int64_t b_offset(int64_t pass, int64_t chunk, int n, 
                                             int64_t n_chunks) {
   return ((pass * n_chunks + chunk) * npad) * 128 + ((kin >> 4) * (npad >> 3) + (n >> 3)) * 128 +
          (n & 7) * 16 + (kin & 15);
-}
-
-// Fragment order for the decode-shape kernel (ft_gemv.cu): per chunk, per n8
-// block nb, per lane L = 4g + r, 8 words: word 2ks + kk holds column 8nb + g
-// at K = 32ks + 16kk + 4r .. +3 (one mma.m16n8k32 B fragment register).
-__device__ __forceinline__ int64_t frag_offset(int64_t chunk, int n, int kin) {
-  const int nb = n >> 3, g = n & 7, ks = kin >> 5, kk = (kin >> 4) & 1, r = (kin >> 2) & 3;
-  return (((chunk * 2 + nb) * 32 + 4 * g + r) * 8 + 2 * ks + kk) * 4 + (kin & 3);
 }
 
 __device__ __forceinline__ float load_x(const void* x, int xkind, int64_t i) {
@@ -603,9 +594,11 @@ __global__ void __launch_bounds__(256) prep_b_kernel(const __grid_constant__ Pre
   double mult = 0.0;
   if (pb.xkind != 2) {
     float amax = 0.0f;
-    if (live)
+    if (live) {
+#pragma unroll 8
       for (int64_t k = threadIdx.x; k < K; k += blockDim.x)
         amax = fmaxf(amax, fabsf(load_x(src.x, pb.xkind, t * K + k)));
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     if (lane == 0) red_f[warp] = amax;
@@ -616,6 +609,7 @@ __global__ void __launch_bounds__(256) prep_b_kernel(const __grid_constant__ Pre
     if (threadIdx.x == 0 && live) src.tok_scale[t] = (double)amax / 1073741824.0;
   }
   int csum[4] = {0, 0, 0, 0};
+#pragma unroll 4
   for (int64_t k = threadIdx.x; k < kpad; k += blockDim.x) {
     int dg[4] = {0, 0, 0, 0};
     if (live && k < K) {
@@ -636,9 +630,7 @@ __global__ void __launch_bounds__(256) prep_b_kernel(const __grid_constant__ Pre
     const int64_t chunk = k >> 7;
     const int kin = (int)(k & 127);
     for (int d = 0; d < D; ++d) {
-      const int64_t o = pb.frag_layout ? frag_offset(chunk, lt * D + d, kin)
-                                       : b_offset(pass, chunk, lt * D + d, kin, npad, src.n_chunks);
-      src.bmat[o] = (int8_t)dg[d];
+      src.bmat[b_offset(pass, chunk, lt * D + d, kin, npad, src.n_chunks)] = (int8_t)dg[d];
       csum[d] += dg[d];
     }
   }
@@ -832,11 +824,24 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
       batch.p[q].acc = reinterpret_cast<int32_t*>(zs + acc_off[q]);
       batch.p[q].cnt = reinterpret_cast<int32_t*>(zs + cnt_off[q]);
     }
-  batch.err = reinterpret_cast<int*>(zs + err_off);
-  ctx->err_flag = batch.err;
+  batch.err = ctx->err_word;
+  ctx->err_flag = ctx->err_word;
 
-  // prep launch (one block per source x pass x token slot)
-  {
+  // prep launch: the decode kernel's fragment order, or one block per source
+  // x pass x token slot of the tensor-core operand
+  if (gemv) {
+    GvPrepSource gs[kMaxSources];
+    int64_t max_cols = 0;
+    for (int j = 0; j < nsrc; ++j) {
+      gs[j] = GvPrepSource{src_x[j], reinterpret_cast<int8_t*>(wsb + b_off[j]),
+                           reinterpret_cast<int32_t*>(wsb + cs_off[j]),
+                           reinterpret_cast<double*>(wsb + ts_off[j]), src_k[j],
+                           ceil_div(src_k[j], kChunkK), src_seq[j]};
+      max_cols = src_seq[j] * D > max_cols ? src_seq[j] * D : max_cols;
+    }
+    st = launch_gemv_prep(nsrc, gs, xkind, max_cols > 8 ? 2 : 1, s);
+    if (st != FT_OK) return st;
+  } else {
     static thread_local PrepBatch pb;
     memset(&pb, 0, sizeof(pb));
     pb.nsrc = nsrc;
@@ -844,7 +849,6 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
     pb.D = D;
     pb.npad = npad;
     pb.tok_per_pass = tok_per_pass;
-    pb.frag_layout = gemv ? 1 : 0;
     int64_t blocks = 0;
     for (int j = 0; j < nsrc; ++j) {
       const int64_t passes = ceil_div(src_seq[j], tok_per_pass);

@@ -82,6 +82,35 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* er
   }
 }
 
+// Same, but a waiting thread is suspended by the hardware (up to `hint_ns`
+// per attempt, woken when the phase completes) instead of spinning, so
+// waiting warps leave the issue slots to the others.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity,
+                                                    uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_sleep(uint32_t bar, uint32_t parity, int* err,
+                                                int code, uint32_t hint_ns = 20000) {
+  if (mbar_try_wait_sleep(bar, parity, hint_ns)) return true;
+  unsigned long long t0 = globaltimer();
+  for (;;) {
+    if (mbar_try_wait_sleep(bar, parity, hint_ns)) return true;
+    if (globaltimer() - t0 > kSpinTimeoutNs) {
+      if (err) atomicCAS(err, 0, code);
+      return false;
+    }
+  }
+}
+
 // 1-D bulk copy global -> shared, completion counted on `bar` (tx bytes).
 // dst, src 16-byte aligned, bytes a multiple of 16.
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes,
