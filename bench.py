@@ -263,7 +263,7 @@ def run_ours(args, ws, rank, local):
                      "peak": peak, "unit": "GB/s",
                      "frac": round(ALGO_BYTES * group / (sec * group / steps) / 1e9 / peak, 4),
                      "peak_source": peak_kind, "traffic": traffic,
-                     "kernel": "tq_grouped_kernel<16> (+ prep_b_kernel)",
+                     "kernel": "gemv_kernel<1> (+ prep_frag_kernel)",
                      "algorithmic_bytes_per_launch": ALGO_BYTES * group,
                      "note": f"one launch = {group} GEMVs; achieved = algorithmic bytes per "
                              "launch / per-launch device time (CUDA events over the timed region)"},
@@ -428,7 +428,10 @@ def run_gemm(args, ws, rank, local):
                      "unit": "TOP/s", "frac": round(tops / peak, 4),
                      "peak_source": "2 x measured bf16 dense (int8 dense rate is twice bf16 on B200)"
                                     if bf16_peak else "2 x fallback bf16",
-                     "traffic": None},
+                     "traffic": load_traffic().get("gemm_cfg2", {}).get("dram_bytes_per_launch"),
+                     "kernel": "tq_grouped_kernel<128, 0> (+ prep_b_kernel, quantize_i8_kernel)",
+                     "note": "achieved = the whole step's int ops (quantize + prep + matmul) / "
+                             "step time"},
         "gpu_launches": int(per_step * args.steps),
         "clocks": clocks,
     }
