@@ -608,31 +608,63 @@ __global__ void __launch_bounds__(256) prep_b_kernel(const __grid_constant__ Pre
     if (amax > 0.0f) mult = 1073741824.0 / (double)amax;  // 2^30 / absmax
     if (threadIdx.x == 0 && live) src.tok_scale[t] = (double)amax / 1073741824.0;
   }
+  // 16 consecutive K per step: one 16-byte row of the operand per digit column
   int csum[4] = {0, 0, 0, 0};
-#pragma unroll 4
-  for (int64_t k = threadIdx.x; k < kpad; k += blockDim.x) {
-    int dg[4] = {0, 0, 0, 0};
-    if (live && k < K) {
-      if (pb.xkind == 2) {
-        dg[0] = static_cast<const int8_t*>(src.x)[t * K + k];
-      } else {
-        long long X = __double2ll_rn((double)load_x(src.x, pb.xkind, t * K + k) * mult);
+  const int64_t ngroups = kpad >> 4;
+  for (int64_t kg = threadIdx.x; kg < ngroups; kg += blockDim.x) {
+    const int64_t k0 = kg * 16;
+    uint32_t w[4][4];
 #pragma unroll
-        for (int d = 0; d < 3; ++d) {
-          int lo = (int)(X & 0xFF);
-          lo = (lo ^ 0x80) - 0x80;  // signed low digit
-          dg[d] = lo;
-          X = (X - lo) >> 8;
+    for (int d = 0; d < 4; ++d) w[d][0] = w[d][1] = w[d][2] = w[d][3] = 0u;
+    if (live && k0 < K) {
+      if (pb.xkind == 2) {
+        const int8_t* q = static_cast<const int8_t*>(src.x) + t * K + k0;
+        if (k0 + 16 <= K && (reinterpret_cast<uintptr_t>(q) & 15) == 0) {
+          const uint4 v = __ldg(reinterpret_cast<const uint4*>(q));
+          w[0][0] = v.x; w[0][1] = v.y; w[0][2] = v.z; w[0][3] = v.w;
+        } else {
+          for (int e = 0; e < 16 && k0 + e < K; ++e)
+            w[0][e >> 2] |= (uint32_t)(q[e] & 0xFF) << (8 * (e & 3));
         }
-        dg[3] = (int)X;  // |X| <= 64 here
+#pragma unroll
+        for (int j = 0; j < 4; ++j) csum[0] = __dp4a((int)w[0][j], 0x01010101, csum[0]);
+      } else {
+        float xv[16];
+        const bool vec = pb.xkind == 0 && k0 + 16 <= K &&
+                         (reinterpret_cast<uintptr_t>(static_cast<const float*>(src.x) + t * K + k0) & 15) == 0;
+        if (vec) {
+          const float4* f4 = reinterpret_cast<const float4*>(static_cast<const float*>(src.x) + t * K + k0);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float4 v = __ldg(f4 + j);
+            xv[4 * j] = v.x; xv[4 * j + 1] = v.y; xv[4 * j + 2] = v.z; xv[4 * j + 3] = v.w;
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) xv[e] = k0 + e < K ? load_x(src.x, pb.xkind, t * K + k0 + e) : 0.0f;
+        }
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          int X = __double2int_rn((double)xv[e] * mult);  // |X| <= 2^30
+#pragma unroll
+          for (int d = 0; d < 3; ++d) {
+            const int lo = ((X & 0xFF) ^ 0x80) - 0x80;  // signed low digit
+            w[d][e >> 2] |= (uint32_t)(lo & 0xFF) << (8 * (e & 3));
+            csum[d] += lo;
+            X = (X - lo) >> 8;
+          }
+          w[3][e >> 2] |= (uint32_t)(X & 0xFF) << (8 * (e & 3));  // |X| <= 65 here
+          csum[3] += X;
+        }
       }
     }
-    const int64_t chunk = k >> 7;
-    const int kin = (int)(k & 127);
-    for (int d = 0; d < D; ++d) {
-      src.bmat[b_offset(pass, chunk, lt * D + d, kin, npad, src.n_chunks)] = (int8_t)dg[d];
-      csum[d] += dg[d];
-    }
+    const int64_t chunk = k0 >> 7;
+    const int kin = (int)(k0 & 127);
+#pragma unroll
+    for (int d = 0; d < 4; ++d)
+      if (d < D)
+        *reinterpret_cast<uint4*>(src.bmat + b_offset(pass, chunk, lt * D + d, kin, npad, src.n_chunks)) =
+            make_uint4(w[d][0], w[d][1], w[d][2], w[d][3]);
   }
   for (int d = 0; d < D; ++d) {
     int v = csum[d];
