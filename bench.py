@@ -263,7 +263,7 @@ def run_ours(args, ws, rank, local):
                      "peak": peak, "unit": "GB/s",
                      "frac": round(ALGO_BYTES * group / (sec * group / steps) / 1e9 / peak, 4),
                      "peak_source": peak_kind, "traffic": traffic,
-                     "kernel": "gemv_kernel<1> (+ prep_frag_kernel)",
+                     "kernel": "gemv_kernel<1> (activation prep fused)",
                      "algorithmic_bytes_per_launch": ALGO_BYTES * group,
                      "note": f"one launch = {group} GEMVs; achieved = algorithmic bytes per "
                              "launch / per-launch device time (CUDA events over the timed region)"},

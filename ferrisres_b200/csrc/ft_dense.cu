@@ -11,12 +11,12 @@ namespace {
 template <bool kU32Src>
 __global__ void repack_kernel(const void* __restrict__ src, int64_t rows, int64_t cols,
                               int64_t n_chunks, int64_t total_words, uint32_t* __restrict__ dst) {
-  // one thread per output word; block = 1024 words = [m-block][lane][word ks]
+  // one thread per output word; block = 1024 words = [m-block][lane][word i]
   int64_t gw = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (gw >= total_words) return;
   int64_t block = gw >> 10;
   const int within = (int)(gw & 1023);
-  const int mb = within >> 7, lane = (within >> 2) & 31, ks = within & 3;
+  const int mb = within >> 7, lane = (within >> 2) & 31, wi = within & 3;
   const int g = lane >> 2, r = lane & 3;
   int64_t tile = block / n_chunks, chunk = block % n_chunks;
   int64_t cp = (cols + 15) >> 4;
@@ -25,8 +25,9 @@ __global__ void repack_kernel(const void* __restrict__ src, int64_t rows, int64_
   for (int j = 0; j < 4; ++j)
 #pragma unroll
     for (int b = 0; b < 4; ++b) {
-      const int64_t R = tile * kTileRows + 16 * mb + g + 8 * (j & 1);
-      const int64_t k = chunk * kChunkK + 32 * ks + 16 * (j >> 1) + 4 * r + b;
+      // code slot j of byte b = k-step j; the word picks the row half and k half
+      const int64_t R = tile * kTileRows + 16 * mb + g + 8 * (wi & 1);
+      const int64_t k = chunk * kChunkK + 32 * j + 16 * (wi >> 1) + 4 * r + b;
       uint32_t code = 1u;
       if (R < rows && k < cols) {
         if (kU32Src) {

@@ -4,59 +4,105 @@
 //
 // Same exact formulation as the tensor-core engine (ft_tc.cu): the A operand
 // is the unsigned codes u = w + 1, the B operand the int8 activation columns
-// (fp32/bf16: the signed base-256 digits of X = round(x * 2^30 / absmax(x)),
-// int8: the caller's codes), int32 sums are exact, the epilogue subtracts the
-// column sums and scales.  Here the MMAs are warp-level (mma.sync m16n8k32):
-// every lane loads its 16 bytes of a 4 KB weight block straight from global
-// memory with one coalesced 128-bit load (the lane-major block layout puts a
-// warp's 512 bytes of an m-block contiguous), unpacks each word with one shift
-// and one mask per fragment register, and issues 4 MMAs per n8 block.  The
-// weight stream needs no shared memory staging, barriers or TMEM.
+// (fp32/bf16: the signed base-256 digits of X = round(x * 2^s), 2^s the power
+// of two that puts the token's absmax in [2^29, 2^30); int8: the caller's
+// codes), int32 sums are exact, the epilogue subtracts the column sums and
+// scales.  The MMAs are warp-level (mma.sync m16n8k32, u8 x s8).
 //
-// prep_b_kernel (ft_tc.cu) writes the activation operand in this kernel's
-// fragment order; the kernel is launched as its programmatic dependent, so
-// each warp starts its weight stream before waiting for the prep, then the
-// CTA copies its fragments into shared memory.
+// Weight stream: the lane-major block layout (ft_internal.cuh) gives every
+// lane 16 contiguous bytes of an m-block per 128-K chunk, and code slot j of
+// each byte belongs to k-step j, so the A fragment of k-step j is the loaded
+// word AND (3 << 2j): one logic op per fragment register, no shifts.  The
+// factor 4^j this leaves in the operand is divided out exactly at the end:
+// each k-step has its own accumulator.  Each lane copies its 16-byte pieces
+// into a private cp.async ring (no barriers needed: a lane only reads what it
+// copied) and a warp works on two m-blocks (32 rows) at a time, so one read
+// of the activation fragments feeds 8 MMAs.
 //
-// Work: a CTA of 8 warps covers 8/S m-blocks (16 rows each) of one problem,
-// each split S ways along K (S in {1, 2, 4, 8}, chosen so the launch has
-// enough warps); the S partial sums of an m-block meet in shared memory.
+// Activation fragments are built by every CTA in its own shared memory (no
+// separate prep launch): one pass for the token absmax, one for the digits.
+//
+// Work split: a unit is (row-block of 32 rows, chunk of 128 K).  Problems
+// sharing an activation form a segment; a segment's units are split into
+// row-block-aligned ranges, one per CTA, and a CTA's range is split evenly
+// across its warps at unit granularity.  A row-block cut by a warp boundary
+// is finished by the warp that holds its first chunk, which adds the other
+// warps' partial sums from shared memory after the stream.
+//
+// Launch order: each CTA first lets the next launch start (programmatic
+// dependent launch), starts its weight stream, and only then waits for the
+// previous grid; activations, output and scales are touched after that wait.
+// Weights must therefore not be written by the launch immediately before this
+// one on the stream (uploads end with a copy or a synchronisation).
 #include "ft_internal.cuh"
 #include "ft_tc.cuh"
 
 namespace ft {
 namespace {
 
-constexpr int kGvWarps = 8;
-constexpr int kGvMaxProblems = 64;
-#ifndef FT_GV_DEPTH
-#define FT_GV_DEPTH 6
+#ifndef FT_GV_WARPS
+#define FT_GV_WARPS 8
 #endif
-#ifndef FT_GV_MIN_BLOCKS
-#define FT_GV_MIN_BLOCKS 5
+// one n8 column block (<= 8 operand columns): units of FT_GV_MB1 m-blocks
+#ifndef FT_GV_MB1
+#define FT_GV_MB1 4
 #endif
-constexpr int kDepth = FT_GV_DEPTH;  // weight chunks in flight per warp (cp.async ring)
-constexpr int kRingBytes = kGvWarps * kDepth * 512;
+#ifndef FT_GV_DEPTH1
+#define FT_GV_DEPTH1 4
+#endif
+#ifndef FT_GV_CTAS1
+#define FT_GV_CTAS1 2
+#endif
+// two n8 blocks: units of 2 m-blocks
+#ifndef FT_GV_DEPTH2
+#define FT_GV_DEPTH2 8
+#endif
+#ifndef FT_GV_SLEEP_NS
+#define FT_GV_SLEEP_NS 1000  // suspend hint of the ring waits (woken when the copy lands)
+#endif
+constexpr int kW = FT_GV_WARPS;
+constexpr int kThreads = kW * 32;
+constexpr int kMaxSeg = 64, kMaxProb = 64;
 
-struct GvProblem {
-  const uint4* codes;  // lane-major blocks, 256 uint4 per (tile, chunk)
-  const float* row_scales;
-  int64_t rows, n_tiles, n_chunks;
-  const uint4* bfrag;       // [n_chunks][2][32 lanes][2 uint4] (prep_b_kernel)
-  const int32_t* colsum;    // [16]
-  const double* tok_scale;  // fp32 mode: absmax * 2^-30 per token
-  const float* sx;          // int8 mode: per-token scale
-  float* y;
-  int64_t ldy, seq;
-  int64_t cta_begin;  // first CTA of this problem
-  int ksplit, cps;    // K splits, chunks per split
+// Per operand width: m-blocks per unit (a unit is MB m-blocks x one 128-K
+// chunk, MB * 512 contiguous bytes), ring depth in units, CTAs per SM.
+template <int NB>
+struct GvCfg;
+template <>
+struct GvCfg<1> {
+  static constexpr int MB = FT_GV_MB1, DEPTH = FT_GV_DEPTH1, CTAS = FT_GV_CTAS1;
+};
+template <>
+struct GvCfg<2> {
+  static constexpr int MB = 2, DEPTH = FT_GV_DEPTH2, CTAS = 2;
 };
 
-struct GvBatch {
-  int nprob;
-  int digits;  // 4 (fp32/bf16) or 1 (int8)
-  int nb;      // n8 blocks of B (1 or 2)
-  GvProblem p[kGvMaxProblems];
+struct GvSeg {  // one activation source and the problems that read it
+  const void* x;  // [seq, K]: f32, bf16 or int8 codes
+  int64_t K;
+  int64_t units;  // sum over its problems of row-blocks x chunks
+  int32_t seq, n_chunks;
+  int32_t prob_begin, prob_end;
+  int32_t cta_begin, n_cta;
+  int32_t upp;         // units per problem when all its problems share one shape, else 0
+  int32_t unc, unrb;   // that shape's chunks and row-blocks
+};
+
+struct GvProb {
+  const uint4* codes;
+  const float* row_scales;
+  const float* sx;  // int8 mode: per-token scale
+  float* y;
+  int64_t ldy, rows;
+  int64_t unit_begin;  // first unit of this problem within its segment
+  int32_t n_chunks, n_rb;
+};
+
+struct GvParams {
+  int nseg, nprob, xkind, D;
+  int* err;  // device error word: a bounded wait that gave up records its site
+  GvSeg g[kMaxSeg];
+  GvProb p[kMaxProb];
 };
 
 __device__ __forceinline__ void mma_u8s8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
@@ -68,191 +114,50 @@ __device__ __forceinline__ void mma_u8s8(int (&c)[4], uint32_t a0, uint32_t a1, 
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// 16-byte asynchronous copy global -> shared (bypasses L1 and registers)
-__device__ __forceinline__ void cp_async16(const void* smem_dst, const void* gsrc) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
-                   (uint32_t)__cvta_generic_to_shared(smem_dst)),
-               "l"(gsrc)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() {
-  asm volatile("cp.async.commit_group;" ::: "memory");
-}
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
+// Problem / row-block / chunk cursor over a segment's units.
+struct Cursor {
+  int p;
+  int rb, c;
+};
 
-// the 4 k-steps of one 128-K chunk against the 8 fragment words of one n8 block
-__device__ __forceinline__ void chunk_mma(int (&acc)[4], const uint4 w, const uint4 b0,
-                                          const uint4 b1) {
-  const uint32_t wk[4] = {w.x, w.y, w.z, w.w};
-  const uint32_t bw[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-#pragma unroll
-  for (int ks = 0; ks < 4; ++ks) {
-    const uint32_t a0 = wk[ks] & 0x03030303u;
-    const uint32_t a1 = (wk[ks] >> 2) & 0x03030303u;
-    const uint32_t a2 = (wk[ks] >> 4) & 0x03030303u;
-    const uint32_t a3 = (wk[ks] >> 6) & 0x03030303u;
-    mma_u8s8(acc, a0, a1, a2, a3, bw[2 * ks], bw[2 * ks + 1]);
-  }
+// Problem of segment s holding unit u: arithmetic when the segment's
+// problems share one shape, else a scan of their first units.
+__device__ __forceinline__ int find_prob(const GvParams& P, const GvSeg& s, int64_t u) {
+  if (s.upp > 0) return s.prob_begin + (int)(u / s.upp);
+  int pi = s.prob_begin;
+  while (pi + 1 < s.prob_end && P.p[pi + 1].unit_begin <= u) ++pi;
+  return pi;
 }
 
-template <int NB>
-__global__ void __launch_bounds__(kGvWarps * 32, FT_GV_MIN_BLOCKS) gemv_kernel(const __grid_constant__ GvBatch b) {
-  // dynamic: [warp][kDepth][32 lanes] uint4 weight ring, then the B fragments
-  // [n_chunks][NB][32 lanes][8 words]
-  extern __shared__ __align__(16) uint4 dyn[];
-  uint32_t* frag = reinterpret_cast<uint32_t*>(dyn + kRingBytes / 16);
-  __shared__ int colsum[16];
-  __shared__ double tok_scale[4];
-
-  int pi = 0;
-  while (pi + 1 < b.nprob && b.p[pi + 1].cta_begin <= (int64_t)blockIdx.x) ++pi;
-  const GvProblem& p = b.p[pi];
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int g = lane >> 2, r = lane & 3;
-  const int S = p.ksplit;
-  const int64_t mblock = (blockIdx.x - p.cta_begin) * (kGvWarps / S) + warp / S;
-  const int split = warp % S;
-  const int64_t tile = mblock >> 3;
-  const int mb = (int)(mblock & 7);
-  const bool active = tile < p.n_tiles;
-  int64_t c0 = (int64_t)split * p.cps, c1 = c0 + p.cps;
-  if (c1 > p.n_chunks) c1 = p.n_chunks;
-  if (!active) c1 = c0;
-
-  // ---- start the weight stream: each lane copies (and later reads) only its
-  // own 16 bytes of each chunk, so the ring needs no barriers
-  const uint4* wp = p.codes + (tile * p.n_chunks) * 256 + mb * 32 + lane;
-  uint4* ring = dyn + warp * (kDepth * 32) + lane;
-#pragma unroll
-  for (int d = 0; d < kDepth; ++d) {
-    if (c0 + d < c1) cp_async16(ring + d * 32, wp + (c0 + d) * 256);
-    cp_async_commit();  // one group per chunk slot, empty past the range
-  }
-
-  // ---- the activation operand, column sums and token scales of the prep
-  tc::pdl_wait();
-  const int D = b.digits;
-  const int seq = (int)p.seq;
-  {
-    uint4* f4 = reinterpret_cast<uint4*>(frag);
-    const int n16 = (int)(p.n_chunks * NB * 64);  // 16-byte pieces
-    for (int i = tid; i < n16; i += blockDim.x) {
-      const int64_t chunk = i / (NB * 64);
-      const int rem = i % (NB * 64);  // (nb, lane, half)
-      cp_async16(f4 + i, p.bfrag + chunk * 128 + rem);
-    }
-    cp_async_commit();
-    if (tid < 16) colsum[tid] = p.colsum[tid];
-    if (tid < 4 && D == 4) tok_scale[tid] = p.tok_scale[tid];
-    // the weight ring's groups are older, so waiting for all is waiting for this one too
-    cp_async_wait<0>();
-  }
-  __syncthreads();
-
-  // ---- the weight stream against the fragments
-  int acc[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
-  const uint4* fq = reinterpret_cast<const uint4*>(frag);
-  int slot = 0;
-  for (int64_t ch = c0; ch < c1; ++ch) {
-    cp_async_wait<kDepth - 1>();  // this lane's copy of chunk ch has landed
-    const uint4 cur = ring[slot * 32];
-#pragma unroll
-    for (int nb = 0; nb < NB; ++nb) {
-      const uint4* f = fq + ((ch * NB + nb) * 32 + lane) * 2;
-      chunk_mma(acc[nb], cur, f[0], f[1]);
-    }
-    // the MMAs consumed `cur`, so the slot can be refilled
-    if (ch + kDepth < c1) cp_async16(ring + slot * 32, wp + (ch + kDepth) * 256);
-    cp_async_commit();
-    slot = slot + 1 == kDepth ? 0 : slot + 1;
-  }
-  cp_async_wait<0>();
-  __syncthreads();  // the ring is reused for the split sums below
-
-  // ---- combine the K splits of each m-block
-  if (S > 1) {
-    int(*red)[32][8] = reinterpret_cast<int(*)[32][8]>(dyn);  // [warp][lane][8], in the ring
-#pragma unroll
-    for (int nb = 0; nb < 2; ++nb)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) red[warp][lane][nb * 4 + i] = acc[nb][i];
-    __syncthreads();
-    if (split != 0) return;
-    for (int s = 1; s < S; ++s)
-#pragma unroll
-      for (int nb = 0; nb < 2; ++nb)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) acc[nb][i] += red[warp + s][lane][nb * 4 + i];
-  }
-  if (!active) return;
-
-  // ---- epilogue: acc[nb][0..1] = row g, columns 8nb + 2r, +1; [2..3] = row g + 8
-  const int64_t R0 = tile * kTileRows + 16 * mb + g;
-  if (D == 1) {
-#pragma unroll
-    for (int nb = 0; nb < NB; ++nb)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int n = 8 * nb + 2 * r + (i & 1);
-        const int64_t R = R0 + 8 * (i >> 1);
-        if (n < seq && R < p.rows) {
-          const int32_t a = acc[nb][i] - colsum[n];
-          p.y[n * p.ldy + R] = __fmul_rn(__fmul_rn((float)a, p.sx[n]), p.row_scales[R]);
-        }
-      }
+__device__ __forceinline__ Cursor cursor_at(const GvParams& P, const GvSeg& s, int64_t u) {
+  Cursor k;
+  k.p = find_prob(P, s, u);
+  if (s.upp > 0) {
+    const int rel = (int)(u - (int64_t)(k.p - s.prob_begin) * s.upp);
+    k.rb = rel / s.unc;
+    k.c = rel - k.rb * s.unc;
   } else {
-    // token t = n / 4 lives in lanes r = 2(t%2) (digits 0, 1) and r + 1 (digits 2, 3)
-#pragma unroll
-    for (int nb = 0; nb < NB; ++nb) {
-      const int hi0 = __shfl_xor_sync(0xffffffffu, acc[nb][0], 1);
-      const int hi1 = __shfl_xor_sync(0xffffffffu, acc[nb][1], 1);
-      const int hi2 = __shfl_xor_sync(0xffffffffu, acc[nb][2], 1);
-      const int hi3 = __shfl_xor_sync(0xffffffffu, acc[nb][3], 1);
-      if ((r & 1) == 0) {
-        const int t = 2 * nb + (r >> 1);
-        const int n0 = 4 * t;
-        if (t < seq) {
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int64_t R = R0 + 8 * h;
-            if (R >= p.rows) continue;
-            const long long d0 = acc[nb][2 * h] - colsum[n0];
-            const long long d1 = acc[nb][2 * h + 1] - colsum[n0 + 1];
-            const long long d2 = (h ? hi2 : hi0) - colsum[n0 + 2];
-            const long long d3 = (h ? hi3 : hi1) - colsum[n0 + 3];
-            const long long S4 = d0 + d1 * 256 + d2 * 65536 + d3 * 16777216;
-            p.y[t * p.ldy + R] = (float)((double)S4 * tok_scale[t] * (double)p.row_scales[R]);
-          }
-        }
-      }
-    }
+    const GvProb& q = P.p[k.p];
+    const int64_t rel = u - q.unit_begin;
+    k.rb = (int)(rel / q.n_chunks);
+    k.c = (int)(rel - (int64_t)k.rb * q.n_chunks);
   }
+  return k;
 }
 
-// ---------------------------------------------------------------- prep --
-// Activation operand in fragment order for the kernel above, one CTA per
-// (source, token slot): column n = slot*D + d of chunk c sits in lane
-// 4(n%8) + r, word 2ks + kk of n8 block n/8 for K = c*128 + 32ks + 16kk + 4r
-// .. +3.  fp32/bf16: the signed base-256 digits of X = round(x * 2^30 /
-// absmax(x)) (|X| <= 2^30 fits 32 bits); int8: the caller's codes.  Slots
-// past the token count write zeros.  Column sums and token scales as in
-// prep_b_kernel.
-struct FragSource {
-  const void* x;
-  uint32_t* frag;          // [n_chunks][2][32][8] words
-  int32_t* colsum;         // [16]
-  double* tok_scale;       // [4]
-  int64_t K, n_chunks, seq;
-};
-constexpr int kMaxFragSources = 64;
-constexpr int kPrepThreads = 512;
-struct FragBatch {
-  int nsrc, xkind, D, slots;  // token slots per source (8*nb / D)
-  FragSource s[kMaxFragSources];
-};
+// First unit of CTA `c` of a segment: c * units / n_cta rounded down to a
+// row-block boundary (CTA c-1 computes the same value as its end).
+__device__ __forceinline__ int64_t cta_boundary(const GvParams& P, const GvSeg& s, int64_t c) {
+  if (c <= 0) return 0;
+  if (c >= s.n_cta) return s.units;
+  const int64_t t = c * s.units / s.n_cta;
+  if (s.upp > 0) {
+    const int64_t pbase = t / s.upp * s.upp;
+    return pbase + (t - pbase) / s.unc * s.unc;
+  }
+  const GvProb& q = P.p[find_prob(P, s, t)];
+  return q.unit_begin + (t - q.unit_begin) / q.n_chunks * q.n_chunks;
+}
 
 __device__ __forceinline__ float4 load_x4(const void* x, int xkind, int64_t row, int64_t k,
                                           int64_t K) {
@@ -279,107 +184,419 @@ __device__ __forceinline__ float4 load_x4(const void* x, int xkind, int64_t row,
   return v;
 }
 
-__global__ void __launch_bounds__(kPrepThreads) prep_frag_kernel(const __grid_constant__ FragBatch fb) {
-  // let the matmul start streaming its weights, then wait for the producer of x
-  tc::pdl_launch_dependents();
-  tc::pdl_wait();
-  const int si = blockIdx.x / fb.slots, t = blockIdx.x % fb.slots;
-  const FragSource& src = fb.s[si];
-  const int D = fb.D, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const bool live = t < src.seq;
-  const int nquads = (int)(src.n_chunks * 32);
-  constexpr int kQ = 4;  // quads per thread kept in registers (K <= 8192)
-  __shared__ float red_f[kPrepThreads / 32];
-  __shared__ int red_i[kPrepThreads / 32][4];
-  uint32_t word[kQ][4];
-  int cs[4] = {0, 0, 0, 0};
-  if (D == 4) {
-    float4 xv[kQ];
-    float amax = 0.0f;
-#pragma unroll
-    for (int j = 0; j < kQ; ++j) {
-      const int qi = tid + j * kPrepThreads;
-      xv[j] = live && qi < nquads ? load_x4(src.x, fb.xkind, t, 4 * (int64_t)qi, src.K)
-                                  : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-      amax = fmaxf(amax, fmaxf(fmaxf(fabsf(xv[j].x), fabsf(xv[j].y)),
-                               fmaxf(fabsf(xv[j].z), fabsf(xv[j].w))));
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    if (lane == 0) red_f[warp] = amax;
-    __syncthreads();
-    amax = 0.0f;
-#pragma unroll
-    for (int w = 0; w < kPrepThreads / 32; ++w) amax = fmaxf(amax, red_f[w]);
-    const double mult = amax > 0.0f ? 1073741824.0 / (double)amax : 0.0;  // 2^30 / absmax
-    if (tid == 0 && live) src.tok_scale[t] = (double)amax / 1073741824.0;
-#pragma unroll
-    for (int j = 0; j < kQ; ++j) {
-      const float e4[4] = {xv[j].x, xv[j].y, xv[j].z, xv[j].w};
-      word[j][0] = word[j][1] = word[j][2] = word[j][3] = 0u;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        int X = __double2int_rn((double)e4[e] * mult);
-#pragma unroll
-        for (int d = 0; d < 3; ++d) {
-          const int lo = ((X & 0xFF) ^ 0x80) - 0x80;  // signed low digit
-          word[j][d] |= (uint32_t)(lo & 0xFF) << (8 * e);
-          cs[d] += lo;
-          X = (X - lo) >> 8;
-        }
-        word[j][3] |= (uint32_t)(X & 0xFF) << (8 * e);  // |X| <= 65 here
-        cs[3] += X;
-      }
-    }
+// Fragment word of (4 consecutive K at quad q, column n): chunk q/32, k-step
+// j = (q%32)/8, half kk = (q%8)/4, lane 4*(n%8) + q%4; stored as
+// [chunk][n/8][j/2][lane] uint4 holding words (b0, b1) of k-steps 2h, 2h+1.
+__device__ __forceinline__ int frag_word(int q, int n, int nb) {
+  const int c = q >> 5, j = (q >> 3) & 3, kk = (q >> 2) & 1, rr = q & 3;
+  const int lane = 4 * (n & 7) + rr;
+  return ((((c * nb + (n >> 3)) * 2 + (j >> 1)) * 32 + lane) << 2) + 2 * (j & 1) + kk;
+}
+
+// Weight-stream producer of one warp: walks the warp's units in order; the
+// unit (row-block rb, chunk c) is the MB m-blocks (rb % (8/MB)) * MB .. +MB-1
+// of block (rb / (8/MB), c), fetched with one bulk copy.  Offsets are in
+// uint4 from the problem's codes; the step to the next unit is +256 (next
+// chunk) within a row-block, then back to chunk 0 of the next row-block
+// (same tile) or on to the next tile.  Every lane keeps the (uniform) state;
+// lane 0 issues the copies.
+struct Producer {
+  const uint4* base;  // codes of the current problem
+  uint32_t off;       // uint4 offset of the current unit
+  int nc, nrb, rb, c, p;
+};
+
+template <int MB>
+__device__ __forceinline__ void prod_at(Producer& w, const GvParams& P, int p, int rb, int c) {
+  constexpr int RPT = 8 / MB;  // row-blocks per tile
+  const GvProb& q = P.p[p];
+  w.base = q.codes;
+  w.nc = q.n_chunks;
+  w.nrb = q.n_rb;
+  w.p = p;
+  w.rb = rb;
+  w.c = c;
+  w.off = (uint32_t)(((rb / RPT) * q.n_chunks + c) * 256 + (rb % RPT) * (MB * 32));
+}
+
+template <int MB>
+__device__ __forceinline__ void prod_next(Producer& w, const GvParams& P) {
+  constexpr int RPT = 8 / MB;
+  if (++w.c < w.nc) {
+    w.off += 256u;
   } else {
+    w.c = 0;
+    if (++w.rb < w.nrb)
+      w.off += (w.rb % RPT) ? (uint32_t)(MB * 32) - (uint32_t)(w.nc - 1) * 256u
+                            : (uint32_t)(MB * 32);
+    else if (w.p + 1 < P.nprob)
+      prod_at<MB>(w, P, w.p + 1, 0, 0);
+  }
+}
+
+// lane 0: the current unit into ring slot `dst`, completion counted on `bar`
+template <int MB>
+__device__ __forceinline__ void prod_copy(const Producer& w, uint32_t dst, uint32_t bar) {
+  tc::mbar_arrive_expect_tx(bar, MB * 512u);
+  tc::bulk_g2s(dst, w.base + w.off, MB * 512u, bar);
+}
+
+// Output of one row-block (MB m-blocks) from its exact digit sums fin:
+// fin[m][nb][e] = rows 16m + g (+8 for e >= 2), column 8nb + 2r + (e & 1).
+template <int NB, int MB>
+__device__ __forceinline__ void rowblock_store(const int (&fin)[MB][NB][4], const GvProb& q, int rb,
+                                               int seq, int D, const int* colsum,
+                                               const double* tok_scale, int g, int r) {
+  const int64_t rbase = (int64_t)rb * (16 * MB);
+  if (D == 1) {
 #pragma unroll
-    for (int j = 0; j < kQ; ++j) {
-      const int qi = tid + j * kPrepThreads;
-      uint32_t wv = 0u;
-      if (live && qi < nquads) {
-        const int8_t* q = static_cast<const int8_t*>(src.x) + (int64_t)t * src.K;
+    for (int m = 0; m < MB; ++m)
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const int64_t k = 4 * (int64_t)qi + e;
-          const int v = k < src.K ? q[k] : 0;
-          wv |= (uint32_t)(v & 0xFF) << (8 * e);
-          cs[0] += v;
+          const int col = 8 * nb + 2 * r + (e & 1);
+          const int64_t R = rbase + 16 * m + g + 8 * (e >> 1);
+          if (col < seq && R < q.rows)
+            q.y[col * q.ldy + R] = __fmul_rn(
+                __fmul_rn((float)(fin[m][nb][e] - colsum[col]), q.sx[col]), q.row_scales[R]);
+        }
+  } else {
+    // token t = col / 4 lives in lanes r = 2(t%2) (digits 0, 1) and r + 1 (digits 2, 3)
+#pragma unroll
+    for (int m = 0; m < MB; ++m)
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb) {
+        int hi[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) hi[e] = __shfl_xor_sync(0xffffffffu, fin[m][nb][e], 1);
+        const int t = 2 * nb + (r >> 1);
+        if ((r & 1) == 0 && t < seq) {
+          const int n0 = 4 * t;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int64_t R = rbase + 16 * m + g + 8 * h;
+            if (R >= q.rows) continue;
+            const long long d0 = fin[m][nb][2 * h] - colsum[n0];
+            const long long d1 = fin[m][nb][2 * h + 1] - colsum[n0 + 1];
+            const long long d2 = hi[2 * h] - colsum[n0 + 2];
+            const long long d3 = hi[2 * h + 1] - colsum[n0 + 3];
+            const long long s4 = d0 + d1 * 256 + d2 * 65536 + d3 * 16777216;
+            q.y[t * q.ldy + R] = (float)((double)s4 * tok_scale[t] * (double)q.row_scales[R]);
+          }
         }
       }
-      word[j][0] = wv;
-    }
-  }
-#pragma unroll
-  for (int j = 0; j < kQ; ++j) {
-    const int qi = tid + j * kPrepThreads;
-    if (qi >= nquads) break;
-    const int64_t chunk = qi >> 5;
-    const int kin = (qi & 31) * 4;
-    const int rr = (kin >> 2) & 3, ks = kin >> 5, kk = (kin >> 4) & 1;
-    for (int d = 0; d < D; ++d) {
-      const int n = t * D + d;
-      src.frag[((chunk * 2 + (n >> 3)) * 32 + 4 * (n & 7) + rr) * 8 + 2 * ks + kk] = word[j][d];
-    }
-  }
-  // column sums
-#pragma unroll
-  for (int d = 0; d < 4; ++d) {
-    int v = cs[d];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    if (lane == 0) red_i[warp][d] = v;
-  }
-  __syncthreads();
-  if (tid < D) {
-    int v = 0;
-#pragma unroll
-    for (int w = 0; w < kPrepThreads / 32; ++w) v += red_i[w][tid];
-    src.colsum[t * D + tid] = v;
   }
 }
 
 template <int NB>
-int launch_nb(const GvBatch& batch, int64_t ctas, size_t smem, cudaStream_t s) {
+__global__ void __launch_bounds__(kThreads, GvCfg<NB>::CTAS)
+    gemv_kernel(const __grid_constant__ GvParams P) {
+  constexpr int MB = GvCfg<NB>::MB, kDepth = GvCfg<NB>::DEPTH;
+  constexpr int kU4 = MB * 32;  // uint4 per unit
+  constexpr int kRingBytes = kW * kDepth * MB * 512;
+  extern __shared__ __align__(16) uint4 dyn[];
+  // dynamic: weight ring | partial sums [warp][NB][MB][4][32] int | fragments
+  uint4* ring = dyn;
+  int* part = reinterpret_cast<int*>(dyn + kRingBytes / 16);
+  uint32_t* frag = reinterpret_cast<uint32_t*>(part + kW * NB * MB * 128);
+  __shared__ int colsum[16];
+  __shared__ double tok_scale[4];
+  __shared__ float red_f[kW][4];
+  __shared__ int part_id[kW];
+  __shared__ __align__(8) uint64_t full_bar[kW][kDepth];
+
+  tc::pdl_launch_dependents();
+
+  int si = 0;
+  while (si + 1 < P.nseg && P.g[si + 1].cta_begin <= (int)blockIdx.x) ++si;
+  const GvSeg& S = P.g[si];
+  const int64_t cta = (int64_t)blockIdx.x - S.cta_begin;
+  const int64_t A = cta_boundary(P, S, cta), B = cta_boundary(P, S, cta + 1);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, r = lane & 3;
+  const int64_t u0 = A + (B - A) * warp / kW, u1 = A + (B - A) * (warp + 1) / kW;
+  const int n = (int)(u1 - u0);
+
+  // ---- start the weight stream: per-warp ring of kDepth unit slots, one
+  // mbarrier each (phase i / kDepth of slot i % kDepth = unit i landed)
+  uint4* const myring = ring + warp * (kDepth * kU4);
+  const uint32_t ring_s = tc::smem_u32(myring);
+  const uint32_t bar_s = tc::smem_u32(&full_bar[warp][0]);
+  const Cursor start = n > 0 ? cursor_at(P, S, u0) : Cursor{S.prob_begin, 0, 0};
+  Producer pr;
+  prod_at<MB>(pr, P, start.p, start.rb, start.c);
+  if (lane == 0) {
+#pragma unroll
+    for (int d = 0; d < kDepth; ++d) tc::mbar_init(bar_s + 8 * d, 1);
+    tc::fence_barrier_init();
+  }
+  __syncwarp();
+  int issued = 0;
+#pragma unroll
+  for (int d = 0; d < kDepth; ++d) {
+    if (issued < n) {
+      if (lane == 0) prod_copy<MB>(pr, ring_s + d * (MB * 512), bar_s + 8 * d);
+      prod_next<MB>(pr, P);
+      ++issued;
+    }
+  }
+
+  // ---- activation fragments of this CTA's segment (after the previous grid)
+  tc::pdl_wait();
+  const int D = P.D, seq = S.seq;
+  const int nquad = S.n_chunks * 32;
+  {
+    uint4* f4 = reinterpret_cast<uint4*>(frag);
+    for (int i = tid; i < S.n_chunks * NB * 64; i += kThreads) f4[i] = make_uint4(0, 0, 0, 0);
+    if (tid < 16) colsum[tid] = 0;
+    if (tid < kW) part_id[tid] = -1;
+  }
+  if (D == 1) __syncthreads();  // zero-fill above before the word stores below
+  // One token at a time: its x quads stay in registers between the absmax
+  // and the digit split (K up to 4 * kRQ * kThreads in one load).
+  constexpr int kRQ = 4;
+  for (int t = 0; t < seq; ++t) {
+    int cs[4] = {0, 0, 0, 0};
+    if (D == 4) {
+      float4 xr[kRQ];
+      float am = 0.0f;
+#pragma unroll
+      for (int j = 0; j < kRQ; ++j) {
+        const int q = tid + j * kThreads;
+        xr[j] = q < nquad ? load_x4(S.x, P.xkind, t, 4 * (int64_t)q, S.K)
+                          : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        am = fmaxf(am, fmaxf(fmaxf(fabsf(xr[j].x), fabsf(xr[j].y)),
+                             fmaxf(fabsf(xr[j].z), fabsf(xr[j].w))));
+      }
+      for (int q = tid + kRQ * kThreads; q < nquad; q += kThreads) {
+        const float4 v = load_x4(S.x, P.xkind, t, 4 * (int64_t)q, S.K);
+        am = fmaxf(am, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+      if (lane == 0) red_f[warp][t] = am;
+      __syncthreads();
+      float a = 0.0f;
+#pragma unroll
+      for (int w = 0; w < kW; ++w) a = fmaxf(a, red_f[w][t]);
+      // 2^sh puts a in [2^29, 2^30): sh = 30 - ex for a = m * 2^ex, m in [0.5, 1)
+      const uint32_t ebits = __float_as_uint(a) >> 23;
+      int sh = 0;
+      if (ebits != 0u && ebits < 255u) {
+        sh = 156 - (int)ebits;
+      } else if (a > 0.0f && ebits == 0u) {
+        int ex = 0;
+        frexpf(a, &ex);  // subnormal absmax
+        sh = 30 - ex;
+      }
+      if (tid == 0) tok_scale[t] = a > 0.0f ? __longlong_as_double((long long)(1023 - sh) << 52) : 0.0;
+      const int s1 = sh > 127 ? 127 : (sh < -126 ? -126 : sh);
+      const float f1 = __int_as_float((s1 + 127) << 23);
+      const float f2 = __int_as_float((sh - s1 + 127) << 23);
+      auto split = [&](const float4 v, int q) {
+        const float e4[4] = {v.x, v.y, v.z, v.w};
+        uint32_t wd[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          int X = __float2int_rn(__fmul_rn(__fmul_rn(e4[e], f1), f2));  // exact scaling
+#pragma unroll
+          for (int d = 0; d < 3; ++d) {
+            const int lo = ((X & 0xFF) ^ 0x80) - 0x80;  // signed low digit
+            wd[d] |= (uint32_t)(lo & 0xFF) << (8 * e);
+            cs[d] += lo;
+            X = (X - lo) >> 8;
+          }
+          wd[3] |= (uint32_t)(X & 0xFF) << (8 * e);  // |X| <= 64 here
+          cs[3] += X;
+        }
+#pragma unroll
+        for (int d = 0; d < 4; ++d) frag[frag_word(q, 4 * t + d, NB)] = wd[d];
+      };
+#pragma unroll
+      for (int j = 0; j < kRQ; ++j) {
+        const int q = tid + j * kThreads;
+        if (q < nquad) split(xr[j], q);
+      }
+      for (int q = tid + kRQ * kThreads; q < nquad; q += kThreads)
+        split(load_x4(S.x, P.xkind, t, 4 * (int64_t)q, S.K), q);
+    } else {
+      const int8_t* xq = static_cast<const int8_t*>(S.x) + (int64_t)t * S.K;
+      for (int q = tid; q < nquad; q += kThreads) {
+        const int64_t k = 4 * (int64_t)q;
+        uint32_t wv = 0u;
+        if (k + 3 < S.K && (reinterpret_cast<uintptr_t>(xq + k) & 3) == 0) {
+          wv = __ldg(reinterpret_cast<const uint32_t*>(xq + k));
+        } else {
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            if (k + e < S.K) wv |= (uint32_t)(xq[k + e] & 0xFF) << (8 * e);
+        }
+        cs[0] = __dp4a((int)wv, 0x01010101, cs[0]);
+        frag[frag_word(q, t, NB)] = wv;
+      }
+    }
+    // column sums: warp reduction, one shared atomic per warp and column
+#pragma unroll
+    for (int d = 0; d < 4; ++d) {
+      if (d >= D) break;
+      int v = cs[d];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (lane == 0) atomicAdd(&colsum[t * D + d], v);
+    }
+  }
+  __syncthreads();
+
+  // ---- the weight stream against the fragments, one row-block segment at a time
+  int acc[MB][NB][4][4];
+#pragma unroll
+  for (int m = 0; m < MB; ++m)
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        acc[m][nb][j][0] = acc[m][nb][j][1] = acc[m][nb][j][2] = acc[m][nb][j][3] = 0;
+  const uint4* const fbase = reinterpret_cast<const uint4*>(frag) + lane;
+  int slot = 0;
+  uint32_t phase = 0;
+  int consumed = 0;
+  bool ok = true;
+  int cp = start.p, crb = start.rb, c0 = start.c;
+  int left = n;
+  bool keep = false;  // the last row-block is unfinished and owned by this warp
+  while (left > 0) {
+    const int nc = P.p[cp].n_chunks;
+    const int cnt = nc - c0 < left ? nc - c0 : left;
+    const uint4* fp = fbase + c0 * (NB * 64);
+    for (int k = 0; k < cnt; ++k) {
+      ok = ok && tc::mbar_wait_sleep(bar_s + 8 * slot, phase, P.err, 60, FT_GV_SLEEP_NS);
+      if (!ok) break;
+      uint4 w[MB];
+#pragma unroll
+      for (int m = 0; m < MB; ++m) w[m] = myring[slot * kU4 + m * 32 + lane];
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb) {
+        const uint4 blo = fp[nb * 64], bhi = fp[nb * 64 + 32];
+        const uint32_t bj[4][2] = {{blo.x, blo.y}, {blo.z, blo.w}, {bhi.x, bhi.y}, {bhi.z, bhi.w}};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t M = 0x03030303u << (2 * j);
+#pragma unroll
+          for (int m = 0; m < MB; ++m)
+            mma_u8s8(acc[m][nb][j], w[m].x & M, w[m].y & M, w[m].z & M, w[m].w & M, bj[j][0],
+                     bj[j][1]);
+        }
+      }
+      ++consumed;
+      // every lane's reads of the slot are done (the MMAs took them): refill it
+      __syncwarp();
+      if (issued < n) {
+        if (lane == 0) {
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          prod_copy<MB>(pr, ring_s + slot * (MB * 512), bar_s + 8 * slot);
+        }
+        prod_next<MB>(pr, P);
+        ++issued;
+      }
+      if (++slot == kDepth) {
+        slot = 0;
+        phase ^= 1u;
+      }
+      fp += NB * 64;
+    }
+    if (!ok) break;
+    left -= cnt;
+    const bool ends = c0 + cnt == nc;  // this segment reaches the row-block's last chunk
+    int fin[MB][NB][4];
+#pragma unroll
+    for (int m = 0; m < MB; ++m)
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          fin[m][nb][e] = acc[m][nb][0][e] + (acc[m][nb][1][e] >> 2) +
+                          (acc[m][nb][2][e] >> 4) + (acc[m][nb][3][e] >> 6);
+    if (c0 != 0) {
+      // first row-block of this warp, begun by an earlier warp: hand it over
+#pragma unroll
+      for (int m = 0; m < MB; ++m)
+#pragma unroll
+        for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            part[(((warp * NB + nb) * MB + m) * 4 + e) * 32 + lane] = fin[m][nb][e];
+      if (lane == 0) part_id[warp] = (int)(P.p[cp].unit_begin + (int64_t)crb * nc);
+    } else if (ends) {
+      rowblock_store<NB, MB>(fin, P.p[cp], crb, seq, D, colsum, tok_scale, g, r);
+    } else {
+      keep = true;  // finished after the stream, with the later warps' parts
+      break;
+    }
+#pragma unroll
+    for (int m = 0; m < MB; ++m)
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          acc[m][nb][j][0] = acc[m][nb][j][1] = acc[m][nb][j][2] = acc[m][nb][j][3] = 0;
+    c0 = 0;
+    if (++crb == P.p[cp].n_rb) {
+      crb = 0;
+      ++cp;
+    }
+  }
+  if (!ok) {
+    // a wait gave up: let this warp's copies still in flight land before exiting
+    for (; consumed < issued; ++consumed) {
+      tc::mbar_wait(bar_s + 8 * slot, phase, P.err, 61);
+      if (++slot == kDepth) {
+        slot = 0;
+        phase ^= 1u;
+      }
+    }
+    keep = false;
+  }
+  __syncthreads();  // partial sums visible
+
+  if (!keep) return;
+  // ---- the row-block this warp began but did not finish: add the later warps' parts
+  const GvProb& q = P.p[cp];
+  const int id = (int)(q.unit_begin + (int64_t)crb * q.n_chunks);
+  int fin[MB][NB][4];
+#pragma unroll
+  for (int m = 0; m < MB; ++m)
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        fin[m][nb][e] = acc[m][nb][0][e] + (acc[m][nb][1][e] >> 2) + (acc[m][nb][2][e] >> 4) +
+                        (acc[m][nb][3][e] >> 6);
+  for (int w = warp + 1; w < kW; ++w) {
+    if (part_id[w] != id) continue;
+#pragma unroll
+    for (int m = 0; m < MB; ++m)
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) fin[m][nb][e] += part[(((w * NB + nb) * MB + m) * 4 + e) * 32 + lane];
+  }
+  rowblock_store<NB, MB>(fin, q, crb, seq, D, colsum, tok_scale, g, r);
+}
+
+template <int NB>
+size_t smem_for(int64_t max_chunks) {
+  constexpr int MB = GvCfg<NB>::MB, kDepth = GvCfg<NB>::DEPTH;
+  return (size_t)kW * kDepth * MB * 512 + (size_t)kW * NB * MB * 512 +
+         (size_t)max_chunks * NB * 1024;
+}
+
+size_t smem_for(int nb, int64_t max_chunks) {
+  return nb == 1 ? smem_for<1>(max_chunks) : smem_for<2>(max_chunks);
+}
+
+template <int NB>
+int launch_nb(const GvParams& P, int64_t ctas, size_t smem, cudaStream_t s) {
   static int attr_smem = 0;  // per template instance
   if ((int)smem > attr_smem) {
     FT_CUDA(cudaFuncSetAttribute(gemv_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -388,7 +605,7 @@ int launch_nb(const GvBatch& batch, int64_t ctas, size_t smem, cudaStream_t s) {
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)ctas);
-  cfg.blockDim = dim3(kGvWarps * 32);
+  cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -396,7 +613,7 @@ int launch_nb(const GvBatch& batch, int64_t ctas, size_t smem, cudaStream_t s) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  FT_CUDA(cudaLaunchKernelEx(&cfg, gemv_kernel<NB>, batch));
+  FT_CUDA(cudaLaunchKernelEx(&cfg, gemv_kernel<NB>, P));
   FT_LAUNCH_CHECK();
   return FT_OK;
 }
@@ -406,82 +623,92 @@ int launch_nb(const GvBatch& batch, int64_t ctas, size_t smem, cudaStream_t s) {
 bool gemv_fits(const ft_weight* w, int64_t seq, int xkind) {
   const int digits = xkind == 2 ? 1 : 4;
   const int64_t ncols = seq * digits;
-  if (w->format != 0 || ncols > 16) return false;
-  const int64_t nb = ncols > 8 ? 2 : 1;
-  return kRingBytes + w->n_chunks * nb * 1024 <= kGemvMaxSmem;
+  // int32 bound: the k-step-3 accumulator grows by <= 128 * 128 * 32 per chunk
+  if (w->format != 0 || ncols > 16 || w->n_chunks > 2048) return false;
+  const int nb = ncols > 8 ? 2 : 1;
+  return smem_for(nb, w->n_chunks) <= (size_t)kGemvMaxSmem;
 }
 
 int launch_gemv(ft_ctx* ctx, int nprob, const GvLaunchProblem* probs, int xkind,
                 cudaStream_t s) {
-  FT_CHECK(nprob > 0 && nprob <= kGvMaxProblems, FT_ERR_UNSUPPORTED, "bad GEMV group size");
-  static thread_local GvBatch batch;
-  batch.nprob = nprob;
-  batch.digits = xkind == 2 ? 1 : 4;
-  int64_t mblocks = 0, max_nch = 0, max_cols = 0;
-  for (int i = 0; i < nprob; ++i) {
-    mblocks += probs[i].n_tiles * 8;
-    max_nch = probs[i].n_chunks > max_nch ? probs[i].n_chunks : max_nch;
-    const int64_t nc = probs[i].seq * batch.digits;
-    max_cols = nc > max_cols ? nc : max_cols;
-  }
-  batch.nb = max_cols > 8 ? 2 : 1;
-  // K splits: enough warps for ~32 per SM, but a split keeps >= 8 chunks
-  const int64_t want_warps = (int64_t)ctx->num_sms * 32;
-  int64_t ctas = 0;
+  FT_CHECK(nprob > 0 && nprob <= kMaxProb, FT_ERR_UNSUPPORTED, "bad GEMV group size");
+  static thread_local GvParams P;
+  P.xkind = xkind;
+  P.err = ctx->err_word;
+  P.D = xkind == 2 ? 1 : 4;
+  // segments: problems grouped by activation (pointer, K, seq), first-seen order
+  int seg_of[kMaxProb];
+  int nseg = 0;
+  int64_t max_cols = 0, max_chunks = 0;
   for (int i = 0; i < nprob; ++i) {
     const GvLaunchProblem& q = probs[i];
-    GvProblem& p = batch.p[i];
-    int S = 1;
-    while (S < 8 && mblocks * S < want_warps && q.n_chunks >= 8 * S) S *= 2;
-    p.codes = reinterpret_cast<const uint4*>(q.codes);
-    p.row_scales = q.row_scales;
-    p.rows = q.rows;
-    p.n_tiles = q.n_tiles;
-    p.n_chunks = q.n_chunks;
-    p.bfrag = reinterpret_cast<const uint4*>(q.bmat);
-    p.colsum = q.colsum;
-    p.tok_scale = q.tok_scale;
-    p.sx = q.sx;
-    p.y = q.y;
-    p.ldy = q.ldy;
-    p.seq = q.seq;
-    p.ksplit = S;
-    p.cps = (int)ceil_div(q.n_chunks, S);
-    p.cta_begin = ctas;
-    ctas += ceil_div(q.n_tiles * 8, kGvWarps / S);
+    int j = 0;
+    while (j < nseg && !(P.g[j].x == q.x && P.g[j].K == q.K && P.g[j].seq == q.seq)) ++j;
+    if (j == nseg) {
+      P.g[j].x = q.x;
+      P.g[j].K = q.K;
+      P.g[j].seq = (int32_t)q.seq;
+      P.g[j].n_chunks = (int32_t)ceil_div(q.K, kChunkK);
+      ++nseg;
+    }
+    seg_of[i] = j;
+    max_cols = q.seq * P.D > max_cols ? q.seq * P.D : max_cols;
+    max_chunks = q.n_chunks > max_chunks ? q.n_chunks : max_chunks;
   }
-  FT_CHECK(ctas <= 0x7FFFFFFF, FT_ERR_UNSUPPORTED, "GEMV grid too large");
-  const size_t smem = (size_t)kRingBytes + (size_t)max_nch * batch.nb * 1024;
+  P.nseg = nseg;
+  P.nprob = nprob;
+  const int nb = max_cols > 8 ? 2 : 1;
+  const int mb = nb == 1 ? GvCfg<1>::MB : GvCfg<2>::MB;  // m-blocks per unit
+  int64_t total = 0;
+  int np = 0;
+  for (int j = 0; j < nseg; ++j) {
+    GvSeg& g = P.g[j];
+    g.prob_begin = np;
+    int64_t units = 0;
+    for (int i = 0; i < nprob; ++i) {
+      if (seg_of[i] != j) continue;
+      const GvLaunchProblem& q = probs[i];
+      GvProb& p = P.p[np++];
+      p.codes = reinterpret_cast<const uint4*>(q.codes);
+      p.row_scales = q.row_scales;
+      p.sx = q.sx;
+      p.y = q.y;
+      p.ldy = q.ldy;
+      p.rows = q.rows;
+      p.n_chunks = (int32_t)q.n_chunks;
+      p.n_rb = (int32_t)ceil_div(q.rows, 16 * mb);
+      p.unit_begin = units;
+      units += (int64_t)p.n_rb * p.n_chunks;
+    }
+    g.prob_end = np;
+    g.units = units;
+    total += units;
+    bool uni = true;
+    for (int i = g.prob_begin + 1; i < g.prob_end && uni; ++i)
+      uni = P.p[i].n_chunks == P.p[g.prob_begin].n_chunks && P.p[i].n_rb == P.p[g.prob_begin].n_rb;
+    g.unc = P.p[g.prob_begin].n_chunks;
+    g.unrb = P.p[g.prob_begin].n_rb;
+    g.upp = uni ? g.unc * g.unrb : 0;
+  }
+  FT_CHECK(total < (int64_t)1 << 31, FT_ERR_UNSUPPORTED, "GEMV group too large");
+  // CTAs per segment in proportion to its units, at least one, at most one
+  // per row-block
+  const int64_t target = (int64_t)ctx->num_sms * (nb == 1 ? GvCfg<1>::CTAS : GvCfg<2>::CTAS);
+  int64_t ctas = 0;
+  for (int j = 0; j < nseg; ++j) {
+    GvSeg& g = P.g[j];
+    int64_t rbs = 0;
+    for (int i = g.prob_begin; i < g.prob_end; ++i) rbs += P.p[i].n_rb;
+    int64_t c = (g.units * target + total / 2) / total;
+    if (c < 1) c = 1;
+    if (c > rbs) c = rbs;
+    g.cta_begin = (int32_t)ctas;
+    g.n_cta = (int32_t)c;
+    ctas += c;
+  }
+  const size_t smem = smem_for(nb, max_chunks);
   FT_CHECK(smem <= (size_t)kGemvMaxSmem, FT_ERR_UNSUPPORTED, "GEMV operand too large");
-  static_assert(kRingBytes >= kGvWarps * 32 * 8 * 4, "split sums reuse the ring");
-  return batch.nb == 1 ? launch_nb<1>(batch, ctas, smem, s) : launch_nb<2>(batch, ctas, smem, s);
-}
-
-int launch_gemv_prep(int nsrc, const GvPrepSource* srcs, int xkind, int nb, cudaStream_t s) {
-  FT_CHECK(nsrc > 0 && nsrc <= kMaxFragSources, FT_ERR_UNSUPPORTED, "bad source count");
-  static thread_local FragBatch fb;
-  fb.nsrc = nsrc;
-  fb.xkind = xkind;
-  fb.D = xkind == 2 ? 1 : 4;
-  fb.slots = 8 * nb / fb.D;
-  for (int i = 0; i < nsrc; ++i) {
-    FT_CHECK(srcs[i].n_chunks * 32 <= 4 * kPrepThreads, FT_ERR_UNSUPPORTED,
-             "K too large for the decode prep");
-    fb.s[i] = FragSource{srcs[i].x, reinterpret_cast<uint32_t*>(srcs[i].frag), srcs[i].colsum,
-                         srcs[i].tok_scale, srcs[i].K, srcs[i].n_chunks, srcs[i].seq};
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(nsrc * fb.slots));
-  cfg.blockDim = dim3(kPrepThreads);
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  FT_CUDA(cudaLaunchKernelEx(&cfg, prep_frag_kernel, fb));
-  FT_LAUNCH_CHECK();
-  return FT_OK;
+  return nb == 1 ? launch_nb<1>(P, ctas, smem, s) : launch_nb<2>(P, ctas, smem, s);
 }
 
 }  // namespace ft

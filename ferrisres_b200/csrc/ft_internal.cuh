@@ -4,18 +4,21 @@
 //   rows are grouped into tiles of 128 output channels, K into chunks of 128
 //   codes.  Block (tile t, chunk c) is 4096 contiguous bytes at offset
 //   (t * n_chunks + c) * 4096, arranged for the int8 MMA fragments of a warp:
-//       [m-block mb in 0..7][lane L in 0..31][word ks in 0..3]
-//   with L = 4g + r.  Word ks of lane (g, r) in m-block mb holds 4 quads
-//   j = 0..3 of 4 codes: byte b, bits 2j..2j+1 = code of
-//       row 16*mb + g + 8*(j & 1),  K position 32*ks + 16*(j >> 1) + 4*r + b.
-//   Shifting a word right by 2j and masking with 0x03030303 yields four
-//   unsigned bytes {0,1,2} = (w+1): exactly the A fragment register aj of an
-//   m16n8k32 MMA for k-step ks (a0/a1: rows g / g+8, k 4r..4r+3; a2/a3: the
-//   same rows, k 16+4r..16+4r+3), so one 128-bit load per lane feeds four
-//   MMAs.  A row's 128 codes of a chunk are spread over the 4 lanes (g, 0..3)
-//   of its m-block: 64 contiguous bytes.  Codes: 0 -> -1, 1 -> 0, 2 -> +1
-//   (same as the reference).  Padding rows and padding K positions hold code
-//   1 (weight 0).
+//       [m-block mb in 0..7][lane L in 0..31][word i in 0..3]
+//   with L = 4g + r.  Word i of lane (g, r) in m-block mb holds 16 codes:
+//   byte b, bits 2j..2j+1 = code of
+//       row 16*mb + g + 8*(i & 1),  K position 32*j + 16*(i >> 1) + 4*r + b,
+//   i.e. code slot j belongs to k-step j of an m16n8k32 MMA and word i is
+//   fragment register ai of it (a0/a1: rows g / g+8, k 4r..4r+3; a2/a3: the
+//   same rows, k 16+4r..16+4r+3).  So the four words AND (3 << 2j) are the
+//   A fragment of k-step j scaled by 4^j (one logic op per register; the
+//   decode kernel divides the 4^j out of its per-k-step accumulators), and
+//   (word >> 2j) & 0x03030303 are four unsigned bytes {0,1,2} = (w+1) at
+//   K-consecutive positions (the tensor-core engine's TMEM operand).  A
+//   row's 128 codes of a chunk are spread over the 4 lanes (g, 0..3) of its
+//   m-block: 64 contiguous bytes.  Codes: 0 -> -1, 1 -> 0, 2 -> +1 (same as
+//   the reference).  Padding rows and padding K positions hold code 1
+//   (weight 0).
 #pragma once
 
 #include <cuda_runtime.h>
@@ -129,28 +132,19 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
                       const void* const* xs, int xkind, const float* const* sxs, float* const* ys,
                       const int64_t* ldys, cudaStream_t s, const int64_t* seqs = nullptr);
 // Decode-shape kernel (ft_gemv.cu): dense problems whose activations fit 16
-// operand columns; prep_b_kernel writes their operand in fragment order.
-constexpr int kGemvMaxSmem = 64 * 1024;
+// operand columns; the kernel builds its activation operand itself.
+constexpr int kGemvMaxSmem = 200 * 1024;
 struct GvLaunchProblem {
   const uint8_t* codes;
   const float* row_scales;
-  int64_t rows, n_tiles, n_chunks;
-  const int8_t* bmat;  // [n_chunks][2][32 lanes][8 words]
-  const int32_t* colsum;
-  const double* tok_scale;
-  const float* sx;
+  int64_t rows, n_chunks;
+  const void* x;  // [seq, K] activations (f32, bf16 or int8 codes)
+  int64_t K, seq;
+  const float* sx;  // int8 mode: per-token scale
   float* y;
-  int64_t ldy, seq;
+  int64_t ldy;
 };
 bool gemv_fits(const ft_weight* w, int64_t seq, int xkind);
-struct GvPrepSource {
-  const void* x;
-  int8_t* frag;  // [n_chunks][2][32][32 B]
-  int32_t* colsum;
-  double* tok_scale;
-  int64_t K, n_chunks, seq;
-};
-int launch_gemv_prep(int nsrc, const GvPrepSource* srcs, int xkind, int nb, cudaStream_t s);
 int launch_gemv(ft_ctx* ctx, int nprob, const GvLaunchProblem* probs, int xkind,
                 cudaStream_t s);
 int launch_wgsl_op(const uint32_t* words, const float* scales, const float* x, float* y,

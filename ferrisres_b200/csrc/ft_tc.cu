@@ -279,7 +279,7 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
     uint32_t gb = 0, gs = 0;  // weight-block and super-stage counters
     while (cs.valid(b)) {
       const int n = cs.ss_len();
-      uint32_t wv[kSK][16];
+      uint32_t wv[kSK][8];
 #pragma unroll
       for (int j = 0; j < kSK; ++j) {
         if (j < n) {
@@ -292,14 +292,16 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
             for (int i = 0; i < 5; ++i) wv[j][i] = ok ? rw[i] : 0u;
             wv[j][5] = wv[j][6] = wv[j][7] = 0u;
           } else {
-            // row r = 16*mb + g + 8*par: lanes (g, 0..3) of m-block mb, 64 contiguous bytes
+            // row r = 16*mb + g + 8*par: lanes (g, 0..3) of m-block mb, 64 contiguous
+            // bytes; of each lane's 4 words only the two of row half par are this row's
             const uint4* blk = reinterpret_cast<const uint4*>(smem_a + sa * kBlockBytes) +
                                (r >> 4) * 32 + 4 * (r & 7);
+            const bool odd = (r >> 3) & 1;
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
               const uint4 v = ok ? blk[i] : make_uint4(0, 0, 0, 0);
-              wv[j][4 * i + 0] = v.x; wv[j][4 * i + 1] = v.y;
-              wv[j][4 * i + 2] = v.z; wv[j][4 * i + 3] = v.w;
+              wv[j][2 * i + 0] = odd ? v.y : v.x;  // K half 0 of the k-steps
+              wv[j][2 * i + 1] = odd ? v.w : v.z;  // K half 1
             }
           }
           ++gb;
@@ -326,8 +328,8 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
                 a[gg] = s_lut[v];
               }
             } else {
-              // column 8*ks' + 4*a + i (ks = 2h + ks') = word ks of lane i, quad par + 2a
-              const int par = (r >> 3) & 1;
+              // column 8*kk + 4*aa + i (K = 64h + 32kk + 16aa + 4i + b) = k-step
+              // 2h + kk (code slot) of lane i's word for K half aa
 #pragma unroll
               for (int kk = 0; kk < 2; ++kk)
 #pragma unroll
@@ -335,7 +337,7 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
 #pragma unroll
                   for (int i = 0; i < 4; ++i)
                     a[8 * kk + 4 * aa + i] =
-                        (wv[j][4 * i + 2 * h + kk] >> (2 * par + 4 * aa)) & 0x03030303u;
+                        (wv[j][2 * i + aa] >> (2 * (2 * h + kk))) & 0x03030303u;
             }
             if (ok) tc::tmem_st_x16(tmem + lane_off + kACol0 + (s * kSK + j) * 32 + 16 * h, a);
           }
@@ -771,9 +773,23 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
     live[nlive++] = i;
   }
 
-  // decode shapes run on the warp-level kernel (ft_gemv.cu)
+  // decode shapes run on the warp-level kernel (ft_gemv.cu), which builds its
+  // activation operand itself
   bool gemv = true;
   for (int q = 0; q < nlive && gemv; ++q) gemv = gemv_fits(ws[live[q]], src_seq[src_of[q]], xkind);
+  if (gemv) {
+    GvLaunchProblem gp[kMaxProblems];
+    for (int q = 0; q < nlive; ++q) {
+      const int i = live[q];
+      const ft_weight* w = ws[i];
+      const int j = src_of[q];
+      gp[q] = GvLaunchProblem{w->codes, w->row_scales, w->rows, w->n_chunks, src_x[j],
+                              src_k[j], src_seq[j], sxs ? sxs[i] : nullptr, ys[i],
+                              ldys ? ldys[i] : w->rows};
+    }
+    ctx->err_flag = ctx->err_word;
+    return launch_gemv(ctx, nlive, gp, xkind, s);
+  }
 
   // workspace: per source B operand, column sums, token scales
   size_t off = 0;
@@ -859,21 +875,8 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
   batch.err = ctx->err_word;
   ctx->err_flag = ctx->err_word;
 
-  // prep launch: the decode kernel's fragment order, or one block per source
-  // x pass x token slot of the tensor-core operand
-  if (gemv) {
-    GvPrepSource gs[kMaxSources];
-    int64_t max_cols = 0;
-    for (int j = 0; j < nsrc; ++j) {
-      gs[j] = GvPrepSource{src_x[j], reinterpret_cast<int8_t*>(wsb + b_off[j]),
-                           reinterpret_cast<int32_t*>(wsb + cs_off[j]),
-                           reinterpret_cast<double*>(wsb + ts_off[j]), src_k[j],
-                           ceil_div(src_k[j], kChunkK), src_seq[j]};
-      max_cols = src_seq[j] * D > max_cols ? src_seq[j] * D : max_cols;
-    }
-    st = launch_gemv_prep(nsrc, gs, xkind, max_cols > 8 ? 2 : 1, s);
-    if (st != FT_OK) return st;
-  } else {
+  // prep launch: one block per source x pass x token slot of the operand
+  {
     static thread_local PrepBatch pb;
     memset(&pb, 0, sizeof(pb));
     pb.nsrc = nsrc;
@@ -911,15 +914,6 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
     FT_LAUNCH_CHECK();
   }
 
-  if (gemv) {
-    GvLaunchProblem gp[kMaxProblems];
-    for (int q = 0; q < nlive; ++q) {
-      const TqProblem& p = batch.p[q];
-      gp[q] = GvLaunchProblem{p.codes, p.row_scales, p.rows, p.n_tiles, p.n_chunks, p.bmat,
-                              p.colsum, p.tok_scale, p.sx, p.y, p.ldy, p.seq};
-    }
-    return launch_gemv(ctx, nlive, gp, xkind, s);
-  }
   const int64_t grid = items < grid_target ? items : grid_target;
   if (ws[live[0]]->format == 1) {
     switch (npad) {
