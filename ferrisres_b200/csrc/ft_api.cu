@@ -177,6 +177,7 @@ int ft_ctx_destroy(ft_ctx* ctx) {
   cudaDeviceSynchronize();
   if (ctx->ws.ptr) cudaFree(ctx->ws.ptr);
   if (ctx->io.ptr) cudaFree(ctx->io.ptr);
+  if (ctx->hio.ptr) cudaFreeHost(ctx->hio.ptr);
   if (ctx->zs.ptr) cudaFree(ctx->zs.ptr);
   if (ctx->err_word) cudaFree(ctx->err_word);
   if (ctx->host_stream) cudaStreamDestroy(ctx->host_stream);
@@ -468,8 +469,9 @@ int ft_gpu_ternary_matmul_vram(ft_ctx* ctx, const ft_weight* w, const float* inp
   if (seq_len == 0) return FT_OK;
   DeviceGuard g(ctx->device);
   cudaStream_t s = ctx->host_stream;
-  size_t in_bytes = round_up(seq_len * (size_t)w->cols * sizeof(float), 256);
-  size_t out_bytes = seq_len * (size_t)w->rows * sizeof(float);
+  const size_t in_raw = seq_len * (size_t)w->cols * sizeof(float);
+  const size_t in_bytes = round_up(in_raw, 256);
+  const size_t out_bytes = seq_len * (size_t)w->rows * sizeof(float);
   // Device staging is kept in the context and only grows (no per-call malloc).
   if (ctx->io.bytes < in_bytes + out_bytes) {
     FT_CUDA(cudaStreamSynchronize(s));
@@ -479,17 +481,42 @@ int ft_gpu_ternary_matmul_vram(ft_ctx* ctx, const ft_weight* w, const float* inp
     FT_CUDA(cudaMalloc(&ctx->io.ptr, in_bytes + out_bytes));
     ctx->io.bytes = in_bytes + out_bytes;
   }
+  // Pageable host buffers go through a pinned staging buffer of the context
+  // (a host memcpy each way), so the copies stay asynchronous DMA transfers.
+  cudaPointerAttributes ai, ao;
+  const bool in_pinned = cudaPointerGetAttributes(&ai, input_host) == cudaSuccess &&
+                         ai.type == cudaMemoryTypeHost;
+  const bool out_pinned = cudaPointerGetAttributes(&ao, output_host) == cudaSuccess &&
+                          ao.type == cudaMemoryTypeHost;
+  cudaGetLastError();  // an unregistered pointer is not an error here
+  const size_t need = (in_pinned ? 0 : in_bytes) + (out_pinned ? 0 : out_bytes);
+  if (need > 0 && ctx->hio.bytes < need) {
+    FT_CUDA(cudaStreamSynchronize(s));
+    if (ctx->hio.ptr) FT_CUDA(cudaFreeHost(ctx->hio.ptr));
+    ctx->hio.ptr = nullptr;
+    ctx->hio.bytes = 0;
+    FT_CUDA(cudaHostAlloc(&ctx->hio.ptr, need, cudaHostAllocDefault));
+    ctx->hio.bytes = need;
+  }
+  const float* src = input_host;
+  if (!in_pinned) {
+    std::memcpy(ctx->hio.ptr, input_host, in_raw);
+    src = static_cast<const float*>(ctx->hio.ptr);
+  }
+  float* dst = out_pinned ? output_host
+                          : reinterpret_cast<float*>(static_cast<char*>(ctx->hio.ptr) +
+                                                     (in_pinned ? 0 : in_bytes));
   float* dx = static_cast<float*>(ctx->io.ptr);
   float* dy = reinterpret_cast<float*>(static_cast<char*>(ctx->io.ptr) + in_bytes);
-  FT_CUDA(cudaMemcpyAsync(dx, input_host, seq_len * (size_t)w->cols * sizeof(float),
-                          cudaMemcpyHostToDevice, s));
+  FT_CUDA(cudaMemcpyAsync(dx, src, in_raw, cudaMemcpyHostToDevice, s));
   int st = launch_tc_matmul(ctx, w, (int64_t)seq_len, dx, 0, nullptr, dy, s);
   if (st != FT_OK) {
     cudaStreamSynchronize(s);
     return st;
   }
-  FT_CUDA(cudaMemcpyAsync(output_host, dy, out_bytes, cudaMemcpyDeviceToHost, s));
+  FT_CUDA(cudaMemcpyAsync(dst, dy, out_bytes, cudaMemcpyDeviceToHost, s));
   FT_CUDA(cudaStreamSynchronize(s));
+  if (!out_pinned) std::memcpy(output_host, dst, out_bytes);
   return FT_OK;
 }
 

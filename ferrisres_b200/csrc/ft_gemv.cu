@@ -98,12 +98,17 @@ struct GvProb {
   int32_t n_chunks, n_rb;
 };
 
-struct GvParams {
+template <int NP>
+struct GvParamsT {
   int nseg, nprob, xkind, D;
   int* err;  // device error word: a bounded wait that gave up records its site
-  GvSeg g[kMaxSeg];
-  GvProb p[kMaxProb];
+  GvSeg g[NP];
+  GvProb p[NP];
 };
+// Host staging and the large launch; calls of <= kSmallProb problems launch
+// with a small parameter block (cheaper to launch).
+using GvParams = GvParamsT<kMaxProb>;
+constexpr int kSmallProb = 4;
 
 __device__ __forceinline__ void mma_u8s8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                          uint32_t a3, uint32_t b0, uint32_t b1) {
@@ -122,14 +127,16 @@ struct Cursor {
 
 // Problem of segment s holding unit u: arithmetic when the segment's
 // problems share one shape, else a scan of their first units.
-__device__ __forceinline__ int find_prob(const GvParams& P, const GvSeg& s, int64_t u) {
+template <class PT>
+__device__ __forceinline__ int find_prob(const PT& P, const GvSeg& s, int64_t u) {
   if (s.upp > 0) return s.prob_begin + (int)(u / s.upp);
   int pi = s.prob_begin;
   while (pi + 1 < s.prob_end && P.p[pi + 1].unit_begin <= u) ++pi;
   return pi;
 }
 
-__device__ __forceinline__ Cursor cursor_at(const GvParams& P, const GvSeg& s, int64_t u) {
+template <class PT>
+__device__ __forceinline__ Cursor cursor_at(const PT& P, const GvSeg& s, int64_t u) {
   Cursor k;
   k.p = find_prob(P, s, u);
   if (s.upp > 0) {
@@ -147,7 +154,8 @@ __device__ __forceinline__ Cursor cursor_at(const GvParams& P, const GvSeg& s, i
 
 // First unit of CTA `c` of a segment: c * units / n_cta rounded down to a
 // row-block boundary (CTA c-1 computes the same value as its end).
-__device__ __forceinline__ int64_t cta_boundary(const GvParams& P, const GvSeg& s, int64_t c) {
+template <class PT>
+__device__ __forceinline__ int64_t cta_boundary(const PT& P, const GvSeg& s, int64_t c) {
   if (c <= 0) return 0;
   if (c >= s.n_cta) return s.units;
   const int64_t t = c * s.units / s.n_cta;
@@ -206,8 +214,8 @@ struct Producer {
   int nc, nrb, rb, c, p;
 };
 
-template <int MB>
-__device__ __forceinline__ void prod_at(Producer& w, const GvParams& P, int p, int rb, int c) {
+template <int MB, class PT>
+__device__ __forceinline__ void prod_at(Producer& w, const PT& P, int p, int rb, int c) {
   constexpr int RPT = 8 / MB;  // row-blocks per tile
   const GvProb& q = P.p[p];
   w.base = q.codes;
@@ -219,8 +227,8 @@ __device__ __forceinline__ void prod_at(Producer& w, const GvParams& P, int p, i
   w.off = (uint32_t)(((rb / RPT) * q.n_chunks + c) * 256 + (rb % RPT) * (MB * 32));
 }
 
-template <int MB>
-__device__ __forceinline__ void prod_next(Producer& w, const GvParams& P) {
+template <int MB, class PT>
+__device__ __forceinline__ void prod_next(Producer& w, const PT& P) {
   constexpr int RPT = 8 / MB;
   if (++w.c < w.nc) {
     w.off += 256u;
@@ -289,9 +297,9 @@ __device__ __forceinline__ void rowblock_store(const int (&fin)[MB][NB][4], cons
   }
 }
 
-template <int NB>
+template <int NB, int NP>
 __global__ void __launch_bounds__(kThreads, GvCfg<NB>::CTAS)
-    gemv_kernel(const __grid_constant__ GvParams P) {
+    gemv_kernel(const __grid_constant__ GvParamsT<NP> P) {
   constexpr int MB = GvCfg<NB>::MB, kDepth = GvCfg<NB>::DEPTH;
   constexpr int kU4 = MB * 32;  // uint4 per unit
   constexpr int kRingBytes = kW * kDepth * MB * 512;
@@ -595,11 +603,11 @@ size_t smem_for(int nb, int64_t max_chunks) {
   return nb == 1 ? smem_for<1>(max_chunks) : smem_for<2>(max_chunks);
 }
 
-template <int NB>
-int launch_nb(const GvParams& P, int64_t ctas, size_t smem, cudaStream_t s) {
+template <int NB, int NP>
+int launch_nb(const GvParamsT<NP>& P, int64_t ctas, size_t smem, cudaStream_t s) {
   static int attr_smem = 0;  // per template instance
   if ((int)smem > attr_smem) {
-    FT_CUDA(cudaFuncSetAttribute(gemv_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    FT_CUDA(cudaFuncSetAttribute(gemv_kernel<NB, NP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)smem));
     attr_smem = (int)smem;
   }
@@ -613,9 +621,25 @@ int launch_nb(const GvParams& P, int64_t ctas, size_t smem, cudaStream_t s) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  FT_CUDA(cudaLaunchKernelEx(&cfg, gemv_kernel<NB>, P));
+  FT_CUDA(cudaLaunchKernelEx(&cfg, gemv_kernel<NB, NP>, P));
   FT_LAUNCH_CHECK();
   return FT_OK;
+}
+
+template <int NB>
+int launch_sized(const GvParams& P, int64_t ctas, size_t smem, cudaStream_t s) {
+  if (P.nprob <= kSmallProb) {
+    static thread_local GvParamsT<kSmallProb> Q;
+    Q.nseg = P.nseg;
+    Q.nprob = P.nprob;
+    Q.xkind = P.xkind;
+    Q.D = P.D;
+    Q.err = P.err;
+    for (int i = 0; i < P.nseg; ++i) Q.g[i] = P.g[i];
+    for (int i = 0; i < P.nprob; ++i) Q.p[i] = P.p[i];
+    return launch_nb<NB, kSmallProb>(Q, ctas, smem, s);
+  }
+  return launch_nb<NB, kMaxProb>(P, ctas, smem, s);
 }
 
 }  // namespace
@@ -708,7 +732,7 @@ int launch_gemv(ft_ctx* ctx, int nprob, const GvLaunchProblem* probs, int xkind,
   }
   const size_t smem = smem_for(nb, max_chunks);
   FT_CHECK(smem <= (size_t)kGemvMaxSmem, FT_ERR_UNSUPPORTED, "GEMV operand too large");
-  return nb == 1 ? launch_nb<1>(P, ctas, smem, s) : launch_nb<2>(P, ctas, smem, s);
+  return nb == 1 ? launch_sized<1>(P, ctas, smem, s) : launch_sized<2>(P, ctas, smem, s);
 }
 
 }  // namespace ft

@@ -86,6 +86,7 @@ struct ft_ctx {
   ft::Workspace ws;
   cudaStream_t host_stream = nullptr;  // used by the synchronous host-buffer calls
   ft::Workspace io;                    // device staging for the host-buffer calls
+  ft::Workspace hio;                   // pinned host staging for pageable host buffers
   ft::Workspace zs;                    // zero-initialised scratch (split-K sums, tickets)
   int* err_word = nullptr;             // device word set by a kernel whose bounded wait gave up
   int* err_flag = nullptr;             // word of the latest launch (err_word, or the static

@@ -21,7 +21,7 @@ import numpy as np
 import torch
 
 from . import _lib
-from ._lib import ShapeError, call
+from ._lib import ShapeError, call, check, lib
 
 _ctxs: dict[int, "Context"] = {}
 _ctx_lock = threading.Lock()
@@ -67,6 +67,16 @@ def _dptr(t: torch.Tensor):
     if not t.is_contiguous():
         raise ShapeError("expected a contiguous tensor")
     return C.c_void_p(t.data_ptr())
+
+
+_VRAM = None
+
+
+def _vram_fn():
+    global _VRAM
+    if _VRAM is None:
+        _VRAM = lib().ft_gpu_ternary_matmul_vram
+    return _VRAM
 
 
 def _host(a, dtype):
@@ -309,10 +319,12 @@ class GpuMatmulAccelerator:
                                 out_rows):
         if weight.cols != in_cols or weight.rows != out_rows:
             raise ShapeError("weight shape does not match in_cols/out_rows")
-        x = _host(input, np.float32)
+        x = input
+        if not (type(x) is np.ndarray and x.dtype == np.float32 and x.flags.c_contiguous):
+            x = _host(input, np.float32)
         if x.size < seq_len * in_cols:
             raise ShapeError("input too small")
         y = np.empty(seq_len * out_rows, np.float32)
-        call("ft_gpu_ternary_matmul_vram", self.ctx.handle, weight.handle,
-             x.ctypes.data_as(C.c_void_p), int(seq_len), y.ctypes.data_as(C.c_void_p))
+        check(_vram_fn()(self.ctx.handle, weight.handle, x.ctypes.data, int(seq_len),
+                         y.ctypes.data))
         return y
