@@ -25,9 +25,12 @@
 //              blocks into a 16-deep smem ring (64 KB in flight per CTA),
 //              running ahead across item boundaries.
 //   warp 5     B producer: bulk copies of the B chunks into their own ring.
-//   warps 0-3  converters: thread r reads row r's 64 bytes of the
-//              lane-major block (lanes (g, 0..3) of its m-block), unpacks,
-//              tcgen05.st into TMEM A stage s.
+//   warps 0-3 (+ 11.. for further groups) converters, in groups of 4 warps
+//              (one per TMEM sub-partition) taking alternate super-stages:
+//              a warp reads its two m-blocks of the lane-major block as two
+//              conflict-free 512-byte rows, unpacks each lane's 16 bytes and
+//              writes them with one 16x128b tcgen05.st per m-block (the store
+//              shape's lane/column map is the block's lane map).
 //   warp 6     MMA issuer: 4 x tcgen05.mma (K = 32 each) per chunk into one of
 //              two TMEM accumulators; tcgen05.commit frees stages / signals D.
 //              Also owns the TMEM allocation.
@@ -44,10 +47,23 @@
 namespace ft {
 namespace {
 
-constexpr int kSA = 16;  // smem ring of 4 KB weight blocks (64 KB in flight per CTA)
+#ifndef FT_TC_SA
+#define FT_TC_SA 16
+#endif
+#ifndef FT_TC_BBUDGET
+#define FT_TC_BBUDGET 98304
+#endif
+constexpr int kSA = FT_TC_SA;  // smem ring of 4 KB weight blocks
 constexpr int kSK = 2;   // K chunks per super-stage: one barrier wait / commit per 8 KB of weights
 constexpr int kWarpLoadA = 4, kWarpLoadB = 5, kWarpMma = 6;  // warps 0-3 convert, 7-10 epilogue
-constexpr int kThreads = 11 * 32;
+#ifndef FT_TC_CONV_GROUPS
+#define FT_TC_CONV_GROUPS 2
+#endif
+// Converter groups of 4 warps (one per TMEM sub-partition): group k converts
+// super-stages k, k + G, k + 2G, ...  A group's pass over a super-stage is a
+// long chain of waits and short latencies, so several groups work at once.
+constexpr int kConvGroups = FT_TC_CONV_GROUPS;
+constexpr int kThreads = (11 + 4 * (kConvGroups - 1)) * 32;  // extra groups are warps 11..
 constexpr int kMaxProblems = 64;
 
 struct TqProblem {
@@ -152,7 +168,7 @@ __host__ __device__ constexpr uint32_t tmem_cols_for(int npad) {
 // B-operand smem super-stages, between 2 and 8: within ~46 KB when two CTAs
 // share an SM (256 TMEM columns each), else within ~96 KB.
 __host__ __device__ constexpr int b_ss_raw(int npad) {
-  return (tmem_cols_for(npad) <= 256 ? 47104 : 98304) / (kSK * npad * 128);
+  return (tmem_cols_for(npad) <= 256 ? 47104 : FT_TC_BBUDGET) / (kSK * npad * 128);
 }
 __host__ __device__ constexpr int b_ss_for(int npad) {
   return b_ss_raw(npad) < 2 ? 2 : b_ss_raw(npad) > 8 ? 8 : b_ss_raw(npad);
@@ -270,16 +286,25 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
   const uint32_t tmem = tmem_base_sh;
   bool ok = true;
 
-  if (warp < 4) {
+  if (warp < 4 || warp >= 11) {
     // ------------------------------------------------------ converters --
-    const int r = threadIdx.x;  // warp w may only touch TMEM lanes 32w..32w+31
-    const uint32_t lane_off = (uint32_t)(32 * warp) << 16;
+    const int cgroup = warp < 4 ? 0 : 1 + (warp - 11) / 4;
+    const int sub = warp & 3;       // warp w may only touch TMEM lanes 32(w%4)..+31
+    const int r = sub * 32 + lane;  // the tile row (TMEM lane) this thread converts
+    const uint32_t lane_off = (uint32_t)(32 * sub) << 16;
     Cursor cs;
     cs.start(b);
     uint32_t gb = 0, gs = 0;  // weight-block and super-stage counters
+    // this group's first super-stage
+    for (int k = 0; k < cgroup && cs.valid(b); ++k) {
+      gb += (uint32_t)cs.ss_len();
+      ++gs;
+      cs.advance_ss(b);
+    }
     while (cs.valid(b)) {
       const int n = cs.ss_len();
-      uint32_t wv[kSK][8];
+      uint32_t wv[kSK][8];  // 2:4 sparse: row r's 5 words per chunk
+      uint4 wd[kSK][2];     // dense: this lane's 16 bytes of m-blocks 2*sub and 2*sub+1
 #pragma unroll
       for (int j = 0; j < kSK; ++j) {
         if (j < n) {
@@ -292,17 +317,11 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
             for (int i = 0; i < 5; ++i) wv[j][i] = ok ? rw[i] : 0u;
             wv[j][5] = wv[j][6] = wv[j][7] = 0u;
           } else {
-            // row r = 16*mb + g + 8*par: lanes (g, 0..3) of m-block mb, 64 contiguous
-            // bytes; of each lane's 4 words only the two of row half par are this row's
-            const uint4* blk = reinterpret_cast<const uint4*>(smem_a + sa * kBlockBytes) +
-                               (r >> 4) * 32 + 4 * (r & 7);
-            const bool odd = (r >> 3) & 1;
+            // the warp reads its two m-blocks as 2 x 512 contiguous bytes
+            const uint4* blk = reinterpret_cast<const uint4*>(smem_a + sa * kBlockBytes);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const uint4 v = ok ? blk[i] : make_uint4(0, 0, 0, 0);
-              wv[j][2 * i + 0] = odd ? v.y : v.x;  // K half 0 of the k-steps
-              wv[j][2 * i + 1] = odd ? v.w : v.z;  // K half 1
-            }
+            for (int m = 0; m < 2; ++m)
+              wd[j][m] = ok ? blk[(2 * sub + m) * 32 + lane] : make_uint4(0, 0, 0, 0);
           }
           ++gb;
         }
@@ -315,10 +334,11 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
 #pragma unroll
       for (int j = 0; j < kSK; ++j) {
         if (j < n) {
+          const uint32_t col = kACol0 + (s * kSK + j) * 32;
+          if (kSparse) {
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {  // two halves of 64 codes: 16 TMEM columns each
-            uint32_t a[16];
-            if (kSparse) {
+            for (int h = 0; h < 2; ++h) {  // two halves of 64 codes: 16 TMEM columns each
+              uint32_t a[16];
 #pragma unroll
               for (int gg = 0; gg < 16; ++gg) {  // group g covers K 4g..4g+3 = TMEM column g
                 const int bit = 5 * (h * 16 + gg);
@@ -327,19 +347,23 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
                                             : __funnelshift_r(wv[j][wi], wv[j][wi + 1], sh) & 31u;
                 a[gg] = s_lut[v];
               }
-            } else {
-              // column 8*kk + 4*aa + i (K = 64h + 32kk + 16aa + 4i + b) = k-step
-              // 2h + kk (code slot) of lane i's word for K half aa
-#pragma unroll
-              for (int kk = 0; kk < 2; ++kk)
-#pragma unroll
-                for (int aa = 0; aa < 2; ++aa)
-#pragma unroll
-                  for (int i = 0; i < 4; ++i)
-                    a[8 * kk + 4 * aa + i] =
-                        (wv[j][2 * i + aa] >> (2 * (2 * h + kk))) & 0x03030303u;
+              if (ok) tc::tmem_st_x16(tmem + lane_off + col + 16 * h, a);
             }
-            if (ok) tc::tmem_st_x16(tmem + lane_off + kACol0 + (s * kSK + j) * 32 + 16 * h, a);
+          } else {
+            // Lane (g, r) of an m-block holds word i of k-step j's fragment:
+            // row g + 8(i&1), TMEM column 8j + 4(i>>1) + r = the 16x128b
+            // store's register 4j + i.  One store per m-block.
+#pragma unroll
+            for (int m = 0; m < 2; ++m) {
+              const uint32_t w4[4] = {wd[j][m].x, wd[j][m].y, wd[j][m].z, wd[j][m].w};
+              uint32_t a[16];
+#pragma unroll
+              for (int kj = 0; kj < 4; ++kj)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) a[4 * kj + i] = (w4[i] >> (2 * kj)) & 0x03030303u;
+              if (ok)
+                tc::tmem_st_16x128b_x8(tmem + ((uint32_t)(32 * sub + 16 * m) << 16) + col, a);
+            }
           }
         }
       }
@@ -359,6 +383,12 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
       if (lane == 0) tc::mbar_arrive(tc::smem_u32(&bar_afull[s]));
       ++gs;
       cs.advance_ss(b);
+      // skip the other groups' super-stages
+      for (int k = 1; k < kConvGroups && cs.valid(b); ++k) {
+        gb += (uint32_t)cs.ss_len();
+        ++gs;
+        cs.advance_ss(b);
+      }
     }
   } else if (warp == kWarpLoadA) {
     // ------------------------------------------- weight-block producer --
