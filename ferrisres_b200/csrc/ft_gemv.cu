@@ -62,7 +62,7 @@ namespace {
 #endif
 constexpr int kW = FT_GV_WARPS;
 constexpr int kThreads = kW * 32;
-constexpr int kMaxSeg = 64, kMaxProb = 64;
+constexpr int kMaxProb = 64;
 
 // Per operand width: m-blocks per unit (a unit is MB m-blocks x one 128-K
 // chunk, MB * 512 contiguous bytes), ring depth in units, CTAs per SM.
@@ -80,7 +80,8 @@ struct GvCfg<2> {
 struct GvSeg {  // one activation source and the problems that read it
   const void* x;  // [seq, K]: f32, bf16 or int8 codes
   int64_t K;
-  int64_t units;  // sum over its problems of row-blocks x chunks
+  int32_t units;         // sum over its problems of row-blocks x chunks (< 2^31)
+  int32_t q_cta, r_cta;  // units / n_cta, units % n_cta: CTA c starts near c*q + min(c, r)
   int32_t seq, n_chunks;
   int32_t prob_begin, prob_end;
   int32_t cta_begin, n_cta;
@@ -94,7 +95,7 @@ struct GvProb {
   const float* sx;  // int8 mode: per-token scale
   float* y;
   int64_t ldy, rows;
-  int64_t unit_begin;  // first unit of this problem within its segment
+  int32_t unit_begin;  // first unit of this problem within its segment
   int32_t n_chunks, n_rb;
 };
 
@@ -128,7 +129,7 @@ struct Cursor {
 // Problem of segment s holding unit u: arithmetic when the segment's
 // problems share one shape, else a scan of their first units.
 template <class PT>
-__device__ __forceinline__ int find_prob(const PT& P, const GvSeg& s, int64_t u) {
+__device__ __forceinline__ int find_prob(const PT& P, const GvSeg& s, int u) {
   if (s.upp > 0) return s.prob_begin + (int)(u / s.upp);
   int pi = s.prob_begin;
   while (pi + 1 < s.prob_end && P.p[pi + 1].unit_begin <= u) ++pi;
@@ -136,31 +137,32 @@ __device__ __forceinline__ int find_prob(const PT& P, const GvSeg& s, int64_t u)
 }
 
 template <class PT>
-__device__ __forceinline__ Cursor cursor_at(const PT& P, const GvSeg& s, int64_t u) {
+__device__ __forceinline__ Cursor cursor_at(const PT& P, const GvSeg& s, int u) {
   Cursor k;
   k.p = find_prob(P, s, u);
   if (s.upp > 0) {
-    const int rel = (int)(u - (int64_t)(k.p - s.prob_begin) * s.upp);
+    const int rel = u - (k.p - s.prob_begin) * s.upp;
     k.rb = rel / s.unc;
     k.c = rel - k.rb * s.unc;
   } else {
     const GvProb& q = P.p[k.p];
-    const int64_t rel = u - q.unit_begin;
-    k.rb = (int)(rel / q.n_chunks);
-    k.c = (int)(rel - (int64_t)k.rb * q.n_chunks);
+    const int rel = u - q.unit_begin;
+    k.rb = rel / q.n_chunks;
+    k.c = rel - k.rb * q.n_chunks;
   }
   return k;
 }
 
-// First unit of CTA `c` of a segment: c * units / n_cta rounded down to a
-// row-block boundary (CTA c-1 computes the same value as its end).
+// First unit of CTA `c` of a segment: c * q + min(c, r) (an even split of
+// the units) rounded down to a row-block boundary; CTA c-1 computes the same
+// value as its end.  32-bit arithmetic (segments have fewer than 2^31 units).
 template <class PT>
-__device__ __forceinline__ int64_t cta_boundary(const PT& P, const GvSeg& s, int64_t c) {
+__device__ __forceinline__ int cta_boundary(const PT& P, const GvSeg& s, int c) {
   if (c <= 0) return 0;
   if (c >= s.n_cta) return s.units;
-  const int64_t t = c * s.units / s.n_cta;
+  const int t = c * s.q_cta + (c < s.r_cta ? c : s.r_cta);
   if (s.upp > 0) {
-    const int64_t pbase = t / s.upp * s.upp;
+    const int pbase = t / s.upp * s.upp;
     return pbase + (t - pbase) / s.unc * s.unc;
   }
   const GvProb& q = P.p[find_prob(P, s, t)];
@@ -319,11 +321,11 @@ __global__ void __launch_bounds__(kThreads, GvCfg<NB>::CTAS)
   int si = 0;
   while (si + 1 < P.nseg && P.g[si + 1].cta_begin <= (int)blockIdx.x) ++si;
   const GvSeg& S = P.g[si];
-  const int64_t cta = (int64_t)blockIdx.x - S.cta_begin;
-  const int64_t A = cta_boundary(P, S, cta), B = cta_boundary(P, S, cta + 1);
+  const int cta = (int)blockIdx.x - S.cta_begin;
+  const int A = cta_boundary(P, S, cta), B = cta_boundary(P, S, cta + 1);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, r = lane & 3;
-  const int64_t u0 = A + (B - A) * warp / kW, u1 = A + (B - A) * (warp + 1) / kW;
+  const int u0 = A + (int)((int64_t)(B - A) * warp / kW), u1 = A + (int)((int64_t)(B - A) * (warp + 1) / kW);
   const int n = (int)(u1 - u0);
 
   // ---- start the weight stream: per-warp ring of kDepth unit slots, one
@@ -534,7 +536,7 @@ __global__ void __launch_bounds__(kThreads, GvCfg<NB>::CTAS)
 #pragma unroll
           for (int e = 0; e < 4; ++e)
             part[(((warp * NB + nb) * MB + m) * 4 + e) * 32 + lane] = fin[m][nb][e];
-      if (lane == 0) part_id[warp] = (int)(P.p[cp].unit_begin + (int64_t)crb * nc);
+      if (lane == 0) part_id[warp] = P.p[cp].unit_begin + crb * nc;
     } else if (ends) {
       rowblock_store<NB, MB>(fin, P.p[cp], crb, seq, D, colsum, tok_scale, g, r);
     } else {
@@ -570,7 +572,7 @@ __global__ void __launch_bounds__(kThreads, GvCfg<NB>::CTAS)
   if (!keep) return;
   // ---- the row-block this warp began but did not finish: add the later warps' parts
   const GvProb& q = P.p[cp];
-  const int id = (int)(q.unit_begin + (int64_t)crb * q.n_chunks);
+  const int id = q.unit_begin + crb * q.n_chunks;
   int fin[MB][NB][4];
 #pragma unroll
   for (int m = 0; m < MB; ++m)
@@ -701,11 +703,11 @@ int launch_gemv(ft_ctx* ctx, int nprob, const GvLaunchProblem* probs, int xkind,
       p.rows = q.rows;
       p.n_chunks = (int32_t)q.n_chunks;
       p.n_rb = (int32_t)ceil_div(q.rows, 16 * mb);
-      p.unit_begin = units;
+      p.unit_begin = (int32_t)units;
       units += (int64_t)p.n_rb * p.n_chunks;
     }
     g.prob_end = np;
-    g.units = units;
+    g.units = (int32_t)units;
     total += units;
     bool uni = true;
     for (int i = g.prob_begin + 1; i < g.prob_end && uni; ++i)
@@ -723,11 +725,13 @@ int launch_gemv(ft_ctx* ctx, int nprob, const GvLaunchProblem* probs, int xkind,
     GvSeg& g = P.g[j];
     int64_t rbs = 0;
     for (int i = g.prob_begin; i < g.prob_end; ++i) rbs += P.p[i].n_rb;
-    int64_t c = (g.units * target + total / 2) / total;
+    int64_t c = ((int64_t)g.units * target + total / 2) / total;
     if (c < 1) c = 1;
     if (c > rbs) c = rbs;
     g.cta_begin = (int32_t)ctas;
     g.n_cta = (int32_t)c;
+    g.q_cta = (int32_t)(g.units / c);
+    g.r_cta = (int32_t)(g.units % c);
     ctas += c;
   }
   const size_t smem = smem_for(nb, max_chunks);
