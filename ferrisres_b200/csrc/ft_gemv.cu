@@ -404,24 +404,27 @@ __global__ void __launch_bounds__(kThreads, GvCfg<NB>::CTAS)
       const int s1 = sh > 127 ? 127 : (sh < -126 ? -126 : sh);
       const float f1 = __int_as_float((s1 + 127) << 23);
       const float f2 = __int_as_float((sh - s1 + 127) << 23);
+      // X = round(x * 2^sh), |X| < 2^30.  With U = X + 0x808080 the low three
+      // bytes of U are the low signed base-256 digits + 128 and the top byte
+      // is the top digit (|.| <= 64): byte permutes gather digit d of the four
+      // elements into word d, the XOR re-signs the low three.
       auto split = [&](const float4 v, int q) {
-        const float e4[4] = {v.x, v.y, v.z, v.w};
-        uint32_t wd[4] = {0u, 0u, 0u, 0u};
+        const uint32_t u0 = (uint32_t)__float2int_rn(__fmul_rn(__fmul_rn(v.x, f1), f2)) + 0x808080u;
+        const uint32_t u1 = (uint32_t)__float2int_rn(__fmul_rn(__fmul_rn(v.y, f1), f2)) + 0x808080u;
+        const uint32_t u2 = (uint32_t)__float2int_rn(__fmul_rn(__fmul_rn(v.z, f1), f2)) + 0x808080u;
+        const uint32_t u3 = (uint32_t)__float2int_rn(__fmul_rn(__fmul_rn(v.w, f1), f2)) + 0x808080u;
+        const uint32_t lo01 = __byte_perm(u0, u1, 0x5140), lo23 = __byte_perm(u2, u3, 0x5140);
+        const uint32_t hi01 = __byte_perm(u0, u1, 0x7362), hi23 = __byte_perm(u2, u3, 0x7362);
+        const uint32_t wd[4] = {__byte_perm(lo01, lo23, 0x5410) ^ 0x80808080u,
+                                __byte_perm(lo01, lo23, 0x7632) ^ 0x80808080u,
+                                __byte_perm(hi01, hi23, 0x5410) ^ 0x80808080u,
+                                __byte_perm(hi01, hi23, 0x7632)};
+        const int base = frag_word(q, 4 * t, NB);  // digit d: lane + 4d, word + 16d
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          int X = __float2int_rn(__fmul_rn(__fmul_rn(e4[e], f1), f2));  // exact scaling
-#pragma unroll
-          for (int d = 0; d < 3; ++d) {
-            const int lo = ((X & 0xFF) ^ 0x80) - 0x80;  // signed low digit
-            wd[d] |= (uint32_t)(lo & 0xFF) << (8 * e);
-            cs[d] += lo;
-            X = (X - lo) >> 8;
-          }
-          wd[3] |= (uint32_t)(X & 0xFF) << (8 * e);  // |X| <= 64 here
-          cs[3] += X;
+        for (int d = 0; d < 4; ++d) {
+          cs[d] = __dp4a((int)wd[d], 0x01010101, cs[d]);
+          frag[base + 16 * d] = wd[d];
         }
-#pragma unroll
-        for (int d = 0; d < 4; ++d) frag[frag_word(q, 4 * t + d, NB)] = wd[d];
       };
 #pragma unroll
       for (int j = 0; j < kRQ; ++j) {
