@@ -14,15 +14,16 @@
 // each byte belongs to k-step j, so the A fragment of k-step j is the loaded
 // word AND (3 << 2j): one logic op per fragment register, no shifts.  The
 // factor 4^j this leaves in the operand is divided out exactly at the end:
-// each k-step has its own accumulator.  Each lane copies its 16-byte pieces
-// into a private cp.async ring (no barriers needed: a lane only reads what it
-// copied) and a warp works on two m-blocks (32 rows) at a time, so one read
-// of the activation fragments feeds 8 MMAs.
+// each k-step has its own accumulator.  A unit is MB m-blocks (16 * MB
+// rows) of one chunk, MB * 512 contiguous bytes, fetched by one bulk copy
+// into the warp's ring (one mbarrier per slot, bounded waits); one read of
+// the activation fragments feeds 4 * MB MMAs per operand block.
 //
 // Activation fragments are built by every CTA in its own shared memory (no
-// separate prep launch): one pass for the token absmax, one for the digits.
+// separate prep launch): the token's x is loaded once, its absmax reduced
+// over the CTA, then split into digits.
 //
-// Work split: a unit is (row-block of 32 rows, chunk of 128 K).  Problems
+// Work split: a unit is (row-block of 16 * MB rows, chunk of 128 K).  Problems
 // sharing an activation form a segment; a segment's units are split into
 // row-block-aligned ranges, one per CTA, and a CTA's range is split evenly
 // across its warps at unit granularity.  A row-block cut by a warp boundary

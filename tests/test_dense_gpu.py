@@ -122,6 +122,58 @@ def test_grouped_i8_bit_exact(gpu):
         assert_bits_equal(y.cpu().numpy(), ref, what="grouped i8")
 
 
+@pytest.mark.parametrize("seq,mode", [(1, "f32"), (3, "f32"), (2, "i8"), (9, "i8")])
+def test_grouped_large(gpu, seq, mode):
+    """A large group in one launch: 44 weights over four activations (four
+    segments, CTAs split among them by work), ragged row counts, both operand
+    widths, run twice."""
+    rng = np.random.default_rng(90 + seq)
+    kinds = [(5632, 2048)] * 4 + [(1000, 2048), (2050, 1408), (129, 70)]
+    mats = [ternary_matrix(rng, r, c) for r, c in kinds]
+    scales = [rng.uniform(0.01, 0.1, r).astype(np.float32) for r, _ in kinds]
+    acts = {}
+    for key, cols in [(0, 2048), (1, 2048), (2, 1408), (3, 70)]:
+        x = rng.standard_normal(seq * cols).astype(np.float32)
+        if mode == "i8":
+            q, sx = fo.quantize_absmax_i8(x, seq, cols)
+            acts[key] = (x, q, sx, torch.from_numpy(q).cuda().view(seq, cols),
+                         torch.from_numpy(sx).cuda())
+        else:
+            acts[key] = (x, None, None, torch.from_numpy(x).cuda().view(seq, cols), None)
+    plan = [(i % 4, i % 2) for i in range(32)] + [(4, 0), (4, 1)] * 2 + [(5, 2)] * 6 + [(6, 3)] * 2
+    uploaded = [gpu.DeviceTernaryWeight.from_packed_u8(fo.pack_ternary(t), r, c, s)
+                for t, (r, c), s in zip(mats, kinds, scales)]
+    refs = {}
+    ws, xs, sxs, ys, conds = [], [], [], [], []
+    for m, a in plan:
+        rows, cols = kinds[m]
+        x, q, sx, xt, sxt = acts[a]
+        if (m, a) not in refs:
+            if mode == "i8":
+                refs[(m, a)] = fo.ternary_matmul_i8(mats[m], q, sx, scales[m], seq, cols, rows)
+            else:
+                refs[(m, a)] = np.concatenate(
+                    [fo.ternary_matmul(mats[m], 1.0, x[s * cols:(s + 1) * cols], rows, cols, 1)
+                     * scales[m] for s in range(seq)])
+        ws.append(uploaded[m])
+        xs.append(xt)
+        sxs.append(sxt)
+        ys.append(torch.full((seq, rows), float("nan"), device="cuda"))
+        conds.append(None if mode == "i8" else condition(mats[m], x, rows, cols, seq, scales[m]))
+    for rep in range(2):
+        for y in ys:
+            y.fill_(float("nan"))
+        if mode == "i8":
+            gpu.GroupCall(ws, xs, ys, qs_sx=sxs)()
+        else:
+            gpu.GroupCall(ws, xs, ys)()
+        for i, ((m, a), y) in enumerate(zip(plan, ys)):
+            if mode == "i8":
+                assert_bits_equal(y.cpu().numpy(), refs[(m, a)], what=f"large i8 #{i} rep {rep}")
+            else:
+                assert_fp32_close(y.cpu().numpy(), refs[(m, a)], conds[i], what=f"large #{i} rep {rep}")
+
+
 def test_no_kernel_timeouts(gpu):
     """Run after the others in this module: no bounded wait inside a kernel gave up."""
     gpu.get_context().check()
