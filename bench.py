@@ -457,7 +457,8 @@ S_N, S_K = 14336, 4096
 
 def run_sparse(args, ws, rank, local):
     """2:4 sparse ternary matmul, K=4096, N=14336, fp32 x,
-    at M=1 (bandwidth-bound GEMV, grouped launches of min(--group, 16)) and M=64.
+    at M=1 (bandwidth-bound decode GEMV kernel, grouped launches of min(--group, 16))
+    and M=64 (tensor-core engine).
     Weights enter in the reference SparseTernaryMatrix layout and are stored
     at 1.25 bits/weight; copies rotate beyond 2x L2."""
     import numpy as np
@@ -535,7 +536,7 @@ def run_sparse(args, ws, rank, local):
                      "algorithmic_bytes_per_gemv": algo, "traffic": None},
         "m64": {"ms": round(sec64 * 1e3, 4), "TOPS_nonzero": round(2 * 64 * S_N * S_K / 2 / sec64 / 1e12, 2),
                 "GBps_weights": round(dev_bytes / sec64 / 1e9, 1)},
-        "gpu_launches": int(reps * len(calls) * 2),
+        "gpu_launches": int(reps * len(calls)),  # one decode-GEMV launch per grouped call
         "clocks": clocks,
     }
 

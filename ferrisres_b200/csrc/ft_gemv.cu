@@ -78,6 +78,24 @@ struct GvCfg<2> {
   static constexpr int MB = 2, DEPTH = FT_GV_DEPTH2, CTAS = 2;
 };
 
+// 2:4 sparse weights: an m-block of one chunk is 16 rows x 20 bytes (32
+// five-bit group codes per row), 320 contiguous bytes; the ring is deepened so
+// that about as many bytes are in flight per warp as for dense units.
+#ifndef FT_GV_SPDEPTH1
+#define FT_GV_SPDEPTH1 6
+#endif
+#ifndef FT_GV_SPDEPTH2
+#define FT_GV_SPDEPTH2 12
+#endif
+template <int NB, bool SP>
+struct GvUnit {
+  static constexpr int MB = GvCfg<NB>::MB, CTAS = GvCfg<NB>::CTAS;
+  static constexpr int DEPTH = SP ? (NB == 1 ? FT_GV_SPDEPTH1 : FT_GV_SPDEPTH2) : GvCfg<NB>::DEPTH;
+  static constexpr int MU = SP ? 20 : 32;    // uint4 per m-block of one chunk
+  static constexpr int BU = SP ? 160 : 256;  // uint4 per block (tile, chunk)
+  static constexpr uint32_t BYTES = MB * MU * 16;  // one unit
+};
+
 struct GvSeg {  // one activation source and the problems that read it
   const void* x;  // [seq, K]: f32, bf16 or int8 codes
   int64_t K;
@@ -198,7 +216,19 @@ __device__ __forceinline__ float4 load_x4(const void* x, int xkind, int64_t row,
 // Fragment word of (4 consecutive K at quad q, column n): chunk q/32, k-step
 // j = (q%32)/8, half kk = (q%8)/4, lane 4*(n%8) + q%4; stored as
 // [chunk][n/8][j/2][lane] uint4 holding words (b0, b1) of k-steps 2h, 2h+1.
+//
+// 2:4 sparse weights use another K order inside a chunk (A and B only need to
+// agree): MMA lane r's A registers of k-step j hold groups (quads) 8r + 2j and
+// 8r + 2j + 1, so a lane decodes 8 consecutive group codes of a row.  The B
+// word of quad q = 8r + 4h + e (e = 0..3) for column n is word e of the uint4
+// at [chunk][n/8][h][4 * (n % 8) + r].
+template <bool SP>
 __device__ __forceinline__ int frag_word(int q, int n, int nb) {
+  if (SP) {
+    const int c = q >> 5, rr = (q >> 3) & 3, h = (q >> 2) & 1, e = q & 3;
+    const int lane = 4 * (n & 7) + rr;
+    return ((((c * nb + (n >> 3)) * 2 + h) * 32 + lane) << 2) + e;
+  }
   const int c = q >> 5, j = (q >> 3) & 3, kk = (q >> 2) & 1, rr = q & 3;
   const int lane = 4 * (n & 7) + rr;
   return ((((c * nb + (n >> 3)) * 2 + (j >> 1)) * 32 + lane) << 2) + 2 * (j & 1) + kk;
@@ -217,9 +247,10 @@ struct Producer {
   int nc, nrb, rb, c, p;
 };
 
-template <int MB, class PT>
+template <int MB, bool SP, class PT>
 __device__ __forceinline__ void prod_at(Producer& w, const PT& P, int p, int rb, int c) {
   constexpr int RPT = 8 / MB;  // row-blocks per tile
+  constexpr int MU = SP ? 20 : 32, BU = SP ? 160 : 256;
   const GvProb& q = P.p[p];
   w.base = q.codes;
   w.nc = q.n_chunks;
@@ -227,29 +258,30 @@ __device__ __forceinline__ void prod_at(Producer& w, const PT& P, int p, int rb,
   w.p = p;
   w.rb = rb;
   w.c = c;
-  w.off = (uint32_t)(((rb / RPT) * q.n_chunks + c) * 256 + (rb % RPT) * (MB * 32));
+  w.off = (uint32_t)(((rb / RPT) * q.n_chunks + c) * BU + (rb % RPT) * (MB * MU));
 }
 
-template <int MB, class PT>
+template <int MB, bool SP, class PT>
 __device__ __forceinline__ void prod_next(Producer& w, const PT& P) {
   constexpr int RPT = 8 / MB;
+  constexpr uint32_t MU = SP ? 20 : 32, BU = SP ? 160 : 256;
   if (++w.c < w.nc) {
-    w.off += 256u;
+    w.off += BU;
   } else {
     w.c = 0;
     if (++w.rb < w.nrb)
-      w.off += (w.rb % RPT) ? (uint32_t)(MB * 32) - (uint32_t)(w.nc - 1) * 256u
-                            : (uint32_t)(MB * 32);
+      w.off += (w.rb % RPT) ? MB * MU - (uint32_t)(w.nc - 1) * BU : MB * MU;
     else if (w.p + 1 < P.nprob)
-      prod_at<MB>(w, P, w.p + 1, 0, 0);
+      prod_at<MB, SP>(w, P, w.p + 1, 0, 0);
   }
 }
 
 // lane 0: the current unit into ring slot `dst`, completion counted on `bar`
-template <int MB>
+template <int MB, bool SP>
 __device__ __forceinline__ void prod_copy(const Producer& w, uint32_t dst, uint32_t bar) {
-  tc::mbar_arrive_expect_tx(bar, MB * 512u);
-  tc::bulk_g2s(dst, w.base + w.off, MB * 512u, bar);
+  constexpr uint32_t bytes = MB * (SP ? 320u : 512u);
+  tc::mbar_arrive_expect_tx(bar, bytes);
+  tc::bulk_g2s(dst, w.base + w.off, bytes, bar);
 }
 
 // Output of one row-block (MB m-blocks) from its exact digit sums fin:
@@ -300,12 +332,13 @@ __device__ __forceinline__ void rowblock_store(const int (&fin)[MB][NB][4], cons
   }
 }
 
-template <int NB, int NP>
+template <int NB, int NP, bool SP>
 __global__ void __launch_bounds__(kThreads, GvCfg<NB>::CTAS)
     gemv_kernel(const __grid_constant__ GvParamsT<NP> P) {
-  constexpr int MB = GvCfg<NB>::MB, kDepth = GvCfg<NB>::DEPTH;
-  constexpr int kU4 = MB * 32;  // uint4 per unit
-  constexpr int kRingBytes = kW * kDepth * MB * 512;
+  using U = GvUnit<NB, SP>;
+  constexpr int MB = U::MB, kDepth = U::DEPTH;
+  constexpr int kU4 = MB * U::MU;  // uint4 per unit
+  constexpr int kRingBytes = kW * kDepth * (int)U::BYTES;
   extern __shared__ __align__(16) uint4 dyn[];
   // dynamic: weight ring | partial sums [warp][NB][MB][4][32] int | fragments
   uint4* ring = dyn;
@@ -315,6 +348,7 @@ __global__ void __launch_bounds__(kThreads, GvCfg<NB>::CTAS)
   __shared__ double tok_scale[4];
   __shared__ float red_f[kW][4];
   __shared__ int part_id[kW];
+  __shared__ uint32_t s_lut[SP ? 32 : 1];  // 2:4 group code -> A register (bytes w + 1)
   __shared__ __align__(8) uint64_t full_bar[kW][kDepth];
 
   tc::pdl_launch_dependents();
@@ -336,7 +370,7 @@ __global__ void __launch_bounds__(kThreads, GvCfg<NB>::CTAS)
   const uint32_t bar_s = tc::smem_u32(&full_bar[warp][0]);
   const Cursor start = n > 0 ? cursor_at(P, S, u0) : Cursor{S.prob_begin, 0, 0};
   Producer pr;
-  prod_at<MB>(pr, P, start.p, start.rb, start.c);
+  prod_at<MB, SP>(pr, P, start.p, start.rb, start.c);
   if (lane == 0) {
 #pragma unroll
     for (int d = 0; d < kDepth; ++d) tc::mbar_init(bar_s + 8 * d, 1);
@@ -347,11 +381,26 @@ __global__ void __launch_bounds__(kThreads, GvCfg<NB>::CTAS)
 #pragma unroll
   for (int d = 0; d < kDepth; ++d) {
     if (issued < n) {
-      if (lane == 0) prod_copy<MB>(pr, ring_s + d * (MB * 512), bar_s + 8 * d);
-      prod_next<MB>(pr, P);
+      if (lane == 0) prod_copy<MB, SP>(pr, ring_s + d * U::BYTES, bar_s + 8 * d);
+      prod_next<MB, SP>(pr, P);
       ++issued;
     }
   }
+
+  if (SP && tid < 32) {
+    // group code 4p + s: pattern p places the nonzeros at (0,1) (0,2) (0,3)
+    // (1,2) (1,3) (2,3); sign bit 0 (1) is the first (second) nonzero, set =
+    // -1; codes 24..31 are all-zero groups.  Read after the barrier below.
+    uint32_t v = 0x01010101u;
+    if (tid < 24) {
+      const int pat = tid >> 2;
+      const int p0 = pat < 3 ? 0 : (pat < 5 ? 1 : 2);
+      const int p1 = pat == 0 ? 1 : ((pat == 1 || pat == 3) ? 2 : 3);
+      v ^= (((tid & 1) ? 1u : 3u) << (8 * p0)) ^ (((tid & 2) ? 1u : 3u) << (8 * p1));
+    }
+    s_lut[SP ? tid : 0] = v;
+  }
+  const int sp_word = (5 * r) >> 2, sp_shift = 8 * ((5 * r) & 3);
 
   // ---- activation fragments of this CTA's segment (after the previous grid)
   tc::pdl_wait();
@@ -420,7 +469,7 @@ __global__ void __launch_bounds__(kThreads, GvCfg<NB>::CTAS)
                                 __byte_perm(lo01, lo23, 0x7632) ^ 0x80808080u,
                                 __byte_perm(hi01, hi23, 0x5410) ^ 0x80808080u,
                                 __byte_perm(hi01, hi23, 0x7632)};
-        const int base = frag_word(q, 4 * t, NB);  // digit d: lane + 4d, word + 16d
+        const int base = frag_word<SP>(q, 4 * t, NB);  // digit d: lane + 4d, word + 16d
 #pragma unroll
         for (int d = 0; d < 4; ++d) {
           cs[d] = __dp4a((int)wd[d], 0x01010101, cs[d]);
@@ -447,7 +496,7 @@ __global__ void __launch_bounds__(kThreads, GvCfg<NB>::CTAS)
             if (k + e < S.K) wv |= (uint32_t)(xq[k + e] & 0xFF) << (8 * e);
         }
         cs[0] = __dp4a((int)wv, 0x01010101, cs[0]);
-        frag[frag_word(q, t, NB)] = wv;
+        frag[frag_word<SP>(q, t, NB)] = wv;
       }
     }
     // column sums: warp reduction, one shared atomic per warp and column
@@ -486,20 +535,63 @@ __global__ void __launch_bounds__(kThreads, GvCfg<NB>::CTAS)
     for (int k = 0; k < cnt; ++k) {
       ok = ok && tc::mbar_wait_sleep(bar_s + 8 * slot, phase, P.err, 60, FT_GV_SLEEP_NS);
       if (!ok) break;
-      uint4 w[MB];
+      if constexpr (!SP) {
+        uint4 w[MB];
 #pragma unroll
-      for (int m = 0; m < MB; ++m) w[m] = myring[slot * kU4 + m * 32 + lane];
+        for (int m = 0; m < MB; ++m) w[m] = myring[slot * kU4 + m * 32 + lane];
 #pragma unroll
-      for (int nb = 0; nb < NB; ++nb) {
-        const uint4 blo = fp[nb * 64], bhi = fp[nb * 64 + 32];
-        const uint32_t bj[4][2] = {{blo.x, blo.y}, {blo.z, blo.w}, {bhi.x, bhi.y}, {bhi.z, bhi.w}};
+        for (int nb = 0; nb < NB; ++nb) {
+          const uint4 blo = fp[nb * 64], bhi = fp[nb * 64 + 32];
+          const uint32_t bj[4][2] = {{blo.x, blo.y}, {blo.z, blo.w}, {bhi.x, bhi.y}, {bhi.z, bhi.w}};
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint32_t M = 0x03030303u << (2 * j);
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t M = 0x03030303u << (2 * j);
 #pragma unroll
-          for (int m = 0; m < MB; ++m)
-            mma_u8s8(acc[m][nb][j], w[m].x & M, w[m].y & M, w[m].z & M, w[m].w & M, bj[j][0],
-                     bj[j][1]);
+            for (int m = 0; m < MB; ++m)
+              mma_u8s8(acc[m][nb][j], w[m].x & M, w[m].y & M, w[m].z & M, w[m].w & M, bj[j][0],
+                       bj[j][1]);
+          }
+        }
+      } else {
+        // 2:4 sparse: this lane's 8 group codes of rows g and g + 8 are the 40
+        // bits at byte 5r of each 20-byte row record; each code's A register
+        // (4 bytes w + 1) comes from the shared table.  No 4^j factors here:
+        // one accumulator per m-block and operand block.
+        uint32_t bj[NB][4][2];
+#pragma unroll
+        for (int nb = 0; nb < NB; ++nb) {
+          const uint4 blo = fp[nb * 64], bhi = fp[nb * 64 + 32];
+          bj[nb][0][0] = blo.x; bj[nb][0][1] = blo.y; bj[nb][1][0] = blo.z; bj[nb][1][1] = blo.w;
+          bj[nb][2][0] = bhi.x; bj[nb][2][1] = bhi.y; bj[nb][3][0] = bhi.z; bj[nb][3][1] = bhi.w;
+        }
+        const uint32_t* u32 = reinterpret_cast<const uint32_t*>(myring + slot * kU4);
+#pragma unroll
+        for (int m = 0; m < MB; ++m) {
+          uint32_t lo[2], hi[2];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint32_t* rw = u32 + (16 * m + g + 8 * h) * 5 + sp_word;
+            const uint32_t w0 = rw[0], w1 = rw[1];
+            lo[h] = __funnelshift_r(w0, w1, sp_shift);
+            hi[h] = w1 >> sp_shift;
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint32_t a[2][2];  // [row half][group 2j, 2j + 1]
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+              for (int e = 0; e < 2; ++e) {
+                const int i = 2 * j + e;
+                const uint32_t code =
+                    i < 7 ? (__funnelshift_r(lo[h], hi[h], 5 * i) & 31u) : ((hi[h] >> 3) & 31u);
+                a[h][e] = s_lut[code];
+              }
+#pragma unroll
+            for (int nb = 0; nb < NB; ++nb)
+              mma_u8s8(acc[m][nb][0], a[0][0], a[1][0], a[0][1], a[1][1], bj[nb][j][0],
+                       bj[nb][j][1]);
+          }
         }
       }
       ++consumed;
@@ -508,9 +600,9 @@ __global__ void __launch_bounds__(kThreads, GvCfg<NB>::CTAS)
       if (issued < n) {
         if (lane == 0) {
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-          prod_copy<MB>(pr, ring_s + slot * (MB * 512), bar_s + 8 * slot);
+          prod_copy<MB, SP>(pr, ring_s + slot * U::BYTES, bar_s + 8 * slot);
         }
-        prod_next<MB>(pr, P);
+        prod_next<MB, SP>(pr, P);
         ++issued;
       }
       if (++slot == kDepth) {
@@ -529,8 +621,9 @@ __global__ void __launch_bounds__(kThreads, GvCfg<NB>::CTAS)
       for (int nb = 0; nb < NB; ++nb)
 #pragma unroll
         for (int e = 0; e < 4; ++e)
-          fin[m][nb][e] = acc[m][nb][0][e] + (acc[m][nb][1][e] >> 2) +
-                          (acc[m][nb][2][e] >> 4) + (acc[m][nb][3][e] >> 6);
+          fin[m][nb][e] = SP ? acc[m][nb][0][e]
+                             : acc[m][nb][0][e] + (acc[m][nb][1][e] >> 2) +
+                                   (acc[m][nb][2][e] >> 4) + (acc[m][nb][3][e] >> 6);
     if (c0 != 0) {
       // first row-block of this warp, begun by an earlier warp: hand it over
 #pragma unroll
@@ -584,8 +677,9 @@ __global__ void __launch_bounds__(kThreads, GvCfg<NB>::CTAS)
     for (int nb = 0; nb < NB; ++nb)
 #pragma unroll
       for (int e = 0; e < 4; ++e)
-        fin[m][nb][e] = acc[m][nb][0][e] + (acc[m][nb][1][e] >> 2) + (acc[m][nb][2][e] >> 4) +
-                        (acc[m][nb][3][e] >> 6);
+        fin[m][nb][e] = SP ? acc[m][nb][0][e]
+                           : acc[m][nb][0][e] + (acc[m][nb][1][e] >> 2) + (acc[m][nb][2][e] >> 4) +
+                                 (acc[m][nb][3][e] >> 6);
   for (int w = warp + 1; w < kW; ++w) {
     if (part_id[w] != id) continue;
 #pragma unroll
@@ -598,22 +692,23 @@ __global__ void __launch_bounds__(kThreads, GvCfg<NB>::CTAS)
   rowblock_store<NB, MB>(fin, q, crb, seq, D, colsum, tok_scale, g, r);
 }
 
-template <int NB>
+template <int NB, bool SP>
 size_t smem_for(int64_t max_chunks) {
-  constexpr int MB = GvCfg<NB>::MB, kDepth = GvCfg<NB>::DEPTH;
-  return (size_t)kW * kDepth * MB * 512 + (size_t)kW * NB * MB * 512 +
+  using U = GvUnit<NB, SP>;
+  return (size_t)kW * U::DEPTH * U::BYTES + (size_t)kW * NB * U::MB * 512 +
          (size_t)max_chunks * NB * 1024;
 }
 
-size_t smem_for(int nb, int64_t max_chunks) {
-  return nb == 1 ? smem_for<1>(max_chunks) : smem_for<2>(max_chunks);
+size_t smem_for(int nb, bool sp, int64_t max_chunks) {
+  if (sp) return nb == 1 ? smem_for<1, true>(max_chunks) : smem_for<2, true>(max_chunks);
+  return nb == 1 ? smem_for<1, false>(max_chunks) : smem_for<2, false>(max_chunks);
 }
 
-template <int NB, int NP>
+template <int NB, int NP, bool SP>
 int launch_nb(const GvParamsT<NP>& P, int64_t ctas, size_t smem, cudaStream_t s) {
   static int attr_smem = 0;  // per template instance
   if ((int)smem > attr_smem) {
-    FT_CUDA(cudaFuncSetAttribute(gemv_kernel<NB, NP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    FT_CUDA(cudaFuncSetAttribute(gemv_kernel<NB, NP, SP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)smem));
     attr_smem = (int)smem;
   }
@@ -627,12 +722,12 @@ int launch_nb(const GvParamsT<NP>& P, int64_t ctas, size_t smem, cudaStream_t s)
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  FT_CUDA(cudaLaunchKernelEx(&cfg, gemv_kernel<NB, NP>, P));
+  FT_CUDA(cudaLaunchKernelEx(&cfg, gemv_kernel<NB, NP, SP>, P));
   FT_LAUNCH_CHECK();
   return FT_OK;
 }
 
-template <int NB>
+template <int NB, bool SP>
 int launch_sized(const GvParams& P, int64_t ctas, size_t smem, cudaStream_t s) {
   if (P.nprob <= kSmallProb) {
     static thread_local GvParamsT<kSmallProb> Q;
@@ -643,9 +738,9 @@ int launch_sized(const GvParams& P, int64_t ctas, size_t smem, cudaStream_t s) {
     Q.err = P.err;
     for (int i = 0; i < P.nseg; ++i) Q.g[i] = P.g[i];
     for (int i = 0; i < P.nprob; ++i) Q.p[i] = P.p[i];
-    return launch_nb<NB, kSmallProb>(Q, ctas, smem, s);
+    return launch_nb<NB, kSmallProb, SP>(Q, ctas, smem, s);
   }
-  return launch_nb<NB, kMaxProb>(P, ctas, smem, s);
+  return launch_nb<NB, kMaxProb, SP>(P, ctas, smem, s);
 }
 
 }  // namespace
@@ -654,12 +749,12 @@ bool gemv_fits(const ft_weight* w, int64_t seq, int xkind) {
   const int digits = xkind == 2 ? 1 : 4;
   const int64_t ncols = seq * digits;
   // int32 bound: the k-step-3 accumulator grows by <= 128 * 128 * 32 per chunk
-  if (w->format != 0 || ncols > 16 || w->n_chunks > 2048) return false;
+  if ((w->format != 0 && w->format != 1) || ncols > 16 || w->n_chunks > 2048) return false;
   const int nb = ncols > 8 ? 2 : 1;
-  return smem_for(nb, w->n_chunks) <= (size_t)kGemvMaxSmem;
+  return smem_for(nb, w->format == 1, w->n_chunks) <= (size_t)kGemvMaxSmem;
 }
 
-int launch_gemv(ft_ctx* ctx, int nprob, const GvLaunchProblem* probs, int xkind,
+int launch_gemv(ft_ctx* ctx, int nprob, const GvLaunchProblem* probs, int xkind, bool sparse,
                 cudaStream_t s) {
   FT_CHECK(nprob > 0 && nprob <= kMaxProb, FT_ERR_UNSUPPORTED, "bad GEMV group size");
   static thread_local GvParams P;
@@ -738,9 +833,11 @@ int launch_gemv(ft_ctx* ctx, int nprob, const GvLaunchProblem* probs, int xkind,
     g.r_cta = (int32_t)(g.units % c);
     ctas += c;
   }
-  const size_t smem = smem_for(nb, max_chunks);
+  const size_t smem = smem_for(nb, sparse, max_chunks);
   FT_CHECK(smem <= (size_t)kGemvMaxSmem, FT_ERR_UNSUPPORTED, "GEMV operand too large");
-  return nb == 1 ? launch_sized<1>(P, ctas, smem, s) : launch_sized<2>(P, ctas, smem, s);
+  if (sparse)
+    return nb == 1 ? launch_sized<1, true>(P, ctas, smem, s) : launch_sized<2, true>(P, ctas, smem, s);
+  return nb == 1 ? launch_sized<1, false>(P, ctas, smem, s) : launch_sized<2, false>(P, ctas, smem, s);
 }
 
 }  // namespace ft

@@ -146,7 +146,8 @@ struct GvLaunchProblem {
   int64_t ldy;
 };
 bool gemv_fits(const ft_weight* w, int64_t seq, int xkind);
-int launch_gemv(ft_ctx* ctx, int nprob, const GvLaunchProblem* probs, int xkind,
+// All problems of one launch have the same weight format (sparse: 2:4).
+int launch_gemv(ft_ctx* ctx, int nprob, const GvLaunchProblem* probs, int xkind, bool sparse,
                 cudaStream_t s);
 int launch_wgsl_op(const uint32_t* words, const float* scales, const float* x, float* y,
                    uint32_t seq, uint32_t in_cols, uint32_t out_rows, cudaStream_t s);

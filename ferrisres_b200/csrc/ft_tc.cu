@@ -818,7 +818,7 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
                               ldys ? ldys[i] : w->rows};
     }
     ctx->err_flag = ctx->err_word;
-    return launch_gemv(ctx, nlive, gp, xkind, s);
+    return launch_gemv(ctx, nlive, gp, xkind, ws[live[0]]->format == 1, s);
   }
 
   // workspace: per source B operand, column sums, token scales
