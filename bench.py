@@ -457,7 +457,7 @@ S_N, S_K = 14336, 4096
 
 def run_sparse(args, ws, rank, local):
     """2:4 sparse ternary matmul, K=4096, N=14336, fp32 x,
-    at M=1 (bandwidth-bound decode GEMV kernel, grouped launches of min(--group, 16))
+    at M=1 (bandwidth-bound decode GEMV kernel, grouped launches of --group)
     and M=64 (tensor-core engine).
     Weights enter in the reference SparseTernaryMatrix layout and are stored
     at 1.25 bits/weight; copies rotate beyond 2x L2."""
@@ -470,17 +470,18 @@ def run_sparse(args, ws, rank, local):
     device = torch.device("cuda", local)
     dev_bytes = (S_N // 128) * (S_K // 128) * 2560
     algo = dev_bytes + S_N * 4 + S_K * 4 + S_N * 4  # weights + scales + x + y per GEMV
-    group = min(args.group, 16)
+    group = min(args.group, 64)
     n_copies = -(-max(4, -(-2 * L2_BYTES // dev_bytes)) // group) * group
     rng = np.random.default_rng(0)
     ng = S_N * S_K // 4
     weights = []
     for i in range(n_copies):
-        lo = rng.integers(0, 6, size=(ng + 1) // 2, dtype=np.uint8)
-        hi = rng.integers(0, 6, size=(ng + 1) // 2, dtype=np.uint8)
-        pat = (lo | (hi << 4)).astype(np.uint8)
-        sg = rng.integers(0, 256, size=(ng + 3) // 4, dtype=np.uint8)
-        rs = rng.uniform(0.01, 0.1, S_N).astype(np.float32)
+        if i < 8:  # 8 distinct matrices, uploaded as separate copies beyond that
+            lo = rng.integers(0, 6, size=(ng + 1) // 2, dtype=np.uint8)
+            hi = rng.integers(0, 6, size=(ng + 1) // 2, dtype=np.uint8)
+            pat = (lo | (hi << 4)).astype(np.uint8)
+            sg = rng.integers(0, 256, size=(ng + 3) // 4, dtype=np.uint8)
+            rs = rng.uniform(0.01, 0.1, S_N).astype(np.float32)
         weights.append(gpu.DeviceTernaryWeight.from_sparse_host(pat, sg, S_N, S_K, rs, local))
     assert weights[0].device_bytes() == dev_bytes + S_N * 4
     x1 = torch.randn(1, S_K, device=device)

@@ -582,10 +582,13 @@ __global__ void __launch_bounds__(kThreads, GvCfg<NB>::CTAS)
             for (int h = 0; h < 2; ++h)
 #pragma unroll
               for (int e = 0; e < 2; ++e) {
+                // byte offset 4 * code of code i (bits 5i .. 5i + 4 of the 40)
                 const int i = 2 * j + e;
-                const uint32_t code =
-                    i < 7 ? (__funnelshift_r(lo[h], hi[h], 5 * i) & 31u) : ((hi[h] >> 3) & 31u);
-                a[h][e] = s_lut[code];
+                const uint32_t off = i == 0 ? (lo[h] << 2) & 0x7Cu
+                                     : i < 7 ? __funnelshift_r(lo[h], hi[h], 5 * i - 2) & 0x7Cu
+                                             : (hi[h] >> 1) & 0x7Cu;
+                a[h][e] = *reinterpret_cast<const uint32_t*>(
+                    reinterpret_cast<const unsigned char*>(s_lut) + off);
               }
 #pragma unroll
             for (int nb = 0; nb < NB; ++nb)
