@@ -33,7 +33,9 @@ def sparse24(rng, rows, cols):
     return t.ravel()
 
 
-SHAPES = [(4, 4, 1), (130, 200, 3), (300, 512, 5), (14336, 4096, 1), (256, 1408, 9), (64, 20, 17)]
+# seq <= 4 runs on the decode GEMV (one or two n8 operand blocks), larger seq on the engine
+SHAPES = [(4, 4, 1), (130, 200, 3), (300, 512, 5), (14336, 4096, 1), (256, 1408, 9), (64, 20, 17),
+          (2050, 1412, 2), (129, 4100, 4)]
 
 
 @pytest.mark.parametrize("rows,cols,seq", SHAPES)
@@ -49,7 +51,8 @@ def test_sparse_host_layout_f32(gpu, rows, cols, seq):
     assert_fp32_close(y, ref, condition(t, x, rows, cols, seq, rs), what=f"{rows}x{cols}x{seq}")
 
 
-@pytest.mark.parametrize("rows,cols,seq", [(300, 512, 2), (14336, 4096, 64)])
+@pytest.mark.parametrize("rows,cols,seq", [(300, 512, 2), (2050, 1412, 12), (129, 4100, 16),
+                                           (14336, 4096, 64)])
 def test_sparse_i8_bit_exact(gpu, rows, cols, seq):
     rng = np.random.default_rng(rows * 5 + seq)
     t = sparse24(rng, rows, cols)
