@@ -534,7 +534,9 @@ def run_sparse(args, ws, rank, local):
                    "launch_group": group, "weight_copies": n_copies},
         "roofline": {"bound": "hbm", "achieved": round(gbps, 2), "peak": peak, "unit": "GB/s",
                      "frac": round(gbps / peak, 4), "peak_source": peak_kind,
-                     "algorithmic_bytes_per_gemv": algo, "traffic": None},
+                     "algorithmic_bytes_per_gemv": algo,
+                     "traffic": load_traffic().get("sparse_cfg3", {}).get("dram_bytes_per_launch"),
+                     "traffic_launch": "64 GEMVs", "kernel": "gemv_kernel<1,64,true>"},
         "m64": {"ms": round(sec64 * 1e3, 4), "TOPS_nonzero": round(2 * 64 * S_N * S_K / 2 / sec64 / 1e12, 2),
                 "GBps_weights": round(dev_bytes / sec64 / 1e9, 1)},
         "gpu_launches": int(reps * len(calls)),  # one decode-GEMV launch per grouped call
