@@ -49,7 +49,12 @@ namespace {
 #define FT_GV_MB1 4
 #endif
 #ifndef FT_GV_DEPTH1
-#define FT_GV_DEPTH1 4
+#define FT_GV_DEPTH1 3
+#endif
+// launches of <= 4 problems, one n8 block, dense: units of 2 m-blocks (1 KB),
+// so a single GEMV spreads over more warps
+#ifndef FT_GV_DEPTH1S
+#define FT_GV_DEPTH1S 4
 #endif
 #ifndef FT_GV_CTAS1
 #define FT_GV_CTAS1 2
@@ -87,10 +92,15 @@ struct GvCfg<2> {
 #ifndef FT_GV_SPDEPTH2
 #define FT_GV_SPDEPTH2 12
 #endif
-template <int NB, bool SP>
+// m-blocks per unit; `small`: a launch of <= 4 problems
+constexpr int unit_mb(int nb, bool sp, bool small) {
+  return (!sp && small && nb == 1) ? 2 : (nb == 1 ? FT_GV_MB1 : 2);
+}
+template <int NB, bool SP, bool SMALL>
 struct GvUnit {
-  static constexpr int MB = GvCfg<NB>::MB, CTAS = GvCfg<NB>::CTAS;
-  static constexpr int DEPTH = SP ? (NB == 1 ? FT_GV_SPDEPTH1 : FT_GV_SPDEPTH2) : GvCfg<NB>::DEPTH;
+  static constexpr int MB = unit_mb(NB, SP, SMALL), CTAS = GvCfg<NB>::CTAS;
+  static constexpr int DEPTH = SP ? (NB == 1 ? FT_GV_SPDEPTH1 : FT_GV_SPDEPTH2)
+                                  : (MB != GvCfg<NB>::MB ? FT_GV_DEPTH1S : GvCfg<NB>::DEPTH);
   static constexpr int MU = SP ? 20 : 32;    // uint4 per m-block of one chunk
   static constexpr int BU = SP ? 160 : 256;  // uint4 per block (tile, chunk)
   static constexpr uint32_t BYTES = MB * MU * 16;  // one unit
@@ -335,7 +345,7 @@ __device__ __forceinline__ void rowblock_store(const int (&fin)[MB][NB][4], cons
 template <int NB, int NP, bool SP>
 __global__ void __launch_bounds__(kThreads, GvCfg<NB>::CTAS)
     gemv_kernel(const __grid_constant__ GvParamsT<NP> P) {
-  using U = GvUnit<NB, SP>;
+  using U = GvUnit<NB, SP, (NP <= kSmallProb)>;
   constexpr int MB = U::MB, kDepth = U::DEPTH;
   constexpr int kU4 = MB * U::MU;  // uint4 per unit
   constexpr int kRingBytes = kW * kDepth * (int)U::BYTES;
@@ -695,16 +705,20 @@ __global__ void __launch_bounds__(kThreads, GvCfg<NB>::CTAS)
   rowblock_store<NB, MB>(fin, q, crb, seq, D, colsum, tok_scale, g, r);
 }
 
-template <int NB, bool SP>
+template <int NB, bool SP, bool SMALL>
 size_t smem_for(int64_t max_chunks) {
-  using U = GvUnit<NB, SP>;
+  using U = GvUnit<NB, SP, SMALL>;
   return (size_t)kW * U::DEPTH * U::BYTES + (size_t)kW * NB * U::MB * 512 +
          (size_t)max_chunks * NB * 1024;
 }
 
-size_t smem_for(int nb, bool sp, int64_t max_chunks) {
-  if (sp) return nb == 1 ? smem_for<1, true>(max_chunks) : smem_for<2, true>(max_chunks);
-  return nb == 1 ? smem_for<1, false>(max_chunks) : smem_for<2, false>(max_chunks);
+size_t smem_for(int nb, bool sp, bool small, int64_t max_chunks) {
+  if (small) {
+    if (sp) return nb == 1 ? smem_for<1, true, true>(max_chunks) : smem_for<2, true, true>(max_chunks);
+    return nb == 1 ? smem_for<1, false, true>(max_chunks) : smem_for<2, false, true>(max_chunks);
+  }
+  if (sp) return nb == 1 ? smem_for<1, true, false>(max_chunks) : smem_for<2, true, false>(max_chunks);
+  return nb == 1 ? smem_for<1, false, false>(max_chunks) : smem_for<2, false, false>(max_chunks);
 }
 
 template <int NB, int NP, bool SP>
@@ -754,7 +768,8 @@ bool gemv_fits(const ft_weight* w, int64_t seq, int xkind) {
   // int32 bound: the k-step-3 accumulator grows by <= 128 * 128 * 32 per chunk
   if ((w->format != 0 && w->format != 1) || ncols > 16 || w->n_chunks > 2048) return false;
   const int nb = ncols > 8 ? 2 : 1;
-  return smem_for(nb, w->format == 1, w->n_chunks) <= (size_t)kGemvMaxSmem;
+  return smem_for(nb, w->format == 1, false, w->n_chunks) <= (size_t)kGemvMaxSmem &&
+         smem_for(nb, w->format == 1, true, w->n_chunks) <= (size_t)kGemvMaxSmem;
 }
 
 int launch_gemv(ft_ctx* ctx, int nprob, const GvLaunchProblem* probs, int xkind, bool sparse,
@@ -786,7 +801,8 @@ int launch_gemv(ft_ctx* ctx, int nprob, const GvLaunchProblem* probs, int xkind,
   P.nseg = nseg;
   P.nprob = nprob;
   const int nb = max_cols > 8 ? 2 : 1;
-  const int mb = nb == 1 ? GvCfg<1>::MB : GvCfg<2>::MB;  // m-blocks per unit
+  const bool small = nprob <= kSmallProb;  // the kernel instance launch_sized picks
+  const int mb = unit_mb(nb, sparse, small);  // m-blocks per unit
   int64_t total = 0;
   int np = 0;
   for (int j = 0; j < nseg; ++j) {
@@ -836,7 +852,7 @@ int launch_gemv(ft_ctx* ctx, int nprob, const GvLaunchProblem* probs, int xkind,
     g.r_cta = (int32_t)(g.units % c);
     ctas += c;
   }
-  const size_t smem = smem_for(nb, sparse, max_chunks);
+  const size_t smem = smem_for(nb, sparse, small, max_chunks);
   FT_CHECK(smem <= (size_t)kGemvMaxSmem, FT_ERR_UNSUPPORTED, "GEMV operand too large");
   if (sparse)
     return nb == 1 ? launch_sized<1, true>(P, ctas, smem, s) : launch_sized<2, true>(P, ctas, smem, s);
