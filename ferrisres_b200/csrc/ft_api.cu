@@ -462,6 +462,9 @@ int ft_gpu_ternary_matmul(ft_ctx* ctx, const uint32_t* packed_weights_host,
   return st;
 }
 
+// Outputs up to this size are written by the kernel into mapped pinned memory.
+constexpr size_t kDirectOutBytes = 256 * 1024;
+
 int ft_gpu_ternary_matmul_vram(ft_ctx* ctx, const ft_weight* w, const float* input_host,
                                size_t seq_len, float* output_host) {
   FT_CHECK(ctx && w, FT_ERR_SHAPE, "null context or weight");
@@ -508,13 +511,26 @@ int ft_gpu_ternary_matmul_vram(ft_ctx* ctx, const ft_weight* w, const float* inp
                                                      (in_pinned ? 0 : in_bytes));
   float* dx = static_cast<float*>(ctx->io.ptr);
   float* dy = reinterpret_cast<float*>(static_cast<char*>(ctx->io.ptr) + in_bytes);
+  // A small output is written by the kernel straight into the pinned host
+  // buffer through its device mapping: no device staging and no copy back.
+  float* ky = dy;
+  if (out_bytes <= kDirectOutBytes) {
+    void* mapped = nullptr;
+    if (out_pinned && dst == output_host) {
+      mapped = ao.devicePointer;
+    } else if (cudaHostGetDevicePointer(&mapped, dst, 0) != cudaSuccess) {
+      mapped = nullptr;
+      cudaGetLastError();  // not mapped: copy back as for large outputs
+    }
+    if (mapped) ky = static_cast<float*>(mapped);
+  }
   FT_CUDA(cudaMemcpyAsync(dx, src, in_raw, cudaMemcpyHostToDevice, s));
-  int st = launch_tc_matmul(ctx, w, (int64_t)seq_len, dx, 0, nullptr, dy, s);
+  int st = launch_tc_matmul(ctx, w, (int64_t)seq_len, dx, 0, nullptr, ky, s);
   if (st != FT_OK) {
     cudaStreamSynchronize(s);
     return st;
   }
-  FT_CUDA(cudaMemcpyAsync(dst, dy, out_bytes, cudaMemcpyDeviceToHost, s));
+  if (ky == dy) FT_CUDA(cudaMemcpyAsync(dst, dy, out_bytes, cudaMemcpyDeviceToHost, s));
   FT_CUDA(cudaStreamSynchronize(s));
   if (!out_pinned) std::memcpy(output_host, dst, out_bytes);
   return FT_OK;

@@ -264,6 +264,32 @@ def test_accelerator_host_buffers(gpu):
     assert_fp32_close(y2, ref, condition(t, x, rows, cols, seq, rs))
 
 
+@pytest.mark.parametrize("rows,cols,seq", [(300, 256, 2), (300, 256, 9), (16384, 512, 5)])
+def test_host_buffer_outputs(gpu, rows, cols, seq):
+    """ft_gpu_ternary_matmul_vram with a pageable output (staged in pinned
+    memory) and a pinned caller output; small outputs are written by the kernel
+    through the pinned memory's mapping (decode GEMV and engine shapes), the
+    16384-row output is copied back."""
+    from ferrisres_b200.gpu import _vram_fn
+    rng = np.random.default_rng(rows + seq)
+    t = ternary_matrix(rng, rows, cols)
+    rs = rng.uniform(0.01, 0.1, rows).astype(np.float32)
+    x = rng.standard_normal(seq * cols).astype(np.float32)
+    w = gpu.DeviceTernaryWeight.from_packed_u8(fo.pack_ternary(t), rows, cols, rs)
+    ref = np.concatenate([fo.ternary_matmul(t, 1.0, x[s * cols:(s + 1) * cols], rows, cols, 1) * rs
+                          for s in range(seq)])
+    cond = condition(t, x, rows, cols, seq, rs)
+    acc = gpu.GpuMatmulAccelerator()
+    for _ in range(2):
+        assert_fp32_close(acc.gpu_ternary_matmul_vram(w, x, seq, cols, rows), ref, cond,
+                          what="pageable output")
+    xp = torch.from_numpy(x).pin_memory()
+    yp = torch.full((seq * rows,), float("nan"), dtype=torch.float32).pin_memory()
+    from ferrisres_b200._lib import check
+    check(_vram_fn()(w.ctx.handle, w.handle, xp.data_ptr(), int(seq), yp.data_ptr()))
+    assert_fp32_close(yp.numpy(), ref, cond, what="pinned output")
+
+
 def test_reference_kats_on_gpu(gpu):
     """The reference's own known answers, run through the GPU path."""
     acc = gpu.GpuMatmulAccelerator()
