@@ -51,8 +51,8 @@ namespace {
 #ifndef FT_GV_DEPTH1
 #define FT_GV_DEPTH1 3
 #endif
-// launches of <= 4 problems, one n8 block, dense: units of 2 m-blocks (1 KB),
-// so a single GEMV spreads over more warps
+// launches of <= 4 problems, one n8 block: units of 2 m-blocks, so a single
+// GEMV spreads over more warps
 #ifndef FT_GV_DEPTH1S
 #define FT_GV_DEPTH1S 4
 #endif
@@ -94,7 +94,7 @@ struct GvCfg<2> {
 #endif
 // m-blocks per unit; `small`: a launch of <= 4 problems
 constexpr int unit_mb(int nb, bool sp, bool small) {
-  return (!sp && small && nb == 1) ? 2 : (nb == 1 ? FT_GV_MB1 : 2);
+  return (small && nb == 1) ? 2 : (nb == 1 ? FT_GV_MB1 : 2);
 }
 template <int NB, bool SP, bool SMALL>
 struct GvUnit {
