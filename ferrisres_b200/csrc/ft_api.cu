@@ -497,9 +497,14 @@ int ft_gpu_ternary_matmul_vram(ft_ctx* ctx, const ft_weight* w, const float* inp
     FT_CUDA(cudaStreamSynchronize(s));
     if (ctx->hio.ptr) FT_CUDA(cudaFreeHost(ctx->hio.ptr));
     ctx->hio.ptr = nullptr;
+    ctx->hio_dev = nullptr;
     ctx->hio.bytes = 0;
     FT_CUDA(cudaHostAlloc(&ctx->hio.ptr, need, cudaHostAllocDefault));
     ctx->hio.bytes = need;
+    if (cudaHostGetDevicePointer(&ctx->hio_dev, ctx->hio.ptr, 0) != cudaSuccess) {
+      ctx->hio_dev = nullptr;
+      cudaGetLastError();  // not mapped: outputs are copied back
+    }
   }
   const float* src = input_host;
   if (!in_pinned) {
@@ -518,9 +523,9 @@ int ft_gpu_ternary_matmul_vram(ft_ctx* ctx, const ft_weight* w, const float* inp
     void* mapped = nullptr;
     if (out_pinned && dst == output_host) {
       mapped = ao.devicePointer;
-    } else if (cudaHostGetDevicePointer(&mapped, dst, 0) != cudaSuccess) {
-      mapped = nullptr;
-      cudaGetLastError();  // not mapped: copy back as for large outputs
+    } else if (ctx->hio_dev) {
+      mapped = static_cast<char*>(ctx->hio_dev) +
+               (reinterpret_cast<char*>(dst) - static_cast<char*>(ctx->hio.ptr));
     }
     if (mapped) ky = static_cast<float*>(mapped);
   }

@@ -87,6 +87,7 @@ struct ft_ctx {
   cudaStream_t host_stream = nullptr;  // used by the synchronous host-buffer calls
   ft::Workspace io;                    // device staging for the host-buffer calls
   ft::Workspace hio;                   // pinned host staging for pageable host buffers
+  void* hio_dev = nullptr;             // device mapping of hio.ptr (null if not mapped)
   ft::Workspace zs;                    // zero-initialised scratch (split-K sums, tickets)
   int* err_word = nullptr;             // device word set by a kernel whose bounded wait gave up
   int* err_flag = nullptr;             // word of the latest launch (err_word, or the static

@@ -83,6 +83,15 @@ def _host(a, dtype):
     return np.ascontiguousarray(np.asarray(a), dtype=dtype)
 
 
+def _addr(a):
+    """Address of a contiguous numpy array's data (a writable array through
+    its buffer, which is cheaper than ``a.ctypes``)."""
+    try:
+        return C.addressof(C.c_char.from_buffer(a))
+    except (TypeError, ValueError, BufferError):
+        return a.ctypes.data
+
+
 class DeviceTernaryWeight:
     """A dense ternary matrix [rows, cols] resident in HBM with per-row scales."""
 
@@ -325,6 +334,5 @@ class GpuMatmulAccelerator:
         if x.size < seq_len * in_cols:
             raise ShapeError("input too small")
         y = np.empty(seq_len * out_rows, np.float32)
-        check(_vram_fn()(self.ctx.handle, weight.handle, x.ctypes.data, int(seq_len),
-                         y.ctypes.data))
+        check(_vram_fn()(self.ctx.handle, weight.handle, _addr(x), int(seq_len), _addr(y)))
         return y
