@@ -35,6 +35,10 @@ namespace {
 constexpr int kRouterTok = 16;  // tokens per router block
 constexpr int kRouterKc = 64;   // K chunk staged in shared memory
 constexpr int kMaxExperts = 64;
+constexpr int kRouterThreads = 256;
+static_assert(kRouterTok * kRouterKc % kRouterThreads == 0 &&
+                  kMaxExperts * kRouterKc % kRouterThreads == 0,
+              "router chunk loads must split evenly over the block");
 
 __device__ __forceinline__ float load_act(const void* x, int bf16, int64_t i) {
   return bf16 ? __uint_as_float((uint32_t) static_cast<const uint16_t*>(x)[i] << 16)
@@ -44,7 +48,7 @@ __device__ __forceinline__ float load_act(const void* x, int bf16, int64_t i) {
 // One block = 16 tokens x all experts (E <= 64); thread t owns token t/16 and
 // experts t%16 + 16m.  Then one thread per token does softmax and top-k in the
 // reference's sequential order.
-__global__ void __launch_bounds__(256) moe_router_kernel(
+__global__ void __launch_bounds__(kRouterThreads) moe_router_kernel(
     const void* __restrict__ x, int bf16, int64_t T, int64_t H, int E, int K,
     const float* __restrict__ R, int32_t* __restrict__ topk_idx, float* __restrict__ topk_w,
     float* __restrict__ probs_out, int32_t* __restrict__ counts) {
@@ -54,19 +58,42 @@ __global__ void __launch_bounds__(256) moe_router_kernel(
   const int tt = threadIdx.x >> 4, el = threadIdx.x & 15;
   const int64_t t0 = (int64_t)blockIdx.x * kRouterTok;
   float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-  for (int64_t k0 = 0; k0 < H; k0 += kRouterKc) {
-    __syncthreads();
-    for (int i = threadIdx.x; i < kRouterTok * kRouterKc; i += blockDim.x) {
+  // The next K chunk is loaded into registers while the current one is
+  // computed (the loads are L2/HBM latency-bound otherwise).
+  constexpr int kXL = kRouterTok * kRouterKc / kRouterThreads;   // x values per thread
+  constexpr int kRL = kMaxExperts * kRouterKc / kRouterThreads;  // R values per thread
+  float px[kXL], pr[kRL];
+  auto fetch = [&](int64_t k0) {
+#pragma unroll
+    for (int j = 0; j < kXL; ++j) {
+      const int i = threadIdx.x + j * kRouterThreads;
       const int a = i / kRouterKc, kk = i % kRouterKc;
       const int64_t t = t0 + a, k = k0 + kk;
-      xs[a][kk] = (t < T && k < H) ? load_act(x, bf16, t * H + k) : 0.0f;
+      px[j] = (t < T && k < H) ? load_act(x, bf16, t * H + k) : 0.0f;
     }
-    for (int i = threadIdx.x; i < E * kRouterKc; i += blockDim.x) {
+#pragma unroll
+    for (int j = 0; j < kRL; ++j) {
+      const int i = threadIdx.x + j * kRouterThreads;
       const int e = i / kRouterKc, kk = i % kRouterKc;
       const int64_t k = k0 + kk;
-      rs[kk][e] = k < H ? R[(int64_t)e * H + k] : 0.0f;
+      pr[j] = (e < E && k < H) ? R[(int64_t)e * H + k] : 0.0f;
+    }
+  };
+  fetch(0);
+  for (int64_t k0 = 0; k0 < H; k0 += kRouterKc) {
+    __syncthreads();  // the previous chunk is no longer read
+#pragma unroll
+    for (int j = 0; j < kXL; ++j) {
+      const int i = threadIdx.x + j * kRouterThreads;
+      xs[i / kRouterKc][i % kRouterKc] = px[j];
+    }
+#pragma unroll
+    for (int j = 0; j < kRL; ++j) {
+      const int i = threadIdx.x + j * kRouterThreads;
+      rs[i % kRouterKc][i / kRouterKc] = pr[j];
     }
     __syncthreads();
+    if (k0 + kRouterKc < H) fetch(k0 + kRouterKc);
     const int kn = (int)((H - k0) < kRouterKc ? (H - k0) : kRouterKc);
     for (int kk = 0; kk < kn; ++kk) {
       const float xv = xs[tt][kk];
@@ -252,7 +279,7 @@ int moe_route(ft_ctx* ctx, ft_moe* m, int64_t T, const void* x, int bf16, int32_
               float* topk_w, float* probs, int32_t* counts, cudaStream_t s) {
   FT_CUDA(cudaMemsetAsync(counts, 0, m->E * sizeof(int32_t), s));
   if (T == 0) return FT_OK;
-  moe_router_kernel<<<(unsigned)ceil_div(T, kRouterTok), 256, 0, s>>>(
+  moe_router_kernel<<<(unsigned)ceil_div(T, kRouterTok), kRouterThreads, 0, s>>>(
       x, bf16, T, m->H, (int)m->E, m->top_k, m->router, topk_idx, topk_w, probs, counts);
   FT_LAUNCH_CHECK();
   return FT_OK;
