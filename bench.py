@@ -2,26 +2,34 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload (the metric's "ternary GEMV HBM GB/s"):
+Headline (BASELINE.json config 0/1, the metric's "ternary GEMV HBM GB/s"):
 dense ternary GEMV, x f32 [1, 2048] ~ N(0,1), W [5632, 2048] ternary with
 P(-1)=P(0)=P(+1)=1/3 packed in the reference's 2-bit layout, per-row scales
-~ U(0.01, 0.1).  One step = one GEMV y = scale * (W x) on one weight copy.
-The steps rotate over R distinct weight copies whose total size exceeds 2x
-the 126 MB L2, so every step streams its weights from HBM.  Inputs are made
-on the device from a seeded generator (synthetic data; no dataset exists for
-this path).
+~ U(0.01, 0.1).  One STEP = one grouped launch of 64 such GEMVs over 64
+distinct weight copies reading the same token x (the independent projections
+of one decode step).  The K timed steps rotate over 128 weight copies
+(352 MiB, more than 2x the 126 MB L2; every launch reads 188 MB), so each step
+streams its weights from HBM.  Inputs are made on the device from a seeded
+generator (synthetic data; no dataset exists for this path).
 
-value: algorithmic GB/s over all ranks = steps * ranks * 2,936,832 B / max
+value: algorithmic GB/s over all ranks = K * 64 * 2,936,832 B * ranks / max
 over ranks of the device time of the K timed steps (CUDA events on the
-launching stream; launches replayed from CUDA graphs).
+launching stream; the K launches replayed from one CUDA graph).
+
+The same line carries, as sub-objects, the other BASELINE configs timed in
+the same run: gemm_cfg2 (int8 prefill GEMM), sparse_cfg3 (2:4 sparse, M=1
+and M=64), kv_cfg5 (3-bit KV flash decode) -- on one GPU -- and moe_cfg4
+(the MoE layer, expert-parallel over all ranks, with per-phase times and a
+parity check of sampled tokens against the CPU oracle) at every N.
 
 Multi-GPU: the GEMV does not shard; each rank runs its own replica stream
-(weak scaling, no collective on the data path).  Rank 0 prints the line.
+(weak scaling, no collective on the data path).  The MoE layer shards its
+experts over the ranks (strong scaling: the 4096-token batch is fixed).
 
---impl reference times the reference's CPU algorithm for the same workload:
-the C restatement of ternary_matmul_packed_parallel (src/model/ternary.rs:
-471-529) with per-row scales, on all host cores (the reference itself is Rust
-and cannot be built on this image; see oracle/).
+--impl reference times the reference's CPU algorithm for the headline
+workload: the C restatement of ternary_matmul_packed_parallel
+(src/model/ternary.rs:471-529) with per-row scales, on all host cores (the
+reference itself is Rust and cannot be built on this image; see oracle/).
 """
 from __future__ import annotations
 
@@ -41,18 +49,21 @@ if ROOT not in sys.path:
 
 ROWS, COLS = 5632, 2048
 ALGO_BYTES = ROWS * COLS // 4 + ROWS * 4 + COLS * 4 + ROWS * 4  # W + scales + x + y
+GROUP = 64  # GEMVs per launch (one step)
+N_COPIES = 128
 METRIC = "ternary GEMV HBM GB/s"
 UNIT = "GB/s"
 L2_BYTES = 126 * 1024 * 1024
 
 
 def load_peaks():
+    """(HBM GB/s, bf16 burst TFLOP/s, source) from MEASURED_PEAKS.json, else the fallback."""
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
         d = json.load(open(p))
-        return float(d["hbm_gbs"]), "measured"
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
     except Exception:
-        return 6650.0, "fallback"
+        return 6650.0, 1590.0, "fallback"
 
 
 def load_traffic():
@@ -61,6 +72,11 @@ def load_traffic():
         return json.load(open(p))
     except Exception:
         return {}
+
+
+def _scaled_traffic(key, factor):
+    v = load_traffic().get(key, {}).get("dram_bytes_per_launch")
+    return None if v is None else int(v * factor)
 
 
 def dist_env():
@@ -116,227 +132,243 @@ class ClockSampler:
                 "samples": len(sms)}
 
 
-# ------------------------------------------------------------------ ours --
+class Timer:
+    """Device time of work issued on `stream`, max over ranks (CUDA events,
+    a barrier and a synchronize on both sides)."""
+
+    def __init__(self, torch, dist, stream, device, ws):
+        self.torch, self.dist, self.stream, self.device, self.ws = torch, dist, stream, device, ws
+
+    def __call__(self, fn):
+        torch = self.torch
+        torch.cuda.synchronize()
+        if self.ws > 1:
+            self.dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(self.stream):
+            e0.record(self.stream)
+            fn()
+            e1.record(self.stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / 1e3], device=self.device, dtype=torch.float64)
+        if self.ws > 1:
+            self.dist.barrier()
+            self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+
+def _graph_of(torch, stream, fns):
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for f in fns:
+            f()
+    return graph
+
+
+def _upload_u32(gpu, torch, ctx, words, rows, cols, scales, device):
+    import ctypes as C
+
+    from ferrisres_b200._lib import call
+    h = C.c_void_p()
+    call("ft_weight_from_device_u32", ctx.handle, C.c_void_p(words.data_ptr()), rows, cols,
+         C.c_void_p(scales.data_ptr()), C.c_void_p(torch.cuda.current_stream().cuda_stream),
+         C.byref(h))
+    torch.cuda.synchronize()
+    return gpu.DeviceTernaryWeight(h, rows, cols, ctx)
+
+
+def _words_from_codes(torch, codes):
+    """codes int64 {0,1,2} [n] (n % 16 == 0) -> u32 words, 16 codes per word LSB first."""
+    words = (codes.view(-1, 16) << torch.arange(0, 32, 2, device=codes.device)).sum(dim=1)
+    return torch.where(words >= 2**31, words - 2**32, words).to(torch.int32).contiguous()
+
+
+# --------------------------------------------------------------- headline --
 def make_weights(gpu, torch, n_copies, device):
-    """n_copies ternary [ROWS, COLS] matrices with row scales, made on the device."""
+    """n_copies ternary [ROWS, COLS] matrices (P = 1/3 each) with row scales, made on the device."""
     weights = []
     g = torch.Generator(device=device)
+    ctx = gpu.get_context(device.index)
     for i in range(n_copies):
         g.manual_seed(i)
-        codes = torch.randint(0, 3, (ROWS * COLS,), generator=g, device=device, dtype=torch.int32)
-        c = codes.view(-1, 16)
-        shifts = torch.arange(0, 32, 2, device=device, dtype=torch.int64)
-        words = (c.to(torch.int64) << shifts).sum(dim=1)  # 16 codes per u32, LSB first
-        words = torch.where(words >= 2**31, words - 2**32, words).to(torch.int32).contiguous()
+        codes = torch.randint(0, 3, (ROWS * COLS,), generator=g, device=device, dtype=torch.int64)
         scales = (torch.rand(ROWS, generator=g, device=device) * 0.09 + 0.01).contiguous()
-        import ctypes as C
-        h = C.c_void_p()
-        ctx = gpu.get_context(device.index)
-        from ferrisres_b200._lib import call
-        call("ft_weight_from_device_u32", ctx.handle, C.c_void_p(words.data_ptr()), ROWS, COLS,
-             C.c_void_p(scales.data_ptr()), C.c_void_p(torch.cuda.current_stream().cuda_stream),
-             C.byref(h))
-        torch.cuda.synchronize()
-        weights.append(gpu.DeviceTernaryWeight(h, ROWS, COLS, ctx))
-        del codes, words
+        weights.append(_upload_u32(gpu, torch, ctx, _words_from_codes(torch, codes), ROWS, COLS,
+                                   scales, device))
+        del codes
     return weights
 
 
-def run_ours(args, ws, rank, local):
-    import torch
-    import torch.distributed as dist
-
+def run_gemv(args, ws, rank, local, torch, dist, device):
     from ferrisres_b200 import _lib, gpu
 
-    torch.cuda.set_device(local)
-    device = torch.device("cuda", local)
-    if ws > 1 and not dist.is_initialized():
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
-
-    group = args.group
-    n_copies = max(8, -(-2 * L2_BYTES // (ROWS * COLS // 4)))  # > 2x L2 of weights
-    n_copies = -(-n_copies // max(group, 16)) * max(group, 16)
-    weights = make_weights(gpu, torch, n_copies, device)
+    weights = make_weights(gpu, torch, N_COPIES, device)
     g = torch.Generator(device=device).manual_seed(1000 + rank)
     x = torch.randn(1, COLS, generator=g, device=device)
-    ys = [torch.empty(1, ROWS, device=device) for _ in range(n_copies)]
-    # one grouped call per G consecutive weight copies, all reading the token x
-    calls = [gpu.GroupCall(weights[i:i + group], [x] * group, ys[i:i + group])
-             for i in range(0, n_copies, group)]
-    singles = [gpu.GroupCall([weights[i]], [x], [ys[i]]) for i in range(n_copies)]
-
+    ys = [torch.empty(1, ROWS, device=device) for _ in range(N_COPIES)]
+    calls = [gpu.GroupCall(weights[i:i + GROUP], [x] * GROUP, ys[i:i + GROUP])
+             for i in range(0, N_COPIES, GROUP)]
+    singles = [gpu.GroupCall([weights[i]], [x], [ys[i]]) for i in range(N_COPIES)]
     stream = torch.cuda.Stream(device=device)
-    with torch.cuda.stream(stream):  # warm-up; also sizes workspaces before capture
-        for i in range(max(args.warmup // group, 3)):
+    timer = Timer(torch, dist, stream, device, ws)
+    with torch.cuda.stream(stream):  # warm-up (also sizes workspaces before capture)
+        for i in range(max(args.warmup, 3)):
             calls[i % len(calls)]()
         for i in range(3):
             singles[i]()
     stream.synchronize()
 
-    def capture(fns):
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=stream):
-            for f in fns:
-                f()
-        return graph
-
+    # the K timed steps: K grouped launches, rotating over the weight copies,
+    # replayed from CUDA graphs of at most 256 launches
     steps = args.steps
+    chunk = min(steps, 256)
     launches0 = _lib.lib().ft_launch_counter()
-    g_full = capture(calls)  # one sweep = n_copies steps
-    per_sweep = _lib.lib().ft_launch_counter() - launches0
-    full, rem = divmod(steps, n_copies)
-    rem_groups, rem_single = divmod(rem, group)
-    launches0 = _lib.lib().ft_launch_counter()
-    g_rem = capture(calls[:rem_groups] + singles[rem_groups * group:rem_groups * group + rem_single]) \
-        if rem else None
-    rem_launches = _lib.lib().ft_launch_counter() - launches0
-    gpu_launches = full * per_sweep + rem_launches
+    g_main = _graph_of(torch, stream, [calls[i % len(calls)] for i in range(chunk)])
+    reps, rem = divmod(steps, chunk)
+    g_rem = _graph_of(torch, stream, [calls[i % len(calls)] for i in range(rem)]) if rem else None
+    captured = _lib.lib().ft_launch_counter() - launches0
+    assert captured == chunk + rem, (captured, chunk, rem)  # one kernel launch per step
+    gpu_launches = reps * chunk + rem
+    with torch.cuda.stream(stream):  # warm both graphs
+        g_main.replay()
+        if g_rem is not None:
+            g_rem.replay()
 
-    def timed(graph_list):
-        with torch.cuda.stream(stream):
-            graph_list[0][0].replay()  # warm
-        stream.synchronize()
-        if ws > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with torch.cuda.stream(stream):
-            e0.record(stream)
-            for gr, reps in graph_list:
-                for _ in range(reps):
-                    gr.replay()
-            e1.record(stream)
-        torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1)
-        t = torch.tensor([ms], device=device, dtype=torch.float64)
-        if ws > 1:
-            dist.barrier()
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+    def timed_steps():
+        for _ in range(reps):
+            g_main.replay()
+        if g_rem is not None:
+            g_rem.replay()
 
     sampler = ClockSampler(local)
     sampler.start()
-    plan = [(g_full, full)] + ([(g_rem, 1)] if g_rem is not None else [])
-    ms = timed(plan)
+    sec = timer(timed_steps)
     clocks = sampler.stop()
-    sec = ms / 1e3
-    value = steps * ws * ALGO_BYTES / sec / 1e9
+    launch_s = sec / steps
+    value = ws * steps * GROUP * ALGO_BYTES / sec / 1e9
+    achieved = GROUP * ALGO_BYTES / launch_s / 1e9
 
-    # smaller launches: 16 GEMVs per launch over the same weights
+    # the same GEMVs, 16 per launch, one sweep of the copies per replay
     calls16 = [gpu.GroupCall(weights[i:i + 16], [x] * 16, ys[i:i + 16])
-               for i in range(0, n_copies, 16)]
-    g16 = capture(calls16)
-    reps16 = max(1, min(full, 20))
-    ms16 = timed([(g16, reps16)])
-    g16_launch_s = ms16 / 1e3 / (reps16 * len(calls16))
+               for i in range(0, N_COPIES, 16)]
+    g16 = _graph_of(torch, stream, calls16)
+    with torch.cuda.stream(stream):
+        g16.replay()
+    ms16 = timer(lambda: [g16.replay() for _ in range(5)])
+    l16 = ms16 / (5 * len(calls16))
     del g16
-
-    # dependent-chain reference: the same steps as single-GEMV launches
-    g_chain = capture(singles)
-    chain_reps = max(1, min(full, 20))
-    ms_chain = timed([(g_chain, chain_reps)])
-    chain_step_s = ms_chain / 1e3 / (chain_reps * n_copies)
+    # dependent chain: each GEMV its own launch, back to back
+    g_chain = _graph_of(torch, stream, singles)
+    with torch.cuda.stream(stream):
+        g_chain.replay()
+    s_chain = timer(lambda: [g_chain.replay() for _ in range(5)]) / (5 * N_COPIES)
     del g_chain
 
-    # end to end through the host-buffer accelerator call (pinned host memory)
-    import numpy as np
+    # end to end through the host-buffer accelerator call: pinned x in, y out
     acc = gpu.GpuMatmulAccelerator(local)
     xh = torch.empty(COLS, dtype=torch.float32, pin_memory=True)
     xh.copy_(x.view(-1).cpu())
-    n_e2e = min(args.steps, 2000)
+    xn = xh.numpy()
+    for i in range(5):
+        acc.gpu_ternary_matmul_vram(weights[i], xn, 1, COLS, ROWS)
+    n_e2e = max(64, min(steps * GROUP, 4096))
+    if ws > 1:
+        dist.barrier()
     t0 = time.perf_counter()
     for i in range(n_e2e):
-        acc.gpu_ternary_matmul_vram(weights[i % n_copies], xh.numpy(), 1, COLS, ROWS)
-    e2e_sec = time.perf_counter() - t0
-    e2e_local = torch.tensor([e2e_sec / n_e2e], device=device, dtype=torch.float64)
+        acc.gpu_ternary_matmul_vram(weights[i % N_COPIES], xn, 1, COLS, ROWS)
+    e2e_local = torch.tensor([(time.perf_counter() - t0) / n_e2e], device=device,
+                             dtype=torch.float64)
     if ws > 1:
         dist.all_reduce(e2e_local, op=dist.ReduceOp.MAX)
     e2e_value = ws * ALGO_BYTES / float(e2e_local.item()) / 1e9
 
-    peak, peak_kind = load_peaks()
-    traffic = load_traffic().get("gemv_cfg0", {}).get("dram_bytes_per_launch")
-    result = {
+    peak, _, peak_kind = load_peaks()
+    tr = load_traffic().get("gemv_cfg1_g64", {})
+    res = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": ws,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": launch_s * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded, generated on device)",
-        "config": {"workload": "cfg0 dense ternary GEMV x f32 [1,2048] . W [5632,2048]^T, "
-                               "per-row scales", "rows": ROWS, "cols": COLS, "seq": 1,
-                   "weight_copies": n_copies,
-                   "l2": f"weights rotate over {n_copies} copies "
-                         f"({n_copies * ROWS * COLS // 4 / 2**20:.0f} MiB > 2x L2)",
-                   "parallelism": f"replicas x{ws}", "graph": "CUDA graph replay",
-                   "launch_group": f"{group} GEMVs (shared token x) per launch, e.g. the "
-                                   "expert projections of one decode step"},
-        "roofline": {"bound": "hbm", "achieved": round(ALGO_BYTES * group / (sec * group / steps) / 1e9, 2),
-                     "peak": peak, "unit": "GB/s",
-                     "frac": round(ALGO_BYTES * group / (sec * group / steps) / 1e9 / peak, 4),
-                     "peak_source": peak_kind, "traffic": traffic,
-                     "kernel": "gemv_kernel<1> (activation prep fused)",
-                     "algorithmic_bytes_per_launch": ALGO_BYTES * group,
-                     "note": f"one launch = {group} GEMVs; achieved = algorithmic bytes per "
-                             "launch / per-launch device time (CUDA events over the timed region)"},
-        "launch_of_16": {"GBps": round(16 * ALGO_BYTES / g16_launch_s / 1e9, 2),
-                         "frac": round(16 * ALGO_BYTES / g16_launch_s / 1e9 / peak, 4),
-                         "us_per_launch": round(g16_launch_s * 1e6, 3),
-                         "note": "the same GEMVs, 16 per launch"},
-        "single_gemv_chain": {"us_per_gemv": round(chain_step_s * 1e6, 3),
-                              "GBps": round(ALGO_BYTES / chain_step_s / 1e9, 2),
-                              "frac": round(ALGO_BYTES / chain_step_s / 1e9 / peak, 4),
-                              "note": "each GEMV its own launch (prep + matmul), back to back "
-                                      "in a CUDA graph with programmatic dependent launch"},
-        "e2e": {"value": round(e2e_value, 3), "unit": UNIT, "h2d_bytes_per_step": COLS * 4,
-                "d2h_bytes_per_step": ROWS * 4, "steps": n_e2e,
-                "api": "ft_gpu_ternary_matmul_vram (GpuMatmulAccelerator::gpu_ternary_matmul_vram)"},
+        "config": {"workload": "cfg1 dense ternary GEMV x f32 [1,2048] . W [5632,2048]^T, "
+                               "per-row scales; one step = one launch of 64 GEMVs",
+                   "rows": ROWS, "cols": COLS, "seq": 1, "gemvs_per_step": GROUP,
+                   "weight_copies": N_COPIES,
+                   "l2": f"inputs larger than L2: a step reads {GROUP * ROWS * COLS // 4 / 1e6:.0f} "
+                         f"MB of weights; steps rotate over {N_COPIES} copies "
+                         f"({N_COPIES * ROWS * COLS // 4 / 2**20:.0f} MiB)",
+                   "parallelism": f"replicas x{ws}", "graph": "CUDA graph replay"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+                     "traffic": tr.get("dram_bytes_per_launch"),
+                     "traffic_source": tr.get("source"),
+                     "kernel": tr.get("kernel", "gemv_kernel<1, 64, false>"),
+                     "algorithmic_bytes_per_launch": GROUP * ALGO_BYTES,
+                     "note": f"the timed launch: {GROUP} GEMVs of 2,936,832 algorithmic bytes "
+                             "each; achieved = those bytes / the launch's average device time "
+                             "(CUDA events over the K timed launches)"},
+        "launch_of_16": {"GBps": round(16 * ALGO_BYTES / l16 / 1e9, 2),
+                         "frac": round(16 * ALGO_BYTES / l16 / 1e9 / peak, 4),
+                         "us_per_launch": round(l16 * 1e6, 3)},
+        "single_gemv_chain": {"us_per_gemv": round(s_chain * 1e6, 3),
+                              "GBps": round(ALGO_BYTES / s_chain / 1e9, 2),
+                              "frac": round(ALGO_BYTES / s_chain / 1e9 / peak, 4),
+                              "note": "each GEMV its own launch, back to back in a CUDA graph "
+                                      "with programmatic dependent launch"},
+        "e2e": {"value": round(e2e_value, 3), "unit": UNIT, "h2d_bytes_per_step": GROUP * COLS * 4,
+                "d2h_bytes_per_step": GROUP * ROWS * 4, "calls": n_e2e,
+                "us_per_gemv_call": round(float(e2e_local.item()) * 1e6, 2),
+                "api": "ft_gpu_ternary_matmul_vram (GpuMatmulAccelerator::gpu_ternary_matmul_vram), "
+                       "one synchronous call per GEMV: pinned host x in, host y out"},
         "gpu_launches": int(gpu_launches),
         "clocks": clocks,
     }
-    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
-        result["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
-    del g_full, g_rem
-    if ws > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-    return result
+    del g_main, g_rem
+    for w in weights:
+        w.close()
+    return res
 
 
 # ------------------------------------------------------------- CPU side --
-CPU_COPIES = 128
-
-
 def cpu_setup():
-    import numpy as np
-
     from oracle import oracle as fo
     rng = np.random.default_rng(0)
     t = rng.integers(-1, 2, size=ROWS * COLS).astype(np.int8)
     packed = fo.pack_ternary(t)
     rs = rng.uniform(0.01, 0.1, ROWS).astype(np.float32)
     x = rng.standard_normal(COLS).astype(np.float32)
-    # the GPU arm's rotation: CPU_COPIES separate copies of the weights (352 MiB),
+    # the GPU arm's rotation: N_COPIES separate copies of the weights (352 MiB),
     # so the timed GEMVs stream them from memory rather than from the last-level cache
-    copies = [packed.copy() for _ in range(CPU_COPIES)]
+    copies = [packed.copy() for _ in range(N_COPIES)]
     return fo, copies, rs, x
+
+
+def cpu_gemv_step(fo, copies, rs, x, step, threads):
+    """One headline step on the CPU: GROUP GEMVs over consecutive weight copies."""
+    for j in range(GROUP):
+        fo.ternary_matmul_packed_parallel_rows(copies[(step * GROUP + j) % N_COPIES], rs, x, ROWS,
+                                               COLS, threads)
 
 
 def cpu_baseline(seconds):
     """Oracle restatement of ternary_matmul_packed_parallel timed on all host cores."""
     fo, copies, rs, x = cpu_setup()
     threads = fo.num_threads(0)
-    fo.ternary_matmul_packed_parallel_rows(copies[0], rs, x, ROWS, COLS, threads)  # warm
+    cpu_gemv_step(fo, copies, rs, x, 0, threads)  # warm
     n, t0 = 0, time.perf_counter()
     while True:
-        fo.ternary_matmul_packed_parallel_rows(copies[n % CPU_COPIES], rs, x, ROWS, COLS, threads)
+        cpu_gemv_step(fo, copies, rs, x, n, threads)
         n += 1
         el = time.perf_counter() - t0
         if el >= seconds and n >= 3:
             break
-    return {"value": round(n * ALGO_BYTES / el / 1e9, 3), "unit": UNIT, "cores": threads,
+    return {"value": round(n * GROUP * ALGO_BYTES / el / 1e9, 3), "unit": UNIT, "cores": threads,
             "kind": "port",
-            "sample": f"{n} GEMVs [5632x2048] in {el:.1f} s (ternary_matmul_packed_parallel, "
-                      f"per-row scales, 32 row batches over {threads} threads; weights rotated "
-                      f"over {CPU_COPIES} copies, 352 MiB, as in the GPU arm)"}
+            "sample": f"{n} steps of {GROUP} GEMVs [5632x2048] in {el:.1f} s "
+                      f"(ternary_matmul_packed_parallel, per-row scales, 32 row batches over "
+                      f"{threads} threads; weights rotated over {N_COPIES} copies, 352 MiB, as "
+                      "in the GPU arm)"}
 
 
 def run_reference(args, ws, rank):
@@ -344,27 +376,32 @@ def run_reference(args, ws, rank):
         return None
     fo, copies, rs, x = cpu_setup()
     threads = fo.num_threads(0)
-    for i in range(args.warmup):
-        fo.ternary_matmul_packed_parallel_rows(copies[i % CPU_COPIES], rs, x, ROWS, COLS, threads)
-    steps = args.steps if args.steps <= 2000 else 2000  # bounded sample
-    t0 = time.perf_counter()
-    for i in range(steps):
-        fo.ternary_matmul_packed_parallel_rows(copies[i % CPU_COPIES], rs, x, ROWS, COLS, threads)
+    for i in range(min(args.warmup, 3)):
+        cpu_gemv_step(fo, copies, rs, x, i, threads)
+    # bounded sample: at most 60 s of CPU work, whatever --steps asks
+    steps, t0 = 0, time.perf_counter()
+    while steps < args.steps:
+        cpu_gemv_step(fo, copies, rs, x, steps, threads)
+        steps += 1
+        if time.perf_counter() - t0 > 60.0:
+            break
     el = time.perf_counter() - t0
-    value = steps * ALGO_BYTES / el / 1e9
+    value = steps * GROUP * ALGO_BYTES / el / 1e9
     return {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT,
         "n_gpus": ws, "steps": steps, "warmup": args.warmup, "ms_per_step": el * 1e3 / steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded)",
-        "config": {"workload": "cfg0 dense ternary GEMV x f32 [1,2048] . W [5632,2048]^T, "
-                               "per-row scales", "rows": ROWS, "cols": COLS, "seq": 1,
-                   "weight_copies": CPU_COPIES},
+        "config": {"workload": "cfg1 dense ternary GEMV x f32 [1,2048] . W [5632,2048]^T, "
+                               "per-row scales; one step = 64 GEMVs",
+                   "rows": ROWS, "cols": COLS, "seq": 1, "gemvs_per_step": GROUP,
+                   "weight_copies": N_COPIES},
         "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": f"{steps} GEMVs (requested {args.steps}); C restatement of "
-                                   "ternary_matmul_packed_parallel, src/model/ternary.rs:471-529; "
-                                   f"weights rotated over {CPU_COPIES} copies (352 MiB), as in "
-                                   "the GPU arm"},
+                         "sample": f"{steps} steps of {GROUP} GEMVs (requested {args.steps}; "
+                                   "capped at 60 s); C restatement of "
+                                   "ternary_matmul_packed_parallel, src/model/ternary.rs:471-529, "
+                                   f"on a persistent pool of {threads} threads; weights rotated "
+                                   f"over {N_COPIES} copies (352 MiB), as in the GPU arm"},
         "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -375,118 +412,128 @@ G_M, G_K, G_N = 512, 4096, 11008
 G_OPS = 2 * G_M * G_K * G_N
 
 
-def run_gemm(args, ws, rank, local):
+def run_gemm(args, torch, dist, device, local, sub_steps, cpu_seconds):
     """int8 prefill GEMM (bf16 x -> per-token absmax int8 ->
     exact int32 ternary matmul -> f32), W [11008, 4096] with P(0)=0.5.  One step
     = quantize + matmul; weights rotate over copies totalling > 2x L2."""
-    import torch
-
     from ferrisres_b200 import _lib, gpu
 
-    torch.cuda.set_device(local)
-    device = torch.device("cuda", local)
     n_copies = max(3, -(-2 * L2_BYTES // (G_N * G_K // 4)))
     weights = []
     g = torch.Generator(device=device)
-    import ctypes as C
-    from ferrisres_b200._lib import call
     ctx = gpu.get_context(local)
     for i in range(n_copies):
         g.manual_seed(100 + i)
         u = torch.rand(G_N * G_K, generator=g, device=device)
         codes = torch.where(u < 0.25, 0, torch.where(u < 0.75, 1, 2)).to(torch.int64)
-        words = (codes.view(-1, 16) << torch.arange(0, 32, 2, device=device)).sum(dim=1)
-        words = torch.where(words >= 2**31, words - 2**32, words).to(torch.int32).contiguous()
         scales = (torch.rand(G_N, generator=g, device=device) * 0.09 + 0.01).contiguous()
-        h = C.c_void_p()
-        call("ft_weight_from_device_u32", ctx.handle, C.c_void_p(words.data_ptr()), G_N, G_K,
-             C.c_void_p(scales.data_ptr()), C.c_void_p(torch.cuda.current_stream().cuda_stream),
-             C.byref(h))
-        torch.cuda.synchronize()
-        weights.append(gpu.DeviceTernaryWeight(h, G_N, G_K, ctx))
-        del u, codes, words
+        weights.append(_upload_u32(gpu, torch, ctx, _words_from_codes(torch, codes), G_N, G_K,
+                                   scales, device))
+        del u, codes
     g.manual_seed(7)
     xb = torch.randn(G_M, G_K, generator=g, device=device).to(torch.bfloat16)
     y = torch.empty(G_M, G_N, device=device)
+    q = torch.empty(G_M, G_K, dtype=torch.int8, device=device)
+    sx = torch.empty(G_M, dtype=torch.float32, device=device)
     stream = torch.cuda.Stream(device=device)
+    timer = Timer(torch, dist, stream, device, 1)
+    import ctypes as C
 
-    def step(i):
-        q, sx = gpu.quantize_absmax_i8(xb)
-        weights[i % n_copies].matmul_i8(q, sx, out=y)
+    from ferrisres_b200._lib import call
 
-    with torch.cuda.stream(stream):
-        for i in range(max(args.warmup, 3)):
-            step(i)
+    def step(i, quant=True):
+        s = C.c_void_p(stream.cuda_stream)
+        if quant:
+            call("ft_quantize_absmax_i8_bf16", ctx.handle, G_M, G_K, C.c_void_p(xb.data_ptr()),
+                 C.c_void_p(q.data_ptr()), C.c_void_p(sx.data_ptr()), s)
+        call("ft_ternary_matmul_i8", ctx.handle, weights[i % n_copies].handle, G_M,
+             C.c_void_p(q.data_ptr()), C.c_void_p(sx.data_ptr()), C.c_void_p(y.data_ptr()), s)
+
+    for i in range(3):
+        step(i)
     stream.synchronize()
     launches0 = _lib.lib().ft_launch_counter()
-    with torch.cuda.stream(stream):
-        step(0)
+    step(0)
     per_step = _lib.lib().ft_launch_counter() - launches0
     stream.synchronize()
     sampler = ClockSampler(local)
     sampler.start()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        e0.record(stream)
-        for i in range(args.steps):
-            step(i)
-        e1.record(stream)
-    torch.cuda.synchronize()
+    sec = timer(lambda: [step(i) for i in range(sub_steps)]) / sub_steps
     clocks = sampler.stop()
-    sec = e0.elapsed_time(e1) / 1e3
-    tops = args.steps * G_OPS / sec / 1e12
-    bf16_peak = None
-    try:
-        bf16_peak = float(json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["bf16_tflops"])
-    except Exception:
-        pass
-    peak = 2 * (bf16_peak or 1590.0)
-    return {
+    mm = timer(lambda: [step(i, False) for i in range(sub_steps)]) / sub_steps
+    _, bf16, kind = load_peaks()
+    peak = 2 * bf16
+    tops = G_OPS / sec / 1e12
+    res = {
         "metric": "ternary int8 prefill GEMM TOPS", "value": round(tops, 2), "unit": "TOPS",
-        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": sec * 1e3 / args.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded, generated on device)",
+        "steps": sub_steps, "ms_per_step": sec * 1e3, "dtype": "int8",
         "config": {"workload": "cfg2 prefill GEMM M=512 K=4096 N=11008, bf16 x -> absmax int8",
                    "weight_copies": n_copies, "l2": "weights rotate over copies > 2x L2"},
-        "roofline": {"bound": "tensor", "achieved": round(tops, 2), "peak": round(peak, 1),
-                     "unit": "TOP/s", "frac": round(tops / peak, 4),
-                     "peak_source": "2 x measured bf16 dense (int8 dense rate is twice bf16 on B200)"
-                                    if bf16_peak else "2 x fallback bf16",
+        "roofline": {"bound": "tensor", "achieved": round(G_OPS / mm / 1e12, 2),
+                     "peak": round(peak, 1), "unit": "TOP/s",
+                     "frac": round(G_OPS / mm / 1e12 / peak, 4),
+                     "peak_source": f"2 x {kind} bf16 dense burst (int8 dense rate is twice "
+                                    "bf16 on B200)",
                      "traffic": load_traffic().get("gemm_cfg2", {}).get("dram_bytes_per_launch"),
-                     "kernel": "tq_grouped_kernel<128, 0> (+ prep_b_kernel, quantize_i8_kernel)",
-                     "note": "achieved = the whole step's int ops (quantize + prep + matmul) / "
-                             "step time"},
-        "gpu_launches": int(per_step * args.steps),
+                     "kernel": "tq_grouped_kernel<128, false> (+ prep_b_kernel)",
+                     "ms_matmul": round(mm * 1e3, 4),
+                     "note": "achieved = int ops / device time of the matmul call alone "
+                             "(prep + tensor-core kernel); value includes the quantizer"},
+        "step_frac": round(tops / peak, 4),
+        "gpu_launches": int(per_step * sub_steps),
         "clocks": clocks,
     }
+    for w in weights:
+        w.close()
+    if cpu_seconds > 0:
+        res["cpu_baseline"] = gemm_cpu_baseline(cpu_seconds)
+    return res
+
+
+def gemm_cpu_baseline(seconds):
+    """Oracle restatement of ternary_matmul_parallel (over tokens) on int8 codes as f32,
+    on all host cores, over a bounded sample of the 512 tokens."""
+    from oracle import oracle as fo
+    rng = np.random.default_rng(0)
+    t = rng.choice(np.array([-1, 0, 1], np.int8), size=G_N * G_K, p=[0.25, 0.5, 0.25])
+    sw = rng.uniform(0.01, 0.1, G_N).astype(np.float32)
+    tok = 32
+    x = rng.standard_normal((tok, G_K)).astype(np.float32)
+    qx, sxs = fo.quantize_absmax_i8(x.ravel(), tok, G_K)
+    threads = fo.num_threads(0)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        fo.ternary_matmul_i8(t, qx, sxs, sw, tok, G_K, G_N, threads, via_f32=True)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds and n >= 2:
+            break
+    ops = n * 2 * tok * G_K * G_N
+    return {"value": round(ops / el / 1e12, 5), "unit": "TOPS", "cores": threads, "kind": "port",
+            "sample": f"{n} x {tok} of the 512 tokens in {el:.1f} s (ternary_matmul_parallel on "
+                      "the int8 codes as f32, src/model/ternary.rs:333-389, parallel over tokens)"}
 
 
 # ------------------------------------------------------------ cfg3 2:4 ---
 S_N, S_K = 14336, 4096
+S_GROUP, S_COPIES = 32, 64
 
 
-def run_sparse(args, ws, rank, local):
+def run_sparse(args, torch, dist, device, local, sub_steps, cpu_seconds):
     """2:4 sparse ternary matmul, K=4096, N=14336, fp32 x,
-    at M=1 (bandwidth-bound decode GEMV kernel, grouped launches of --group)
-    and M=64 (tensor-core engine).
-    Weights enter in the reference SparseTernaryMatrix layout and are stored
-    at 1.25 bits/weight; copies rotate beyond 2x L2."""
-    import numpy as np
-    import torch
+    at M=1 (decode GEMV kernel; one step = one launch of 32 GEMVs over distinct
+    weight copies) and M=64 (tensor-core engine).  Weights enter in the
+    reference SparseTernaryMatrix layout and are stored at 1.25 bits/weight;
+    copies rotate beyond 2x L2."""
+    from ferrisres_b200 import gpu
 
-    from ferrisres_b200 import _lib, gpu
-
-    torch.cuda.set_device(local)
-    device = torch.device("cuda", local)
     dev_bytes = (S_N // 128) * (S_K // 128) * 2560
     algo = dev_bytes + S_N * 4 + S_K * 4 + S_N * 4  # weights + scales + x + y per GEMV
-    group = min(args.group, 64)
-    n_copies = -(-max(4, -(-2 * L2_BYTES // dev_bytes)) // group) * group
     rng = np.random.default_rng(0)
     ng = S_N * S_K // 4
     weights = []
-    for i in range(n_copies):
-        if i < 8:  # 8 distinct matrices, uploaded as separate copies beyond that
+    for i in range(S_COPIES):
+        if i < 4:  # 4 distinct matrices, uploaded as separate copies beyond that
             lo = rng.integers(0, 6, size=(ng + 1) // 2, dtype=np.uint8)
             hi = rng.integers(0, 6, size=(ng + 1) // 2, dtype=np.uint8)
             pat = (lo | (hi << 4)).astype(np.uint8)
@@ -496,67 +543,91 @@ def run_sparse(args, ws, rank, local):
     assert weights[0].device_bytes() == dev_bytes + S_N * 4
     x1 = torch.randn(1, S_K, device=device)
     x64 = torch.randn(64, S_K, device=device)
-    ys = [torch.empty(1, S_N, device=device) for _ in range(n_copies)]
+    ys = [torch.empty(1, S_N, device=device) for _ in range(S_COPIES)]
     y64 = torch.empty(64, S_N, device=device)
-    calls = [gpu.GroupCall(weights[i:i + group], [x1] * group, ys[i:i + group])
-             for i in range(0, n_copies, group)]
+    calls = [gpu.GroupCall(weights[i:i + S_GROUP], [x1] * S_GROUP, ys[i:i + S_GROUP])
+             for i in range(0, S_COPIES, S_GROUP)]
     stream = torch.cuda.Stream(device=device)
+    timer = Timer(torch, dist, stream, device, 1)
     with torch.cuda.stream(stream):
         for c in calls:
             c()
         weights[0].matmul_f32(x64, out=y64)
     stream.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
-        for c in calls:
-            c()
-    reps = max(1, args.steps // n_copies)
-    sampler = ClockSampler(local)
-    sampler.start()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    graph = _graph_of(torch, stream, [calls[i % len(calls)] for i in range(sub_steps)])
     with torch.cuda.stream(stream):
         graph.replay()
-        e0.record(stream)
-        for _ in range(reps):
-            graph.replay()
-        e1.record(stream)
-    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    sec = timer(graph.replay) / sub_steps
     clocks = sampler.stop()
-    sec = e0.elapsed_time(e1) / 1e3
-    gbps = reps * n_copies * algo / sec / 1e9
-    # M = 64 (one matmul per step, weights rotating)
-    m64_steps = max(4, min(args.steps, 200))
+    gbps = S_GROUP * algo / sec / 1e9
+
+    def m64():
+        for i in range(sub_steps):
+            weights[i % S_COPIES].matmul_f32(x64, out=y64)
     with torch.cuda.stream(stream):
-        e0.record(stream)
-        for i in range(m64_steps):
-            weights[i % n_copies].matmul_f32(x64, out=y64)
-        e1.record(stream)
-    torch.cuda.synchronize()
-    sec64 = e0.elapsed_time(e1) / 1e3 / m64_steps
-    peak, peak_kind = load_peaks()
-    return {
+        m64()
+    sec64 = timer(lambda: m64()) / sub_steps
+    peak, _, kind = load_peaks()
+    del graph
+    for w in weights:
+        w.close()
+    res = {
         "metric": "2:4 sparse ternary GEMV HBM GB/s", "value": round(gbps, 2), "unit": "GB/s",
-        "n_gpus": 1, "steps": reps * n_copies, "warmup": n_copies,
-        "ms_per_step": sec * 1e3 / (reps * n_copies), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded 2:4 patterns and signs)",
-        "config": {"workload": "cfg3 2:4 sparse K=4096 N=14336, M=1 (grouped) and M=64",
-                   "device_bytes_per_weight": dev_bytes, "bits_per_weight": 1.25,
-                   "launch_group": group, "weight_copies": n_copies},
+        "steps": sub_steps, "ms_per_step": sec * 1e3, "dtype": "f32",
+        "config": {"workload": "cfg3 2:4 sparse K=4096 N=14336, M=1 (one step = one launch of "
+                               f"{S_GROUP} GEMVs) and M=64", "device_bytes_per_weight": dev_bytes,
+                   "bits_per_weight": 1.25, "weight_copies": S_COPIES,
+                   "l2": f"a step reads {S_GROUP * dev_bytes / 1e6:.0f} MB of weights (> L2)"},
         "roofline": {"bound": "hbm", "achieved": round(gbps, 2), "peak": peak, "unit": "GB/s",
-                     "frac": round(gbps / peak, 4), "peak_source": peak_kind,
-                     "algorithmic_bytes_per_gemv": algo,
-                     "traffic": load_traffic().get("sparse_cfg3", {}).get("dram_bytes_per_launch"),
-                     "traffic_launch": "64 GEMVs", "kernel": "gemv_kernel<1,64,true>"},
-        "m64": {"ms": round(sec64 * 1e3, 4), "TOPS_nonzero": round(2 * 64 * S_N * S_K / 2 / sec64 / 1e12, 2),
+                     "frac": round(gbps / peak, 4), "peak_source": kind,
+                     "algorithmic_bytes_per_launch": S_GROUP * algo,
+                     "traffic": _scaled_traffic("sparse_cfg3", S_GROUP / 64),
+                     "traffic_note": "DRAM bytes of a captured 64-GEMV launch x 32/64 (traffic "
+                                     "grows with the GEMVs per launch)",
+                     "kernel": "gemv_kernel<1, 64, true>"},
+        "m64": {"ms": round(sec64 * 1e3, 4),
+                "TOPS_nonzero": round(2 * 64 * S_N * S_K / 2 / sec64 / 1e12, 2),
                 "GBps_weights": round(dev_bytes / sec64 / 1e9, 1)},
-        "gpu_launches": int(reps * len(calls)),  # one decode-GEMV launch per grouped call
+        "gpu_launches": int(sub_steps),
         "clocks": clocks,
     }
+    if cpu_seconds > 0:
+        res["cpu_baseline"] = sparse_cpu_baseline(cpu_seconds, algo)
+    return res
+
+
+def sparse_cpu_baseline(seconds, algo):
+    """Oracle restatement of sparse_ternary_matmul (src/model/sparse_ternary.rs:203-252),
+    M=1, host layout, all host cores."""
+    from oracle import oracle as fo
+    rng = np.random.default_rng(0)
+    ng = S_N * S_K // 4
+    lo = rng.integers(0, 6, size=(ng + 1) // 2, dtype=np.uint8)
+    hi = rng.integers(0, 6, size=(ng + 1) // 2, dtype=np.uint8)
+    pat = (lo | (hi << 4)).astype(np.uint8)
+    sg = rng.integers(0, 256, size=(ng + 3) // 4, dtype=np.uint8)
+    rs = rng.uniform(0.01, 0.1, S_N).astype(np.float32)
+    x = rng.standard_normal(S_K).astype(np.float32)
+    threads = fo.num_threads(0)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        fo.sparse_ternary_matmul(pat, sg, 1.0, rs, S_N, S_K, x, 1, threads)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds and n >= 3:
+            break
+    return {"value": round(n * algo / el / 1e9, 3), "unit": "GB/s", "cores": threads,
+            "kind": "port",
+            "sample": f"{n} GEMVs (M=1) in {el:.1f} s; bytes counted as the GPU arm's "
+                      "algorithmic bytes per GEMV"}
 
 
 # ------------------------------------------------------------- cfg4 MoE ---
 M_E, M_H, M_F, M_T, M_K = 64, 2048, 1408, 4096, 2
 M_OPS = M_T * M_K * (3 * 2 * M_H * M_F) + 2 * M_T * M_E * M_H
+M_SAMPLE = 16  # tokens of rank 0's shard checked against the oracle
 
 
 def _rand_packed(rng, rows, cols):
@@ -565,37 +636,85 @@ def _rand_packed(rng, rows, cols):
     return (c[:, 0] | (c[:, 1] << 2) | (c[:, 2] << 4) | (c[:, 3] << 6)).astype(np.uint8)
 
 
-def run_moe(args, ws, rank, local):
+def _moe_expert(e):
+    """Expert e's packed gate/up/down bytes and row scales (seeded by e; the
+    same on every rank)."""
+    wrng = np.random.default_rng(1000 + e)
+    g = _rand_packed(wrng, M_F, M_H)
+    u = _rand_packed(wrng, M_F, M_H)
+    d = _rand_packed(wrng, M_H, M_F)
+    gs = wrng.uniform(0.01, 0.1, M_F).astype(np.float32)
+    us = wrng.uniform(0.01, 0.1, M_F).astype(np.float32)
+    ds = wrng.uniform(0.01, 0.1, M_H).astype(np.float32)
+    return g, u, d, gs, us, ds
+
+
+def _moe_router():
+    import torch
+    rng = np.random.default_rng(4)
+    router = (rng.standard_normal(M_E * M_H) * 0.02).astype(np.float32)
+    return torch.from_numpy(router).to(torch.bfloat16).float().numpy()  # bf16 router weights
+
+
+def moe_parity(x_sample, y_sample, router):
+    """Checks sampled tokens of the layer output against the oracle's
+    TernaryMoELayer::forward restatement (per-row scales).  Routing must agree
+    except on near-ties (k-th and (k+1)-th probabilities within 1e-6); outputs
+    of agreeing tokens within 1e-4 * rms(y_ref[t]) + 1e-7 per element."""
+    from oracle import oracle as fo
+    T = x_sample.shape[0]
+    x = x_sample.astype(np.float32)
+    # routing on the CPU first, to build only the experts the sample needs
+    logits = (x.astype(np.float64) @ router.reshape(M_E, M_H).T.astype(np.float64))
+    top = np.argsort(-logits, axis=1)[:, :M_K + 2]
+    need = sorted(set(top.ravel().tolist()))
+    zero_in = np.zeros(M_F * M_H, np.int8)
+    zero_s_f = np.zeros(M_F, np.float32)
+    zero_s_h = np.zeros(M_H, np.float32)
+    g, u, d, gs, us, ds = ([zero_in] * M_E, [zero_in] * M_E, [zero_in] * M_E, [zero_s_f] * M_E,
+                           [zero_s_f] * M_E, [zero_s_h] * M_E)
+    g, u, d, gs, us, ds = list(g), list(u), list(d), list(gs), list(us), list(ds)
+    for e in need:
+        pg, pu, pd, sg, su, sd = _moe_expert(e)
+        g[e] = fo.unpack_ternary(pg, M_F * M_H)
+        u[e] = fo.unpack_ternary(pu, M_F * M_H)
+        d[e] = fo.unpack_ternary(pd, M_H * M_F)
+        gs[e], us[e], ds[e] = sg, su, sd
+    ref_y, ref_route, ref_probs = fo.moe_forward(router, g, gs, u, us, d, ds, M_H, M_F, M_K,
+                                                 x.ravel(), T)
+    ref_y = ref_y.reshape(T, M_H).astype(np.float64)
+    ref_probs = ref_probs.reshape(T, M_E)
+    ref_route = ref_route.reshape(T, M_K)
+    if not set(ref_route.ravel().tolist()) <= set(need):
+        return {"ok": False, "why": "oracle routed to an expert outside the prepared set"}
+    srt = -np.sort(-ref_probs, axis=1)
+    near_tie = (srt[:, M_K - 1] - srt[:, M_K]) < 1e-6
+    rms = np.sqrt(np.mean(ref_y ** 2, axis=1, keepdims=True))
+    err = np.abs(y_sample.astype(np.float64) - ref_y) / (1e-4 * rms + 1e-7)
+    worst_tok = err.max(axis=1)
+    ok = bool(((worst_tok <= 1.0) | near_tie).all())
+    return {"ok": ok, "tokens": int(T), "near_ties": int(near_tie.sum()),
+            "worst_err_over_tol": round(float(worst_tok[~near_tie].max()) if (~near_tie).any()
+                                        else 0.0, 4),
+            "rule": "|y - y_ref| <= 1e-4 * rms(y_ref[t]) + 1e-7, near-ties excepted"}
+
+
+def run_moe(args, torch, dist, device, ws, rank, local, sub_steps, cpu_seconds):
     """ternary MoE FFN layer, 64 experts, H=2048, F=1408,
     SwiGLU, top-2, 4096 bf16 tokens; expert-parallel over the ranks (rank r
     holds experts [r*64/N, (r+1)*64/N) and routes 4096/N tokens).  One step = one
     layer forward over the global batch.  value = 4096 tokens / max-over-ranks
     device time (strong scaling: the layer and batch are fixed)."""
-    import datetime
-
-    import torch
-    import torch.distributed as dist
-
     from ferrisres_b200 import moe, moe_ep
 
-    torch.cuda.set_device(local)
-    device = torch.device("cuda", local)
-    if ws > 1 and not dist.is_initialized():
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
-    rng = np.random.default_rng(4)
-    router = (rng.standard_normal(M_E * M_H) * 0.02).astype(np.float32)
-    router = torch.from_numpy(router).to(torch.bfloat16).float().numpy()  # bf16 router weights
+    router = _moe_router()
     per = M_E // ws
     mine = range(rank * per, (rank + 1) * per)
     g, u, d, gs, us, ds = [], [], [], [], [], []
     for e in range(M_E):
-        wrng = np.random.default_rng(1000 + e)
         if e in mine:
-            g.append(_rand_packed(wrng, M_F, M_H)); u.append(_rand_packed(wrng, M_F, M_H))
-            d.append(_rand_packed(wrng, M_H, M_F))
-            gs.append(wrng.uniform(0.01, 0.1, M_F).astype(np.float32))
-            us.append(wrng.uniform(0.01, 0.1, M_F).astype(np.float32))
-            ds.append(wrng.uniform(0.01, 0.1, M_H).astype(np.float32))
+            pg, pu, pd, sg, su, sd = _moe_expert(e)
+            g.append(pg); u.append(pu); d.append(pd); gs.append(sg); us.append(su); ds.append(sd)
         else:
             for lst in (g, u, d, gs, us, ds):
                 lst.append(None)
@@ -605,41 +724,86 @@ def run_moe(args, ws, rank, local):
     x = torch.randn(M_T, M_H, generator=gx, device=device).to(torch.bfloat16)
     shard = x.chunk(ws)[rank].contiguous()
     stream = torch.cuda.Stream(device=device)
+    timer = Timer(torch, dist, stream, device, ws)
     with torch.cuda.stream(stream):
-        for _ in range(max(args.warmup, 3)):
+        for _ in range(3):
+            y = moe_ep.ep_forward(shard, be, M_E, rank, ws)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+
+    def steps():
+        for _ in range(sub_steps):
             moe_ep.ep_forward(shard, be, M_E, rank, ws)
+    sec = timer(steps) / sub_steps
+    clocks = sampler.stop()
+    # per-phase device times of one instrumented step (max over ranks)
+    marks, stats = [], {}
     torch.cuda.synchronize()
     if ws > 1:
         dist.barrier()
-    sampler = ClockSampler(local)
-    sampler.start()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
-        e0.record(stream)
-        for _ in range(args.steps):
-            moe_ep.ep_forward(shard, be, M_E, rank, ws)
-        e1.record(stream)
+        y = moe_ep.ep_forward(shard, be, M_E, rank, ws, marks=marks, stats=stats)
     torch.cuda.synchronize()
-    clocks = sampler.stop()
-    t = torch.tensor([e0.elapsed_time(e1) / 1e3], device=device, dtype=torch.float64)
+    ph = torch.tensor([marks[i - 1][1].elapsed_time(marks[i][1]) * 1e3
+                       for i in range(1, len(marks))], device=device, dtype=torch.float64)
     if ws > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    sec = float(t.item()) / args.steps
+        dist.all_reduce(ph, op=dist.ReduceOp.MAX)
+    phases = {marks[i][0]: round(float(ph[i - 1]), 1) for i in range(1, len(marks))}
+    nb = torch.tensor([stats.get("sent_rows_remote", 0) * M_H * 2,
+                       stats.get("recv_rows_remote", 0) * M_H * 4], device=device,
+                      dtype=torch.float64)
+    if ws > 1:
+        dist.all_reduce(nb)
+    parity = None
+    if rank == 0:
+        parity = moe_parity(shard[:M_SAMPLE].float().cpu().numpy(),
+                            y[:M_SAMPLE].cpu().numpy(), router)
+    if ws > 1:
+        dist.barrier()
+    layer.close()
     res = {
         "metric": "MoE-layer tokens/s", "value": round(M_T / sec, 1), "unit": "tokens/s",
-        "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3,
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (seeded ternary experts, bf16 router and tokens)",
+        "n_gpus": ws, "steps": sub_steps, "ms_per_step": sec * 1e3, "scaling": "strong",
+        "dtype": "bf16 x, ternary experts, exact int8-digit expert GEMMs",
         "config": {"workload": "cfg4 ternary MoE FFN: 64 experts, H=2048, F=1408, SwiGLU, top-2, "
                                "4096 tokens", "parallelism": f"ep{ws}",
                    "experts_per_gpu": per, "tokens_per_gpu": M_T // ws},
         "algorithmic_TOPS": round(M_OPS / sec / 1e12, 2),
+        "phases_us": phases,
+        "nccl_bytes_per_step": {"dispatch": int(nb[0].item()), "combine": int(nb[1].item()),
+                                "note": "rows sent to other ranks (bf16 in, fp32 out), all ranks"},
+        "parity": parity,
         "clocks": clocks,
     }
-    if ws > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    if rank == 0 and ws == 1 and cpu_seconds > 0:
+        res["cpu_baseline"] = moe_cpu_baseline(cpu_seconds, router)
     return res
+
+
+def moe_cpu_baseline(seconds, router):
+    """Oracle restatement of TernaryMoELayer::forward (per-row scales), parallel over
+    tokens on all host cores, over a bounded sample of tokens."""
+    from oracle import oracle as fo
+    g, u, d, gs, us, ds = [], [], [], [], [], []
+    for e in range(M_E):
+        pg, pu, pd, sg, su, sd = _moe_expert(e)
+        g.append(fo.unpack_ternary(pg, M_F * M_H)); u.append(fo.unpack_ternary(pu, M_F * M_H))
+        d.append(fo.unpack_ternary(pd, M_H * M_F)); gs.append(sg); us.append(su); ds.append(sd)
+    rng = np.random.default_rng(9)
+    tok = 64
+    x = rng.standard_normal(tok * M_H).astype(np.float32)
+    threads = fo.num_threads(0)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        fo.moe_forward(router, g, gs, u, us, d, ds, M_H, M_F, M_K, x, tok, nthreads=threads)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds and n >= 2:
+            break
+    return {"value": round(n * tok / el, 1), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{n} x {tok} tokens in {el:.1f} s (TernaryMoELayer::forward restated, "
+                      "src/model/ternary_moe.rs:145-223, parallel over tokens)"}
 
 
 # ---------------------------------------------------------- cfg5 3-bit KV --
@@ -649,25 +813,16 @@ KV_IO_BYTES = 2 * KV_B * KV_HQ * KV_D * 4                  # q in, out
 KV_ALGO_BYTES = KV_CACHE_BYTES + KV_IO_BYTES
 
 
-def run_kv(args, ws, rank, local):
+def run_kv(args, torch, dist, device, local, sub_steps, cpu_seconds):
     """TurboQuant 3-bit KV flash decode, B=32, Hq=32, Hkv=8,
     d=128, context 32768 (reference scheme: per-vector min/max, 3-bit codes).
     One step = append one position per sequence (bf16 K, V) + evict the oldest
     (the context stays at 32768) + flash decode over the cache.  value = the
-    step's algorithmic bytes (cache read + q/out) / device time, over all ranks
-    (replicas: each rank decodes its own batch)."""
-    import torch
-    import torch.distributed as dist
-
+    step's algorithmic bytes (cache read + q/out) / device time."""
     from ferrisres_b200 import _lib, kv
 
-    torch.cuda.set_device(local)
-    device = torch.device("cuda", local)
-    if ws > 1 and not dist.is_initialized():
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
     cache = kv.Kv3Cache(KV_B, KV_HKV, KV_S + 64, device=local)
-    gen = torch.Generator(device=device).manual_seed(5 + rank)
+    gen = torch.Generator(device=device).manual_seed(5)
     chunk = 4096
     for _ in range(KV_S // chunk):
         kk = torch.randn((KV_B, chunk, KV_HKV, KV_D), device=device, generator=gen).to(torch.bfloat16)
@@ -679,42 +834,25 @@ def run_kv(args, ws, rank, local):
     k1 = torch.randn((KV_B, 1, KV_HKV, KV_D), device=device, generator=gen).to(torch.bfloat16)
     v1 = torch.randn((KV_B, 1, KV_HKV, KV_D), device=device, generator=gen).to(torch.bfloat16)
     stream = torch.cuda.Stream(device=device)
+    timer = Timer(torch, dist, stream, device, 1)
 
     def step():
         cache.append(k1, v1, stream=stream)
         cache.evict_front(1)
         cache.flash_decode(q, out=out, stream=stream)
 
-    for _ in range(max(args.warmup, 3)):
+    for _ in range(3):
         step()
     stream.synchronize()
-    if ws > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-
-    def timed(fn, n):
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(n):
-            fn()
-        e1.record(stream)
-        torch.cuda.synchronize()
-        t = torch.tensor([e0.elapsed_time(e1) / 1e3], device=device, dtype=torch.float64)
-        if ws > 1:
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
     launches0 = _lib.lib().ft_launch_counter()
     sampler = ClockSampler(local)
     sampler.start()
-    sec = timed(step, args.steps)
+    step_s = timer(lambda: [step() for _ in range(sub_steps)]) / sub_steps
     clocks = sampler.stop()
     gpu_launches = _lib.lib().ft_launch_counter() - launches0
-    # the dominant kernel alone (decode + split combine), for the roofline
-    n_dec = max(5, min(args.steps, 50))
-    dec_sec = timed(lambda: cache.flash_decode(q, out=out, stream=stream), n_dec) / n_dec
-    step_s = sec / args.steps
-    value = ws * KV_ALGO_BYTES / step_s / 1e9
+    dec_s = timer(lambda: [cache.flash_decode(q, out=out, stream=stream)
+                           for _ in range(sub_steps)]) / sub_steps
+    value = KV_ALGO_BYTES / step_s / 1e9
 
     # end to end through the public API with host buffers: q and the new K/V
     # from pinned host memory, the output read back every step
@@ -724,11 +862,9 @@ def run_kv(args, ws, rank, local):
     kh.copy_(k1.cpu())
     oh = torch.empty_like(out, device="cpu").pin_memory()
     qd, kd, vd = torch.empty_like(q), torch.empty_like(k1), torch.empty_like(v1)
-    n_e2e = max(3, min(args.steps, 50))
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    with torch.cuda.stream(stream):
-        for _ in range(n_e2e):
+
+    def e2e_steps():
+        for _ in range(sub_steps):
             qd.copy_(qh, non_blocking=True)
             kd.copy_(kh, non_blocking=True)
             vd.copy_(kh, non_blocking=True)
@@ -736,47 +872,34 @@ def run_kv(args, ws, rank, local):
             cache.evict_front(1)
             cache.flash_decode(qd, out=out, stream=stream)
             oh.copy_(out, non_blocking=True)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    t = torch.tensor([e0.elapsed_time(e1) / 1e3 / n_e2e], device=device, dtype=torch.float64)
-    if ws > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    e2e_value = ws * KV_ALGO_BYTES / float(t.item()) / 1e9
+    e2e_s = timer(e2e_steps) / sub_steps
     cache.ctx.check()
-
-    peak, peak_kind = load_peaks()
-    traffic = load_traffic().get("kv_cfg5", {}).get("dram_bytes_per_launch")
-    dec_gbs = KV_ALGO_BYTES / dec_sec / 1e9
+    peak, _, kind = load_peaks()
+    dec_gbs = KV_ALGO_BYTES / dec_s / 1e9
+    cache.close()
     res = {
         "metric": "3-bit KV flash-decode HBM GB/s", "value": round(value, 2), "unit": "GB/s",
-        "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8 codes / f32",
-        "data": "synthetic (K, V ~ N(0,1) bf16 quantised to 3 bits; q ~ N(0,1))",
+        "steps": sub_steps, "ms_per_step": step_s * 1e3, "dtype": "u8 codes / f32",
         "config": {"workload": "cfg5 3-bit KV flash decode: B=32, Hq=32, Hkv=8, d=128, ctx 32768, "
                                "reference TurboQuantKVCache scheme (min/max per 128-vector)",
                    "step": "append 1 position + evict oldest + decode",
                    "l2": f"cache {KV_CACHE_BYTES / 2**20:.0f} MiB > L2",
-                   "parallelism": f"replicas x{ws}",
-                   "decode_tokens_per_s": round(ws * KV_B / step_s, 1)},
+                   "decode_tokens_per_s": round(KV_B / step_s, 1)},
         "roofline": {"bound": "hbm", "achieved": round(dec_gbs, 2), "peak": peak, "unit": "GB/s",
-                     "frac": round(dec_gbs / peak, 4), "peak_source": peak_kind,
-                     "traffic": traffic, "kernel": "kv3_decode_kernel (+ kv3_combine_kernel)",
+                     "frac": round(dec_gbs / peak, 4), "peak_source": kind,
+                     "traffic": load_traffic().get("kv_cfg5", {}).get("dram_bytes_per_launch"),
+                     "kernel": "kv3_decode_kernel (+ kv3_combine_kernel)",
                      "algorithmic_bytes_per_launch": KV_ALGO_BYTES,
-                     "note": "112 B per (sequence, position, kv head) + q/out; decode launch "
-                             "timed alone with CUDA events"},
-        "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
+                     "note": "112 B per (sequence, position, kv head) + q/out; decode timed alone"},
+        "e2e": {"value": round(KV_ALGO_BYTES / e2e_s / 1e9, 2), "unit": "GB/s",
                 "h2d_bytes_per_step": q.numel() * 4 + 2 * k1.numel() * 2,
-                "d2h_bytes_per_step": out.numel() * 4, "steps": n_e2e,
+                "d2h_bytes_per_step": out.numel() * 4,
                 "api": "Kv3Cache.append + flash_decode (ft_kv3_append, ft_flash_decode_3bit)"},
         "gpu_launches": int(gpu_launches),
         "clocks": clocks,
     }
-    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
-        res["cpu_baseline"] = kv_cpu_baseline(args.cpu_seconds)
-    cache.close()
-    if ws > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    if cpu_seconds > 0:
+        res["cpu_baseline"] = kv_cpu_baseline(cpu_seconds)
     return res
 
 
@@ -807,34 +930,65 @@ def kv_cpu_baseline(seconds):
                       f"(get_range dequant + flash_decode_ref, parallel over heads)"}
 
 
+# -------------------------------------------------------------------- main --
+def _compact(d):
+    drop = ("metric", "higher_is_better", "scaling", "vs_baseline", "data")
+    return {k: v for k, v in d.items() if k not in drop}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20000)
-    ap.add_argument("--warmup", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--group", type=int, default=64, help="GEMVs per launch (1..64)")
-    ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--workload", choices=["gemv", "gemm_cfg2", "sparse_cfg3", "moe_cfg4", "kv_cfg5"],
-                    default="gemv",
-                    help="gemv = the headline cfg0 line; gemm_cfg2 = the int8 prefill GEMM")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0,
+                    help="headline CPU baseline sample (s); each sub-config uses a third")
+    ap.add_argument("--workload", choices=["all", "gemv", "gemm_cfg2", "sparse_cfg3", "moe_cfg4",
+                                           "kv_cfg5"], default="all",
+                    help="all = the headline GEMV line with every config as a sub-object")
+    ap.add_argument("--sub-steps", type=int, default=0,
+                    help="steps of each sub-config (default: max(--steps, 10), at most 200)")
     args = ap.parse_args()
     ws, rank, local = dist_env()
     if args.gpus != ws and ws > 1:
         print(f"warning: --gpus {args.gpus} but WORLD_SIZE={ws}", file=sys.stderr)
-    if args.workload == "gemm_cfg2" and args.impl == "ours":
-        res = run_gemm(args, ws, rank, local)
-    elif args.workload == "sparse_cfg3" and args.impl == "ours":
-        res = run_sparse(args, ws, rank, local)
-    elif args.workload == "moe_cfg4" and args.impl == "ours":
-        res = run_moe(args, ws, rank, local)
-    elif args.workload == "kv_cfg5" and args.impl == "ours":
-        res = run_kv(args, ws, rank, local)
-    elif args.impl == "reference":
+    if args.impl == "reference":
         res = run_reference(args, ws, rank)
-    else:
-        res = run_ours(args, ws, rank, local)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if ws > 1 and not dist.is_initialized():
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    sub_steps = args.sub_steps or min(max(args.steps, 10), 200)
+    cpu_s = 0.0 if args.no_cpu_baseline or rank != 0 or ws != 1 else args.cpu_seconds
+    sub_cpu = cpu_s / 3
+    res = None
+    w = args.workload
+    if w in ("all", "gemv"):
+        res = run_gemv(args, ws, rank, local, torch, dist, device)
+        if cpu_s > 0:
+            res["cpu_baseline"] = cpu_baseline(cpu_s)
+    if w in ("all", "moe_cfg4"):
+        r = run_moe(args, torch, dist, device, ws, rank, local, sub_steps, sub_cpu)
+        res = r if res is None else {**res, "moe_cfg4": _compact(r)}
+    if ws == 1:
+        for name, fn in (("gemm_cfg2", run_gemm), ("sparse_cfg3", run_sparse),
+                         ("kv_cfg5", run_kv)):
+            if w in ("all", name):
+                torch.cuda.empty_cache()
+                r = fn(args, torch, dist, device, local, sub_steps, sub_cpu)
+                res = r if res is None else {**res, name: _compact(r)}
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
     if rank == 0 and res is not None:
         print(json.dumps(res), flush=True)
 

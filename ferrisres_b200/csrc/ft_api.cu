@@ -66,7 +66,6 @@ int zero_scratch_reserve(ft_ctx* ctx, size_t bytes, cudaStream_t stream) {
     FT_CUDA(cudaFree(ctx->zs.ptr));
     ctx->zs.ptr = nullptr;
     ctx->zs.bytes = 0;
-    ctx->err_flag = nullptr;
   }
   size_t grow = bytes + bytes / 4 + (1 << 20);
   FT_CUDA(cudaMalloc(&ctx->zs.ptr, grow));
@@ -166,7 +165,6 @@ int ft_ctx_create(int device, ft_ctx** out) {
     delete c;
     return fail(FT_ERR_GPU, "error word allocation failed: %s", cudaGetErrorString(se));
   }
-  c->err_flag = c->err_word;
   *out = c;
   return FT_OK;
 }
@@ -391,7 +389,7 @@ int ft_ctx_check(ft_ctx* ctx) {
   FT_CHECK(ctx, FT_ERR_SHAPE, "null context");
   DeviceGuard g(ctx->device);
   FT_CUDA(cudaDeviceSynchronize());
-  int* words[2] = {ctx->err_word, ctx->err_flag != ctx->err_word ? ctx->err_flag : nullptr};
+  int* words[2] = {ctx->err_word, ctx->na_err};
   for (int* wd : words) {
     if (!wd) continue;
     int code = 0;

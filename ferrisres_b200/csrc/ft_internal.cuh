@@ -90,8 +90,8 @@ struct ft_ctx {
   void* hio_dev = nullptr;             // device mapping of hio.ptr (null if not mapped)
   ft::Workspace zs;                    // zero-initialised scratch (split-K sums, tickets)
   int* err_word = nullptr;             // device word set by a kernel whose bounded wait gave up
-  int* err_flag = nullptr;             // word of the latest launch (err_word, or the static
-                                       // word of the allocation-free entry point)
+  int* na_err = nullptr;               // the allocation-free entry point's static error word,
+                                       // once this context has used that entry point (sticky)
 };
 
 struct ft_weight {

@@ -817,7 +817,6 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
                               src_k[j], src_seq[j], sxs ? sxs[i] : nullptr, ys[i],
                               ldys ? ldys[i] : w->rows};
     }
-    ctx->err_flag = ctx->err_word;
     return launch_gemv(ctx, nlive, gp, xkind, ws[live[0]]->format == 1, s);
   }
 
@@ -903,7 +902,6 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
       batch.p[q].cnt = reinterpret_cast<int32_t*>(zs + cnt_off[q]);
     }
   batch.err = ctx->err_word;
-  ctx->err_flag = ctx->err_word;
 
   // prep launch: one block per source x pass x token slot of the operand
   {
@@ -1032,8 +1030,6 @@ int launch_tc_noalloc(ft_ctx* ctx, const ft_weight* w, int64_t seq, const float*
   char* zs = nullptr;
   int st = noalloc_scratch(ctx->device, &zs);
   if (st != FT_OK) return st;
-  // the split-K sums, tickets and error word must start at zero
-  FT_CUDA(cudaMemsetAsync(zs + kNaAccOff, 0, kNaBytes - kNaAccOff, s));
 
   const int D = 4, npad = kNaNpad, tok_per_pass = npad / D;
   static thread_local TqBatch batch;
@@ -1065,8 +1061,16 @@ int launch_tc_noalloc(ft_ctx* ctx, const ft_weight* w, int64_t seq, const float*
   p.acc = reinterpret_cast<int32_t*>(zs + kNaAccOff);
   p.cnt = reinterpret_cast<int32_t*>(zs + kNaCntOff);
   batch.total_items = w->n_tiles * p.ksplit;
+  // The split-K sums and tickets this call uses must start at zero (the kernel
+  // leaves them zeroed, but a launch whose wait gave up may not have).  The
+  // error word is not cleared here: it keeps a report until ft_ctx_check of a
+  // context that used this entry point reads and clears it.
+  if (p.ksplit > 1) {
+    FT_CUDA(cudaMemsetAsync(zs + kNaAccOff, 0, (size_t)w->n_tiles * kNaNpad * kTileRows * 4, s));
+    FT_CUDA(cudaMemsetAsync(zs + kNaCntOff, 0, (size_t)w->n_tiles * 4, s));
+  }
   batch.err = reinterpret_cast<int*>(zs + kNaErrOff);
-  ctx->err_flag = batch.err;
+  ctx->na_err = batch.err;
 
   static thread_local PrepBatch pb;
   memset(&pb, 0, sizeof(pb));

@@ -90,40 +90,63 @@ class GpuMoEBackend:
         return y
 
 
-def ep_forward(x, backend, n_experts, rank=0, world=1, group=None):
-    """One expert-parallel MoE forward of this rank's tokens x [T, H]."""
+def ep_forward(x, backend, n_experts, rank=0, world=1, group=None, marks=None, stats=None):
+    """One expert-parallel MoE forward of this rank's tokens x [T, H].
+
+    ``marks`` (optional list): a CUDA event is recorded on the current stream
+    after each phase and appended as (phase name, event), for per-phase
+    timing.  ``stats`` (optional dict) receives the rows this rank sent to and
+    received from other ranks."""
+
+    def mark(name):
+        if marks is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            marks.append((name, ev))
+
     E = n_experts
     if E % world:
         raise ShapeError(f"{E} experts do not split over {world} ranks")
     per = E // world
     H = x.shape[1]
+    mark("start")
     idx, w, counts = backend.route(x)
     slot_of, token_of = backend.layout(idx, counts)
     xg = backend.gather(x, token_of)  # [T*K, H], expert-major
+    mark("route")
     if world == 1:
         ac = counts.cpu().numpy().reshape(1, E).astype(np.int64)
     else:
         parts = [torch.empty_like(counts) for _ in range(world)]
         dist.all_gather(parts, counts, group=group)
         ac = torch.stack(parts).cpu().numpy().astype(np.int64)  # [src rank, expert]
+    mark("counts")
     send_rows = [int(ac[rank, d * per:(d + 1) * per].sum()) for d in range(world)]
     recv_rows = [int(ac[s, rank * per:(rank + 1) * per].sum()) for s in range(world)]
+    if stats is not None:
+        stats["sent_rows_remote"] = sum(n for d, n in enumerate(send_rows) if d != rank)
+        stats["recv_rows_remote"] = sum(n for s, n in enumerate(recv_rows) if s != rank)
     if world == 1:
         recv = xg
     else:
         recv = torch.empty(sum(recv_rows), H, dtype=xg.dtype, device=xg.device)
         dist.all_to_all_single(recv.view(-1), xg.reshape(-1), [r * H for r in recv_rows],
                                [r * H for r in send_rows], group=group)
+    mark("dispatch")
     seg_e, seg_n = [], []
     for s in range(world):
         for e in range(rank * per, (rank + 1) * per):
             seg_e.append(e)
             seg_n.append(int(ac[s, e]))
     o_recv = backend.experts(seg_e, seg_n, recv)
+    mark("experts")
     if world == 1:
         o_send = o_recv
     else:
         o_send = torch.empty(xg.shape[0], H, dtype=o_recv.dtype, device=xg.device)
         dist.all_to_all_single(o_send.view(-1), o_recv.view(-1), [r * H for r in send_rows],
                                [r * H for r in recv_rows], group=group)
-    return backend.combine(o_send, slot_of, w)
+    mark("combine")
+    y = backend.combine(o_send, slot_of, w)
+    mark("sum")
+    return y

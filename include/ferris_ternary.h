@@ -136,7 +136,10 @@ int ft_ternary_matmul_i8_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws,
  * that first call before any stream capture.  All calls share the array (each
  * clears what must start at zero), so calls that overlap on the GPU -- other
  * streams, other host threads, other contexts on the same device -- race:
- * order them. */
+ * order them.  Its kernels record a bounded wait that gave up in an error word
+ * inside the same array; the word keeps that report across later calls until
+ * ft_ctx_check on a context that has used this entry point (on that device)
+ * reads and clears it. */
 int ft_ternary_matmul_f32_noalloc(ft_ctx* ctx, const ft_weight* w, int64_t seq, const float* x_dev,
                                   float* y_dev, void* stream);
 /* Per-token absmax int8 quantizer: sx[s] = absmax/127 (1 when absmax == 0),

@@ -47,6 +47,47 @@ int fo_num_threads(int requested) {
   return n > 0 ? (int)n : 1;
 }
 
+/* Persistent worker threads (rayon's global pool is persistent too, so a timed
+ * call pays no thread creation).  Workers sleep on a condition variable and
+ * wake for each job; the calling thread works as well.  One job at a time. */
+typedef struct {
+  pthread_mutex_t mu;
+  pthread_cond_t start, done;
+  pthread_mutex_t call_mu; /* serialises callers from several host threads */
+  int nworkers;            /* threads created so far */
+  int want;                /* workers 0..want-1 take part in the current job */
+  int finished;            /* of those, how many are done */
+  unsigned gen;            /* job generation */
+  fo_pool_job* job;
+} fo_pool;
+
+static fo_pool g_pool = {PTHREAD_MUTEX_INITIALIZER, PTHREAD_COND_INITIALIZER,
+                         PTHREAD_COND_INITIALIZER, PTHREAD_MUTEX_INITIALIZER, 0, 0, 0, 0, NULL};
+
+typedef struct {
+  int id;
+  unsigned born; /* generation before the first job this thread may take */
+} fo_thread_arg;
+
+static void* fo_pool_thread(void* arg) {
+  const fo_thread_arg a = *(const fo_thread_arg*)arg;
+  free(arg);
+  const int id = a.id;
+  unsigned seen = a.born;
+  pthread_mutex_lock(&g_pool.mu);
+  for (;;) {
+    while (g_pool.gen == seen) pthread_cond_wait(&g_pool.start, &g_pool.mu);
+    seen = g_pool.gen;
+    if (id >= g_pool.want) continue;
+    fo_pool_job* job = g_pool.job;
+    pthread_mutex_unlock(&g_pool.mu);
+    fo_worker(job);
+    pthread_mutex_lock(&g_pool.mu);
+    if (++g_pool.finished == g_pool.want) pthread_cond_signal(&g_pool.done);
+  }
+  return NULL;
+}
+
 static void fo_parallel_for(size_t n, int nthreads, fo_item_fn fn, void* ctx) {
   int t = fo_num_threads(nthreads);
   if ((size_t)t > n) t = (int)n;
@@ -59,11 +100,33 @@ static void fo_parallel_for(size_t n, int nthreads, fo_item_fn fn, void* ctx) {
     fo_worker(&job);
     return;
   }
-  pthread_t* th = (pthread_t*)malloc(sizeof(pthread_t) * (size_t)(t - 1));
-  for (int i = 0; i < t - 1; ++i) pthread_create(&th[i], NULL, fo_worker, &job);
+  pthread_mutex_lock(&g_pool.call_mu);
+  pthread_mutex_lock(&g_pool.mu);
+  while (g_pool.nworkers < t - 1) {
+    pthread_t th;
+    fo_thread_arg* a = (fo_thread_arg*)malloc(sizeof(fo_thread_arg));
+    if (!a) break;
+    a->id = g_pool.nworkers;
+    a->born = g_pool.gen;
+    if (pthread_create(&th, NULL, fo_pool_thread, a) != 0) {
+      free(a);
+      break;
+    }
+    pthread_detach(th);
+    ++g_pool.nworkers;
+  }
+  g_pool.want = g_pool.nworkers < t - 1 ? g_pool.nworkers : t - 1;
+  g_pool.finished = 0;
+  g_pool.job = &job;
+  ++g_pool.gen;
+  pthread_cond_broadcast(&g_pool.start);
+  pthread_mutex_unlock(&g_pool.mu);
   fo_worker(&job);
-  for (int i = 0; i < t - 1; ++i) pthread_join(th[i], NULL);
-  free(th);
+  pthread_mutex_lock(&g_pool.mu);
+  while (g_pool.finished < g_pool.want) pthread_cond_wait(&g_pool.done, &g_pool.mu);
+  g_pool.job = NULL;
+  pthread_mutex_unlock(&g_pool.mu);
+  pthread_mutex_unlock(&g_pool.call_mu);
 }
 
 /* ------------------------------------------------------------------------ */
