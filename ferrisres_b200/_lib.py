@@ -67,6 +67,7 @@ SIGNATURES = {
     "ft_weight_upload_packed_u32": [_p, _p, _i64, _i64, _p, _p],
     "ft_weight_from_device_u32": [_p, _p, _i64, _i64, _p, _p, _p],
     "ft_weight_destroy": [_p],
+    "ft_weight_export_packed_u8": [_p, _p, _p],
     "ft_sparse_upload_host": [_p, _p, _p, _i64, _i64, _p, _p],
     "ft_sparse_upload_wgsl": [_p, _p, _i64, _i64, _p, _p],
     "ft_gpu_sparse_ternary_matmul": [_p, _p, C.c_float, _p, _sz, _sz, _sz, _p],
@@ -76,6 +77,12 @@ SIGNATURES = {
     "ft_ternary_matmul_f32_grouped": [_p, _i, _p, _i64, _p, _p, _p],
     "ft_ternary_matmul_i8_grouped": [_p, _i, _p, _i64, _p, _p, _p, _p],
     "ft_ternary_matmul_f32_noalloc": [_p, _p, _i64, _p, _p, _p],
+    "ft_ternary_matmul_blocked_f32": [_p, _p, _i64, _p, _p, _i64, _p, _p],
+    "ft_weight_upload_index_lists": [_p, _i64, _i64, _p, _p, _p, _p, _p, _p],
+    "ft_weight_quantize_f32": [_p, _p, _i64, _i64, _p, _p],
+    "ft_weight_requantize": [_p, _p, _p, _i, C.c_float, _p],
+    "ft_shadow_alpha": [_p, _i, _p, _p, _i, _p],
+    "ft_moe_create_f32": [_p, _i64, _i64, _i64, _i, _i, _p, _p, _p, _p, _p],
     "ft_quantize_absmax_i8_f32": [_p, _i64, _i64, _p, _p, _p, _p],
     "ft_quantize_absmax_i8_bf16": [_p, _i64, _i64, _p, _p, _p, _p],
     "ft_ternary_matmul_i8": [_p, _p, _i64, _p, _p, _p, _p],
@@ -86,6 +93,7 @@ SIGNATURES = {
     "ft_moe_destroy": [_p],
     "ft_moe_forward": [_p, _p, _i64, _p, _i, _p, _p, _p],
     "ft_moe_forward_host": [_p, _p, _p, _sz, _p],
+    "ft_moe_decode": [_p, _p, _i64, _p, _i, _p, _p, _p, _p, _p],
     "ft_moe_route": [_p, _p, _i64, _p, _i, _p, _p, _p, _p, _p],
     "ft_moe_dispatch_layout": [_p, _p, _i64, _p, _p, _p, _p, _p, _p, _p],
     "ft_moe_gather_rows": [_p, _p, _i, _i64, _p, _i64, _p, _p],

@@ -86,8 +86,7 @@ struct DeviceGuard {
   }
 };
 
-static int alloc_weight(ft_ctx* ctx, int64_t rows, int64_t cols, ft_weight** out,
-                        int format = 0) {
+int alloc_weight(ft_ctx* ctx, int64_t rows, int64_t cols, ft_weight** out, int format) {
   FT_CHECK(ctx && out, FT_ERR_SHAPE, "null argument");
   FT_CHECK(rows > 0 && cols > 0, FT_ERR_SHAPE, "weight shape [%lld, %lld] must be positive",
            (long long)rows, (long long)cols);
@@ -113,6 +112,15 @@ static int alloc_weight(ft_ctx* ctx, int64_t rows, int64_t cols, ft_weight** out
   }
   *out = w;
   return FT_OK;
+}
+
+float host_absmean_alpha(const float* w, int64_t n) {
+  // Iterator::sum over f32 is a sequential left fold; the compiler keeps this
+  // order (no reassociation without fast-math).
+  float sum_abs = 0.0f;
+  for (int64_t i = 0; i < n; ++i) sum_abs += fabsf(w[i]);
+  const float ABSMEAN_NORM = 0.7978845608f;  // src/model/ternary.rs:15
+  return sum_abs > 0.0f ? (sum_abs / (float)n) / ABSMEAN_NORM : 1.0f;
 }
 
 static int finish_scales(ft_weight* w, const float* scales, bool host, cudaStream_t s) {
@@ -536,6 +544,154 @@ int ft_gpu_ternary_matmul_vram(ft_ctx* ctx, const ft_weight* w, const float* inp
   if (ky == dy) FT_CUDA(cudaMemcpyAsync(dst, dy, out_bytes, cudaMemcpyDeviceToHost, s));
   FT_CUDA(cudaStreamSynchronize(s));
   if (!out_pinned) std::memcpy(output_host, dst, out_bytes);
+  return FT_OK;
+}
+
+// ---- block-scale, index-list and fp32-ingestion entry points ------------
+
+int ft_ternary_matmul_blocked_f32(ft_ctx* ctx, const ft_weight* w, int64_t seq, const float* x_dev,
+                                  const float* block_scales_dev, int64_t block_size, float* y_dev,
+                                  void* stream) {
+  FT_CHECK(ctx && w, FT_ERR_SHAPE, "null context or weight");
+  FT_CHECK(seq >= 0, FT_ERR_SHAPE, "seq must be >= 0");
+  FT_CHECK(block_size >= 1, FT_ERR_SHAPE, "block_size must be >= 1");
+  FT_CHECK(seq == 0 || (x_dev && y_dev && block_scales_dev), FT_ERR_SHAPE, "null pointer");
+  FT_CHECK(w->device == ctx->device, FT_ERR_DEVICE, "weight lives on device %d, context on %d",
+           w->device, ctx->device);
+  if (seq == 0) return FT_OK;
+  DeviceGuard g(ctx->device);
+  const ft_weight* ws[1] = {w};
+  const void* xs[1] = {x_dev};
+  float* ys[1] = {y_dev};
+  return launch_tc_grouped(ctx, 1, ws, seq, xs, 0, nullptr, ys, nullptr,
+                           static_cast<cudaStream_t>(stream), nullptr, 0, block_scales_dev,
+                           block_size);
+}
+
+int ft_weight_upload_index_lists(ft_ctx* ctx, int64_t rows, int64_t cols, const int64_t* pos_off,
+                                 const int64_t* pos_idx, const int64_t* neg_off,
+                                 const int64_t* neg_idx, const float* row_scales_host,
+                                 ft_weight** out) {
+  FT_CHECK(ctx && out && pos_off && neg_off && row_scales_host, FT_ERR_SHAPE, "null argument");
+  FT_CHECK(rows > 0 && cols > 0, FT_ERR_SHAPE, "shape [%lld, %lld] must be positive",
+           (long long)rows, (long long)cols);
+  FT_CHECK(pos_off[0] == 0 && neg_off[0] == 0, FT_ERR_SHAPE, "offsets must start at 0");
+  FT_CHECK((pos_off[rows] == 0 || pos_idx) && (neg_off[rows] == 0 || neg_idx), FT_ERR_SHAPE,
+           "null index array");
+  // The flat pack_ternary stream: all zero weights (code 1), then the lists'
+  // columns set to +1 (code 2) or -1 (code 0).  Each row's lists must be
+  // strictly increasing, in range, and disjoint (what ternary_sparse_indices
+  // produces): a 2-bit code holds one weight per position.
+  std::vector<uint8_t> packed((size_t)((rows * cols + 3) / 4), 0x55);
+  for (int64_t r = 0; r < rows; ++r) {
+    FT_CHECK(pos_off[r + 1] >= pos_off[r] && neg_off[r + 1] >= neg_off[r], FT_ERR_SHAPE,
+             "row %lld: offsets decrease", (long long)r);
+    for (int sign = 0; sign < 2; ++sign) {
+      const int64_t* off = sign ? neg_off : pos_off;
+      const int64_t* idx = sign ? neg_idx : pos_idx;
+      int64_t last = -1;
+      for (int64_t i = off[r]; i < off[r + 1]; ++i) {
+        const int64_t j = idx[i];
+        FT_CHECK(j > last && j < cols, FT_ERR_SHAPE,
+                 "row %lld: column %lld out of range or out of order", (long long)r, (long long)j);
+        last = j;
+        const int64_t f = r * cols + j;
+        uint8_t& byte = packed[(size_t)(f >> 2)];
+        const int sh = (int)(f & 3) * 2;
+        FT_CHECK(((byte >> sh) & 3) == 1, FT_ERR_SHAPE,
+                 "row %lld: column %lld is in both the +1 and the -1 list", (long long)r,
+                 (long long)j);
+        byte = (uint8_t)((byte & ~(3 << sh)) | ((sign ? 0 : 2) << sh));
+      }
+    }
+  }
+  return ft_weight_upload_packed_u8(ctx, packed.data(), rows, cols, row_scales_host, out);
+}
+
+int ft_weight_quantize_f32(ft_ctx* ctx, const float* w_host, int64_t rows, int64_t cols,
+                           float* alpha_out, ft_weight** out) {
+  FT_CHECK(ctx && w_host && out, FT_ERR_SHAPE, "null argument");
+  DeviceGuard g(ctx->device);
+  ft_weight* w = nullptr;
+  int st = alloc_weight(ctx, rows, cols, &w);
+  if (st != FT_OK) return st;
+  const float alpha = host_absmean_alpha(w_host, rows * cols);
+  cudaStream_t s = ctx->host_stream;
+  float* staging = nullptr;
+  const size_t nbytes = (size_t)(rows * cols) * 4;
+  cudaError_t e = cudaMalloc(&staging, nbytes);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(staging, w_host, nbytes, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess) st = launch_fill_scales(w, alpha, s);
+  if (e == cudaSuccess && st == FT_OK) st = launch_quantize_pack(staging, false, 0, w, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (staging) cudaFree(staging);
+  if (e != cudaSuccess || st != FT_OK) {
+    ft_weight_destroy(w);
+    if (e != cudaSuccess) return fail(FT_ERR_GPU, "quantize upload failed: %s", cudaGetErrorString(e));
+    return st;
+  }
+  if (alpha_out) *alpha_out = alpha;
+  *out = w;
+  return FT_OK;
+}
+
+int ft_weight_requantize(ft_ctx* ctx, ft_weight* w, const void* src_dev, int src_bf16, float alpha,
+                         void* stream) {
+  FT_CHECK(ctx && w && src_dev, FT_ERR_SHAPE, "null argument");
+  FT_CHECK(w->format == 0, FT_ERR_UNSUPPORTED, "requantize needs a dense weight");
+  FT_CHECK(w->device == ctx->device, FT_ERR_DEVICE, "weight lives on device %d, context on %d",
+           w->device, ctx->device);
+  DeviceGuard g(ctx->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int st = launch_fill_scales(w, alpha, s);
+  if (st != FT_OK) return st;
+  return launch_quantize_pack(src_dev, src_bf16 != 0, 1, w, s);
+}
+
+int ft_shadow_alpha(ft_ctx* ctx, int n, const void* const* src_dev, const int64_t* counts,
+                    int src_bf16, float* alpha_out) {
+  FT_CHECK(ctx && alpha_out && (n == 0 || (src_dev && counts)), FT_ERR_SHAPE, "null argument");
+  FT_CHECK(n >= 0, FT_ERR_SHAPE, "negative buffer count");
+  DeviceGuard g(ctx->device);
+  int64_t total = 0;
+  for (int i = 0; i < n; ++i) {
+    FT_CHECK(counts[i] >= 0 && (counts[i] == 0 || src_dev[i]), FT_ERR_SHAPE, "bad buffer %d", i);
+    total += counts[i];
+  }
+  if (total == 0) return FT_OK;  // the reference keeps the previous alpha
+  cudaStream_t s = ctx->host_stream;
+  double* acc = nullptr;
+  FT_CUDA(cudaMalloc(&acc, sizeof(double)));
+  cudaError_t e = cudaMemsetAsync(acc, 0, sizeof(double), s);
+  int st = FT_OK;
+  for (int i = 0; i < n && e == cudaSuccess && st == FT_OK; ++i)
+    st = launch_abs_sum(src_dev[i], src_bf16 != 0, counts[i], acc, s);
+  double sum = 0.0;
+  if (e == cudaSuccess) e = cudaMemcpyAsync(&sum, acc, sizeof(double), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  cudaFree(acc);
+  if (st != FT_OK) return st;
+  FT_CHECK(e == cudaSuccess, FT_ERR_GPU, "abs-sum failed: %s", cudaGetErrorString(e));
+  *alpha_out = (float)(sum / (double)total);
+  return FT_OK;
+}
+
+int ft_weight_export_packed_u8(ft_ctx* ctx, const ft_weight* w, uint8_t* packed_host) {
+  FT_CHECK(ctx && w && packed_host, FT_ERR_SHAPE, "null argument");
+  FT_CHECK(w->device == ctx->device, FT_ERR_DEVICE, "weight lives on device %d, context on %d",
+           w->device, ctx->device);
+  DeviceGuard g(ctx->device);
+  cudaStream_t s = ctx->host_stream;
+  const size_t nbytes = (size_t)((w->rows * w->cols + 3) / 4);
+  uint8_t* staging = nullptr;
+  FT_CUDA(cudaMalloc(&staging, nbytes));
+  int st = launch_export_u8(w, staging, s);
+  cudaError_t e = cudaSuccess;
+  if (st == FT_OK) e = cudaMemcpyAsync(packed_host, staging, nbytes, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  cudaFree(staging);
+  if (st != FT_OK) return st;
+  FT_CHECK(e == cudaSuccess, FT_ERR_GPU, "export failed: %s", cudaGetErrorString(e));
   return FT_OK;
 }
 

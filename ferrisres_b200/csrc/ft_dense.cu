@@ -164,6 +164,104 @@ __global__ void wgsl_op_kernel(const uint32_t* __restrict__ words, const float* 
   if (lane == 0) y[(int64_t)s * out_rows + row] = sum * scales[row];
 }
 
+// ------------------------------------------------------- quantize + pack --
+// One thread per output u32 word of the tiled layout: quantizes the word's 16
+// source elements (fp32, or bf16 bit patterns) to codes.  alpha = row_alpha[R]:
+//   mode 0, absmean (quantize_ternary, src/model/ternary.rs:31-57):
+//     q = clamp(round_half_away(v * (1 / alpha)), -1, 1); NaN -> 0 (Rust's
+//     `as i32` maps NaN to 0);
+//   mode 1, STE requantize (BitMoELayer::requantize_all,
+//     src/training/bit_moe.rs:243-262): n = v / alpha, q = +1 if n > 0.5,
+//     -1 if n < -0.5, else 0; alpha < 1e-10 gives 0.
+__global__ void quantize_pack_kernel(const void* __restrict__ src, int bf16, int64_t rows,
+                                     int64_t cols, int64_t n_chunks, int64_t total_words,
+                                     const float* __restrict__ row_alpha, int mode,
+                                     uint32_t* __restrict__ dst) {
+  const int64_t gw = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (gw >= total_words) return;
+  const int64_t block = gw >> 10;
+  const int within = (int)(gw & 1023);
+  const int mb = within >> 7, lane = (within >> 2) & 31, wi = within & 3;
+  const int g = lane >> 2, r = lane & 3;
+  const int64_t tile = block / n_chunks, chunk = block % n_chunks;
+  const int64_t R = tile * kTileRows + 16 * mb + g + 8 * (wi & 1);
+  float inv = 0.0f, alpha = 0.0f;
+  if (R < rows) {
+    alpha = row_alpha[R];
+    inv = 1.0f / alpha;
+  }
+  uint32_t out = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const int64_t k = chunk * kChunkK + 32 * j + 16 * (wi >> 1) + 4 * r + b;
+      uint32_t code = 1u;
+      if (R < rows && k < cols) {
+        const int64_t i = R * cols + k;
+        const float v = bf16 ? __uint_as_float((uint32_t) static_cast<const uint16_t*>(src)[i] << 16)
+                             : static_cast<const float*>(src)[i];
+        int q = 0;
+        if (mode == 0) {
+          const float rv = roundf(__fmul_rn(v, inv));
+          q = rv != rv ? 0 : (rv >= 1.0f ? 1 : (rv <= -1.0f ? -1 : 0));
+        } else if (!(alpha < 1e-10f)) {
+          const float n = __fdiv_rn(v, alpha);
+          q = n > 0.5f ? 1 : (n < -0.5f ? -1 : 0);
+        }
+        code = (uint32_t)(q + 1);
+      }
+      out |= code << (8 * b + 2 * j);
+    }
+  dst[gw] = out;
+}
+
+__global__ void fill_scales_kernel(float* __restrict__ dst, int64_t rows, int64_t padded,
+                                   float alpha) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < padded) dst[i] = i < rows ? alpha : 0.0f;
+}
+
+// Sum of |v| over n elements (fp32 or bf16) in f64, added into *acc.
+__global__ void abs_sum_kernel(const void* __restrict__ src, int bf16, int64_t n,
+                               double* __restrict__ acc) {
+  double part = 0.0;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float v = bf16 ? __uint_as_float((uint32_t) static_cast<const uint16_t*>(src)[i] << 16)
+                         : static_cast<const float*>(src)[i];
+    part += (double)fabsf(v);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+  __shared__ double red[32];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = part;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
+    atomicAdd(acc, t);
+  }
+}
+
+// One thread per byte of the reference pack_ternary stream (4 codes, LSB
+// first): reads the codes back from the resident layout (dense or 2:4).
+__global__ void export_u8_kernel(const uint8_t* __restrict__ codes, int format, int64_t rows,
+                                 int64_t cols, int64_t n_chunks, int64_t nbytes,
+                                 uint8_t* __restrict__ out) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= nbytes) return;
+  uint32_t b = 0;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const int64_t f = 4 * i + e;
+    if (f >= rows * cols) break;  // padding bits stay 0, as pack_ternary leaves them
+    const int w = weight_at(codes, format, n_chunks, f / cols, f % cols);
+    b |= (uint32_t)(w + 1) << (2 * e);
+  }
+  out[i] = (uint8_t)b;
+}
+
 }  // namespace
 
 int launch_repack_u8(const uint8_t* packed, int64_t rows, int64_t cols, ft_weight* w,
@@ -216,6 +314,40 @@ int launch_wgsl_op(const uint32_t* words, const float* scales, const float* x, f
   if (warps == 0) return FT_OK;
   wgsl_op_kernel<<<(unsigned)ceil_div(warps * 32, 256), 256, 0, s>>>(words, scales, x, y, seq,
                                                                     in_cols, out_rows);
+  FT_LAUNCH_CHECK();
+  return FT_OK;
+}
+
+int launch_quantize_pack(const void* src, bool bf16, int mode, ft_weight* w, cudaStream_t s) {
+  const int64_t total = w->n_tiles * w->n_chunks * (kBlockBytes / 4);
+  quantize_pack_kernel<<<(unsigned)ceil_div(total, 256), 256, 0, s>>>(
+      src, bf16 ? 1 : 0, w->rows, w->cols, w->n_chunks, total, w->row_scales, mode,
+      reinterpret_cast<uint32_t*>(w->codes));
+  FT_LAUNCH_CHECK();
+  return FT_OK;
+}
+
+int launch_fill_scales(ft_weight* w, float alpha, cudaStream_t s) {
+  const int64_t padded = w->n_tiles * kTileRows;
+  fill_scales_kernel<<<(unsigned)ceil_div(padded, 256), 256, 0, s>>>(w->row_scales, w->rows, padded,
+                                                                     alpha);
+  FT_LAUNCH_CHECK();
+  return FT_OK;
+}
+
+int launch_abs_sum(const void* src, bool bf16, int64_t n, double* acc, cudaStream_t s) {
+  if (n <= 0) return FT_OK;
+  int64_t blocks = ceil_div(n, 256 * 8);
+  if (blocks > 1184) blocks = 1184;
+  abs_sum_kernel<<<(unsigned)blocks, 256, 0, s>>>(src, bf16 ? 1 : 0, n, acc);
+  FT_LAUNCH_CHECK();
+  return FT_OK;
+}
+
+int launch_export_u8(const ft_weight* w, uint8_t* out, cudaStream_t s) {
+  const int64_t nbytes = (w->rows * w->cols + 3) / 4;
+  export_u8_kernel<<<(unsigned)ceil_div(nbytes, 256), 256, 0, s>>>(w->codes, w->format, w->rows,
+                                                                   w->cols, w->n_chunks, nbytes, out);
   FT_LAUNCH_CHECK();
   return FT_OK;
 }

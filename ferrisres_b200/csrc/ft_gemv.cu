@@ -1,13 +1,18 @@
 // Decode-shape ternary matmul (GEMV and small M): y = scale * (W . x) for a
 // group of independent problems whose activations fit 16 operand columns
-// (fp32/bf16: <= 4 tokens as 4 base-256 digits each; int8: <= 16 tokens).
+// (fp32/bf16: <= 2 tokens as 8 base-256 digits each, or <= 4 tokens as 4
+// digits; int8: <= 16 tokens).
 //
 // Same exact formulation as the tensor-core engine (ft_tc.cu): the A operand
 // is the unsigned codes u = w + 1, the B operand the int8 activation columns
 // (fp32/bf16: the signed base-256 digits of X = round(x * 2^s), 2^s the power
-// of two that puts the token's absmax in [2^29, 2^30); int8: the caller's
-// codes), int32 sums are exact, the epilogue subtracts the column sums and
-// scales.  The MMAs are warp-level (mma.sync m16n8k32, u8 x s8).
+// of two that puts the token's largest finite |x| in [2^(8D-3), 2^(8D-2));
+// int8: the caller's codes), int32 sums are exact, the epilogue subtracts the
+// column sums and scales.  With D = 8 every element within 2^38 of the token's
+// absmax is represented exactly, so the result is the correctly rounded dot
+// product.  The MMAs are warp-level (mma.sync m16n8k32, u8 x s8).  Non-finite
+// activations enter the digits as 0; their positions are kept per token and
+// the rows that meet them are finished by the reference's rule (nonfinite_row).
 //
 // Weight stream: the lane-major block layout (ft_internal.cuh) gives every
 // lane 16 contiguous bytes of an m-block per 128-K chunk, and code slot j of
@@ -63,6 +68,12 @@ namespace {
 #ifndef FT_GV_DEPTH2
 #define FT_GV_DEPTH2 8
 #endif
+#ifndef FT_GV_GRID_SMALL
+#define FT_GV_GRID_SMALL 2
+#endif
+#ifndef FT_GV_GRID_LARGE
+#define FT_GV_GRID_LARGE 2
+#endif
 #ifndef FT_GV_SLEEP_NS
 #define FT_GV_SLEEP_NS 1000  // suspend hint of the ring waits (woken when the copy lands)
 #endif
@@ -98,17 +109,17 @@ constexpr int unit_mb(int nb, bool sp, bool small) {
 }
 template <int NB, bool SP, bool SMALL>
 struct GvUnit {
-  static constexpr int MB = unit_mb(NB, SP, SMALL), CTAS = GvCfg<NB>::CTAS;
+  static constexpr int MB = unit_mb(NB, SP, SMALL);
   static constexpr int DEPTH = SP ? (NB == 1 ? FT_GV_SPDEPTH1 : FT_GV_SPDEPTH2)
                                   : (MB != GvCfg<NB>::MB ? FT_GV_DEPTH1S : GvCfg<NB>::DEPTH);
   static constexpr int MU = SP ? 20 : 32;    // uint4 per m-block of one chunk
-  static constexpr int BU = SP ? 160 : 256;  // uint4 per block (tile, chunk)
   static constexpr uint32_t BYTES = MB * MU * 16;  // one unit
 };
 
 struct GvSeg {  // one activation source and the problems that read it
   const void* x;  // [seq, K]: f32, bf16 or int8 codes
-  int64_t K;
+  const float* kscale;  // column-block scales folded into x (blocked matmul), or null
+  int64_t K, kblock;
   int32_t units;         // sum over its problems of row-blocks x chunks (< 2^31)
   int32_t q_cta, r_cta;  // units / n_cta, units % n_cta: CTA c starts near c*q + min(c, r)
   int32_t seq, n_chunks;
@@ -199,6 +210,21 @@ __device__ __forceinline__ int cta_boundary(const PT& P, const GvSeg& s, int c) 
 }
 
 __device__ __forceinline__ float4 load_x4(const void* x, int xkind, int64_t row, int64_t k,
+                                          int64_t K);
+
+// load_x4 with the segment's column-block scales applied (x' = scale * x)
+__device__ __forceinline__ float4 load_xs4(const GvSeg& S, int xkind, int64_t row, int64_t k) {
+  float4 v = load_x4(S.x, xkind, row, k, S.K);
+  if (S.kscale) {
+    float* e = reinterpret_cast<float*>(&v);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      if (k + i < S.K) e[i] = __fmul_rn(e[i], S.kscale[(k + i) / S.kblock]);
+  }
+  return v;
+}
+
+__device__ __forceinline__ float4 load_x4(const void* x, int xkind, int64_t row, int64_t k,
                                           int64_t K) {
   // elements k .. k+3 of row `row` (zero past K)
   float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
@@ -286,21 +312,67 @@ __device__ __forceinline__ void prod_next(Producer& w, const PT& P) {
   }
 }
 
-// lane 0: the current unit into ring slot `dst`, completion counted on `bar`
+// lane 0: the current unit into ring slot `dst`, completion counted on `bar`;
+// the weights are read once per launch, so they are marked evict-first in L2.
 template <int MB, bool SP>
-__device__ __forceinline__ void prod_copy(const Producer& w, uint32_t dst, uint32_t bar) {
+__device__ __forceinline__ void prod_copy(const Producer& w, uint32_t dst, uint32_t bar,
+                                          uint64_t policy) {
   constexpr uint32_t bytes = MB * (SP ? 320u : 512u);
   tc::mbar_arrive_expect_tx(bar, bytes);
-  tc::bulk_g2s(dst, w.base + w.off, bytes, bar);
+  tc::bulk_g2s_hint(dst, w.base + w.off, bytes, bar, policy);
 }
+
+// Non-finite activations of the CTA's segment (shared memory): count and the
+// first kNfCap positions per token, and what the fix-up needs to read weights.
+struct GvNf {
+  const int* cnt;             // [4]
+  const int (*pos)[kNfCap];   // [4][kNfCap]
+  const void* x;              // segment activations [seq, K]
+  int64_t K;
+  bool bf16;
+  int format;
+  const float* kscale;        // column-block scales, or null
+  int64_t kblock;
+};
 
 // Output of one row-block (MB m-blocks) from its exact digit sums fin:
 // fin[m][nb][e] = rows 16m + g (+8 for e >= 2), column 8nb + 2r + (e & 1).
 template <int NB, int MB>
 __device__ __forceinline__ void rowblock_store(const int (&fin)[MB][NB][4], const GvProb& q, int rb,
                                                int seq, int D, const int* colsum,
-                                               const double* tok_scale, int g, int r) {
+                                               const double* tok_scale, const GvNf& nf, int g,
+                                               int r) {
   const int64_t rbase = (int64_t)rb * (16 * MB);
+  auto finish = [&](int t, int64_t R, float y) {
+    if (nf.cnt[t] != 0)
+      y = nonfinite_row(y, reinterpret_cast<const uint8_t*>(q.codes), nf.format, q.n_chunks, R,
+                        static_cast<const char*>(nf.x) + (int64_t)t * nf.K * (nf.bf16 ? 2 : 4),
+                        nf.bf16, nf.K, nf.pos[t], nf.cnt[t], q.row_scales[R], nf.kscale,
+                        nf.kblock);
+    q.y[t * q.ldy + R] = y;
+  };
+  if (D == 8) {
+    // token t = nb: lane r holds digits 2r and 2r + 1 of both row halves
+#pragma unroll
+    for (int m = 0; m < MB; ++m)
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb) {
+        if (nb >= seq) continue;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int n0 = 8 * nb + 2 * r;
+          double part = (double)(fin[m][nb][2 * h] - colsum[n0]) * (double)(1ll << (16 * r)) +
+                        (double)(fin[m][nb][2 * h + 1] - colsum[n0 + 1]) *
+                            (double)(1ll << (16 * r + 8));
+          part += __shfl_xor_sync(0xffffffffu, part, 1);
+          part += __shfl_xor_sync(0xffffffffu, part, 2);
+          const int64_t R = rbase + 16 * m + g + 8 * h;
+          if (r == 0 && R < q.rows)
+            finish(nb, R, (float)(part * tok_scale[nb] * (double)q.row_scales[R]));
+        }
+      }
+    return;
+  }
   if (D == 1) {
 #pragma unroll
     for (int m = 0; m < MB; ++m)
@@ -335,14 +407,16 @@ __device__ __forceinline__ void rowblock_store(const int (&fin)[MB][NB][4], cons
             const long long d2 = hi[2 * h] - colsum[n0 + 2];
             const long long d3 = hi[2 * h + 1] - colsum[n0 + 3];
             const long long s4 = d0 + d1 * 256 + d2 * 65536 + d3 * 16777216;
-            q.y[t * q.ldy + R] = (float)((double)s4 * tok_scale[t] * (double)q.row_scales[R]);
+            finish(t, R, (float)((double)s4 * tok_scale[t] * (double)q.row_scales[R]));
           }
         }
       }
   }
 }
 
-template <int NB, int NP, bool SP>
+// DT: digits per token (1: int8 codes; 4 or 8: fp32/bf16), a template
+// parameter so that each instance carries only its own operand build.
+template <int NB, int NP, bool SP, int DT>
 __global__ void __launch_bounds__(kThreads, GvCfg<NB>::CTAS)
     gemv_kernel(const __grid_constant__ GvParamsT<NP> P) {
   using U = GvUnit<NB, SP, (NP <= kSmallProb)>;
@@ -357,6 +431,9 @@ __global__ void __launch_bounds__(kThreads, GvCfg<NB>::CTAS)
   __shared__ int colsum[16];
   __shared__ double tok_scale[4];
   __shared__ float red_f[kW][4];
+  __shared__ int red_n[kW][4];
+  __shared__ int nf_cnt[4];
+  __shared__ int nf_pos[4][kNfCap];
   __shared__ int part_id[kW];
   __shared__ uint32_t s_lut[SP ? 32 : 1];  // 2:4 group code -> A register (bytes w + 1)
   __shared__ __align__(8) uint64_t full_bar[kW][kDepth];
@@ -387,11 +464,12 @@ __global__ void __launch_bounds__(kThreads, GvCfg<NB>::CTAS)
     tc::fence_barrier_init();
   }
   __syncwarp();
+  const uint64_t l2_policy = tc::policy_evict_first();
   int issued = 0;
 #pragma unroll
   for (int d = 0; d < kDepth; ++d) {
     if (issued < n) {
-      if (lane == 0) prod_copy<MB, SP>(pr, ring_s + d * U::BYTES, bar_s + 8 * d);
+      if (lane == 0) prod_copy<MB, SP>(pr, ring_s + d * U::BYTES, bar_s + 8 * d, l2_policy);
       prod_next<MB, SP>(pr, P);
       ++issued;
     }
@@ -414,12 +492,17 @@ __global__ void __launch_bounds__(kThreads, GvCfg<NB>::CTAS)
 
   // ---- activation fragments of this CTA's segment (after the previous grid)
   tc::pdl_wait();
-  const int D = P.D, seq = S.seq;
+  constexpr int D = DT;
+  const int seq = S.seq;
   const int nquad = S.n_chunks * 32;
   {
-    uint4* f4 = reinterpret_cast<uint4*>(frag);
-    for (int i = tid; i < S.n_chunks * NB * 64; i += kThreads) f4[i] = make_uint4(0, 0, 0, 0);
+    // columns no token uses must read as zero
+    if (D * seq < 8 * NB) {
+      uint4* f4 = reinterpret_cast<uint4*>(frag);
+      for (int i = tid; i < S.n_chunks * NB * 64; i += kThreads) f4[i] = make_uint4(0, 0, 0, 0);
+    }
     if (tid < 16) colsum[tid] = 0;
+    if (tid < 4) nf_cnt[tid] = 0;
     if (tid < kW) part_id[tid] = -1;
   }
   if (D == 1) __syncthreads();  // zero-fill above before the word stores below
@@ -427,63 +510,137 @@ __global__ void __launch_bounds__(kThreads, GvCfg<NB>::CTAS)
   // and the digit split (K up to 4 * kRQ * kThreads in one load).
   constexpr int kRQ = 4;
   for (int t = 0; t < seq; ++t) {
-    int cs[4] = {0, 0, 0, 0};
-    if (D == 4) {
+    int cs[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (D != 1) {
       float4 xr[kRQ];
       float am = 0.0f;
+      int nnf = 0;  // this thread's non-finite elements
+      auto scan = [&](float4& v) {
+        float* e = reinterpret_cast<float*>(&v);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          if (is_nonfinite(e[i])) {
+            ++nnf;
+            e[i] = 0.0f;
+          }
+          am = fmaxf(am, fabsf(e[i]));
+        }
+      };
 #pragma unroll
       for (int j = 0; j < kRQ; ++j) {
         const int q = tid + j * kThreads;
-        xr[j] = q < nquad ? load_x4(S.x, P.xkind, t, 4 * (int64_t)q, S.K)
+        xr[j] = q < nquad ? load_xs4(S, P.xkind, t, 4 * (int64_t)q)
                           : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        am = fmaxf(am, fmaxf(fmaxf(fabsf(xr[j].x), fabsf(xr[j].y)),
-                             fmaxf(fabsf(xr[j].z), fabsf(xr[j].w))));
+        scan(xr[j]);
       }
       for (int q = tid + kRQ * kThreads; q < nquad; q += kThreads) {
-        const float4 v = load_x4(S.x, P.xkind, t, 4 * (int64_t)q, S.K);
-        am = fmaxf(am, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+        float4 v = load_xs4(S, P.xkind, t, 4 * (int64_t)q);
+        scan(v);
       }
+      // warp: absmax, and an exclusive scan of the non-finite counts (only
+      // when the warp holds any)
+      int nf_before = 0, nf_warp = 0;
+      if (__any_sync(0xffffffffu, nnf != 0)) {
+        int incl = nnf;
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-      if (lane == 0) red_f[warp][t] = am;
+        for (int o = 1; o < 32; o <<= 1) {
+          const int v = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += v;
+        }
+        nf_before = incl - nnf;
+        nf_warp = __shfl_sync(0xffffffffu, incl, 31);
+      }
+      // |x| >= 0 orders like its bit pattern: one warp-wide integer max
+      am = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(am)));
+      if (lane == 0) {
+        red_f[warp][t] = am;
+        red_n[warp][t] = nf_warp;
+      }
       __syncthreads();
       float a = 0.0f;
+      int nf_tot = 0;
 #pragma unroll
-      for (int w = 0; w < kW; ++w) a = fmaxf(a, red_f[w][t]);
-      // 2^sh puts a in [2^29, 2^30): sh = 30 - ex for a = m * 2^ex, m in [0.5, 1)
-      const uint32_t ebits = __float_as_uint(a) >> 23;
-      int sh = 0;
-      if (ebits != 0u && ebits < 255u) {
-        sh = 156 - (int)ebits;
-      } else if (a > 0.0f && ebits == 0u) {
-        int ex = 0;
-        frexpf(a, &ex);  // subnormal absmax
-        sh = 30 - ex;
+      for (int w = 0; w < kW; ++w) {
+        a = fmaxf(a, red_f[w][t]);
+        if (w < warp) nf_before += red_n[w][t];
+        nf_tot += red_n[w][t];
       }
+      if (nf_tot != 0) {
+        // record this thread's non-finite positions (in K order within the
+        // thread; the fix-up does not depend on the order)
+        if (tid == 0) nf_cnt[t] = nf_tot;
+        if (nnf != 0 && nf_tot <= kNfCap) {
+          int slot = nf_before;
+          for (int q = tid; q < nquad; q += kThreads) {
+            const float4 v = load_xs4(S, P.xkind, t, 4 * (int64_t)q);
+            const float e4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              if (is_nonfinite(e4[i])) nf_pos[t][slot++] = 4 * q + i;
+          }
+        }
+      }
+      const int sh = a > 0.0f ? digit_shift(a, D) : 0;
       if (tid == 0) tok_scale[t] = a > 0.0f ? __longlong_as_double((long long)(1023 - sh) << 52) : 0.0;
       const int s1 = sh > 127 ? 127 : (sh < -126 ? -126 : sh);
       const float f1 = __int_as_float((s1 + 127) << 23);
       const float f2 = __int_as_float((sh - s1 + 127) << 23);
-      // X = round(x * 2^sh), |X| < 2^30.  With U = X + 0x808080 the low three
-      // bytes of U are the low signed base-256 digits + 128 and the top byte
-      // is the top digit (|.| <= 64): byte permutes gather digit d of the four
-      // elements into word d, the XOR re-signs the low three.
-      auto split = [&](const float4 v, int q) {
-        const uint32_t u0 = (uint32_t)__float2int_rn(__fmul_rn(__fmul_rn(v.x, f1), f2)) + 0x808080u;
-        const uint32_t u1 = (uint32_t)__float2int_rn(__fmul_rn(__fmul_rn(v.y, f1), f2)) + 0x808080u;
-        const uint32_t u2 = (uint32_t)__float2int_rn(__fmul_rn(__fmul_rn(v.z, f1), f2)) + 0x808080u;
-        const uint32_t u3 = (uint32_t)__float2int_rn(__fmul_rn(__fmul_rn(v.w, f1), f2)) + 0x808080u;
+      // Byte permutes gather digit d of four elements (bytes of U0..U3) into
+      // one word: [byte d of U0, U1, U2, U3].
+      auto gather = [](uint32_t u0, uint32_t u1, uint32_t u2, uint32_t u3, uint32_t (&wd)[4]) {
         const uint32_t lo01 = __byte_perm(u0, u1, 0x5140), lo23 = __byte_perm(u2, u3, 0x5140);
         const uint32_t hi01 = __byte_perm(u0, u1, 0x7362), hi23 = __byte_perm(u2, u3, 0x7362);
-        const uint32_t wd[4] = {__byte_perm(lo01, lo23, 0x5410) ^ 0x80808080u,
-                                __byte_perm(lo01, lo23, 0x7632) ^ 0x80808080u,
-                                __byte_perm(hi01, hi23, 0x5410) ^ 0x80808080u,
-                                __byte_perm(hi01, hi23, 0x7632)};
-        const int base = frag_word<SP>(q, 4 * t, NB);  // digit d: lane + 4d, word + 16d
+        wd[0] = __byte_perm(lo01, lo23, 0x5410);
+        wd[1] = __byte_perm(lo01, lo23, 0x7632);
+        wd[2] = __byte_perm(hi01, hi23, 0x5410);
+        wd[3] = __byte_perm(hi01, hi23, 0x7632);
+      };
+      auto split = [&](float4 v, int q) {
+        if (q >= kRQ * kThreads) {  // reloaded quads: non-finite -> 0
+          if (is_nonfinite(v.x)) v.x = 0.0f;
+          if (is_nonfinite(v.y)) v.y = 0.0f;
+          if (is_nonfinite(v.z)) v.z = 0.0f;
+          if (is_nonfinite(v.w)) v.w = 0.0f;
+        }
+        const int base = frag_word<SP>(q, D * t, NB);  // digit d: lane + 4d, word + 16d
+        if (D == 4) {
+          // X = round(x * 2^sh), |X| < 2^30.  With U = X + 0x808080 the low
+          // three bytes of U are the low signed base-256 digits + 128 and the
+          // top byte is the top digit (|.| <= 64); the XOR re-signs the low three.
+          uint32_t wd[4];
+          gather((uint32_t)__float2int_rn(__fmul_rn(__fmul_rn(v.x, f1), f2)) + 0x808080u,
+                 (uint32_t)__float2int_rn(__fmul_rn(__fmul_rn(v.y, f1), f2)) + 0x808080u,
+                 (uint32_t)__float2int_rn(__fmul_rn(__fmul_rn(v.z, f1), f2)) + 0x808080u,
+                 (uint32_t)__float2int_rn(__fmul_rn(__fmul_rn(v.w, f1), f2)) + 0x808080u, wd);
+          wd[0] ^= 0x80808080u;
+          wd[1] ^= 0x80808080u;
+          wd[2] ^= 0x80808080u;
 #pragma unroll
-        for (int d = 0; d < 4; ++d) {
-          cs[d] = __dp4a((int)wd[d], 0x01010101, cs[d]);
-          frag[base + 16 * d] = wd[d];
+          for (int d = 0; d < 4; ++d) {
+            cs[d] = __dp4a((int)wd[d], 0x01010101, cs[d]);
+            frag[base + 16 * d] = wd[d];
+          }
+        } else {
+          // X = round(x * 2^sh), |X| < 2^62, U = X + 0x0080808080808080: bytes
+          // 0..6 of U are the low digits + 128, byte 7 the top digit.
+          const unsigned long long b7 = 0x0080808080808080ull;
+          const unsigned long long U0 = (unsigned long long)__float2ll_rn(__fmul_rn(__fmul_rn(v.x, f1), f2)) + b7;
+          const unsigned long long U1 = (unsigned long long)__float2ll_rn(__fmul_rn(__fmul_rn(v.y, f1), f2)) + b7;
+          const unsigned long long U2 = (unsigned long long)__float2ll_rn(__fmul_rn(__fmul_rn(v.z, f1), f2)) + b7;
+          const unsigned long long U3 = (unsigned long long)__float2ll_rn(__fmul_rn(__fmul_rn(v.w, f1), f2)) + b7;
+          uint32_t lo[4], hi[4];
+          gather((uint32_t)U0, (uint32_t)U1, (uint32_t)U2, (uint32_t)U3, lo);
+          gather((uint32_t)(U0 >> 32), (uint32_t)(U1 >> 32), (uint32_t)(U2 >> 32),
+                 (uint32_t)(U3 >> 32), hi);
+#pragma unroll
+          for (int d = 0; d < 4; ++d) {
+            lo[d] ^= 0x80808080u;
+            if (d < 3) hi[d] ^= 0x80808080u;
+            cs[d] = __dp4a((int)lo[d], 0x01010101, cs[d]);
+            cs[d + 4] = __dp4a((int)hi[d], 0x01010101, cs[d + 4]);
+            frag[base + 16 * d] = lo[d];
+            frag[base + 16 * (d + 4)] = hi[d];
+          }
         }
       };
 #pragma unroll
@@ -492,7 +649,7 @@ __global__ void __launch_bounds__(kThreads, GvCfg<NB>::CTAS)
         if (q < nquad) split(xr[j], q);
       }
       for (int q = tid + kRQ * kThreads; q < nquad; q += kThreads)
-        split(load_x4(S.x, P.xkind, t, 4 * (int64_t)q, S.K), q);
+        split(load_xs4(S, P.xkind, t, 4 * (int64_t)q), q);
     } else {
       const int8_t* xq = static_cast<const int8_t*>(S.x) + (int64_t)t * S.K;
       for (int q = tid; q < nquad; q += kThreads) {
@@ -509,17 +666,18 @@ __global__ void __launch_bounds__(kThreads, GvCfg<NB>::CTAS)
         frag[frag_word<SP>(q, t, NB)] = wv;
       }
     }
-    // column sums: warp reduction, one shared atomic per warp and column
+    // column sums: one warp-wide integer add per column, one shared atomic
+    // per warp and column
 #pragma unroll
-    for (int d = 0; d < 4; ++d) {
-      if (d >= D) break;
-      int v = cs[d];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      if (lane == 0) atomicAdd(&colsum[t * D + d], v);
+    for (int d = 0; d < 8; ++d) {
+      if (d < D) {
+        const int v = __reduce_add_sync(0xffffffffu, cs[d]);
+        if (lane == 0) atomicAdd(&colsum[t * D + d], v);
+      }
     }
   }
   __syncthreads();
+  const GvNf nfv{nf_cnt, nf_pos, S.x, S.K, P.xkind == 1, SP ? 1 : 0, S.kscale, S.kblock};
 
   // ---- the weight stream against the fragments, one row-block segment at a time
   int acc[MB][NB][4][4];
@@ -613,7 +771,7 @@ __global__ void __launch_bounds__(kThreads, GvCfg<NB>::CTAS)
       if (issued < n) {
         if (lane == 0) {
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-          prod_copy<MB, SP>(pr, ring_s + slot * U::BYTES, bar_s + 8 * slot);
+          prod_copy<MB, SP>(pr, ring_s + slot * U::BYTES, bar_s + 8 * slot, l2_policy);
         }
         prod_next<MB, SP>(pr, P);
         ++issued;
@@ -648,7 +806,7 @@ __global__ void __launch_bounds__(kThreads, GvCfg<NB>::CTAS)
             part[(((warp * NB + nb) * MB + m) * 4 + e) * 32 + lane] = fin[m][nb][e];
       if (lane == 0) part_id[warp] = P.p[cp].unit_begin + crb * nc;
     } else if (ends) {
-      rowblock_store<NB, MB>(fin, P.p[cp], crb, seq, D, colsum, tok_scale, g, r);
+      rowblock_store<NB, MB>(fin, P.p[cp], crb, seq, D, colsum, tok_scale, nfv, g, r);
     } else {
       keep = true;  // finished after the stream, with the later warps' parts
       break;
@@ -702,7 +860,7 @@ __global__ void __launch_bounds__(kThreads, GvCfg<NB>::CTAS)
 #pragma unroll
         for (int e = 0; e < 4; ++e) fin[m][nb][e] += part[(((w * NB + nb) * MB + m) * 4 + e) * 32 + lane];
   }
-  rowblock_store<NB, MB>(fin, q, crb, seq, D, colsum, tok_scale, g, r);
+  rowblock_store<NB, MB>(fin, q, crb, seq, D, colsum, tok_scale, nfv, g, r);
 }
 
 template <int NB, bool SP, bool SMALL>
@@ -721,11 +879,11 @@ size_t smem_for(int nb, bool sp, bool small, int64_t max_chunks) {
   return nb == 1 ? smem_for<1, false, false>(max_chunks) : smem_for<2, false, false>(max_chunks);
 }
 
-template <int NB, int NP, bool SP>
+template <int NB, int NP, bool SP, int DT>
 int launch_nb(const GvParamsT<NP>& P, int64_t ctas, size_t smem, cudaStream_t s) {
   static int attr_smem = 0;  // per template instance
   if ((int)smem > attr_smem) {
-    FT_CUDA(cudaFuncSetAttribute(gemv_kernel<NB, NP, SP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    FT_CUDA(cudaFuncSetAttribute(gemv_kernel<NB, NP, SP, DT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)smem));
     attr_smem = (int)smem;
   }
@@ -739,7 +897,7 @@ int launch_nb(const GvParamsT<NP>& P, int64_t ctas, size_t smem, cudaStream_t s)
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  FT_CUDA(cudaLaunchKernelEx(&cfg, gemv_kernel<NB, NP, SP>, P));
+  FT_CUDA(cudaLaunchKernelEx(&cfg, gemv_kernel<NB, NP, SP, DT>, P));
   FT_LAUNCH_CHECK();
   return FT_OK;
 }
@@ -755,16 +913,23 @@ int launch_sized(const GvParams& P, int64_t ctas, size_t smem, cudaStream_t s) {
     Q.err = P.err;
     for (int i = 0; i < P.nseg; ++i) Q.g[i] = P.g[i];
     for (int i = 0; i < P.nprob; ++i) Q.p[i] = P.p[i];
-    return launch_nb<NB, kSmallProb, SP>(Q, ctas, smem, s);
+    return P.D == 1 ? launch_nb<NB, kSmallProb, SP, 1>(Q, ctas, smem, s)
+         : P.D == 4 ? launch_nb<NB, kSmallProb, SP, 4>(Q, ctas, smem, s)
+                    : launch_nb<NB, kSmallProb, SP, 8>(Q, ctas, smem, s);
   }
-  return launch_nb<NB, kMaxProb, SP>(P, ctas, smem, s);
+  return P.D == 1 ? launch_nb<NB, kMaxProb, SP, 1>(P, ctas, smem, s)
+       : P.D == 4 ? launch_nb<NB, kMaxProb, SP, 4>(P, ctas, smem, s)
+                  : launch_nb<NB, kMaxProb, SP, 8>(P, ctas, smem, s);
 }
 
 }  // namespace
 
-bool gemv_fits(const ft_weight* w, int64_t seq, int xkind) {
-  const int digits = xkind == 2 ? 1 : 4;
-  const int64_t ncols = seq * digits;
+int gemv_digits(int xkind, int digits) {
+  return xkind == 2 ? 1 : (digits > 4 ? 8 : 4);
+}
+
+bool gemv_fits(const ft_weight* w, int64_t seq, int xkind, int digits) {
+  const int64_t ncols = seq * gemv_digits(xkind, digits);
   // int32 bound: the k-step-3 accumulator grows by <= 128 * 128 * 32 per chunk
   if ((w->format != 0 && w->format != 1) || ncols > 16 || w->n_chunks > 2048) return false;
   const int nb = ncols > 8 ? 2 : 1;
@@ -773,12 +938,12 @@ bool gemv_fits(const ft_weight* w, int64_t seq, int xkind) {
 }
 
 int launch_gemv(ft_ctx* ctx, int nprob, const GvLaunchProblem* probs, int xkind, bool sparse,
-                cudaStream_t s) {
+                int digits, cudaStream_t s) {
   FT_CHECK(nprob > 0 && nprob <= kMaxProb, FT_ERR_UNSUPPORTED, "bad GEMV group size");
   static thread_local GvParams P;
   P.xkind = xkind;
   P.err = ctx->err_word;
-  P.D = xkind == 2 ? 1 : 4;
+  P.D = gemv_digits(xkind, digits);
   // segments: problems grouped by activation (pointer, K, seq), first-seen order
   int seg_of[kMaxProb];
   int nseg = 0;
@@ -786,10 +951,14 @@ int launch_gemv(ft_ctx* ctx, int nprob, const GvLaunchProblem* probs, int xkind,
   for (int i = 0; i < nprob; ++i) {
     const GvLaunchProblem& q = probs[i];
     int j = 0;
-    while (j < nseg && !(P.g[j].x == q.x && P.g[j].K == q.K && P.g[j].seq == q.seq)) ++j;
+    while (j < nseg && !(P.g[j].x == q.x && P.g[j].K == q.K && P.g[j].seq == q.seq &&
+                         P.g[j].kscale == q.kscale && P.g[j].kblock == q.kblock))
+      ++j;
     if (j == nseg) {
       P.g[j].x = q.x;
       P.g[j].K = q.K;
+      P.g[j].kscale = q.kscale;
+      P.g[j].kblock = q.kblock;
       P.g[j].seq = (int32_t)q.seq;
       P.g[j].n_chunks = (int32_t)ceil_div(q.K, kChunkK);
       ++nseg;
@@ -837,7 +1006,13 @@ int launch_gemv(ft_ctx* ctx, int nprob, const GvLaunchProblem* probs, int xkind,
   FT_CHECK(total < (int64_t)1 << 31, FT_ERR_UNSUPPORTED, "GEMV group too large");
   // CTAs per segment in proportion to its units, at least one, at most one
   // per row-block
-  const int64_t target = (int64_t)ctx->num_sms * (nb == 1 ? GvCfg<1>::CTAS : GvCfg<2>::CTAS);
+  // CTAs per SM the grid targets: launches of <= kSmallProb problems and
+  // larger ones separately (fewer than the SM can hold leaves room for the
+  // next launch's CTAs to start streaming while this one finishes).
+  const int per_sm = small ? FT_GV_GRID_SMALL : FT_GV_GRID_LARGE;
+  const int64_t target = (int64_t)ctx->num_sms *
+                         (per_sm < (nb == 1 ? GvCfg<1>::CTAS : GvCfg<2>::CTAS)
+                              ? per_sm : (nb == 1 ? GvCfg<1>::CTAS : GvCfg<2>::CTAS));
   int64_t ctas = 0;
   for (int j = 0; j < nseg; ++j) {
     GvSeg& g = P.g[j];

@@ -72,6 +72,120 @@ int fail(int status, const char* fmt, ...);
 inline int64_t round_up(int64_t a, int64_t b) { return (a + b - 1) / b * b; }
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+// Fixed-point digits of an fp32/bf16 activation token: the kernels multiply
+// the token by the power of two 2^sh that puts its largest finite |x| in
+// [2^(8D-3), 2^(8D-2)) and split X = round(x * 2^sh) into D signed base-256
+// digits (the top one within +-64).  D = 8 (the public fp32/bf16 entry points)
+// represents every element within 2^38 of the token's absmax exactly, so the
+// exact int32 digit sums give the correctly rounded dot product; D = 4 (the
+// MoE expert GEMMs, tolerance 1e-4 of the output rms) rounds elements below
+// absmax * 2^-6 to a quantum of absmax * 2^-30.
+constexpr int kDigitsExact = 8;
+constexpr int kDigitsMoE = 4;
+// Non-finite activation positions remembered per token; a token with more is
+// handled by scanning its whole row.
+constexpr int kNfCap = 16;
+
+#ifdef __CUDACC__
+// sh such that 2^sh * a lies in [2^(8D-3), 2^(8D-2)) for a finite a > 0.
+__device__ __forceinline__ int digit_shift(float a, int D) {
+  const uint32_t ebits = __float_as_uint(a) >> 23;
+  if (ebits != 0u) return (8 * D - 2) + 126 - (int)ebits;
+  int ex = 0;
+  frexpf(a, &ex);  // subnormal absmax
+  return (8 * D - 2) - ex;
+}
+
+// Weight w in {-1, 0, +1} at (row R, column k) of a resident weight, read from
+// its tiled layout (ft_internal.cuh header comment; 2:4 blocks: row records of
+// 32 five-bit group codes, group g of the chunk at bit 5g).  A slow scalar
+// lookup for the non-finite activation path.
+__device__ __forceinline__ int weight_at(const uint8_t* codes, int format, int64_t n_chunks,
+                                         int64_t R, int64_t k) {
+  const int64_t t = R >> 7, c = k >> 7;
+  const int r = (int)(R & 127), kk = (int)(k & 127);
+  if (format == 0) {
+    const uint8_t* blk = codes + (t * n_chunks + c) * kBlockBytes;
+    const int mb = r >> 4, g = r & 7, ih = (r >> 3) & 1;
+    const int j = kk >> 5, il = (kk >> 4) & 1, rr = (kk >> 2) & 3, b = kk & 3;
+    const int byte = blk[(mb * 32 + 4 * g + rr) * 16 + (2 * il + ih) * 4 + b];
+    return ((byte >> (2 * j)) & 3) - 1;
+  }
+  const uint8_t* rec = codes + (t * n_chunks + c) * kSparseBlockBytes + r * 20;
+  const int bit = 5 * (kk >> 2), e = kk & 3;
+  uint32_t v = rec[bit >> 3];
+  if ((bit & 7) > 3) v |= (uint32_t)rec[(bit >> 3) + 1] << 8;
+  v = (v >> (bit & 7)) & 31u;
+  if (v >= 24u) return 0;
+  const int p = (int)(v >> 2);
+  const int p0 = p < 3 ? 0 : (p < 5 ? 1 : 2);
+  const int p1 = p == 0 ? 1 : ((p == 1 || p == 3) ? 2 : 3);
+  if (e == p0) return (v & 1u) ? -1 : 1;
+  if (e == p1) return (v & 2u) ? -1 : 1;
+  return 0;
+}
+
+// round(xs) as a 64-bit integer, |xs| < 2^63: integer-valued floats
+// (|xs| >= 2^23) are read straight from their bits, smaller ones go through
+// the 32-bit conversion.
+__device__ __forceinline__ long long float_to_ll_exact(float xs) {
+  const uint32_t b = __float_as_uint(xs);
+  const int e = (int)((b >> 23) & 255u);
+  if (e < 150) return (long long)__float2int_rn(xs);
+  const unsigned long long m = (unsigned long long)((b & 0x7fffffu) | 0x800000u) << (e - 150);
+  return (b >> 31) ? -(long long)m : (long long)m;
+}
+
+__device__ __forceinline__ bool is_nonfinite(float v) {
+  return (__float_as_uint(v) & 0x7f800000u) == 0x7f800000u;
+}
+
+// Output of row R for a token x_row [K] (fp32, or bf16 bit patterns when
+// bf16) that holds non-finite elements.  The reference's per-row-scale
+// matmuls (TernaryMatMulOp, src/compute/kernels/ternary_matmul.rs:54-70, and
+// gpu_ternary_mm_cpu, src/model/cpu_block_attn_res.rs:2373-2398) add x[k] only
+// where the weight is nonzero, in fp32: a row meeting a NaN, or infinities of
+// both signs, ends NaN; one sign of infinity gives +-inf; then sum * scale.
+// `pos` lists the token's non-finite positions (cnt of them; more than kNfCap:
+// the whole row is scanned).  y_finite is returned when the row meets none.
+//
+// Column-block scales (ternary_matmul_blocked, src/model/ternary.rs:541-579:
+// kscale != null, one scale per kblock columns): the kernels fold the scale
+// into the activation, x' = kscale[k / kblock] * x, and that reference
+// multiplies w * x in fp32, so a zero weight meeting an infinity gives NaN
+// too (0 * inf).
+// Kept out of line: it runs only for tokens with non-finite elements, and
+// inlining its loops into the kernels' epilogues slows their common path.
+static __device__ __noinline__ float nonfinite_row(float y_finite, const uint8_t* codes, int format,
+                                               int64_t n_chunks, int64_t R, const void* x_row,
+                                               bool bf16, int64_t K, const int* pos, int cnt,
+                                               float scale, const float* kscale,
+                                               int64_t kblock) {
+  bool nan = false, pinf = false, ninf = false;
+  const bool all = cnt > kNfCap;
+  const int64_t n = all ? K : cnt;
+  for (int64_t i = 0; i < n; ++i) {
+    const int64_t k = all ? i : pos[i];
+    float v = bf16 ? __uint_as_float((uint32_t) static_cast<const uint16_t*>(x_row)[k] << 16)
+                   : static_cast<const float*>(x_row)[k];
+    if (kscale) v = __fmul_rn(v, kscale[k / kblock]);
+    if (!is_nonfinite(v)) continue;
+    const int w = weight_at(codes, format, n_chunks, R, k);
+    if (w == 0) {
+      if (kscale) nan = true;  // 0 * inf or 0 * NaN
+      continue;
+    }
+    if (v != v) nan = true;
+    else if ((v > 0.0f) == (w > 0)) pinf = true;
+    else ninf = true;
+  }
+  if (nan || (pinf && ninf)) return __int_as_float(0x7fc00000);
+  if (pinf) return __fmul_rn(__int_as_float(0x7f800000), scale);
+  if (ninf) return __fmul_rn(__int_as_float(0xff800000), scale);
+  return y_finite;
+}
+#endif
+
 // Per-context device workspace (grown on demand, freed with the context).
 struct Workspace {
   void* ptr = nullptr;
@@ -124,15 +238,33 @@ int launch_repack_sparse_wgsl(const uint32_t* words, int64_t rows, int64_t cols,
                               cudaStream_t s);
 int launch_quantize_i8(const void* x, bool bf16, int64_t seq, int64_t cols, int8_t* q, float* sx,
                        cudaStream_t s);
+// Quantizes a row-major [w->rows, w->cols] fp32/bf16 device matrix into w's
+// codes with alpha = w->row_scales[row] (mode 0 absmean rule, 1 STE rule).
+int launch_quantize_pack(const void* src, bool bf16, int mode, ft_weight* w, cudaStream_t s);
+int launch_fill_scales(ft_weight* w, float alpha, cudaStream_t s);
+// w's codes as the reference pack_ternary byte stream ((rows*cols+3)/4 bytes).
+int launch_export_u8(const ft_weight* w, uint8_t* out, cudaStream_t s);
+// *acc += sum |src[i]| in f64 (acc: device double).
+int launch_abs_sum(const void* src, bool bf16, int64_t n, double* acc, cudaStream_t s);
+// Absmean scale of quantize_ternary (src/model/ternary.rs:36-45): sequential
+// fp32 sum of |w| in element order, (sum / n) / ABSMEAN_NORM, 1 when the sum
+// is not positive.  Host code.
+float host_absmean_alpha(const float* w, int64_t n);
+int alloc_weight(ft_ctx* ctx, int64_t rows, int64_t cols, ft_weight** out, int format = 0);
 // Tensor-core path (ft_tc.cu).  xkind: 0 f32, 1 bf16, 2 int8 codes (then sx
 // is the per-token scale).
 int launch_tc_matmul(ft_ctx* ctx, const ft_weight* w, int64_t seq, const void* x, int xkind,
                      const float* sx, float* y, cudaStream_t s);
 // Group of up to 64 independent problems (same seq and activation kind) in
 // one persistent launch; identical activation pointers share one operand.
+// digits: fixed-point digits per fp32/bf16 token (kDigitsExact or kDigitsMoE;
+// 0 = kDigitsExact); ignored for int8 codes.
+// kscale/kblock (fp32/bf16 only): one scale per kblock columns, folded into
+// the activations (the blocked matmul); applies to every problem of the group.
 int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t seq,
                       const void* const* xs, int xkind, const float* const* sxs, float* const* ys,
-                      const int64_t* ldys, cudaStream_t s, const int64_t* seqs = nullptr);
+                      const int64_t* ldys, cudaStream_t s, const int64_t* seqs = nullptr,
+                      int digits = 0, const float* kscale = nullptr, int64_t kblock = 1);
 // Decode-shape kernel (ft_gemv.cu): dense problems whose activations fit 16
 // operand columns; the kernel builds its activation operand itself.
 constexpr int kGemvMaxSmem = 200 * 1024;
@@ -145,11 +277,16 @@ struct GvLaunchProblem {
   const float* sx;  // int8 mode: per-token scale
   float* y;
   int64_t ldy;
+  const float* kscale = nullptr;  // fp32 mode: column-block scales (blocked matmul), or null
+  int64_t kblock = 1;             // columns per block scale
 };
-bool gemv_fits(const ft_weight* w, int64_t seq, int xkind);
+// Digits per fp32/bf16 token on the decode kernel for a requested count
+// (8 when more than 4 are asked for, else 4); 1 for int8 codes.
+int gemv_digits(int xkind, int digits);
+bool gemv_fits(const ft_weight* w, int64_t seq, int xkind, int digits);
 // All problems of one launch have the same weight format (sparse: 2:4).
 int launch_gemv(ft_ctx* ctx, int nprob, const GvLaunchProblem* probs, int xkind, bool sparse,
-                cudaStream_t s);
+                int digits, cudaStream_t s);
 int launch_wgsl_op(const uint32_t* words, const float* scales, const float* x, float* y,
                    uint32_t seq, uint32_t in_cols, uint32_t out_rows, cudaStream_t s);
 }  // namespace ft

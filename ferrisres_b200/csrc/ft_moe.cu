@@ -12,22 +12,13 @@
 //             reference's accumulation order.
 // The stages are exported separately so an expert-parallel host can put its
 // all-to-all exchanges between them.
+#include <cmath>
 #include <cstring>
 #include <vector>
 
 #include "ft_internal.cuh"
 
-struct ft_moe {
-  int device = 0;
-  int64_t E = 0, H = 0, F = 0;
-  int top_k = 2;
-  int use_gelu = 0;
-  float* router = nullptr;  // [E, H] fp32 (row e = expert e)
-  std::vector<ft_weight*> gate_up;  // [2F, H] each: gate rows then up rows
-  std::vector<ft_weight*> down;     // [H, F] each
-  ft::Workspace buf;                // forward intermediates (grown on demand)
-  std::vector<int32_t> counts_host;
-};
+#include "ft_moe.cuh"
 
 namespace ft {
 namespace {
@@ -44,6 +35,12 @@ __device__ __forceinline__ float load_act(const void* x, int bf16, int64_t i) {
   return bf16 ? __uint_as_float((uint32_t) static_cast<const uint16_t*>(x)[i] << 16)
               : static_cast<const float*>(x)[i];
 }
+
+__device__ __forceinline__ void route_token(float* s, int E, int K, int64_t t,
+                                            int32_t* __restrict__ topk_idx,
+                                            float* __restrict__ topk_w,
+                                            float* __restrict__ probs_out,
+                                            int32_t* __restrict__ counts);
 
 // One block = 16 tokens x all experts (E <= 64); thread t owns token t/16 and
 // experts t%16 + 16m.  Then one thread per token does softmax and top-k in the
@@ -110,7 +107,17 @@ __global__ void __launch_bounds__(kRouterThreads) moe_router_kernel(
   __syncthreads();
   const int64_t t = t0 + tt;
   if (el != 0 || t >= T) return;
-  float* s = sc[tt];
+  route_token(sc[tt], E, K, t, topk_idx, topk_w, probs_out, counts);
+}
+
+// Softmax over the E scores of one token, then stable descending top-k with
+// gates renormalised by their sum (TernaryMoELayer::forward,
+// src/model/ternary_moe.rs:163-215), sequential in the reference's order.
+__device__ __forceinline__ void route_token(float* s, int E, int K, int64_t t,
+                                            int32_t* __restrict__ topk_idx,
+                                            float* __restrict__ topk_w,
+                                            float* __restrict__ probs_out,
+                                            int32_t* __restrict__ counts) {
   float mx = -INFINITY;
   for (int e = 0; e < E; ++e) mx = fmaxf(mx, s[e]);
   float se = 0.0f;
@@ -121,7 +128,6 @@ __global__ void __launch_bounds__(kRouterThreads) moe_router_kernel(
   for (int e = 0; e < E; ++e) s[e] = s[e] / se;
   if (probs_out)
     for (int e = 0; e < E; ++e) probs_out[t * E + e] = s[e];
-  // stable descending top-k: the largest remaining, lowest index first on ties
   uint64_t taken = 0;
   int idx[8];
   float wsum = 0.0f;
@@ -138,6 +144,132 @@ __global__ void __launch_bounds__(kRouterThreads) moe_router_kernel(
     topk_w[t * K + k] = wsum > 0.0f ? s[idx[k]] / wsum : s[idx[k]];
     atomicAdd(&counts[idx[k]], 1);
   }
+}
+
+// Router scores on the tensor cores.  x (fp32 or bf16) and the router (fp32)
+// are sums of bf16 planes -- x = x0 + x1 + x2 exactly for fp32 (each plane the
+// bf16 rounding of what the planes before it leave), one plane for bf16 x; the
+// router planes are prepared at creation (one when the router is bf16-exact,
+// as in BASELINE's bf16 router).  Products of bf16 planes are exact in fp32;
+// mma.sync m16n8k16 accumulates them in fp32 over the plane pairs (i, j) with
+// i + j <= 2 (the dropped pairs weigh below 2^-24 of the product), each 64-K
+// chunk in its own fp32 MMA chain, the chunks summed in f64: the scores come
+// out closer to the exact dot than the reference's sequential fp32 sum is.  Block:
+// 32 tokens x 64 experts, 4 warps (16 tokens x 32 experts each), K in chunks
+// of 64 staged in shared memory (rows padded to 72 bf16: conflict-free
+// fragment loads).  Then one thread per token routes it.
+constexpr int kRtTok = 32, kRtK = 64, kRtPad = 72, kRtThreads = 128;
+
+__device__ __forceinline__ uint32_t bf16_rn_bits(float v) {
+  uint32_t u = __float_as_uint(v);
+  if ((u & 0x7f800000u) == 0x7f800000u) return u >> 16;  // inf / NaN: keep
+  u += 0x7fffu + ((u >> 16) & 1u);
+  return u >> 16;
+}
+
+__device__ __forceinline__ void mma_bf16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+      "{%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__global__ void __launch_bounds__(kRtThreads) moe_router_mma_kernel(
+    const void* __restrict__ x, int bf16, int64_t T, int64_t H, int64_t Hpad, int E, int K,
+    const uint16_t* __restrict__ Rp, int n_rplanes, int32_t* __restrict__ topk_idx,
+    float* __restrict__ topk_w, float* __restrict__ probs_out, int32_t* __restrict__ counts) {
+  // x planes; after the K loop the same bytes hold the scores
+  __shared__ __align__(16) unsigned char xbuf[3 * kRtTok * kRtPad * 2];
+  __shared__ __align__(16) uint16_t rs[3][kMaxExperts][kRtPad];
+  static_assert(sizeof(float) * kRtTok * (kMaxExperts + 1) <= sizeof(xbuf), "scores alias x");
+  auto xs = reinterpret_cast<uint16_t(*)[kRtTok][kRtPad]>(xbuf);
+  auto sc = reinterpret_cast<float(*)[kMaxExperts + 1]>(xbuf);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, tq = lane & 3;
+  const int th = warp & 1, eh = warp >> 1;  // token half, expert half
+  const int64_t t0 = (int64_t)blockIdx.x * kRtTok;
+  const int nxp = bf16 ? 1 : 3;
+  // Tensor-core fp32 accumulation truncates; each 64-K chunk accumulates in a
+  // fresh fp32 chain and the chunk results are summed in f64.
+  double acc[4][4];
+#pragma unroll
+  for (int n = 0; n < 4; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0;
+  for (int64_t k0 = 0; k0 < Hpad; k0 += kRtK) {
+    float part[4][4];
+#pragma unroll
+    for (int n = 0; n < 4; ++n) part[n][0] = part[n][1] = part[n][2] = part[n][3] = 0.0f;
+    __syncthreads();  // the previous chunk is no longer read
+    // x chunk: 32 tokens x 64 k, 16 elements per thread, split into planes
+    for (int i = tid; i < kRtTok * kRtK / 2; i += kRtThreads) {
+      const int a = i / (kRtK / 2), kk = 2 * (i % (kRtK / 2));
+      const int64_t t = t0 + a, k = k0 + kk;
+      float v[2] = {0.0f, 0.0f};
+#pragma unroll
+      for (int e = 0; e < 2; ++e)
+        if (t < T && k + e < H) v[e] = load_act(x, bf16, t * H + k + e);
+      uint32_t pl[3][2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        float r = v[e];
+#pragma unroll
+        for (int q = 0; q < 3; ++q) {
+          pl[q][e] = bf16_rn_bits(r);
+          r = __fsub_rn(r, __uint_as_float(pl[q][e] << 16));
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 3; ++q)
+        if (q < nxp) *reinterpret_cast<uint32_t*>(&xs[q][a][kk]) = pl[q][0] | (pl[q][1] << 16);
+    }
+    // router planes: 64 experts x 64 k each, 16-byte loads (zero rows past E)
+    for (int i = tid; i < n_rplanes * kMaxExperts * (kRtK / 8); i += kRtThreads) {
+      const int q = i / (kMaxExperts * (kRtK / 8));
+      const int rem = i % (kMaxExperts * (kRtK / 8));
+      const int e = rem / (kRtK / 8), kk = 8 * (rem % (kRtK / 8));
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (e < E)
+        v = __ldg(reinterpret_cast<const uint4*>(Rp + ((int64_t)q * kMaxExperts + e) * Hpad + k0 + kk));
+      *reinterpret_cast<uint4*>(&rs[q][e][kk]) = v;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int ks = 0; ks < kRtK; ks += 16) {
+      for (int i = 0; i < nxp; ++i) {
+        const uint16_t* ar = &xs[i][16 * th][0];
+        const uint32_t a0 = *reinterpret_cast<const uint32_t*>(ar + g * kRtPad + ks + 2 * tq);
+        const uint32_t a1 = *reinterpret_cast<const uint32_t*>(ar + (g + 8) * kRtPad + ks + 2 * tq);
+        const uint32_t a2 = *reinterpret_cast<const uint32_t*>(ar + g * kRtPad + ks + 8 + 2 * tq);
+        const uint32_t a3 = *reinterpret_cast<const uint32_t*>(ar + (g + 8) * kRtPad + ks + 8 + 2 * tq);
+        for (int j = 0; j < n_rplanes && i + j <= 2; ++j) {
+#pragma unroll
+          for (int n = 0; n < 4; ++n) {
+            const uint16_t* br = &rs[j][32 * eh + 8 * n + g][0];
+            const uint32_t b0 = *reinterpret_cast<const uint32_t*>(br + ks + 2 * tq);
+            const uint32_t b1 = *reinterpret_cast<const uint32_t*>(br + ks + 8 + 2 * tq);
+            mma_bf16(part[n], a0, a1, a2, a3, b0, b1);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int n = 0; n < 4; ++n)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[n][i] += (double)part[n][i];
+  }
+  __syncthreads();  // every warp is done reading x before the scores overwrite it
+#pragma unroll
+  for (int n = 0; n < 4; ++n) {
+    const int e0 = 32 * eh + 8 * n + 2 * tq;
+    sc[16 * th + g][e0] = (float)acc[n][0];
+    sc[16 * th + g][e0 + 1] = (float)acc[n][1];
+    sc[16 * th + g + 8][e0] = (float)acc[n][2];
+    sc[16 * th + g + 8][e0 + 1] = (float)acc[n][3];
+  }
+  __syncthreads();
+  const int64_t t = t0 + tid;
+  if (tid < kRtTok && t < T) route_token(sc[tid], E, K, t, topk_idx, topk_w, probs_out, counts);
 }
 
 __global__ void moe_offsets_kernel(const int32_t* __restrict__ counts, int E,
@@ -279,8 +411,14 @@ int moe_route(ft_ctx* ctx, ft_moe* m, int64_t T, const void* x, int bf16, int32_
               float* topk_w, float* probs, int32_t* counts, cudaStream_t s) {
   FT_CUDA(cudaMemsetAsync(counts, 0, m->E * sizeof(int32_t), s));
   if (T == 0) return FT_OK;
-  moe_router_kernel<<<(unsigned)ceil_div(T, kRouterTok), kRouterThreads, 0, s>>>(
-      x, bf16, T, m->H, (int)m->E, m->top_k, m->router, topk_idx, topk_w, probs, counts);
+  if (m->router_planes) {
+    moe_router_mma_kernel<<<(unsigned)ceil_div(T, kRtTok), kRtThreads, 0, s>>>(
+        x, bf16, T, m->H, m->Hpad, (int)m->E, m->top_k, m->router_planes, m->n_rplanes, topk_idx,
+        topk_w, probs, counts);
+  } else {
+    moe_router_kernel<<<(unsigned)ceil_div(T, kRouterTok), kRouterThreads, 0, s>>>(
+        x, bf16, T, m->H, (int)m->E, m->top_k, m->router, topk_idx, topk_w, probs, counts);
+  }
   FT_LAUNCH_CHECK();
   return FT_OK;
 }
@@ -311,14 +449,75 @@ int moe_expert_segments(ft_ctx* ctx, ft_moe* m, int nseg, const int32_t* seg_exp
     total += seg_rows[i];
   }
   if (total == 0) return FT_OK;
+  // Expert GEMMs take kDigitsMoE fixed-point digits per token: the layer's
+  // tolerance is 1e-4 of each output row's rms (ft_internal.cuh).
   int st = launch_tc_grouped(ctx, nseg, wgu.data(), 0, xs.data(), bf16 ? 1 : 0, nullptr, gus.data(),
-                             nullptr, s, seg_rows);
+                             nullptr, s, seg_rows, kDigitsMoE);
   if (st != FT_OK) return st;
   moe_act_kernel<<<(unsigned)ceil_div(total * m->F, 256), 256, 0, s>>>(gu, total, m->F, m->use_gelu,
                                                                        h);
   FT_LAUNCH_CHECK();
   return launch_tc_grouped(ctx, nseg, wd.data(), 0, hs.data(), 0, nullptr, ys.data(), nullptr, s,
-                           seg_rows);
+                           seg_rows, kDigitsMoE);
+}
+
+// Router planes for moe_router_mma_kernel: router = p0 + p1 + p2 with each
+// plane the bf16 rounding (to nearest even) of what the planes before it
+// leave, which is exact for finite fp32 values; as few planes as the router
+// needs (one for a bf16-exact router).  A router with non-finite values keeps
+// the sequential kernel.
+static uint16_t host_bf16_rn(float v, float* rest) {
+  uint32_t u;
+  memcpy(&u, &v, 4);
+  u += 0x7fffu + ((u >> 16) & 1u);
+  const uint16_t h = (uint16_t)(u >> 16);
+  const uint32_t hb = (uint32_t)h << 16;
+  float hv;
+  memcpy(&hv, &hb, 4);
+  *rest = v - hv;
+  return h;
+}
+
+// Device tables of the experts' codes and row scales for the fused decode
+// kernel: [gate_up codes][gate_up scales][down codes][down scales], E each.
+int build_decode_tables(ft_moe* m) {
+  std::vector<const void*> tab(4 * m->E, nullptr);
+  for (int64_t e = 0; e < m->E; ++e) {
+    if (m->gate_up[e]) {
+      tab[e] = m->gate_up[e]->codes;
+      tab[m->E + e] = m->gate_up[e]->row_scales;
+    }
+    if (m->down[e]) {
+      tab[2 * m->E + e] = m->down[e]->codes;
+      tab[3 * m->E + e] = m->down[e]->row_scales;
+    }
+  }
+  FT_CUDA(cudaMalloc(&m->dtab, tab.size() * sizeof(void*)));
+  FT_CUDA(cudaMemcpy(m->dtab, tab.data(), tab.size() * sizeof(void*), cudaMemcpyHostToDevice));
+  return FT_OK;
+}
+
+int prepare_router_planes(ft_moe* m, const float* router_host) {
+  const int64_t E = m->E, H = m->H;
+  const int64_t Hpad = ceil_div(H, kRtK) * kRtK;
+  std::vector<uint16_t> planes((size_t)3 * kMaxExperts * Hpad, 0);
+  int need = 1;
+  for (int64_t e = 0; e < E; ++e)
+    for (int64_t k = 0; k < H; ++k) {
+      float r = router_host[e * H + k];
+      if (!std::isfinite(r)) return FT_OK;  // sequential router
+      for (int q = 0; q < 3; ++q) {
+        const uint16_t h = host_bf16_rn(r, &r);
+        planes[((size_t)q * kMaxExperts + e) * Hpad + k] = h;
+        if (h != 0 && q + 1 > need) need = q + 1;
+      }
+    }
+  const size_t bytes = (size_t)need * kMaxExperts * Hpad * 2;
+  FT_CUDA(cudaMalloc(&m->router_planes, bytes));
+  FT_CUDA(cudaMemcpy(m->router_planes, planes.data(), bytes, cudaMemcpyHostToDevice));
+  m->n_rplanes = need;
+  m->Hpad = Hpad;
+  return FT_OK;
 }
 
 }  // namespace ft
@@ -357,6 +556,7 @@ int ft_moe_create(ft_ctx* ctx, int64_t n_experts, int64_t hidden, int64_t inter,
   if (e == cudaSuccess)
     e = cudaMemcpy(m->router, router_host, (size_t)n_experts * hidden * 4, cudaMemcpyHostToDevice);
   if (e != cudaSuccess) st = fail(FT_ERR_GPU, "router upload failed: %s", cudaGetErrorString(e));
+  if (st == FT_OK) st = prepare_router_planes(m, router_host);
   const size_t mat_bytes = (size_t)(inter * hidden) / 4;
   std::vector<uint8_t> gu_bytes(2 * mat_bytes);
   std::vector<float> gu_scales(2 * inter);
@@ -382,11 +582,112 @@ int ft_moe_create(ft_ctx* ctx, int64_t n_experts, int64_t hidden, int64_t inter,
     if (st != FT_OK) break;
     m->down.push_back(w);
   }
+  if (st == FT_OK) st = build_decode_tables(m);
   if (prev >= 0 && prev != ctx->device) cudaSetDevice(prev);
   if (st != FT_OK) {
     for (auto* w : m->gate_up) ft_weight_destroy(w);
     for (auto* w : m->down) ft_weight_destroy(w);
     if (m->router) cudaFree(m->router);
+    if (m->router_planes) cudaFree(m->router_planes);
+    if (m->dtab) cudaFree(m->dtab);
+    delete m;
+    return st;
+  }
+  *out = m;
+  return FT_OK;
+}
+
+int ft_moe_create_f32(ft_ctx* ctx, int64_t n_experts, int64_t hidden, int64_t inter, int top_k,
+                      int use_gelu, const float* router_host, const float* const* gate_f32,
+                      const float* const* up_f32, const float* const* down_f32, ft_moe** out) {
+  FT_CHECK(ctx && out && router_host && gate_f32 && up_f32 && down_f32, FT_ERR_SHAPE,
+           "null argument");
+  FT_CHECK(n_experts >= 1 && n_experts <= kMaxExperts, FT_ERR_UNSUPPORTED,
+           "n_experts must be in [1, %d]", kMaxExperts);
+  FT_CHECK(top_k >= 1 && top_k <= 8 && top_k <= n_experts, FT_ERR_UNSUPPORTED,
+           "top_k must be in [1, min(8, n_experts)]");
+  FT_CHECK(hidden > 0 && inter > 0, FT_ERR_SHAPE, "hidden and inter must be positive");
+  int prev = -1;
+  cudaGetDevice(&prev);
+  if (prev != ctx->device) cudaSetDevice(ctx->device);
+  ft_moe* m = new ft_moe();
+  m->device = ctx->device;
+  m->E = n_experts;
+  m->H = hidden;
+  m->F = inter;
+  m->top_k = top_k;
+  m->use_gelu = use_gelu;
+  m->counts_host.assign(n_experts + 1, 0);
+  int st = FT_OK;
+  cudaStream_t s = ctx->host_stream;
+  float* staging = nullptr;
+  cudaError_t e = cudaMalloc(&m->router, (size_t)n_experts * hidden * 4);
+  if (e == cudaSuccess)
+    e = cudaMemcpy(m->router, router_host, (size_t)n_experts * hidden * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMalloc(&staging, (size_t)(2 * inter * hidden) * 4);
+  if (e != cudaSuccess) st = fail(FT_ERR_GPU, "MoE upload failed: %s", cudaGetErrorString(e));
+  if (st == FT_OK) st = prepare_router_planes(m, router_host);
+  const size_t mat = (size_t)(inter * hidden);
+  std::vector<float> gu_scales(2 * inter);
+  for (int64_t x = 0; x < n_experts && st == FT_OK; ++x) {
+    if (!gate_f32[x]) {  // expert held by another rank (expert parallelism)
+      m->gate_up.push_back(nullptr);
+      m->down.push_back(nullptr);
+      continue;
+    }
+    if (!up_f32[x] || !down_f32[x]) {
+      st = fail(FT_ERR_SHAPE, "expert %lld: gate given but up/down missing", (long long)x);
+      break;
+    }
+    // TernaryExpert::from_fp32 (src/model/cpu_moe.rs:33-37) per matrix: the
+    // absmean scale of quantize_ternary, then the rounding rule, here on the
+    // device straight into the tiled layout; gate and up stacked as [2F, H].
+    const float ag = host_absmean_alpha(gate_f32[x], (int64_t)mat);
+    const float au = host_absmean_alpha(up_f32[x], (int64_t)mat);
+    const float ad = host_absmean_alpha(down_f32[x], (int64_t)mat);
+    for (int64_t i = 0; i < inter; ++i) {
+      gu_scales[i] = ag;
+      gu_scales[inter + i] = au;
+    }
+    ft_weight* w = nullptr;
+    st = alloc_weight(ctx, 2 * inter, hidden, &w);
+    if (st != FT_OK) break;
+    m->gate_up.push_back(w);
+    e = cudaMemcpyAsync(staging, gate_f32[x], mat * 4, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(staging + mat, up_f32[x], mat * 4, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(w->row_scales, 0, (size_t)w->n_tiles * kTileRows * 4, s);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(w->row_scales, gu_scales.data(), (size_t)(2 * inter) * 4,
+                          cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) st = launch_quantize_pack(staging, false, 0, w, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess || st != FT_OK) {
+      if (st == FT_OK) st = fail(FT_ERR_GPU, "expert upload failed: %s", cudaGetErrorString(e));
+      m->down.push_back(nullptr);
+      break;
+    }
+    st = alloc_weight(ctx, hidden, inter, &w);
+    if (st != FT_OK) {
+      m->down.push_back(nullptr);
+      break;
+    }
+    m->down.push_back(w);
+    e = cudaMemcpyAsync(staging, down_f32[x], mat * 4, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) st = launch_fill_scales(w, ad, s);
+    if (e == cudaSuccess && st == FT_OK) st = launch_quantize_pack(staging, false, 0, w, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess && st == FT_OK)
+      st = fail(FT_ERR_GPU, "expert upload failed: %s", cudaGetErrorString(e));
+  }
+  if (staging) cudaFree(staging);
+  if (st == FT_OK) st = build_decode_tables(m);
+  if (prev >= 0 && prev != ctx->device) cudaSetDevice(prev);
+  if (st != FT_OK) {
+    for (auto* w : m->gate_up) ft_weight_destroy(w);
+    for (auto* w : m->down) ft_weight_destroy(w);
+    if (m->router) cudaFree(m->router);
+    if (m->router_planes) cudaFree(m->router_planes);
+    if (m->dtab) cudaFree(m->dtab);
     delete m;
     return st;
   }
@@ -403,6 +704,9 @@ int ft_moe_destroy(ft_moe* m) {
   for (auto* w : m->gate_up) ft_weight_destroy(w);
   for (auto* w : m->down) ft_weight_destroy(w);
   if (m->router) cudaFree(m->router);
+  if (m->router_planes) cudaFree(m->router_planes);
+  if (m->dtab) cudaFree(m->dtab);
+  if (m->dbuf.ptr) cudaFree(m->dbuf.ptr);
   if (m->buf.ptr) cudaFree(m->buf.ptr);
   if (prev >= 0 && prev != m->device) cudaSetDevice(prev);
   delete m;

@@ -7,16 +7,19 @@
 // output channels of one tile).  The activations are the signed 8-bit B
 // operand, K-major in shared memory, N = NPAD columns:
 //   * int8 mode: one column per token, the caller's int8 codes q;
-//   * fp32 mode: four columns per token, the signed base-256 digits of the
-//     31-bit fixed-point image X = round(x * 2^30 / absmax(token)).
+//   * fp32/bf16 mode: D columns per token (D = 8, or 4 for the MoE experts),
+//     the signed base-256 digits of the fixed-point image X = round(x * 2^sh),
+//     2^sh the power of two that puts the token's largest finite |x| in
+//     [2^(8D-3), 2^(8D-2)).
 // tcgen05.mma kind::i8 accumulates exact int32 sums D = sum_k u_k b_k in TMEM;
 // the epilogue subtracts sum_k b_k (so D becomes sum_k w_k b_k) and scales:
 //   int8: y = ((float)D * sx[s]) * scale[r]      (bit-exact vs the reference)
-//   fp32: y = (double)(sum_d D_d << 8d) * absmax/2^30 * scale[r]
-// For fp32 activations the only approximation is the fixed-point image of x
-// (error <= absmax * 2^-31 per element), far inside the 1e-5
-// condition-relative tolerance unless a row's inputs are all ~1e4x smaller
-// than the token's largest element.
+//   fp32: y = (double)(sum_d D_d * 256^d) * 2^-sh * scale[r]
+// With D = 8 every element within 2^38 of the token's absmax is exact, so the
+// result is the correctly rounded dot product.  Non-finite activations enter
+// as 0; the prep kernel lists their positions per token (a negative token
+// scale flags them) and the epilogue finishes the rows that meet them by the
+// reference's rule (nonfinite_row, ft_internal.cuh).
 //
 // Work items.  A problem (one weight, its activations and output) is cut
 // into items = (column pass, 128-row tile, K range).  The launch is persistent:
@@ -40,6 +43,7 @@
 // scratch area; the last CTA of a tile (atomic ticket) runs the final
 // epilogue and clears the scratch again, so it stays zero between calls.
 #include <cstring>
+#include <type_traits>
 
 #include "ft_internal.cuh"
 #include "ft_tc.cuh"
@@ -72,7 +76,13 @@ struct TqProblem {
   int64_t rows, n_tiles, n_chunks;
   const int8_t* bmat;       // [passes][n_chunks][NPAD*128]
   const int32_t* colsum;    // [passes][NPAD]
-  const double* tok_scale;  // fp32 mode: absmax * 2^-30 per token
+  const double* tok_scale;  // fp32 mode: 2^-sh per token, negative when the token has
+                            // non-finite elements
+  const int32_t* nf;        // fp32 mode: per token [count, kNfCap positions]
+  const void* x;            // fp32 mode: the activations (read by the non-finite fix-up)
+  int64_t K;
+  const float* kscale;      // fp32 mode: column-block scales folded into x, or null
+  int64_t kblock;
   const float* sx;          // int8 mode: per-token scale
   float* y;                 // y[t * ldy + r]
   int64_t ldy;
@@ -86,6 +96,7 @@ struct TqProblem {
 struct TqBatch {
   int nprob;
   int digits;
+  int bf16;  // fp32 mode: activations are bf16 bit patterns
   int64_t total_items;
   int* err;
   TqProblem p[kMaxProblems];
@@ -181,9 +192,38 @@ __device__ __forceinline__ void named_sync_epilogue() {
   asm volatile("bar.sync 1, 128;" ::: "memory");
 }
 
-template <int NPAD>
-__device__ __forceinline__ void epilogue_group(const TqProblem& p, int digits, int pass,
+// fp32 output of token t, row R from its digit-sum total S.
+template <bool kSparse>
+__device__ __forceinline__ void store_fp(const TqProblem& p, bool bf16, int64_t t, int64_t R,
+                                         double S) {
+  const double ts = p.tok_scale[t];
+  float y = (float)(S * fabs(ts) * (double)p.row_scales[R]);
+  if (ts < 0.0) {
+    const int32_t* nf = p.nf + t * (kNfCap + 1);
+    y = nonfinite_row(y, p.codes, kSparse ? 1 : 0, p.n_chunks, R,
+                      static_cast<const char*>(p.x) + t * p.K * (bf16 ? 2 : 4), bf16, p.K, nf + 1,
+                      nf[0], p.row_scales[R], p.kscale, p.kblock);
+  }
+  p.y[t * p.ldy + R] = y;
+}
+
+template <int NPAD, bool kSparse>
+__device__ __forceinline__ void epilogue_group(const TqProblem& p, int digits, bool bf16, int pass,
                                                int64_t R, int col0, const int32_t (&v)[16]) {
+  if (digits == 8) {
+#pragma unroll
+    for (int c = 0; c < 16; c += 8) {
+      const int lt = (col0 + c) >> 3;
+      const int64_t t = (int64_t)pass * p.tok_per_pass + lt;
+      if (t >= p.seq || lt >= p.tok_per_pass) break;
+      double S = 0.0;
+#pragma unroll
+      for (int d = 0; d < 8; ++d)
+        S += (double)(v[c + d] - p.colsum[pass * NPAD + col0 + c + d]) * (double)(1ll << (8 * d));
+      store_fp<kSparse>(p, bf16, t, R, S);
+    }
+    return;
+  }
   if (digits == 1) {
 #pragma unroll
     for (int c = 0; c < 16; ++c) {
@@ -205,7 +245,7 @@ __device__ __forceinline__ void epilogue_group(const TqProblem& p, int digits, i
         const long long a = (long long)(v[c + d] - p.colsum[pass * NPAD + col0 + c + d]);
         S += a * (1ll << (8 * d));
       }
-      p.y[t * p.ldy + R] = (float)((double)S * p.tok_scale[t] * (double)p.row_scales[R]);
+      store_fp<kSparse>(p, bf16, t, R, (double)S);
     }
   }
 }
@@ -518,7 +558,7 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
 #pragma unroll
           for (int c = 0; c < 16; ++c) v[c] = (int32_t)u[c];
           if (ok && R < p.rows && cg * 16 < ncols)
-            epilogue_group<NPAD>(p, b.digits, it.pass, R, cg * 16, v);
+            epilogue_group<NPAD, kSparse>(p, b.digits, b.bf16 != 0, it.pass, R, cg * 16, v);
         }
       } else {
         int32_t* accp = p.acc + (((int64_t)it.pass * p.n_tiles + it.tile) * NPAD) * kTileRows;
@@ -557,7 +597,7 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
               v[c] = __ldcg(a);
               __stcg(a, 0);  // leave the scratch zeroed for the next call
             }
-            if (ok && R < p.rows) epilogue_group<NPAD>(p, b.digits, it.pass, R, cg * 16, v);
+            if (ok && R < p.rows) epilogue_group<NPAD, kSparse>(p, b.digits, b.bf16 != 0, it.pass, R, cg * 16, v);
           }
           if (r == 0) p.cnt[(int64_t)it.pass * p.n_tiles + it.tile] = 0;
         }
@@ -576,12 +616,16 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
 // ------------------------------------------------------------- B prep -----
 // One block per (source, pass, token slot): writes the token's digit columns
 // of the K-major interleaved B operand for every chunk, their column sums,
-// and the token scale.  Slots past `seq` write zero columns.
+// the token scale and its non-finite positions.  Slots past `seq` write zero
+// columns.
 struct PrepSource {
   const void* x;
+  const float* kscale;  // column-block scales folded into x, or null
+  int64_t kblock;
   int8_t* bmat;
   int32_t* colsum;
   double* tok_scale;
+  int32_t* nf;  // [seq][1 + kNfCap]
   int64_t seq, K, n_chunks;
   int passes;
 };
@@ -605,6 +649,15 @@ __device__ __forceinline__ float load_x(const void* x, int xkind, int64_t i) {
                     : __uint_as_float((uint32_t) static_cast<const uint16_t*>(x)[i] << 16);
 }
 
+// element i of a source's activations, with its column-block scale applied
+__device__ __forceinline__ float load_xs(const PrepSource& src, int xkind, int64_t i, int64_t k) {
+  const float v = load_x(src.x, xkind, i);
+  return src.kscale ? __fmul_rn(v, src.kscale[k / src.kblock]) : v;
+}
+
+// DT: digits per token (1: int8 codes, 4 or 8), a template parameter so that
+// the digit arrays stay in registers.
+template <int DT>
 __global__ void __launch_bounds__(256) prep_b_kernel(const __grid_constant__ PrepBatch pb) {
   // Let the matmul that consumes this launch start streaming its weights now;
   // then wait for the previous matmul, which may still be reading bmat.
@@ -618,36 +671,72 @@ __global__ void __launch_bounds__(256) prep_b_kernel(const __grid_constant__ Pre
   const int lt = (int)(local % pb.tok_per_pass);
   const int64_t t = pass * pb.tok_per_pass + lt;
   const int64_t K = src.K, kpad = src.n_chunks * 128;
-  const int D = pb.D, npad = pb.npad;
+  constexpr int D = DT;
+  const int npad = pb.npad;
   __shared__ float red_f[8];
-  __shared__ int red_i[8][4];
+  __shared__ int red_n[8];
+  __shared__ int red_i[8][8];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool live = t < src.seq;
-  double mult = 0.0;
+  float f1 = 1.0f, f2 = 1.0f;
   if (pb.xkind != 2) {
+    // largest finite |x| and the non-finite count
     float amax = 0.0f;
+    int nnf = 0;
     if (live) {
 #pragma unroll 8
-      for (int64_t k = threadIdx.x; k < K; k += blockDim.x)
-        amax = fmaxf(amax, fabsf(load_x(src.x, pb.xkind, t * K + k)));
+      for (int64_t k = threadIdx.x; k < K; k += blockDim.x) {
+        const float v = load_xs(src, pb.xkind, t * K + k, k);
+        if (is_nonfinite(v)) ++nnf;
+        else amax = fmaxf(amax, fabsf(v));
+      }
     }
+    int incl = nnf;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(amax)));
     if (lane == 0) red_f[warp] = amax;
+    if (lane == 31) red_n[warp] = incl;
     __syncthreads();
     amax = 0.0f;
-    for (int w = 0; w < 8; ++w) amax = fmaxf(amax, red_f[w]);
-    if (amax > 0.0f) mult = 1073741824.0 / (double)amax;  // 2^30 / absmax
-    if (threadIdx.x == 0 && live) src.tok_scale[t] = (double)amax / 1073741824.0;
+    int before = incl - nnf, total = 0;
+    for (int w = 0; w < 8; ++w) {
+      amax = fmaxf(amax, red_f[w]);
+      if (w < warp) before += red_n[w];
+      total += red_n[w];
+    }
+    const int sh = amax > 0.0f ? digit_shift(amax, D) : 0;
+    const int s1 = sh > 127 ? 127 : (sh < -126 ? -126 : sh);
+    f1 = __int_as_float((s1 + 127) << 23);
+    f2 = __int_as_float((sh - s1 + 127) << 23);
+    if (live) {
+      int32_t* nf = src.nf + t * (kNfCap + 1);
+      if (threadIdx.x == 0) {
+        // 2^-sh (1 for an all-zero token), negative when non-finite elements exist
+        const double sc = amax > 0.0f ? __longlong_as_double((long long)(1023 - sh) << 52) : 1.0;
+        src.tok_scale[t] = total ? -sc : sc;
+        nf[0] = total;
+      }
+      if (nnf != 0 && total <= kNfCap) {
+        int slot = before;
+        for (int64_t k = threadIdx.x; k < K; k += blockDim.x)
+          if (is_nonfinite(load_xs(src, pb.xkind, t * K + k, k))) nf[1 + slot++] = (int32_t)k;
+      }
+    }
   }
   // 16 consecutive K per step: one 16-byte row of the operand per digit column
-  int csum[4] = {0, 0, 0, 0};
+  int csum[D];
+#pragma unroll
+  for (int d = 0; d < D; ++d) csum[d] = 0;
   const int64_t ngroups = kpad >> 4;
   for (int64_t kg = threadIdx.x; kg < ngroups; kg += blockDim.x) {
     const int64_t k0 = kg * 16;
-    uint32_t w[4][4];
+    uint32_t w[D][4];
 #pragma unroll
-    for (int d = 0; d < 4; ++d) w[d][0] = w[d][1] = w[d][2] = w[d][3] = 0u;
+    for (int d = 0; d < D; ++d) w[d][0] = w[d][1] = w[d][2] = w[d][3] = 0u;
     if (live && k0 < K) {
       if (pb.xkind == 2) {
         const int8_t* q = static_cast<const int8_t*>(src.x) + t * K + k0;
@@ -655,14 +744,15 @@ __global__ void __launch_bounds__(256) prep_b_kernel(const __grid_constant__ Pre
           const uint4 v = __ldg(reinterpret_cast<const uint4*>(q));
           w[0][0] = v.x; w[0][1] = v.y; w[0][2] = v.z; w[0][3] = v.w;
         } else {
-          for (int e = 0; e < 16 && k0 + e < K; ++e)
-            w[0][e >> 2] |= (uint32_t)(q[e] & 0xFF) << (8 * (e & 3));
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            if (k0 + e < K) w[0][e >> 2] |= (uint32_t)(q[e] & 0xFF) << (8 * (e & 3));
         }
 #pragma unroll
         for (int j = 0; j < 4; ++j) csum[0] = __dp4a((int)w[0][j], 0x01010101, csum[0]);
       } else {
         float xv[16];
-        const bool vec = pb.xkind == 0 && k0 + 16 <= K &&
+        const bool vec = pb.xkind == 0 && k0 + 16 <= K && !src.kscale &&
                          (reinterpret_cast<uintptr_t>(static_cast<const float*>(src.x) + t * K + k0) & 15) == 0;
         if (vec) {
           const float4* f4 = reinterpret_cast<const float4*>(static_cast<const float*>(src.x) + t * K + k0);
@@ -673,35 +763,39 @@ __global__ void __launch_bounds__(256) prep_b_kernel(const __grid_constant__ Pre
           }
         } else {
 #pragma unroll
-          for (int e = 0; e < 16; ++e) xv[e] = k0 + e < K ? load_x(src.x, pb.xkind, t * K + k0 + e) : 0.0f;
+          for (int e = 0; e < 16; ++e)
+            xv[e] = k0 + e < K ? load_xs(src, pb.xkind, t * K + k0 + e, k0 + e) : 0.0f;
         }
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          int X = __double2int_rn((double)xv[e] * mult);  // |X| <= 2^30
+          const float xs = is_nonfinite(xv[e]) ? 0.0f : __fmul_rn(__fmul_rn(xv[e], f1), f2);
+          // X = round(x * 2^sh), |X| < 2^(8D-2); balanced base-256 digits (64-bit
+          // arithmetic only for D = 8)
+          using XT = typename std::conditional<(D > 4), long long, int>::type;
+          XT X = D > 4 ? (XT)__float2ll_rn(xs) : (XT)__float2int_rn(xs);
 #pragma unroll
-          for (int d = 0; d < 3; ++d) {
-            const int lo = ((X & 0xFF) ^ 0x80) - 0x80;  // signed low digit
+          for (int d = 0; d < D - 1; ++d) {
+            const int lo = ((int)(X & 0xFF) ^ 0x80) - 0x80;  // signed low digit
             w[d][e >> 2] |= (uint32_t)(lo & 0xFF) << (8 * (e & 3));
             csum[d] += lo;
             X = (X - lo) >> 8;
           }
-          w[3][e >> 2] |= (uint32_t)(X & 0xFF) << (8 * (e & 3));  // |X| <= 65 here
-          csum[3] += X;
+          // the top digit, |X| <= 64 here
+          w[D - 1][e >> 2] |= (uint32_t)((int)X & 0xFF) << (8 * (e & 3));
+          csum[D - 1] += (int)X;
         }
       }
     }
     const int64_t chunk = k0 >> 7;
     const int kin = (int)(k0 & 127);
 #pragma unroll
-    for (int d = 0; d < 4; ++d)
-      if (d < D)
-        *reinterpret_cast<uint4*>(src.bmat + b_offset(pass, chunk, lt * D + d, kin, npad, src.n_chunks)) =
-            make_uint4(w[d][0], w[d][1], w[d][2], w[d][3]);
+    for (int d = 0; d < D; ++d)
+      *reinterpret_cast<uint4*>(src.bmat + b_offset(pass, chunk, lt * D + d, kin, npad, src.n_chunks)) =
+          make_uint4(w[d][0], w[d][1], w[d][2], w[d][3]);
   }
-  for (int d = 0; d < D; ++d) {
-    int v = csum[d];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  for (int d = 0; d < D; ++d) {
+    const int v = __reduce_add_sync(0xffffffffu, csum[d]);
     if (lane == 0) red_i[warp][d] = v;
   }
   __syncthreads();
@@ -758,10 +852,16 @@ int launch_grouped_t(const TqBatch& batch, int64_t grid, cudaStream_t s) {
 // activation pointer, K and seq share one prepared B operand.
 int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t seq,
                       const void* const* xs, int xkind, const float* const* sxs, float* const* ys,
-                      const int64_t* ldys, cudaStream_t s, const int64_t* seqs) {
+                      const int64_t* ldys, cudaStream_t s, const int64_t* seqs, int digits,
+                      const float* kscale, int64_t kblock) {
   FT_CHECK(n >= 1 && n <= kMaxProblems, FT_ERR_UNSUPPORTED, "group size %d not in [1, %d]", n,
            kMaxProblems);
-  const int D = xkind == 2 ? 1 : 4;
+  if (digits <= 0) digits = kDigitsExact;
+  FT_CHECK(xkind == 2 || digits == kDigitsExact || digits == kDigitsMoE, FT_ERR_UNSUPPORTED,
+           "unsupported digit count %d", digits);
+  const int D = xkind == 2 ? 1 : digits;
+  FT_CHECK(!kscale || (xkind != 2 && kblock >= 1), FT_ERR_UNSUPPORTED,
+           "column-block scales need fp32/bf16 activations and a block size >= 1");
   int64_t max_seq = 0;
   for (int i = 0; i < n; ++i) {
     const int64_t si = seqs ? seqs[i] : seq;
@@ -806,7 +906,8 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
   // decode shapes run on the warp-level kernel (ft_gemv.cu), which builds its
   // activation operand itself
   bool gemv = true;
-  for (int q = 0; q < nlive && gemv; ++q) gemv = gemv_fits(ws[live[q]], src_seq[src_of[q]], xkind);
+  for (int q = 0; q < nlive && gemv; ++q)
+    gemv = gemv_fits(ws[live[q]], src_seq[src_of[q]], xkind, D);
   if (gemv) {
     GvLaunchProblem gp[kMaxProblems];
     for (int q = 0; q < nlive; ++q) {
@@ -815,14 +916,14 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
       const int j = src_of[q];
       gp[q] = GvLaunchProblem{w->codes, w->row_scales, w->rows, w->n_chunks, src_x[j],
                               src_k[j], src_seq[j], sxs ? sxs[i] : nullptr, ys[i],
-                              ldys ? ldys[i] : w->rows};
+                              ldys ? ldys[i] : w->rows, kscale, kblock};
     }
-    return launch_gemv(ctx, nlive, gp, xkind, ws[live[0]]->format == 1, s);
+    return launch_gemv(ctx, nlive, gp, xkind, ws[live[0]]->format == 1, D, s);
   }
 
-  // workspace: per source B operand, column sums, token scales
+  // workspace: per source B operand, column sums, token scales, non-finite lists
   size_t off = 0;
-  size_t b_off[kMaxSources], cs_off[kMaxSources], ts_off[kMaxSources];
+  size_t b_off[kMaxSources], cs_off[kMaxSources], ts_off[kMaxSources], nf_off[kMaxSources];
   for (int j = 0; j < nsrc; ++j) {
     const int64_t nch = ceil_div(src_k[j], kChunkK);
     const int64_t passes = ceil_div(src_seq[j], tok_per_pass);
@@ -832,6 +933,8 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
     off = round_up((int64_t)(off + passes * npad * 4), 256);
     ts_off[j] = off;
     off = round_up((int64_t)(off + src_seq[j] * 8), 256);
+    nf_off[j] = off;
+    off = round_up((int64_t)(off + src_seq[j] * (kNfCap + 1) * 4), 256);
   }
   int st = workspace_reserve(ctx, off, s);
   if (st != FT_OK) return st;
@@ -850,6 +953,7 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
   memset(&batch, 0, sizeof(batch));
   batch.nprob = nlive;
   batch.digits = D;
+  batch.bf16 = xkind == 1;
   int64_t items = 0;
   for (int q = 0; q < nlive; ++q) {
     const int i = live[q];
@@ -875,6 +979,11 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
     p.bmat = reinterpret_cast<const int8_t*>(wsb + b_off[j]);
     p.colsum = reinterpret_cast<const int32_t*>(wsb + cs_off[j]);
     p.tok_scale = reinterpret_cast<const double*>(wsb + ts_off[j]);
+    p.nf = reinterpret_cast<const int32_t*>(wsb + nf_off[j]);
+    p.x = src_x[j];
+    p.K = src_k[j];
+    p.kscale = kscale;
+    p.kblock = kblock;
     p.sx = sxs ? sxs[i] : nullptr;
     p.y = ys[i];
     p.ldy = ldys ? ldys[i] : w->rows;
@@ -918,9 +1027,12 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
       pb.block_begin[j] = blocks;
       PrepSource& ps = pb.s[j];
       ps.x = src_x[j];
+      ps.kscale = kscale;
+      ps.kblock = kblock;
       ps.bmat = reinterpret_cast<int8_t*>(wsb + b_off[j]);
       ps.colsum = reinterpret_cast<int32_t*>(wsb + cs_off[j]);
       ps.tok_scale = reinterpret_cast<double*>(wsb + ts_off[j]);
+      ps.nf = reinterpret_cast<int32_t*>(wsb + nf_off[j]);
       ps.seq = src_seq[j];
       ps.K = src_k[j];
       ps.n_chunks = ceil_div(src_k[j], kChunkK);
@@ -938,7 +1050,9 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    FT_CUDA(cudaLaunchKernelEx(&cfg, prep_b_kernel, pb));
+    if (D == 1) FT_CUDA(cudaLaunchKernelEx(&cfg, prep_b_kernel<1>, pb));
+    else if (D == 4) FT_CUDA(cudaLaunchKernelEx(&cfg, prep_b_kernel<4>, pb));
+    else FT_CUDA(cudaLaunchKernelEx(&cfg, prep_b_kernel<8>, pb));
     FT_LAUNCH_CHECK();
   }
 
@@ -988,20 +1102,22 @@ int launch_tc_matmul(ft_ctx* ctx, const ft_weight* w, int64_t seq, const void* x
 // ---------------------------------------------------------------------------
 namespace ft {
 namespace {
-constexpr int64_t kNaMaxSeq = 4;        // tokens per call (4 digit columns each -> NPAD 16)
+constexpr int64_t kNaMaxSeq = 4;  // tokens per call (8 digit columns each -> NPAD 32)
 constexpr int64_t kNaMaxCols = 16384;
 constexpr int64_t kNaMaxRows = 16384;
-constexpr int kNaNpad = 16;
+constexpr int kNaNpad = 32;
 constexpr size_t kNaBOff = 0;
-constexpr size_t kNaBBytes = (size_t)(kNaMaxCols / kChunkK) * kNaNpad * 128;        // 256 KiB
-constexpr size_t kNaColsumOff = kNaBOff + kNaBBytes;                                  // 16 x int32
+constexpr size_t kNaBBytes = (size_t)(kNaMaxCols / kChunkK) * kNaNpad * 128;        // 512 KiB
+constexpr size_t kNaColsumOff = kNaBOff + kNaBBytes;                                  // 32 x int32
 constexpr size_t kNaTokOff = kNaColsumOff + 256;                                      // 4 x double
-constexpr size_t kNaAccOff = kNaTokOff + 256;
-constexpr size_t kNaAccBytes = (size_t)(kNaMaxRows / kTileRows) * kNaNpad * kTileRows * 4;  // 1 MiB
+constexpr size_t kNaNfOff = kNaTokOff + 256;                      // 4 x (1 + kNfCap) int32
+constexpr size_t kNaAccOff = kNaNfOff + 512;
+constexpr size_t kNaAccBytes = (size_t)(kNaMaxRows / kTileRows) * kNaNpad * kTileRows * 4;  // 2 MiB
 constexpr size_t kNaCntOff = kNaAccOff + kNaAccBytes;
 constexpr size_t kNaCntBytes = (size_t)(kNaMaxRows / kTileRows) * 4;
 constexpr size_t kNaErrOff = kNaCntOff + (kNaCntBytes + 255) / 256 * 256;
-constexpr size_t kNaBytes = kNaErrOff + 256;  // about 1.3 MB
+constexpr size_t kNaBytes = kNaErrOff + 256;  // about 2.6 MB
+static_assert(kNaMaxSeq * (1 + kNfCap) * 4 <= 512, "non-finite lists must fit their slot");
 constexpr int kNaMaxDevices = 64;
 
 static void* g_na_ptr[kNaMaxDevices];  // device address of g_noalloc_scratch, per device
@@ -1031,11 +1147,12 @@ int launch_tc_noalloc(ft_ctx* ctx, const ft_weight* w, int64_t seq, const float*
   int st = noalloc_scratch(ctx->device, &zs);
   if (st != FT_OK) return st;
 
-  const int D = 4, npad = kNaNpad, tok_per_pass = npad / D;
+  const int D = kDigitsExact, npad = kNaNpad, tok_per_pass = npad / D;
   static thread_local TqBatch batch;
   memset(&batch, 0, sizeof(batch));
   batch.nprob = 1;
   batch.digits = D;
+  batch.bf16 = 0;
   const int64_t grid_target = (int64_t)ctx->num_sms * (tmem_cols_for(npad) <= 256 ? 2 : 1);
   TqProblem& p = batch.p[0];
   int64_t want = (4 * grid_target + w->n_tiles - 1) / w->n_tiles;
@@ -1051,6 +1168,11 @@ int launch_tc_noalloc(ft_ctx* ctx, const ft_weight* w, int64_t seq, const float*
   p.bmat = reinterpret_cast<const int8_t*>(zs + kNaBOff);
   p.colsum = reinterpret_cast<const int32_t*>(zs + kNaColsumOff);
   p.tok_scale = reinterpret_cast<const double*>(zs + kNaTokOff);
+  p.nf = reinterpret_cast<const int32_t*>(zs + kNaNfOff);
+  p.x = x;
+  p.K = w->cols;
+  p.kscale = nullptr;
+  p.kblock = 1;
   p.sx = nullptr;
   p.y = y;
   p.ldy = w->rows;
@@ -1083,17 +1205,20 @@ int launch_tc_noalloc(ft_ctx* ctx, const ft_weight* w, int64_t seq, const float*
   pb.block_begin[1] = tok_per_pass;
   PrepSource& ps = pb.s[0];
   ps.x = x;
+  ps.kscale = nullptr;
+  ps.kblock = 1;
   ps.bmat = reinterpret_cast<int8_t*>(zs + kNaBOff);
   ps.colsum = reinterpret_cast<int32_t*>(zs + kNaColsumOff);
   ps.tok_scale = reinterpret_cast<double*>(zs + kNaTokOff);
+  ps.nf = reinterpret_cast<int32_t*>(zs + kNaNfOff);
   ps.seq = seq;
   ps.K = w->cols;
   ps.n_chunks = w->n_chunks;
   ps.passes = 1;
-  prep_b_kernel<<<tok_per_pass, 256, 0, s>>>(pb);
+  prep_b_kernel<kDigitsExact><<<tok_per_pass, 256, 0, s>>>(pb);
   FT_LAUNCH_CHECK();
   const int64_t grid = batch.total_items < grid_target ? batch.total_items : grid_target;
-  return launch_grouped_t<16>(batch, grid, s);
+  return launch_grouped_t<kNaNpad>(batch, grid, s);
 }
 }  // namespace
 }  // namespace ft

@@ -161,6 +161,79 @@ class DeviceTernaryWeight:
         from .ternary import pack_ternary
         return cls.from_packed_u8(pack_ternary(values), rows, cols, row_scales, device)
 
+    @classmethod
+    def from_sparse_indices(cls, pos, neg, rows, cols, row_scales, device=None):
+        """Index-list weights (ternary_sparse_indices, src/model/ternary.rs:681-707):
+        per row the columns of +1 (``pos``) and -1 (``neg``).  Stored densely at
+        2 bits/weight."""
+        from .ternary import index_lists_to_csr
+        ctx = get_context(device)
+        if len(pos) != rows or len(neg) != rows:
+            raise ShapeError("pos/neg need one index list per row")
+        po, pi = index_lists_to_csr(pos)
+        no, ni = index_lists_to_csr(neg)
+        s = _host(row_scales, np.float32)
+        if s.size == 1:
+            s = np.full(rows, s[0], np.float32)
+        if s.size < rows:
+            raise ShapeError("row_scales too short")
+        pi = pi if pi.size else np.zeros(1, np.int64)
+        ni = ni if ni.size else np.zeros(1, np.int64)
+        h = C.c_void_p()
+        call("ft_weight_upload_index_lists", ctx.handle, int(rows), int(cols),
+             po.ctypes.data_as(C.c_void_p), pi.ctypes.data_as(C.c_void_p),
+             no.ctypes.data_as(C.c_void_p), ni.ctypes.data_as(C.c_void_p),
+             s.ctypes.data_as(C.c_void_p), C.byref(h))
+        return cls(h, rows, cols, ctx)
+
+    @classmethod
+    def from_fp32(cls, weights, rows, cols, device=None):
+        """TernaryExpert::from_fp32 (src/model/cpu_moe.rs:33-37): absmean-quantized on
+        the device.  Returns the weight; its scale is ``.alpha``."""
+        ctx = get_context(device)
+        w = _host(weights, np.float32)
+        if w.size != rows * cols:
+            raise ShapeError("weights must hold rows * cols floats")
+        h = C.c_void_p()
+        a = C.c_float()
+        call("ft_weight_quantize_f32", ctx.handle, w.ctypes.data_as(C.c_void_p), int(rows),
+             int(cols), C.byref(a), C.byref(h))
+        out = cls(h, rows, cols, ctx)
+        out.alpha = np.float32(a.value)
+        return out
+
+    def requantize(self, shadow: torch.Tensor, alpha: float, stream=None):
+        """STE re-quantization with a layer-shared alpha (src/training/bit_moe.rs:243-262)
+        from a [rows, cols] float32 or bfloat16 CUDA tensor."""
+        if shadow.numel() != self.rows * self.cols or shadow.dtype not in (torch.float32,
+                                                                          torch.bfloat16):
+            raise ShapeError("shadow must be float32/bfloat16 [rows, cols]")
+        call("ft_weight_requantize", self.ctx.handle, self.handle, _dptr(shadow),
+             int(shadow.dtype == torch.bfloat16), float(alpha), _stream_ptr(stream))
+
+    def export_packed_u8(self) -> np.ndarray:
+        """The resident codes as the reference pack_ternary byte stream."""
+        out = np.empty((self.rows * self.cols + 3) // 4, np.uint8)
+        call("ft_weight_export_packed_u8", self.ctx.handle, self.handle,
+             out.ctypes.data_as(C.c_void_p))
+        return out
+
+    def matmul_blocked_f32(self, x: torch.Tensor, block_scales: torch.Tensor, block_size: int,
+                           out: torch.Tensor | None = None, stream=None):
+        """ternary_matmul_blocked (src/model/ternary.rs:541-579): one scale per block of
+        ``block_size`` columns, shared by all rows (times the row scale)."""
+        if x.dtype != torch.float32 or x.shape[-1] != self.cols:
+            raise ShapeError(f"x must be float32 [..., {self.cols}]")
+        nb = -(-self.cols // int(block_size))
+        if block_scales.dtype != torch.float32 or block_scales.numel() != nb:
+            raise ShapeError(f"block_scales must be float32 [{nb}]")
+        seq = x.numel() // self.cols
+        if out is None:
+            out = torch.empty(seq, self.rows, dtype=torch.float32, device=x.device)
+        call("ft_ternary_matmul_blocked_f32", self.ctx.handle, self.handle, seq, _dptr(x),
+             _dptr(block_scales), int(block_size), _dptr(out), _stream_ptr(stream))
+        return out
+
     def device_bytes(self) -> int:
         b = C.c_int64()
         call("ft_weight_info", self.handle, None, None, C.byref(b))
@@ -336,3 +409,34 @@ class GpuMatmulAccelerator:
         y = np.empty(seq_len * out_rows, np.float32)
         check(_vram_fn()(self.ctx.handle, weight.handle, _addr(x), int(seq_len), _addr(y)))
         return y
+
+
+def shadow_alpha(shadows, device=None):
+    """BitMoELayer::recompute_alpha (src/training/bit_moe.rs:210-241): mean |v| over
+    the given float32/bfloat16 CUDA tensors, summed in f64.  None when they are empty."""
+    ctx = get_context(device)
+    if not shadows:
+        return None
+    bf16 = shadows[0].dtype == torch.bfloat16
+    if any((t.dtype == torch.bfloat16) != bf16 for t in shadows):
+        raise ShapeError("shadows must share one dtype")
+    ptrs = (C.c_void_p * len(shadows))(*[t.data_ptr() for t in shadows])
+    cnts = (C.c_int64 * len(shadows))(*[t.numel() for t in shadows])
+    for t in shadows:
+        _dptr(t)
+    a = C.c_float(np.nan)
+    call("ft_shadow_alpha", ctx.handle, len(shadows), ptrs, cnts, int(bf16), C.byref(a))
+    return None if np.isnan(a.value) else np.float32(a.value)
+
+
+def ternary_matmul_sparse_decode(pos_indices, neg_indices, scale, input, out_rows, device=None):
+    """src/model/ternary.rs:647-672 with host slices: index lists in, host vector out
+    (the lists are uploaded densely; keep a DeviceTernaryWeight.from_sparse_indices
+    weight for repeated decode steps)."""
+    x = _host(input, np.float32)
+    w = DeviceTernaryWeight.from_sparse_indices(pos_indices, neg_indices, out_rows, x.size,
+                                                np.float32(scale), device)
+    y = w.matmul_f32(torch.from_numpy(x).to(f"cuda:{w.ctx.device}").view(1, -1))
+    out = y.cpu().numpy().ravel()
+    w.close()
+    return out

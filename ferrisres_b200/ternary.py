@@ -72,3 +72,43 @@ def round_half_away(a) -> np.ndarray:
 def dequantize_ternary(values, scale) -> np.ndarray:
     """src/model/ternary.rs:62-64."""
     return np.asarray(values, np.int8).astype(np.float32) * np.float32(scale)
+
+
+def quantize_ternary_blocked(weights, block_size: int):
+    """Block-wise absmean quantizer (src/model/ternary.rs:76-110): flat blocks of
+    ``block_size`` elements, one alpha per block.  Returns (int8 values, scales)."""
+    w = np.asarray(weights, dtype=np.float32).ravel()
+    if w.size == 0:
+        return np.zeros(0, np.int8), np.zeros(0, np.float32)
+    q = np.zeros(w.size, np.int8)
+    scales = []
+    for b0 in range(0, w.size, block_size):
+        qb, a = quantize_ternary(w[b0:b0 + block_size])
+        q[b0:b0 + block_size] = qb
+        scales.append(a)
+    return q, np.asarray(scales, np.float32)
+
+
+def dequantize_ternary_blocked(values, scales, block_size: int) -> np.ndarray:
+    """src/model/ternary.rs:113-130."""
+    v = np.asarray(values, np.int8).astype(np.float32)
+    s = np.repeat(np.asarray(scales, np.float32), block_size)[:v.size]
+    return (s * v).astype(np.float32)
+
+
+def ternary_sparse_indices(values, out_rows: int, in_cols: int):
+    """src/model/ternary.rs:681-707: per row, the columns holding +1 and -1.
+    Returns (pos, neg), two lists of ``out_rows`` int64 arrays in column order."""
+    t = np.asarray(values, np.int8).reshape(out_rows, in_cols)
+    pos = [np.nonzero(row == 1)[0].astype(np.int64) for row in t]
+    neg = [np.nonzero(row == -1)[0].astype(np.int64) for row in t]
+    return pos, neg
+
+
+def index_lists_to_csr(lists):
+    """A list of per-row index arrays -> (offsets [rows + 1], concatenated indices)."""
+    off = np.zeros(len(lists) + 1, np.int64)
+    off[1:] = np.cumsum([len(a) for a in lists])
+    idx = np.concatenate([np.asarray(a, np.int64) for a in lists]) if off[-1] else \
+        np.zeros(0, np.int64)
+    return off, idx

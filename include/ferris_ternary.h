@@ -99,13 +99,61 @@ int ft_sparse_upload_host(ft_ctx* ctx, const uint8_t* patterns_host, const uint8
  * 1 = -1) per word. */
 int ft_sparse_upload_wgsl(ft_ctx* ctx, const uint32_t* words_host, int64_t rows, int64_t cols,
                           const float* row_scales_host, ft_weight** out);
+/* The codes of a resident weight (dense or 2:4) back as the reference pack_ternary
+ * byte stream (src/model/ternary.rs:141-163): (rows*cols+3)/4 host bytes, padding
+ * bits 0.  Synchronous.  For saving weights (the reference's TernaryExpert::to_fp32
+ * path, src/model/cpu_moe.rs:64-66) and for checking device-side quantization. */
+int ft_weight_export_packed_u8(ft_ctx* ctx, const ft_weight* w, uint8_t* packed_host);
 int ft_weight_destroy(ft_weight* w);
 int ft_weight_info(const ft_weight* w, int64_t* rows, int64_t* cols, int64_t* device_bytes);
+
+/* Index-list form (ternary_sparse_indices, src/model/ternary.rs:681-707, used by
+ * ternary_matmul_sparse_decode, :647-672): per row the columns holding +1 and
+ * -1, as CSR host arrays (pos_off/neg_off [rows + 1], starting at 0; each
+ * row's columns strictly increasing and the two lists disjoint, as
+ * ternary_sparse_indices produces them; otherwise FT_ERR_SHAPE).  Stored as a
+ * dense 2-bit weight (2 bits per weight beats a 32-bit index below ~94%
+ * sparsity); ternary_matmul_sparse_decode is then ft_ternary_matmul_f32 with
+ * seq 1 and the scale broadcast into row_scales_host. */
+int ft_weight_upload_index_lists(ft_ctx* ctx, int64_t rows, int64_t cols, const int64_t* pos_off,
+                                 const int64_t* pos_idx, const int64_t* neg_off,
+                                 const int64_t* neg_idx, const float* row_scales_host,
+                                 ft_weight** out);
+/* fp32 weights quantized on the device: TernaryExpert::from_fp32
+ * (src/model/cpu_moe.rs:33-37) = quantize_ternary (src/model/ternary.rs:31-57):
+ * alpha = (sequential fp32 sum |w| / n) / 0.7978845608 (1 when not positive),
+ * q = clamp(round_half_away(w * (1 / alpha)), -1, 1), NaN -> 0; every row
+ * scale = alpha (returned in alpha_out when non-null).  w_host [rows, cols]. */
+int ft_weight_quantize_f32(ft_ctx* ctx, const float* w_host, int64_t rows, int64_t cols,
+                           float* alpha_out, ft_weight** out);
+/* STE re-quantization in place (BitMoELayer::requantize_all, shared alpha,
+ * src/training/bit_moe.rs:243-262): from a [rows, cols] fp32 (or bf16 bit
+ * patterns when src_bf16) device matrix, n = v / alpha, q = +1 if n > 0.5, -1
+ * if n < -0.5, else 0 (all 0 when alpha < 1e-10); every row scale = alpha.
+ * Asynchronous on stream; the weight must not be in use by earlier work on
+ * other streams. */
+int ft_weight_requantize(ft_ctx* ctx, ft_weight* w, const void* src_dev, int src_bf16, float alpha,
+                         void* stream);
+/* The layer-shared alpha of BitMoELayer::recompute_alpha (src/training/bit_moe.rs:210-241):
+ * mean |v| over n device buffers (counts[i] elements each, fp32 or bf16), summed in f64,
+ * then (float)(sum / count).  A parallel f64 sum: it equals the reference's sequential one
+ * whenever the f64 partial sums are exact (bf16 magnitudes within about 2^(44 - log2 n) of
+ * each other).  Synchronous.  Leaves *alpha_out unchanged when the buffers hold no element,
+ * as the reference keeps its previous alpha. */
+int ft_shadow_alpha(ft_ctx* ctx, int n, const void* const* src_dev, const int64_t* counts,
+                    int src_bf16, float* alpha_out);
 
 /* ---- dense compute (device pointers, caller stream) -------------------- */
 /* y[s, r] = row_scale[r] * sum_k W[r, k] * x[s, k], fp32 activations.
  * Replaces TernaryMatMulOp::dispatch (src/compute/kernels/ternary_matmul.rs:167-225)
- * for weights held as ft_weight.  Any seq >= 1 (decode GEMV and prefill GEMM). */
+ * for weights held as ft_weight.  Any seq >= 1 (decode GEMV and prefill GEMM).
+ * Precision: the activations enter as 64-bit fixed point per token (exact for
+ * every element within 2^38 of the token's largest finite |x|) and the sums are
+ * exact integers, so each output is the correctly rounded value of the exact
+ * sum times the row scale.  Non-finite activations follow the reference shader
+ * (src/compute/kernels/ternary_matmul.rs:54-70): x[k] enters a row only where
+ * its weight is nonzero, so a row meeting NaN or infinities of both signs is
+ * NaN, one sign of infinity gives that infinity times the row scale. */
 int ft_ternary_matmul_f32(ft_ctx* ctx, const ft_weight* w, int64_t seq, const float* x_dev,
                           float* y_dev, void* stream);
 /* Same with bf16 activations (bit patterns as uint16). */
@@ -128,7 +176,7 @@ int ft_ternary_matmul_i8_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws,
  * itself (a serving engine with a fixed arena, or an FFI contract that forbids
  * hidden allocations on the hot path), or a real-time loop that cannot take
  * cudaMalloc's implicit device-wide synchronisation.  It calls no cudaMalloc or
- * cudaFree: its scratch is one ~1.3 MB array reserved in the library image on
+ * cudaFree: its scratch is one ~2.6 MB array reserved in the library image on
  * every GPU that loads the library, held until the process exits.  Limits:
  * seq <= 4, w rows <= 16384, w cols <= 16384; larger shapes return
  * FT_ERR_UNSUPPORTED.  The context and weight are created beforehand as usual.
@@ -142,6 +190,16 @@ int ft_ternary_matmul_i8_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws,
  * reads and clears it. */
 int ft_ternary_matmul_f32_noalloc(ft_ctx* ctx, const ft_weight* w, int64_t seq, const float* x_dev,
                                   float* y_dev, void* stream);
+/* ternary_matmul_blocked (src/model/ternary.rs:541-579): y[s, r] = row_scale[r] *
+ * sum_b block_scales[b] * sum_{k in block b} W[r, k] x[s, k], block b = columns
+ * [b * block_size, (b + 1) * block_size), block_scales_dev = ceil(cols / block_size)
+ * device floats shared by every row (upload the weight with row scales 1 for the
+ * reference's form).  The block scales are folded into the activations
+ * (x' = scale * x) before the fixed-point image.  Non-finite inputs follow that
+ * reference's products w * x: a zero weight meeting an infinity gives NaN too. */
+int ft_ternary_matmul_blocked_f32(ft_ctx* ctx, const ft_weight* w, int64_t seq, const float* x_dev,
+                                  const float* block_scales_dev, int64_t block_size, float* y_dev,
+                                  void* stream);
 /* Per-token absmax int8 quantizer: sx[s] = absmax/127 (1 when absmax == 0),
  * q = clamp(round_half_away(x * (127/absmax)), -127, 127).  No reference
  * counterpart (the reference has no int8 activation path); the formula is
@@ -204,6 +262,29 @@ int ft_moe_destroy(ft_moe* m);
  * TernaryMoELayer::forward (src/model/ternary_moe.rs:145). */
 int ft_moe_forward(ft_ctx* ctx, ft_moe* m, int64_t T, const void* x_dev, int x_is_bf16,
                    float* y_dev, float* probs_dev, void* stream);
+/* Same layer from fp32 expert matrices (the checkpoint's
+ * layers.{i}.moe.expert.{e}.{gate,up,down}, src/model/checkpoint.rs:21-24, which
+ * the reference re-quantizes at load, :387-400): each matrix is quantized on the
+ * device as ft_weight_quantize_f32 does (its own absmean alpha as every row scale).
+ * gate_f32/up_f32 [inter, hidden], down_f32 [hidden, inter], host; NULL gate for
+ * experts held by another rank. */
+int ft_moe_create_f32(ft_ctx* ctx, int64_t n_experts, int64_t hidden, int64_t inter, int top_k,
+                      int use_gelu, const float* router_host, const float* const* gate_f32,
+                      const float* const* up_f32, const float* const* down_f32, ft_moe** out);
+/* Fused decode step for 1..8 tokens (tokens x top_k <= 16): the whole layer
+ * (router, softmax top-k, gate/up, SwiGLU or GeLU, down, weighted combine) in
+ * ONE cooperative kernel launch, with no host synchronisation (capturable in a
+ * CUDA graph after a first call has sized the scratch).  Replaces the
+ * reference's per-expert decode loop (src/model/cpu_block_attn_res.rs:2284-2316)
+ * over TernaryMoELayer::forward (src/model/ternary_moe.rs:145-223).  y_dev
+ * [T, hidden] fp32; topk_idx_dev / topk_w_dev [T, top_k] receive the routing;
+ * probs_dev (optional) [T, n_experts].  Every expert must be on this device.
+ * Router scores are fp32 dots in a different order than the reference's
+ * sequential sum; expert activations use 4 fixed-point digits (the layer's
+ * tolerance); non-finite activations are not propagated (use ft_moe_forward). */
+int ft_moe_decode(ft_ctx* ctx, ft_moe* m, int64_t T, const void* x_dev, int x_is_bf16,
+                  float* y_dev, int32_t* topk_idx_dev, float* topk_w_dev, float* probs_dev,
+                  void* stream);
 /* Same with host buffers (fp32), the reference's &[f32] -> Vec<f32> form. */
 int ft_moe_forward_host(ft_ctx* ctx, ft_moe* m, const float* input_host, size_t seq,
                         float* output_host);

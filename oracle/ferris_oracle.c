@@ -183,6 +183,14 @@ void fo_pack_ternary_rows_u32(const int8_t* values, size_t rows, size_t cols, ui
     }
 }
 
+/* Rust's `f32 as i32`: saturating, NaN -> 0 (C's cast is undefined there). */
+static int fo_as_i32(float r) {
+  if (r != r) return 0;
+  if (r >= 2147483648.0f) return 2147483647;
+  if (r <= -2147483648.0f) return (int)(-2147483647 - 1);
+  return (int)r;
+}
+
 /* src/model/ternary.rs:31-57 */
 float fo_quantize_ternary(const float* w, size_t n, int8_t* q) {
   if (n == 0) return 0.0f;
@@ -193,7 +201,7 @@ float fo_quantize_ternary(const float* w, size_t n, int8_t* q) {
   float inv = 1.0f / alpha;
   for (size_t i = 0; i < n; ++i) {
     float r = roundf(w[i] * inv); /* f32::round: half away from zero */
-    int ri = (int)r;               /* `as i32` saturates; |r| is small here */
+    int ri = fo_as_i32(r);         /* `as i32` */
     q[i] = (int8_t)(ri < -1 ? -1 : ri > 1 ? 1 : ri);
   }
   return alpha;
@@ -265,6 +273,123 @@ void fo_ternary_matmul_decode(const int8_t* t, float scale, const float* x, size
     for (size_t j = chunks * 8; j < in_cols; ++j) sum += (float)w[j] * x[j];
     y[r] = scale * sum;
   }
+}
+
+/* src/model/ternary.rs:541-579: one scale per block of block_size columns,
+ * shared by every row; per block an fp32 block_sum of w * x, then
+ * sum += alpha * block_sum. */
+void fo_ternary_matmul_blocked(const int8_t* t, const float* scales, size_t block_size,
+                               const float* x, size_t out_rows, size_t in_cols, size_t seq,
+                               float* y) {
+  const size_t nb = (in_cols + block_size - 1) / block_size;
+  for (size_t s = 0; s < seq; ++s) {
+    const float* xr = x + s * in_cols;
+    for (size_t r = 0; r < out_rows; ++r) {
+      const int8_t* w = t + r * in_cols;
+      float sum = 0.0f;
+      for (size_t b = 0; b < nb; ++b) {
+        const size_t c0 = b * block_size;
+        size_t c1 = c0 + block_size;
+        if (c1 > in_cols) c1 = in_cols;
+        float block_sum = 0.0f;
+        for (size_t j = c0; j < c1; ++j) block_sum += (float)w[j] * xr[j];
+        sum += scales[b] * block_sum;
+      }
+      y[s * out_rows + r] = sum;
+    }
+  }
+}
+
+/* src/model/ternary.rs:76-110: flat blocks of block_size elements, absmean
+ * alpha per block (sequential f32 sum of |w|), round half away, clamp. */
+void fo_quantize_ternary_blocked(const float* w, size_t n, size_t block_size, int8_t* q,
+                                 float* scales) {
+  const float ABSMEAN_NORM = 0.7978845608f; /* ternary.rs:15 */
+  const size_t nb = (n + block_size - 1) / block_size;
+  for (size_t b = 0; b < nb; ++b) {
+    const size_t s0 = b * block_size;
+    size_t s1 = s0 + block_size;
+    if (s1 > n) s1 = n;
+    float sum_abs = 0.0f;
+    for (size_t i = s0; i < s1; ++i) sum_abs += fabsf(w[i]);
+    const float alpha = sum_abs > 0.0f ? (sum_abs / (float)(s1 - s0)) / ABSMEAN_NORM : 1.0f;
+    scales[b] = alpha;
+    const float inv = 1.0f / alpha;
+    for (size_t i = s0; i < s1; ++i) {
+      const int r = fo_as_i32(roundf(w[i] * inv));
+      q[i] = (int8_t)(r < -1 ? -1 : r > 1 ? 1 : r);
+    }
+  }
+}
+
+/* src/model/ternary.rs:681-707: per row, the columns holding +1 and -1, in
+ * column order.  Written as CSR: pos_off/neg_off [out_rows + 1], pos_idx /
+ * neg_idx (capacity out_rows * in_cols each). */
+void fo_ternary_sparse_indices(const int8_t* t, size_t out_rows, size_t in_cols, int64_t* pos_off,
+                               int64_t* pos_idx, int64_t* neg_off, int64_t* neg_idx) {
+  int64_t np = 0, nn = 0;
+  for (size_t r = 0; r < out_rows; ++r) {
+    pos_off[r] = np;
+    neg_off[r] = nn;
+    for (size_t j = 0; j < in_cols; ++j) {
+      if (t[r * in_cols + j] == 1) pos_idx[np++] = (int64_t)j;
+      else if (t[r * in_cols + j] == -1) neg_idx[nn++] = (int64_t)j;
+    }
+  }
+  pos_off[out_rows] = np;
+  neg_off[out_rows] = nn;
+}
+
+/* src/model/ternary.rs:647-672: sum += x[j] over the row's +1 list, then
+ * sum -= x[j] over its -1 list, y = scale * sum. */
+void fo_ternary_matmul_sparse_decode(const int64_t* pos_off, const int64_t* pos_idx,
+                                     const int64_t* neg_off, const int64_t* neg_idx, float scale,
+                                     const float* x, size_t out_rows, float* y) {
+  for (size_t r = 0; r < out_rows; ++r) {
+    float sum = 0.0f;
+    for (int64_t i = pos_off[r]; i < pos_off[r + 1]; ++i) sum += x[pos_idx[i]];
+    for (int64_t i = neg_off[r]; i < neg_off[r + 1]; ++i) sum -= x[neg_idx[i]];
+    y[r] = scale * sum;
+  }
+}
+
+/* src/training/bit_moe.rs:243-262 (ScaleSync::PerBlock): q = +1 if v / alpha > 0.5,
+ * -1 if < -0.5, else 0; all 0 when alpha < 1e-10.  v: bf16 bit patterns. */
+void fo_bitmoe_requantize(const uint16_t* shadow_bf16, size_t n, float alpha, int8_t* q) {
+  for (size_t i = 0; i < n; ++i) {
+    union {
+      uint32_t u;
+      float f;
+    } c;
+    c.u = (uint32_t)shadow_bf16[i] << 16;
+    if (alpha < 1e-10f) {
+      q[i] = 0;
+      continue;
+    }
+    const float nv = c.f / alpha;
+    q[i] = nv > 0.5f ? 1 : (nv < -0.5f ? -1 : 0);
+  }
+}
+
+/* src/training/bit_moe.rs:210-241: total_abs += |v| as f64 over every shadow in
+ * order, alpha = (total / count) as f32.  Returns 0 (alpha unchanged) when empty. */
+int fo_bitmoe_recompute_alpha(const uint16_t* const* shadows, const size_t* counts, size_t n,
+                              float* alpha) {
+  double total = 0.0;
+  size_t count = 0;
+  for (size_t b = 0; b < n; ++b)
+    for (size_t i = 0; i < counts[b]; ++i) {
+      union {
+        uint32_t u;
+        float f;
+      } c;
+      c.u = (uint32_t)shadows[b][i] << 16;
+      total += (double)fabsf(c.f);
+      ++count;
+    }
+  if (count == 0) return 0;
+  *alpha = (float)(total / (double)count);
+  return 1;
 }
 
 /* src/model/ternary.rs:471-529, per-row scales */

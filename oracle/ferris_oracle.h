@@ -47,6 +47,25 @@ void fo_ternary_matmul_packed(const uint8_t* packed, float scale, const float* x
 /* src/model/ternary.rs:591-633 (8-way unrolled sequential) */
 void fo_ternary_matmul_decode(const int8_t* t, float scale, const float* x, size_t out_rows,
                               size_t in_cols, float* y);
+/* src/model/ternary.rs:541-579 (one scale per column block, shared by the rows) */
+void fo_ternary_matmul_blocked(const int8_t* t, const float* scales, size_t block_size,
+                               const float* x, size_t out_rows, size_t in_cols, size_t seq,
+                               float* y);
+/* src/model/ternary.rs:76-110 (flat blocks of block_size elements) */
+void fo_quantize_ternary_blocked(const float* w, size_t n, size_t block_size, int8_t* q,
+                                 float* scales);
+/* src/model/ternary.rs:681-707 as CSR (offsets [out_rows + 1]) */
+void fo_ternary_sparse_indices(const int8_t* t, size_t out_rows, size_t in_cols, int64_t* pos_off,
+                               int64_t* pos_idx, int64_t* neg_off, int64_t* neg_idx);
+/* src/model/ternary.rs:647-672 */
+void fo_ternary_matmul_sparse_decode(const int64_t* pos_off, const int64_t* pos_idx,
+                                     const int64_t* neg_off, const int64_t* neg_idx, float scale,
+                                     const float* x, size_t out_rows, float* y);
+/* src/training/bit_moe.rs:243-262 (STE requantize with a shared alpha; bf16 shadows) */
+void fo_bitmoe_requantize(const uint16_t* shadow_bf16, size_t n, float alpha, int8_t* q);
+/* src/training/bit_moe.rs:210-241 (sequential f64 mean of |shadow|); 0 when empty */
+int fo_bitmoe_recompute_alpha(const uint16_t* const* shadows, const size_t* counts, size_t n,
+                              float* alpha);
 /* src/model/ternary.rs:471-529 restated with per-row scales (row_scales[r] in place of the
  * scalar, which is what gpu_packed() broadcasts, src/model/cpu_moe.rs:73-78).  Threads: the
  * reference's 32 row batches over `nthreads` workers (nthreads<=0: all cores). */

@@ -54,6 +54,12 @@ def _declare(L):
         "fo_ternary_matmul": (None, [_p, C.c_float, _p, _sz, _sz, _sz, _p]),
         "fo_ternary_matmul_packed": (None, [_p, C.c_float, _p, _sz, _sz, _sz, _p]),
         "fo_ternary_matmul_decode": (None, [_p, C.c_float, _p, _sz, _sz, _p]),
+        "fo_ternary_matmul_blocked": (None, [_p, _p, _sz, _p, _sz, _sz, _sz, _p]),
+        "fo_quantize_ternary_blocked": (None, [_p, _sz, _sz, _p, _p]),
+        "fo_ternary_sparse_indices": (None, [_p, _sz, _sz, _p, _p, _p, _p]),
+        "fo_ternary_matmul_sparse_decode": (None, [_p, _p, _p, _p, C.c_float, _p, _sz, _p]),
+        "fo_bitmoe_requantize": (None, [_p, _sz, C.c_float, _p]),
+        "fo_bitmoe_recompute_alpha": (C.c_int, [_p, _p, _sz, _p]),
         "fo_ternary_matmul_packed_parallel_rows": (None, [_p, _p, _p, _sz, _sz, _p, C.c_int]),
         "fo_gpu_ternary_mm_cpu": (None, [_p, _p, _p, _sz, _sz, _sz, _p]),
         "fo_ternary_matmul_parallel": (None, [_p, C.c_float, _p, _sz, _sz, _sz, _p, C.c_int]),
@@ -148,6 +154,65 @@ def ternary_matmul_decode(t, scale, x, out_rows, in_cols):
     y = np.zeros(out_rows, np.float32)
     lib().fo_ternary_matmul_decode(_ptr(t), float(scale), _ptr(x), out_rows, in_cols, _ptr(y))
     return y
+
+
+def ternary_matmul_blocked(t, scales, block_size, x, out_rows, in_cols, seq):
+    """src/model/ternary.rs:541-579."""
+    t, sc, x = _c(t, np.int8), _c(scales, np.float32), _c(x, np.float32)
+    y = np.zeros(seq * out_rows, np.float32)
+    lib().fo_ternary_matmul_blocked(_ptr(t), _ptr(sc), block_size, _ptr(x), out_rows, in_cols,
+                                    seq, _ptr(y))
+    return y
+
+
+def quantize_ternary_blocked(w, block_size):
+    """src/model/ternary.rs:76-110: (int8 values, per-block scales)."""
+    w = _c(w, np.float32)
+    q = np.zeros(w.size, np.int8)
+    sc = np.zeros((w.size + block_size - 1) // block_size, np.float32)
+    if w.size:
+        lib().fo_quantize_ternary_blocked(_ptr(w), w.size, block_size, _ptr(q), _ptr(sc))
+    return q, sc
+
+
+def ternary_sparse_indices(t, out_rows, in_cols):
+    """src/model/ternary.rs:681-707 as CSR: (pos_off, pos_idx, neg_off, neg_idx)."""
+    t = _c(t, np.int8)
+    po, no = np.zeros(out_rows + 1, np.int64), np.zeros(out_rows + 1, np.int64)
+    pi, ni = np.zeros(max(1, t.size), np.int64), np.zeros(max(1, t.size), np.int64)
+    lib().fo_ternary_sparse_indices(_ptr(t), out_rows, in_cols, _ptr(po), _ptr(pi), _ptr(no),
+                                    _ptr(ni))
+    return po, pi[:po[-1]].copy(), no, ni[:no[-1]].copy()
+
+
+def ternary_matmul_sparse_decode(pos_off, pos_idx, neg_off, neg_idx, scale, x, out_rows):
+    """src/model/ternary.rs:647-672."""
+    po, no = _c(pos_off, np.int64), _c(neg_off, np.int64)
+    pi = _c(pos_idx if len(pos_idx) else np.zeros(1, np.int64), np.int64)
+    ni = _c(neg_idx if len(neg_idx) else np.zeros(1, np.int64), np.int64)
+    x = _c(x, np.float32)
+    y = np.zeros(out_rows, np.float32)
+    lib().fo_ternary_matmul_sparse_decode(_ptr(po), _ptr(pi), _ptr(no), _ptr(ni), float(scale),
+                                          _ptr(x), out_rows, _ptr(y))
+    return y
+
+
+def bitmoe_requantize(shadow_bf16_bits, alpha):
+    """src/training/bit_moe.rs:243-262 on bf16 bit patterns (uint16)."""
+    sh = _c(shadow_bf16_bits, np.uint16)
+    q = np.zeros(sh.size, np.int8)
+    lib().fo_bitmoe_requantize(_ptr(sh), sh.size, float(alpha), _ptr(q))
+    return q
+
+
+def bitmoe_recompute_alpha(shadows_bf16_bits):
+    """src/training/bit_moe.rs:210-241; None when there is no element."""
+    arrs = [_c(a, np.uint16) for a in shadows_bf16_bits]
+    ptrs = (C.c_void_p * max(1, len(arrs)))(*[a.ctypes.data for a in arrs])
+    cnt = (C.c_size_t * max(1, len(arrs)))(*[a.size for a in arrs])
+    out = C.c_float(0.0)
+    ok = lib().fo_bitmoe_recompute_alpha(ptrs, cnt, len(arrs), C.byref(out))
+    return np.float32(out.value) if ok else None
 
 
 def ternary_matmul_packed_parallel_rows(packed, row_scales, x, out_rows, in_cols, nthreads=0):

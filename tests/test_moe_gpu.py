@@ -149,3 +149,52 @@ def test_moe_host_forward_and_stages(moe_mod):
     assert L.ft_moe_combine(ctx.handle, layer.handle, T, p(o), p(slot_of), p(w), p(y), st) == 0
     assert torch.equal(y.cpu(), torch.from_numpy(y_host).view(T, H))
     ctx.check()
+
+
+@pytest.mark.parametrize("T,bf16_x", [(1, True), (4, True), (8, True), (3, False)])
+def test_moe_decode_fused(moe_mod, T, bf16_x):
+    """The fused decode step (ft_moe_decode: one cooperative launch, no host sync)
+    against the oracle's TernaryMoELayer::forward at the cfg4 layer shape."""
+    rng = np.random.default_rng(50 + T)
+    E, H, F, K = 64, 2048, 1408, 2
+    router, g, gs, u, us, d, ds = make_layer(rng, E, H, F)
+    layer = moe_mod.TernaryMoELayer.from_ternary(router, g, gs, u, us, d, ds, H, F, K)
+    x = rng.standard_normal((T, H)).astype(np.float32)
+    xt = torch.from_numpy(x).cuda()
+    if bf16_x:
+        xt = xt.to(torch.bfloat16)
+        x = xt.float().cpu().numpy()
+    y, idx, w, p = layer.decode_device(xt, probs=True)
+    torch.cuda.synchronize()
+    layer.ctx.check()  # no barrier wait gave up
+    ref_y, ref_route, ref_probs = fo.moe_forward(router, g, gs, u, us, d, ds, H, F, K, x.ravel(), T)
+    check(y.cpu().numpy(), idx.cpu().numpy(), p.cpu().numpy(), ref_y, ref_route, ref_probs, T, H,
+          K, E)
+    # the gates are the renormalised top-k probabilities
+    pr = p.cpu().numpy()
+    sel = idx.cpu().numpy()
+    top = np.take_along_axis(pr, sel, axis=1)
+    assert np.allclose(w.cpu().numpy(), top / top.sum(axis=1, keepdims=True), rtol=1e-6, atol=1e-7)
+
+
+def test_moe_decode_small_gelu_top3(moe_mod):
+    rng = np.random.default_rng(60)
+    E, H, F, K, T = 5, 200, 132, 3, 5
+    router, g, gs, u, us, d, ds = make_layer(rng, E, H, F)
+    layer = moe_mod.TernaryMoELayer.from_ternary(router, g, gs, u, us, d, ds, H, F, K, True)
+    x = rng.standard_normal((T, H)).astype(np.float32)
+    y, idx, w, p = layer.decode_device(torch.from_numpy(x).cuda(), probs=True)
+    torch.cuda.synchronize()
+    ref_y, ref_route, ref_probs = fo.moe_forward(router, g, gs, u, us, d, ds, H, F, K, x.ravel(), T,
+                                                 use_gelu=True)
+    check(y.cpu().numpy(), idx.cpu().numpy(), p.cpu().numpy(), ref_y, ref_route, ref_probs, T, H,
+          K, E)
+
+
+def test_moe_decode_rejects_unsupported(moe_mod):
+    from ferrisres_b200._lib import UnsupportedError
+    rng = np.random.default_rng(61)
+    router, g, gs, u, us, d, ds = make_layer(rng, 8, 256, 128)
+    layer = moe_mod.TernaryMoELayer.from_ternary(router, g, gs, u, us, d, ds, 256, 128, 2)
+    with pytest.raises(UnsupportedError):
+        layer.decode_device(torch.zeros(9, 256, device="cuda"))  # more than 8 tokens

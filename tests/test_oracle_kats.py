@@ -427,3 +427,102 @@ def test_quantize_absmax_i8_edges():
     assert sx[1] == np.float32(2.0) / np.float32(127.0)
     assert list(q[4:8]) == [64, -127, 32, 0]  # 63.5 rounds half away from zero
     assert list(q[8:12]) == [127, -127, 1, 2]
+
+
+# ------------------------------------ block scales and index lists (A7, (f)4)
+def _cosine(a, b):
+    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    return float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b)))
+
+
+def test_blocked_quantize_roundtrip():  # ternary.rs:824-843
+    w = np.sin(np.arange(1000, dtype=np.float32) * np.float32(0.01) - np.float32(5.0))
+    q, s = fo.quantize_ternary_blocked(w, 128)
+    assert s.size == 8
+    r = np.repeat(s, 128)[:1000] * q.astype(np.float32)
+    assert _cosine(w, r) > 0.90
+
+
+def test_blocked_vs_per_tensor():  # ternary.rs:846-873
+    i = np.arange(512, dtype=np.float32)
+    w = np.where(i < 256, i * np.float32(0.001) - np.float32(0.128),
+                 i * np.float32(0.01) - np.float32(2.56)).astype(np.float32)
+    qt, st = fo.quantize_ternary(w)
+    qb, sb = fo.quantize_ternary_blocked(w, 64)
+    cos_t = _cosine(w, qt.astype(np.float32) * st)
+    cos_b = _cosine(w, np.repeat(sb, 64) * qb.astype(np.float32))
+    assert cos_b >= cos_t - 0.01
+
+
+def blocked_kat_case():
+    """The inputs of ternary.rs:1098-1176 (test_ternary_matmul_blocked_vs_scalar)."""
+    out_rows, in_cols, bs = 4, 32, 8
+    w = (np.sin(np.arange(out_rows * in_cols, dtype=np.float32) * np.float32(1.618))
+         * np.float32(0.5)).astype(np.float32).reshape(out_rows, in_cols)
+    nb = in_cols // bs
+    scales = np.zeros(nb, np.float32)
+    norm = np.float32(0.7978845608)
+    for b in range(nb):
+        s = np.float32(0.0)
+        for r in range(out_rows):  # rows outer, columns inner: the reference's loop order
+            for j in range(b * bs, (b + 1) * bs):
+                s = np.float32(s + abs(w[r, j]))
+        scales[b] = np.float32(np.float32(s / np.float32(out_rows * bs)) / norm) if s > 0 else 1
+    t = np.zeros((out_rows, in_cols), np.int8)
+    for b in range(nb):
+        inv = np.float32(np.float32(1.0) / scales[b])
+        v = (w[:, b * bs:(b + 1) * bs] * inv).astype(np.float32)
+        t[:, b * bs:(b + 1) * bs] = np.clip(np.trunc(v + np.copysign(np.float32(0.5), v)), -1, 1)
+    x = np.cos(np.arange(in_cols, dtype=np.float32) * np.float32(0.1)).astype(np.float32)
+    ref = np.zeros(out_rows, np.float32)
+    for r in range(out_rows):
+        for b in range(nb):
+            for j in range(b * bs, (b + 1) * bs):
+                ref[r] = np.float32(ref[r] + np.float32(scales[b] * np.float32(t[r, j])) * x[j])
+    return t.ravel(), scales, bs, x, out_rows, in_cols, ref
+
+
+def test_ternary_matmul_blocked_vs_scalar():  # ternary.rs:1098-1176
+    t, scales, bs, x, rows, cols, ref = blocked_kat_case()
+    y = fo.ternary_matmul_blocked(t, scales, bs, x, rows, cols, 1)
+    assert np.abs(y - ref).max() < 1e-4
+
+
+def test_ternary_sparse_decode_vs_general():  # ternary.rs:1208-1235
+    rows, cols, scale = 4, 16, 0.5
+    i = np.arange(rows * cols)
+    t = np.where(i % 3 == 0, 1, np.where(i % 3 == 1, -1, 0)).astype(np.int8)
+    x = (np.arange(cols, dtype=np.float32) * np.float32(0.1)).astype(np.float32)
+    po, pi, no, ni = fo.ternary_sparse_indices(t, rows, cols)
+    y = fo.ternary_matmul_sparse_decode(po, pi, no, ni, scale, x, rows)
+    g = fo.ternary_matmul_decode(t, scale, x, rows, cols)
+    assert np.abs(y - g).max() < 1e-5
+
+
+def test_sparse_indices_counts():  # ternary.rs:1238-1253
+    t = np.array([1, -1, 0, 1, -1, 0, 0, -1, 0, 0, 0, 0], np.int8)
+    po, pi, no, ni = fo.ternary_sparse_indices(t, 3, 4)
+    assert list(pi[po[0]:po[1]]) == [0, 3] and list(ni[no[0]:no[1]]) == [1]
+    assert list(pi[po[1]:po[2]]) == [] and list(ni[no[1]:no[2]]) == [0, 3]
+    assert list(pi[po[2]:po[3]]) == [] and list(ni[no[2]:no[3]]) == []
+
+
+def test_bitmoe_synchronized_alpha_and_requantize():  # bit_moe.rs:319-386
+    # make_test_bit_moe: hidden 4, inter 8, 2 experts, weights sin((i + base) * 0.1);
+    # init_shadows_from_ternary then recompute_alpha; requantize with that alpha.
+    import torch
+    hd, idim, ne = 4, 8, 2
+    mats = []
+    for e in range(ne):
+        for base, size in ((e, idim * hd), (e + 0.5, idim * hd), (e + 1.0, hd * idim)):
+            w = np.sin((np.arange(size, dtype=np.float32) + np.float32(base)) * np.float32(0.1))
+            q, a = fo.quantize_ternary(w.astype(np.float32))
+            shadow = torch.from_numpy(q.astype(np.float32) * a).to(torch.bfloat16)
+            mats.append(shadow.view(torch.int16).numpy().view(np.uint16))
+    alpha = fo.bitmoe_recompute_alpha(mats)
+    assert alpha is not None and alpha > 0
+    for m in mats:
+        q = fo.bitmoe_requantize(m, alpha)
+        assert set(np.unique(q)) <= {-1, 0, 1}
+    assert fo.bitmoe_recompute_alpha([]) is None
+    assert (fo.bitmoe_requantize(mats[0], 0.0) == 0).all()  # alpha < 1e-10 -> all zero
