@@ -761,7 +761,6 @@ def run_moe(args, torch, dist, device, ws, rank, local, sub_steps, cpu_seconds):
                             y[:M_SAMPLE].cpu().numpy(), router)
     if ws > 1:
         dist.barrier()
-    layer.close()
     res = {
         "metric": "MoE-layer tokens/s", "value": round(M_T / sec, 1), "unit": "tokens/s",
         "n_gpus": ws, "steps": sub_steps, "ms_per_step": sec * 1e3, "scaling": "strong",
@@ -776,9 +775,58 @@ def run_moe(args, torch, dist, device, ws, rank, local, sub_steps, cpu_seconds):
         "parity": parity,
         "clocks": clocks,
     }
+    if ws == 1:
+        res["decode"] = moe_decode_times(torch, layer, x, stream, timer)
+    layer.close()
     if rank == 0 and ws == 1 and cpu_seconds > 0:
         res["cpu_baseline"] = moe_cpu_baseline(cpu_seconds, router)
     return res
+
+
+def moe_decode_times(torch, layer, x, stream, timer):
+    """Decode steps of the same layer: the fused single-launch ft_moe_decode at
+    T = 1, 4, 8 tokens (replayed from a CUDA graph: the step has no host
+    synchronisation), against the general ft_moe_forward at T = 1 (which reads
+    the per-expert counts back to size its launches)."""
+    out = {}
+    reps = 50
+    for T in (1, 4, 8):
+        xt = x[:T].contiguous()
+        with torch.cuda.stream(stream):
+            layer.decode_device(xt)  # sizes the scratch before capture
+        stream.synchronize()
+        try:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for _ in range(reps):
+                    layer.decode_device(xt)
+            with torch.cuda.stream(stream):
+                g.replay()
+            sec = timer(g.replay) / reps
+            out["graph"] = True
+            del g
+        except Exception as e:  # capture refused: time direct launches instead
+            out["graph"] = f"not captured ({type(e).__name__})"
+            torch.cuda.synchronize()
+
+            def direct():
+                for _ in range(reps):
+                    layer.decode_device(xt)
+            sec = timer(direct) / reps
+        out[f"T{T}_us"] = round(sec * 1e6, 2)
+        out[f"T{T}_us_per_token"] = round(sec * 1e6 / T, 2)
+    x1 = x[:1].contiguous()
+
+    def fwd():
+        for _ in range(reps):
+            layer.forward_device(x1)
+    with torch.cuda.stream(stream):
+        fwd()
+    out["forward_T1_us"] = round(timer(fwd) / reps * 1e6, 2)
+    out["note"] = ("ft_moe_decode: router, top-2, gate/up, SwiGLU, down and combine in one "
+                   "cooperative launch; forward_T1: the general layer (route, layout, gather, host "
+                   "read of the counts, grouped expert GEMMs, combine)")
+    return out
 
 
 def moe_cpu_baseline(seconds, router):
@@ -877,6 +925,7 @@ def run_kv(args, torch, dist, device, local, sub_steps, cpu_seconds):
     peak, _, kind = load_peaks()
     dec_gbs = KV_ALGO_BYTES / dec_s / 1e9
     cache.close()
+    mode_t = kv_mode_t_times(torch, kv, device, local, timer, stream, q, out, k1, v1, sub_steps)
     res = {
         "metric": "3-bit KV flash-decode HBM GB/s", "value": round(value, 2), "unit": "GB/s",
         "steps": sub_steps, "ms_per_step": step_s * 1e3, "dtype": "u8 codes / f32",
@@ -897,10 +946,45 @@ def run_kv(args, torch, dist, device, local, sub_steps, cpu_seconds):
                 "api": "Kv3Cache.append + flash_decode (ft_kv3_append, ft_flash_decode_3bit)"},
         "gpu_launches": int(gpu_launches),
         "clocks": clocks,
+        "mode_t": mode_t,
     }
     if cpu_seconds > 0:
         res["cpu_baseline"] = kv_cpu_baseline(cpu_seconds)
     return res
+
+
+def kv_mode_t_times(torch, kv, device, local, timer, stream, q, out, k1, v1, sub_steps):
+    """The same step and decode over a mode-T cache (rotation + uniform 3-bit
+    codebook + norm): same stored bytes per position, plus the q and output
+    rotations."""
+    cache = kv.Kv3Cache(KV_B, KV_HKV, KV_S + 64, device=local, mode="T", seed=1)
+    gen = torch.Generator(device=device).manual_seed(6)
+    chunk = 4096
+    for _ in range(KV_S // chunk):
+        kk = torch.randn((KV_B, chunk, KV_HKV, KV_D), device=device, generator=gen).to(torch.bfloat16)
+        vv = torch.randn((KV_B, chunk, KV_HKV, KV_D), device=device, generator=gen).to(torch.bfloat16)
+        cache.append(kk, vv)
+        del kk, vv
+
+    def step():
+        cache.append(k1, v1, stream=stream)
+        cache.evict_front(1)
+        cache.flash_decode(q, out=out, stream=stream)
+
+    for _ in range(3):
+        step()
+    stream.synchronize()
+    step_s = timer(lambda: [step() for _ in range(sub_steps)]) / sub_steps
+    dec_s = timer(lambda: [cache.flash_decode(q, out=out, stream=stream)
+                           for _ in range(sub_steps)]) / sub_steps
+    cache.ctx.check()
+    cache.close()
+    peak, _, _ = load_peaks()
+    gbs = KV_ALGO_BYTES / dec_s / 1e9
+    return {"ms_per_step": step_s * 1e3, "value": round(KV_ALGO_BYTES / step_s / 1e9, 2),
+            "decode_us": round(dec_s * 1e6, 2), "decode_gbs": round(gbs, 2),
+            "decode_frac": round(gbs / peak, 4),
+            "decode_tokens_per_s": round(KV_B / step_s, 1)}
 
 
 def kv_cpu_baseline(seconds):

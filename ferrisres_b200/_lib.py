@@ -100,6 +100,8 @@ SIGNATURES = {
     "ft_moe_expert_ffn": [_p, _p, _i, _p, _p, _p, _i, _p, _p],
     "ft_moe_combine": [_p, _p, _i64, _p, _p, _p, _p, _p],
     "ft_kv3_create": [_p, _i64, _i64, _i64, _i64, _p],
+    "ft_kv3_create_mode": [_p, _i64, _i64, _i64, _i64, _i, C.c_uint64, _p],
+    "ft_kv3_signs": [_p, _p],
     "ft_kv3_destroy": [_p],
     "ft_kv3_append": [_p, _p, _i64, _p, _p, _i, _p],
     "ft_kv3_append_packed": [_p, _p, _i64, _p, _p, _p, _p, _p],

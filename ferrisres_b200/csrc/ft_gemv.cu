@@ -54,7 +54,7 @@ namespace {
 #define FT_GV_MB1 4
 #endif
 #ifndef FT_GV_DEPTH1
-#define FT_GV_DEPTH1 3
+#define FT_GV_DEPTH1 5
 #endif
 // launches of <= 4 problems, one n8 block: units of 2 m-blocks, so a single
 // GEMV spreads over more warps

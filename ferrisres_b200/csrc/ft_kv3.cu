@@ -48,8 +48,21 @@
 // when the running max or the scale 2^E changes, and at the end.  The
 // min * p term is a per-head scalar added to every dim.  Each split writes
 // (m, l, numerator) partials; a combine kernel merges the splits.
+//
+// Mode T (ft_kv3_create_mode with mode 1; no working reference implementation,
+// so parity is against this project's own oracle): each vector v is stored
+// rotated, y = H D v / ||v|| (D = seeded +-1 signs, H the 128-point
+// Walsh-Hadamard transform), coded as code = clamp(floor((y / 2.5 + 1) * 4), 0, 7)
+// -- the nearest of the 8 uniform centroids (2i+1)/8 - 1 on [-1, 1] of y/2.5,
+// the levels the reference's compute_mse_centroids (src/compute/turboquant.rs:
+// 197-220) converges to -- and (min, max) = (-m, +m), m = ||v|| * 2.5 * 7/8 /
+// sqrt(128).  In the rotated domain the vector is then affine in the code, so
+// the same record and the same decode serve both modes: decode rotates q with
+// H D / sqrt(128), and the split combine rotates the output back with
+// D H / sqrt(128).
 #include <cmath>
 #include <cstring>
+#include <vector>
 
 #include "ft_internal.cuh"
 #include "ft_tc.cuh"
@@ -60,6 +73,9 @@ struct ft_kv3 {
   int64_t head = 0, len = 0;                   // ring start slot, live positions
   uint32_t* blocks = nullptr;  // [row][cap/32] block records
   ft::Workspace part;  // split partials
+  int mode = 0;                // 0: the reference's min/max scheme, 1: mode T
+  float* signs = nullptr;      // mode T: the 128 rotation signs (device)
+  ft::Workspace rot;           // mode T: the rotated queries
 };
 
 namespace ft {
@@ -151,7 +167,48 @@ struct AppendParams {
   int bf16;
   int64_t n_pos, Hkv, cap, nbc, s0;
   uint32_t* blocks;
+  const float* signs;  // mode T rotation signs, or null (the reference's scheme)
 };
+
+// Mode T constants: clip at 2.5 and the (min, max) factor 2.5 * 7/8 / sqrt(128).
+constexpr float kTClip = 2.5f;
+__device__ __forceinline__ float kvt_mm_const() {
+  return __fdiv_rn(__fdiv_rn(__fmul_rn(kTClip, 7.0f), 8.0f), __fsqrt_rn(128.0f));
+}
+
+// In-place 128-point Walsh-Hadamard transform of y (shared), thread d = one
+// element, butterflies h = 1, 2, ..., 64: y[j] = a + b, y[j + h] = a - b.
+// Block-wide (128 threads).
+__device__ __forceinline__ void fwht128(float* y, int d) {
+  __syncthreads();  // the callers' writes of y are visible
+#pragma unroll
+  for (int h = 1; h < kD; h <<= 1) {
+    const float a = y[d & ~h], b = y[d | h];
+    __syncthreads();
+    y[d] = (d & h) ? __fsub_rn(a, b) : __fadd_rn(a, b);
+    __syncthreads();
+  }
+}
+
+// Mode T code of element d of vector x (block-wide: every thread passes its
+// element); returns the code and the vector's norm.
+__device__ __forceinline__ uint32_t kvt_code(float x, float sign, int d, float* ybuf,
+                                             float (*red)[4], int slot, float* norm_out) {
+  const int warp = d >> 5, lane = d & 31;
+  float sq = __fmul_rn(x, x);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sq = __fadd_rn(sq, __shfl_xor_sync(0xffffffffu, sq, o));
+  if (lane == 0) red[warp][slot] = sq;
+  __syncthreads();
+  const float n2 = __fadd_rn(__fadd_rn(__fadd_rn(red[0][slot], red[1][slot]), red[2][slot]),
+                             red[3][slot]);
+  const float norm = __fsqrt_rn(n2);
+  ybuf[d] = norm > 0.0f ? __fmul_rn(__fdiv_rn(x, norm), sign) : 0.0f;
+  fwht128(ybuf, d);
+  const float c = floorf(__fmul_rn(__fadd_rn(__fdiv_rn(ybuf[d], kTClip), 1.0f), 4.0f));
+  *norm_out = norm;
+  return c <= 0.0f ? 0u : (c >= 7.0f ? 7u : (uint32_t)c);
+}
 
 // code idx of a reference LSB-first 3-bit stream (the next byte is read only
 // when the code straddles it)
@@ -178,6 +235,7 @@ __global__ void __launch_bounds__(kD) kv3_append_kernel(AppendParams p) {
   const int u_end = u_end64 > kBlk ? kBlk : (int)u_end64;
   __shared__ float red[4][4];
   __shared__ uint32_t kw[kBlkWords], vw[kBlkWords];
+  __shared__ float ybk[kD], ybv[kD];
   uint32_t* kg = p.blocks + (row * p.nbc + pb) * kRecWords;
   uint32_t* vg = kg + kRecV;
   float2* kmm = reinterpret_cast<float2*>(kg + kRecKmm);
@@ -202,6 +260,19 @@ __global__ void __launch_bounds__(kD) kv3_append_kernel(AppendParams p) {
       kmax = p.kmm_in[vec * 2 + 1];
       vmin = p.vmm_in[vec * 2];
       vmax = p.vmm_in[vec * 2 + 1];
+    } else if (p.signs) {
+      // mode T: norm, signs, Walsh-Hadamard, uniform codebook
+      const float xk = load_act(p.k, vec * kD + d, p.bf16);
+      const float xv = load_act(p.v, vec * kD + d, p.bf16);
+      const float sg = p.signs[d];
+      float nk, nv;
+      ck = kvt_code(xk, sg, d, ybk, red, 0, &nk);
+      cv = kvt_code(xv, sg, d, ybv, red, 1, &nv);
+      const float C = kvt_mm_const();
+      kmax = __fmul_rn(C, nk);
+      kmin = -kmax;
+      vmax = __fmul_rn(C, nv);
+      vmin = -vmax;
     } else {
       const float xk = load_act(p.k, vec * kD + d, p.bf16);
       const float xv = load_act(p.v, vec * kD + d, p.bf16);
@@ -257,8 +328,10 @@ struct RangeParams {
 
 // get_range (turboquant_kv.rs:271-291): out [B][n][Hkv][128] f32, dequantised
 // with the reference's roundings (dequantize_3bit :110-117).
+// Mode T (signs != null): the rotated-domain values are rotated back,
+// v = D H y / sqrt(128).
 __global__ void kv3_dequant_kernel(RangeParams p, float* __restrict__ kout,
-                                   float* __restrict__ vout) {
+                                   float* __restrict__ vout, const float* __restrict__ signs) {
   const int64_t vec = blockIdx.x;  // (b, pos, h)
   const int d = threadIdx.x;
   const int64_t h = vec % p.Hkv;
@@ -284,8 +357,32 @@ __global__ void kv3_dequant_kernel(RangeParams p, float* __restrict__ kout,
   } else {
     vv = __fadd_rn(vm.x, __fmul_rn((float)cv, __fdiv_rn(__fsub_rn(vm.y, vm.x), 7.0f)));
   }
+  if (signs) {
+    __shared__ float yk[kD], yv[kD];
+    yk[d] = kv;
+    yv[d] = vv;
+    fwht128(yk, d);
+    fwht128(yv, d);
+    const float sc = __fdiv_rn(1.0f, __fsqrt_rn(128.0f));
+    kv = __fmul_rn(__fmul_rn(yk[d], sc), signs[d]);
+    vv = __fmul_rn(__fmul_rn(yv[d], sc), signs[d]);
+  }
   kout[vec * kD + d] = kv;
   vout[vec * kD + d] = vv;
+}
+
+// Mode T rotation of 128-vectors (one CTA each): out = H D in / sqrt(128)
+// (forward) or D H in / sqrt(128) (inverse).
+__global__ void kv3_rotate_kernel(const float* __restrict__ in, float* __restrict__ out,
+                                  const float* __restrict__ signs, int inverse) {
+  __shared__ float y[kD];
+  const int64_t v = blockIdx.x;
+  const int d = threadIdx.x;
+  const float x = in[v * kD + d];
+  y[d] = inverse ? x : __fmul_rn(x, signs[d]);
+  fwht128(y, d);
+  const float sc = __fdiv_rn(1.0f, __fsqrt_rn(128.0f));
+  out[v * kD + d] = inverse ? __fmul_rn(__fmul_rn(y[d], sc), signs[d]) : __fmul_rn(y[d], sc);
 }
 
 // The reference's stored form: codes [B][n][Hkv*48] bytes (pack_3bit over the
@@ -761,8 +858,9 @@ __global__ void __launch_bounds__((kDecWarps + 1) * 32, FT_KV_MIN_BLOCKS)
 }
 
 // Merges the split partials of one (sequence, q head): thread = dim.
+// Mode T (signs != null): the rotated-domain output is rotated back.
 __global__ void kv3_combine_kernel(const float* __restrict__ part, int nsplit,
-                                   float* __restrict__ out) {
+                                   float* __restrict__ out, const float* __restrict__ signs) {
   const int64_t bh = blockIdx.x;
   const int d = threadIdx.x;
   const float* pp = part + bh * nsplit * kPart;
@@ -776,7 +874,14 @@ __global__ void kv3_combine_kernel(const float* __restrict__ part, int nsplit,
     l = fmaf(pp[s * kPart + 1], f, l);
     a = fmaf(pp[s * kPart + 2 + d], f, a);
   }
-  out[bh * kD + d] = a / l;
+  float r = a / l;
+  if (signs) {
+    __shared__ float y[kD];
+    y[d] = r;
+    fwht128(y, d);
+    r = __fmul_rn(__fmul_rn(y[d], __fdiv_rn(1.0f, __fsqrt_rn(128.0f))), signs[d]);
+  }
+  out[bh * kD + d] = r;
 }
 
 // Opts the decode kernel into its dynamic shared memory (once per device) and
@@ -869,6 +974,7 @@ int append_common(ft_kv3* c, int64_t n_pos, const AppendParams& proto, bool pack
   p.nbc = c->cap / kBlk;
   p.s0 = (c->head + c->len) % c->cap;
   p.blocks = c->blocks;
+  p.signs = packed ? nullptr : c->signs;
   const int64_t nblk = (p.s0 % kBlk + n_pos + kBlk - 1) / kBlk;
   // a block is touched by one CTA only: the new slots never wrap onto a block
   // that an earlier CTA of this launch also writes
@@ -930,12 +1036,51 @@ int ft_kv3_create(ft_ctx* ctx, int64_t batch, int64_t kv_heads, int64_t head_dim
   return FT_OK;
 }
 
+int ft_kv3_create_mode(ft_ctx* ctx, int64_t batch, int64_t kv_heads, int64_t head_dim,
+                       int64_t max_seq, int mode, uint64_t seed, ft_kv3** out) {
+  FT_CHECK(mode == 0 || mode == 1, FT_ERR_UNSUPPORTED, "mode must be 0 (reference) or 1 (T)");
+  int st = ft_kv3_create(ctx, batch, kv_heads, head_dim, max_seq, out);
+  if (st != FT_OK || mode == 0) return st;
+  ft_kv3* c = *out;
+  // the 128 signs from SplitMix64(seed): bit 63 of each draw set -> -1
+  std::vector<float> sg(kD);
+  uint64_t z = seed;
+  for (int i = 0; i < kD; ++i) {
+    z += 0x9e3779b97f4a7c15ull;
+    uint64_t r = z;
+    r = (r ^ (r >> 30)) * 0xbf58476d1ce4e5b9ull;
+    r = (r ^ (r >> 27)) * 0x94d049bb133111ebull;
+    r ^= r >> 31;
+    sg[i] = (r >> 63) ? -1.0f : 1.0f;
+  }
+  DeviceScope scope(c->device);
+  cudaError_t e = cudaMalloc(&c->signs, kD * sizeof(float));
+  if (e == cudaSuccess) e = cudaMemcpy(c->signs, sg.data(), kD * sizeof(float), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    ft_kv3_destroy(c);
+    *out = nullptr;
+    return fail(FT_ERR_GPU, "mode T setup failed: %s", cudaGetErrorString(e));
+  }
+  c->mode = 1;
+  return FT_OK;
+}
+
+int ft_kv3_signs(const ft_kv3* c, float* signs_host) {
+  FT_CHECK(c && signs_host, FT_ERR_SHAPE, "null argument");
+  FT_CHECK(c->signs, FT_ERR_UNSUPPORTED, "the cache is not in mode T");
+  DeviceScope scope(c->device);
+  FT_CUDA(cudaMemcpy(signs_host, c->signs, kD * sizeof(float), cudaMemcpyDeviceToHost));
+  return FT_OK;
+}
+
 int ft_kv3_destroy(ft_kv3* c) {
   if (!c) return FT_OK;
   DeviceScope scope(c->device);
   cudaDeviceSynchronize();
   cudaFree(c->blocks);
   if (c->part.ptr) cudaFree(c->part.ptr);
+  if (c->signs) cudaFree(c->signs);
+  if (c->rot.ptr) cudaFree(c->rot.ptr);
   delete c;
   return FT_OK;
 }
@@ -1005,7 +1150,7 @@ int ft_kv3_get_range(ft_ctx* ctx, const ft_kv3* c, int64_t start, int64_t end, f
   DeviceScope scope(c->device);
   kv3_dequant_kernel<<<(unsigned)(c->batch * n * c->kv_heads), kD, 0,
                        static_cast<cudaStream_t>(stream)>>>(range_params(c, start, n), k_out_dev,
-                                                            v_out_dev);
+                                                            v_out_dev, c->signs);
   FT_LAUNCH_CHECK();
   return FT_OK;
 }
@@ -1042,6 +1187,28 @@ int ft_flash_decode_3bit(ft_ctx* ctx, ft_kv3* c, const float* q_dev, int64_t q_h
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   DecodeParams p{};
   p.q = q_dev;
+  if (c->signs) {
+    // mode T: attention runs in the rotated domain
+    const size_t qb = (size_t)(c->batch * q_heads * kD) * 4;
+    if (c->rot.bytes < qb) {
+      cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+      if (s) cudaStreamIsCapturing(s, &cs);
+      FT_CHECK(cs == cudaStreamCaptureStatusNone, FT_ERR_UNSUPPORTED,
+               "the rotated-query buffer must grow but the stream is being captured");
+      if (c->rot.ptr) {
+        FT_CUDA(cudaStreamSynchronize(s));
+        FT_CUDA(cudaFree(c->rot.ptr));
+        c->rot.ptr = nullptr;
+        c->rot.bytes = 0;
+      }
+      FT_CUDA(cudaMalloc(&c->rot.ptr, qb));
+      c->rot.bytes = qb;
+    }
+    kv3_rotate_kernel<<<(unsigned)(c->batch * q_heads), kD, 0, s>>>(
+        q_dev, static_cast<float*>(c->rot.ptr), c->signs, 0);
+    FT_LAUNCH_CHECK();
+    p.q = static_cast<const float*>(c->rot.ptr);
+  }
   p.Hq = q_heads;
   p.Hkv = c->kv_heads;
   p.G = (int)(q_heads / c->kv_heads);
@@ -1097,7 +1264,8 @@ int ft_flash_decode_3bit(ft_ctx* ctx, ft_kv3* c, const float* q_dev, int64_t q_h
   dim3 grid((unsigned)nsplit, (unsigned)(c->kv_heads * p.hgroups), (unsigned)c->batch);
   kv3_decode_kernel<<<grid, (kDecWarps + 1) * 32, kDecSmem, s>>>(p);
   FT_LAUNCH_CHECK();
-  kv3_combine_kernel<<<(unsigned)(c->batch * q_heads), kD, 0, s>>>(p.part, (int)nsplit, out_dev);
+  kv3_combine_kernel<<<(unsigned)(c->batch * q_heads), kD, 0, s>>>(p.part, (int)nsplit, out_dev,
+                                                                     c->signs);
   FT_LAUNCH_CHECK();
   return FT_OK;
 }

@@ -154,11 +154,12 @@ __device__ __forceinline__ void route_token(float* s, int E, int K, int64_t t,
 // mma.sync m16n8k16 accumulates them in fp32 over the plane pairs (i, j) with
 // i + j <= 2 (the dropped pairs weigh below 2^-24 of the product), each 64-K
 // chunk in its own fp32 MMA chain, the chunks summed in f64: the scores come
-// out closer to the exact dot than the reference's sequential fp32 sum is.  Block:
-// 32 tokens x 64 experts, 4 warps (16 tokens x 32 experts each), K in chunks
-// of 64 staged in shared memory (rows padded to 72 bf16: conflict-free
-// fragment loads).  Then one thread per token routes it.
-constexpr int kRtTok = 32, kRtK = 64, kRtPad = 72, kRtThreads = 128;
+// out closer to the exact dot than the reference's sequential fp32 sum is.
+// Block: 16 tokens x 64 experts, 4 warps (16 experts each); K in chunks of 64
+// staged in shared memory (rows padded to 72 bf16: conflict-free fragment
+// loads), the next chunk prefetched into registers while the tensor cores work
+// on the current one.  Then one thread per token routes it.
+constexpr int kRtTok = 16, kRtK = 64, kRtPad = 72, kRtThreads = 128;
 
 __device__ __forceinline__ uint32_t bf16_rn_bits(float v) {
   uint32_t u = __float_as_uint(v);
@@ -188,31 +189,59 @@ __global__ void __launch_bounds__(kRtThreads) moe_router_mma_kernel(
   auto sc = reinterpret_cast<float(*)[kMaxExperts + 1]>(xbuf);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, tq = lane & 3;
-  const int th = warp & 1, eh = warp >> 1;  // token half, expert half
   const int64_t t0 = (int64_t)blockIdx.x * kRtTok;
   const int nxp = bf16 ? 1 : 3;
-  // Tensor-core fp32 accumulation truncates; each 64-K chunk accumulates in a
-  // fresh fp32 chain and the chunk results are summed in f64.
-  double acc[4][4];
+  // this thread's share of a chunk: 8 consecutive k of token xa, and 16-byte
+  // pieces of the router planes
+  const int xa = tid >> 3, xk = 8 * (tid & 7);
+  const bool xvec = (H & 7) == 0 &&
+                    (reinterpret_cast<uintptr_t>(x) & 15) == 0;  // 16-byte aligned rows
+  float xv[8];
+  uint4 rv[3][4];
+  auto fetch = [&](int64_t k0) {
+    const int64_t t = t0 + xa, k = k0 + xk;
+    if (t < T && xvec && k + 8 <= H) {
+      if (bf16) {
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(x) + t * H + k));
+        const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-  for (int n = 0; n < 4; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0;
+        for (int i = 0; i < 4; ++i) {
+          xv[2 * i] = __uint_as_float(w4[i] << 16);
+          xv[2 * i + 1] = __uint_as_float(w4[i] & 0xffff0000u);
+        }
+      } else {
+        const float4* f = reinterpret_cast<const float4*>(static_cast<const float*>(x) + t * H + k);
+        const float4 a = __ldg(f), b = __ldg(f + 1);
+        xv[0] = a.x; xv[1] = a.y; xv[2] = a.z; xv[3] = a.w;
+        xv[4] = b.x; xv[5] = b.y; xv[6] = b.z; xv[7] = b.w;
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) xv[e] = (t < T && k + e < H) ? load_act(x, bf16, t * H + k + e) : 0.0f;
+    }
+#pragma unroll
+    for (int q = 0; q < 3; ++q)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int piece = tid + i * kRtThreads;  // 512 pieces of 8 bf16 per plane
+        const int e = piece >> 3, kk = 8 * (piece & 7);
+        rv[q][i] = (q < n_rplanes && e < E)
+                       ? __ldg(reinterpret_cast<const uint4*>(Rp + ((int64_t)q * kMaxExperts + e) * Hpad + k0 + kk))
+                       : make_uint4(0, 0, 0, 0);
+      }
+  };
+  double acc[2][4];
+#pragma unroll
+  for (int n = 0; n < 2; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0;
+  fetch(0);
   for (int64_t k0 = 0; k0 < Hpad; k0 += kRtK) {
-    float part[4][4];
-#pragma unroll
-    for (int n = 0; n < 4; ++n) part[n][0] = part[n][1] = part[n][2] = part[n][3] = 0.0f;
     __syncthreads();  // the previous chunk is no longer read
-    // x chunk: 32 tokens x 64 k, 16 elements per thread, split into planes
-    for (int i = tid; i < kRtTok * kRtK / 2; i += kRtThreads) {
-      const int a = i / (kRtK / 2), kk = 2 * (i % (kRtK / 2));
-      const int64_t t = t0 + a, k = k0 + kk;
-      float v[2] = {0.0f, 0.0f};
+    {
+      // x split into planes (exact decomposition), 8 values -> 4 words per plane
+      uint32_t pl[3][8];
 #pragma unroll
-      for (int e = 0; e < 2; ++e)
-        if (t < T && k + e < H) v[e] = load_act(x, bf16, t * H + k + e);
-      uint32_t pl[3][2];
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        float r = v[e];
+      for (int e = 0; e < 8; ++e) {
+        float r = xv[e];
 #pragma unroll
         for (int q = 0; q < 3; ++q) {
           pl[q][e] = bf16_rn_bits(r);
@@ -221,31 +250,36 @@ __global__ void __launch_bounds__(kRtThreads) moe_router_mma_kernel(
       }
 #pragma unroll
       for (int q = 0; q < 3; ++q)
-        if (q < nxp) *reinterpret_cast<uint32_t*>(&xs[q][a][kk]) = pl[q][0] | (pl[q][1] << 16);
-    }
-    // router planes: 64 experts x 64 k each, 16-byte loads (zero rows past E)
-    for (int i = tid; i < n_rplanes * kMaxExperts * (kRtK / 8); i += kRtThreads) {
-      const int q = i / (kMaxExperts * (kRtK / 8));
-      const int rem = i % (kMaxExperts * (kRtK / 8));
-      const int e = rem / (kRtK / 8), kk = 8 * (rem % (kRtK / 8));
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (e < E)
-        v = __ldg(reinterpret_cast<const uint4*>(Rp + ((int64_t)q * kMaxExperts + e) * Hpad + k0 + kk));
-      *reinterpret_cast<uint4*>(&rs[q][e][kk]) = v;
+        if (q < nxp)
+          *reinterpret_cast<uint4*>(&xs[q][xa][xk]) =
+              make_uint4(pl[q][0] | (pl[q][1] << 16), pl[q][2] | (pl[q][3] << 16),
+                         pl[q][4] | (pl[q][5] << 16), pl[q][6] | (pl[q][7] << 16));
+#pragma unroll
+      for (int q = 0; q < 3; ++q)
+        if (q < n_rplanes)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int piece = tid + i * kRtThreads;
+            *reinterpret_cast<uint4*>(&rs[q][piece >> 3][8 * (piece & 7)]) = rv[q][i];
+          }
     }
     __syncthreads();
+    if (k0 + kRtK < Hpad) fetch(k0 + kRtK);  // in flight while the tensor cores work
+    float part[2][4];
+#pragma unroll
+    for (int n = 0; n < 2; ++n) part[n][0] = part[n][1] = part[n][2] = part[n][3] = 0.0f;
 #pragma unroll
     for (int ks = 0; ks < kRtK; ks += 16) {
       for (int i = 0; i < nxp; ++i) {
-        const uint16_t* ar = &xs[i][16 * th][0];
+        const uint16_t* ar = &xs[i][0][0];
         const uint32_t a0 = *reinterpret_cast<const uint32_t*>(ar + g * kRtPad + ks + 2 * tq);
         const uint32_t a1 = *reinterpret_cast<const uint32_t*>(ar + (g + 8) * kRtPad + ks + 2 * tq);
         const uint32_t a2 = *reinterpret_cast<const uint32_t*>(ar + g * kRtPad + ks + 8 + 2 * tq);
         const uint32_t a3 = *reinterpret_cast<const uint32_t*>(ar + (g + 8) * kRtPad + ks + 8 + 2 * tq);
         for (int j = 0; j < n_rplanes && i + j <= 2; ++j) {
 #pragma unroll
-          for (int n = 0; n < 4; ++n) {
-            const uint16_t* br = &rs[j][32 * eh + 8 * n + g][0];
+          for (int n = 0; n < 2; ++n) {
+            const uint16_t* br = &rs[j][16 * warp + 8 * n + g][0];
             const uint32_t b0 = *reinterpret_cast<const uint32_t*>(br + ks + 2 * tq);
             const uint32_t b1 = *reinterpret_cast<const uint32_t*>(br + ks + 8 + 2 * tq);
             mma_bf16(part[n], a0, a1, a2, a3, b0, b1);
@@ -254,18 +288,18 @@ __global__ void __launch_bounds__(kRtThreads) moe_router_mma_kernel(
       }
     }
 #pragma unroll
-    for (int n = 0; n < 4; ++n)
+    for (int n = 0; n < 2; ++n)
 #pragma unroll
       for (int i = 0; i < 4; ++i) acc[n][i] += (double)part[n][i];
   }
   __syncthreads();  // every warp is done reading x before the scores overwrite it
 #pragma unroll
-  for (int n = 0; n < 4; ++n) {
-    const int e0 = 32 * eh + 8 * n + 2 * tq;
-    sc[16 * th + g][e0] = (float)acc[n][0];
-    sc[16 * th + g][e0 + 1] = (float)acc[n][1];
-    sc[16 * th + g + 8][e0] = (float)acc[n][2];
-    sc[16 * th + g + 8][e0 + 1] = (float)acc[n][3];
+  for (int n = 0; n < 2; ++n) {
+    const int e0 = 16 * warp + 8 * n + 2 * tq;
+    sc[g][e0] = (float)acc[n][0];
+    sc[g][e0 + 1] = (float)acc[n][1];
+    sc[g + 8][e0] = (float)acc[n][2];
+    sc[g + 8][e0 + 1] = (float)acc[n][3];
   }
   __syncthreads();
   const int64_t t = t0 + tid;

@@ -99,6 +99,8 @@ struct TqBatch {
   int bf16;  // fp32 mode: activations are bf16 bit patterns
   int64_t total_items;
   int* err;
+  // first item of each problem, contiguous (item decoding reads only this)
+  int64_t item_begin[kMaxProblems + 1];
   TqProblem p[kMaxProblems];
 };
 
@@ -111,10 +113,16 @@ struct Item {
 };
 
 __device__ __forceinline__ Item decode_item(const TqBatch& b, int64_t item) {
-  int pi = 0;
-  while (pi + 1 < b.nprob && b.p[pi + 1].item_begin <= item) ++pi;
+  // the last problem whose first item is <= item (binary search)
+  int lo = 0, hi = b.nprob - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (b.item_begin[mid] <= item) lo = mid;
+    else hi = mid - 1;
+  }
+  const int pi = lo;
   const TqProblem& p = b.p[pi];
-  int64_t local = item - p.item_begin;
+  int64_t local = item - b.item_begin[pi];
   Item it;
   it.prob = pi;
   const int ks = (int)(local % p.ksplit);
@@ -644,21 +652,18 @@ __device__ __forceinline__ int64_t b_offset(int64_t pass, int64_t chunk, int n, 
          (n & 7) * 16 + (kin & 15);
 }
 
-__device__ __forceinline__ float load_x(const void* x, int xkind, int64_t i) {
-  return xkind == 0 ? static_cast<const float*>(x)[i]
-                    : __uint_as_float((uint32_t) static_cast<const uint16_t*>(x)[i] << 16);
-}
-
-// element i of a source's activations, with its column-block scale applied
-__device__ __forceinline__ float load_xs(const PrepSource& src, int xkind, int64_t i, int64_t k) {
-  const float v = load_x(src.x, xkind, i);
-  return src.kscale ? __fmul_rn(v, src.kscale[k / src.kblock]) : v;
-}
-
 // DT: digits per token (1: int8 codes, 4 or 8), a template parameter so that
 // the digit arrays stay in registers.
+//
+// One pass over the token: thread i holds elements 8i .. 8i+7 of every 2048-K
+// stretch (one 16-byte load of bf16 / int8, two of fp32, when aligned), kept in
+// registers (kPrepRegs stretches; longer rows are reloaded) for the absmax,
+// the non-finite count, the digit split and the column sums.  Each thread
+// writes 8 bytes of each digit column's 16-byte operand row.
+constexpr int kPrepThreads = 256, kPrepRegs = 2;
+
 template <int DT>
-__global__ void __launch_bounds__(256) prep_b_kernel(const __grid_constant__ PrepBatch pb) {
+__global__ void __launch_bounds__(kPrepThreads) prep_b_kernel(const __grid_constant__ PrepBatch pb) {
   // Let the matmul that consumes this launch start streaming its weights now;
   // then wait for the previous matmul, which may still be reading bmat.
   tc::pdl_launch_dependents();
@@ -672,24 +677,98 @@ __global__ void __launch_bounds__(256) prep_b_kernel(const __grid_constant__ Pre
   const int64_t t = pass * pb.tok_per_pass + lt;
   const int64_t K = src.K, kpad = src.n_chunks * 128;
   constexpr int D = DT;
-  const int npad = pb.npad;
+  const int npad = pb.npad, xkind = pb.xkind;
+  const float* kscale = src.kscale;
+  const int64_t kblock = src.kblock;
+  const void* xsrc = src.x;
   __shared__ float red_f[8];
   __shared__ int red_n[8];
   __shared__ int red_i[8][8];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool live = t < src.seq;
+  constexpr int kStretch = 8 * kPrepThreads;  // 2048 K per stretch
+  const int64_t nstr = (kpad + kStretch - 1) / kStretch;
+
+  // the 8 elements at k0 .. k0+7 of this token (zero past K), as floats
+  // (int8 codes: their integer values)
+  auto load8 = [&](int64_t k0, float (&v)[8]) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = 0.0f;
+    if (!live || k0 >= K) return;
+    const int64_t i0 = t * K + k0;
+    if (xkind == 2) {
+      const int8_t* q = static_cast<const int8_t*>(xsrc) + i0;
+      if (k0 + 8 <= K && (reinterpret_cast<uintptr_t>(q) & 7) == 0) {
+        const uint2 u = __ldg(reinterpret_cast<const uint2*>(q));
+        const uint32_t w2[2] = {u.x, u.y};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = (float)(int8_t)(w2[e >> 2] >> (8 * (e & 3)));
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (k0 + e < K) v[e] = (float)q[e];
+      }
+      return;
+    }
+    if (xkind == 1) {
+      const uint16_t* h = static_cast<const uint16_t*>(xsrc) + i0;
+      if (k0 + 8 <= K && (reinterpret_cast<uintptr_t>(h) & 15) == 0) {
+        const uint4 u = __ldg(reinterpret_cast<const uint4*>(h));
+        const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          v[2 * e] = __uint_as_float(w4[e] << 16);
+          v[2 * e + 1] = __uint_as_float(w4[e] & 0xffff0000u);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (k0 + e < K) v[e] = __uint_as_float((uint32_t)h[e] << 16);
+      }
+    } else {
+      const float* f = static_cast<const float*>(xsrc) + i0;
+      if (k0 + 8 <= K && (reinterpret_cast<uintptr_t>(f) & 15) == 0) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(f));
+        const float4 b = __ldg(reinterpret_cast<const float4*>(f) + 1);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (k0 + e < K) v[e] = f[e];
+      }
+    }
+    if (kscale) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (k0 + e < K) v[e] = __fmul_rn(v[e], kscale[(k0 + e) / kblock]);
+    }
+  };
+
+  float xr[kPrepRegs][8];
+#pragma unroll
+  for (int r = 0; r < kPrepRegs; ++r)
+    if (r < nstr) load8(r * (int64_t)kStretch + 8 * threadIdx.x, xr[r]);
   float f1 = 1.0f, f2 = 1.0f;
-  if (pb.xkind != 2) {
+  if (D != 1) {
     // largest finite |x| and the non-finite count
     float amax = 0.0f;
     int nnf = 0;
-    if (live) {
-#pragma unroll 8
-      for (int64_t k = threadIdx.x; k < K; k += blockDim.x) {
-        const float v = load_xs(src, pb.xkind, t * K + k, k);
-        if (is_nonfinite(v)) ++nnf;
-        else amax = fmaxf(amax, fabsf(v));
+    auto scan = [&](const float (&v)[8]) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const bool nf = is_nonfinite(v[e]);
+        nnf += nf ? 1 : 0;
+        amax = fmaxf(amax, nf ? 0.0f : fabsf(v[e]));
       }
+    };
+#pragma unroll
+    for (int r = 0; r < kPrepRegs; ++r)
+      if (r < nstr) scan(xr[r]);
+    for (int64_t r = kPrepRegs; r < nstr; ++r) {
+      float v[8];
+      load8(r * kStretch + 8 * threadIdx.x, v);
+      scan(v);
     }
     int incl = nnf;
 #pragma unroll
@@ -721,77 +800,65 @@ __global__ void __launch_bounds__(256) prep_b_kernel(const __grid_constant__ Pre
         nf[0] = total;
       }
       if (nnf != 0 && total <= kNfCap) {
+        // this thread's positions, in its element order
         int slot = before;
-        for (int64_t k = threadIdx.x; k < K; k += blockDim.x)
-          if (is_nonfinite(load_xs(src, pb.xkind, t * K + k, k))) nf[1 + slot++] = (int32_t)k;
+        for (int64_t r = 0; r < nstr; ++r) {
+          float v[8];
+          load8(r * kStretch + 8 * threadIdx.x, v);
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            if (is_nonfinite(v[e])) nf[1 + slot++] = (int32_t)(r * kStretch + 8 * threadIdx.x + e);
+        }
       }
     }
   }
-  // 16 consecutive K per step: one 16-byte row of the operand per digit column
+  // digits of each element; one 8-byte word pair per digit column
   int csum[D];
 #pragma unroll
   for (int d = 0; d < D; ++d) csum[d] = 0;
-  const int64_t ngroups = kpad >> 4;
-  for (int64_t kg = threadIdx.x; kg < ngroups; kg += blockDim.x) {
-    const int64_t k0 = kg * 16;
-    uint32_t w[D][4];
+  auto emit = [&](int64_t k0, const float (&v)[8]) {
+    if (k0 >= kpad) return;
+    uint32_t w[D][2];
 #pragma unroll
-    for (int d = 0; d < D; ++d) w[d][0] = w[d][1] = w[d][2] = w[d][3] = 0u;
-    if (live && k0 < K) {
-      if (pb.xkind == 2) {
-        const int8_t* q = static_cast<const int8_t*>(src.x) + t * K + k0;
-        if (k0 + 16 <= K && (reinterpret_cast<uintptr_t>(q) & 15) == 0) {
-          const uint4 v = __ldg(reinterpret_cast<const uint4*>(q));
-          w[0][0] = v.x; w[0][1] = v.y; w[0][2] = v.z; w[0][3] = v.w;
-        } else {
+    for (int d = 0; d < D; ++d) w[d][0] = w[d][1] = 0u;
 #pragma unroll
-          for (int e = 0; e < 16; ++e)
-            if (k0 + e < K) w[0][e >> 2] |= (uint32_t)(q[e] & 0xFF) << (8 * (e & 3));
-        }
-#pragma unroll
-        for (int j = 0; j < 4; ++j) csum[0] = __dp4a((int)w[0][j], 0x01010101, csum[0]);
+    for (int e = 0; e < 8; ++e) {
+      if (D == 1) {
+        const int q = (int)v[e];
+        w[0][e >> 2] |= (uint32_t)(q & 0xFF) << (8 * (e & 3));
+        csum[0] += q;
       } else {
-        float xv[16];
-        const bool vec = pb.xkind == 0 && k0 + 16 <= K && !src.kscale &&
-                         (reinterpret_cast<uintptr_t>(static_cast<const float*>(src.x) + t * K + k0) & 15) == 0;
-        if (vec) {
-          const float4* f4 = reinterpret_cast<const float4*>(static_cast<const float*>(src.x) + t * K + k0);
+        const float xs = is_nonfinite(v[e]) ? 0.0f : __fmul_rn(__fmul_rn(v[e], f1), f2);
+        // X = round(x * 2^sh), |X| < 2^(8D-2); balanced base-256 digits (64-bit
+        // arithmetic only for D = 8)
+        using XT = typename std::conditional<(D > 4), long long, int>::type;
+        XT X = D > 4 ? (XT)__float2ll_rn(xs) : (XT)__float2int_rn(xs);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float4 v = __ldg(f4 + j);
-            xv[4 * j] = v.x; xv[4 * j + 1] = v.y; xv[4 * j + 2] = v.z; xv[4 * j + 3] = v.w;
-          }
-        } else {
-#pragma unroll
-          for (int e = 0; e < 16; ++e)
-            xv[e] = k0 + e < K ? load_xs(src, pb.xkind, t * K + k0 + e, k0 + e) : 0.0f;
+        for (int d = 0; d < D - 1; ++d) {
+          const int lo = ((int)(X & 0xFF) ^ 0x80) - 0x80;  // signed low digit
+          w[d][e >> 2] |= (uint32_t)(lo & 0xFF) << (8 * (e & 3));
+          csum[d] += lo;
+          X = (X - lo) >> 8;
         }
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const float xs = is_nonfinite(xv[e]) ? 0.0f : __fmul_rn(__fmul_rn(xv[e], f1), f2);
-          // X = round(x * 2^sh), |X| < 2^(8D-2); balanced base-256 digits (64-bit
-          // arithmetic only for D = 8)
-          using XT = typename std::conditional<(D > 4), long long, int>::type;
-          XT X = D > 4 ? (XT)__float2ll_rn(xs) : (XT)__float2int_rn(xs);
-#pragma unroll
-          for (int d = 0; d < D - 1; ++d) {
-            const int lo = ((int)(X & 0xFF) ^ 0x80) - 0x80;  // signed low digit
-            w[d][e >> 2] |= (uint32_t)(lo & 0xFF) << (8 * (e & 3));
-            csum[d] += lo;
-            X = (X - lo) >> 8;
-          }
-          // the top digit, |X| <= 64 here
-          w[D - 1][e >> 2] |= (uint32_t)((int)X & 0xFF) << (8 * (e & 3));
-          csum[D - 1] += (int)X;
-        }
+        // the top digit, |X| <= 64 here
+        w[D - 1][e >> 2] |= (uint32_t)((int)X & 0xFF) << (8 * (e & 3));
+        csum[D - 1] += (int)X;
       }
     }
     const int64_t chunk = k0 >> 7;
     const int kin = (int)(k0 & 127);
 #pragma unroll
     for (int d = 0; d < D; ++d)
-      *reinterpret_cast<uint4*>(src.bmat + b_offset(pass, chunk, lt * D + d, kin, npad, src.n_chunks)) =
-          make_uint4(w[d][0], w[d][1], w[d][2], w[d][3]);
+      *reinterpret_cast<uint2*>(src.bmat + b_offset(pass, chunk, lt * D + d, kin & ~15, npad, src.n_chunks) +
+                                (kin & 8)) = make_uint2(w[d][0], w[d][1]);
+  };
+#pragma unroll
+  for (int r = 0; r < kPrepRegs; ++r)
+    if (r < nstr) emit(r * (int64_t)kStretch + 8 * threadIdx.x, xr[r]);
+  for (int64_t r = kPrepRegs; r < nstr; ++r) {
+    float v[8];
+    load8(r * kStretch + 8 * threadIdx.x, v);
+    emit(r * kStretch + 8 * threadIdx.x, v);
   }
 #pragma unroll
   for (int d = 0; d < D; ++d) {
@@ -991,6 +1058,7 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
     p.tok_per_pass = tok_per_pass;
     p.passes = (int)passes;
     p.item_begin = items;
+    batch.item_begin[q] = items;
     items += passes * w->n_tiles * p.ksplit;
     acc_off[q] = cnt_off[q] = 0;
     if (p.ksplit > 1) {
@@ -1001,6 +1069,7 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
     }
   }
   batch.total_items = items;
+  batch.item_begin[nlive] = items;
   const size_t err_off = zoff;
   st = zero_scratch_reserve(ctx, err_off + 256, s);
   if (st != FT_OK) return st;
@@ -1043,7 +1112,7 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
     FT_CHECK(blocks <= 0x7FFFFFFF, FT_ERR_UNSUPPORTED, "too many prep blocks");
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)blocks);
-    cfg.blockDim = dim3(256);
+    cfg.blockDim = dim3(kPrepThreads);
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -1180,9 +1249,11 @@ int launch_tc_noalloc(ft_ctx* ctx, const ft_weight* w, int64_t seq, const float*
   p.tok_per_pass = tok_per_pass;
   p.passes = 1;
   p.item_begin = 0;
+  batch.item_begin[0] = 0;
   p.acc = reinterpret_cast<int32_t*>(zs + kNaAccOff);
   p.cnt = reinterpret_cast<int32_t*>(zs + kNaCntOff);
   batch.total_items = w->n_tiles * p.ksplit;
+  batch.item_begin[1] = batch.total_items;
   // The split-K sums and tickets this call uses must start at zero (the kernel
   // leaves them zeroed, but a launch whose wait gave up may not have).  The
   // error word is not cleared here: it keeps a report until ft_ctx_check of a
@@ -1215,7 +1286,7 @@ int launch_tc_noalloc(ft_ctx* ctx, const ft_weight* w, int64_t seq, const float*
   ps.K = w->cols;
   ps.n_chunks = w->n_chunks;
   ps.passes = 1;
-  prep_b_kernel<kDigitsExact><<<tok_per_pass, 256, 0, s>>>(pb);
+  prep_b_kernel<kDigitsExact><<<tok_per_pass, kPrepThreads, 0, s>>>(pb);
   FT_LAUNCH_CHECK();
   const int64_t grid = batch.total_items < grid_target ? batch.total_items : grid_target;
   return launch_grouped_t<kNaNpad>(batch, grid, s);

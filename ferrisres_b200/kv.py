@@ -31,14 +31,27 @@ class Kv3Cache:
     """One layer's 3-bit KV cache for ``batch`` sequences on one GPU."""
 
     def __init__(self, batch: int, kv_heads: int, max_seq: int, head_dim: int = HEAD_DIM,
-                 device=None):
+                 device=None, mode: str = "R", seed: int = 0):
+        """mode "R": the reference TurboQuantKVCache scheme (min/max per vector);
+        mode "T": rotation + uniform 3-bit codebook + per-vector norm (see
+        ft_kv3_create_mode), rotation signs drawn from ``seed``."""
         self.ctx = get_context(device)
         self.batch, self.kv_heads = int(batch), int(kv_heads)
+        if mode not in ("R", "T"):
+            raise ShapeError("mode must be 'R' or 'T'")
+        self.mode = mode
         h = C.c_void_p()
-        call("ft_kv3_create", self.ctx.handle, self.batch, self.kv_heads, int(head_dim),
-             int(max_seq), C.byref(h))
+        call("ft_kv3_create_mode", self.ctx.handle, self.batch, self.kv_heads, int(head_dim),
+             int(max_seq), 0 if mode == "R" else 1, int(seed) & (2**64 - 1), C.byref(h))
         self.handle = h
         self.device = torch.device("cuda", self.ctx.device)
+
+    def signs(self):
+        """Mode T: the 128 rotation signs (numpy float32)."""
+        import numpy as np
+        out = np.empty(HEAD_DIM, np.float32)
+        call("ft_kv3_signs", self.handle, out.ctypes.data_as(C.c_void_p))
+        return out
 
     # ---- state
     def __len__(self) -> int:

@@ -322,6 +322,21 @@ int ft_moe_combine(ft_ctx* ctx, ft_moe* m, int64_t T, const float* o_rows_dev,
  * the reference's Vec storage grows.  Replaces TurboQuantKVCache::new (:211). */
 int ft_kv3_create(ft_ctx* ctx, int64_t batch, int64_t kv_heads, int64_t head_dim,
                   int64_t max_seq, ft_kv3** out);
+/* Same with a quantisation mode: 0 = the reference scheme above; 1 = "mode T"
+ * (BASELINE's TurboQuant description: rotation + 3-bit codebook + fp32 norm;
+ * the reference has no working implementation, src/compute/turboquant.rs:89-367,
+ * so this mode's spec and oracle are this project's own): each vector is
+ * rotated by H D / ||v|| (D = 128 signs drawn from SplitMix64(seed), H the
+ * Walsh-Hadamard transform) and each coordinate y coded as
+ * clamp(floor((y / 2.5 + 1) * 4), 0, 7), the nearest of the 8 uniform centroids on
+ * [-1, 1] that the reference's compute_mse_centroids (:197-220) converges to; the
+ * record's (min, max) holds -/+ ||v|| * 2.5 * 7/8 / sqrt(128).  append, get_range
+ * (rotated back), flash decode (q rotated in, the output rotated back) and
+ * export / append_packed (the stored rotated codes) work in both modes. */
+int ft_kv3_create_mode(ft_ctx* ctx, int64_t batch, int64_t kv_heads, int64_t head_dim,
+                       int64_t max_seq, int mode, uint64_t seed, ft_kv3** out);
+/* Mode T: the 128 rotation signs (+-1) into signs_host. */
+int ft_kv3_signs(const ft_kv3* c, float* signs_host);
 int ft_kv3_destroy(ft_kv3* c);
 /* Appends n_pos positions per sequence: k, v [batch, n_pos, kv_heads, 128]
  * fp32 (bf16 bit patterns when is_bf16), quantised exactly as append /

@@ -992,3 +992,76 @@ void fo_flash_decode_3bit(const float* q, const uint8_t* kc, const float* kmm, c
   fo_fd_ctx c = {q, NULL, NULL, kc, kmm, vc, vmm, batch, seq, hq, hkv, d, out};
   fo_parallel_for(batch * hq, nthreads, fo_fd_item, &c);
 }
+
+/* ------------------------------------------------------------------------ */
+/* 3-bit KV "mode T": rotation + uniform codebook + per-vector norm.        */
+/* The reference has no working implementation of this scheme (its          */
+/* TurboQuantEngine, src/compute/turboquant.rs:89-367, draws an unseeded     */
+/* rotation and its WGSL does not compile); this is this project's spec:     */
+/*   norm = ||v||_2 (fp32; squares summed as 4 warps of 32 lanes, each warp  */
+/*          by the xor butterfly 16, 8, 4, 2, 1, then ((w0+w1)+w2)+w3)       */
+/*   u    = v / norm, u_i *= sign_i (seeded +-1)                             */
+/*   y    = H u (Walsh-Hadamard, butterflies h = 1, 2, ..., 64 in place:     */
+/*          a = y[j], b = y[j+h]; y[j] = a + b; y[j+h] = a - b)              */
+/*   z    = y / 2.5 (y_i ~ N(0, 1) for a random direction: clip at 2.5 sigma)*/
+/*   code = clamp(floor((z + 1) * 4), 0, 7): the nearest of the 8 uniform    */
+/*          centroids (2i+1)/8 - 1 on [-1, 1] (the centroids that            */
+/*          compute_mse_centroids, turboquant.rs:197-220, converges to)      */
+/* Dequantized, the rotated unit vector has coordinates                      */
+/*   yhat_i = 2.5 * ((2 code_i + 1)/8 - 1) / sqrt(128)                       */
+/* and v = norm * D H yhat / sqrt(128)... i.e. in the rotated domain the     */
+/* vector is affine in the code: min + code * (max - min) / 7 with           */
+/*   max = -min = norm * (2.5 * 7/8 / sqrt(128)).                            */
+/* Attention in the rotated domain: q' = H D q / sqrt(128), o = D H o' /     */
+/* sqrt(128).                                                                */
+/* ------------------------------------------------------------------------ */
+static const float FO_KVT_CLIP = 2.5f;
+
+static void fo_fwht128(float* y) {
+  for (int h = 1; h < 128; h <<= 1)
+    for (int i = 0; i < 128; i += 2 * h)
+      for (int j = i; j < i + h; ++j) {
+        const float a = y[j], b = y[j + h];
+        y[j] = a + b;
+        y[j + h] = a - b;
+      }
+}
+
+float fo_kvt_mm_const(void) { return (FO_KVT_CLIP * 7.0f / 8.0f) / sqrtf(128.0f); }
+
+/* one 128-vector -> 128 codes (0..7) and its norm */
+void fo_kvt_quantize(const float* v, const float* signs, uint8_t* codes, float* norm_out) {
+  float sq[128];
+  for (int i = 0; i < 128; ++i) sq[i] = v[i] * v[i];
+  float wsum[4];
+  for (int w = 0; w < 4; ++w) {
+    float lanes[32];
+    for (int l = 0; l < 32; ++l) lanes[l] = sq[32 * w + l];
+    for (int o = 16; o > 0; o >>= 1) {
+      float nl[32];
+      for (int l = 0; l < 32; ++l) nl[l] = lanes[l] + lanes[l ^ o];
+      memcpy(lanes, nl, sizeof(lanes));
+    }
+    wsum[w] = lanes[0];
+  }
+  const float n2 = ((wsum[0] + wsum[1]) + wsum[2]) + wsum[3];
+  const float norm = sqrtf(n2);
+  *norm_out = norm;
+  float y[128];
+  for (int i = 0; i < 128; ++i) y[i] = norm > 0.0f ? (v[i] / norm) * signs[i] : 0.0f;
+  fo_fwht128(y);
+  for (int i = 0; i < 128; ++i) {
+    const float z = y[i] / FO_KVT_CLIP;
+    const float c = floorf((z + 1.0f) * 4.0f);
+    codes[i] = (uint8_t)(c <= 0.0f ? 0 : (c >= 7.0f ? 7 : (int)c));
+  }
+}
+
+/* q' = H D q / sqrt(128) (inverse = 0) or o = D H o' / sqrt(128) (inverse = 1) */
+void fo_kvt_rotate(const float* in, const float* signs, int inverse, float* out) {
+  float y[128];
+  for (int i = 0; i < 128; ++i) y[i] = inverse ? in[i] : in[i] * signs[i];
+  fo_fwht128(y);
+  const float s = 1.0f / sqrtf(128.0f);
+  for (int i = 0; i < 128; ++i) out[i] = inverse ? (y[i] * s) * signs[i] : y[i] * s;
+}

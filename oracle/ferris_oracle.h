@@ -144,6 +144,12 @@ void fo_flash_decode_3bit(const float* q, const uint8_t* kc, const float* kmm, c
 
 int fo_num_threads(int requested);
 
+/* 3-bit KV mode T (this project's spec; see ferris_oracle.c): one 128-vector ->
+ * codes 0..7 and its norm; (min, max) of the shared record = -/+ norm * fo_kvt_mm_const() */
+void fo_kvt_quantize(const float* v, const float* signs, uint8_t* codes, float* norm_out);
+float fo_kvt_mm_const(void);
+/* q' = H D q / sqrt(128) (inverse 0) or o = D H o' / sqrt(128) (inverse 1) */
+void fo_kvt_rotate(const float* in, const float* signs, int inverse, float* out);
 #ifdef __cplusplus
 }
 #endif

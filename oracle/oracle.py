@@ -60,6 +60,9 @@ def _declare(L):
         "fo_ternary_matmul_sparse_decode": (None, [_p, _p, _p, _p, C.c_float, _p, _sz, _p]),
         "fo_bitmoe_requantize": (None, [_p, _sz, C.c_float, _p]),
         "fo_bitmoe_recompute_alpha": (C.c_int, [_p, _p, _sz, _p]),
+        "fo_kvt_quantize": (None, [_p, _p, _p, _p]),
+        "fo_kvt_mm_const": (C.c_float, []),
+        "fo_kvt_rotate": (None, [_p, _p, C.c_int, _p]),
         "fo_ternary_matmul_packed_parallel_rows": (None, [_p, _p, _p, _sz, _sz, _p, C.c_int]),
         "fo_gpu_ternary_mm_cpu": (None, [_p, _p, _p, _sz, _sz, _sz, _p]),
         "fo_ternary_matmul_parallel": (None, [_p, C.c_float, _p, _sz, _sz, _sz, _p, C.c_int]),
@@ -389,3 +392,54 @@ def flash_decode_3bit(q, kc, kmm, vc, vmm, batch, seq, hq, hkv, d, nthreads=0):
 
 def num_threads(requested=0):
     return lib().fo_num_threads(requested)
+
+
+# --------------------------------------------- 3-bit KV mode T (own spec) --
+def kvt_quantize(v, signs):
+    """One 128-vector -> (codes uint8[128], norm) under mode T (ferris_oracle.c)."""
+    v, sg = _c(v, np.float32), _c(signs, np.float32)
+    codes = np.zeros(128, np.uint8)
+    n = C.c_float()
+    lib().fo_kvt_quantize(_ptr(v), _ptr(sg), _ptr(codes), C.byref(n))
+    return codes, np.float32(n.value)
+
+
+def kvt_signs(seed):
+    """The 128 mode-T rotation signs: SplitMix64 draws from ``seed``, -1 where
+    bit 63 of the draw is set (the published SplitMix64 of Steele, Lea and
+    Flood, OOPSLA 2014)."""
+    m = (1 << 64) - 1
+    z, out = int(seed) & m, np.empty(128, np.float32)
+    for i in range(128):
+        z = (z + 0x9E3779B97F4A7C15) & m
+        r = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & m
+        r = ((r ^ (r >> 27)) * 0x94D049BB133111EB) & m
+        r ^= r >> 31
+        out[i] = -1.0 if r >> 63 else 1.0
+    return out
+
+
+def kvt_store_vector(v, signs):
+    """One 128-vector in mode T's stored form: (48 packed code bytes,
+    (min, max) = -/+ norm * kvt_mm_const())."""
+    codes, norm = kvt_quantize(v, signs)
+    mx = np.float32(kvt_mm_const() * norm)
+    return pack_3bit(codes), np.array([-mx, mx], np.float32)
+
+
+def kvt_load_vector(packed, minmax, signs):
+    """The stored form back in the original domain: the affine dequantisation
+    of the rotated codes, then the inverse rotation."""
+    return kvt_rotate(dequantize_3bit(unpack_3bit(packed, 128), minmax[0], minmax[1]), signs,
+                      inverse=True)
+
+
+def kvt_mm_const():
+    return np.float32(lib().fo_kvt_mm_const())
+
+
+def kvt_rotate(x, signs, inverse=False):
+    x, sg = _c(x, np.float32), _c(signs, np.float32)
+    out = np.zeros(128, np.float32)
+    lib().fo_kvt_rotate(_ptr(x), _ptr(sg), int(inverse), _ptr(out))
+    return out

@@ -74,3 +74,18 @@ def test_host_quantize_matches_oracle():
     q1, a1 = ternary.quantize_ternary(w)
     q2, a2 = fo.quantize_ternary(w)
     assert a1 == a2 and (q1 == q2).all()
+
+
+def test_rust_sys_crate_matches_header():
+    """rust/ferris-ternary-sys declares every entry point of include/ferris_ternary.h with
+    the same number of arguments (the crate cannot be compiled in this image)."""
+    import re
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    h = open(os.path.join(root, "include", "ferris_ternary.h")).read()
+    h = re.sub(r"/\*.*?\*/", "", h, flags=re.S)
+    c = {n: len([a for a in args.split(",") if a.strip() and a.strip() != "void"])
+         for n, args in re.findall(r"\b(ft_[a-z0-9_]+)\(([^)]*)\);", h, flags=re.S)}
+    rs = open(os.path.join(root, "rust", "ferris-ternary-sys", "src", "lib.rs")).read()
+    r = {n: len([a for a in args.split(",") if a.strip()])
+         for n, args in re.findall(r"pub fn (ft_[a-z0-9_]+)\(([^)]*)\)", rs, flags=re.S)}
+    assert c == r

@@ -526,3 +526,29 @@ def test_bitmoe_synchronized_alpha_and_requantize():  # bit_moe.rs:319-386
         assert set(np.unique(q)) <= {-1, 0, 1}
     assert fo.bitmoe_recompute_alpha([]) is None
     assert (fo.bitmoe_requantize(mats[0], 0.0) == 0).all()  # alpha < 1e-10 -> all zero
+
+
+def test_kvt_known_answers():
+    """Mode T of the 3-bit KV cache (own spec): v = D (H e_0) = the signs gives
+    D v = 1, H 1 = 128 e_0, norm sqrt(128), rotated y = sqrt(128) e_0: code 7
+    at 0 (clamped) and code 4 (the centroid above 0) elsewhere."""
+    s = fo.kvt_signs(42)
+    assert set(np.unique(s)) == {-1.0, 1.0}
+    codes, norm = fo.kvt_quantize(s, s)
+    assert norm == np.float32(np.sqrt(np.float32(128)))
+    assert codes[0] == 7 and (codes[1:] == 4).all()
+    # zero vector: norm 0, every code 4, (min, max) = (-0, 0)
+    p, mm = fo.kvt_store_vector(np.zeros(128, np.float32), s)
+    assert (fo.unpack_3bit(p, 128) == 4).all() and mm.tolist() == [0.0, 0.0]
+    # the rotation is orthonormal: forward then inverse is the identity to fp32 rounding
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal(128).astype(np.float32)
+    y = fo.kvt_rotate(x, s)
+    assert abs(np.linalg.norm(y) - np.linalg.norm(x)) < 1e-5 * np.linalg.norm(x)
+    assert np.max(np.abs(fo.kvt_rotate(y, s, inverse=True) - x)) < 1e-5
+    # Gaussian vectors: relative reconstruction error near the 8-level
+    # uniform quantiser's (step 0.625 sigma -> about 0.19)
+    v = rng.standard_normal((64, 128)).astype(np.float32)
+    err = [np.linalg.norm(fo.kvt_load_vector(*fo.kvt_store_vector(r, s), s) - r) / np.linalg.norm(r)
+           for r in v]
+    assert 0.12 < np.mean(err) < 0.25, np.mean(err)
