@@ -926,6 +926,7 @@ def run_kv(args, torch, dist, device, local, sub_steps, cpu_seconds):
     dec_gbs = KV_ALGO_BYTES / dec_s / 1e9
     cache.close()
     mode_t = kv_mode_t_times(torch, kv, device, local, timer, stream, q, out, k1, v1, sub_steps)
+    paged = kv_paged_times(torch, device, local, timer, stream, q, out, sub_steps)
     res = {
         "metric": "3-bit KV flash-decode HBM GB/s", "value": round(value, 2), "unit": "GB/s",
         "steps": sub_steps, "ms_per_step": step_s * 1e3, "dtype": "u8 codes / f32",
@@ -947,10 +948,54 @@ def run_kv(args, torch, dist, device, local, sub_steps, cpu_seconds):
         "gpu_launches": int(gpu_launches),
         "clocks": clocks,
         "mode_t": mode_t,
+        "paged": paged,
     }
     if cpu_seconds > 0:
         res["cpu_baseline"] = kv_cpu_baseline(cpu_seconds)
     return res
+
+
+def kv_paged_times(torch, device, local, timer, stream, q, out, sub_steps):
+    """The cfg5 decode through block tables: 32 requests of 32768 positions in
+    a page pool (pages handed out by the PagedAttention allocator, so a
+    request's pages are not contiguous), decoded by ft_kvp_flash_decode with
+    the tables already on the device."""
+    import ctypes as C
+
+    from ferrisres_b200 import paged
+    from ferrisres_b200._lib import call
+    from ferrisres_b200.gpu import _dptr
+    pages_per = KV_S // paged.PAGE_POSITIONS
+    cache = paged.PagedKv3Cache(1, KV_B * pages_per + 8, KV_HKV, device=local)
+    rids = [cache.create_request() for _ in range(KV_B)]
+    gen = torch.Generator(device=device).manual_seed(7)
+    chunk = 4096
+    for _ in range(KV_S // chunk):
+        kk = torch.randn((KV_B, chunk, KV_HKV, KV_D), device=device, generator=gen).to(torch.bfloat16)
+        vv = torch.randn((KV_B, chunk, KV_HKV, KV_D), device=device, generator=gen).to(torch.bfloat16)
+        cache.append(0, rids, kk, vv)
+        del kk, vv
+    tables, stride = cache._tables(0, rids)
+    lens = torch.full((KV_B,), KV_S, dtype=torch.int32, device=device)
+
+    def dec():
+        call("ft_kvp_flash_decode", cache.ctx.handle, cache.handle, KV_B, _dptr(tables), stride,
+             _dptr(lens), KV_S, _dptr(q), KV_HQ, C.c_float(0.0), _dptr(out),
+             C.c_void_p(stream.cuda_stream))
+
+    for _ in range(3):
+        with torch.cuda.stream(stream):
+            dec()
+    stream.synchronize()
+    dec_s = timer(lambda: [dec() for _ in range(sub_steps)]) / sub_steps
+    cache.ctx.check()
+    cache.close()
+    peak, _, _ = load_peaks()
+    gbs = KV_ALGO_BYTES / dec_s / 1e9
+    return {"decode_us": round(dec_s * 1e6, 2), "decode_gbs": round(gbs, 2),
+            "decode_frac": round(gbs / peak, 4),
+            "note": "32 requests x 32768 positions in 32-position pages from the block "
+                    "allocator; tables resident on the device"}
 
 
 def kv_mode_t_times(torch, kv, device, local, timer, stream, q, out, k1, v1, sub_steps):

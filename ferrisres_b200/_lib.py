@@ -112,6 +112,15 @@ SIGNATURES = {
     "ft_kv3_get_range": [_p, _p, _i64, _i64, _p, _p, _p],
     "ft_kv3_export_range": [_p, _p, _i64, _i64, _p, _p, _p, _p, _p],
     "ft_flash_decode_3bit": [_p, _p, _p, _i64, C.c_float, _p, _p],
+    "ft_kvp_create": [_p, _i64, _i64, _i64, _i64, _i, C.c_uint64, _p],
+    "ft_kvp_destroy": [_p],
+    "ft_kvp_signs": [_p, _p],
+    "ft_kvp_append": [_p, _p, _i64, _i64, _p, _i64, _p, _p, _p, _i, _p],
+    "ft_kvp_append_packed": [_p, _p, _i64, _i64, _p, _i64, _p, _p, _p, _p, _p, _p],
+    "ft_kvp_copy_pages": [_p, _p, _i64, _p, _p, _p],
+    "ft_kvp_get_range": [_p, _p, _i64, _p, _i64, _i64, _i64, _p, _p, _p],
+    "ft_kvp_export_range": [_p, _p, _i64, _p, _i64, _i64, _i64, _p, _p, _p, _p, _p],
+    "ft_kvp_flash_decode": [_p, _p, _i64, _p, _i64, _p, _i64, _p, _i64, C.c_float, _p, _p],
 }
 _RESTYPE = {"ft_version": C.c_char_p, "ft_last_error_string": C.c_char_p,
             "ft_launch_counter": C.c_uint64}

@@ -405,6 +405,9 @@ int ft_ctx_check(ft_ctx* ctx) {
     if (code != 0) {
       int zero = 0;
       FT_CUDA(cudaMemcpy(wd, &zero, sizeof(int), cudaMemcpyHostToDevice));
+      if (code >= 1000)
+        return fail(FT_ERR_SHAPE, "a kernel met an out-of-range page or position (site %d) "
+                    "and skipped it; results of that launch are invalid", code);
       return fail(FT_ERR_TIMEOUT, "a kernel's bounded wait gave up (site %d); results of that "
                   "launch are invalid", code);
     }

@@ -78,6 +78,19 @@ struct ft_kv3 {
   ft::Workspace rot;           // mode T: the rotated queries
 };
 
+// The page pool of the paged cache: page P holds 32 positions of every kv
+// head, record (P, h) at (P * kv_heads + h) * 3584 bytes -- the ring's record,
+// so the same kernels serve both.  The pool is storage only: which pages a
+// sequence owns, and in which order, is the caller's block table.
+struct ft_kvp {
+  int device = 0;
+  int64_t n_pages = 0, kv_heads = 0;
+  uint32_t* blocks = nullptr;
+  int mode = 0;
+  float* signs = nullptr;
+  ft::Workspace part, rot;
+};
+
 namespace ft {
 namespace {
 
@@ -168,7 +181,25 @@ struct AppendParams {
   int64_t n_pos, Hkv, cap, nbc, s0;
   uint32_t* blocks;
   const float* signs;  // mode T rotation signs, or null (the reference's scheme)
+  // paged pool (table != null): sequence b writes positions pos0[b] .. +n_pos,
+  // logical block j of b lives in page table[b * tstride + j] (< n_pages)
+  const int32_t* table;
+  const int32_t* pos0;
+  int64_t tstride, n_pages;
+  int* err;
 };
+
+// A page index read from a caller's block table, checked: out-of-range
+// entries are recorded in the error word (site `code`) and replaced by -1.
+__device__ __forceinline__ int64_t checked_page(const int32_t* table, int64_t idx,
+                                                int64_t n_pages, int* err, int code) {
+  const int32_t pg = table[idx];
+  if (pg < 0 || pg >= n_pages) {
+    if (err) atomicCAS(err, 0, code);
+    return -1;
+  }
+  return pg;
+}
 
 // Mode T constants: clip at 2.5 and the (min, max) factor 2.5 * 7/8 / sqrt(128).
 constexpr float kTClip = 2.5f;
@@ -228,15 +259,29 @@ __global__ void __launch_bounds__(kD) kv3_append_kernel(AppendParams p) {
   const int64_t x = blockIdx.x, row = blockIdx.y;
   const int64_t b = row / p.Hkv, h = row % p.Hkv;
   const int d = threadIdx.x, warp = d >> 5, lane = d & 31;
-  const int64_t off0 = p.s0 % kBlk;
-  const int64_t pb = (p.s0 / kBlk + x) % p.nbc;
+  const int64_t s0 = p.table ? (int64_t)p.pos0[b] : p.s0;
+  const int64_t off0 = s0 % kBlk;
   const int u_begin = x == 0 ? (int)off0 : 0;
   int64_t u_end64 = p.n_pos + off0 - x * kBlk;
   const int u_end = u_end64 > kBlk ? kBlk : (int)u_end64;
+  if (u_begin >= u_end) return;  // paged: this sequence touches fewer blocks
+  int64_t rec;                   // record index of the block
+  if (p.table) {
+    const int64_t lb = s0 / kBlk + x;
+    if (s0 < 0 || lb >= p.tstride) {
+      if (d == 0) atomicCAS(p.err, 0, 1001);
+      return;
+    }
+    const int64_t pg = checked_page(p.table, b * p.tstride + lb, p.n_pages, p.err, 1002);
+    if (pg < 0) return;
+    rec = pg * p.Hkv + h;
+  } else {
+    rec = row * p.nbc + (s0 / kBlk + x) % p.nbc;
+  }
   __shared__ float red[4][4];
   __shared__ uint32_t kw[kBlkWords], vw[kBlkWords];
   __shared__ float ybk[kD], ybv[kD];
-  uint32_t* kg = p.blocks + (row * p.nbc + pb) * kRecWords;
+  uint32_t* kg = p.blocks + rec * kRecWords;
   uint32_t* vg = kg + kRecV;
   float2* kmm = reinterpret_cast<float2*>(kg + kRecKmm);
   float2* vmm = reinterpret_cast<float2*>(kg + kRecVmm);
@@ -324,7 +369,25 @@ __global__ void __launch_bounds__(kD) kv3_append_kernel(AppendParams p) {
 struct RangeParams {
   int64_t B, Hkv, cap, nbc, head, start, n;
   const uint32_t* blocks;
+  const int32_t* table;  // paged pool: positions start + pos of sequence b through the table
+  int64_t tstride, n_pages;
+  int* err;
 };
+
+// The record holding position `pos` of the range for (b, h) and its slot in
+// the block; null for a bad table entry (recorded in the error word).
+__device__ __forceinline__ const uint32_t* range_record(const RangeParams& p, int64_t b,
+                                                       int64_t h, int64_t pos, int* s) {
+  if (p.table) {
+    const int64_t lpos = p.start + pos;
+    *s = (int)(lpos % kBlk);
+    const int64_t pg = checked_page(p.table, b * p.tstride + lpos / kBlk, p.n_pages, p.err, 1003);
+    return pg < 0 ? nullptr : p.blocks + (pg * p.Hkv + h) * kRecWords;
+  }
+  const int64_t slot = (p.head + p.start + pos) % p.cap;
+  *s = (int)(slot % kBlk);
+  return p.blocks + ((b * p.Hkv + h) * p.nbc + slot / kBlk) * kRecWords;
+}
 
 // get_range (turboquant_kv.rs:271-291): out [B][n][Hkv][128] f32, dequantised
 // with the reference's roundings (dequantize_3bit :110-117).
@@ -337,11 +400,13 @@ __global__ void kv3_dequant_kernel(RangeParams p, float* __restrict__ kout,
   const int64_t h = vec % p.Hkv;
   const int64_t pos = (vec / p.Hkv) % p.n;
   const int64_t b = vec / (p.Hkv * p.n);
-  const int64_t row = b * p.Hkv + h;
-  const int64_t slot = (p.head + p.start + pos) % p.cap;
-  const int64_t blk = row * p.nbc + slot / kBlk;
-  const int s = (int)(slot % kBlk);
-  const uint32_t* rec = p.blocks + blk * kRecWords;
+  int s;
+  const uint32_t* rec = range_record(p, b, h, pos, &s);
+  if (!rec) {  // uniform over the block: no barrier is skipped by part of it
+    kout[vec * kD + d] = 0.0f;
+    vout[vec * kD + d] = 0.0f;
+    return;
+  }
   const uint32_t ck = k_code(rec, s, d);
   const uint32_t cv = v_code(rec + kRecV, s, d);
   const float2 km = reinterpret_cast<const float2*>(rec + kRecKmm)[mm_index(s)];
@@ -395,11 +460,9 @@ __global__ void kv3_export_kernel(RangeParams p, uint8_t* __restrict__ kbytes,
   const int64_t h = vec % p.Hkv;
   const int64_t pos = (vec / p.Hkv) % p.n;
   const int64_t b = vec / (p.Hkv * p.n);
-  const int64_t row = b * p.Hkv + h;
-  const int64_t slot = (p.head + p.start + pos) % p.cap;
-  const int64_t blk = row * p.nbc + slot / kBlk;
-  const int s = (int)(slot % kBlk);
-  const uint32_t* kb = p.blocks + blk * kRecWords;
+  int s;
+  const uint32_t* kb = range_record(p, b, h, pos, &s);
+  if (!kb) return;
   const uint32_t* vb = kb + kRecV;
   uint32_t kbits = 0, vbits = 0;
 #pragma unroll
@@ -436,6 +499,11 @@ struct DecodeParams {
   const uint32_t* blocks;
   float* part;  // [B][Hq][nsplit][kPart]
   int* err;
+  // paged pool (table != null): sequence b holds seq_lens[b] positions (at
+  // most len), logical block j in page table[b * tstride + j] (< n_pages)
+  const int32_t* table;
+  const int32_t* seq_lens;
+  int64_t tstride, n_pages;
 };
 
 __device__ __forceinline__ void mma_u8s8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
@@ -495,8 +563,18 @@ __global__ void __launch_bounds__((kDecWarps + 1) * 32, FT_KV_MIN_BLOCKS)
   int nheads = p.G - 4 * hg;
   if (nheads > 4) nheads = 4;
   const int64_t qh0 = kvh * p.G + 4 * hg;  // first q head of this CTA
+  // live positions and logical blocks of this sequence
+  int64_t len_b = p.len, nlb_b = p.nlb;
+  if (p.table) {
+    len_b = p.seq_lens[b];
+    if (len_b < 0 || len_b > p.len) {
+      if (tid == 0) atomicCAS(p.err, 0, 1004);
+      len_b = len_b < 0 ? 0 : p.len;
+    }
+    nlb_b = (len_b + kBlk - 1) / kBlk;
+  }
 
-  const int64_t ntiles_all = (p.nlb + kDecWarps - 1) / kDecWarps;
+  const int64_t ntiles_all = (nlb_b + kDecWarps - 1) / kDecWarps;
   const int64_t t_begin = (int64_t)split * p.tiles_per;
   int64_t t_end = t_begin + p.tiles_per;
   if (t_end > ntiles_all) t_end = ntiles_all;
@@ -576,18 +654,29 @@ __global__ void __launch_bounds__((kDecWarps + 1) * 32, FT_KV_MIN_BLOCKS)
           ok = tc::mbar_wait(empty0 + 8 * s, ((it / kStages) - 1) & 1, p.err, 31);
         if (!ok) break;
         const int64_t j0 = (t_begin + it) * kDecWarps;
-        const int nb = p.nlb - j0 < kDecWarps ? (int)(p.nlb - j0) : kDecWarps;
+        const int nb = nlb_b - j0 < kDecWarps ? (int)(nlb_b - j0) : kDecWarps;
         tc::mbar_arrive_expect_tx(full0 + 8 * s, nb * kRecBytes);
         const uint32_t sb = stage_base + s * kStageBytes;
-        // nb consecutive records from physical block pb, wrapping at most once
-        const int n1 = pb + nb <= p.nbc ? nb : (int)(p.nbc - pb);
-        tc::bulk_g2s(sb, p.blocks + (row * p.nbc + pb) * kRecWords, n1 * kRecBytes,
-                     full0 + 8 * s);
-        if (n1 < nb)
-          tc::bulk_g2s(sb + n1 * kRecBytes, p.blocks + row * p.nbc * kRecWords,
-                       (nb - n1) * kRecBytes, full0 + 8 * s);
-        pb += nb;
-        if (pb >= p.nbc) pb -= p.nbc;
+        if (p.table) {
+          // one record per page; a bad table entry reads page 0 (the launch
+          // is reported invalid through the error word)
+          for (int i = 0; i < nb; ++i) {
+            int64_t pg = checked_page(p.table, b * p.tstride + j0 + i, p.n_pages, p.err, 1005);
+            if (pg < 0) pg = 0;
+            tc::bulk_g2s(sb + i * kRecBytes, p.blocks + (pg * p.Hkv + kvh) * kRecWords,
+                         kRecBytes, full0 + 8 * s);
+          }
+        } else {
+          // nb consecutive records from physical block pb, wrapping at most once
+          const int n1 = pb + nb <= p.nbc ? nb : (int)(p.nbc - pb);
+          tc::bulk_g2s(sb, p.blocks + (row * p.nbc + pb) * kRecWords, n1 * kRecBytes,
+                       full0 + 8 * s);
+          if (n1 < nb)
+            tc::bulk_g2s(sb + n1 * kRecBytes, p.blocks + row * p.nbc * kRecWords,
+                         (nb - n1) * kRecBytes, full0 + 8 * s);
+          pb += nb;
+          if (pb >= p.nbc) pb -= p.nbc;
+        }
         ++issued;
       }
       // the copies of the last stages must land before the CTA may exit
@@ -635,7 +724,7 @@ __global__ void __launch_bounds__((kDecWarps + 1) * 32, FT_KV_MIN_BLOCKS)
   };
 
   // 32-bit block arithmetic: the host keeps head_off + len below 2^31 - 64
-  const int nlb32 = (int)p.nlb, hoff = (int)p.head_off, len32 = (int)p.len;
+  const int nlb32 = (int)nlb_b, hoff = p.table ? 0 : (int)p.head_off, len32 = (int)len_b;
   int j = (int)(t_begin * kDecWarps) + warp;  // logical block of this warp in tile `it`
   for (int it = 0; it < ntiles; ++it, j += kDecWarps) {
     const int s = it % kStages;
@@ -874,7 +963,7 @@ __global__ void kv3_combine_kernel(const float* __restrict__ part, int nsplit,
     l = fmaf(pp[s * kPart + 1], f, l);
     a = fmaf(pp[s * kPart + 2 + d], f, a);
   }
-  float r = a / l;
+  float r = l > 0.0f ? a / l : 0.0f;  // l == 0: an empty paged sequence
   if (signs) {
     __shared__ float y[kD];
     y[d] = r;
@@ -989,8 +1078,26 @@ int append_common(ft_kv3* c, int64_t n_pos, const AppendParams& proto, bool pack
   return FT_OK;
 }
 
+// The 128 mode-T signs from SplitMix64(seed) (bit 63 of each draw set -> -1),
+// uploaded to a new device array.
+cudaError_t upload_signs(uint64_t seed, float** out) {
+  std::vector<float> sg(kD);
+  uint64_t z = seed;
+  for (int i = 0; i < kD; ++i) {
+    z += 0x9e3779b97f4a7c15ull;
+    uint64_t r = z;
+    r = (r ^ (r >> 30)) * 0xbf58476d1ce4e5b9ull;
+    r = (r ^ (r >> 27)) * 0x94d049bb133111ebull;
+    r ^= r >> 31;
+    sg[i] = (r >> 63) ? -1.0f : 1.0f;
+  }
+  cudaError_t e = cudaMalloc(out, kD * sizeof(float));
+  if (e == cudaSuccess) e = cudaMemcpy(*out, sg.data(), kD * sizeof(float), cudaMemcpyHostToDevice);
+  return e;
+}
+
 RangeParams range_params(const ft_kv3* c, int64_t start, int64_t n) {
-  RangeParams p;
+  RangeParams p{};
   p.B = c->batch;
   p.Hkv = c->kv_heads;
   p.cap = c->cap;
@@ -1042,20 +1149,8 @@ int ft_kv3_create_mode(ft_ctx* ctx, int64_t batch, int64_t kv_heads, int64_t hea
   int st = ft_kv3_create(ctx, batch, kv_heads, head_dim, max_seq, out);
   if (st != FT_OK || mode == 0) return st;
   ft_kv3* c = *out;
-  // the 128 signs from SplitMix64(seed): bit 63 of each draw set -> -1
-  std::vector<float> sg(kD);
-  uint64_t z = seed;
-  for (int i = 0; i < kD; ++i) {
-    z += 0x9e3779b97f4a7c15ull;
-    uint64_t r = z;
-    r = (r ^ (r >> 30)) * 0xbf58476d1ce4e5b9ull;
-    r = (r ^ (r >> 27)) * 0x94d049bb133111ebull;
-    r ^= r >> 31;
-    sg[i] = (r >> 63) ? -1.0f : 1.0f;
-  }
   DeviceScope scope(c->device);
-  cudaError_t e = cudaMalloc(&c->signs, kD * sizeof(float));
-  if (e == cudaSuccess) e = cudaMemcpy(c->signs, sg.data(), kD * sizeof(float), cudaMemcpyHostToDevice);
+  cudaError_t e = upload_signs(seed, &c->signs);
   if (e != cudaSuccess) {
     ft_kv3_destroy(c);
     *out = nullptr;
@@ -1174,58 +1269,57 @@ int ft_kv3_export_range(ft_ctx* ctx, const ft_kv3* c, int64_t start, int64_t end
   return FT_OK;
 }
 
-int ft_flash_decode_3bit(ft_ctx* ctx, ft_kv3* c, const float* q_dev, int64_t q_heads, float scale,
-                         float* out_dev, void* stream) {
-  FT_CHECK(ctx && c && q_dev && out_dev, FT_ERR_SHAPE, "null argument");
-  FT_CHECK(q_heads > 0 && q_heads % c->kv_heads == 0, FT_ERR_SHAPE,
-           "q_heads (%lld) must be a multiple of kv_heads (%lld)", (long long)q_heads,
-           (long long)c->kv_heads);
-  FT_CHECK(c->len > 0, FT_ERR_SHAPE, "flash decode over an empty cache");
-  FT_CHECK(c->len + kBlk < (int64_t)INT32_MAX - 64, FT_ERR_UNSUPPORTED,
-           "cache too long for the decode's 32-bit slot arithmetic");
-  DeviceScope scope(c->device);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  DecodeParams p{};
+}  // extern "C"
+
+namespace ft {
+namespace {
+
+// Grows a workspace outside stream capture (a capture may only reuse it).
+int ensure_ws(Workspace& w, size_t need, cudaStream_t s, const char* what) {
+  if (w.bytes >= need) return FT_OK;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (s) cudaStreamIsCapturing(s, &cs);
+  FT_CHECK(cs == cudaStreamCaptureStatusNone, FT_ERR_UNSUPPORTED,
+           "the %s buffer must grow but the stream is being captured", what);
+  if (w.ptr) {
+    FT_CUDA(cudaStreamSynchronize(s));
+    FT_CUDA(cudaFree(w.ptr));
+    w.ptr = nullptr;
+    w.bytes = 0;
+  }
+  FT_CUDA(cudaMalloc(&w.ptr, need));
+  w.bytes = need;
+  return FT_OK;
+}
+
+// Rotates q (mode T), picks the split of the slots, launches the decode and
+// the combine.  p carries the cache geometry (ring or paged); p.len is the
+// longest sequence.
+int launch_decode(ft_ctx* ctx, DecodeParams p, int64_t batch, int64_t kv_heads, int64_t q_heads,
+                  const float* signs, Workspace& part, Workspace& rot, const float* q_dev,
+                  float scale, float* out_dev, cudaStream_t s) {
   p.q = q_dev;
-  if (c->signs) {
+  if (signs) {
     // mode T: attention runs in the rotated domain
-    const size_t qb = (size_t)(c->batch * q_heads * kD) * 4;
-    if (c->rot.bytes < qb) {
-      cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-      if (s) cudaStreamIsCapturing(s, &cs);
-      FT_CHECK(cs == cudaStreamCaptureStatusNone, FT_ERR_UNSUPPORTED,
-               "the rotated-query buffer must grow but the stream is being captured");
-      if (c->rot.ptr) {
-        FT_CUDA(cudaStreamSynchronize(s));
-        FT_CUDA(cudaFree(c->rot.ptr));
-        c->rot.ptr = nullptr;
-        c->rot.bytes = 0;
-      }
-      FT_CUDA(cudaMalloc(&c->rot.ptr, qb));
-      c->rot.bytes = qb;
-    }
-    kv3_rotate_kernel<<<(unsigned)(c->batch * q_heads), kD, 0, s>>>(
-        q_dev, static_cast<float*>(c->rot.ptr), c->signs, 0);
+    const int rc = ensure_ws(rot, (size_t)(batch * q_heads * kD) * 4, s, "rotated-query");
+    if (rc != FT_OK) return rc;
+    kv3_rotate_kernel<<<(unsigned)(batch * q_heads), kD, 0, s>>>(
+        q_dev, static_cast<float*>(rot.ptr), signs, 0);
     FT_LAUNCH_CHECK();
-    p.q = static_cast<const float*>(c->rot.ptr);
+    p.q = static_cast<const float*>(rot.ptr);
   }
   p.Hq = q_heads;
-  p.Hkv = c->kv_heads;
-  p.G = (int)(q_heads / c->kv_heads);
+  p.Hkv = kv_heads;
+  p.G = (int)(q_heads / kv_heads);
   p.hgroups = (p.G + 3) / 4;
-  p.nbc = c->cap / kBlk;
-  p.head_off = c->head % kBlk;
-  p.head_blk = c->head / kBlk;
-  p.len = c->len;
-  p.nlb = (p.head_off + c->len + kBlk - 1) / kBlk;
+  p.nlb = (p.head_off + p.len + kBlk - 1) / kBlk;
   const float sc = scale > 0.0f ? scale : 1.0f / sqrtf((float)kD);
   p.qk_log2 = sc * 1.4426950408889634f;
-  p.blocks = c->blocks;
   p.err = ctx->err_word;
   // split choice: minimise waves x (tiles per CTA + per-CTA overhead); at most
   // 2^15 tiles (2^20 slots, 2^18 per warp) per CTA keeps every int32 digit sum
   // exact (7 * 255 * 2^18 < 2^31)
-  const int64_t units = c->batch * c->kv_heads * p.hgroups;
+  const int64_t units = batch * kv_heads * p.hgroups;
   const int64_t ntiles = (p.nlb + kDecWarps - 1) / kDecWarps;
   const int64_t resident = (int64_t)decode_occupancy(ctx->device) * ctx->num_sms;
   int64_t best_cost = INT64_MAX, best_per = ntiles;
@@ -1243,31 +1337,260 @@ int ft_flash_decode_3bit(ft_ctx* ctx, ft_kv3* c, const float* q_dev, int64_t q_h
   FT_CHECK(best_per <= 32768, FT_ERR_UNSUPPORTED, "cache too long for one decode launch");
   p.tiles_per = best_per;
   const int64_t nsplit = ceil_div(ntiles, best_per);
-  FT_CHECK(nsplit <= 65535 && c->kv_heads * p.hgroups <= 65535 && c->batch <= 65535,
+  FT_CHECK(nsplit <= 65535 && kv_heads * p.hgroups <= 65535 && batch <= 65535,
            FT_ERR_UNSUPPORTED, "decode grid too large");
-  const size_t need = (size_t)(c->batch * q_heads * nsplit * kPart) * 4;
-  if (c->part.bytes < need) {
-    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-    if (s) cudaStreamIsCapturing(s, &cs);
-    FT_CHECK(cs == cudaStreamCaptureStatusNone, FT_ERR_UNSUPPORTED,
-             "the decode partials buffer must grow but the stream is being captured");
-    if (c->part.ptr) {
-      FT_CUDA(cudaStreamSynchronize(s));
-      FT_CUDA(cudaFree(c->part.ptr));
-      c->part.ptr = nullptr;
-      c->part.bytes = 0;
-    }
-    FT_CUDA(cudaMalloc(&c->part.ptr, need));
-    c->part.bytes = need;
-  }
-  p.part = static_cast<float*>(c->part.ptr);
-  dim3 grid((unsigned)nsplit, (unsigned)(c->kv_heads * p.hgroups), (unsigned)c->batch);
+  const int rc = ensure_ws(part, (size_t)(batch * q_heads * nsplit * kPart) * 4, s,
+                           "decode partials");
+  if (rc != FT_OK) return rc;
+  p.part = static_cast<float*>(part.ptr);
+  dim3 grid((unsigned)nsplit, (unsigned)(kv_heads * p.hgroups), (unsigned)batch);
   kv3_decode_kernel<<<grid, (kDecWarps + 1) * 32, kDecSmem, s>>>(p);
   FT_LAUNCH_CHECK();
-  kv3_combine_kernel<<<(unsigned)(c->batch * q_heads), kD, 0, s>>>(p.part, (int)nsplit, out_dev,
-                                                                     c->signs);
+  kv3_combine_kernel<<<(unsigned)(batch * q_heads), kD, 0, s>>>(p.part, (int)nsplit, out_dev,
+                                                                  signs);
   FT_LAUNCH_CHECK();
   return FT_OK;
+}
+
+}  // namespace
+}  // namespace ft
+
+extern "C" {
+
+int ft_flash_decode_3bit(ft_ctx* ctx, ft_kv3* c, const float* q_dev, int64_t q_heads, float scale,
+                         float* out_dev, void* stream) {
+  FT_CHECK(ctx && c && q_dev && out_dev, FT_ERR_SHAPE, "null argument");
+  FT_CHECK(q_heads > 0 && q_heads % c->kv_heads == 0, FT_ERR_SHAPE,
+           "q_heads (%lld) must be a multiple of kv_heads (%lld)", (long long)q_heads,
+           (long long)c->kv_heads);
+  FT_CHECK(c->len > 0, FT_ERR_SHAPE, "flash decode over an empty cache");
+  FT_CHECK(c->len + kBlk < (int64_t)INT32_MAX - 64, FT_ERR_UNSUPPORTED,
+           "cache too long for the decode's 32-bit slot arithmetic");
+  DeviceScope scope(c->device);
+  DecodeParams p{};
+  p.nbc = c->cap / kBlk;
+  p.head_off = c->head % kBlk;
+  p.head_blk = c->head / kBlk;
+  p.len = c->len;
+  p.blocks = c->blocks;
+  return launch_decode(ctx, p, c->batch, c->kv_heads, q_heads, c->signs, c->part, c->rot, q_dev,
+                       scale, out_dev, static_cast<cudaStream_t>(stream));
+}
+
+// ---- paged pool
+int ft_kvp_create(ft_ctx* ctx, int64_t num_pages, int64_t kv_heads, int64_t head_dim,
+                  int64_t page_size, int mode, uint64_t seed, ft_kvp** out) {
+  FT_CHECK(ctx && out, FT_ERR_SHAPE, "null argument");
+  *out = nullptr;
+  FT_CHECK(head_dim == kD, FT_ERR_UNSUPPORTED, "head_dim %lld: only 128 is supported",
+           (long long)head_dim);
+  FT_CHECK(page_size == kBlk, FT_ERR_UNSUPPORTED, "page_size %lld: only %d is supported",
+           (long long)page_size, kBlk);
+  FT_CHECK(num_pages > 0 && num_pages < INT32_MAX && kv_heads > 0 && kv_heads <= 65535,
+           FT_ERR_SHAPE, "bad pool shape (%lld pages, %lld kv heads)", (long long)num_pages,
+           (long long)kv_heads);
+  FT_CHECK(mode == 0 || mode == 1, FT_ERR_UNSUPPORTED, "mode must be 0 (reference) or 1 (T)");
+  DeviceScope scope(ctx->device);
+  ft_kvp* c = new ft_kvp();
+  c->device = ctx->device;
+  c->n_pages = num_pages;
+  c->kv_heads = kv_heads;
+  c->mode = mode;
+  const size_t bytes = (size_t)(num_pages * kv_heads) * kRecBytes;
+  cudaError_t e = cudaMalloc(&c->blocks, bytes);
+  if (e == cudaSuccess) e = cudaMemset(c->blocks, 0, bytes);
+  if (e == cudaSuccess && mode == 1) e = upload_signs(seed, &c->signs);
+  if (e != cudaSuccess) {
+    ft_kvp_destroy(c);
+    return fail(e == cudaErrorMemoryAllocation ? FT_ERR_OOM : FT_ERR_GPU,
+                "page pool of %lld pages failed: %s", (long long)num_pages, cudaGetErrorString(e));
+  }
+  *out = c;
+  return FT_OK;
+}
+
+int ft_kvp_destroy(ft_kvp* c) {
+  if (!c) return FT_OK;
+  DeviceScope scope(c->device);
+  cudaFree(c->blocks);
+  if (c->signs) cudaFree(c->signs);
+  if (c->part.ptr) cudaFree(c->part.ptr);
+  if (c->rot.ptr) cudaFree(c->rot.ptr);
+  delete c;
+  return FT_OK;
+}
+
+int ft_kvp_signs(const ft_kvp* c, float* signs_host) {
+  FT_CHECK(c && signs_host, FT_ERR_SHAPE, "null argument");
+  FT_CHECK(c->signs, FT_ERR_UNSUPPORTED, "the pool is not in mode T");
+  DeviceScope scope(c->device);
+  FT_CUDA(cudaMemcpy(signs_host, c->signs, kD * sizeof(float), cudaMemcpyDeviceToHost));
+  return FT_OK;
+}
+
+static int kvp_append(ft_ctx* ctx, ft_kvp* c, int64_t batch, int64_t n_pos,
+                      const int32_t* tables_dev, int64_t table_stride,
+                      const int32_t* start_pos_dev, AppendParams p, bool packed, void* stream) {
+  FT_CHECK(ctx && c && tables_dev && start_pos_dev, FT_ERR_SHAPE, "null argument");
+  FT_CHECK(batch >= 0 && batch <= 65535 && n_pos >= 0 && table_stride > 0, FT_ERR_SHAPE,
+           "bad append shape (batch %lld, %lld positions, table stride %lld)", (long long)batch,
+           (long long)n_pos, (long long)table_stride);
+  if (batch == 0 || n_pos == 0) return FT_OK;
+  FT_CHECK(n_pos <= table_stride * kBlk, FT_ERR_SHAPE,
+           "%lld positions do not fit a block table of %lld pages", (long long)n_pos,
+           (long long)table_stride);
+  DeviceScope scope(c->device);
+  p.n_pos = n_pos;
+  p.Hkv = c->kv_heads;
+  p.blocks = c->blocks;
+  p.signs = packed ? nullptr : c->signs;
+  p.table = tables_dev;
+  p.pos0 = start_pos_dev;
+  p.tstride = table_stride;
+  p.n_pages = c->n_pages;
+  p.err = ctx->err_word;
+  const int64_t nblk = (kBlk - 1 + n_pos + kBlk - 1) / kBlk;  // most blocks one sequence touches
+  dim3 grid((unsigned)nblk, (unsigned)(batch * c->kv_heads));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (packed)
+    kv3_append_kernel<true><<<grid, kD, 0, s>>>(p);
+  else
+    kv3_append_kernel<false><<<grid, kD, 0, s>>>(p);
+  FT_LAUNCH_CHECK();
+  return FT_OK;
+}
+
+int ft_kvp_append(ft_ctx* ctx, ft_kvp* c, int64_t batch, int64_t n_pos, const int32_t* tables_dev,
+                  int64_t table_stride, const int32_t* start_pos_dev, const void* k_dev,
+                  const void* v_dev, int is_bf16, void* stream) {
+  FT_CHECK(n_pos == 0 || batch == 0 || (k_dev && v_dev), FT_ERR_SHAPE, "null argument");
+  AppendParams p{};
+  p.k = k_dev;
+  p.v = v_dev;
+  p.bf16 = is_bf16 ? 1 : 0;
+  return kvp_append(ctx, c, batch, n_pos, tables_dev, table_stride, start_pos_dev, p, false,
+                    stream);
+}
+
+int ft_kvp_append_packed(ft_ctx* ctx, ft_kvp* c, int64_t batch, int64_t n_pos,
+                         const int32_t* tables_dev, int64_t table_stride,
+                         const int32_t* start_pos_dev, const uint8_t* k_codes_dev,
+                         const float* k_minmax_dev, const uint8_t* v_codes_dev,
+                         const float* v_minmax_dev, void* stream) {
+  FT_CHECK(n_pos == 0 || batch == 0 ||
+               (k_codes_dev && k_minmax_dev && v_codes_dev && v_minmax_dev),
+           FT_ERR_SHAPE, "null argument");
+  AppendParams p{};
+  p.k = k_codes_dev;
+  p.v = v_codes_dev;
+  p.kmm_in = k_minmax_dev;
+  p.vmm_in = v_minmax_dev;
+  return kvp_append(ctx, c, batch, n_pos, tables_dev, table_stride, start_pos_dev, p, true,
+                    stream);
+}
+
+int ft_kvp_copy_pages(ft_ctx* ctx, ft_kvp* c, int64_t n, const int32_t* src_pages_host,
+                      const int32_t* dst_pages_host, void* stream) {
+  FT_CHECK(ctx && c && (n == 0 || (src_pages_host && dst_pages_host)), FT_ERR_SHAPE,
+           "null argument");
+  const size_t pb = (size_t)c->kv_heads * kRecBytes;
+  for (int64_t i = 0; i < n; ++i) {
+    const int64_t a = src_pages_host[i], b = dst_pages_host[i];
+    FT_CHECK(a >= 0 && a < c->n_pages && b >= 0 && b < c->n_pages, FT_ERR_SHAPE,
+             "page copy %lld -> %lld outside the pool of %lld pages", (long long)a, (long long)b,
+             (long long)c->n_pages);
+  }
+  DeviceScope scope(c->device);
+  uint8_t* base = reinterpret_cast<uint8_t*>(c->blocks);
+  for (int64_t i = 0; i < n; ++i) {
+    if (src_pages_host[i] == dst_pages_host[i]) continue;
+    FT_CUDA(cudaMemcpyAsync(base + dst_pages_host[i] * pb, base + src_pages_host[i] * pb, pb,
+                            cudaMemcpyDeviceToDevice, static_cast<cudaStream_t>(stream)));
+  }
+  return FT_OK;
+}
+
+static int kvp_range(ft_ctx* ctx, const ft_kvp* c, int64_t batch, const int32_t* tables_dev,
+                     int64_t table_stride, int64_t start, int64_t end, RangeParams* p) {
+  FT_CHECK(ctx && c && tables_dev, FT_ERR_SHAPE, "null argument");
+  FT_CHECK(batch >= 0 && table_stride > 0 && 0 <= start && start <= end &&
+               end <= table_stride * kBlk,
+           FT_ERR_SHAPE, "range [%lld, %lld) outside block tables of %lld pages",
+           (long long)start, (long long)end, (long long)table_stride);
+  *p = RangeParams{};
+  p->B = batch;
+  p->Hkv = c->kv_heads;
+  p->cap = 1;
+  p->nbc = 1;
+  p->start = start;
+  p->n = end - start;
+  p->blocks = c->blocks;
+  p->table = tables_dev;
+  p->tstride = table_stride;
+  p->n_pages = c->n_pages;
+  p->err = ctx->err_word;
+  return FT_OK;
+}
+
+int ft_kvp_get_range(ft_ctx* ctx, const ft_kvp* c, int64_t batch, const int32_t* tables_dev,
+                     int64_t table_stride, int64_t start, int64_t end, float* k_out_dev,
+                     float* v_out_dev, void* stream) {
+  RangeParams p;
+  const int rc = kvp_range(ctx, c, batch, tables_dev, table_stride, start, end, &p);
+  if (rc != FT_OK) return rc;
+  FT_CHECK(k_out_dev && v_out_dev, FT_ERR_SHAPE, "null argument");
+  if (p.n == 0 || batch == 0) return FT_OK;
+  DeviceScope scope(c->device);
+  kv3_dequant_kernel<<<(unsigned)(batch * p.n * c->kv_heads), kD, 0,
+                       static_cast<cudaStream_t>(stream)>>>(p, k_out_dev, v_out_dev, c->signs);
+  FT_LAUNCH_CHECK();
+  return FT_OK;
+}
+
+int ft_kvp_export_range(ft_ctx* ctx, const ft_kvp* c, int64_t batch, const int32_t* tables_dev,
+                        int64_t table_stride, int64_t start, int64_t end, uint8_t* k_codes_dev,
+                        float* k_minmax_dev, uint8_t* v_codes_dev, float* v_minmax_dev,
+                        void* stream) {
+  RangeParams p;
+  const int rc = kvp_range(ctx, c, batch, tables_dev, table_stride, start, end, &p);
+  if (rc != FT_OK) return rc;
+  FT_CHECK(k_codes_dev && k_minmax_dev && v_codes_dev && v_minmax_dev, FT_ERR_SHAPE,
+           "null argument");
+  if (p.n == 0 || batch == 0) return FT_OK;
+  DeviceScope scope(c->device);
+  kv3_export_kernel<<<(unsigned)(batch * p.n * c->kv_heads), 16, 0,
+                      static_cast<cudaStream_t>(stream)>>>(p, k_codes_dev, k_minmax_dev,
+                                                           v_codes_dev, v_minmax_dev);
+  FT_LAUNCH_CHECK();
+  return FT_OK;
+}
+
+int ft_kvp_flash_decode(ft_ctx* ctx, ft_kvp* c, int64_t batch, const int32_t* tables_dev,
+                        int64_t table_stride, const int32_t* seq_lens_dev, int64_t max_seq_len,
+                        const float* q_dev, int64_t q_heads, float scale, float* out_dev,
+                        void* stream) {
+  FT_CHECK(ctx && c && tables_dev && seq_lens_dev && q_dev && out_dev, FT_ERR_SHAPE,
+           "null argument");
+  FT_CHECK(q_heads > 0 && q_heads % c->kv_heads == 0, FT_ERR_SHAPE,
+           "q_heads (%lld) must be a multiple of kv_heads (%lld)", (long long)q_heads,
+           (long long)c->kv_heads);
+  FT_CHECK(batch > 0 && max_seq_len > 0 && table_stride > 0 &&
+               max_seq_len <= table_stride * kBlk,
+           FT_ERR_SHAPE, "bad decode shape (batch %lld, max_seq_len %lld, table stride %lld)",
+           (long long)batch, (long long)max_seq_len, (long long)table_stride);
+  FT_CHECK(max_seq_len + kBlk < (int64_t)INT32_MAX - 64, FT_ERR_UNSUPPORTED,
+           "sequence too long for the decode's 32-bit slot arithmetic");
+  DeviceScope scope(c->device);
+  DecodeParams p{};
+  p.nbc = 1;
+  p.len = max_seq_len;
+  p.blocks = c->blocks;
+  p.table = tables_dev;
+  p.seq_lens = seq_lens_dev;
+  p.tstride = table_stride;
+  p.n_pages = c->n_pages;
+  return launch_decode(ctx, p, batch, c->kv_heads, q_heads, c->signs, c->part, c->rot, q_dev,
+                       scale, out_dev, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

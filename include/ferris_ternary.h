@@ -46,6 +46,7 @@ typedef struct ft_ctx ft_ctx;       /* one CUDA device + workspace */
 typedef struct ft_weight ft_weight; /* one dense ternary matrix resident in HBM */
 typedef struct ft_moe ft_moe;       /* one ternary MoE FFN layer resident in HBM */
 typedef struct ft_kv3 ft_kv3;       /* one layer's 3-bit KV cache resident in HBM */
+typedef struct ft_kvp ft_kvp;       /* page pool of the paged 3-bit KV cache */
 
 /* ---- library / context ------------------------------------------------ */
 const char* ft_version(void);
@@ -369,6 +370,63 @@ int ft_kv3_export_range(ft_ctx* ctx, const ft_kv3* c, int64_t start, int64_t end
  * with the GQA head map of cpu_attention_raw (src/model/cpu_block_attn_res.rs:471-472). */
 int ft_flash_decode_3bit(ft_ctx* ctx, ft_kv3* c, const float* q_dev, int64_t q_heads, float scale,
                          float* out_dev, void* stream);
+
+/* ---- paged 3-bit KV cache: the GPU storage behind PagedAttention
+ * (src/inference/paged_attention.rs).  The reference keeps only the metadata
+ * there -- BlockAllocator (:44-150) hands out block ids, a BlockTable (:158-224)
+ * per request and layer maps logical block j to a block id, fork_request
+ * (:449-472) shares blocks by reference count -- and creates no GPU buffers.
+ * An ft_kvp is that missing pool: block id P is page P, 32 positions of every
+ * kv head in the ring cache's record format (same quantisation, both modes).
+ * The calls below take the caller's tables as a device int32 array
+ * [batch][table_stride] (row b = BlockTable::table() of sequence b, padded)
+ * and read or write through them; the allocator, reference counts and
+ * copy-on-write stay with the caller (the Python mirror in
+ * ferrisres_b200/paged.py, or the reference's own manager).  Page ids and
+ * positions read on the device are bounds-checked: a bad entry is skipped and
+ * reported by ft_ctx_check as FT_ERR_SHAPE.  page_size must be 32 (the
+ * reference's default is 16), head_dim 128.  mode / seed as ft_kv3_create_mode.
+ * Replaces BlockAllocator::new's pool (:58) on the device side. */
+int ft_kvp_create(ft_ctx* ctx, int64_t num_pages, int64_t kv_heads, int64_t head_dim,
+                  int64_t page_size, int mode, uint64_t seed, ft_kvp** out);
+int ft_kvp_destroy(ft_kvp* pool);
+int ft_kvp_signs(const ft_kvp* pool, float* signs_host);
+/* Writes n_pos positions of each of `batch` sequences: sequence b's at
+ * positions start_pos[b] .. start_pos[b] + n_pos - 1 (start_pos int32 on the
+ * device), through its table row.  k, v [batch, n_pos, kv_heads, 128] fp32
+ * (bf16 bit patterns when is_bf16), quantised as ft_kv3_append.  The pages a
+ * call writes must not be shared between its sequences (copy them first:
+ * ft_kvp_copy_pages). */
+int ft_kvp_append(ft_ctx* ctx, ft_kvp* pool, int64_t batch, int64_t n_pos,
+                  const int32_t* tables_dev, int64_t table_stride, const int32_t* start_pos_dev,
+                  const void* k_dev, const void* v_dev, int is_bf16, void* stream);
+/* Same with positions already in the reference's stored form (see
+ * ft_kv3_append_packed). */
+int ft_kvp_append_packed(ft_ctx* ctx, ft_kvp* pool, int64_t batch, int64_t n_pos,
+                         const int32_t* tables_dev, int64_t table_stride,
+                         const int32_t* start_pos_dev, const uint8_t* k_codes_dev,
+                         const float* k_minmax_dev, const uint8_t* v_codes_dev,
+                         const float* v_minmax_dev, void* stream);
+/* Copy-on-write: page dst[i] := page src[i] (host arrays of page ids), one
+ * device copy each, on `stream`. */
+int ft_kvp_copy_pages(ft_ctx* ctx, ft_kvp* pool, int64_t n, const int32_t* src_pages_host,
+                      const int32_t* dst_pages_host, void* stream);
+/* Positions [start, end) of every sequence through its table: dequantised
+ * [batch, end-start, kv_heads, 128] fp32, or the reference's stored form. */
+int ft_kvp_get_range(ft_ctx* ctx, const ft_kvp* pool, int64_t batch, const int32_t* tables_dev,
+                     int64_t table_stride, int64_t start, int64_t end, float* k_out_dev,
+                     float* v_out_dev, void* stream);
+int ft_kvp_export_range(ft_ctx* ctx, const ft_kvp* pool, int64_t batch, const int32_t* tables_dev,
+                        int64_t table_stride, int64_t start, int64_t end, uint8_t* k_codes_dev,
+                        float* k_minmax_dev, uint8_t* v_codes_dev, float* v_minmax_dev,
+                        void* stream);
+/* Flash decode of `batch` sequences of ragged lengths seq_lens[b] (int32 on
+ * the device, 0 <= seq_lens[b] <= max_seq_len; an empty sequence gives 0):
+ * math, GQA map and output as ft_flash_decode_3bit. */
+int ft_kvp_flash_decode(ft_ctx* ctx, ft_kvp* pool, int64_t batch, const int32_t* tables_dev,
+                        int64_t table_stride, const int32_t* seq_lens_dev, int64_t max_seq_len,
+                        const float* q_dev, int64_t q_heads, float scale, float* out_dev,
+                        void* stream);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

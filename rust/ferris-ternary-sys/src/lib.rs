@@ -22,6 +22,10 @@ pub struct ft_moe {
 pub struct ft_kv3 {
     _p: [u8; 0],
 }
+#[repr(C)]
+pub struct ft_kvp {
+    _p: [u8; 0],
+}
 
 /// Status codes (map onto FerrisResError, src/error.rs:3-36).
 pub const FT_OK: c_int = 0;
@@ -88,4 +92,13 @@ extern "C" {
     pub fn ft_kv3_get_range(ctx: *mut ft_ctx, c: *const ft_kv3, start: i64, end: i64, k_out_dev: *mut f32, v_out_dev: *mut f32, stream: *mut c_void) -> c_int;
     pub fn ft_kv3_export_range(ctx: *mut ft_ctx, c: *const ft_kv3, start: i64, end: i64, k_codes_dev: *mut u8, k_minmax_dev: *mut f32, v_codes_dev: *mut u8, v_minmax_dev: *mut f32, stream: *mut c_void) -> c_int;
     pub fn ft_flash_decode_3bit(ctx: *mut ft_ctx, c: *mut ft_kv3, q_dev: *const f32, q_heads: i64, scale: f32, out_dev: *mut f32, stream: *mut c_void) -> c_int;
+    pub fn ft_kvp_create(ctx: *mut ft_ctx, num_pages: i64, kv_heads: i64, head_dim: i64, page_size: i64, mode: c_int, seed: u64, out: *mut *mut ft_kvp) -> c_int;
+    pub fn ft_kvp_destroy(pool: *mut ft_kvp) -> c_int;
+    pub fn ft_kvp_signs(pool: *const ft_kvp, signs_host: *mut f32) -> c_int;
+    pub fn ft_kvp_append(ctx: *mut ft_ctx, pool: *mut ft_kvp, batch: i64, n_pos: i64, tables_dev: *const i32, table_stride: i64, start_pos_dev: *const i32, k_dev: *const c_void, v_dev: *const c_void, is_bf16: c_int, stream: *mut c_void) -> c_int;
+    pub fn ft_kvp_append_packed(ctx: *mut ft_ctx, pool: *mut ft_kvp, batch: i64, n_pos: i64, tables_dev: *const i32, table_stride: i64, start_pos_dev: *const i32, k_codes_dev: *const u8, k_minmax_dev: *const f32, v_codes_dev: *const u8, v_minmax_dev: *const f32, stream: *mut c_void) -> c_int;
+    pub fn ft_kvp_copy_pages(ctx: *mut ft_ctx, pool: *mut ft_kvp, n: i64, src_pages_host: *const i32, dst_pages_host: *const i32, stream: *mut c_void) -> c_int;
+    pub fn ft_kvp_get_range(ctx: *mut ft_ctx, pool: *const ft_kvp, batch: i64, tables_dev: *const i32, table_stride: i64, start: i64, end: i64, k_out_dev: *mut f32, v_out_dev: *mut f32, stream: *mut c_void) -> c_int;
+    pub fn ft_kvp_export_range(ctx: *mut ft_ctx, pool: *const ft_kvp, batch: i64, tables_dev: *const i32, table_stride: i64, start: i64, end: i64, k_codes_dev: *mut u8, k_minmax_dev: *mut f32, v_codes_dev: *mut u8, v_minmax_dev: *mut f32, stream: *mut c_void) -> c_int;
+    pub fn ft_kvp_flash_decode(ctx: *mut ft_ctx, pool: *mut ft_kvp, batch: i64, tables_dev: *const i32, table_stride: i64, seq_lens_dev: *const i32, max_seq_len: i64, q_dev: *const f32, q_heads: i64, scale: f32, out_dev: *mut f32, stream: *mut c_void) -> c_int;
 }
