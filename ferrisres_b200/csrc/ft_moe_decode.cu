@@ -4,18 +4,22 @@
 // makes several per expert: src/model/cpu_block_attn_res.rs:2284-2316).
 //
 // Phases, separated by grid-wide barriers (bounded waits):
-//   R  router scores: one warp per (token, expert), fp32 dot in lane order
-//      then a butterfly -- barrier;
-//   S  every CTA routes every token (softmax, stable descending top-k,
-//      renormalised gates: the reference's sequential order) and builds the
-//      tokens' int8-digit operand in shared memory;
+//   R  router partial scores: one warp per (expert, 256-wide K part) loads
+//      that part of the router row once and dots it with every token (fp32,
+//      8 products per lane in order, then a butterfly) -- barrier;
+//   S  every CTA sums the parts in order and routes every token (softmax,
+//      stable descending top-k, renormalised gates: the reference's
+//      sequential order) and builds the tokens' int8-digit operand in shared
+//      memory;
 //   G  gate||up: work units are (pair = token x chosen expert, 64-row block);
 //      a CTA's 8 warps split the unit's 128-K chunks, each streams its chunks'
 //      2-bit codes with 16-byte loads and runs mma.sync m16n8k32 (u8 codes AND
 //      the slot mask x s8 digits, exact int32), the warps' sums meet in shared
 //      memory and the unit's 64 outputs go to global scratch -- barrier;
+//      CTAs without a G unit meanwhile pull the chosen experts' down
+//      weights into L2 (bulk prefetch);
 //   H  every CTA forms h = SwiGLU(gate, up) (or GeLU-tanh) of every pair and
-//      its operand;
+//      its operand, one warp per pair;
 //   D  down projection, same scheme -- barrier;
 //   C  y[t] = sum_k w[t,k] * o[t,k] in top-k order.
 // Activations use 4 base-256 digits per token (the MoE's tolerance, 1e-4 of
@@ -36,12 +40,14 @@ constexpr int kMdRows = 64;  // rows per work unit (4 m-blocks of 16)
 
 struct MdParams {
   int T, K, E, use_gelu, x_bf16;
+  int nparts;  // 256-wide K parts of the router dot
+  int x_vec;   // H % 8 == 0 and x 16-byte aligned: vector loads
   int64_t H, F;
   int64_t nch_h, nch_f;   // 128-K chunks of H and of F
   const void* x;          // [T, H]
   const float* router;    // [E, H]
   const void* const* tab; // [4][E]: gate_up codes, gate_up scales, down codes, down scales
-  float* logits;          // [T, E]
+  float* logits;          // [T, E, nparts] partial router scores
   float* gu;              // [P, 2F]
   float* o;               // [P, H]
   int32_t* topk_idx;      // [T, K] (output)
@@ -83,13 +89,12 @@ __device__ bool grid_sync(unsigned* bar, unsigned& gen, int* err, int site) {
       atomicAdd(&bar[1], 1u);
     } else {
       const unsigned long long t0 = tc::globaltimer();
-      while (atomicAdd(&bar[1], 0u) == gen) {
-        if (tc::globaltimer() - t0 > 2000000000ull) {
+      for (unsigned it = 1; tc::ld_acquire_u32(&bar[1]) == gen; ++it) {
+        if ((it & 63u) == 0u && tc::globaltimer() - t0 > 2000000000ull) {
           atomicExch(err, site);
           ok = 0;
           break;
         }
-        __nanosleep(64);
       }
     }
     __threadfence();
@@ -151,6 +156,90 @@ __device__ void build_operand(Load load, int64_t n, int nchunks, int col, int nb
     if (lane == 0) atomicAdd(&colsum[col][d], v);
   }
   if (tid == 0) tok_scale[col] = a > 0.0f ? __longlong_as_double((long long)(1023 - sh) << 52) : 0.0;
+}
+
+// The 4 digit words of a quad of 4 consecutive values (x already scaled by
+// f1 * f2 when passed through digit_words).
+__device__ __forceinline__ void digit_words(const float (&v)[4], float f1, float f2,
+                                            uint32_t (&wd)[4]) {
+  uint32_t u[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e)
+    u[e] = (uint32_t)__float2int_rn(__fmul_rn(__fmul_rn(v[e], f1), f2)) + 0x808080u;
+  const uint32_t lo01 = __byte_perm(u[0], u[1], 0x5140), lo23 = __byte_perm(u[2], u[3], 0x5140);
+  const uint32_t hi01 = __byte_perm(u[0], u[1], 0x7362), hi23 = __byte_perm(u[2], u[3], 0x7362);
+  wd[0] = __byte_perm(lo01, lo23, 0x5410) ^ 0x80808080u;
+  wd[1] = __byte_perm(lo01, lo23, 0x7632) ^ 0x80808080u;
+  wd[2] = __byte_perm(hi01, hi23, 0x5410) ^ 0x80808080u;
+  wd[3] = __byte_perm(hi01, hi23, 0x7632);
+}
+
+// build_operand for one warp: the values stay in registers (kWq quads per
+// lane; longer rows are loaded again) and no block barrier is taken, so the
+// warps of a CTA build different rows at the same time.
+constexpr int kWq = 12;
+template <class Load>
+__device__ void warp_build_operand(Load load, int64_t n, int nchunks, int col, int nb,
+                                   uint32_t* frag, int* colsum4, double* tok_scale) {
+  const int lane = threadIdx.x & 31;
+  const int nquad = nchunks * 32;
+  auto quad = [&](int q, float (&x)[4]) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int64_t k = 4 * (int64_t)q + e;
+      float v = k < n ? load(k) : 0.0f;
+      x[e] = is_nonfinite(v) ? 0.0f : v;
+    }
+  };
+  float v[kWq][4];
+  float am = 0.0f;
+#pragma unroll
+  for (int i = 0; i < kWq; ++i) {
+    const int q = lane + 32 * i;
+    if (q < nquad) {
+      quad(q, v[i]);
+    } else {
+      v[i][0] = v[i][1] = v[i][2] = v[i][3] = 0.0f;
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) am = fmaxf(am, fabsf(v[i][e]));
+  }
+  for (int q = lane + 32 * kWq; q < nquad; q += 32) {
+    float x[4];
+    quad(q, x);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) am = fmaxf(am, fabsf(x[e]));
+  }
+  am = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(am)));
+  const int sh = am > 0.0f ? digit_shift(am, 4) : 0;
+  const int s1 = sh > 127 ? 127 : (sh < -126 ? -126 : sh);
+  const float f1 = __int_as_float((s1 + 127) << 23);
+  const float f2 = __int_as_float((sh - s1 + 127) << 23);
+  int cs[4] = {0, 0, 0, 0};
+  auto emit = [&](int q, const float (&x)[4]) {
+    uint32_t wd[4];
+    digit_words(x, f1, f2, wd);
+    const int base = frag_word(q, 4 * col, nb);
+#pragma unroll
+    for (int d = 0; d < 4; ++d) {
+      cs[d] = __dp4a((int)wd[d], 0x01010101, cs[d]);
+      frag[base + 16 * d] = wd[d];
+    }
+  };
+#pragma unroll
+  for (int i = 0; i < kWq; ++i)
+    if (lane + 32 * i < nquad) emit(lane + 32 * i, v[i]);
+  for (int q = lane + 32 * kWq; q < nquad; q += 32) {
+    float x[4];
+    quad(q, x);
+    emit(q, x);
+  }
+#pragma unroll
+  for (int d = 0; d < 4; ++d) {
+    const int c = __reduce_add_sync(0xffffffffu, cs[d]);
+    if (lane == 0) colsum4[d] = c;
+  }
+  if (lane == 0) *tok_scale = am > 0.0f ? __longlong_as_double((long long)(1023 - sh) << 52) : 0.0;
 }
 
 // One work unit: rows [64 rb, 64 rb + 64) of a tiled weight (codes, nch
@@ -238,28 +327,67 @@ __global__ void __launch_bounds__(kMdThreads, 1) moe_decode_kernel(const __grid_
   unsigned gen = 0;
   tc::pdl_wait();
 
-  // ---- R: router scores, one warp per (token, expert)
+  // ---- R: router partial scores, one warp per (expert, 256-wide K part)
   {
+    const int np = P.nparts;
     const int gw = blockIdx.x * kMdWarps + warp, nw = gridDim.x * kMdWarps;
-    for (int i = gw; i < T * E; i += nw) {
-      const int t = i / E, e = i % E;
-      const float* r = P.router + (int64_t)e * H;
-      float acc = 0.0f;
-      for (int64_t k = lane; k < H; k += 32) {
-        const float xv = P.x_bf16
-            ? __uint_as_float((uint32_t) static_cast<const uint16_t*>(P.x)[t * H + k] << 16)
-            : static_cast<const float*>(P.x)[t * H + k];
-        acc = __fadd_rn(acc, __fmul_rn(xv, r[k]));
-      }
+    for (int i = gw; i < E * np; i += nw) {
+      const int e = i / np, part = i % np;
+      const int64_t k0 = (int64_t)part * 256 + lane * 8;
+      const bool full = P.x_vec && k0 + 8 <= H;
+      const float* rr = P.router + (int64_t)e * H + k0;
+      float r[8];
+      if (full) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(rr));
+        const float4 b = __ldg(reinterpret_cast<const float4*>(rr) + 1);
+        r[0] = a.x; r[1] = a.y; r[2] = a.z; r[3] = a.w;
+        r[4] = b.x; r[5] = b.y; r[6] = b.z; r[7] = b.w;
+      } else {
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
-      if (lane == 0) P.logits[i] = acc;
+        for (int j = 0; j < 8; ++j) r[j] = k0 + j < H ? rr[j] : 0.0f;
+      }
+      for (int t = 0; t < T; ++t) {
+        float xv[8];
+        if (full && P.x_bf16) {
+          const uint4 u = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(P.x) + t * H + k0);
+          const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            xv[2 * j] = __uint_as_float(w4[j] << 16);
+            xv[2 * j + 1] = __uint_as_float(w4[j] & 0xffff0000u);
+          }
+        } else if (full) {
+          const float4* xp = reinterpret_cast<const float4*>(static_cast<const float*>(P.x) + t * H + k0);
+          const float4 a = xp[0], b = xp[1];
+          xv[0] = a.x; xv[1] = a.y; xv[2] = a.z; xv[3] = a.w;
+          xv[4] = b.x; xv[5] = b.y; xv[6] = b.z; xv[7] = b.w;
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int64_t k = k0 + j;
+            xv[j] = k >= H ? 0.0f
+                  : P.x_bf16 ? __uint_as_float((uint32_t) static_cast<const uint16_t*>(P.x)[t * H + k] << 16)
+                             : static_cast<const float*>(P.x)[t * H + k];
+          }
+        }
+        float acc = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc = __fadd_rn(acc, __fmul_rn(xv[j], r[j]));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
+        if (lane == 0) P.logits[((int64_t)t * E + e) * np + part] = acc;
+      }
     }
   }
   if (!grid_sync(P.bar, gen, P.err, 101)) return;
 
   // ---- S: routing of every token (the reference's sequential softmax / top-k)
-  for (int i = tid; i < T * E; i += kMdThreads) sc[i / E][i % E] = __ldcg(P.logits + i);
+  for (int i = tid; i < T * E; i += kMdThreads) {
+    const float* lp = P.logits + (int64_t)i * P.nparts;
+    float v = 0.0f;
+    for (int j = 0; j < P.nparts; ++j) v = __fadd_rn(v, __ldcg(lp + j));
+    sc[i / E][i % E] = v;
+  }
   if (tid < kMdMaxPairs * 4) colsum[tid >> 2][tid & 3] = 0;
   __syncthreads();
   if (tid < T) {
@@ -309,6 +437,19 @@ __global__ void __launch_bounds__(kMdThreads, 1) moe_decode_kernel(const __grid_
 
   // ---- G: gate||up of every (token, expert) pair
   const int64_t rb_gu = (2 * F + kMdRows - 1) / kMdRows;
+  if ((int64_t)blockIdx.x >= NP * rb_gu && tid == 0) {
+    // no G unit here: pull the chosen experts' down weights into L2 for D
+    const int64_t idle = gridDim.x - NP * rb_gu, me = blockIdx.x - NP * rb_gu;
+    const int64_t bytes = ((H + 127) / 128) * P.nch_f * 4096;  // tiled codes of one down weight
+    constexpr int64_t kPiece = 65536;
+    const int64_t pieces = (bytes + kPiece - 1) / kPiece;
+    for (int64_t j = me; j < NP * pieces; j += idle) {
+      const int p = (int)(j / pieces);
+      const int64_t off = (j % pieces) * kPiece;
+      const int64_t sz = bytes - off < kPiece ? bytes - off : kPiece;
+      tc::bulk_prefetch_l2(static_cast<const char*>(P.tab[2 * E + sel[p]]) + off, (uint32_t)sz);
+    }
+  }
   for (int64_t u = blockIdx.x; u < NP * rb_gu; u += gridDim.x) {
     const int p = (int)(u / rb_gu);
     const int64_t rb = u % rb_gu;
@@ -318,11 +459,9 @@ __global__ void __launch_bounds__(kMdThreads, 1) moe_decode_kernel(const __grid_
   }
   if (!grid_sync(P.bar, gen, P.err, 102)) return;
 
-  // ---- H: h = act(gate, up) of every pair as column block p
-  if (tid < kMdMaxPairs * 4) colsum[tid >> 2][tid & 3] = 0;
-  __syncthreads();
+  // ---- H: h = act(gate, up) of every pair as column block p, one warp per pair
   const int nbh = (NP + 1) / 2;
-  for (int p = 0; p < NP; ++p) {
+  for (int p = warp; p < NP; p += kMdWarps) {
     const float* gp = P.gu + (int64_t)p * 2 * F;
     const int gelu = P.use_gelu;
     auto act = [&](int64_t j) -> float {
@@ -335,7 +474,7 @@ __global__ void __launch_bounds__(kMdThreads, 1) moe_decode_kernel(const __grid_
       const float silu = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
       return __fmul_rn(silu, __ldcg(gp + F + j));
     };
-    build_operand(act, F, (int)P.nch_f, p, nbh, frag, colsum, tok_scale, red);
+    warp_build_operand(act, F, (int)P.nch_f, p, nbh, frag, colsum[p], &tok_scale[p]);
   }
   __syncthreads();
 
@@ -384,8 +523,9 @@ int moe_decode(ft_ctx* ctx, ft_moe* m, int64_t T, const void* x, int bf16, float
   const size_t smem = md_smem(T, m->top_k, nch_h, nch_f);
   FT_CHECK(smem <= 200 * 1024, FT_ERR_UNSUPPORTED, "layer too wide for the fused decode");
   const int64_t NP = T * m->top_k;
-  // scratch: logits | gu | o | barrier
-  const size_t off_gu = round_up((int64_t)(T * m->E * 4), 256);
+  // scratch: partial router scores | gu | o | barrier
+  const int nparts = (int)ceil_div(m->H, 256);
+  const size_t off_gu = round_up((int64_t)(T * m->E * nparts * 4), 256);
   const size_t off_o = off_gu + round_up(NP * 2 * m->F * 4, 256);
   const size_t off_bar = off_o + round_up(NP * m->H * 4, 256);
   const size_t need = off_bar + 256;
@@ -413,6 +553,8 @@ int moe_decode(ft_ctx* ctx, ft_moe* m, int64_t T, const void* x, int bf16, float
   P.E = (int)m->E;
   P.use_gelu = m->use_gelu;
   P.x_bf16 = bf16;
+  P.nparts = nparts;
+  P.x_vec = (m->H % 8 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) ? 1 : 0;
   P.H = m->H;
   P.F = m->F;
   P.nch_h = nch_h;

@@ -263,6 +263,19 @@ __device__ __forceinline__ void mma_commit(uint32_t bar) {
 }
 
 // Programmatic dependent launch controls (no-ops when launched without PDL).
+// Acquire load of a flag another CTA releases (a plain load: pollers do not
+// contend for the atomic unit).
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Hint: pull `bytes` (multiple of 16, 16-byte aligned address) into L2.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ void pdl_wait() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
 }

@@ -1,6 +1,7 @@
 """Expert-parallel MoE layer on 2 GPUs (NCCL over NVLink): every rank holds
 only its experts and routes its own tokens; the gathered result must equal
-the single-GPU layer bit for bit (same kernels, same per-token arithmetic).
+the single-GPU layer bit for bit (same kernels, same per-token arithmetic),
+and the single-GPU layer must match the oracle's TernaryMoELayer::forward.
 Skipped with fewer than 2 GPUs."""
 import os
 import socket
@@ -70,7 +71,17 @@ def test_ep_two_gpus_equals_single_gpu():
     E, H, F, world = 8, 512, 256, 2
     router, g, gs, u, us, d, ds, x = build_params(E, H, F)
     layer = moe.TernaryMoELayer.from_ternary(router, g, gs, u, us, d, ds, H, F, 2, device=0)
-    ref = layer.forward_device(x.cuda()).cpu().numpy()
+    ref_t, probs = layer.forward_device(x.cuda(), probs=True)
+    ref = ref_t.cpu().numpy()
+    # the single-GPU layer against the oracle's TernaryMoELayer::forward
+    # (near-tie rule of test_moe_gpu), so the bit-equal EP result is pinned too
+    from oracle import oracle as fo
+    from test_moe_gpu import check
+    T = x.shape[0]
+    xf = x.float().numpy()
+    oy, oroute, oprobs = fo.moe_forward(router, g, gs, u, us, d, ds, H, F, 2, xf.ravel(), T)
+    p = probs.cpu().numpy()
+    check(ref, np.argsort(-p, axis=1, kind="stable")[:, :2], p, oy, oroute, oprobs, T, H, 2, E)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
