@@ -77,28 +77,11 @@ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 // [2^(8D-3), 2^(8D-2)) and split X = round(x * 2^sh) into D signed base-256
 // digits (the top one within +-64).  D = 8 (the public fp32/bf16 entry points)
 // represents every element within 2^38 of the token's absmax exactly, so the
-// exact int32 digit sums give the correctly rounded dot product; D = 3 (the
-// MoE expert GEMMs, tolerance 1e-4 of the output rms) rounds every element to
-// a quantum of at most absmax * 2^-21, an error of at most absmax * 2^-22 per
-// element: over K products with |w| <= 1 the error of a row is at most
-// K * absmax * 2^-22 (2^-11 absmax at K = 2048, i.e. 1.3e-5 of the rms of a
-// Gaussian row's output, absmax / rms ~ 4), and typically sqrt(K) times less.
-// Three digits per token take 3 operand columns; five tokens share a 16-column
-// group (column 16 (t/5) + 3 (t%5) + d, the 16th column unused).
+// exact int32 digit sums give the correctly rounded dot product; D = 4 (the
+// MoE expert GEMMs, tolerance 1e-4 of the output rms) rounds elements below
+// absmax * 2^-6 to a quantum of absmax * 2^-30.
 constexpr int kDigitsExact = 8;
-constexpr int kDigitsMoE = 3;
-
-// Operand column of digit d of token slot t in a pass (D digits per token).
-__host__ __device__ constexpr int digit_col(int t, int d, int D) {
-  return D == 3 ? 16 * (t / 5) + 3 * (t % 5) + d : t * D + d;
-}
-// Token slots of a pass of npad columns, and the columns they span.
-__host__ __device__ constexpr int toks_per_pass(int npad, int D) {
-  return D == 3 ? (npad / 16) * 5 : npad / D;
-}
-__host__ __device__ constexpr int64_t pass_cols(int64_t tok, int D) {
-  return D == 3 ? (tok + 4) / 5 * 16 : tok * D;
-}
+constexpr int kDigitsMoE = 4;
 // Non-finite activation positions remembered per token; a token with more is
 // handled by scanning its whole row.
 constexpr int kNfCap = 16;

@@ -54,7 +54,7 @@ struct MdParams {
   float* topk_w;          // [T, K] (output)
   float* probs;           // [T, E] (optional output)
   float* y;               // [T, H] (output)
-  unsigned* bar;          // grid barrier: [count, generation], zero at launch
+  unsigned* bar;          // grid barrier: arrival counter, zero at launch
   int* err;
 };
 
@@ -75,30 +75,25 @@ __device__ __forceinline__ int frag_word(int q, int n, int nb) {
   return ((((c * nb + (n >> 3)) * 2 + (j >> 1)) * 32 + lane) << 2) + 2 * (j & 1) + kk;
 }
 
-// Grid-wide barrier with a bounded wait: the last CTA to arrive resets the
-// count and advances the generation.  Returns false everywhere when the wait
-// gave up (site recorded in *err).
-__device__ bool grid_sync(unsigned* bar, unsigned& gen, int* err, int site) {
+// Grid-wide barrier with a bounded wait: every CTA adds 1 to a counter that
+// the launch starts at zero and waits until it reaches `target` (advanced by
+// the grid size per barrier).  Returns false everywhere when the wait gave up
+// (site recorded in *err).
+__device__ bool grid_sync(unsigned* bar, unsigned& target, int* err, int site) {
   __syncthreads();
   int ok = 1;
   if (threadIdx.x == 0) {
+    target += gridDim.x;
     __threadfence();
-    if (atomicAdd(&bar[0], 1u) == gridDim.x - 1) {
-      atomicExch(&bar[0], 0u);
-      __threadfence();
-      atomicAdd(&bar[1], 1u);
-    } else {
-      const unsigned long long t0 = tc::globaltimer();
-      for (unsigned it = 1; tc::ld_acquire_u32(&bar[1]) == gen; ++it) {
-        if ((it & 63u) == 0u && tc::globaltimer() - t0 > 2000000000ull) {
-          atomicExch(err, site);
-          ok = 0;
-          break;
-        }
+    atomicAdd(bar, 1u);
+    const unsigned long long t0 = tc::globaltimer();
+    for (unsigned it = 1; tc::ld_acquire_u32(bar) < target; ++it) {
+      if ((it & 63u) == 0u && tc::globaltimer() - t0 > 2000000000ull) {
+        atomicExch(err, site);
+        ok = 0;
+        break;
       }
     }
-    __threadfence();
-    ++gen;
   }
   return __syncthreads_and(ok) != 0;
 }
@@ -183,24 +178,21 @@ __device__ void warp_build_operand(Load load, int64_t n, int nchunks, int col, i
                                    uint32_t* frag, int* colsum4, double* tok_scale) {
   const int lane = threadIdx.x & 31;
   const int nquad = nchunks * 32;
+  // loads at clamped (in-range) positions, results past n zeroed: no branch,
+  // so the loads of all kWq quads are issued together
   auto quad = [&](int q, float (&x)[4]) {
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const int64_t k = 4 * (int64_t)q + e;
-      float v = k < n ? load(k) : 0.0f;
-      x[e] = is_nonfinite(v) ? 0.0f : v;
+      const float v = load(k < n ? k : n - 1);
+      x[e] = (k >= n || is_nonfinite(v)) ? 0.0f : v;
     }
   };
   float v[kWq][4];
   float am = 0.0f;
 #pragma unroll
   for (int i = 0; i < kWq; ++i) {
-    const int q = lane + 32 * i;
-    if (q < nquad) {
-      quad(q, v[i]);
-    } else {
-      v[i][0] = v[i][1] = v[i][2] = v[i][3] = 0.0f;
-    }
+    quad(lane + 32 * i, v[i]);
 #pragma unroll
     for (int e = 0; e < 4; ++e) am = fmaxf(am, fabsf(v[i][e]));
   }
@@ -324,7 +316,7 @@ __global__ void __launch_bounds__(kMdThreads, 1) moe_decode_kernel(const __grid_
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int T = P.T, K = P.K, E = P.E, NP = T * K;
   const int64_t H = P.H, F = P.F;
-  unsigned gen = 0;
+  unsigned target = 0;
   tc::pdl_wait();
 
   // ---- R: router partial scores, one warp per (expert, 256-wide K part)
@@ -379,7 +371,7 @@ __global__ void __launch_bounds__(kMdThreads, 1) moe_decode_kernel(const __grid_
       }
     }
   }
-  if (!grid_sync(P.bar, gen, P.err, 101)) return;
+  if (!grid_sync(P.bar, target, P.err, 101)) return;
 
   // ---- S: routing of every token (the reference's sequential softmax / top-k)
   for (int i = tid; i < T * E; i += kMdThreads) {
@@ -457,7 +449,7 @@ __global__ void __launch_bounds__(kMdThreads, 1) moe_decode_kernel(const __grid_
     unit_matvec(static_cast<const uint4*>(P.tab[e]), static_cast<const float*>(P.tab[E + e]), 2 * F,
                 P.nch_h, rb, p / K, nbx, frag4, colsum, tok_scale, part, P.gu + (int64_t)p * 2 * F);
   }
-  if (!grid_sync(P.bar, gen, P.err, 102)) return;
+  if (!grid_sync(P.bar, target, P.err, 102)) return;
 
   // ---- H: h = act(gate, up) of every pair as column block p, one warp per pair
   const int nbh = (NP + 1) / 2;
@@ -488,7 +480,7 @@ __global__ void __launch_bounds__(kMdThreads, 1) moe_decode_kernel(const __grid_
                 static_cast<const float*>(P.tab[3 * E + e]), H, P.nch_f, rb, p, nbh, frag4, colsum,
                 tok_scale, part, P.o + (int64_t)p * H);
   }
-  if (!grid_sync(P.bar, gen, P.err, 103)) return;
+  if (!grid_sync(P.bar, target, P.err, 103)) return;
 
   // ---- C: y[t] = (0 + w_0 o_0) + w_1 o_1 ... in top-k order
   for (int64_t i = (int64_t)blockIdx.x * kMdThreads + tid; i < T * H;

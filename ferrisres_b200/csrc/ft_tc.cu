@@ -241,21 +241,20 @@ __device__ __forceinline__ void epilogue_group(const TqProblem& p, int digits, b
       const int32_t a = v[c] - p.colsum[pass * NPAD + lt];
       p.y[t * p.ldy + R] = __fmul_rn(__fmul_rn((float)a, p.sx[t]), p.row_scales[R]);
     }
-    return;
-  }
-  // three digits: five tokens per 16-column group
+  } else {
 #pragma unroll
-  for (int c = 0; c < 15; c += 3) {
-    const int lt = (col0 >> 4) * 5 + c / 3;
-    const int64_t t = (int64_t)pass * p.tok_per_pass + lt;
-    if (t >= p.seq || lt >= p.tok_per_pass) break;
-    long long S = 0;
+    for (int c = 0; c < 16; c += 4) {
+      const int lt = (col0 + c) >> 2;
+      const int64_t t = (int64_t)pass * p.tok_per_pass + lt;
+      if (t >= p.seq || lt >= p.tok_per_pass) break;
+      long long S = 0;
 #pragma unroll
-    for (int d = 0; d < 3; ++d) {
-      const long long a = (long long)(v[c + d] - p.colsum[pass * NPAD + col0 + c + d]);
-      S += a * (1ll << (8 * d));
+      for (int d = 0; d < 4; ++d) {
+        const long long a = (long long)(v[c + d] - p.colsum[pass * NPAD + col0 + c + d]);
+        S += a * (1ll << (8 * d));
+      }
+      store_fp<kSparse>(p, bf16, t, R, (double)S);
     }
-    store_fp<kSparse>(p, bf16, t, R, (double)S);
   }
 }
 
@@ -550,7 +549,7 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
         waited_pdl = true;
       }
       const int64_t R = it.tile * kTileRows + r;
-      const int ncols = (int)pass_cols(p.tok_per_pass, b.digits);
+      const int ncols = p.tok_per_pass * b.digits;
       const uint32_t dcol = tmem + lane_off + d * kDStride;
       if (p.ksplit == 1) {
 #pragma unroll 1
@@ -653,7 +652,7 @@ __device__ __forceinline__ int64_t b_offset(int64_t pass, int64_t chunk, int n, 
          (n & 7) * 16 + (kin & 15);
 }
 
-// DT: digits per token (1: int8 codes, 3 or 8), a template parameter so that
+// DT: digits per token (1: int8 codes, 4 or 8), a template parameter so that
 // the digit arrays stay in registers.
 //
 // One pass over the token: thread i holds elements 8i .. 8i+7 of every 2048-K
@@ -850,8 +849,7 @@ __global__ void __launch_bounds__(kPrepThreads) prep_b_kernel(const __grid_const
     const int kin = (int)(k0 & 127);
 #pragma unroll
     for (int d = 0; d < D; ++d)
-      *reinterpret_cast<uint2*>(src.bmat + b_offset(pass, chunk, digit_col(lt, d, D), kin & ~15, npad,
-                                                    src.n_chunks) +
+      *reinterpret_cast<uint2*>(src.bmat + b_offset(pass, chunk, lt * D + d, kin & ~15, npad, src.n_chunks) +
                                 (kin & 8)) = make_uint2(w[d][0], w[d][1]);
   };
 #pragma unroll
@@ -871,7 +869,7 @@ __global__ void __launch_bounds__(kPrepThreads) prep_b_kernel(const __grid_const
   if (threadIdx.x < D) {
     int v = 0;
     for (int w = 0; w < 8; ++w) v += red_i[w][threadIdx.x];
-    src.colsum[pass * npad + digit_col(lt, threadIdx.x, D)] = v;
+    src.colsum[pass * npad + lt * D + threadIdx.x] = v;
   }
 }
 
@@ -938,8 +936,8 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
     max_seq = si > max_seq ? si : max_seq;
   }
   if (max_seq == 0) return FT_OK;
-  const int npad = pick_npad(pass_cols(max_seq, D));
-  const int tok_per_pass = toks_per_pass(npad, D);
+  const int npad = pick_npad(max_seq * D);
+  const int tok_per_pass = npad / D;
   FT_CHECK(ceil_div(max_seq, tok_per_pass) <= (1 << 20), FT_ERR_UNSUPPORTED, "seq %lld too large",
            (long long)max_seq);
 
@@ -1122,7 +1120,7 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     if (D == 1) FT_CUDA(cudaLaunchKernelEx(&cfg, prep_b_kernel<1>, pb));
-    else if (D == 3) FT_CUDA(cudaLaunchKernelEx(&cfg, prep_b_kernel<3>, pb));
+    else if (D == 4) FT_CUDA(cudaLaunchKernelEx(&cfg, prep_b_kernel<4>, pb));
     else FT_CUDA(cudaLaunchKernelEx(&cfg, prep_b_kernel<8>, pb));
     FT_LAUNCH_CHECK();
   }
