@@ -19,7 +19,7 @@
 //      CTAs without a G unit meanwhile pull the chosen experts' down
 //      weights into L2 (bulk prefetch);
 //   H  every CTA forms h = SwiGLU(gate, up) (or GeLU-tanh) of every pair and
-//      its operand, one warp per pair;
+//      its operand (all loads of a row issued before any arithmetic);
 //   D  down projection, same scheme -- barrier;
 //   C  y[t] = sum_k w[t,k] * o[t,k] in top-k order.
 // Activations use 4 base-256 digits per token (the MoE's tolerance, 1e-4 of
@@ -98,61 +98,6 @@ __device__ bool grid_sync(unsigned* bar, unsigned& target, int* err, int site) {
   return __syncthreads_and(ok) != 0;
 }
 
-// Digits of one activation row v[0..n) (fp32 values from `load`) as operand
-// column block `col` (4 digits at columns 4 * (col & 1) + d of n8 block
-// col >> 1); writes colsum[col][d] and the row's scale 2^-sh.  Block-wide.
-template <class Load>
-__device__ void build_operand(Load load, int64_t n, int nchunks, int col, int nb, uint32_t* frag,
-                              int (*colsum)[4], double* tok_scale, float* red) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  float am = 0.0f;
-  for (int64_t k = tid; k < n; k += kMdThreads) {
-    const float v = load(k);
-    if (!is_nonfinite(v)) am = fmaxf(am, fabsf(v));
-  }
-  am = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(am)));
-  if (lane == 0) red[warp] = am;
-  __syncthreads();
-  float a = 0.0f;
-#pragma unroll
-  for (int w = 0; w < kMdWarps; ++w) a = fmaxf(a, red[w]);
-  __syncthreads();  // red is reused by the next call
-  const int sh = a > 0.0f ? digit_shift(a, 4) : 0;
-  const int s1 = sh > 127 ? 127 : (sh < -126 ? -126 : sh);
-  const float f1 = __int_as_float((s1 + 127) << 23);
-  const float f2 = __int_as_float((sh - s1 + 127) << 23);
-  int cs[4] = {0, 0, 0, 0};
-  const int nquad = nchunks * 32;
-  for (int q = tid; q < nquad; q += kMdThreads) {
-    uint32_t u[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int64_t k = 4 * (int64_t)q + e;
-      float v = k < n ? load(k) : 0.0f;
-      if (is_nonfinite(v)) v = 0.0f;
-      u[e] = (uint32_t)__float2int_rn(__fmul_rn(__fmul_rn(v, f1), f2)) + 0x808080u;
-    }
-    const uint32_t lo01 = __byte_perm(u[0], u[1], 0x5140), lo23 = __byte_perm(u[2], u[3], 0x5140);
-    const uint32_t hi01 = __byte_perm(u[0], u[1], 0x7362), hi23 = __byte_perm(u[2], u[3], 0x7362);
-    const uint32_t wd[4] = {__byte_perm(lo01, lo23, 0x5410) ^ 0x80808080u,
-                            __byte_perm(lo01, lo23, 0x7632) ^ 0x80808080u,
-                            __byte_perm(hi01, hi23, 0x5410) ^ 0x80808080u,
-                            __byte_perm(hi01, hi23, 0x7632)};
-    const int base = frag_word(q, 4 * col, nb);  // digit d: lane + 4d, word + 16d
-#pragma unroll
-    for (int d = 0; d < 4; ++d) {
-      cs[d] = __dp4a((int)wd[d], 0x01010101, cs[d]);
-      frag[base + 16 * d] = wd[d];
-    }
-  }
-#pragma unroll
-  for (int d = 0; d < 4; ++d) {
-    const int v = __reduce_add_sync(0xffffffffu, cs[d]);
-    if (lane == 0) atomicAdd(&colsum[col][d], v);
-  }
-  if (tid == 0) tok_scale[col] = a > 0.0f ? __longlong_as_double((long long)(1023 - sh) << 52) : 0.0;
-}
-
 // The 4 digit words of a quad of 4 consecutive values (x already scaled by
 // f1 * f2 when passed through digit_words).
 __device__ __forceinline__ void digit_words(const float (&v)[4], float f1, float f2,
@@ -169,69 +114,101 @@ __device__ __forceinline__ void digit_words(const float (&v)[4], float f1, float
   wd[3] = __byte_perm(hi01, hi23, 0x7632);
 }
 
-// build_operand for one warp: the values stay in registers (kWq quads per
-// lane; longer rows are loaded again) and no block barrier is taken, so the
-// warps of a CTA build different rows at the same time.
-constexpr int kWq = 12;
-template <class Load>
-__device__ void warp_build_operand(Load load, int64_t n, int nchunks, int col, int nb,
-                                   uint32_t* frag, int* colsum4, double* tok_scale) {
-  const int lane = threadIdx.x & 31;
+// Digit operands of NR activation rows (row r = operand column block r:
+// 4 digits at columns 4 * (r & 1) + d of n8 block r >> 1), with the column
+// sums and each row's scale 2^-sh.  Rows are built G at a time (G the largest
+// power of two <= min(NR, 8)) by 8 / G warps each.  A thread first issues
+// every load of its first kRq quads (`fetch`: raw values, positions clamped
+// into [0, n)), then transforms them (`xform`: raw -> fp32, applied again when
+// the digits are written), so a row costs about one memory round trip; quads
+// past kRq per thread are loaded again in a second pass.  colsum must be zero
+// on entry.  Block-wide.
+constexpr int kRq = 12;
+template <class Fetch, class Xform>
+__device__ void build_rows(int NR, Fetch fetch, Xform xform, int64_t n, int nchunks, int nb,
+                           uint32_t* frag, int (*colsum)[4], double* tok_scale, float* red) {
+  using Raw = decltype(fetch(0, (int64_t)0));
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int G = NR >= 8 ? 8 : NR >= 4 ? 4 : NR >= 2 ? 2 : 1;
+  const int wpp = kMdWarps / G, slot = warp / wpp, sub = warp % wpp;
+  const int nthr = 32 * wpp, ts = sub * 32 + lane;
   const int nquad = nchunks * 32;
-  // loads at clamped (in-range) positions, results past n zeroed: no branch,
-  // so the loads of all kWq quads are issued together
-  auto quad = [&](int q, float (&x)[4]) {
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int64_t k = 4 * (int64_t)q + e;
-      const float v = load(k < n ? k : n - 1);
-      x[e] = (k >= n || is_nonfinite(v)) ? 0.0f : v;
-    }
+  auto value = [&](const Raw& raw, int64_t k) -> float {
+    const float v = xform(raw);
+    return (k >= n || is_nonfinite(v)) ? 0.0f : v;
   };
-  float v[kWq][4];
-  float am = 0.0f;
+  for (int r0 = 0; r0 < NR; r0 += G) {
+    const int r = r0 + slot;
+    const bool live = r < NR;
+    Raw raw[kRq][4];
 #pragma unroll
-  for (int i = 0; i < kWq; ++i) {
-    quad(lane + 32 * i, v[i]);
+    for (int i = 0; i < kRq; ++i)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) am = fmaxf(am, fabsf(v[i][e]));
-  }
-  for (int q = lane + 32 * kWq; q < nquad; q += 32) {
-    float x[4];
-    quad(q, x);
+      for (int e = 0; e < 4; ++e) {
+        const int64_t k = 4 * (int64_t)(ts + nthr * i) + e;
+        raw[i][e] = fetch(live ? r : 0, k < n ? k : n - 1);
+      }
+    float am = 0.0f;
 #pragma unroll
-    for (int e = 0; e < 4; ++e) am = fmaxf(am, fabsf(x[e]));
-  }
-  am = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(am)));
-  const int sh = am > 0.0f ? digit_shift(am, 4) : 0;
-  const int s1 = sh > 127 ? 127 : (sh < -126 ? -126 : sh);
-  const float f1 = __int_as_float((s1 + 127) << 23);
-  const float f2 = __int_as_float((sh - s1 + 127) << 23);
-  int cs[4] = {0, 0, 0, 0};
-  auto emit = [&](int q, const float (&x)[4]) {
-    uint32_t wd[4];
-    digit_words(x, f1, f2, wd);
-    const int base = frag_word(q, 4 * col, nb);
+    for (int i = 0; i < kRq; ++i)
 #pragma unroll
-    for (int d = 0; d < 4; ++d) {
-      cs[d] = __dp4a((int)wd[d], 0x01010101, cs[d]);
-      frag[base + 16 * d] = wd[d];
+      for (int e = 0; e < 4; ++e)
+        am = fmaxf(am, fabsf(value(raw[i][e], 4 * (int64_t)(ts + nthr * i) + e)));
+    for (int q = ts + nthr * kRq; q < nquad; q += nthr)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int64_t k = 4 * (int64_t)q + e;
+        am = fmaxf(am, fabsf(value(fetch(live ? r : 0, k < n ? k : n - 1), k)));
+      }
+    am = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(am)));
+    if (lane == 0) red[warp] = am;
+    __syncthreads();
+    float a = 0.0f;
+    for (int w = slot * wpp; w < slot * wpp + wpp; ++w) a = fmaxf(a, red[w]);
+    const int sh = a > 0.0f ? digit_shift(a, 4) : 0;
+    const int s1 = sh > 127 ? 127 : (sh < -126 ? -126 : sh);
+    const float f1 = __int_as_float((s1 + 127) << 23);
+    const float f2 = __int_as_float((sh - s1 + 127) << 23);
+    if (live) {
+      int cs[4] = {0, 0, 0, 0};
+      auto emit = [&](int q, const float (&x)[4]) {
+        uint32_t wd[4];
+        digit_words(x, f1, f2, wd);
+        const int base = frag_word(q, 4 * r, nb);
+#pragma unroll
+        for (int d = 0; d < 4; ++d) {
+          cs[d] = __dp4a((int)wd[d], 0x01010101, cs[d]);
+          frag[base + 16 * d] = wd[d];
+        }
+      };
+#pragma unroll
+      for (int i = 0; i < kRq; ++i) {
+        const int q = ts + nthr * i;
+        if (q < nquad) {
+          float x[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) x[e] = value(raw[i][e], 4 * (int64_t)q + e);
+          emit(q, x);
+        }
+      }
+      for (int q = ts + nthr * kRq; q < nquad; q += nthr) {
+        float x[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int64_t k = 4 * (int64_t)q + e;
+          x[e] = value(fetch(r, k < n ? k : n - 1), k);
+        }
+        emit(q, x);
+      }
+#pragma unroll
+      for (int d = 0; d < 4; ++d) {
+        const int c = __reduce_add_sync(0xffffffffu, cs[d]);
+        if (lane == 0) atomicAdd(&colsum[r][d], c);
+      }
+      if (ts == 0) tok_scale[r] = a > 0.0f ? __longlong_as_double((long long)(1023 - sh) << 52) : 0.0;
     }
-  };
-#pragma unroll
-  for (int i = 0; i < kWq; ++i)
-    if (lane + 32 * i < nquad) emit(lane + 32 * i, v[i]);
-  for (int q = lane + 32 * kWq; q < nquad; q += 32) {
-    float x[4];
-    quad(q, x);
-    emit(q, x);
+    __syncthreads();  // red is reused by the next round
   }
-#pragma unroll
-  for (int d = 0; d < 4; ++d) {
-    const int c = __reduce_add_sync(0xffffffffu, cs[d]);
-    if (lane == 0) colsum4[d] = c;
-  }
-  if (lane == 0) *tok_scale = am > 0.0f ? __longlong_as_double((long long)(1023 - sh) << 52) : 0.0;
 }
 
 // One work unit: rows [64 rb, 64 rb + 64) of a tiled weight (codes, nch
@@ -418,14 +395,16 @@ __global__ void __launch_bounds__(kMdThreads, 1) moe_decode_kernel(const __grid_
   __syncthreads();
   // the tokens' operand: token t is column block t
   const int nbx = (T + 1) / 2;
-  for (int t = 0; t < T; ++t) {
-    auto ld = [&](int64_t k) -> float {
-      return P.x_bf16 ? __uint_as_float((uint32_t) static_cast<const uint16_t*>(P.x)[t * H + k] << 16)
-                      : static_cast<const float*>(P.x)[t * H + k];
-    };
-    build_operand(ld, H, (int)P.nch_h, t, nbx, frag, colsum, tok_scale, red);
+  if (P.x_bf16) {
+    const uint16_t* xb = static_cast<const uint16_t*>(P.x);
+    build_rows(T, [&](int t, int64_t k) { return xb[t * H + k]; },
+               [](uint16_t b) { return __uint_as_float((uint32_t)b << 16); }, H, (int)P.nch_h, nbx,
+               frag, colsum, tok_scale, red);
+  } else {
+    const float* xf = static_cast<const float*>(P.x);
+    build_rows(T, [&](int t, int64_t k) { return xf[t * H + k]; }, [](float v) { return v; }, H,
+               (int)P.nch_h, nbx, frag, colsum, tok_scale, red);
   }
-  __syncthreads();
 
   // ---- G: gate||up of every (token, expert) pair
   const int64_t rb_gu = (2 * F + kMdRows - 1) / kMdRows;
@@ -451,22 +430,28 @@ __global__ void __launch_bounds__(kMdThreads, 1) moe_decode_kernel(const __grid_
   }
   if (!grid_sync(P.bar, target, P.err, 102)) return;
 
-  // ---- H: h = act(gate, up) of every pair as column block p, one warp per pair
+  // ---- H: h = act(gate, up) of every pair as column block p
+  if (tid < kMdMaxPairs * 4) colsum[tid >> 2][tid & 3] = 0;
+  __syncthreads();
   const int nbh = (NP + 1) / 2;
-  for (int p = warp; p < NP; p += kMdWarps) {
-    const float* gp = P.gu + (int64_t)p * 2 * F;
-    const int gelu = P.use_gelu;
-    auto act = [&](int64_t j) -> float {
-      const float g = __ldcg(gp + j);
-      if (gelu) {
+  {
+    const float* gu = P.gu;
+    const int64_t F2 = 2 * F;
+    auto fetch = [&](int p, int64_t j) {
+      return make_float2(__ldcg(gu + p * F2 + j), __ldcg(gu + p * F2 + F + j));
+    };
+    if (P.use_gelu) {
+      build_rows(NP, fetch, [](float2 v) {
+        const float g = v.x;
         const float ta = __fmul_rn(0.7978845608f,
                                    __fadd_rn(g, __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, g), g), g)));
         return __fmul_rn(__fmul_rn(0.5f, g), __fadd_rn(1.0f, tanhf(ta)));
-      }
-      const float silu = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
-      return __fmul_rn(silu, __ldcg(gp + F + j));
-    };
-    warp_build_operand(act, F, (int)P.nch_f, p, nbh, frag, colsum[p], &tok_scale[p]);
+      }, F, (int)P.nch_f, nbh, frag, colsum, tok_scale, red);
+    } else {
+      build_rows(NP, fetch, [](float2 v) {
+        return __fmul_rn(__fdiv_rn(v.x, __fadd_rn(1.0f, expf(-v.x))), v.y);
+      }, F, (int)P.nch_f, nbh, frag, colsum, tok_scale, red);
+    }
   }
   __syncthreads();
 

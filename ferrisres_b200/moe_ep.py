@@ -4,7 +4,9 @@ Rank r holds experts [r*E/W, (r+1)*E/W) and routes its own tokens.  One layer
 forward is:
   1. route (router GEMV + softmax + top-k, on the GPU) and build the
      expert-major layout of this rank's (token, k) entries;
-  2. exchange the per-expert counts (all_gather of E int32 per rank);
+  2. exchange the per-expert counts (all_gather of E int32 per rank) and
+     read them on the host (a pinned copy and an event wait, while the GPU
+     gathers the rows);
   3. dispatch: all_to_all_single of the gathered activation rows to the
      experts' owners (uneven splits from the counts);
   4. every owner runs ONE grouped expert launch over its (source rank,
@@ -90,6 +92,17 @@ class GpuMoEBackend:
         return y
 
 
+_PINNED = {}
+
+
+def _pinned_counts(world, E, dtype):
+    """A reused pinned host buffer for the gathered counts."""
+    key = (world, E, dtype)
+    if key not in _PINNED:
+        _PINNED[key] = torch.empty(world, E, dtype=dtype).pin_memory()
+    return _PINNED[key]
+
+
 def ep_forward(x, backend, n_experts, rank=0, world=1, group=None, marks=None, stats=None):
     """One expert-parallel MoE forward of this rank's tokens x [T, H].
 
@@ -112,17 +125,30 @@ def ep_forward(x, backend, n_experts, rank=0, world=1, group=None, marks=None, s
     mark("start")
     idx, w, counts = backend.route(x)
     slot_of, token_of = backend.layout(idx, counts)
+    # the per-expert counts of every rank, to the host: the only host
+    # synchronisation of the step (NCCL's split sizes and the grouped expert
+    # launch are sized on the host); the row gather runs on the GPU meanwhile
+    if world == 1:
+        ac_dev = counts.view(1, E)
+    else:
+        ac_dev = torch.empty(world * E, dtype=counts.dtype, device=counts.device)
+        dist.all_gather_into_tensor(ac_dev, counts, group=group)
+        ac_dev = ac_dev.view(world, E)
+    if ac_dev.is_cuda:
+        ac_host = _pinned_counts(world, E, counts.dtype)
+        ac_host.copy_(ac_dev, non_blocking=True)
+        ready = torch.cuda.Event()
+        ready.record()
+    else:
+        ac_host, ready = ac_dev, None
     xg = backend.gather(x, token_of)  # [T*K, H], expert-major
     mark("route")
-    if world == 1:
-        ac = counts.cpu().numpy().reshape(1, E).astype(np.int64)
-    else:
-        parts = [torch.empty_like(counts) for _ in range(world)]
-        dist.all_gather(parts, counts, group=group)
-        ac = torch.stack(parts).cpu().numpy().astype(np.int64)  # [src rank, expert]
+    if ready is not None:
+        ready.synchronize()
+    ac = ac_host.numpy().astype(np.int64)  # [src rank, expert]
     mark("counts")
-    send_rows = [int(ac[rank, d * per:(d + 1) * per].sum()) for d in range(world)]
-    recv_rows = [int(ac[s, rank * per:(rank + 1) * per].sum()) for s in range(world)]
+    send_rows = ac[rank].reshape(world, per).sum(axis=1).tolist()
+    recv_rows = ac[:, rank * per:(rank + 1) * per].sum(axis=1).tolist()
     if stats is not None:
         stats["sent_rows_remote"] = sum(n for d, n in enumerate(send_rows) if d != rank)
         stats["recv_rows_remote"] = sum(n for s, n in enumerate(recv_rows) if s != rank)
@@ -133,11 +159,8 @@ def ep_forward(x, backend, n_experts, rank=0, world=1, group=None, marks=None, s
         dist.all_to_all_single(recv.view(-1), xg.reshape(-1), [r * H for r in recv_rows],
                                [r * H for r in send_rows], group=group)
     mark("dispatch")
-    seg_e, seg_n = [], []
-    for s in range(world):
-        for e in range(rank * per, (rank + 1) * per):
-            seg_e.append(e)
-            seg_n.append(int(ac[s, e]))
+    seg_e = np.tile(np.arange(rank * per, (rank + 1) * per, dtype=np.int32), world)
+    seg_n = ac[:, rank * per:(rank + 1) * per].reshape(-1)
     o_recv = backend.experts(seg_e, seg_n, recv)
     mark("experts")
     if world == 1:
