@@ -523,11 +523,12 @@ def run_sparse(args, torch, dist, device, local, sub_steps, cpu_seconds):
     """2:4 sparse ternary matmul, K=4096, N=14336, fp32 x,
     at M=1 (decode GEMV kernel; one step = one launch of 32 GEMVs over distinct
     weight copies) and M=64 (tensor-core engine).  Weights enter in the
-    reference SparseTernaryMatrix layout and are stored at 1.25 bits/weight;
-    copies rotate beyond 2x L2."""
+    reference SparseTernaryMatrix layout and are stored at 1.5 bits/weight
+    (the sparse MMA's metadata nibble + two sign bits per group of 4, the size
+    of the reference's own packing); copies rotate beyond 2x L2."""
     from ferrisres_b200 import gpu
 
-    dev_bytes = (S_N // 128) * (S_K // 128) * 2560
+    dev_bytes = (S_N // 128) * (S_K // 128) * 3072
     algo = dev_bytes + S_N * 4 + S_K * 4 + S_N * 4  # weights + scales + x + y per GEMV
     rng = np.random.default_rng(0)
     ng = S_N * S_K // 4
@@ -578,7 +579,7 @@ def run_sparse(args, torch, dist, device, local, sub_steps, cpu_seconds):
         "steps": sub_steps, "ms_per_step": sec * 1e3, "dtype": "f32",
         "config": {"workload": "cfg3 2:4 sparse K=4096 N=14336, M=1 (one step = one launch of "
                                f"{S_GROUP} GEMVs) and M=64", "device_bytes_per_weight": dev_bytes,
-                   "bits_per_weight": 1.25, "weight_copies": S_COPIES,
+                   "bits_per_weight": 1.5, "weight_copies": S_COPIES,
                    "l2": f"a step reads {S_GROUP * dev_bytes / 1e6:.0f} MB of weights (> L2)"},
         "roofline": {"bound": "hbm", "achieved": round(gbps, 2), "peak": peak, "unit": "GB/s",
                      "frac": round(gbps / peak, 4), "peak_source": kind,

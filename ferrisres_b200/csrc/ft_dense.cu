@@ -46,49 +46,71 @@ __global__ void repack_kernel(const void* __restrict__ src, int64_t rows, int64_
 }
 
 // -------------------------------------------------------- sparse repack --
-// One thread per (tile, chunk, row): decodes the row's 32 groups of this chunk
-// from the reference layout and writes 32 x 5-bit codes (160 bits, LSB first)
-// = 5 words.  Code = pattern * 4 + signs (bit 0/1: first/second nonzero is
-// negative); 24 = all-zero group (padding rows or K).
+// The metadata nibble and the two sign bits (1 = -1) of group kg (K / 4) of
+// row R, read from a reference layout; padding (R >= rows or kg >= groups)
+// gives positions (0, 1) and signs +1.
+template <bool kWgsl>
+__device__ __forceinline__ void ref_group(const uint8_t* pat, const uint8_t* sgn,
+                                          const uint32_t* words, int64_t rows, int64_t gpr,
+                                          int64_t R, int64_t kg, uint32_t& nib, uint32_t& s0,
+                                          uint32_t& s1) {
+  uint32_t p = 0, sb = 0;
+  if (R < rows && kg < gpr) {
+    if (kWgsl) {
+      const int64_t wpr = (gpr + 5) / 6;
+      const uint32_t v = (words[R * wpr + kg / 6] >> ((kg % 6) * 5)) & 31u;
+      p = v & 7u;
+      if (p > 5) p = 5;          // the WGSL shader clamps the pattern
+      sb = (v >> 3) & 3u;        // 1 = negative
+    } else {
+      const int64_t gi = R * gpr + kg;  // flat group index of the host matrix
+      p = (gi % 2 == 0) ? (pat[gi / 2] & 7u) : ((pat[gi / 2] >> 4) & 7u);
+      if (p > 5) p = 0;          // to_ternary's fallback for an invalid pattern
+      sb = (~(uint32_t)(sgn[gi / 4] >> ((gi % 4) * 2))) & 3u;  // host: 1 = positive
+    }
+  }
+  nib = sparse_nibble((int)p);
+  s0 = sb & 1u;
+  s1 = (sb >> 1) & 1u;
+}
+
+// One thread per (tile, chunk, m-block, lane): that lane's metadata words and
+// sign bits of the block (layout at the top of ft_internal.cuh).
 template <bool kWgsl>
 __global__ void repack_sparse_kernel(const uint8_t* __restrict__ pat, const uint8_t* __restrict__ sgn,
                                      const uint32_t* __restrict__ words, int64_t rows, int64_t cols,
-                                     int64_t n_chunks, int64_t total, uint32_t* __restrict__ dst) {
-  int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+                                     int64_t n_chunks, int64_t total, uint8_t* __restrict__ dst) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= total) return;
-  const int64_t block = idx >> 7;
-  const int row = (int)(idx & 127);
+  const int L = (int)(idx & 31), mb = (int)((idx >> 5) & 7);
+  const int64_t block = idx >> 8;
   const int64_t tile = block / n_chunks, chunk = block % n_chunks;
-  const int64_t R = tile * kTileRows + row;
+  const int g = L >> 2, t = L & 3;
   const int64_t gpr = cols / 4;  // groups per row (cols % 4 == 0)
-  const int64_t wpr = (gpr + 5) / 6;
-  uint32_t out[5] = {0, 0, 0, 0, 0};
-#pragma unroll 4
-  for (int g = 0; g < 32; ++g) {
-    const int64_t kg = chunk * 32 + g;
-    uint32_t code = 24;
-    if (R < rows && kg < gpr) {
-      uint32_t p, sbits;
-      if (kWgsl) {
-        const uint32_t v = (words[R * wpr + kg / 6] >> ((kg % 6) * 5)) & 31u;
-        p = v & 7u;
-        if (p > 5) p = 5;          // the WGSL shader clamps the pattern
-        sbits = (v >> 3) & 3u;     // 1 = negative
-      } else {
-        const int64_t gi = R * gpr + kg;  // flat group index of the host matrix
-        p = (gi % 2 == 0) ? (pat[gi / 2] & 7u) : ((pat[gi / 2] >> 4) & 7u);
-        if (p > 5) p = 0;          // to_ternary's fallback for an invalid pattern
-        sbits = (~(uint32_t)(sgn[gi / 4] >> ((gi % 4) * 2))) & 3u;  // host: 1 = positive
-      }
-      code = p * 4 + sbits;
-    }
-    const int bit = 5 * g;
-    out[bit >> 5] |= code << (bit & 31);
-    if ((bit & 31) > 27) out[(bit >> 5) + 1] |= code >> (32 - (bit & 31));
-  }
-  uint32_t* d = dst + block * (kSparseBlockBytes / 4) + row * 5;
+  const int64_t r0 = tile * kTileRows + mb * 16 + g;
+  uint32_t meta[2] = {0u, 0u}, signs = 0u;
 #pragma unroll
-  for (int i = 0; i < 5; ++i) d[i] = out[i];
+  for (int s = 0; s < 2; ++s) {
+    const int64_t gb = chunk * 32 + 16 * s;  // first group of this k64 step
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      uint32_t nib, a, b;
+      ref_group<kWgsl>(pat, sgn, words, rows, gpr, r0 + 8 * (t & 1), gb + 8 * (t >> 1) + i, nib, a, b);
+      meta[s] |= nib << (4 * i);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t nib, a, b;
+        ref_group<kWgsl>(pat, sgn, words, rows, gpr, r0 + 8 * (i & 1), gb + 8 * (i >> 1) + 2 * t + h,
+                         nib, a, b);
+        signs |= (a << (4 * i + 2 * h) | b << (4 * i + 2 * h + 1)) << (16 * s);
+      }
+  }
+  uint8_t* rec = dst + block * kSparseBlockBytes + mb * kSparseMbBytes;
+  reinterpret_cast<uint2*>(rec)[L] = make_uint2(meta[0], meta[1]);
+  reinterpret_cast<uint32_t*>(rec + 256)[L] = signs;
 }
 
 // ------------------------------------------------------------- quantizer --
@@ -284,18 +306,18 @@ int launch_repack_u32(const uint32_t* words, int64_t rows, int64_t cols, ft_weig
 
 int launch_repack_sparse_host(const uint8_t* patterns, const uint8_t* signs, int64_t rows,
                               int64_t cols, ft_weight* w, cudaStream_t s) {
-  int64_t total = w->n_tiles * w->n_chunks * kTileRows;
-  repack_sparse_kernel<false><<<(unsigned)ceil_div(total, 128), 128, 0, s>>>(
-      patterns, signs, nullptr, rows, cols, w->n_chunks, total, reinterpret_cast<uint32_t*>(w->codes));
+  int64_t total = w->n_tiles * w->n_chunks * 256;
+  repack_sparse_kernel<false><<<(unsigned)ceil_div(total, 256), 256, 0, s>>>(
+      patterns, signs, nullptr, rows, cols, w->n_chunks, total, w->codes);
   FT_LAUNCH_CHECK();
   return FT_OK;
 }
 
 int launch_repack_sparse_wgsl(const uint32_t* words, int64_t rows, int64_t cols, ft_weight* w,
                               cudaStream_t s) {
-  int64_t total = w->n_tiles * w->n_chunks * kTileRows;
-  repack_sparse_kernel<true><<<(unsigned)ceil_div(total, 128), 128, 0, s>>>(
-      nullptr, nullptr, words, rows, cols, w->n_chunks, total, reinterpret_cast<uint32_t*>(w->codes));
+  int64_t total = w->n_tiles * w->n_chunks * 256;
+  repack_sparse_kernel<true><<<(unsigned)ceil_div(total, 256), 256, 0, s>>>(
+      nullptr, nullptr, words, rows, cols, w->n_chunks, total, w->codes);
   FT_LAUNCH_CHECK();
   return FT_OK;
 }

@@ -94,14 +94,14 @@ struct GvCfg<2> {
   static constexpr int MB = 2, DEPTH = FT_GV_DEPTH2, CTAS = 2;
 };
 
-// 2:4 sparse weights: an m-block of one chunk is 16 rows x 20 bytes (32
-// five-bit group codes per row), 320 contiguous bytes; the ring is deepened so
+// 2:4 sparse weights: an m-block of one chunk is the 384-byte metadata + sign
+// record of the sparse MMA operand (ft_internal.cuh); the ring is deepened so
 // that about as many bytes are in flight per warp as for dense units.
 #ifndef FT_GV_SPDEPTH1
-#define FT_GV_SPDEPTH1 6
+#define FT_GV_SPDEPTH1 5
 #endif
 #ifndef FT_GV_SPDEPTH2
-#define FT_GV_SPDEPTH2 12
+#define FT_GV_SPDEPTH2 10
 #endif
 // m-blocks per unit; `small`: a launch of <= 4 problems
 constexpr int unit_mb(int nb, bool sp, bool small) {
@@ -112,7 +112,7 @@ struct GvUnit {
   static constexpr int MB = unit_mb(NB, SP, SMALL);
   static constexpr int DEPTH = SP ? (NB == 1 ? FT_GV_SPDEPTH1 : FT_GV_SPDEPTH2)
                                   : (MB != GvCfg<NB>::MB ? FT_GV_DEPTH1S : GvCfg<NB>::DEPTH);
-  static constexpr int MU = SP ? 20 : 32;    // uint4 per m-block of one chunk
+  static constexpr int MU = SP ? 24 : 32;    // uint4 per m-block of one chunk
   static constexpr uint32_t BYTES = MB * MU * 16;  // one unit
 };
 
@@ -158,6 +158,25 @@ __device__ __forceinline__ void mma_u8s8(int (&c)[4], uint32_t a0, uint32_t a1, 
       "{%8, %9}, {%0, %1, %2, %3};"
       : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Sparse MMA m16n8k64 (2:4 along K): A = the 16 x 32 compressed +-1 values,
+// e = this lane's metadata word (selector 0: every lane contributes).
+__device__ __forceinline__ void mma_sp_s8(int (&c)[4], const uint32_t (&a)[4], const uint4& b,
+                                          uint32_t e) {
+  asm volatile(
+      "mma.sp::ordered_metadata.sync.aligned.m16n8k64.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, "
+      "{%4, %5, %6, %7}, {%8, %9, %10, %11}, {%0, %1, %2, %3}, %12, 0x0;"
+      : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b.x), "r"(b.y), "r"(b.z), "r"(b.w),
+        "r"(e));
+}
+
+// Four sign bits (bit e set = -1) -> the A register of four s8 values +-1:
+// the bits spread to the low bit of each byte, then 0x01 ^ 0xFE per set bit.
+__device__ __forceinline__ uint32_t sign_bytes(uint32_t bits) {
+  const uint32_t spread = ((bits & 0xFu) * 0x00204081u) & 0x01010101u;
+  return 0x01010101u ^ (spread * 0xFEu);
 }
 
 // Problem / row-block / chunk cursor over a segment's units.
@@ -252,19 +271,9 @@ __device__ __forceinline__ float4 load_x4(const void* x, int xkind, int64_t row,
 // Fragment word of (4 consecutive K at quad q, column n): chunk q/32, k-step
 // j = (q%32)/8, half kk = (q%8)/4, lane 4*(n%8) + q%4; stored as
 // [chunk][n/8][j/2][lane] uint4 holding words (b0, b1) of k-steps 2h, 2h+1.
-//
-// 2:4 sparse weights use another K order inside a chunk (A and B only need to
-// agree): MMA lane r's A registers of k-step j hold groups (quads) 8r + 2j and
-// 8r + 2j + 1, so a lane decodes 8 consecutive group codes of a row.  The B
-// word of quad q = 8r + 4h + e (e = 0..3) for column n is word e of the uint4
-// at [chunk][n/8][h][4 * (n % 8) + r].
-template <bool SP>
+// That uint4 is also the B operand (b0..b3) of the sparse m16n8k64 MMA over
+// K 64h .. 64h+63 of the chunk, so dense and 2:4 weights share the layout.
 __device__ __forceinline__ int frag_word(int q, int n, int nb) {
-  if (SP) {
-    const int c = q >> 5, rr = (q >> 3) & 3, h = (q >> 2) & 1, e = q & 3;
-    const int lane = 4 * (n & 7) + rr;
-    return ((((c * nb + (n >> 3)) * 2 + h) * 32 + lane) << 2) + e;
-  }
   const int c = q >> 5, j = (q >> 3) & 3, kk = (q >> 2) & 1, rr = q & 3;
   const int lane = 4 * (n & 7) + rr;
   return ((((c * nb + (n >> 3)) * 2 + (j >> 1)) * 32 + lane) << 2) + 2 * (j & 1) + kk;
@@ -286,7 +295,7 @@ struct Producer {
 template <int MB, bool SP, class PT>
 __device__ __forceinline__ void prod_at(Producer& w, const PT& P, int p, int rb, int c) {
   constexpr int RPT = 8 / MB;  // row-blocks per tile
-  constexpr int MU = SP ? 20 : 32, BU = SP ? 160 : 256;
+  constexpr int MU = SP ? 24 : 32, BU = SP ? 192 : 256;
   const GvProb& q = P.p[p];
   w.base = q.codes;
   w.nc = q.n_chunks;
@@ -300,7 +309,7 @@ __device__ __forceinline__ void prod_at(Producer& w, const PT& P, int p, int rb,
 template <int MB, bool SP, class PT>
 __device__ __forceinline__ void prod_next(Producer& w, const PT& P) {
   constexpr int RPT = 8 / MB;
-  constexpr uint32_t MU = SP ? 20 : 32, BU = SP ? 160 : 256;
+  constexpr uint32_t MU = SP ? 24 : 32, BU = SP ? 192 : 256;
   if (++w.c < w.nc) {
     w.off += BU;
   } else {
@@ -317,7 +326,7 @@ __device__ __forceinline__ void prod_next(Producer& w, const PT& P) {
 template <int MB, bool SP>
 __device__ __forceinline__ void prod_copy(const Producer& w, uint32_t dst, uint32_t bar,
                                           uint64_t policy) {
-  constexpr uint32_t bytes = MB * (SP ? 320u : 512u);
+  constexpr uint32_t bytes = MB * (SP ? (uint32_t)kSparseMbBytes : 512u);
   tc::mbar_arrive_expect_tx(bar, bytes);
   tc::bulk_g2s_hint(dst, w.base + w.off, bytes, bar, policy);
 }
@@ -435,7 +444,6 @@ __global__ void __launch_bounds__(kThreads, GvCfg<NB>::CTAS)
   __shared__ int nf_cnt[4];
   __shared__ int nf_pos[4][kNfCap];
   __shared__ int part_id[kW];
-  __shared__ uint32_t s_lut[SP ? 32 : 1];  // 2:4 group code -> A register (bytes w + 1)
   __shared__ __align__(8) uint64_t full_bar[kW][kDepth];
 
   tc::pdl_launch_dependents();
@@ -474,21 +482,6 @@ __global__ void __launch_bounds__(kThreads, GvCfg<NB>::CTAS)
       ++issued;
     }
   }
-
-  if (SP && tid < 32) {
-    // group code 4p + s: pattern p places the nonzeros at (0,1) (0,2) (0,3)
-    // (1,2) (1,3) (2,3); sign bit 0 (1) is the first (second) nonzero, set =
-    // -1; codes 24..31 are all-zero groups.  Read after the barrier below.
-    uint32_t v = 0x01010101u;
-    if (tid < 24) {
-      const int pat = tid >> 2;
-      const int p0 = pat < 3 ? 0 : (pat < 5 ? 1 : 2);
-      const int p1 = pat == 0 ? 1 : ((pat == 1 || pat == 3) ? 2 : 3);
-      v ^= (((tid & 1) ? 1u : 3u) << (8 * p0)) ^ (((tid & 2) ? 1u : 3u) << (8 * p1));
-    }
-    s_lut[SP ? tid : 0] = v;
-  }
-  const int sp_word = (5 * r) >> 2, sp_shift = 8 * ((5 * r) & 3);
 
   // ---- activation fragments of this CTA's segment (after the previous grid)
   tc::pdl_wait();
@@ -602,7 +595,7 @@ __global__ void __launch_bounds__(kThreads, GvCfg<NB>::CTAS)
           if (is_nonfinite(v.z)) v.z = 0.0f;
           if (is_nonfinite(v.w)) v.w = 0.0f;
         }
-        const int base = frag_word<SP>(q, D * t, NB);  // digit d: lane + 4d, word + 16d
+        const int base = frag_word(q, D * t, NB);  // digit d: lane + 4d, word + 16d
         if (D == 4) {
           // X = round(x * 2^sh), |X| < 2^30.  With U = X + 0x808080 the low
           // three bytes of U are the low signed base-256 digits + 128 and the
@@ -663,14 +656,15 @@ __global__ void __launch_bounds__(kThreads, GvCfg<NB>::CTAS)
             if (k + e < S.K) wv |= (uint32_t)(xq[k + e] & 0xFF) << (8 * e);
         }
         cs[0] = __dp4a((int)wv, 0x01010101, cs[0]);
-        frag[frag_word<SP>(q, t, NB)] = wv;
+        frag[frag_word(q, t, NB)] = wv;
       }
     }
     // column sums: one warp-wide integer add per column, one shared atomic
     // per warp and column
+    // (2:4 weights need none: their A operand is w itself, not w + 1)
 #pragma unroll
     for (int d = 0; d < 8; ++d) {
-      if (d < D) {
+      if (d < D && !SP) {
         const int v = __reduce_add_sync(0xffffffffu, cs[d]);
         if (lane == 0) atomicAdd(&colsum[t * D + d], v);
       }
@@ -721,47 +715,22 @@ __global__ void __launch_bounds__(kThreads, GvCfg<NB>::CTAS)
           }
         }
       } else {
-        // 2:4 sparse: this lane's 8 group codes of rows g and g + 8 are the 40
-        // bits at byte 5r of each 20-byte row record; each code's A register
-        // (4 bytes w + 1) comes from the shared table.  No 4^j factors here:
-        // one accumulator per m-block and operand block.
-        uint32_t bj[NB][4][2];
-#pragma unroll
-        for (int nb = 0; nb < NB; ++nb) {
-          const uint4 blo = fp[nb * 64], bhi = fp[nb * 64 + 32];
-          bj[nb][0][0] = blo.x; bj[nb][0][1] = blo.y; bj[nb][1][0] = blo.z; bj[nb][1][1] = blo.w;
-          bj[nb][2][0] = bhi.x; bj[nb][2][1] = bhi.y; bj[nb][3][0] = bhi.z; bj[nb][3][1] = bhi.w;
-        }
-        const uint32_t* u32 = reinterpret_cast<const uint32_t*>(myring + slot * kU4);
+        // 2:4 sparse: per m-block and k64 step, this lane's metadata word and
+        // 16 sign bits form the A operand of one sparse MMA per operand block
+        // (A holds the weights +-1 themselves: no column-sum correction).
+        const unsigned char* rec0 = reinterpret_cast<const unsigned char*>(myring + slot * kU4);
 #pragma unroll
         for (int m = 0; m < MB; ++m) {
-          uint32_t lo[2], hi[2];
+          const unsigned char* rec = rec0 + m * kSparseMbBytes;
+          const uint2 meta = reinterpret_cast<const uint2*>(rec)[lane];
+          const uint32_t sg = reinterpret_cast<const uint32_t*>(rec + 256)[lane];
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            const uint32_t* rw = u32 + (16 * m + g + 8 * h) * 5 + sp_word;
-            const uint32_t w0 = rw[0], w1 = rw[1];
-            lo[h] = __funnelshift_r(w0, w1, sp_shift);
-            hi[h] = w1 >> sp_shift;
-          }
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            uint32_t a[2][2];  // [row half][group 2j, 2j + 1]
-#pragma unroll
-            for (int h = 0; h < 2; ++h)
-#pragma unroll
-              for (int e = 0; e < 2; ++e) {
-                // byte offset 4 * code of code i (bits 5i .. 5i + 4 of the 40)
-                const int i = 2 * j + e;
-                const uint32_t off = i == 0 ? (lo[h] << 2) & 0x7Cu
-                                     : i < 7 ? __funnelshift_r(lo[h], hi[h], 5 * i - 2) & 0x7Cu
-                                             : (hi[h] >> 1) & 0x7Cu;
-                a[h][e] = *reinterpret_cast<const uint32_t*>(
-                    reinterpret_cast<const unsigned char*>(s_lut) + off);
-              }
+            const uint32_t a[4] = {sign_bytes(sg >> (16 * h)), sign_bytes(sg >> (16 * h + 4)),
+                                   sign_bytes(sg >> (16 * h + 8)), sign_bytes(sg >> (16 * h + 12))};
 #pragma unroll
             for (int nb = 0; nb < NB; ++nb)
-              mma_u8s8(acc[m][nb][0], a[0][0], a[1][0], a[0][1], a[1][1], bj[nb][j][0],
-                       bj[nb][j][1]);
+              mma_sp_s8(acc[m][nb][0], a, fp[nb * 64 + 32 * h], h ? meta.y : meta.x);
           }
         }
       }

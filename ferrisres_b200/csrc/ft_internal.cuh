@@ -19,6 +19,23 @@
 //   m-block: 64 contiguous bytes.  Codes: 0 -> -1, 1 -> 0, 2 -> +1 (same as
 //   the reference).  Padding rows and padding K positions hold code 1
 //   (weight 0).
+//
+// Device layout of a 2:4 sparse weight (every group of 4 K positions holds
+// exactly two +-1): the same tiles and chunks; block (t, c) is 3072 bytes,
+// 8 m-blocks of 384 bytes each, in the operand form of the sparse tensor-core
+// MMA (mma.sp m16n8k64 s8, ordered metadata): per m-block and k64 step s
+// (chunk K 64s .. 64s+63, 16 groups j) lane L = 4g + t holds
+//   * metadata: 8 nibbles, nibble i = (idx0 | idx1 << 2), the positions
+//     inside group j = 8 * (t >> 1) + i of row 16*mb + g + 8 * (t & 1)
+//     (idx0 < idx1) -- as uint2 (s = 0, 1) at byte 8L of the m-block record;
+//   * signs: 16 bits, bit 4i + e = the sign (1 = -1) of compressed value e of
+//     A register i, i.e. of nonzero (e & 1) of group 8 * (i >> 1) + 2t + (e >> 1)
+//     of row g + 8 * (i & 1) -- as the low (s = 0) / high (s = 1) half of the
+//     u32 at byte 256 + 4L.
+// 1.5 bits per weight, the size of the reference's own packing (3-bit
+// pattern in a nibble + 2 sign bits per group).  Padding rows and groups
+// hold positions (0, 1) with signs +1: their products meet zero activations
+// (K padding) or land in outputs that are never stored (row padding).
 #pragma once
 
 #include <cuda_runtime.h>
@@ -36,9 +53,14 @@ namespace ft {
 constexpr int kTileRows = 128;  // output channels per tile
 constexpr int kChunkK = 128;    // K codes per chunk
 constexpr int kBlockBytes = kTileRows * kChunkK / 4;  // 4096 (dense 2-bit block)
-// 2:4 sparse block: each row's 32 groups of 4 codes as 5-bit group codes
-// (pattern * 4 + signs, 24 = all-zero padding group), 20 bytes per row.
-constexpr int kSparseBlockBytes = kTileRows * 20;      // 2560
+// 2:4 sparse block: 8 m-blocks x 384 bytes (metadata + signs, see above).
+constexpr int kSparseMbBytes = 384;
+constexpr int kSparseBlockBytes = 8 * kSparseMbBytes;  // 3072
+// reference pattern p (the two nonzero positions of a group, in order) ->
+// metadata nibble idx0 | idx1 << 2: (0,1) (0,2) (0,3) (1,2) (1,3) (2,3)
+__host__ __device__ constexpr uint32_t sparse_nibble(int p) {
+  return (0xED9C84u >> (4 * p)) & 0xFu;
+}
 
 void set_error(const char* fmt, ...);
 extern std::atomic<uint64_t> g_launches;  // kernels launched by this library
@@ -97,9 +119,8 @@ __device__ __forceinline__ int digit_shift(float a, int D) {
 }
 
 // Weight w in {-1, 0, +1} at (row R, column k) of a resident weight, read from
-// its tiled layout (ft_internal.cuh header comment; 2:4 blocks: row records of
-// 32 five-bit group codes, group g of the chunk at bit 5g).  A slow scalar
-// lookup for the non-finite activation path.
+// its tiled layout (dense or 2:4, both described at the top of this file).  A
+// slow scalar lookup for the non-finite activation path and the export.
 __device__ __forceinline__ int weight_at(const uint8_t* codes, int format, int64_t n_chunks,
                                          int64_t R, int64_t k) {
   const int64_t t = R >> 7, c = k >> 7;
@@ -111,18 +132,17 @@ __device__ __forceinline__ int weight_at(const uint8_t* codes, int format, int64
     const int byte = blk[(mb * 32 + 4 * g + rr) * 16 + (2 * il + ih) * 4 + b];
     return ((byte >> (2 * j)) & 3) - 1;
   }
-  const uint8_t* rec = codes + (t * n_chunks + c) * kSparseBlockBytes + r * 20;
-  const int bit = 5 * (kk >> 2), e = kk & 3;
-  uint32_t v = rec[bit >> 3];
-  if ((bit & 7) > 3) v |= (uint32_t)rec[(bit >> 3) + 1] << 8;
-  v = (v >> (bit & 7)) & 31u;
-  if (v >= 24u) return 0;
-  const int p = (int)(v >> 2);
-  const int p0 = p < 3 ? 0 : (p < 5 ? 1 : 2);
-  const int p1 = p == 0 ? 1 : ((p == 1 || p == 3) ? 2 : 3);
-  if (e == p0) return (v & 1u) ? -1 : 1;
-  if (e == p1) return (v & 2u) ? -1 : 1;
-  return 0;
+  // 2:4: the metadata nibble of group j in k64 step s, then its sign bit
+  const uint8_t* mbr = codes + (t * n_chunks + c) * kSparseBlockBytes + (r >> 4) * kSparseMbBytes;
+  const int g = r & 7, h8 = (r >> 3) & 1, s = kk >> 6, j = (kk & 63) >> 2, e = kk & 3;
+  const uint32_t meta = reinterpret_cast<const uint32_t*>(mbr)[2 * (4 * g + 2 * (j >> 3) + h8) + s];
+  const uint32_t nib = (meta >> (4 * (j & 7))) & 0xFu;
+  const int i0 = (int)(nib & 3u), i1 = (int)(nib >> 2);
+  if (e != i0 && e != i1) return 0;
+  const int pos = e == i0 ? 0 : 1;
+  const uint32_t sg = reinterpret_cast<const uint32_t*>(mbr + 256)[4 * g + ((j & 7) >> 1)] >> (16 * s);
+  const int bit = 4 * (2 * (j >> 3) + h8) + 2 * (j & 1) + pos;
+  return ((sg >> bit) & 1u) ? -1 : 1;
 }
 
 // round(xs) as a 64-bit integer, |xs| < 2^63: integer-valued floats
@@ -210,10 +230,10 @@ struct ft_ctx {
 
 struct ft_weight {
   int device = 0;
-  int format = 0;             // 0: dense 2-bit (T128 tiles), 1: 2:4 sparse (5-bit groups)
+  int format = 0;             // 0: dense 2-bit (T128 tiles), 1: 2:4 sparse (mma.sp operand form)
   int64_t rows = 0, cols = 0;
   int64_t n_tiles = 0, n_chunks = 0;
-  uint8_t* codes = nullptr;   // n_tiles*n_chunks blocks of 4096 (dense) or 2560 (sparse) bytes
+  uint8_t* codes = nullptr;   // n_tiles*n_chunks blocks of 4096 (dense) or 3072 (sparse) bytes
   float* row_scales = nullptr;  // [n_tiles*128], zero on padding rows
 };
 

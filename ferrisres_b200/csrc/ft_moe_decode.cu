@@ -7,10 +7,10 @@
 //   R  router partial scores: one warp per (expert, 256-wide K part) loads
 //      that part of the router row once and dots it with every token (fp32,
 //      8 products per lane in order, then a butterfly) -- barrier;
-//   S  every CTA sums the parts in order and routes every token (softmax,
-//      stable descending top-k, renormalised gates: the reference's
-//      sequential order) and builds the tokens' int8-digit operand in shared
-//      memory;
+//   S  every CTA sums the parts in order and routes every token, one warp
+//      each (softmax with the exponentials' sum in the reference's order,
+//      stable descending top-k, renormalised gates) and builds the tokens'
+//      int8-digit operand in shared memory;
 //   G  gate||up: work units are (pair = token x chosen expert, 64-row block);
 //      a CTA's 8 warps split the unit's 128-K chunks, each streams its chunks'
 //      2-bit codes with 16-byte loads and runs mma.sync m16n8k32 (u8 codes AND
@@ -118,10 +118,10 @@ __device__ __forceinline__ void digit_words(const float (&v)[4], float f1, float
 // 4 digits at columns 4 * (r & 1) + d of n8 block r >> 1), with the column
 // sums and each row's scale 2^-sh.  Rows are built G at a time (G the largest
 // power of two <= min(NR, 8)) by 8 / G warps each.  A thread first issues
-// every load of its first kRq quads (`fetch`: raw values, positions clamped
-// into [0, n)), then transforms them (`xform`: raw -> fp32, applied again when
-// the digits are written), so a row costs about one memory round trip; quads
-// past kRq per thread are loaded again in a second pass.  colsum must be zero
+// every load of its first kRq quads (`fetch`: raw values; predicated, no
+// load past the row), then transforms them (`xform`: raw -> fp32, applied
+// again when the digits are written), so a row costs about one memory round
+// trip; quads past kRq per thread are loaded again in a second pass.  colsum must be zero
 // on entry.  Block-wide.
 constexpr int kRq = 12;
 template <class Fetch, class Xform>
@@ -140,25 +140,37 @@ __device__ void build_rows(int NR, Fetch fetch, Xform xform, int64_t n, int nchu
   for (int r0 = 0; r0 < NR; r0 += G) {
     const int r = r0 + slot;
     const bool live = r < NR;
+    // predicated loads (no branch), so all of them are in flight together;
+    // quads past the row are not loaded at all
     Raw raw[kRq][4];
 #pragma unroll
     for (int i = 0; i < kRq; ++i)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int64_t k = 4 * (int64_t)(ts + nthr * i) + e;
-        raw[i][e] = fetch(live ? r : 0, k < n ? k : n - 1);
+        raw[i][e] = (live && k < n) ? fetch(r, k) : Raw{};
       }
+    // each loaded value is transformed once (quads past the row are skipped)
+    float v[kRq][4];
     float am = 0.0f;
 #pragma unroll
-    for (int i = 0; i < kRq; ++i)
+    for (int i = 0; i < kRq; ++i) {
+      const int q = ts + nthr * i;
 #pragma unroll
-      for (int e = 0; e < 4; ++e)
-        am = fmaxf(am, fabsf(value(raw[i][e], 4 * (int64_t)(ts + nthr * i) + e)));
-    for (int q = ts + nthr * kRq; q < nquad; q += nthr)
+      for (int e = 0; e < 4; ++e) v[i][e] = 0.0f;
+      if (q < nquad) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          v[i][e] = value(raw[i][e], 4 * (int64_t)q + e);
+          am = fmaxf(am, fabsf(v[i][e]));
+        }
+      }
+    }
+    for (int q = ts + nthr * kRq; live && q < nquad; q += nthr)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int64_t k = 4 * (int64_t)q + e;
-        am = fmaxf(am, fabsf(value(fetch(live ? r : 0, k < n ? k : n - 1), k)));
+        am = fmaxf(am, fabsf(value(k < n ? fetch(r, k) : Raw{}, k)));
       }
     am = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(am)));
     if (lane == 0) red[warp] = am;
@@ -182,21 +194,14 @@ __device__ void build_rows(int NR, Fetch fetch, Xform xform, int64_t n, int nchu
         }
       };
 #pragma unroll
-      for (int i = 0; i < kRq; ++i) {
-        const int q = ts + nthr * i;
-        if (q < nquad) {
-          float x[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) x[e] = value(raw[i][e], 4 * (int64_t)q + e);
-          emit(q, x);
-        }
-      }
+      for (int i = 0; i < kRq; ++i)
+        if (ts + nthr * i < nquad) emit(ts + nthr * i, v[i]);
       for (int q = ts + nthr * kRq; q < nquad; q += nthr) {
         float x[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int64_t k = 4 * (int64_t)q + e;
-          x[e] = value(fetch(r, k < n ? k : n - 1), k);
+          x[e] = value(k < n ? fetch(r, k) : Raw{}, k);
         }
         emit(q, x);
       }
@@ -359,37 +364,75 @@ __global__ void __launch_bounds__(kMdThreads, 1) moe_decode_kernel(const __grid_
   }
   if (tid < kMdMaxPairs * 4) colsum[tid >> 2][tid & 3] = 0;
   __syncthreads();
-  if (tid < T) {
-    float* s = sc[tid];
-    float mx = -INFINITY;
-    for (int e = 0; e < E; ++e) mx = fmaxf(mx, s[e]);
+  // warp t routes token t: lanes hold experts lane and lane + 32 (E <= 64);
+  // the max, the exponentials and the divisions are elementwise or exact, the
+  // sum of the exponentials runs in the reference's order on lane 0, top-k
+  // takes the largest probability, the lowest index among equals
+  if (warp < T) {
+    const int t = warp;
+    float* s = sc[t];
+    const bool h0 = lane < E, h1 = lane + 32 < E;
+    const float v0 = h0 ? s[lane] : -INFINITY, v1 = h1 ? s[lane + 32] : -INFINITY;
+    float mx = fmaxf(v0, v1);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const float e0 = h0 ? expf(v0 - mx) : 0.0f, e1 = h1 ? expf(v1 - mx) : 0.0f;
+    if (h0) s[lane] = e0;
+    if (h1) s[lane + 32] = e1;
+    __syncwarp();
     float se = 0.0f;
-    for (int e = 0; e < E; ++e) {
-      s[e] = expf(s[e] - mx);
-      se += s[e];
-    }
-    for (int e = 0; e < E; ++e) s[e] = s[e] / se;
+    if (lane == 0)
+      for (int e = 0; e < E; ++e) se += s[e];
+    se = __shfl_sync(0xffffffffu, se, 0);
+    const float p0 = e0 / se, p1 = e1 / se;
+    __syncwarp();
+    if (h0) s[lane] = p0;
+    if (h1) s[lane + 32] = p1;
+    __syncwarp();
     uint64_t taken = 0;
     float wsum = 0.0f;
     for (int k = 0; k < K; ++k) {
-      int best = -1;
-      for (int e = 0; e < E; ++e)
-        if (!((taken >> e) & 1ull) && (best < 0 || s[e] > s[best])) best = e;
-      taken |= 1ull << best;
-      sel[tid * K + k] = best;
-      wsum += s[best];
-    }
-    for (int k = 0; k < K; ++k) {
-      const float p = s[sel[tid * K + k]];
-      wts[tid * K + k] = wsum > 0.0f ? p / wsum : p;
-    }
-    if (blockIdx.x == 0) {
-      for (int k = 0; k < K; ++k) {
-        P.topk_idx[tid * K + k] = sel[tid * K + k];
-        P.topk_w[tid * K + k] = wts[tid * K + k];
+      // candidates (valid, value, index); a beats b: valid first, then larger, then lower index
+      bool bv = h0 && !((taken >> lane) & 1ull);
+      float bp = p0;
+      int bi = lane;
+      if (h1 && !((taken >> (lane + 32)) & 1ull) && (!bv || p1 > bp)) {
+        bv = true;
+        bp = p1;
+        bi = lane + 32;
       }
-      if (P.probs)
-        for (int e = 0; e < E; ++e) P.probs[tid * E + e] = s[e];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const bool ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const float op = __shfl_xor_sync(0xffffffffu, bp, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov && (!bv || op > bp || (!(op < bp) && oi < bi))) {
+          bv = ov;
+          bp = op;
+          bi = oi;
+        }
+      }
+      taken |= 1ull << bi;
+      if (lane == 0) {
+        sel[t * K + k] = bi;
+        wsum += s[bi];
+      }
+    }
+    if (lane == 0)
+      for (int k = 0; k < K; ++k) {
+        const float p = s[sel[t * K + k]];
+        wts[t * K + k] = wsum > 0.0f ? p / wsum : p;
+      }
+    __syncwarp();
+    if (blockIdx.x == 0) {
+      if (lane < K) {
+        P.topk_idx[t * K + lane] = sel[t * K + lane];
+        P.topk_w[t * K + lane] = wts[t * K + lane];
+      }
+      if (P.probs) {
+        if (h0) P.probs[t * E + lane] = p0;
+        if (h1) P.probs[t * E + lane + 32] = p1;
+      }
     }
   }
   __syncthreads();

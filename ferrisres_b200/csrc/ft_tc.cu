@@ -260,10 +260,11 @@ __device__ __forceinline__ void epilogue_group(const TqProblem& p, int digits, b
 
 template <int NPAD, bool kSparse>
 __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_constant__ TqBatch b) {
-  // weight block bytes in HBM and in the smem ring (2:4 blocks use the first 2560 bytes)
+  // weight block bytes in HBM and in the smem ring (2:4 blocks use the first 3072 bytes)
   constexpr uint32_t kBlk = kSparse ? kSparseBlockBytes : kBlockBytes;
-  // 2:4 group code -> four unsigned codes w+1 (bytes in K order); 24..31 = zero group
-  __shared__ uint32_t s_lut[32];
+  // 2:4 group (metadata nibble << 2 | the two sign bits) -> four unsigned
+  // codes w + 1 (bytes in K order)
+  __shared__ uint32_t s_lut[64];
   // dynamic smem: [kSA weight blocks of 4096 B][kSBS B super-stages of kSK*NPAD*128 B]
   extern __shared__ __align__(1024) uint8_t smem_dyn[];
   constexpr uint32_t kBStage = NPAD * 128;       // B bytes per chunk
@@ -293,18 +294,11 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  if (kSparse && threadIdx.x < 32) {
-    const int c = threadIdx.x;
+  if (kSparse && threadIdx.x < 64) {
+    const uint32_t c = threadIdx.x, i0 = (c >> 2) & 3u, i1 = c >> 4;
     uint32_t v = 0x01010101u;
-    if (c < 24) {
-      const int pat = c >> 2, sg = c & 3;
-      // pattern -> positions (0,1),(0,2),(0,3),(1,2),(1,3),(2,3)
-      const int p0 = pat < 3 ? 0 : (pat < 5 ? 1 : 2);
-      const int p1 = pat == 0 ? 1 : (pat == 1 || pat == 3) ? 2 : 3;
-      v &= ~(0xFFu << (8 * p0)) & ~(0xFFu << (8 * p1));
-      v |= (uint32_t)((sg & 1) ? 0 : 2) << (8 * p0);
-      v |= (uint32_t)((sg & 2) ? 0 : 2) << (8 * p1);
-    }
+    v ^= ((c & 1u) ? 1u : 3u) << (8 * i0);  // byte 1 -> 0 (w = -1) or 2 (w = +1)
+    v ^= ((c & 2u) ? 1u : 3u) << (8 * i1);
     s_lut[c] = v;
   }
   if (threadIdx.x == 0) {
@@ -351,7 +345,7 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
     }
     while (cs.valid(b)) {
       const int n = cs.ss_len();
-      uint32_t wv[kSK][8];  // 2:4 sparse: row r's 5 words per chunk
+      uint32_t wv[kSK][8];  // 2:4 sparse: row r's 4 metadata words and 4 sign words per chunk
       uint4 wd[kSK][2];     // dense: this lane's 16 bytes of m-blocks 2*sub and 2*sub+1
 #pragma unroll
       for (int j = 0; j < kSK; ++j) {
@@ -359,11 +353,19 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
           const uint32_t sa = gb % kSA;
           ok = ok && tc::mbar_wait(tc::smem_u32(&bar_sa_full[sa]), (gb / kSA) & 1, b.err, 10);
           if (kSparse) {
-            // row r's 20 bytes: stride 5 words -> conflict-free across the warp
-            const uint32_t* rw = reinterpret_cast<const uint32_t*>(smem_a + sa * kBlockBytes) + r * 5;
+            // row r's metadata (groups 0-7 and 8-15 of both k64 steps) and the
+            // sign words of the 4 lanes holding its values
+            const unsigned char* mbr = smem_a + sa * kBlockBytes + (r >> 4) * kSparseMbBytes;
+            const uint32_t* mw = reinterpret_cast<const uint32_t*>(mbr);
+            const uint32_t* sw = reinterpret_cast<const uint32_t*>(mbr + 256);
+            const int g8 = r & 7, h8 = (r >> 3) & 1;
 #pragma unroll
-            for (int i = 0; i < 5; ++i) wv[j][i] = ok ? rw[i] : 0u;
-            wv[j][5] = wv[j][6] = wv[j][7] = 0u;
+            for (int i = 0; i < 2; ++i) {
+              wv[j][2 * i] = ok ? mw[2 * (4 * g8 + 2 * i + h8)] : 0u;
+              wv[j][2 * i + 1] = ok ? mw[2 * (4 * g8 + 2 * i + h8) + 1] : 0u;
+            }
+#pragma unroll
+            for (int t2 = 0; t2 < 4; ++t2) wv[j][4 + t2] = ok ? sw[4 * g8 + t2] : 0u;
           } else {
             // the warp reads its two m-blocks as 2 x 512 contiguous bytes
             const uint4* blk = reinterpret_cast<const uint4*>(smem_a + sa * kBlockBytes);
@@ -384,16 +386,17 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
         if (j < n) {
           const uint32_t col = kACol0 + (s * kSK + j) * 32;
           if (kSparse) {
+            const int h8 = (r >> 3) & 1;
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {  // two halves of 64 codes: 16 TMEM columns each
+            for (int h = 0; h < 2; ++h) {  // k64 step h: 16 groups = 16 TMEM columns
               uint32_t a[16];
 #pragma unroll
-              for (int gg = 0; gg < 16; ++gg) {  // group g covers K 4g..4g+3 = TMEM column g
-                const int bit = 5 * (h * 16 + gg);
-                const int wi = bit >> 5, sh = bit & 31;
-                const uint32_t v = sh <= 27 ? (wv[j][wi] >> sh) & 31u
-                                            : __funnelshift_r(wv[j][wi], wv[j][wi + 1], sh) & 31u;
-                a[gg] = s_lut[v];
+              for (int gg = 0; gg < 16; ++gg) {  // group gg covers K 4gg..4gg+3
+                const uint32_t meta = wv[j][2 * (gg >> 3) + h];
+                const uint32_t nib = (meta >> (4 * (gg & 7))) & 0xFu;
+                const uint32_t sgw = wv[j][4 + ((gg & 7) >> 1)] >> (16 * h);
+                const uint32_t sb = (sgw >> (4 * (2 * (gg >> 3) + h8) + 2 * (gg & 1))) & 3u;
+                a[gg] = s_lut[(nib << 2) | sb];
               }
               if (ok) tc::tmem_st_x16(tmem + lane_off + col + 16 * h, a);
             }

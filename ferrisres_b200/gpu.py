@@ -129,7 +129,7 @@ class DeviceTernaryWeight:
     @classmethod
     def from_sparse_host(cls, patterns, signs, rows, cols, row_scales, device=None):
         """2:4 weights in the reference SparseTernaryMatrix layout
-        (src/model/sparse_ternary.rs:52-70); stored at 1.25 bits/weight."""
+        (src/model/sparse_ternary.rs:52-70); stored at 1.5 bits/weight."""
         ctx = get_context(device)
         ng = rows * cols // 4
         pt, sg = _host(patterns, np.uint8), _host(signs, np.uint8)

@@ -11,7 +11,7 @@ little-endian, 24-byte header, then the host SparseTernaryMatrix layout
 byte; two sign bits per group, four groups per byte, bit set = +1).  The
 reference decodes a file into a host SparseTernaryMatrix on first access; here
 the pattern and sign bytes go to the device as they are and are repacked there
-into the 1.25 bit/weight 2:4 format (`ft_sparse_upload_host`), with the file's
+into the 1.5 bit/weight 2:4 format (`ft_sparse_upload_host`), with the file's
 single scale broadcast to every row (the reference's `gpu_packed()` semantics,
 src/model/cpu_moe.rs:73-78).
 """

@@ -90,8 +90,10 @@ int ft_weight_from_device_u32(ft_ctx* ctx, const uint32_t* words_dev, int64_t ro
  * From the reference host type SparseTernaryMatrix (src/model/sparse_ternary.rs:52-70):
  * patterns = ceil(groups/2) bytes (3-bit pattern, even group in the low nibble),
  * signs = ceil(groups/4) bytes (2 bits per group, 1 = +1); groups = rows*cols/4,
- * cols % 4 == 0.  Stored on the device at 1.25 bits per weight (5-bit group
- * codes) and usable with every ft_ternary_matmul_* entry point. */
+ * cols % 4 == 0.  Stored on the device at 1.5 bits per weight, in the operand
+ * form of the sparse tensor-core MMA (per group a 4-bit position nibble = the
+ * 2:4 metadata, and one sign bit per nonzero), and usable with every
+ * ft_ternary_matmul_* entry point. */
 int ft_sparse_upload_host(ft_ctx* ctx, const uint8_t* patterns_host, const uint8_t* signs_host,
                           int64_t rows, int64_t cols, const float* row_scales_host,
                           ft_weight** out);

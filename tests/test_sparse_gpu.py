@@ -129,7 +129,7 @@ def test_sparse_grouped_and_bytes(gpu):
     gpu.GroupCall(ws, [xt] * 3, ys)()
     for y, ref, c in zip(ys, refs, conds):
         assert_fp32_close(y.cpu().numpy(), ref, c, what="sparse grouped")
-    # 1.25 bits/weight on the device (plus row scales)
-    assert ws[0].device_bytes() == (rows // 128 + (rows % 128 > 0)) * (cols // 128) * 2560 + \
+    # 1.5 bits/weight on the device (metadata nibble + 2 sign bits per group; plus row scales)
+    assert ws[0].device_bytes() == (rows // 128 + (rows % 128 > 0)) * (cols // 128) * 3072 + \
         (rows + 127) // 128 * 128 * 4
     gpu.get_context().check()
