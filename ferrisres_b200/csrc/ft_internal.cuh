@@ -281,10 +281,14 @@ int launch_tc_matmul(ft_ctx* ctx, const ft_weight* w, int64_t seq, const void* x
 // 0 = kDigitsExact); ignored for int8 codes.
 // kscale/kblock (fp32/bf16 only): one scale per kblock columns, folded into
 // the activations (the blocked matmul); applies to every problem of the group.
+// act (MoE gate/up weights with interleaved 16-row gate/up m-blocks, 4
+// digits): 1 = SwiGLU, 2 = GeLU-tanh; output y[t * ldy + j] = act(gate_j,
+// up_j) for j < fout instead of the weight's rows.
 int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t seq,
                       const void* const* xs, int xkind, const float* const* sxs, float* const* ys,
                       const int64_t* ldys, cudaStream_t s, const int64_t* seqs = nullptr,
-                      int digits = 0, const float* kscale = nullptr, int64_t kblock = 1);
+                      int digits = 0, const float* kscale = nullptr, int64_t kblock = 1,
+                      int act = 0, int64_t fout = 0);
 // Decode-shape kernel (ft_gemv.cu): dense problems whose activations fit 16
 // operand columns; the kernel builds its activation operand itself.
 constexpr int kGemvMaxSmem = 200 * 1024;

@@ -349,24 +349,29 @@ __global__ void moe_gather_kernel(const void* __restrict__ x, int elem_bytes, in
   }
 }
 
-// h[r, i] = silu(g) * u with silu(g) = g / (1 + exp(-g))  (ternary_moe.rs:206-209),
-// or gelu_tanh(g) (ternary_moe.rs:199-204); gu rows are [gate (F) | up (F)].
-__global__ void moe_act_kernel(const float* __restrict__ gu, int64_t rows, int64_t F, int use_gelu,
-                               float* __restrict__ h) {
+// The gate/up weight of an expert as one matrix with interleaved 16-row
+// m-blocks: m-block 2b = gate rows 16b .. 16b+15, m-block 2b+1 = up rows
+// 16b .. 16b+15 (2 * ceil(F/16) m-blocks; missing rows are weight 0, scale 0),
+// so the engine's epilogue finds a gate row and its up row 16 lanes apart.
+// One thread per uint4 of the stacked blocks (32 per m-block per chunk).
+__global__ void interleave_gu_kernel(const uint4* __restrict__ gate, const uint4* __restrict__ up,
+                                     const float* __restrict__ gs, const float* __restrict__ us,
+                                     int64_t src_tiles, int64_t n_chunks, int64_t total,
+                                     uint4* __restrict__ dst, float* __restrict__ dscale) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= rows * F) return;
-  const int64_t r = i / F, c = i % F;
-  const float g = gu[r * 2 * F + c];
-  float out;
-  if (use_gelu) {
-    const float ta = __fmul_rn(0.7978845608f,
-                               __fadd_rn(g, __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, g), g), g)));
-    out = __fmul_rn(__fmul_rn(0.5f, g), __fadd_rn(1.0f, tanhf(ta)));
-  } else {
-    const float silu = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
-    out = __fmul_rn(silu, gu[r * 2 * F + F + c]);
+  if (i >= total) return;
+  const int lane = (int)(i & 31), M = (int)((i >> 5) & 7);
+  const int64_t blk = i >> 8, T = blk / n_chunks, c = blk % n_chunks;
+  const int64_t b = 4 * T + (M >> 1);  // source m-block
+  const int64_t st = b >> 3;
+  const uint4* src = (M & 1) ? up : gate;
+  uint4 v = make_uint4(0x55555555u, 0x55555555u, 0x55555555u, 0x55555555u);  // code 1: w = 0
+  if (st < src_tiles) v = src[((st * n_chunks + c) * 8 + (b & 7)) * 32 + lane];
+  dst[i] = v;
+  if (c == 0 && lane < 16) {
+    const float* ss = (M & 1) ? us : gs;
+    dscale[T * kTileRows + 16 * M + lane] = st < src_tiles ? ss[16 * b + lane] : 0.0f;
   }
-  h[i] = out;
 }
 
 // y[t, j] = sum_k w[t, k] * o[slot_of[t, k], j], accumulated from 0 in k order
@@ -411,10 +416,39 @@ struct MoeBufs {
   int32_t* slot_of;
   int32_t* token_of;
   void* xg;
-  float* gu;
   float* h;
   float* o;
 };
+
+// gate/up rows of the interleaved weight: 32 per 16 rows of F
+int64_t gu_rows(int64_t F) { return 32 * ceil_div(F, 16); }
+
+// Stacks separately uploaded gate and up weights ([F, H] each) into the
+// interleaved gate/up weight; the two inputs are destroyed.
+int stack_gate_up(ft_ctx* ctx, ft_weight* gate, ft_weight* up, cudaStream_t s, ft_weight** out) {
+  *out = nullptr;
+  ft_weight* w = nullptr;
+  int st = alloc_weight(ctx, gu_rows(gate->rows), gate->cols, &w);
+  if (st == FT_OK) {
+    const int64_t total = w->n_tiles * w->n_chunks * 256;
+    interleave_gu_kernel<<<(unsigned)ceil_div(total, 256), 256, 0, s>>>(
+        reinterpret_cast<const uint4*>(gate->codes), reinterpret_cast<const uint4*>(up->codes),
+        gate->row_scales, up->row_scales, gate->n_tiles, w->n_chunks, total,
+        reinterpret_cast<uint4*>(w->codes), w->row_scales);
+    const cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) g_launches.fetch_add(1, std::memory_order_relaxed);
+    const cudaError_t e2 = e == cudaSuccess ? cudaStreamSynchronize(s) : e;
+    if (e2 != cudaSuccess) st = fail(FT_ERR_GPU, "gate/up stacking failed: %s", cudaGetErrorString(e2));
+  }
+  ft_weight_destroy(gate);
+  ft_weight_destroy(up);
+  if (st != FT_OK) {
+    ft_weight_destroy(w);
+    return st;
+  }
+  *out = w;
+  return FT_OK;
+}
 
 // Layout of the forward intermediates for T tokens.
 size_t moe_layout(const ft_moe* m, int64_t T, int x_bytes, char* base, MoeBufs* b) {
@@ -433,7 +467,6 @@ size_t moe_layout(const ft_moe* m, int64_t T, int x_bytes, char* base, MoeBufs* 
   b->slot_of = reinterpret_cast<int32_t*>(take(n * 4));
   b->token_of = reinterpret_cast<int32_t*>(take(n * 4));
   b->xg = take((size_t)n * m->H * x_bytes);
-  b->gu = reinterpret_cast<float*>(take((size_t)n * 2 * m->F * 4));
   b->h = reinterpret_cast<float*>(take((size_t)n * m->F * 4));
   b->o = reinterpret_cast<float*>(take((size_t)n * m->H * 4));
   return off;
@@ -460,13 +493,13 @@ int moe_route(ft_ctx* ctx, ft_moe* m, int64_t T, const void* x, int bf16, int32_
 // Expert FFN over rows grouped in segments: segment i has seg_rows[i] rows for
 // expert seg_expert[i], stored consecutively in x_rows / y_rows.
 int moe_expert_segments(ft_ctx* ctx, ft_moe* m, int nseg, const int32_t* seg_expert,
-                        const int64_t* seg_rows, const void* x_rows, int bf16, float* gu,
-                        float* h, float* y_rows, cudaStream_t s) {
+                        const int64_t* seg_rows, const void* x_rows, int bf16, float* h,
+                        float* y_rows, cudaStream_t s) {
   FT_CHECK(nseg >= 0 && nseg <= 64, FT_ERR_UNSUPPORTED, "at most 64 segments per call");
   int64_t total = 0;
   std::vector<const ft_weight*> wgu(nseg), wd(nseg);
   std::vector<const void*> xs(nseg), hs(nseg);
-  std::vector<float*> gus(nseg), ys(nseg);
+  std::vector<float*> hw(nseg), ys(nseg);
   const int xb = bf16 ? 2 : 4;
   for (int i = 0; i < nseg; ++i) {
     FT_CHECK(seg_expert[i] >= 0 && seg_expert[i] < m->E, FT_ERR_SHAPE, "segment %d: bad expert %d",
@@ -477,20 +510,19 @@ int moe_expert_segments(ft_ctx* ctx, ft_moe* m, int nseg, const int32_t* seg_exp
     wgu[i] = m->gate_up[seg_expert[i]];
     wd[i] = m->down[seg_expert[i]];
     xs[i] = static_cast<const char*>(x_rows) + total * m->H * xb;
-    gus[i] = gu + total * 2 * m->F;
-    hs[i] = h + total * m->F;
+    hw[i] = h + total * m->F;
+    hs[i] = hw[i];
     ys[i] = y_rows + total * m->H;
     total += seg_rows[i];
   }
   if (total == 0) return FT_OK;
   // Expert GEMMs take kDigitsMoE fixed-point digits per token: the layer's
-  // tolerance is 1e-4 of each output row's rms (ft_internal.cuh).
-  int st = launch_tc_grouped(ctx, nseg, wgu.data(), 0, xs.data(), bf16 ? 1 : 0, nullptr, gus.data(),
-                             nullptr, s, seg_rows, kDigitsMoE);
+  // tolerance is 1e-4 of each output row's rms (ft_internal.cuh).  The gate/up
+  // GEMM's epilogue applies the activation and writes h [rows, F] itself.
+  int st = launch_tc_grouped(ctx, nseg, wgu.data(), 0, xs.data(), bf16 ? 1 : 0, nullptr, hw.data(),
+                             nullptr, s, seg_rows, kDigitsMoE, nullptr, 1, m->use_gelu ? 2 : 1,
+                             m->F);
   if (st != FT_OK) return st;
-  moe_act_kernel<<<(unsigned)ceil_div(total * m->F, 256), 256, 0, s>>>(gu, total, m->F, m->use_gelu,
-                                                                       h);
-  FT_LAUNCH_CHECK();
   return launch_tc_grouped(ctx, nseg, wd.data(), 0, hs.data(), 0, nullptr, ys.data(), nullptr, s,
                            seg_rows, kDigitsMoE);
 }
@@ -591,9 +623,6 @@ int ft_moe_create(ft_ctx* ctx, int64_t n_experts, int64_t hidden, int64_t inter,
     e = cudaMemcpy(m->router, router_host, (size_t)n_experts * hidden * 4, cudaMemcpyHostToDevice);
   if (e != cudaSuccess) st = fail(FT_ERR_GPU, "router upload failed: %s", cudaGetErrorString(e));
   if (st == FT_OK) st = prepare_router_planes(m, router_host);
-  const size_t mat_bytes = (size_t)(inter * hidden) / 4;
-  std::vector<uint8_t> gu_bytes(2 * mat_bytes);
-  std::vector<float> gu_scales(2 * inter);
   for (int64_t x = 0; x < n_experts && st == FT_OK; ++x) {
     if (!gate_packed[x]) {  // expert held by another rank (expert parallelism)
       m->gate_up.push_back(nullptr);
@@ -602,14 +631,16 @@ int ft_moe_create(ft_ctx* ctx, int64_t n_experts, int64_t hidden, int64_t inter,
     }
     FT_CHECK(up_packed[x] && down_packed[x] && gate_scales[x] && up_scales[x] && down_scales[x],
              FT_ERR_SHAPE, "expert %lld: gate given but up/down/scales missing", (long long)x);
-    // [gate; up] stacked: the flat code streams of two row-major matrices
-    // concatenate into one [2F, H] matrix (F*H % 4 == 0 keeps bytes aligned).
-    memcpy(gu_bytes.data(), gate_packed[x], mat_bytes);
-    memcpy(gu_bytes.data() + mat_bytes, up_packed[x], mat_bytes);
-    memcpy(gu_scales.data(), gate_scales[x], inter * 4);
-    memcpy(gu_scales.data() + inter, up_scales[x], inter * 4);
-    ft_weight* w = nullptr;
-    st = ft_weight_upload_packed_u8(ctx, gu_bytes.data(), 2 * inter, hidden, gu_scales.data(), &w);
+    // gate and up uploaded separately, then interleaved by 16-row m-blocks
+    ft_weight *wg = nullptr, *wu = nullptr, *w = nullptr;
+    st = ft_weight_upload_packed_u8(ctx, gate_packed[x], inter, hidden, gate_scales[x], &wg);
+    if (st == FT_OK) st = ft_weight_upload_packed_u8(ctx, up_packed[x], inter, hidden, up_scales[x], &wu);
+    if (st == FT_OK) {
+      st = stack_gate_up(ctx, wg, wu, ctx->host_stream, &w);
+    } else {
+      ft_weight_destroy(wg);
+      ft_weight_destroy(wu);
+    }
     if (st != FT_OK) break;
     m->gate_up.push_back(w);
     st = ft_weight_upload_packed_u8(ctx, down_packed[x], hidden, inter, down_scales[x], &w);
@@ -658,11 +689,10 @@ int ft_moe_create_f32(ft_ctx* ctx, int64_t n_experts, int64_t hidden, int64_t in
   cudaError_t e = cudaMalloc(&m->router, (size_t)n_experts * hidden * 4);
   if (e == cudaSuccess)
     e = cudaMemcpy(m->router, router_host, (size_t)n_experts * hidden * 4, cudaMemcpyHostToDevice);
-  if (e == cudaSuccess) e = cudaMalloc(&staging, (size_t)(2 * inter * hidden) * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&staging, (size_t)(inter * hidden) * 4);
   if (e != cudaSuccess) st = fail(FT_ERR_GPU, "MoE upload failed: %s", cudaGetErrorString(e));
   if (st == FT_OK) st = prepare_router_planes(m, router_host);
   const size_t mat = (size_t)(inter * hidden);
-  std::vector<float> gu_scales(2 * inter);
   for (int64_t x = 0; x < n_experts && st == FT_OK; ++x) {
     if (!gate_f32[x]) {  // expert held by another rank (expert parallelism)
       m->gate_up.push_back(nullptr);
@@ -675,31 +705,33 @@ int ft_moe_create_f32(ft_ctx* ctx, int64_t n_experts, int64_t hidden, int64_t in
     }
     // TernaryExpert::from_fp32 (src/model/cpu_moe.rs:33-37) per matrix: the
     // absmean scale of quantize_ternary, then the rounding rule, here on the
-    // device straight into the tiled layout; gate and up stacked as [2F, H].
-    const float ag = host_absmean_alpha(gate_f32[x], (int64_t)mat);
-    const float au = host_absmean_alpha(up_f32[x], (int64_t)mat);
+    // device straight into the tiled layout; gate and up are then interleaved.
     const float ad = host_absmean_alpha(down_f32[x], (int64_t)mat);
-    for (int64_t i = 0; i < inter; ++i) {
-      gu_scales[i] = ag;
-      gu_scales[inter + i] = au;
-    }
+    ft_weight* part[2] = {nullptr, nullptr};
     ft_weight* w = nullptr;
-    st = alloc_weight(ctx, 2 * inter, hidden, &w);
-    if (st != FT_OK) break;
-    m->gate_up.push_back(w);
-    e = cudaMemcpyAsync(staging, gate_f32[x], mat * 4, cudaMemcpyHostToDevice, s);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(staging + mat, up_f32[x], mat * 4, cudaMemcpyHostToDevice, s);
-    if (e == cudaSuccess) e = cudaMemsetAsync(w->row_scales, 0, (size_t)w->n_tiles * kTileRows * 4, s);
-    if (e == cudaSuccess)
-      e = cudaMemcpyAsync(w->row_scales, gu_scales.data(), (size_t)(2 * inter) * 4,
-                          cudaMemcpyHostToDevice, s);
-    if (e == cudaSuccess) st = launch_quantize_pack(staging, false, 0, w, s);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
-    if (e != cudaSuccess || st != FT_OK) {
-      if (st == FT_OK) st = fail(FT_ERR_GPU, "expert upload failed: %s", cudaGetErrorString(e));
+    for (int i = 0; i < 2 && st == FT_OK; ++i) {
+      const float* src = i == 0 ? gate_f32[x] : up_f32[x];
+      st = alloc_weight(ctx, inter, hidden, &part[i]);
+      if (st != FT_OK) break;
+      e = cudaMemcpyAsync(staging, src, mat * 4, cudaMemcpyHostToDevice, s);
+      if (e == cudaSuccess) st = launch_fill_scales(part[i], host_absmean_alpha(src, (int64_t)mat), s);
+      if (e == cudaSuccess && st == FT_OK) st = launch_quantize_pack(staging, false, 0, part[i], s);
+      if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+      if (e != cudaSuccess && st == FT_OK)
+        st = fail(FT_ERR_GPU, "expert upload failed: %s", cudaGetErrorString(e));
+    }
+    if (st == FT_OK) {
+      st = stack_gate_up(ctx, part[0], part[1], s, &w);
+    } else {
+      ft_weight_destroy(part[0]);
+      ft_weight_destroy(part[1]);
+    }
+    if (st != FT_OK) {
+      m->gate_up.push_back(nullptr);
       m->down.push_back(nullptr);
       break;
     }
+    m->gate_up.push_back(w);
     st = alloc_weight(ctx, hidden, inter, &w);
     if (st != FT_OK) {
       m->down.push_back(nullptr);
@@ -792,13 +824,12 @@ int ft_moe_expert_ffn(ft_ctx* ctx, ft_moe* m, int nseg, const int32_t* seg_exper
   int64_t total = 0;
   for (int i = 0; i < nseg; ++i) total += seg_rows_host[i] > 0 ? seg_rows_host[i] : 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // gate/up and activation scratch: 3F floats per row
-  int st = moe_reserve(m, (size_t)total * 3 * m->F * 4 + 512, s);
+  // activation scratch: F floats per row
+  int st = moe_reserve(m, (size_t)total * m->F * 4 + 512, s);
   if (st != FT_OK) return st;
-  float* gu = static_cast<float*>(m->buf.ptr);
-  float* h = gu + round_up(total * 2 * m->F, 64);
+  float* h = static_cast<float*>(m->buf.ptr);
   return moe_expert_segments(ctx, m, nseg, seg_expert_host, seg_rows_host, x_rows_dev, x_is_bf16,
-                             gu, h, y_rows_dev, s);
+                             h, y_rows_dev, s);
 }
 
 int ft_moe_combine(ft_ctx* ctx, ft_moe* m, int64_t T, const float* o_rows_dev,
@@ -848,7 +879,7 @@ int ft_moe_forward(ft_ctx* ctx, ft_moe* m, int64_t T, const void* x_dev, int x_i
       ex[e] = (int32_t)e;
       rows[e] = m->counts_host[e];
     }
-    st = moe_expert_segments(ctx, m, (int)m->E, ex.data(), rows.data(), b.xg, x_is_bf16, b.gu, b.h,
+    st = moe_expert_segments(ctx, m, (int)m->E, ex.data(), rows.data(), b.xg, x_is_bf16, b.h,
                              b.o, s);
   }
   if (st == FT_OK) st = ft_moe_combine(ctx, m, T, b.o, b.slot_of, b.topk_w, y_dev, s);

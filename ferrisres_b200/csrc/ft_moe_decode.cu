@@ -43,12 +43,13 @@ struct MdParams {
   int nparts;  // 256-wide K parts of the router dot
   int x_vec;   // H % 8 == 0 and x 16-byte aligned: vector loads
   int64_t H, F;
+  int64_t F2;             // rows of the interleaved gate/up weight (16-row gate/up m-blocks)
   int64_t nch_h, nch_f;   // 128-K chunks of H and of F
   const void* x;          // [T, H]
   const float* router;    // [E, H]
   const void* const* tab; // [4][E]: gate_up codes, gate_up scales, down codes, down scales
   float* logits;          // [T, E, nparts] partial router scores
-  float* gu;              // [P, 2F]
+  float* gu;              // [P, F2] interleaved gate/up rows
   float* o;               // [P, H]
   int32_t* topk_idx;      // [T, K] (output)
   float* topk_w;          // [T, K] (output)
@@ -297,7 +298,7 @@ __global__ void __launch_bounds__(kMdThreads, 1) moe_decode_kernel(const __grid_
   const uint4* frag4 = reinterpret_cast<const uint4*>(frag);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int T = P.T, K = P.K, E = P.E, NP = T * K;
-  const int64_t H = P.H, F = P.F;
+  const int64_t H = P.H, F = P.F, F2 = P.F2;
   unsigned target = 0;
   tc::pdl_wait();
 
@@ -450,7 +451,7 @@ __global__ void __launch_bounds__(kMdThreads, 1) moe_decode_kernel(const __grid_
   }
 
   // ---- G: gate||up of every (token, expert) pair
-  const int64_t rb_gu = (2 * F + kMdRows - 1) / kMdRows;
+  const int64_t rb_gu = (F2 + kMdRows - 1) / kMdRows;
   if ((int64_t)blockIdx.x >= NP * rb_gu && tid == 0) {
     // no G unit here: pull the chosen experts' down weights into L2 for D
     const int64_t idle = gridDim.x - NP * rb_gu, me = blockIdx.x - NP * rb_gu;
@@ -468,8 +469,8 @@ __global__ void __launch_bounds__(kMdThreads, 1) moe_decode_kernel(const __grid_
     const int p = (int)(u / rb_gu);
     const int64_t rb = u % rb_gu;
     const int e = sel[p];
-    unit_matvec(static_cast<const uint4*>(P.tab[e]), static_cast<const float*>(P.tab[E + e]), 2 * F,
-                P.nch_h, rb, p / K, nbx, frag4, colsum, tok_scale, part, P.gu + (int64_t)p * 2 * F);
+    unit_matvec(static_cast<const uint4*>(P.tab[e]), static_cast<const float*>(P.tab[E + e]), F2,
+                P.nch_h, rb, p / K, nbx, frag4, colsum, tok_scale, part, P.gu + (int64_t)p * F2);
   }
   if (!grid_sync(P.bar, target, P.err, 102)) return;
 
@@ -479,9 +480,10 @@ __global__ void __launch_bounds__(kMdThreads, 1) moe_decode_kernel(const __grid_
   const int nbh = (NP + 1) / 2;
   {
     const float* gu = P.gu;
-    const int64_t F2 = 2 * F;
+    // gate row j is interleaved row 32 (j / 16) + j % 16, its up row 16 further
     auto fetch = [&](int p, int64_t j) {
-      return make_float2(__ldcg(gu + p * F2 + j), __ldcg(gu + p * F2 + F + j));
+      const float* gp = gu + p * F2 + 32 * (j >> 4) + (j & 15);
+      return make_float2(__ldcg(gp), __ldcg(gp + 16));
     };
     if (P.use_gelu) {
       build_rows(NP, fetch, [](float2 v) {
@@ -546,7 +548,8 @@ int moe_decode(ft_ctx* ctx, ft_moe* m, int64_t T, const void* x, int bf16, float
   // scratch: partial router scores | gu | o | barrier
   const int nparts = (int)ceil_div(m->H, 256);
   const size_t off_gu = round_up((int64_t)(T * m->E * nparts * 4), 256);
-  const size_t off_o = off_gu + round_up(NP * 2 * m->F * 4, 256);
+  const int64_t F2 = m->gate_up[0] ? m->gate_up[0]->rows : 32 * ceil_div(m->F, 16);
+  const size_t off_o = off_gu + round_up(NP * F2 * 4, 256);
   const size_t off_bar = off_o + round_up(NP * m->H * 4, 256);
   const size_t need = off_bar + 256;
   if (m->dbuf.bytes < need) {
@@ -577,6 +580,7 @@ int moe_decode(ft_ctx* ctx, ft_moe* m, int64_t T, const void* x, int bf16, float
   P.x_vec = (m->H % 8 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) ? 1 : 0;
   P.H = m->H;
   P.F = m->F;
+  P.F2 = F2;
   P.nch_h = nch_h;
   P.nch_f = nch_f;
   P.x = x;

@@ -91,6 +91,12 @@ struct TqProblem {
   int32_t* acc;             // [passes][n_tiles][NPAD][128], zero between calls
   int32_t* cnt;             // [passes][n_tiles], zero between calls
   int64_t item_begin;
+  // MoE gate/up with the activation fused (act = 1 SwiGLU, 2 GeLU-tanh, 0
+  // off): the weight interleaves 16-row m-blocks of gate (even) and up (odd),
+  // so a gate row and its up row sit 16 TMEM lanes apart in one epilogue
+  // warp; y[t * ldy + j] = act(gate_j, up_j) for j < fout.
+  int act;
+  int64_t fout;
 };
 
 struct TqBatch {
@@ -202,8 +208,8 @@ __device__ __forceinline__ void named_sync_epilogue() {
 
 // fp32 output of token t, row R from its digit-sum total S.
 template <bool kSparse>
-__device__ __forceinline__ void store_fp(const TqProblem& p, bool bf16, int64_t t, int64_t R,
-                                         double S) {
+__device__ __forceinline__ float value_fp(const TqProblem& p, bool bf16, int64_t t, int64_t R,
+                                          double S) {
   const double ts = p.tok_scale[t];
   float y = (float)(S * fabs(ts) * (double)p.row_scales[R]);
   if (ts < 0.0) {
@@ -212,7 +218,58 @@ __device__ __forceinline__ void store_fp(const TqProblem& p, bool bf16, int64_t 
                       static_cast<const char*>(p.x) + t * p.K * (bf16 ? 2 : 4), bf16, p.K, nf + 1,
                       nf[0], p.row_scales[R], p.kscale, p.kblock);
   }
-  p.y[t * p.ldy + R] = y;
+  return y;
+}
+
+template <bool kSparse>
+__device__ __forceinline__ void store_fp(const TqProblem& p, bool bf16, int64_t t, int64_t R,
+                                         double S) {
+  p.y[t * p.ldy + R] = value_fp<kSparse>(p, bf16, t, R, S);
+}
+
+// The expert activation of the reference (ternary_moe.rs:199-209): SwiGLU
+// silu(g) * u with silu(g) = g / (1 + e^-g), or GeLU-tanh of g.
+__device__ __forceinline__ float expert_act(float g, float u, int act) {
+  if (act == 2) {
+    const float ta = __fmul_rn(0.7978845608f,
+                               __fadd_rn(g, __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, g), g), g)));
+    return __fmul_rn(__fmul_rn(0.5f, g), __fadd_rn(1.0f, tanhf(ta)));
+  }
+  return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+}
+
+// Fused-activation epilogue of one 16-column group (4 digits per token: four
+// tokens).  Warp-collective: every lane of the epilogue warp calls it; lane
+// l < 16 holds gate row j = 16 * (R / 32) + l % 16, lane l + 16 its up row.
+template <int NPAD, bool kSparse>
+__device__ __forceinline__ void epilogue_act(const TqProblem& p, bool bf16, int pass, int64_t R,
+                                             int col0, const int32_t (&v)[16], bool row_ok,
+                                             int lane) {
+  float y[4];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const int lt = (col0 >> 2) + c;
+    const int64_t t = (int64_t)pass * p.tok_per_pass + lt;
+    y[c] = 0.0f;
+    if (row_ok && t < p.seq && lt < p.tok_per_pass) {
+      long long S = 0;
+#pragma unroll
+      for (int d = 0; d < 4; ++d)
+        S += (long long)(v[4 * c + d] - p.colsum[pass * NPAD + col0 + 4 * c + d]) * (1ll << (8 * d));
+      y[c] = value_fp<kSparse>(p, bf16, t, R, (double)S);
+    }
+  }
+  float u[4];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) u[c] = __shfl_down_sync(0xffffffffu, y[c], 16);
+  const int64_t j = (R >> 5) * 16 + (R & 15);
+  if ((lane & 16) || !row_ok || j >= p.fout) return;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const int lt = (col0 >> 2) + c;
+    const int64_t t = (int64_t)pass * p.tok_per_pass + lt;
+    if (t < p.seq && lt < p.tok_per_pass) p.y[t * p.ldy + j] = expert_act(y[c], u[c], p.act);
+  }
 }
 
 template <int NPAD, bool kSparse>
@@ -568,8 +625,12 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
           int32_t v[16];
 #pragma unroll
           for (int c = 0; c < 16; ++c) v[c] = (int32_t)u[c];
-          if (ok && R < p.rows && cg * 16 < ncols)
+          if (p.act) {
+            if (ok && cg * 16 < ncols)
+              epilogue_act<NPAD, kSparse>(p, b.bf16 != 0, it.pass, R, cg * 16, v, R < p.rows, lane);
+          } else if (ok && R < p.rows && cg * 16 < ncols) {
             epilogue_group<NPAD, kSparse>(p, b.digits, b.bf16 != 0, it.pass, R, cg * 16, v);
+          }
         }
       } else {
         int32_t* accp = p.acc + (((int64_t)it.pass * p.n_tiles + it.tile) * NPAD) * kTileRows;
@@ -608,7 +669,11 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
               v[c] = __ldcg(a);
               __stcg(a, 0);  // leave the scratch zeroed for the next call
             }
-            if (ok && R < p.rows) epilogue_group<NPAD, kSparse>(p, b.digits, b.bf16 != 0, it.pass, R, cg * 16, v);
+            if (p.act) {
+              if (ok) epilogue_act<NPAD, kSparse>(p, b.bf16 != 0, it.pass, R, cg * 16, v, R < p.rows, lane);
+            } else if (ok && R < p.rows) {
+              epilogue_group<NPAD, kSparse>(p, b.digits, b.bf16 != 0, it.pass, R, cg * 16, v);
+            }
           }
           if (r == 0) p.cnt[(int64_t)it.pass * p.n_tiles + it.tile] = 0;
         }
@@ -667,9 +732,10 @@ constexpr int kPrepThreads = 256, kPrepRegs = 2;
 
 template <int DT>
 __global__ void __launch_bounds__(kPrepThreads) prep_b_kernel(const __grid_constant__ PrepBatch pb) {
-  // Let the matmul that consumes this launch start streaming its weights now;
-  // then wait for the previous matmul, which may still be reading bmat.
-  tc::pdl_launch_dependents();
+  // Wait for the previous matmul, which may still be reading bmat.  The
+  // matmul that consumes this launch is released only at the end of each
+  // block: its persistent CTAs, once resident, would leave this grid's
+  // remaining blocks a fraction of the SM's registers.
   tc::pdl_wait();
   int si = 0;
   while (si + 1 < pb.nsrc && pb.block_begin[si + 1] <= (int64_t)blockIdx.x) ++si;
@@ -874,6 +940,7 @@ __global__ void __launch_bounds__(kPrepThreads) prep_b_kernel(const __grid_const
     for (int w = 0; w < 8; ++w) v += red_i[w][threadIdx.x];
     src.colsum[pass * npad + lt * D + threadIdx.x] = v;
   }
+  tc::pdl_launch_dependents();
 }
 
 #ifndef FT_MAX_NPAD
@@ -923,13 +990,15 @@ int launch_grouped_t(const TqBatch& batch, int64_t grid, cudaStream_t s) {
 int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t seq,
                       const void* const* xs, int xkind, const float* const* sxs, float* const* ys,
                       const int64_t* ldys, cudaStream_t s, const int64_t* seqs, int digits,
-                      const float* kscale, int64_t kblock) {
+                      const float* kscale, int64_t kblock, int act, int64_t fout) {
   FT_CHECK(n >= 1 && n <= kMaxProblems, FT_ERR_UNSUPPORTED, "group size %d not in [1, %d]", n,
            kMaxProblems);
   if (digits <= 0) digits = kDigitsExact;
   FT_CHECK(xkind == 2 || digits == kDigitsExact || digits == kDigitsMoE, FT_ERR_UNSUPPORTED,
            "unsupported digit count %d", digits);
   const int D = xkind == 2 ? 1 : digits;
+  FT_CHECK(!act || (xkind != 2 && digits == 4 && !kscale), FT_ERR_UNSUPPORTED,
+           "the fused activation needs 4-digit fp32/bf16 activations");
   FT_CHECK(!kscale || (xkind != 2 && kblock >= 1), FT_ERR_UNSUPPORTED,
            "column-block scales need fp32/bf16 activations and a block size >= 1");
   int64_t max_seq = 0;
@@ -1056,7 +1125,9 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
     p.kblock = kblock;
     p.sx = sxs ? sxs[i] : nullptr;
     p.y = ys[i];
-    p.ldy = ldys ? ldys[i] : w->rows;
+    p.ldy = ldys ? ldys[i] : (act ? fout : w->rows);
+    p.act = act;
+    p.fout = fout;
     p.seq = src_seq[j];
     p.tok_per_pass = tok_per_pass;
     p.passes = (int)passes;
