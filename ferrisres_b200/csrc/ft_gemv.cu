@@ -117,9 +117,11 @@ struct GvUnit {
 };
 
 struct GvSeg {  // one activation source and the problems that read it
-  const void* x;  // [seq, K]: f32, bf16 or int8 codes
+  const void* x;  // [seq, ldx]: f32, bf16 or int8 codes
   const float* kscale;  // column-block scales folded into x (blocked matmul), or null
   int64_t K, kblock;
+  int64_t ldx;    // elements per activation row (K, or the gate/up width with act)
+  int32_t act;    // x holds interleaved gate/up rows: element k = expert_act(gate_k, up_k)
   int32_t units;         // sum over its problems of row-blocks x chunks (< 2^31)
   int32_t q_cta, r_cta;  // units / n_cta, units % n_cta: CTA c starts near c*q + min(c, r)
   int32_t seq, n_chunks;
@@ -229,11 +231,29 @@ __device__ __forceinline__ int cta_boundary(const PT& P, const GvSeg& s, int c) 
 }
 
 __device__ __forceinline__ float4 load_x4(const void* x, int xkind, int64_t row, int64_t k,
-                                          int64_t K);
+                                          int64_t K, int64_t ldx);
 
-// load_x4 with the segment's column-block scales applied (x' = scale * x)
+// load_x4 with the segment's column-block scales applied (x' = scale * x), or
+// the activation of interleaved gate/up rows (S.act)
 __device__ __forceinline__ float4 load_xs4(const GvSeg& S, int xkind, int64_t row, int64_t k) {
-  float4 v = load_x4(S.x, xkind, row, k, S.K);
+  if (S.act) {
+    // k .. k+3 lie in one 16-wide group: gate row 32 (k/16) + k%16, up row 16 further
+    float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    const float* gp = static_cast<const float*>(S.x) + row * S.ldx + 32 * (k >> 4) + (k & 15);
+    float* e = reinterpret_cast<float*>(&v);
+    if (k + 4 <= S.K && (reinterpret_cast<uintptr_t>(gp) & 15) == 0) {
+      const float4 g4 = __ldg(reinterpret_cast<const float4*>(gp));
+      const float4 u4 = __ldg(reinterpret_cast<const float4*>(gp + 16));
+      v = make_float4(expert_act(g4.x, u4.x, S.act), expert_act(g4.y, u4.y, S.act),
+                      expert_act(g4.z, u4.z, S.act), expert_act(g4.w, u4.w, S.act));
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (k + i < S.K) e[i] = expert_act(__ldg(gp + i), __ldg(gp + 16 + i), S.act);
+    }
+    return v;
+  }
+  float4 v = load_x4(S.x, xkind, row, k, S.K, S.ldx);
   if (S.kscale) {
     float* e = reinterpret_cast<float*>(&v);
 #pragma unroll
@@ -244,10 +264,10 @@ __device__ __forceinline__ float4 load_xs4(const GvSeg& S, int xkind, int64_t ro
 }
 
 __device__ __forceinline__ float4 load_x4(const void* x, int xkind, int64_t row, int64_t k,
-                                          int64_t K) {
-  // elements k .. k+3 of row `row` (zero past K)
+                                          int64_t K, int64_t ldx) {
+  // elements k .. k+3 of row `row` (rows of ldx elements; zero past K)
   float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-  const int64_t i = row * K + k;
+  const int64_t i = row * ldx + k;
   if (xkind == 0) {
     const float* f = static_cast<const float*>(x);
     if (k + 3 < K && ((reinterpret_cast<uintptr_t>(f + i) & 15) == 0)) {
@@ -342,6 +362,8 @@ struct GvNf {
   int format;
   const float* kscale;        // column-block scales, or null
   int64_t kblock;
+  int64_t ldx;                // elements per activation row
+  int act;                    // interleaved gate/up activations
 };
 
 // Output of one row-block (MB m-blocks) from its exact digit sums fin:
@@ -355,9 +377,9 @@ __device__ __forceinline__ void rowblock_store(const int (&fin)[MB][NB][4], cons
   auto finish = [&](int t, int64_t R, float y) {
     if (nf.cnt[t] != 0)
       y = nonfinite_row(y, reinterpret_cast<const uint8_t*>(q.codes), nf.format, q.n_chunks, R,
-                        static_cast<const char*>(nf.x) + (int64_t)t * nf.K * (nf.bf16 ? 2 : 4),
+                        static_cast<const char*>(nf.x) + (int64_t)t * nf.ldx * (nf.bf16 ? 2 : 4),
                         nf.bf16, nf.K, nf.pos[t], nf.cnt[t], q.row_scales[R], nf.kscale,
-                        nf.kblock);
+                        nf.kblock, nf.act);
     q.y[t * q.ldy + R] = y;
   };
   if (D == 8) {
@@ -644,7 +666,7 @@ __global__ void __launch_bounds__(kThreads, GvCfg<NB>::CTAS)
       for (int q = tid + kRQ * kThreads; q < nquad; q += kThreads)
         split(load_xs4(S, P.xkind, t, 4 * (int64_t)q), q);
     } else {
-      const int8_t* xq = static_cast<const int8_t*>(S.x) + (int64_t)t * S.K;
+      const int8_t* xq = static_cast<const int8_t*>(S.x) + (int64_t)t * S.ldx;
       for (int q = tid; q < nquad; q += kThreads) {
         const int64_t k = 4 * (int64_t)q;
         uint32_t wv = 0u;
@@ -671,7 +693,8 @@ __global__ void __launch_bounds__(kThreads, GvCfg<NB>::CTAS)
     }
   }
   __syncthreads();
-  const GvNf nfv{nf_cnt, nf_pos, S.x, S.K, P.xkind == 1, SP ? 1 : 0, S.kscale, S.kblock};
+  const GvNf nfv{nf_cnt, nf_pos, S.x, S.K, P.xkind == 1, SP ? 1 : 0, S.kscale, S.kblock,
+                 S.ldx, S.act};
 
   // ---- the weight stream against the fragments, one row-block segment at a time
   int acc[MB][NB][4][4];
@@ -921,11 +944,14 @@ int launch_gemv(ft_ctx* ctx, int nprob, const GvLaunchProblem* probs, int xkind,
     const GvLaunchProblem& q = probs[i];
     int j = 0;
     while (j < nseg && !(P.g[j].x == q.x && P.g[j].K == q.K && P.g[j].seq == q.seq &&
-                         P.g[j].kscale == q.kscale && P.g[j].kblock == q.kblock))
+                         P.g[j].kscale == q.kscale && P.g[j].kblock == q.kblock &&
+                         P.g[j].act == q.act))
       ++j;
     if (j == nseg) {
       P.g[j].x = q.x;
       P.g[j].K = q.K;
+      P.g[j].act = q.act;
+      P.g[j].ldx = q.ldx > 0 ? q.ldx : q.K;
       P.g[j].kscale = q.kscale;
       P.g[j].kblock = q.kblock;
       P.g[j].seq = (int32_t)q.seq;

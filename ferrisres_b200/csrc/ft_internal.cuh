@@ -160,6 +160,17 @@ __device__ __forceinline__ bool is_nonfinite(float v) {
   return (__float_as_uint(v) & 0x7f800000u) == 0x7f800000u;
 }
 
+// The expert activation of the reference (ternary_moe.rs:199-209), act 1:
+// SwiGLU silu(g) * u with silu(g) = g / (1 + e^-g); act 2: GeLU-tanh of g.
+__device__ __forceinline__ float expert_act(float g, float u, int act) {
+  if (act == 2) {
+    const float ta = __fmul_rn(0.7978845608f,
+                               __fadd_rn(g, __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, g), g), g)));
+    return __fmul_rn(__fmul_rn(0.5f, g), __fadd_rn(1.0f, tanhf(ta)));
+  }
+  return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+}
+
 // Output of row R for a token x_row [K] (fp32, or bf16 bit patterns when
 // bf16) that holds non-finite elements.  The reference's per-row-scale
 // matmuls (TernaryMatMulOp, src/compute/kernels/ternary_matmul.rs:54-70, and
@@ -168,6 +179,9 @@ __device__ __forceinline__ bool is_nonfinite(float v) {
 // both signs, ends NaN; one sign of infinity gives +-inf; then sum * scale.
 // `pos` lists the token's non-finite positions (cnt of them; more than kNfCap:
 // the whole row is scanned).  y_finite is returned when the row meets none.
+//
+// act != 0: x_row is a row of interleaved gate/up outputs and element k is
+// expert_act(gate_k, up_k) (the MoE's fused activation operand).
 //
 // Column-block scales (ternary_matmul_blocked, src/model/ternary.rs:541-579:
 // kscale != null, one scale per kblock columns): the kernels fold the scale
@@ -180,14 +194,20 @@ static __device__ __noinline__ float nonfinite_row(float y_finite, const uint8_t
                                                int64_t n_chunks, int64_t R, const void* x_row,
                                                bool bf16, int64_t K, const int* pos, int cnt,
                                                float scale, const float* kscale,
-                                               int64_t kblock) {
+                                               int64_t kblock, int act = 0) {
   bool nan = false, pinf = false, ninf = false;
   const bool all = cnt > kNfCap;
   const int64_t n = all ? K : cnt;
   for (int64_t i = 0; i < n; ++i) {
     const int64_t k = all ? i : pos[i];
-    float v = bf16 ? __uint_as_float((uint32_t) static_cast<const uint16_t*>(x_row)[k] << 16)
-                   : static_cast<const float*>(x_row)[k];
+    float v;
+    if (act) {  // x_row holds interleaved gate/up values (fp32)
+      const float* gp = static_cast<const float*>(x_row) + 32 * (k >> 4) + (k & 15);
+      v = expert_act(gp[0], gp[16], act);
+    } else {
+      v = bf16 ? __uint_as_float((uint32_t) static_cast<const uint16_t*>(x_row)[k] << 16)
+               : static_cast<const float*>(x_row)[k];
+    }
     if (kscale) v = __fmul_rn(v, kscale[k / kblock]);
     if (!is_nonfinite(v)) continue;
     const int w = weight_at(codes, format, n_chunks, R, k);
@@ -281,14 +301,15 @@ int launch_tc_matmul(ft_ctx* ctx, const ft_weight* w, int64_t seq, const void* x
 // 0 = kDigitsExact); ignored for int8 codes.
 // kscale/kblock (fp32/bf16 only): one scale per kblock columns, folded into
 // the activations (the blocked matmul); applies to every problem of the group.
-// act (MoE gate/up weights with interleaved 16-row gate/up m-blocks, 4
-// digits): 1 = SwiGLU, 2 = GeLU-tanh; output y[t * ldy + j] = act(gate_j,
-// up_j) for j < fout instead of the weight's rows.
+// act (fp32 only): the activations are the outputs of a gate/up weight with
+// interleaved 16-row m-blocks, rows of ldx floats; the operand's element k is
+// then expert_act(x[32 (k/16) + k%16], x[that + 16], act) (1 SwiGLU, 2 GeLU),
+// so the MoE's activation needs no pass of its own.
 int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t seq,
                       const void* const* xs, int xkind, const float* const* sxs, float* const* ys,
                       const int64_t* ldys, cudaStream_t s, const int64_t* seqs = nullptr,
                       int digits = 0, const float* kscale = nullptr, int64_t kblock = 1,
-                      int act = 0, int64_t fout = 0);
+                      int act = 0, int64_t ldx = 0);
 // Decode-shape kernel (ft_gemv.cu): dense problems whose activations fit 16
 // operand columns; the kernel builds its activation operand itself.
 constexpr int kGemvMaxSmem = 200 * 1024;
@@ -303,6 +324,8 @@ struct GvLaunchProblem {
   int64_t ldy;
   const float* kscale = nullptr;  // fp32 mode: column-block scales (blocked matmul), or null
   int64_t kblock = 1;             // columns per block scale
+  int act = 0;                    // x is interleaved gate/up rows (see launch_tc_grouped)
+  int64_t ldx = 0;                // elements per activation row (0: K)
 };
 // Digits per fp32/bf16 token on the decode kernel for a requested count
 // (8 when more than 4 are asked for, else 4); 1 for int8 codes.

@@ -416,7 +416,7 @@ struct MoeBufs {
   int32_t* slot_of;
   int32_t* token_of;
   void* xg;
-  float* h;
+  float* gu;  // gate/up outputs [n, interleaved rows]
   float* o;
 };
 
@@ -467,7 +467,7 @@ size_t moe_layout(const ft_moe* m, int64_t T, int x_bytes, char* base, MoeBufs* 
   b->slot_of = reinterpret_cast<int32_t*>(take(n * 4));
   b->token_of = reinterpret_cast<int32_t*>(take(n * 4));
   b->xg = take((size_t)n * m->H * x_bytes);
-  b->h = reinterpret_cast<float*>(take((size_t)n * m->F * 4));
+  b->gu = reinterpret_cast<float*>(take((size_t)n * gu_rows(m->F) * 4));
   b->o = reinterpret_cast<float*>(take((size_t)n * m->H * 4));
   return off;
 }
@@ -493,13 +493,14 @@ int moe_route(ft_ctx* ctx, ft_moe* m, int64_t T, const void* x, int bf16, int32_
 // Expert FFN over rows grouped in segments: segment i has seg_rows[i] rows for
 // expert seg_expert[i], stored consecutively in x_rows / y_rows.
 int moe_expert_segments(ft_ctx* ctx, ft_moe* m, int nseg, const int32_t* seg_expert,
-                        const int64_t* seg_rows, const void* x_rows, int bf16, float* h,
+                        const int64_t* seg_rows, const void* x_rows, int bf16, float* gu,
                         float* y_rows, cudaStream_t s) {
   FT_CHECK(nseg >= 0 && nseg <= 64, FT_ERR_UNSUPPORTED, "at most 64 segments per call");
   int64_t total = 0;
   std::vector<const ft_weight*> wgu(nseg), wd(nseg);
-  std::vector<const void*> xs(nseg), hs(nseg);
-  std::vector<float*> hw(nseg), ys(nseg);
+  std::vector<const void*> xs(nseg), gin(nseg);
+  std::vector<float*> gout(nseg), ys(nseg);
+  const int64_t F2 = gu_rows(m->F);
   const int xb = bf16 ? 2 : 4;
   for (int i = 0; i < nseg; ++i) {
     FT_CHECK(seg_expert[i] >= 0 && seg_expert[i] < m->E, FT_ERR_SHAPE, "segment %d: bad expert %d",
@@ -510,21 +511,21 @@ int moe_expert_segments(ft_ctx* ctx, ft_moe* m, int nseg, const int32_t* seg_exp
     wgu[i] = m->gate_up[seg_expert[i]];
     wd[i] = m->down[seg_expert[i]];
     xs[i] = static_cast<const char*>(x_rows) + total * m->H * xb;
-    hw[i] = h + total * m->F;
-    hs[i] = hw[i];
+    gout[i] = gu + total * F2;
+    gin[i] = gout[i];
     ys[i] = y_rows + total * m->H;
     total += seg_rows[i];
   }
   if (total == 0) return FT_OK;
   // Expert GEMMs take kDigitsMoE fixed-point digits per token: the layer's
-  // tolerance is 1e-4 of each output row's rms (ft_internal.cuh).  The gate/up
-  // GEMM's epilogue applies the activation and writes h [rows, F] itself.
-  int st = launch_tc_grouped(ctx, nseg, wgu.data(), 0, xs.data(), bf16 ? 1 : 0, nullptr, hw.data(),
-                             nullptr, s, seg_rows, kDigitsMoE, nullptr, 1, m->use_gelu ? 2 : 1,
-                             m->F);
+  // tolerance is 1e-4 of each output row's rms (ft_internal.cuh).  The down
+  // GEMM builds its operand from the interleaved gate/up outputs, applying the
+  // activation (SwiGLU, or GeLU) as it reads them: no pass of its own.
+  int st = launch_tc_grouped(ctx, nseg, wgu.data(), 0, xs.data(), bf16 ? 1 : 0, nullptr,
+                             gout.data(), nullptr, s, seg_rows, kDigitsMoE);
   if (st != FT_OK) return st;
-  return launch_tc_grouped(ctx, nseg, wd.data(), 0, hs.data(), 0, nullptr, ys.data(), nullptr, s,
-                           seg_rows, kDigitsMoE);
+  return launch_tc_grouped(ctx, nseg, wd.data(), 0, gin.data(), 0, nullptr, ys.data(), nullptr, s,
+                           seg_rows, kDigitsMoE, nullptr, 1, m->use_gelu ? 2 : 1, F2);
 }
 
 // Router planes for moe_router_mma_kernel: router = p0 + p1 + p2 with each
@@ -824,12 +825,12 @@ int ft_moe_expert_ffn(ft_ctx* ctx, ft_moe* m, int nseg, const int32_t* seg_exper
   int64_t total = 0;
   for (int i = 0; i < nseg; ++i) total += seg_rows_host[i] > 0 ? seg_rows_host[i] : 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // activation scratch: F floats per row
-  int st = moe_reserve(m, (size_t)total * m->F * 4 + 512, s);
+  // gate/up scratch: the interleaved rows of F per token
+  int st = moe_reserve(m, (size_t)total * gu_rows(m->F) * 4 + 512, s);
   if (st != FT_OK) return st;
-  float* h = static_cast<float*>(m->buf.ptr);
+  float* gu = static_cast<float*>(m->buf.ptr);
   return moe_expert_segments(ctx, m, nseg, seg_expert_host, seg_rows_host, x_rows_dev, x_is_bf16,
-                             h, y_rows_dev, s);
+                             gu, y_rows_dev, s);
 }
 
 int ft_moe_combine(ft_ctx* ctx, ft_moe* m, int64_t T, const float* o_rows_dev,
@@ -879,7 +880,7 @@ int ft_moe_forward(ft_ctx* ctx, ft_moe* m, int64_t T, const void* x_dev, int x_i
       ex[e] = (int32_t)e;
       rows[e] = m->counts_host[e];
     }
-    st = moe_expert_segments(ctx, m, (int)m->E, ex.data(), rows.data(), b.xg, x_is_bf16, b.h,
+    st = moe_expert_segments(ctx, m, (int)m->E, ex.data(), rows.data(), b.xg, x_is_bf16, b.gu,
                              b.o, s);
   }
   if (st == FT_OK) st = ft_moe_combine(ctx, m, T, b.o, b.slot_of, b.topk_w, y_dev, s);

@@ -91,12 +91,10 @@ struct TqProblem {
   int32_t* acc;             // [passes][n_tiles][NPAD][128], zero between calls
   int32_t* cnt;             // [passes][n_tiles], zero between calls
   int64_t item_begin;
-  // MoE gate/up with the activation fused (act = 1 SwiGLU, 2 GeLU-tanh, 0
-  // off): the weight interleaves 16-row m-blocks of gate (even) and up (odd),
-  // so a gate row and its up row sit 16 TMEM lanes apart in one epilogue
-  // warp; y[t * ldy + j] = act(gate_j, up_j) for j < fout.
+  // activation rows: x + t * ldx (ldx = K, or the interleaved gate/up width
+  // when act != 0: element k = act(gate_k, up_k), see act_operand)
+  int64_t ldx;
   int act;
-  int64_t fout;
 };
 
 struct TqBatch {
@@ -215,8 +213,8 @@ __device__ __forceinline__ float value_fp(const TqProblem& p, bool bf16, int64_t
   if (ts < 0.0) {
     const int32_t* nf = p.nf + t * (kNfCap + 1);
     y = nonfinite_row(y, p.codes, kSparse ? 1 : 0, p.n_chunks, R,
-                      static_cast<const char*>(p.x) + t * p.K * (bf16 ? 2 : 4), bf16, p.K, nf + 1,
-                      nf[0], p.row_scales[R], p.kscale, p.kblock);
+                      static_cast<const char*>(p.x) + t * p.ldx * (bf16 ? 2 : 4), bf16, p.K, nf + 1,
+                      nf[0], p.row_scales[R], p.kscale, p.kblock, p.act);
   }
   return y;
 }
@@ -225,51 +223,6 @@ template <bool kSparse>
 __device__ __forceinline__ void store_fp(const TqProblem& p, bool bf16, int64_t t, int64_t R,
                                          double S) {
   p.y[t * p.ldy + R] = value_fp<kSparse>(p, bf16, t, R, S);
-}
-
-// The expert activation of the reference (ternary_moe.rs:199-209): SwiGLU
-// silu(g) * u with silu(g) = g / (1 + e^-g), or GeLU-tanh of g.
-__device__ __forceinline__ float expert_act(float g, float u, int act) {
-  if (act == 2) {
-    const float ta = __fmul_rn(0.7978845608f,
-                               __fadd_rn(g, __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, g), g), g)));
-    return __fmul_rn(__fmul_rn(0.5f, g), __fadd_rn(1.0f, tanhf(ta)));
-  }
-  return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
-}
-
-// Fused-activation epilogue of one 16-column group (4 digits per token: four
-// tokens).  Warp-collective: every lane of the epilogue warp calls it; lane
-// l < 16 holds gate row j = 16 * (R / 32) + l % 16, lane l + 16 its up row.
-template <int NPAD, bool kSparse>
-__device__ __forceinline__ void epilogue_act(const TqProblem& p, bool bf16, int pass, int64_t R,
-                                             int col0, const int32_t (&v)[16], bool row_ok,
-                                             int lane) {
-  float y[4];
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    const int lt = (col0 >> 2) + c;
-    const int64_t t = (int64_t)pass * p.tok_per_pass + lt;
-    y[c] = 0.0f;
-    if (row_ok && t < p.seq && lt < p.tok_per_pass) {
-      long long S = 0;
-#pragma unroll
-      for (int d = 0; d < 4; ++d)
-        S += (long long)(v[4 * c + d] - p.colsum[pass * NPAD + col0 + 4 * c + d]) * (1ll << (8 * d));
-      y[c] = value_fp<kSparse>(p, bf16, t, R, (double)S);
-    }
-  }
-  float u[4];
-#pragma unroll
-  for (int c = 0; c < 4; ++c) u[c] = __shfl_down_sync(0xffffffffu, y[c], 16);
-  const int64_t j = (R >> 5) * 16 + (R & 15);
-  if ((lane & 16) || !row_ok || j >= p.fout) return;
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    const int lt = (col0 >> 2) + c;
-    const int64_t t = (int64_t)pass * p.tok_per_pass + lt;
-    if (t < p.seq && lt < p.tok_per_pass) p.y[t * p.ldy + j] = expert_act(y[c], u[c], p.act);
-  }
 }
 
 template <int NPAD, bool kSparse>
@@ -625,12 +578,8 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
           int32_t v[16];
 #pragma unroll
           for (int c = 0; c < 16; ++c) v[c] = (int32_t)u[c];
-          if (p.act) {
-            if (ok && cg * 16 < ncols)
-              epilogue_act<NPAD, kSparse>(p, b.bf16 != 0, it.pass, R, cg * 16, v, R < p.rows, lane);
-          } else if (ok && R < p.rows && cg * 16 < ncols) {
+          if (ok && R < p.rows && cg * 16 < ncols)
             epilogue_group<NPAD, kSparse>(p, b.digits, b.bf16 != 0, it.pass, R, cg * 16, v);
-          }
         }
       } else {
         int32_t* accp = p.acc + (((int64_t)it.pass * p.n_tiles + it.tile) * NPAD) * kTileRows;
@@ -669,11 +618,7 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
               v[c] = __ldcg(a);
               __stcg(a, 0);  // leave the scratch zeroed for the next call
             }
-            if (p.act) {
-              if (ok) epilogue_act<NPAD, kSparse>(p, b.bf16 != 0, it.pass, R, cg * 16, v, R < p.rows, lane);
-            } else if (ok && R < p.rows) {
-              epilogue_group<NPAD, kSparse>(p, b.digits, b.bf16 != 0, it.pass, R, cg * 16, v);
-            }
+            if (ok && R < p.rows) epilogue_group<NPAD, kSparse>(p, b.digits, b.bf16 != 0, it.pass, R, cg * 16, v);
           }
           if (r == 0) p.cnt[(int64_t)it.pass * p.n_tiles + it.tile] = 0;
         }
@@ -690,12 +635,14 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
 }
 
 // ------------------------------------------------------------- B prep -----
-// One block per (source, pass, token slot): writes the token's digit columns
+// One warp per (source, pass, token slot): writes the token's digit columns
 // of the K-major interleaved B operand for every chunk, their column sums,
 // the token scale and its non-finite positions.  Slots past `seq` write zero
 // columns.
 struct PrepSource {
   const void* x;
+  int64_t ldx;  // elements per activation row (K, or the gate/up width with act)
+  int act;      // x holds interleaved gate/up rows: the operand is act(gate, up)
   const float* kscale;  // column-block scales folded into x, or null
   int64_t kblock;
   int8_t* bmat;
@@ -710,7 +657,7 @@ struct PrepBatch {
   int nsrc;
   int xkind;  // 0 f32, 1 bf16, 2 int8 codes
   int D, npad, tok_per_pass;
-  int64_t block_begin[kMaxSources + 1];
+  int64_t block_begin[kMaxSources + 1];  // first token slot of each source
   PrepSource s[kMaxSources];
 };
 
@@ -723,12 +670,14 @@ __device__ __forceinline__ int64_t b_offset(int64_t pass, int64_t chunk, int n, 
 // DT: digits per token (1: int8 codes, 4 or 8), a template parameter so that
 // the digit arrays stay in registers.
 //
-// One pass over the token: thread i holds elements 8i .. 8i+7 of every 2048-K
-// stretch (one 16-byte load of bf16 / int8, two of fp32, when aligned), kept in
-// registers (kPrepRegs stretches; longer rows are reloaded) for the absmax,
-// the non-finite count, the digit split and the column sums.  Each thread
-// writes 8 bytes of each digit column's 16-byte operand row.
-constexpr int kPrepThreads = 256, kPrepRegs = 2;
+// One warp per (source, pass, token slot), kPrepWarps slots per block, so
+// every reduction is a warp reduction and no block barrier is taken.  Lane l
+// holds elements 256 i + 8 l .. +7 of the token (one 16-byte load of bf16 /
+// int8, two of fp32, when aligned): kPrepIt such stretches (2048 K) stay in
+// registers between the absmax, the non-finite count, the digit split and
+// the column sums; longer rows are read again.  Each lane writes 8 bytes of
+// each digit column's 16-byte operand row.
+constexpr int kPrepThreads = 256, kPrepWarps = kPrepThreads / 32, kPrepIt = 8;
 
 template <int DT>
 __global__ void __launch_bounds__(kPrepThreads) prep_b_kernel(const __grid_constant__ PrepBatch pb) {
@@ -737,208 +686,228 @@ __global__ void __launch_bounds__(kPrepThreads) prep_b_kernel(const __grid_const
   // block: its persistent CTAs, once resident, would leave this grid's
   // remaining blocks a fraction of the SM's registers.
   tc::pdl_wait();
-  int si = 0;
-  while (si + 1 < pb.nsrc && pb.block_begin[si + 1] <= (int64_t)blockIdx.x) ++si;
-  const PrepSource& src = pb.s[si];
-  const int64_t local = blockIdx.x - pb.block_begin[si];
-  const int64_t pass = local / pb.tok_per_pass;
-  const int lt = (int)(local % pb.tok_per_pass);
-  const int64_t t = pass * pb.tok_per_pass + lt;
-  const int64_t K = src.K, kpad = src.n_chunks * 128;
-  constexpr int D = DT;
-  const int npad = pb.npad, xkind = pb.xkind;
-  const float* kscale = src.kscale;
-  const int64_t kblock = src.kblock;
-  const void* xsrc = src.x;
-  __shared__ float red_f[8];
-  __shared__ int red_n[8];
-  __shared__ int red_i[8][8];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const bool live = t < src.seq;
-  constexpr int kStretch = 8 * kPrepThreads;  // 2048 K per stretch
-  const int64_t nstr = (kpad + kStretch - 1) / kStretch;
+  const int64_t slot = (int64_t)blockIdx.x * kPrepWarps + warp;
+  if (slot < pb.block_begin[pb.nsrc]) {
+    // the source holding this slot (binary search over the slot offsets)
+    int lo = 0, hi = pb.nsrc - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (pb.block_begin[mid] <= slot) lo = mid;
+      else hi = mid - 1;
+    }
+    const PrepSource& src = pb.s[lo];
+    const int64_t local = slot - pb.block_begin[lo];
+    const int64_t pass = local / pb.tok_per_pass;
+    const int lt = (int)(local % pb.tok_per_pass);
+    const int64_t t = pass * pb.tok_per_pass + lt;
+    const int64_t K = src.K, kpad = src.n_chunks * 128;
+    constexpr int D = DT;
+    const int npad = pb.npad, xkind = pb.xkind;
+    const float* kscale = src.kscale;
+    const int64_t kblock = src.kblock;
+    const void* xsrc = src.x;
+    const bool live = t < src.seq;
+    const int64_t nst = (kpad + 255) / 256;  // stretches of 256 K
 
-  // the 8 elements at k0 .. k0+7 of this token (zero past K), as floats
-  // (int8 codes: their integer values)
-  auto load8 = [&](int64_t k0, float (&v)[8]) {
+    // the 8 elements at k0 .. k0+7 of this token (zero past K), as floats
+    // (int8 codes: their integer values)
+    auto load8 = [&](int64_t k0, float (&v)[8]) {
 #pragma unroll
-    for (int e = 0; e < 8; ++e) v[e] = 0.0f;
-    if (!live || k0 >= K) return;
-    const int64_t i0 = t * K + k0;
-    if (xkind == 2) {
-      const int8_t* q = static_cast<const int8_t*>(xsrc) + i0;
-      if (k0 + 8 <= K && (reinterpret_cast<uintptr_t>(q) & 7) == 0) {
-        const uint2 u = __ldg(reinterpret_cast<const uint2*>(q));
-        const uint32_t w2[2] = {u.x, u.y};
+      for (int e = 0; e < 8; ++e) v[e] = 0.0f;
+      if (!live || k0 >= K) return;
+      if (src.act) {
+        // k0 .. k0+7 lie in one 16-wide group: gate row 32 (k0/16) + k0%16,
+        // its up row 16 further
+        const float* gp = static_cast<const float*>(xsrc) + t * src.ldx + 32 * (k0 >> 4) + (k0 & 15);
+        if (k0 + 8 <= K && (reinterpret_cast<uintptr_t>(gp) & 15) == 0) {
+          const float4 g0 = __ldg(reinterpret_cast<const float4*>(gp));
+          const float4 g1 = __ldg(reinterpret_cast<const float4*>(gp) + 1);
+          const float4 u0 = __ldg(reinterpret_cast<const float4*>(gp + 16));
+          const float4 u1 = __ldg(reinterpret_cast<const float4*>(gp + 16) + 1);
+          const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+          const float u[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
 #pragma unroll
-        for (int e = 0; e < 8; ++e) v[e] = (float)(int8_t)(w2[e >> 2] >> (8 * (e & 3)));
-      } else {
-#pragma unroll
-        for (int e = 0; e < 8; ++e)
-          if (k0 + e < K) v[e] = (float)q[e];
-      }
-      return;
-    }
-    if (xkind == 1) {
-      const uint16_t* h = static_cast<const uint16_t*>(xsrc) + i0;
-      if (k0 + 8 <= K && (reinterpret_cast<uintptr_t>(h) & 15) == 0) {
-        const uint4 u = __ldg(reinterpret_cast<const uint4*>(h));
-        const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          v[2 * e] = __uint_as_float(w4[e] << 16);
-          v[2 * e + 1] = __uint_as_float(w4[e] & 0xffff0000u);
-        }
-      } else {
-#pragma unroll
-        for (int e = 0; e < 8; ++e)
-          if (k0 + e < K) v[e] = __uint_as_float((uint32_t)h[e] << 16);
-      }
-    } else {
-      const float* f = static_cast<const float*>(xsrc) + i0;
-      if (k0 + 8 <= K && (reinterpret_cast<uintptr_t>(f) & 15) == 0) {
-        const float4 a = __ldg(reinterpret_cast<const float4*>(f));
-        const float4 b = __ldg(reinterpret_cast<const float4*>(f) + 1);
-        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-      } else {
-#pragma unroll
-        for (int e = 0; e < 8; ++e)
-          if (k0 + e < K) v[e] = f[e];
-      }
-    }
-    if (kscale) {
-#pragma unroll
-      for (int e = 0; e < 8; ++e)
-        if (k0 + e < K) v[e] = __fmul_rn(v[e], kscale[(k0 + e) / kblock]);
-    }
-  };
-
-  float xr[kPrepRegs][8];
-#pragma unroll
-  for (int r = 0; r < kPrepRegs; ++r)
-    if (r < nstr) load8(r * (int64_t)kStretch + 8 * threadIdx.x, xr[r]);
-  float f1 = 1.0f, f2 = 1.0f;
-  if (D != 1) {
-    // largest finite |x| and the non-finite count
-    float amax = 0.0f;
-    int nnf = 0;
-    auto scan = [&](const float (&v)[8]) {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const bool nf = is_nonfinite(v[e]);
-        nnf += nf ? 1 : 0;
-        amax = fmaxf(amax, nf ? 0.0f : fabsf(v[e]));
-      }
-    };
-#pragma unroll
-    for (int r = 0; r < kPrepRegs; ++r)
-      if (r < nstr) scan(xr[r]);
-    for (int64_t r = kPrepRegs; r < nstr; ++r) {
-      float v[8];
-      load8(r * kStretch + 8 * threadIdx.x, v);
-      scan(v);
-    }
-    int incl = nnf;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int v = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += v;
-    }
-    amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(amax)));
-    if (lane == 0) red_f[warp] = amax;
-    if (lane == 31) red_n[warp] = incl;
-    __syncthreads();
-    amax = 0.0f;
-    int before = incl - nnf, total = 0;
-    for (int w = 0; w < 8; ++w) {
-      amax = fmaxf(amax, red_f[w]);
-      if (w < warp) before += red_n[w];
-      total += red_n[w];
-    }
-    const int sh = amax > 0.0f ? digit_shift(amax, D) : 0;
-    const int s1 = sh > 127 ? 127 : (sh < -126 ? -126 : sh);
-    f1 = __int_as_float((s1 + 127) << 23);
-    f2 = __int_as_float((sh - s1 + 127) << 23);
-    if (live) {
-      int32_t* nf = src.nf + t * (kNfCap + 1);
-      if (threadIdx.x == 0) {
-        // 2^-sh (1 for an all-zero token), negative when non-finite elements exist
-        const double sc = amax > 0.0f ? __longlong_as_double((long long)(1023 - sh) << 52) : 1.0;
-        src.tok_scale[t] = total ? -sc : sc;
-        nf[0] = total;
-      }
-      if (nnf != 0 && total <= kNfCap) {
-        // this thread's positions, in its element order
-        int slot = before;
-        for (int64_t r = 0; r < nstr; ++r) {
-          float v[8];
-          load8(r * kStretch + 8 * threadIdx.x, v);
+          for (int e = 0; e < 8; ++e) v[e] = expert_act(g[e], u[e], src.act);
+        } else {
 #pragma unroll
           for (int e = 0; e < 8; ++e)
-            if (is_nonfinite(v[e])) nf[1 + slot++] = (int32_t)(r * kStretch + 8 * threadIdx.x + e);
+            if (k0 + e < K) v[e] = expert_act(__ldg(gp + e), __ldg(gp + 16 + e), src.act);
         }
+        return;
       }
-    }
-  }
-  // digits of each element; one 8-byte word pair per digit column
-  int csum[D];
+      const int64_t i0 = t * src.ldx + k0;
+      if (xkind == 2) {
+        const int8_t* q = static_cast<const int8_t*>(xsrc) + i0;
+        if (k0 + 8 <= K && (reinterpret_cast<uintptr_t>(q) & 7) == 0) {
+          const uint2 u = __ldg(reinterpret_cast<const uint2*>(q));
+          const uint32_t w2[2] = {u.x, u.y};
 #pragma unroll
-  for (int d = 0; d < D; ++d) csum[d] = 0;
-  auto emit = [&](int64_t k0, const float (&v)[8]) {
-    if (k0 >= kpad) return;
-    uint32_t w[D][2];
+          for (int e = 0; e < 8; ++e) v[e] = (float)(int8_t)(w2[e >> 2] >> (8 * (e & 3)));
+        } else {
 #pragma unroll
-    for (int d = 0; d < D; ++d) w[d][0] = w[d][1] = 0u;
+          for (int e = 0; e < 8; ++e)
+            if (k0 + e < K) v[e] = (float)q[e];
+        }
+        return;
+      }
+      if (xkind == 1) {
+        const uint16_t* h = static_cast<const uint16_t*>(xsrc) + i0;
+        if (k0 + 8 <= K && (reinterpret_cast<uintptr_t>(h) & 15) == 0) {
+          const uint4 u = __ldg(reinterpret_cast<const uint4*>(h));
+          const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      if (D == 1) {
-        const int q = (int)v[e];
-        w[0][e >> 2] |= (uint32_t)(q & 0xFF) << (8 * (e & 3));
-        csum[0] += q;
+          for (int e = 0; e < 4; ++e) {
+            v[2 * e] = __uint_as_float(w4[e] << 16);
+            v[2 * e + 1] = __uint_as_float(w4[e] & 0xffff0000u);
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            if (k0 + e < K) v[e] = __uint_as_float((uint32_t)h[e] << 16);
+        }
       } else {
-        const float xs = is_nonfinite(v[e]) ? 0.0f : __fmul_rn(__fmul_rn(v[e], f1), f2);
-        // X = round(x * 2^sh), |X| < 2^(8D-2); balanced base-256 digits (64-bit
-        // arithmetic only for D = 8)
-        using XT = typename std::conditional<(D > 4), long long, int>::type;
-        XT X = D > 4 ? (XT)__float2ll_rn(xs) : (XT)__float2int_rn(xs);
+        const float* f = static_cast<const float*>(xsrc) + i0;
+        if (k0 + 8 <= K && (reinterpret_cast<uintptr_t>(f) & 15) == 0) {
+          const float4 a = __ldg(reinterpret_cast<const float4*>(f));
+          const float4 b = __ldg(reinterpret_cast<const float4*>(f) + 1);
+          v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+          v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+        } else {
 #pragma unroll
-        for (int d = 0; d < D - 1; ++d) {
-          const int lo = ((int)(X & 0xFF) ^ 0x80) - 0x80;  // signed low digit
-          w[d][e >> 2] |= (uint32_t)(lo & 0xFF) << (8 * (e & 3));
-          csum[d] += lo;
-          X = (X - lo) >> 8;
+          for (int e = 0; e < 8; ++e)
+            if (k0 + e < K) v[e] = f[e];
         }
-        // the top digit, |X| <= 64 here
-        w[D - 1][e >> 2] |= (uint32_t)((int)X & 0xFF) << (8 * (e & 3));
-        csum[D - 1] += (int)X;
+      }
+      if (kscale) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (k0 + e < K) v[e] = __fmul_rn(v[e], kscale[(k0 + e) / kblock]);
+      }
+    };
+
+    float xr[kPrepIt][8];
+    float f1 = 1.0f, f2 = 1.0f;
+    if (D != 1) {
+#pragma unroll
+      for (int i = 0; i < kPrepIt; ++i)
+        if (i < nst) load8(256 * (int64_t)i + 8 * lane, xr[i]);
+      // largest finite |x| and the non-finite count
+      float amax = 0.0f;
+      int nnf = 0;
+      auto scan = [&](const float (&v)[8]) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const bool nf = is_nonfinite(v[e]);
+          nnf += nf ? 1 : 0;
+          amax = fmaxf(amax, nf ? 0.0f : fabsf(v[e]));
+        }
+      };
+#pragma unroll
+      for (int i = 0; i < kPrepIt; ++i)
+        if (i < nst) scan(xr[i]);
+      for (int64_t i = kPrepIt; i < nst; ++i) {
+        float v[8];
+        load8(256 * i + 8 * lane, v);
+        scan(v);
+      }
+      amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(amax)));
+      const int total = __reduce_add_sync(0xffffffffu, (unsigned)nnf);
+      const int sh = amax > 0.0f ? digit_shift(amax, D) : 0;
+      const int s1 = sh > 127 ? 127 : (sh < -126 ? -126 : sh);
+      f1 = __int_as_float((s1 + 127) << 23);
+      f2 = __int_as_float((sh - s1 + 127) << 23);
+      if (live) {
+        int32_t* nf = src.nf + t * (kNfCap + 1);
+        if (lane == 0) {
+          // 2^-sh (1 for an all-zero token), negative when non-finite elements exist
+          const double sc = amax > 0.0f ? __longlong_as_double((long long)(1023 - sh) << 52) : 1.0;
+          src.tok_scale[t] = total ? -sc : sc;
+          nf[0] = total;
+        }
+        if (total != 0 && total <= kNfCap) {
+          // this lane's positions after those of the lanes below it
+          int incl = nnf;
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
+          }
+          int slot_nf = incl - nnf;
+          if (nnf != 0) {
+            for (int64_t i = 0; i < nst; ++i) {
+              float v[8];
+              load8(256 * i + 8 * lane, v);
+#pragma unroll
+              for (int e = 0; e < 8; ++e)
+                if (is_nonfinite(v[e])) nf[1 + slot_nf++] = (int32_t)(256 * i + 8 * lane + e);
+            }
+          }
+        }
       }
     }
-    const int64_t chunk = k0 >> 7;
-    const int kin = (int)(k0 & 127);
+    // digits of each element; one 8-byte word pair per digit column
+    int csum[D];
 #pragma unroll
-    for (int d = 0; d < D; ++d)
-      *reinterpret_cast<uint2*>(src.bmat + b_offset(pass, chunk, lt * D + d, kin & ~15, npad, src.n_chunks) +
-                                (kin & 8)) = make_uint2(w[d][0], w[d][1]);
-  };
+    for (int d = 0; d < D; ++d) csum[d] = 0;
+    auto emit = [&](int64_t k0, const float (&v)[8]) {
+      if (k0 >= kpad) return;
+      uint32_t w[D][2];
 #pragma unroll
-  for (int r = 0; r < kPrepRegs; ++r)
-    if (r < nstr) emit(r * (int64_t)kStretch + 8 * threadIdx.x, xr[r]);
-  for (int64_t r = kPrepRegs; r < nstr; ++r) {
-    float v[8];
-    load8(r * kStretch + 8 * threadIdx.x, v);
-    emit(r * kStretch + 8 * threadIdx.x, v);
-  }
+      for (int d = 0; d < D; ++d) w[d][0] = w[d][1] = 0u;
 #pragma unroll
-  for (int d = 0; d < D; ++d) {
-    const int v = __reduce_add_sync(0xffffffffu, csum[d]);
-    if (lane == 0) red_i[warp][d] = v;
-  }
-  __syncthreads();
-  if (threadIdx.x < D) {
-    int v = 0;
-    for (int w = 0; w < 8; ++w) v += red_i[w][threadIdx.x];
-    src.colsum[pass * npad + lt * D + threadIdx.x] = v;
+      for (int e = 0; e < 8; ++e) {
+        if (D == 1) {
+          const int q = (int)v[e];
+          w[0][e >> 2] |= (uint32_t)(q & 0xFF) << (8 * (e & 3));
+          csum[0] += q;
+        } else {
+          const float xs = is_nonfinite(v[e]) ? 0.0f : __fmul_rn(__fmul_rn(v[e], f1), f2);
+          // X = round(x * 2^sh), |X| < 2^(8D-2); balanced base-256 digits (64-bit
+          // arithmetic only for D = 8)
+          using XT = typename std::conditional<(D > 4), long long, int>::type;
+          XT X = D > 4 ? (XT)__float2ll_rn(xs) : (XT)__float2int_rn(xs);
+#pragma unroll
+          for (int d = 0; d < D - 1; ++d) {
+            const int lo = ((int)(X & 0xFF) ^ 0x80) - 0x80;  // signed low digit
+            w[d][e >> 2] |= (uint32_t)(lo & 0xFF) << (8 * (e & 3));
+            csum[d] += lo;
+            X = (X - lo) >> 8;
+          }
+          // the top digit, |X| <= 64 here
+          w[D - 1][e >> 2] |= (uint32_t)((int)X & 0xFF) << (8 * (e & 3));
+          csum[D - 1] += (int)X;
+        }
+      }
+      const int64_t chunk = k0 >> 7;
+      const int kin = (int)(k0 & 127);
+#pragma unroll
+      for (int d = 0; d < D; ++d)
+        *reinterpret_cast<uint2*>(src.bmat + b_offset(pass, chunk, lt * D + d, kin & ~15, npad,
+                                                      src.n_chunks) +
+                                  (kin & 8)) = make_uint2(w[d][0], w[d][1]);
+    };
+    if (D != 1) {
+#pragma unroll
+      for (int i = 0; i < kPrepIt; ++i)
+        if (i < nst) emit(256 * (int64_t)i + 8 * lane, xr[i]);
+      for (int64_t i = kPrepIt; i < nst; ++i) {
+        float v[8];
+        load8(256 * i + 8 * lane, v);
+        emit(256 * i + 8 * lane, v);
+      }
+    } else {
+      for (int64_t i = 0; i < nst; ++i) {
+        float v[8];
+        load8(256 * i + 8 * lane, v);
+        emit(256 * i + 8 * lane, v);
+      }
+    }
+#pragma unroll
+    for (int d = 0; d < D; ++d) {
+      const int v = __reduce_add_sync(0xffffffffu, (unsigned)csum[d]);
+      if (lane == 0) src.colsum[pass * npad + lt * D + d] = v;
+    }
   }
   tc::pdl_launch_dependents();
 }
@@ -990,15 +959,15 @@ int launch_grouped_t(const TqBatch& batch, int64_t grid, cudaStream_t s) {
 int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t seq,
                       const void* const* xs, int xkind, const float* const* sxs, float* const* ys,
                       const int64_t* ldys, cudaStream_t s, const int64_t* seqs, int digits,
-                      const float* kscale, int64_t kblock, int act, int64_t fout) {
+                      const float* kscale, int64_t kblock, int act, int64_t ldx) {
   FT_CHECK(n >= 1 && n <= kMaxProblems, FT_ERR_UNSUPPORTED, "group size %d not in [1, %d]", n,
            kMaxProblems);
   if (digits <= 0) digits = kDigitsExact;
   FT_CHECK(xkind == 2 || digits == kDigitsExact || digits == kDigitsMoE, FT_ERR_UNSUPPORTED,
            "unsupported digit count %d", digits);
   const int D = xkind == 2 ? 1 : digits;
-  FT_CHECK(!act || (xkind != 2 && digits == 4 && !kscale), FT_ERR_UNSUPPORTED,
-           "the fused activation needs 4-digit fp32/bf16 activations");
+  FT_CHECK(!act || (xkind == 0 && !kscale), FT_ERR_UNSUPPORTED,
+           "the fused activation needs fp32 gate/up activations");
   FT_CHECK(!kscale || (xkind != 2 && kblock >= 1), FT_ERR_UNSUPPORTED,
            "column-block scales need fp32/bf16 activations and a block size >= 1");
   int64_t max_seq = 0;
@@ -1055,7 +1024,8 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
       const int j = src_of[q];
       gp[q] = GvLaunchProblem{w->codes, w->row_scales, w->rows, w->n_chunks, src_x[j],
                               src_k[j], src_seq[j], sxs ? sxs[i] : nullptr, ys[i],
-                              ldys ? ldys[i] : w->rows, kscale, kblock};
+                              ldys ? ldys[i] : w->rows, kscale, kblock, act,
+                              act ? ldx : src_k[j]};
     }
     return launch_gemv(ctx, nlive, gp, xkind, ws[live[0]]->format == 1, D, s);
   }
@@ -1125,9 +1095,9 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
     p.kblock = kblock;
     p.sx = sxs ? sxs[i] : nullptr;
     p.y = ys[i];
-    p.ldy = ldys ? ldys[i] : (act ? fout : w->rows);
+    p.ldy = ldys ? ldys[i] : w->rows;
     p.act = act;
-    p.fout = fout;
+    p.ldx = act ? ldx : src_k[j];
     p.seq = src_seq[j];
     p.tok_per_pass = tok_per_pass;
     p.passes = (int)passes;
@@ -1170,6 +1140,8 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
       pb.block_begin[j] = blocks;
       PrepSource& ps = pb.s[j];
       ps.x = src_x[j];
+      ps.act = act;
+      ps.ldx = act ? ldx : src_k[j];
       ps.kscale = kscale;
       ps.kblock = kblock;
       ps.bmat = reinterpret_cast<int8_t*>(wsb + b_off[j]);
@@ -1185,7 +1157,7 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
     pb.block_begin[nsrc] = blocks;
     FT_CHECK(blocks <= 0x7FFFFFFF, FT_ERR_UNSUPPORTED, "too many prep blocks");
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)blocks);
+    cfg.gridDim = dim3((unsigned)ceil_div(blocks, kPrepWarps));  // one warp per slot
     cfg.blockDim = dim3(kPrepThreads);
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
@@ -1313,6 +1285,7 @@ int launch_tc_noalloc(ft_ctx* ctx, const ft_weight* w, int64_t seq, const float*
   p.tok_scale = reinterpret_cast<const double*>(zs + kNaTokOff);
   p.nf = reinterpret_cast<const int32_t*>(zs + kNaNfOff);
   p.x = x;
+  p.ldx = w->cols;
   p.K = w->cols;
   p.kscale = nullptr;
   p.kblock = 1;
@@ -1350,6 +1323,7 @@ int launch_tc_noalloc(ft_ctx* ctx, const ft_weight* w, int64_t seq, const float*
   pb.block_begin[1] = tok_per_pass;
   PrepSource& ps = pb.s[0];
   ps.x = x;
+  ps.ldx = w->cols;
   ps.kscale = nullptr;
   ps.kblock = 1;
   ps.bmat = reinterpret_cast<int8_t*>(zs + kNaBOff);
@@ -1360,7 +1334,7 @@ int launch_tc_noalloc(ft_ctx* ctx, const ft_weight* w, int64_t seq, const float*
   ps.K = w->cols;
   ps.n_chunks = w->n_chunks;
   ps.passes = 1;
-  prep_b_kernel<kDigitsExact><<<tok_per_pass, kPrepThreads, 0, s>>>(pb);
+  prep_b_kernel<kDigitsExact><<<(unsigned)ceil_div(tok_per_pass, kPrepWarps), kPrepThreads, 0, s>>>(pb);
   FT_LAUNCH_CHECK();
   const int64_t grid = batch.total_items < grid_target ? batch.total_items : grid_target;
   return launch_grouped_t<kNaNpad>(batch, grid, s);
