@@ -670,246 +670,324 @@ __device__ __forceinline__ int64_t b_offset(int64_t pass, int64_t chunk, int n, 
 // DT: digits per token (1: int8 codes, 4 or 8), a template parameter so that
 // the digit arrays stay in registers.
 //
-// One warp per (source, pass, token slot), kPrepWarps slots per block, so
-// every reduction is a warp reduction and no block barrier is taken.  Lane l
-// holds elements 256 i + 8 l .. +7 of the token (one 16-byte load of bf16 /
-// int8, two of fp32, when aligned): kPrepIt such stretches (2048 K) stay in
-// registers between the absmax, the non-finite count, the digit split and
-// the column sums; longer rows are read again.  Each lane writes 8 bytes of
+// W warps per (source, pass, token slot), 8 / W slots per block: W = 1 for
+// launches of many slots (every reduction is a warp reduction), up to 8 (one
+// block per slot) when there are few slots and long rows.  Thread tg of a
+// slot's group holds elements S i + 8 tg .. +7 (S = 256 W; one 16-byte load of
+// bf16 / int8, two of fp32, when aligned): the first stretches (2 for W = 1,
+// one otherwise) stay in registers between the absmax, the non-finite count,
+// the digit split and the column sums; the rest are read again (from cache),
+// which keeps the warp-per-slot variant at three blocks per SM.  Each thread writes 8 bytes of
 // each digit column's 16-byte operand row.
-constexpr int kPrepThreads = 256, kPrepWarps = kPrepThreads / 32, kPrepIt = 8;
+constexpr int kPrepThreads = 256, kPrepWarps = kPrepThreads / 32;
 
-template <int DT>
-__global__ void __launch_bounds__(kPrepThreads) prep_b_kernel(const __grid_constant__ PrepBatch pb) {
-  // Wait for the previous matmul, which may still be reading bmat.  The
-  // matmul that consumes this launch is released only at the end of each
-  // block: its persistent CTAs, once resident, would leave this grid's
-  // remaining blocks a fraction of the SM's registers.
+template <int DT, int W>
+__global__ void __launch_bounds__(kPrepThreads, W == 1 ? 3 : 1) prep_b_kernel(const __grid_constant__ PrepBatch pb) {
+  // Wait for the previous matmul, which may still be reading bmat.  A launch
+  // of many slots releases the matmul that consumes it only at the end of
+  // each block (that matmul's persistent CTAs, once resident, would leave
+  // the remaining blocks a fraction of the SM's registers); a short one
+  // releases it at once, so the matmul starts its weight stream meanwhile.
+  if (W > 1) tc::pdl_launch_dependents();
   tc::pdl_wait();
+  constexpr int kIt = W >= 2 ? 1 : 2, kS = 256 * W;  // register-cached stretches
+  __shared__ float red_f[kPrepWarps];
+  __shared__ int red_n[kPrepWarps];
+  __shared__ int red_i[kPrepWarps][8];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t slot = (int64_t)blockIdx.x * kPrepWarps + warp;
-  if (slot < pb.block_begin[pb.nsrc]) {
-    // the source holding this slot (binary search over the slot offsets)
-    int lo = 0, hi = pb.nsrc - 1;
+  const int gw = warp % W, w0 = warp - gw;  // this warp's index in its slot group, and the first
+  const int tg = 32 * gw + lane;
+  const int64_t slot = (int64_t)blockIdx.x * (kPrepWarps / W) + warp / W;
+  const bool have = slot < pb.block_begin[pb.nsrc];
+  // the source holding this slot (binary search over the slot offsets)
+  int lo = 0;
+  if (have) {
+    int hi = pb.nsrc - 1;
     while (lo < hi) {
       const int mid = (lo + hi + 1) >> 1;
       if (pb.block_begin[mid] <= slot) lo = mid;
       else hi = mid - 1;
     }
-    const PrepSource& src = pb.s[lo];
-    const int64_t local = slot - pb.block_begin[lo];
-    const int64_t pass = local / pb.tok_per_pass;
-    const int lt = (int)(local % pb.tok_per_pass);
-    const int64_t t = pass * pb.tok_per_pass + lt;
-    const int64_t K = src.K, kpad = src.n_chunks * 128;
-    constexpr int D = DT;
-    const int npad = pb.npad, xkind = pb.xkind;
-    const float* kscale = src.kscale;
-    const int64_t kblock = src.kblock;
-    const void* xsrc = src.x;
-    const bool live = t < src.seq;
-    const int64_t nst = (kpad + 255) / 256;  // stretches of 256 K
+  }
+  const PrepSource& src = pb.s[lo];
+  const int64_t local = have ? slot - pb.block_begin[lo] : 0;
+  const int64_t pass = local / pb.tok_per_pass;
+  const int lt = (int)(local % pb.tok_per_pass);
+  const int64_t t = pass * pb.tok_per_pass + lt;
+  const int64_t K = src.K, kpad = src.n_chunks * 128;
+  constexpr int D = DT;
+  const int npad = pb.npad, xkind = pb.xkind;
+  const float* kscale = src.kscale;
+  const int64_t kblock = src.kblock;
+  const void* xsrc = src.x;
+  const bool live = have && t < src.seq;
+  const int64_t nst = have ? (kpad + kS - 1) / kS : 0;  // stretches of this slot
 
-    // the 8 elements at k0 .. k0+7 of this token (zero past K), as floats
-    // (int8 codes: their integer values)
-    auto load8 = [&](int64_t k0, float (&v)[8]) {
+  // the 8 elements at k0 .. k0+7 of this token (zero past K), as floats
+  // (int8 codes: their integer values)
+  auto load8 = [&](int64_t k0, float (&v)[8]) {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) v[e] = 0.0f;
-      if (!live || k0 >= K) return;
-      if (src.act) {
-        // k0 .. k0+7 lie in one 16-wide group: gate row 32 (k0/16) + k0%16,
-        // its up row 16 further
-        const float* gp = static_cast<const float*>(xsrc) + t * src.ldx + 32 * (k0 >> 4) + (k0 & 15);
-        if (k0 + 8 <= K && (reinterpret_cast<uintptr_t>(gp) & 15) == 0) {
-          const float4 g0 = __ldg(reinterpret_cast<const float4*>(gp));
-          const float4 g1 = __ldg(reinterpret_cast<const float4*>(gp) + 1);
-          const float4 u0 = __ldg(reinterpret_cast<const float4*>(gp + 16));
-          const float4 u1 = __ldg(reinterpret_cast<const float4*>(gp + 16) + 1);
-          const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-          const float u[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+    for (int e = 0; e < 8; ++e) v[e] = 0.0f;
+    if (!live || k0 >= K) return;
+    if (src.act) {
+      // k0 .. k0+7 lie in one 16-wide group: gate row 32 (k0/16) + k0%16,
+      // its up row 16 further
+      const float* gp = static_cast<const float*>(xsrc) + t * src.ldx + 32 * (k0 >> 4) + (k0 & 15);
+      if (k0 + 8 <= K && (reinterpret_cast<uintptr_t>(gp) & 15) == 0) {
+        const float4 g0 = __ldg(reinterpret_cast<const float4*>(gp));
+        const float4 g1 = __ldg(reinterpret_cast<const float4*>(gp) + 1);
+        const float4 u0 = __ldg(reinterpret_cast<const float4*>(gp + 16));
+        const float4 u1 = __ldg(reinterpret_cast<const float4*>(gp + 16) + 1);
+        const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+        const float u[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
 #pragma unroll
-          for (int e = 0; e < 8; ++e) v[e] = expert_act(g[e], u[e], src.act);
-        } else {
-#pragma unroll
-          for (int e = 0; e < 8; ++e)
-            if (k0 + e < K) v[e] = expert_act(__ldg(gp + e), __ldg(gp + 16 + e), src.act);
-        }
-        return;
-      }
-      const int64_t i0 = t * src.ldx + k0;
-      if (xkind == 2) {
-        const int8_t* q = static_cast<const int8_t*>(xsrc) + i0;
-        if (k0 + 8 <= K && (reinterpret_cast<uintptr_t>(q) & 7) == 0) {
-          const uint2 u = __ldg(reinterpret_cast<const uint2*>(q));
-          const uint32_t w2[2] = {u.x, u.y};
-#pragma unroll
-          for (int e = 0; e < 8; ++e) v[e] = (float)(int8_t)(w2[e >> 2] >> (8 * (e & 3)));
-        } else {
-#pragma unroll
-          for (int e = 0; e < 8; ++e)
-            if (k0 + e < K) v[e] = (float)q[e];
-        }
-        return;
-      }
-      if (xkind == 1) {
-        const uint16_t* h = static_cast<const uint16_t*>(xsrc) + i0;
-        if (k0 + 8 <= K && (reinterpret_cast<uintptr_t>(h) & 15) == 0) {
-          const uint4 u = __ldg(reinterpret_cast<const uint4*>(h));
-          const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            v[2 * e] = __uint_as_float(w4[e] << 16);
-            v[2 * e + 1] = __uint_as_float(w4[e] & 0xffff0000u);
-          }
-        } else {
-#pragma unroll
-          for (int e = 0; e < 8; ++e)
-            if (k0 + e < K) v[e] = __uint_as_float((uint32_t)h[e] << 16);
-        }
+        for (int e = 0; e < 8; ++e) v[e] = expert_act(g[e], u[e], src.act);
       } else {
-        const float* f = static_cast<const float*>(xsrc) + i0;
-        if (k0 + 8 <= K && (reinterpret_cast<uintptr_t>(f) & 15) == 0) {
-          const float4 a = __ldg(reinterpret_cast<const float4*>(f));
-          const float4 b = __ldg(reinterpret_cast<const float4*>(f) + 1);
-          v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-          v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-        } else {
-#pragma unroll
-          for (int e = 0; e < 8; ++e)
-            if (k0 + e < K) v[e] = f[e];
-        }
-      }
-      if (kscale) {
 #pragma unroll
         for (int e = 0; e < 8; ++e)
-          if (k0 + e < K) v[e] = __fmul_rn(v[e], kscale[(k0 + e) / kblock]);
+          if (k0 + e < K) v[e] = expert_act(__ldg(gp + e), __ldg(gp + 16 + e), src.act);
       }
-    };
-
-    float xr[kPrepIt][8];
-    float f1 = 1.0f, f2 = 1.0f;
-    if (D != 1) {
-#pragma unroll
-      for (int i = 0; i < kPrepIt; ++i)
-        if (i < nst) load8(256 * (int64_t)i + 8 * lane, xr[i]);
-      // largest finite |x| and the non-finite count
-      float amax = 0.0f;
-      int nnf = 0;
-      auto scan = [&](const float (&v)[8]) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const bool nf = is_nonfinite(v[e]);
-          nnf += nf ? 1 : 0;
-          amax = fmaxf(amax, nf ? 0.0f : fabsf(v[e]));
-        }
-      };
-#pragma unroll
-      for (int i = 0; i < kPrepIt; ++i)
-        if (i < nst) scan(xr[i]);
-      for (int64_t i = kPrepIt; i < nst; ++i) {
-        float v[8];
-        load8(256 * i + 8 * lane, v);
-        scan(v);
-      }
-      amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(amax)));
-      const int total = __reduce_add_sync(0xffffffffu, (unsigned)nnf);
-      const int sh = amax > 0.0f ? digit_shift(amax, D) : 0;
-      const int s1 = sh > 127 ? 127 : (sh < -126 ? -126 : sh);
-      f1 = __int_as_float((s1 + 127) << 23);
-      f2 = __int_as_float((sh - s1 + 127) << 23);
-      if (live) {
-        int32_t* nf = src.nf + t * (kNfCap + 1);
-        if (lane == 0) {
-          // 2^-sh (1 for an all-zero token), negative when non-finite elements exist
-          const double sc = amax > 0.0f ? __longlong_as_double((long long)(1023 - sh) << 52) : 1.0;
-          src.tok_scale[t] = total ? -sc : sc;
-          nf[0] = total;
-        }
-        if (total != 0 && total <= kNfCap) {
-          // this lane's positions after those of the lanes below it
-          int incl = nnf;
-#pragma unroll
-          for (int o = 1; o < 32; o <<= 1) {
-            const int v = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl += v;
-          }
-          int slot_nf = incl - nnf;
-          if (nnf != 0) {
-            for (int64_t i = 0; i < nst; ++i) {
-              float v[8];
-              load8(256 * i + 8 * lane, v);
-#pragma unroll
-              for (int e = 0; e < 8; ++e)
-                if (is_nonfinite(v[e])) nf[1 + slot_nf++] = (int32_t)(256 * i + 8 * lane + e);
-            }
-          }
-        }
-      }
+      return;
     }
-    // digits of each element; one 8-byte word pair per digit column
-    int csum[D];
+    const int64_t i0 = t * src.ldx + k0;
+    if (xkind == 2) {
+      const int8_t* q = static_cast<const int8_t*>(xsrc) + i0;
+      if (k0 + 8 <= K && (reinterpret_cast<uintptr_t>(q) & 7) == 0) {
+        const uint2 u = __ldg(reinterpret_cast<const uint2*>(q));
+        const uint32_t w2[2] = {u.x, u.y};
 #pragma unroll
-    for (int d = 0; d < D; ++d) csum[d] = 0;
-    auto emit = [&](int64_t k0, const float (&v)[8]) {
-      if (k0 >= kpad) return;
-      uint32_t w[D][2];
+        for (int e = 0; e < 8; ++e) v[e] = (float)(int8_t)(w2[e >> 2] >> (8 * (e & 3)));
+      } else {
 #pragma unroll
-      for (int d = 0; d < D; ++d) w[d][0] = w[d][1] = 0u;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        if (D == 1) {
-          const int q = (int)v[e];
-          w[0][e >> 2] |= (uint32_t)(q & 0xFF) << (8 * (e & 3));
-          csum[0] += q;
-        } else {
-          const float xs = is_nonfinite(v[e]) ? 0.0f : __fmul_rn(__fmul_rn(v[e], f1), f2);
-          // X = round(x * 2^sh), |X| < 2^(8D-2); balanced base-256 digits (64-bit
-          // arithmetic only for D = 8)
-          using XT = typename std::conditional<(D > 4), long long, int>::type;
-          XT X = D > 4 ? (XT)__float2ll_rn(xs) : (XT)__float2int_rn(xs);
-#pragma unroll
-          for (int d = 0; d < D - 1; ++d) {
-            const int lo = ((int)(X & 0xFF) ^ 0x80) - 0x80;  // signed low digit
-            w[d][e >> 2] |= (uint32_t)(lo & 0xFF) << (8 * (e & 3));
-            csum[d] += lo;
-            X = (X - lo) >> 8;
-          }
-          // the top digit, |X| <= 64 here
-          w[D - 1][e >> 2] |= (uint32_t)((int)X & 0xFF) << (8 * (e & 3));
-          csum[D - 1] += (int)X;
-        }
+        for (int e = 0; e < 8; ++e)
+          if (k0 + e < K) v[e] = (float)q[e];
       }
-      const int64_t chunk = k0 >> 7;
-      const int kin = (int)(k0 & 127);
+      return;
+    }
+    if (xkind == 1) {
+      const uint16_t* h = static_cast<const uint16_t*>(xsrc) + i0;
+      if (k0 + 8 <= K && (reinterpret_cast<uintptr_t>(h) & 15) == 0) {
+        const uint4 u = __ldg(reinterpret_cast<const uint4*>(h));
+        const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-      for (int d = 0; d < D; ++d)
-        *reinterpret_cast<uint2*>(src.bmat + b_offset(pass, chunk, lt * D + d, kin & ~15, npad,
-                                                      src.n_chunks) +
-                                  (kin & 8)) = make_uint2(w[d][0], w[d][1]);
-    };
-    if (D != 1) {
+        for (int e = 0; e < 4; ++e) {
+          v[2 * e] = __uint_as_float(w4[e] << 16);
+          v[2 * e + 1] = __uint_as_float(w4[e] & 0xffff0000u);
+        }
+      } else {
 #pragma unroll
-      for (int i = 0; i < kPrepIt; ++i)
-        if (i < nst) emit(256 * (int64_t)i + 8 * lane, xr[i]);
-      for (int64_t i = kPrepIt; i < nst; ++i) {
-        float v[8];
-        load8(256 * i + 8 * lane, v);
-        emit(256 * i + 8 * lane, v);
+        for (int e = 0; e < 8; ++e)
+          if (k0 + e < K) v[e] = __uint_as_float((uint32_t)h[e] << 16);
       }
     } else {
-      for (int64_t i = 0; i < nst; ++i) {
-        float v[8];
-        load8(256 * i + 8 * lane, v);
-        emit(256 * i + 8 * lane, v);
+      const float* f = static_cast<const float*>(xsrc) + i0;
+      if (k0 + 8 <= K && (reinterpret_cast<uintptr_t>(f) & 15) == 0) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(f));
+        const float4 b = __ldg(reinterpret_cast<const float4*>(f) + 1);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (k0 + e < K) v[e] = f[e];
       }
     }
+    if (kscale) {
 #pragma unroll
-    for (int d = 0; d < D; ++d) {
-      const int v = __reduce_add_sync(0xffffffffu, (unsigned)csum[d]);
-      if (lane == 0) src.colsum[pass * npad + lt * D + d] = v;
+      for (int e = 0; e < 8; ++e)
+        if (k0 + e < K) v[e] = __fmul_rn(v[e], kscale[(k0 + e) / kblock]);
+    }
+  };
+
+  float xr[kIt][8];
+  float f1 = 1.0f, f2 = 1.0f;
+  if (D != 1) {
+#pragma unroll
+    for (int i = 0; i < kIt; ++i)
+      if (i < nst) load8(kS * (int64_t)i + 8 * tg, xr[i]);
+    // largest finite |x| and the non-finite count
+    float amax = 0.0f;
+    int nnf = 0;
+    auto scan = [&](const float (&v)[8]) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const bool nf = is_nonfinite(v[e]);
+        nnf += nf ? 1 : 0;
+        amax = fmaxf(amax, nf ? 0.0f : fabsf(v[e]));
+      }
+    };
+#pragma unroll
+    for (int i = 0; i < kIt; ++i)
+      if (i < nst) scan(xr[i]);
+    for (int64_t i = kIt; i < nst; ++i) {
+      float v[8];
+      load8(kS * i + 8 * tg, v);
+      scan(v);
+    }
+    int incl = nnf;  // inclusive scan of the non-finite counts over the warp
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(amax)));
+    int before = incl - nnf, total = __shfl_sync(0xffffffffu, incl, 31);
+    if (W > 1) {
+      if (lane == 0) {
+        red_f[warp] = amax;
+        red_n[warp] = total;
+      }
+      __syncthreads();
+      amax = 0.0f;
+      total = 0;
+#pragma unroll
+      for (int w = 0; w < W; ++w) {
+        amax = fmaxf(amax, red_f[w0 + w]);
+        if (w < gw) before += red_n[w0 + w];
+        total += red_n[w0 + w];
+      }
+    }
+    const int sh = amax > 0.0f ? digit_shift(amax, D) : 0;
+    const int s1 = sh > 127 ? 127 : (sh < -126 ? -126 : sh);
+    f1 = __int_as_float((s1 + 127) << 23);
+    f2 = __int_as_float((sh - s1 + 127) << 23);
+    if (live) {
+      int32_t* nf = src.nf + t * (kNfCap + 1);
+      if (tg == 0) {
+        // 2^-sh (1 for an all-zero token), negative when non-finite elements exist
+        const double sc = amax > 0.0f ? __longlong_as_double((long long)(1023 - sh) << 52) : 1.0;
+        src.tok_scale[t] = total ? -sc : sc;
+        nf[0] = total;
+      }
+      if (nnf != 0 && total <= kNfCap) {
+        // this thread's positions after those of the threads below it
+        int slot_nf = before;
+        for (int64_t i = 0; i < nst; ++i) {
+          float v[8];
+          load8(kS * i + 8 * tg, v);
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            if (is_nonfinite(v[e])) nf[1 + slot_nf++] = (int32_t)(kS * i + 8 * tg + e);
+        }
+      }
     }
   }
-  tc::pdl_launch_dependents();
+  // digits of each element; one 8-byte word pair per digit column
+  int csum[D];
+#pragma unroll
+  for (int d = 0; d < D; ++d) csum[d] = 0;
+  // Byte permutes gather digit d of four elements (bytes of U0..U3) into one
+  // word: [byte d of U0, U1, U2, U3].
+  auto gather = [](uint32_t u0, uint32_t u1, uint32_t u2, uint32_t u3, uint32_t (&wd)[4]) {
+    const uint32_t lo01 = __byte_perm(u0, u1, 0x5140), lo23 = __byte_perm(u2, u3, 0x5140);
+    const uint32_t hi01 = __byte_perm(u0, u1, 0x7362), hi23 = __byte_perm(u2, u3, 0x7362);
+    wd[0] = __byte_perm(lo01, lo23, 0x5410);
+    wd[1] = __byte_perm(lo01, lo23, 0x7632);
+    wd[2] = __byte_perm(hi01, hi23, 0x5410);
+    wd[3] = __byte_perm(hi01, hi23, 0x7632);
+  };
+  auto emit = [&](int64_t k0, const float (&v)[8]) {
+    if (k0 >= kpad) return;
+    uint32_t w[D][2];
+#pragma unroll
+    for (int hq = 0; hq < 2; ++hq) {  // elements 4 hq .. 4 hq + 3
+      if (D == 1) {
+        uint32_t q = 0;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) q |= (uint32_t)((int)v[4 * hq + e] & 0xFF) << (8 * e);
+        w[0][hq] = q;
+      } else {
+        float xs[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float x = v[4 * hq + e];
+          xs[e] = is_nonfinite(x) ? 0.0f : __fmul_rn(__fmul_rn(x, f1), f2);
+        }
+        if (D == 4) {
+          // X = round(x * 2^sh), |X| < 2^30; U = X + 0x808080: its low three
+          // bytes are the balanced low digits + 128, its top byte the top digit
+          uint32_t wd[4];
+          gather((uint32_t)__float2int_rn(xs[0]) + 0x808080u, (uint32_t)__float2int_rn(xs[1]) + 0x808080u,
+                 (uint32_t)__float2int_rn(xs[2]) + 0x808080u, (uint32_t)__float2int_rn(xs[3]) + 0x808080u,
+                 wd);
+#pragma unroll
+          for (int d = 0; d < 4; ++d) w[d < D ? d : 0][hq] = d < 3 ? wd[d] ^ 0x80808080u : wd[d];
+        } else {
+          // X = round(x * 2^sh), |X| < 2^62; U = X + 0x0080808080808080: bytes 0..6
+          // are the balanced low digits + 128, byte 7 the top digit
+          const unsigned long long b7 = 0x0080808080808080ull;
+          unsigned long long U[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) U[e] = (unsigned long long)__float2ll_rn(xs[e]) + b7;
+          uint32_t lo[4], hi[4];
+          gather((uint32_t)U[0], (uint32_t)U[1], (uint32_t)U[2], (uint32_t)U[3], lo);
+          gather((uint32_t)(U[0] >> 32), (uint32_t)(U[1] >> 32), (uint32_t)(U[2] >> 32),
+                 (uint32_t)(U[3] >> 32), hi);
+#pragma unroll
+          for (int d = 0; d < 4; ++d) {
+            w[d][hq] = lo[d] ^ 0x80808080u;
+            w[(d + 4) < D ? d + 4 : 0][hq] = d < 3 ? hi[d] ^ 0x80808080u : hi[d];
+          }
+        }
+      }
+    }
+    // column sums: signed bytes of each digit word
+#pragma unroll
+    for (int d = 0; d < D; ++d)
+      csum[d] = __dp4a((int)w[d][1], 0x01010101, __dp4a((int)w[d][0], 0x01010101, csum[d]));
+    const int64_t chunk = k0 >> 7;
+    const int kin = (int)(k0 & 127);
+#pragma unroll
+    for (int d = 0; d < D; ++d)
+      *reinterpret_cast<uint2*>(src.bmat + b_offset(pass, chunk, lt * D + d, kin & ~15, npad,
+                                                    src.n_chunks) +
+                                (kin & 8)) = make_uint2(w[d][0], w[d][1]);
+  };
+  if (D != 1) {
+#pragma unroll
+    for (int i = 0; i < kIt; ++i)
+      if (i < nst) emit(kS * (int64_t)i + 8 * tg, xr[i]);
+  }
+  for (int64_t i = D != 1 ? kIt : 0; i < nst; ++i) {
+    float v[8];
+    load8(kS * i + 8 * tg, v);
+    emit(kS * i + 8 * tg, v);
+  }
+#pragma unroll
+  for (int d = 0; d < D; ++d) {
+    const int v = __reduce_add_sync(0xffffffffu, (unsigned)csum[d]);
+    if (W > 1) {
+      if (lane == 0) red_i[warp][d] = v;
+    } else if (have && lane == 0) {
+      src.colsum[pass * npad + lt * D + d] = v;
+    }
+  }
+  if (W > 1) {
+    __syncthreads();
+    if (have && gw == 0 && lane < D) {
+      int v = 0;
+#pragma unroll
+      for (int w = 0; w < W; ++w) v += red_i[w0 + w][lane];
+      src.colsum[pass * npad + lt * D + lane] = v;
+    }
+  }
+  if (W == 1) tc::pdl_launch_dependents();
+}
+
+// slots -> warps per slot: many slots use one warp each, few slots (long
+// rows, little parallelism) up to a block each
+int prep_warps(int64_t slots) {
+  return slots >= 4096 ? 1 : slots >= 2048 ? 2 : slots >= 1024 ? 4 : 8;
+}
+
+template <int DT>
+cudaError_t launch_prep(const PrepBatch& pb, int64_t slots, cudaLaunchConfig_t cfg) {
+  const int W = prep_warps(slots);
+  cfg.gridDim = dim3((unsigned)ceil_div(slots * W, kPrepWarps));
+  if (W == 1) return cudaLaunchKernelEx(&cfg, prep_b_kernel<DT, 1>, pb);
+  if (W == 2) return cudaLaunchKernelEx(&cfg, prep_b_kernel<DT, 2>, pb);
+  if (W == 4) return cudaLaunchKernelEx(&cfg, prep_b_kernel<DT, 4>, pb);
+  return cudaLaunchKernelEx(&cfg, prep_b_kernel<DT, 8>, pb);
 }
 
 #ifndef FT_MAX_NPAD
@@ -1157,7 +1235,6 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
     pb.block_begin[nsrc] = blocks;
     FT_CHECK(blocks <= 0x7FFFFFFF, FT_ERR_UNSUPPORTED, "too many prep blocks");
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)ceil_div(blocks, kPrepWarps));  // one warp per slot
     cfg.blockDim = dim3(kPrepThreads);
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
@@ -1165,9 +1242,9 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (D == 1) FT_CUDA(cudaLaunchKernelEx(&cfg, prep_b_kernel<1>, pb));
-    else if (D == 4) FT_CUDA(cudaLaunchKernelEx(&cfg, prep_b_kernel<4>, pb));
-    else FT_CUDA(cudaLaunchKernelEx(&cfg, prep_b_kernel<8>, pb));
+    if (D == 1) FT_CUDA(launch_prep<1>(pb, blocks, cfg));
+    else if (D == 4) FT_CUDA(launch_prep<4>(pb, blocks, cfg));
+    else FT_CUDA(launch_prep<8>(pb, blocks, cfg));
     FT_LAUNCH_CHECK();
   }
 
@@ -1334,7 +1411,7 @@ int launch_tc_noalloc(ft_ctx* ctx, const ft_weight* w, int64_t seq, const float*
   ps.K = w->cols;
   ps.n_chunks = w->n_chunks;
   ps.passes = 1;
-  prep_b_kernel<kDigitsExact><<<(unsigned)ceil_div(tok_per_pass, kPrepWarps), kPrepThreads, 0, s>>>(pb);
+  prep_b_kernel<kDigitsExact, 8><<<tok_per_pass, kPrepThreads, 0, s>>>(pb);
   FT_LAUNCH_CHECK();
   const int64_t grid = batch.total_items < grid_target ? batch.total_items : grid_target;
   return launch_grouped_t<kNaNpad>(batch, grid, s);
