@@ -375,18 +375,52 @@ __global__ void interleave_gu_kernel(const uint4* __restrict__ gate, const uint4
 }
 
 // y[t, j] = sum_k w[t, k] * o[slot_of[t, k], j], accumulated from 0 in k order
+// (grid: x over H in float4 pieces, y and z over tokens; K <= 8)
 __global__ void moe_combine_kernel(const float* __restrict__ o, const int32_t* __restrict__ slot_of,
                                    const float* __restrict__ topk_w, int64_t T, int K, int64_t H,
                                    float* __restrict__ y) {
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= T * H) return;
-  const int64_t t = i / H, j = i % H;
-  float acc = 0.0f;
-  for (int k = 0; k < K; ++k) {
-    const float w = topk_w[t * K + k];
-    acc = __fadd_rn(acc, __fmul_rn(w, o[(int64_t)slot_of[t * K + k] * H + j]));
+  const int64_t t = blockIdx.y + (int64_t)blockIdx.z * gridDim.y;
+  if (t >= T) return;
+  int64_t row[8];
+  float w[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    row[k] = k < K ? (int64_t)slot_of[t * K + k] * H : 0;
+    w[k] = k < K ? topk_w[t * K + k] : 0.0f;
   }
-  y[i] = acc;
+  const int64_t j0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if ((H & 3) == 0) {
+    const int64_t j = 4 * j0;
+    if (j >= H) return;
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      if (k >= K) break;
+      const float4 v = *reinterpret_cast<const float4*>(o + row[k] + j);
+      acc.x = __fadd_rn(acc.x, __fmul_rn(w[k], v.x));
+      acc.y = __fadd_rn(acc.y, __fmul_rn(w[k], v.y));
+      acc.z = __fadd_rn(acc.z, __fmul_rn(w[k], v.z));
+      acc.w = __fadd_rn(acc.w, __fmul_rn(w[k], v.w));
+    }
+    *reinterpret_cast<float4*>(y + t * H + j) = acc;
+  } else {
+    for (int64_t j = j0; j < H; j += (int64_t)gridDim.x * blockDim.x) {
+      float acc = 0.0f;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        if (k >= K) break;
+        acc = __fadd_rn(acc, __fmul_rn(w[k], o[row[k] + j]));
+      }
+      y[t * H + j] = acc;
+    }
+  }
+}
+
+// launch geometry of moe_combine_kernel
+dim3 combine_grid(int64_t T, int64_t H) {
+  const int64_t xs = (H & 3) == 0 ? ceil_div(H / 4, 256) : ceil_div(H, 256);
+  const int64_t ys = T < 65535 ? T : 65535;
+  return dim3((unsigned)(xs < 1 ? 1 : xs), (unsigned)(ys < 1 ? 1 : ys), (unsigned)ceil_div(T, ys < 1 ? 1 : ys));
 }
 
 int moe_reserve(ft_moe* m, size_t bytes, cudaStream_t s) {
@@ -838,9 +872,8 @@ int ft_moe_combine(ft_ctx* ctx, ft_moe* m, int64_t T, const float* o_rows_dev,
   FT_CHECK(ctx && m && (T == 0 || (o_rows_dev && slot_of_dev && topk_w_dev && y_dev)),
            FT_ERR_SHAPE, "null argument");
   if (T == 0) return FT_OK;
-  moe_combine_kernel<<<(unsigned)ceil_div(T * m->H, 256), 256, 0,
-                       static_cast<cudaStream_t>(stream)>>>(o_rows_dev, slot_of_dev, topk_w_dev, T,
-                                                            m->top_k, m->H, y_dev);
+  moe_combine_kernel<<<combine_grid(T, m->H), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      o_rows_dev, slot_of_dev, topk_w_dev, T, m->top_k, m->H, y_dev);
   FT_LAUNCH_CHECK();
   return FT_OK;
 }
