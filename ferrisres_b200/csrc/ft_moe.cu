@@ -19,6 +19,7 @@
 #include "ft_internal.cuh"
 
 #include "ft_moe.cuh"
+#include "ft_tc.cuh"
 
 namespace ft {
 namespace {
@@ -306,6 +307,101 @@ __global__ void __launch_bounds__(kRtThreads) moe_router_mma_kernel(
   if (tid < kRtTok && t < T) route_token(sc[tid], E, K, t, topk_idx, topk_w, probs_out, counts);
 }
 
+// bf16 activations against a one-plane (bf16-exact) router, the BASELINE's
+// case: the chunks of x and of the router reach shared memory by cp.async,
+// kRtStages - 1 chunks ahead of the one being multiplied (the plane kernel
+// keeps one chunk in flight, and its K loop is load-latency-bound).  Same
+// arithmetic: an fp32 MMA chain per 64-K chunk, chunks summed in f64.
+constexpr int kRtStages = 4;
+constexpr int kRtXsB = kRtTok * kRtPad * 2, kRtRsB = kMaxExperts * kRtPad * 2;
+constexpr int kRtStB = kRtXsB + kRtRsB;
+static_assert(kRtStages * kRtStB <= 48 * 1024, "router stages fit the default shared memory");
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(tc::smem_u32(dst)), "l"(src)
+               : "memory");
+}
+
+__global__ void __launch_bounds__(kRtThreads) moe_router_bf16_kernel(
+    const uint16_t* __restrict__ x, int64_t T, int64_t H, int64_t Hpad, int E, int K,
+    const uint16_t* __restrict__ Rp, int32_t* __restrict__ topk_idx, float* __restrict__ topk_w,
+    float* __restrict__ probs_out, int32_t* __restrict__ counts) {
+  __shared__ __align__(16) unsigned char st[kRtStages * kRtStB];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, tq = lane & 3;
+  const int64_t t0 = (int64_t)blockIdx.x * kRtTok;
+  const int nch = (int)(Hpad / kRtK);
+  auto issue = [&](int c) {
+    if (c < nch) {
+      unsigned char* sb = st + (c % kRtStages) * kRtStB;
+      const int64_t k0 = (int64_t)c * kRtK;
+      {  // x: 16 tokens x 64 K = 128 pieces of 16 bytes, one per thread
+        const int a = tid >> 3, kk = 8 * (tid & 7);
+        const int64_t t = t0 + a, k = k0 + kk;
+        uint16_t* dst = reinterpret_cast<uint16_t*>(sb) + a * kRtPad + kk;
+        if (t < T && k + 8 <= H) cp_async16(dst, x + t * H + k);
+        else *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {  // router: 64 experts x 64 K = 512 pieces
+        const int piece = tid + i * kRtThreads;
+        const int e = piece >> 3, kk = 8 * (piece & 7);
+        uint16_t* dst = reinterpret_cast<uint16_t*>(sb + kRtXsB) + e * kRtPad + kk;
+        if (e < E) cp_async16(dst, Rp + (int64_t)e * Hpad + k0 + kk);
+        else *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");  // (possibly empty) group per chunk
+  };
+  for (int c = 0; c < kRtStages - 1; ++c) issue(c);
+  double acc[2][4];
+#pragma unroll
+  for (int n = 0; n < 2; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0;
+  for (int c = 0; c < nch; ++c) {
+    asm volatile("cp.async.wait_group %0;" ::"n"(kRtStages - 2) : "memory");
+    __syncthreads();  // chunk c is in; every thread is done with chunk c - 1
+    issue(c + kRtStages - 1);  // into the stage chunk c - 1 used
+    const unsigned char* sb = st + (c % kRtStages) * kRtStB;
+    const uint16_t* xs = reinterpret_cast<const uint16_t*>(sb);
+    const uint16_t* rs = reinterpret_cast<const uint16_t*>(sb + kRtXsB);
+    float part[2][4];
+#pragma unroll
+    for (int n = 0; n < 2; ++n) part[n][0] = part[n][1] = part[n][2] = part[n][3] = 0.0f;
+#pragma unroll
+    for (int ks = 0; ks < kRtK; ks += 16) {
+      const uint32_t a0 = *reinterpret_cast<const uint32_t*>(xs + g * kRtPad + ks + 2 * tq);
+      const uint32_t a1 = *reinterpret_cast<const uint32_t*>(xs + (g + 8) * kRtPad + ks + 2 * tq);
+      const uint32_t a2 = *reinterpret_cast<const uint32_t*>(xs + g * kRtPad + ks + 8 + 2 * tq);
+      const uint32_t a3 = *reinterpret_cast<const uint32_t*>(xs + (g + 8) * kRtPad + ks + 8 + 2 * tq);
+#pragma unroll
+      for (int n = 0; n < 2; ++n) {
+        const uint16_t* br = rs + (16 * warp + 8 * n + g) * kRtPad;
+        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(br + ks + 2 * tq);
+        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(br + ks + 8 + 2 * tq);
+        mma_bf16(part[n], a0, a1, a2, a3, b0, b1);
+      }
+    }
+#pragma unroll
+    for (int n = 0; n < 2; ++n)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[n][i] += (double)part[n][i];
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  __syncthreads();  // every warp is done reading the stages before the scores overwrite them
+  auto sc = reinterpret_cast<float(*)[kMaxExperts + 1]>(st);
+#pragma unroll
+  for (int n = 0; n < 2; ++n) {
+    const int e0 = 16 * warp + 8 * n + 2 * tq;
+    sc[g][e0] = (float)acc[n][0];
+    sc[g][e0 + 1] = (float)acc[n][1];
+    sc[g + 8][e0] = (float)acc[n][2];
+    sc[g + 8][e0 + 1] = (float)acc[n][3];
+  }
+  __syncthreads();
+  const int64_t t = t0 + tid;
+  if (tid < kRtTok && t < T) route_token(sc[tid], E, K, t, topk_idx, topk_w, probs_out, counts);
+}
+
 __global__ void moe_offsets_kernel(const int32_t* __restrict__ counts, int E,
                                    int32_t* __restrict__ offsets, int32_t* __restrict__ fill) {
   if (threadIdx.x == 0) {
@@ -512,7 +608,12 @@ int moe_route(ft_ctx* ctx, ft_moe* m, int64_t T, const void* x, int bf16, int32_
               float* topk_w, float* probs, int32_t* counts, cudaStream_t s) {
   FT_CUDA(cudaMemsetAsync(counts, 0, m->E * sizeof(int32_t), s));
   if (T == 0) return FT_OK;
-  if (m->router_planes) {
+  if (m->router_planes && bf16 && m->n_rplanes == 1 && m->H % 8 == 0 &&
+      (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+    moe_router_bf16_kernel<<<(unsigned)ceil_div(T, kRtTok), kRtThreads, 0, s>>>(
+        static_cast<const uint16_t*>(x), T, m->H, m->Hpad, (int)m->E, m->top_k, m->router_planes,
+        topk_idx, topk_w, probs, counts);
+  } else if (m->router_planes) {
     moe_router_mma_kernel<<<(unsigned)ceil_div(T, kRtTok), kRtThreads, 0, s>>>(
         x, bf16, T, m->H, m->Hpad, (int)m->E, m->top_k, m->router_planes, m->n_rplanes, topk_idx,
         topk_w, probs, counts);
