@@ -36,21 +36,34 @@ def _p(t):
 
 
 class GpuMoEBackend:
-    """Stages of ft_moe_* on the current CUDA stream."""
+    """Stages of ft_moe_* on the current CUDA stream.  Intermediate buffers are
+    kept between calls (one set per name and shape): every stage of a step is
+    ordered on the stream after the previous step's use of the same buffer, and
+    the per-step allocations were a sizeable part of the host's time."""
 
     def __init__(self, layer):
         self.layer = layer
         self.E, self.K, self.H = layer.n_experts, layer.top_k, layer.hidden_dim
+        self._bufs = {}
 
     def _s(self):
         return C.c_void_p(torch.cuda.current_stream().cuda_stream)
 
+    def buf(self, name, shape, dtype, device):
+        key = (name, tuple(shape), dtype, device)
+        t = self._bufs.get(key)
+        if t is None:
+            for k in [k for k in self._bufs if k[0] == name]:  # one shape per name
+                del self._bufs[k]
+            t = self._bufs[key] = torch.empty(shape, dtype=dtype, device=device)
+        return t
+
     def route(self, x):
         T = x.shape[0]
         dev = x.device
-        idx = torch.empty(T, self.K, dtype=torch.int32, device=dev)
-        w = torch.empty(T, self.K, dtype=torch.float32, device=dev)
-        counts = torch.empty(self.E, dtype=torch.int32, device=dev)
+        idx = self.buf("idx", (T, self.K), torch.int32, dev)
+        w = self.buf("w", (T, self.K), torch.float32, dev)
+        counts = self.buf("counts", (self.E,), torch.int32, dev)
         call("ft_moe_route", self.layer.ctx.handle, self.layer.handle, T, _p(x),
              int(x.dtype == torch.bfloat16), _p(idx), _p(w), None, _p(counts), self._s())
         return idx, w, counts
@@ -58,24 +71,24 @@ class GpuMoEBackend:
     def layout(self, idx, counts):
         T = idx.shape[0]
         dev = idx.device
-        offs = torch.empty(self.E + 1, dtype=torch.int32, device=dev)
-        fill = torch.empty(self.E, dtype=torch.int32, device=dev)
-        slot_of = torch.empty(T * self.K, dtype=torch.int32, device=dev)
-        token_of = torch.empty(T * self.K, dtype=torch.int32, device=dev)
+        offs = self.buf("offs", (self.E + 1,), torch.int32, dev)
+        fill = self.buf("fill", (self.E,), torch.int32, dev)
+        slot_of = self.buf("slot_of", (T * self.K,), torch.int32, dev)
+        token_of = self.buf("token_of", (T * self.K,), torch.int32, dev)
         call("ft_moe_dispatch_layout", self.layer.ctx.handle, self.layer.handle, T, _p(idx),
              _p(counts), _p(offs), _p(fill), _p(slot_of), _p(token_of), self._s())
         return slot_of, token_of
 
     def gather(self, x, token_of):
         n = token_of.numel()
-        out = torch.empty(n, self.H, dtype=x.dtype, device=x.device)
+        out = self.buf("xg", (n, self.H), x.dtype, x.device)
         call("ft_moe_gather_rows", self.layer.ctx.handle, _p(x), x.element_size(), self.H,
              _p(token_of), n, _p(out), self._s())
         return out
 
     def experts(self, seg_experts, seg_rows, x_rows):
         total = int(sum(seg_rows))
-        out = torch.empty(total, self.H, dtype=torch.float32, device=x_rows.device)
+        out = self.buf("o_recv", (total, self.H), torch.float32, x_rows.device)
         if len(seg_experts):
             e = np.ascontiguousarray(seg_experts, np.int32)
             r = np.ascontiguousarray(seg_rows, np.int64)
@@ -86,7 +99,7 @@ class GpuMoEBackend:
 
     def combine(self, o_rows, slot_of, w):
         T = w.shape[0]
-        y = torch.empty(T, self.H, dtype=torch.float32, device=o_rows.device)
+        y = torch.empty(T, self.H, dtype=torch.float32, device=o_rows.device)  # returned: fresh
         call("ft_moe_combine", self.layer.ctx.handle, self.layer.handle, T, _p(o_rows),
              _p(slot_of), _p(w), _p(y), self._s())
         return y
