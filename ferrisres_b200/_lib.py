@@ -88,7 +88,7 @@ SIGNATURES = {
     "ft_ternary_matmul_i8": [_p, _p, _i64, _p, _p, _p, _p],
     "ft_ternary_matmul_op_dispatch": [_p, _p, _p, _p, _p, _u32, _u32, _u32, _p],
     "ft_gpu_ternary_matmul": [_p, _p, _p, _p, _sz, _sz, _sz, _p],
-    "ft_gpu_ternary_matmul_vram": [_p, _p, _p, _sz, _p],
+    "ft_gpu_ternary_matmul_vram": [_p, _p, _p, _sz, _sz, _sz, _p],
     "ft_moe_create": [_p, _i64, _i64, _i64, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p],
     "ft_moe_destroy": [_p],
     "ft_moe_forward": [_p, _p, _i64, _p, _i, _p, _p, _p],

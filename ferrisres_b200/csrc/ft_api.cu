@@ -328,7 +328,7 @@ int ft_gpu_sparse_ternary_matmul(ft_ctx* ctx, const uint32_t* sparse_words_host,
   int st = ft_sparse_upload_wgsl(ctx, sparse_words_host, (int64_t)out_rows, (int64_t)in_cols,
                                  scales.data(), &w);
   if (st != FT_OK) return st;
-  st = ft_gpu_ternary_matmul_vram(ctx, w, input_host, seq_len, output_host);
+  st = ft_gpu_ternary_matmul_vram(ctx, w, input_host, seq_len, in_cols, out_rows, output_host);
   ft_weight_destroy(w);
   return st;
 }
@@ -466,7 +466,7 @@ int ft_gpu_ternary_matmul(ft_ctx* ctx, const uint32_t* packed_weights_host,
   int st = ft_weight_upload_packed_u32(ctx, packed_weights_host, (int64_t)out_rows,
                                        (int64_t)in_cols, scales_host, &w);
   if (st != FT_OK) return st;
-  st = ft_gpu_ternary_matmul_vram(ctx, w, input_host, seq_len, output_host);
+  st = ft_gpu_ternary_matmul_vram(ctx, w, input_host, seq_len, in_cols, out_rows, output_host);
   ft_weight_destroy(w);
   return st;
 }
@@ -475,9 +475,13 @@ int ft_gpu_ternary_matmul(ft_ctx* ctx, const uint32_t* packed_weights_host,
 constexpr size_t kDirectOutBytes = 256 * 1024;
 
 int ft_gpu_ternary_matmul_vram(ft_ctx* ctx, const ft_weight* w, const float* input_host,
-                               size_t seq_len, float* output_host) {
+                               size_t seq_len, size_t in_cols, size_t out_rows,
+                               float* output_host) {
   FT_CHECK(ctx && w, FT_ERR_SHAPE, "null context or weight");
   FT_CHECK(input_host && output_host, FT_ERR_SHAPE, "null host buffer");
+  FT_CHECK((int64_t)in_cols == w->cols && (int64_t)out_rows == w->rows, FT_ERR_SHAPE,
+           "in_cols x out_rows = %zu x %zu, the weight is [%lld, %lld]", in_cols, out_rows,
+           (long long)w->rows, (long long)w->cols);
   if (seq_len == 0) return FT_OK;
   DeviceGuard g(ctx->device);
   cudaStream_t s = ctx->host_stream;

@@ -407,7 +407,8 @@ class GpuMatmulAccelerator:
         if x.size < seq_len * in_cols:
             raise ShapeError("input too small")
         y = np.empty(seq_len * out_rows, np.float32)
-        check(_vram_fn()(self.ctx.handle, weight.handle, _addr(x), int(seq_len), _addr(y)))
+        check(_vram_fn()(self.ctx.handle, weight.handle, _addr(x), int(seq_len), int(in_cols),
+                         int(out_rows), _addr(y)))
         return y
 
 

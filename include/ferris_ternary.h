@@ -240,9 +240,13 @@ int ft_gpu_sparse_ternary_matmul(ft_ctx* ctx, const uint32_t* sparse_words_host,
                                  const float* input_host, size_t seq_len, size_t in_cols,
                                  size_t out_rows, float* output_host);
 /* GpuMatmulAccelerator::gpu_ternary_matmul_vram (src/model/gpu_forward.rs:1245-1297):
- * weights already resident (ft_weight); host activations in, host output out. */
+ * weights already resident (ft_weight); host activations [seq_len, in_cols] in,
+ * host output [seq_len, out_rows] out.  in_cols / out_rows are the reference's
+ * arguments: they must equal the weight's cols / rows (FT_ERR_SHAPE otherwise),
+ * so a caller's slice lengths are checked at the boundary. */
 int ft_gpu_ternary_matmul_vram(ft_ctx* ctx, const ft_weight* w, const float* input_host,
-                               size_t seq_len, float* output_host);
+                               size_t seq_len, size_t in_cols, size_t out_rows,
+                               float* output_host);
 
 /* ---- MoE FFN layer: TernaryMoELayer (src/model/ternary_moe.rs:77-223) ------
  * router_host: [n_experts, hidden] fp32, row e = expert e (the layout

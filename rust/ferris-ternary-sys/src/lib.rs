@@ -67,7 +67,7 @@ extern "C" {
     pub fn ft_ternary_matmul_op_dispatch(ctx: *mut ft_ctx, ternary_dev: *const u32, scales_dev: *const f32, input_dev: *const f32, output_dev: *mut f32, seq_len: u32, in_cols: u32, out_rows: u32, stream: *mut c_void) -> c_int;
     pub fn ft_gpu_ternary_matmul(ctx: *mut ft_ctx, packed_weights_host: *const u32, scales_host: *const f32, input_host: *const f32, seq_len: usize, in_cols: usize, out_rows: usize, output_host: *mut f32) -> c_int;
     pub fn ft_gpu_sparse_ternary_matmul(ctx: *mut ft_ctx, sparse_words_host: *const u32, scale: f32, input_host: *const f32, seq_len: usize, in_cols: usize, out_rows: usize, output_host: *mut f32) -> c_int;
-    pub fn ft_gpu_ternary_matmul_vram(ctx: *mut ft_ctx, w: *const ft_weight, input_host: *const f32, seq_len: usize, output_host: *mut f32) -> c_int;
+    pub fn ft_gpu_ternary_matmul_vram(ctx: *mut ft_ctx, w: *const ft_weight, input_host: *const f32, seq_len: usize, in_cols: usize, out_rows: usize, output_host: *mut f32) -> c_int;
     pub fn ft_moe_create(ctx: *mut ft_ctx, n_experts: i64, hidden: i64, inter: i64, top_k: c_int, use_gelu: c_int, router_host: *const f32, gate_packed: *const *const u8, gate_scales: *const *const f32, up_packed: *const *const u8, up_scales: *const *const f32, down_packed: *const *const u8, down_scales: *const *const f32, out: *mut *mut ft_moe) -> c_int;
     pub fn ft_moe_destroy(m: *mut ft_moe) -> c_int;
     pub fn ft_moe_forward(ctx: *mut ft_ctx, m: *mut ft_moe, T: i64, x_dev: *const c_void, x_is_bf16: c_int, y_dev: *mut f32, probs_dev: *mut f32, stream: *mut c_void) -> c_int;

@@ -52,8 +52,12 @@ int main(void) {
   ft_weight* w = NULL;
   st = ft_weight_upload_packed_u8(ctx, packed, rows, cols, rs, &w);
   if (st) return fail("ft_weight_upload_packed_u8", st);
-  st = ft_gpu_ternary_matmul_vram(ctx, w, x, (size_t)seq, y);
+  st = ft_gpu_ternary_matmul_vram(ctx, w, x, (size_t)seq, (size_t)cols, (size_t)rows, y);
   if (st) return fail("ft_gpu_ternary_matmul_vram", st);
+  /* slice lengths that disagree with the weight are refused at the boundary */
+  if (ft_gpu_ternary_matmul_vram(ctx, w, x, (size_t)seq, (size_t)cols, (size_t)rows + 1, y) !=
+      FT_ERR_SHAPE)
+    return fail("ft_gpu_ternary_matmul_vram accepted a wrong out_rows", -1);
   for (long s = 0; s < seq; ++s)
     for (long r = 0; r < rows; ++r) {
       double ref = 0.0, cond = 0.0;
