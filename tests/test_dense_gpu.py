@@ -41,6 +41,20 @@ def test_f32_matches_oracle(gpu, rows, cols, seq):
     assert_fp32_close(y, ref, condition(t, x, rows, cols, seq, rs), what=f"{rows}x{cols}x{seq}")
 
 
+def test_cfg1_baseline_seed0(gpu):
+    """BASELINE config 1 as specified: seed 0, W [5632, 2048] with P(-1)=P(0)=P(+1)=1/3,
+    per-row scales ~ U(0.01, 0.1), x [1, 2048] ~ N(0, 1)."""
+    rng = np.random.default_rng(0)
+    rows, cols = 5632, 2048
+    t = rng.integers(-1, 2, size=rows * cols).astype(np.int8)
+    rs = rng.uniform(0.01, 0.1, rows).astype(np.float32)
+    x = rng.standard_normal(cols).astype(np.float32)
+    w = gpu.DeviceTernaryWeight.from_packed_u8(fo.pack_ternary(t), rows, cols, rs)
+    y = w.matmul_f32(torch.from_numpy(x).cuda().view(1, cols)).cpu().numpy()
+    ref = fo.gpu_ternary_mm_cpu(fo.pack_ternary_rows_u32(t, rows, cols), rs, x, 1, cols, rows)
+    assert_fp32_close(y, ref, condition(t, x, rows, cols, 1, rs), what="cfg1 seed 0")
+
+
 @pytest.mark.parametrize("rows,cols,seq", SHAPES)
 def test_i8_bit_exact(gpu, rows, cols, seq):
     rng = np.random.default_rng(rows + cols * 3 + seq)

@@ -291,20 +291,34 @@ def test_errors(kv):
 
 def test_full_cfg5_sampled(kv):
     """cfg5 at full size (B=32, Hq=32, Hkv=8, ctx 32768): every sequence decoded on
-    the GPU; three of them checked against the oracle and float64."""
+    the GPU; three of them checked against the oracle, and their stored form at
+    512 sampled positions against the oracle's quantisation of what was appended."""
     rng = np.random.default_rng(5)
     B, Hq, Hkv, S = 32, 32, 8, 32768
     c = kv.Kv3Cache(B, Hkv, S)
     gen = torch.Generator(device="cuda").manual_seed(5)
+    sample_pos = np.sort(rng.choice(S, 512, replace=False))
+    kept = {}  # (b, chunk) -> appended K and V of the sampled positions, on the host
     for a in range(0, S, 4096):
         kk = torch.randn((B, 4096, Hkv, D), device="cuda", generator=gen).to(torch.bfloat16)
         vv = torch.randn((B, 4096, Hkv, D), device="cuda", generator=gen).to(torch.bfloat16)
         c.append(kk, vv)
+        sel = sample_pos[(sample_pos >= a) & (sample_pos < a + 4096)] - a
+        for b in (0, 17, 31):
+            kept[(b, a)] = (sel + a, kk[b, sel].float().cpu().numpy(), vv[b, sel].float().cpu().numpy())
     q = rng.standard_normal((B, Hq, D)).astype(np.float32)
     out = c.flash_decode(to_dev(q)).cpu().numpy()
     c.ctx.check()
     assert np.isfinite(out).all()
     kc, km, vc, vm = (t.cpu().numpy() for t in c.export_range(0, S))
+    # the appends at full size: the stored form of sampled positions equals the
+    # oracle's quantisation of the appended values, bit for bit
+    for (b, a), (pos, ks, vs) in kept.items():
+        for i, p in enumerate(pos):
+            for src, codes, mm in ((ks, kc, km), (vs, vc, vm)):
+                rp, rmm = fo.kv_quantize_vector(src[i].reshape(-1), D)
+                assert (codes[b, p] == rp).all(), f"codes of sequence {b}, position {p}"
+                assert (mm[b, p].reshape(-1).view(np.uint32) == rmm.view(np.uint32)).all()
     for b in (0, 17, 31):
         store = (kc[b:b + 1], km[b:b + 1], vc[b:b + 1], vm[b:b + 1])
         ref = fo.flash_decode_3bit(q[b:b + 1], *store, 1, S, Hq, Hkv, D).reshape(Hq, D)
