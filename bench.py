@@ -725,16 +725,19 @@ def run_moe(args, torch, dist, device, ws, rank, local, sub_steps, cpu_seconds):
     shard = x.chunk(ws)[rank].contiguous()
     stream = torch.cuda.Stream(device=device)
     timer = Timer(torch, dist, stream, device, ws)
+    # micro-batches per step: 2 hide the step's host synchronisation (the count
+    # exchange) behind the other micro-batch's work (ferrisres_b200/moe_ep.py)
+    micro = args.ep_micro if args.ep_micro > 0 else 2
     with torch.cuda.stream(stream):
         for _ in range(3):
-            y = moe_ep.ep_forward(shard, be, M_E, rank, ws)
+            y = moe_ep.ep_forward(shard, be, M_E, rank, ws, micro=micro)
     torch.cuda.synchronize()
     sampler = ClockSampler(local)
     sampler.start()
 
     def steps():
         for _ in range(sub_steps):
-            moe_ep.ep_forward(shard, be, M_E, rank, ws)
+            moe_ep.ep_forward(shard, be, M_E, rank, ws, micro=micro)
     sec = timer(steps) / sub_steps
     clocks = sampler.stop()
     # per-phase device times of one instrumented step (max over ranks)
@@ -767,9 +770,12 @@ def run_moe(args, torch, dist, device, ws, rank, local, sub_steps, cpu_seconds):
         "dtype": "bf16 x, ternary experts, exact int8-digit expert GEMMs",
         "config": {"workload": "cfg4 ternary MoE FFN: 64 experts, H=2048, F=1408, SwiGLU, top-2, "
                                "4096 tokens", "parallelism": f"ep{ws}",
-                   "experts_per_gpu": per, "tokens_per_gpu": M_T // ws},
+                   "experts_per_gpu": per, "tokens_per_gpu": M_T // ws,
+                   "micro_batches": micro},
         "algorithmic_TOPS": round(M_OPS / sec / 1e12, 2),
         "phases_us": phases,
+        "phases_note": "one extra step, not micro-batched, each phase closed by an event on the "
+                       "stream (host gaps included); max over ranks",
         "nccl_bytes_per_step": {"dispatch": int(nb[0].item()), "combine": int(nb[1].item()),
                                 "note": "rows sent to other ranks (bf16 in, fp32 out), all ranks"},
         "parity": parity,
@@ -1077,6 +1083,8 @@ def main():
     ap.add_argument("--workload", choices=["all", "gemv", "gemm_cfg2", "sparse_cfg3", "moe_cfg4",
                                            "kv_cfg5"], default="all",
                     help="all = the headline GEMV line with every config as a sub-object")
+    ap.add_argument("--ep-micro", type=int, default=0,
+                    help="MoE micro-batches per step (0: 2)")
     ap.add_argument("--sub-steps", type=int, default=0,
                     help="steps of each sub-config (default: max(--steps, 10), at most 200)")
     args = ap.parse_args()

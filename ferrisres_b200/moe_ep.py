@@ -45,11 +45,13 @@ class GpuMoEBackend:
         self.layer = layer
         self.E, self.K, self.H = layer.n_experts, layer.top_k, layer.hidden_dim
         self._bufs = {}
+        self.tag = 0  # micro-batch in flight: buffers are kept per micro-batch
 
     def _s(self):
         return C.c_void_p(torch.cuda.current_stream().cuda_stream)
 
     def buf(self, name, shape, dtype, device):
+        name = (name, self.tag)
         key = (name, tuple(shape), dtype, device)
         t = self._bufs.get(key)
         if t is None:
@@ -97,9 +99,10 @@ class GpuMoEBackend:
                  int(x_rows.dtype == torch.bfloat16), _p(out), self._s())
         return out
 
-    def combine(self, o_rows, slot_of, w):
+    def combine(self, o_rows, slot_of, w, out=None):
         T = w.shape[0]
-        y = torch.empty(T, self.H, dtype=torch.float32, device=o_rows.device)  # returned: fresh
+        y = out if out is not None else torch.empty(T, self.H, dtype=torch.float32,
+                                                     device=o_rows.device)
         call("ft_moe_combine", self.layer.ctx.handle, self.layer.handle, T, _p(o_rows),
              _p(slot_of), _p(w), _p(y), self._s())
         return y
@@ -108,81 +111,113 @@ class GpuMoEBackend:
 _PINNED = {}
 
 
-def _pinned_counts(world, E, dtype):
-    """A reused pinned host buffer for the gathered counts."""
-    key = (world, E, dtype)
+def _pinned_counts(world, E, dtype, tag=0):
+    """A reused pinned host buffer for the gathered counts (one per micro-batch)."""
+    key = (world, E, dtype, tag)
     if key not in _PINNED:
         _PINNED[key] = torch.empty(world, E, dtype=dtype).pin_memory()
     return _PINNED[key]
 
 
-def ep_forward(x, backend, n_experts, rank=0, world=1, group=None, marks=None, stats=None):
+def ep_forward(x, backend, n_experts, rank=0, world=1, group=None, marks=None, stats=None,
+               micro=1):
     """One expert-parallel MoE forward of this rank's tokens x [T, H].
 
-    ``marks`` (optional list): a CUDA event is recorded on the current stream
-    after each phase and appended as (phase name, event), for per-phase
-    timing.  ``stats`` (optional dict) receives the rows this rank sent to and
-    received from other ranks."""
+    ``micro`` > 1 splits the tokens into that many micro-batches whose routes
+    and count exchanges are all issued first: while the host waits for one
+    micro-batch's counts (the step's host synchronisation) the GPU still has
+    the others' work queued, and while it runs one micro-batch's experts the
+    host issues the next one's exchange.  Results are identical (every token
+    is computed from its own row).
+    ``marks`` (optional list, micro = 1): a CUDA event is recorded on the
+    current stream after each phase and appended as (phase name, event), for
+    per-phase timing.  ``stats`` (optional dict) receives the rows this rank
+    sent to and received from other ranks."""
 
     def mark(name):
-        if marks is not None:
+        if marks is not None and micro <= 1:
             ev = torch.cuda.Event(enable_timing=True)
             ev.record()
             marks.append((name, ev))
+
+    def set_tag(i):
+        if hasattr(backend, "tag"):
+            backend.tag = i
 
     E = n_experts
     if E % world:
         raise ShapeError(f"{E} experts do not split over {world} ranks")
     per = E // world
-    H = x.shape[1]
+    T, H = x.shape[0], x.shape[1]
+    parts = [x] if micro <= 1 or T < micro else list(x.chunk(micro))
     mark("start")
-    idx, w, counts = backend.route(x)
-    slot_of, token_of = backend.layout(idx, counts)
-    # the per-expert counts of every rank, to the host: the only host
-    # synchronisation of the step (NCCL's split sizes and the grouped expert
-    # launch are sized on the host); the row gather runs on the GPU meanwhile
-    if world == 1:
-        ac_dev = counts.view(1, E)
-    else:
-        ac_dev = torch.empty(world * E, dtype=counts.dtype, device=counts.device)
-        dist.all_gather_into_tensor(ac_dev, counts, group=group)
-        ac_dev = ac_dev.view(world, E)
-    if ac_dev.is_cuda:
-        ac_host = _pinned_counts(world, E, counts.dtype)
-        ac_host.copy_(ac_dev, non_blocking=True)
-        ready = torch.cuda.Event()
-        ready.record()
-    else:
-        ac_host, ready = ac_dev, None
-    xg = backend.gather(x, token_of)  # [T*K, H], expert-major
+    # phase 1, every micro-batch: route, expert-major layout, counts of every
+    # rank to the host (pinned copy + event), row gather
+    st = []
+    for i, xc in enumerate(parts):
+        set_tag(i)
+        idx, w, counts = backend.route(xc)
+        slot_of, token_of = backend.layout(idx, counts)
+        if world == 1:
+            ac_dev = counts.view(1, E)
+        else:
+            ac_dev = torch.empty(world * E, dtype=counts.dtype, device=counts.device)
+            dist.all_gather_into_tensor(ac_dev, counts, group=group)
+            ac_dev = ac_dev.view(world, E)
+        if ac_dev.is_cuda:
+            ac_host = _pinned_counts(world, E, counts.dtype, i)
+            ac_host.copy_(ac_dev, non_blocking=True)
+            ready = torch.cuda.Event()
+            ready.record()
+        else:
+            ac_host, ready = ac_dev, None
+        xg = backend.gather(xc, token_of)  # [rows, H], expert-major
+        st.append((xc.shape[0], w, slot_of, xg, ac_host, ready))
     mark("route")
-    if ready is not None:
-        ready.synchronize()
-    ac = ac_host.numpy().astype(np.int64)  # [src rank, expert]
-    mark("counts")
-    send_rows = ac[rank].reshape(world, per).sum(axis=1).tolist()
-    recv_rows = ac[:, rank * per:(rank + 1) * per].sum(axis=1).tolist()
+    out = None
+    if len(parts) > 1 and x.is_cuda:
+        out = torch.empty(T, backend.H if hasattr(backend, "H") else H, dtype=torch.float32,
+                          device=x.device)
+    ys, t0 = [], 0
+    sent = recvd = 0
+    for i, (tc, w, slot_of, xg, ac_host, ready) in enumerate(st):
+        set_tag(i)
+        if ready is not None:
+            ready.synchronize()
+        ac = ac_host.numpy().astype(np.int64)  # [src rank, expert]
+        mark("counts")
+        send_rows = ac[rank].reshape(world, per).sum(axis=1).tolist()
+        recv_rows = ac[:, rank * per:(rank + 1) * per].sum(axis=1).tolist()
+        sent += sum(n for d, n in enumerate(send_rows) if d != rank)
+        recvd += sum(n for s, n in enumerate(recv_rows) if s != rank)
+        if world == 1:
+            recv = xg
+        else:
+            recv = torch.empty(sum(recv_rows), H, dtype=xg.dtype, device=xg.device)
+            dist.all_to_all_single(recv.view(-1), xg.reshape(-1), [r * H for r in recv_rows],
+                                   [r * H for r in send_rows], group=group)
+        mark("dispatch")
+        seg_e = np.tile(np.arange(rank * per, (rank + 1) * per, dtype=np.int32), world)
+        seg_n = ac[:, rank * per:(rank + 1) * per].reshape(-1)
+        o_recv = backend.experts(seg_e, seg_n, recv)
+        mark("experts")
+        if world == 1:
+            o_send = o_recv
+        else:
+            o_send = torch.empty(xg.shape[0], H, dtype=o_recv.dtype, device=xg.device)
+            dist.all_to_all_single(o_send.view(-1), o_recv.view(-1), [r * H for r in send_rows],
+                                   [r * H for r in recv_rows], group=group)
+        mark("combine")
+        if out is not None:
+            backend.combine(o_send, slot_of, w, out=out[t0:t0 + tc])
+        else:
+            ys.append(backend.combine(o_send, slot_of, w))
+        t0 += tc
+        mark("sum")
+    set_tag(0)
     if stats is not None:
-        stats["sent_rows_remote"] = sum(n for d, n in enumerate(send_rows) if d != rank)
-        stats["recv_rows_remote"] = sum(n for s, n in enumerate(recv_rows) if s != rank)
-    if world == 1:
-        recv = xg
-    else:
-        recv = torch.empty(sum(recv_rows), H, dtype=xg.dtype, device=xg.device)
-        dist.all_to_all_single(recv.view(-1), xg.reshape(-1), [r * H for r in recv_rows],
-                               [r * H for r in send_rows], group=group)
-    mark("dispatch")
-    seg_e = np.tile(np.arange(rank * per, (rank + 1) * per, dtype=np.int32), world)
-    seg_n = ac[:, rank * per:(rank + 1) * per].reshape(-1)
-    o_recv = backend.experts(seg_e, seg_n, recv)
-    mark("experts")
-    if world == 1:
-        o_send = o_recv
-    else:
-        o_send = torch.empty(xg.shape[0], H, dtype=o_recv.dtype, device=xg.device)
-        dist.all_to_all_single(o_send.view(-1), o_recv.view(-1), [r * H for r in send_rows],
-                               [r * H for r in recv_rows], group=group)
-    mark("combine")
-    y = backend.combine(o_send, slot_of, w)
-    mark("sum")
-    return y
+        stats["sent_rows_remote"] = sent
+        stats["recv_rows_remote"] = recvd
+    if out is not None:
+        return out
+    return ys[0] if len(ys) == 1 else torch.cat(ys)

@@ -67,14 +67,14 @@ def make(E=8, H=16, F=12, T=24, K=2, seed=0):
     return CpuBackend(R, Wg, Wu, Wd, K), x
 
 
-def _worker(rank, world, port, out_q):
+def _worker(rank, world, port, out_q, micro):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         be, x = make()
         shard = x.chunk(world)[rank]
-        y = ep_forward(shard, be, be.E, rank, world)
+        y = ep_forward(shard, be, be.E, rank, world, micro=micro)
         out_q.put((rank, y.numpy()))
     except Exception as e:  # surface the failure to the parent instead of a queue timeout
         out_q.put((rank, repr(e)))
@@ -88,14 +88,14 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("world", [2, 4])
-def test_ep_matches_single_process(world):
+@pytest.mark.parametrize("world,micro", [(2, 1), (4, 1), (2, 3)])
+def test_ep_matches_single_process(world, micro):
     be, x = make()
     ref = ep_forward(x, be, be.E).numpy()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, micro)) for r in range(world)]
     for p in procs:
         p.start()
     got = dict(q.get(timeout=120) for _ in range(world))

@@ -53,8 +53,12 @@ def _worker(rank, world, port, E, H, F, q):
         layer = moe.TernaryMoELayer.from_ternary(router, keep(g), keep(gs), keep(u), keep(us),
                                                  keep(d), keep(ds), H, F, 2, device=rank)
         shard = x.chunk(world)[rank].cuda()
-        y = moe_ep.ep_forward(shard, moe_ep.GpuMoEBackend(layer), E, rank, world)
+        be = moe_ep.GpuMoEBackend(layer)
+        y = moe_ep.ep_forward(shard, be, E, rank, world)
+        y2 = moe_ep.ep_forward(shard, be, E, rank, world, micro=2)  # micro-batched: identical
         torch.cuda.synchronize()
+        if not torch.equal(y, y2):
+            raise AssertionError("micro-batched EP forward differs")
         q.put((rank, y.cpu().numpy()))
     except Exception as e:  # surface the failure to the parent instead of a queue timeout
         q.put((rank, repr(e)))
