@@ -725,9 +725,10 @@ def run_moe(args, torch, dist, device, ws, rank, local, sub_steps, cpu_seconds):
     shard = x.chunk(ws)[rank].contiguous()
     stream = torch.cuda.Stream(device=device)
     timer = Timer(torch, dist, stream, device, ws)
-    # micro-batches per step: 2 hide the step's host synchronisation (the count
-    # exchange) behind the other micro-batch's work (ferrisres_b200/moe_ep.py)
-    micro = args.ep_micro if args.ep_micro > 0 else 2
+    # micro-batches per step (ferrisres_b200/moe_ep.py): 1 by default -- on one
+    # GPU two micro-batches cost more in launches (1.106 vs 0.994 ms per step)
+    # than the host wait they hide
+    micro = args.ep_micro if args.ep_micro > 0 else 1
     with torch.cuda.stream(stream):
         for _ in range(3):
             y = moe_ep.ep_forward(shard, be, M_E, rank, ws, micro=micro)
@@ -1084,7 +1085,7 @@ def main():
                                            "kv_cfg5"], default="all",
                     help="all = the headline GEMV line with every config as a sub-object")
     ap.add_argument("--ep-micro", type=int, default=0,
-                    help="MoE micro-batches per step (0: 2)")
+                    help="MoE micro-batches per step (0: 1)")
     ap.add_argument("--sub-steps", type=int, default=0,
                     help="steps of each sub-config (default: max(--steps, 10), at most 200)")
     args = ap.parse_args()

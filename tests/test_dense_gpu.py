@@ -300,7 +300,7 @@ def test_host_buffer_outputs(gpu, rows, cols, seq):
     xp = torch.from_numpy(x).pin_memory()
     yp = torch.full((seq * rows,), float("nan"), dtype=torch.float32).pin_memory()
     from ferrisres_b200._lib import check
-    check(_vram_fn()(w.ctx.handle, w.handle, xp.data_ptr(), int(seq), yp.data_ptr()))
+    check(_vram_fn()(w.ctx.handle, w.handle, xp.data_ptr(), int(seq), cols, rows, yp.data_ptr()))
     assert_fp32_close(yp.numpy(), ref, cond, what="pinned output")
 
 
