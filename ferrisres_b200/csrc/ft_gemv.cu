@@ -69,7 +69,7 @@ namespace {
 #define FT_GV_DEPTH2 8
 #endif
 #ifndef FT_GV_GRID_SMALL
-#define FT_GV_GRID_SMALL 2
+#define FT_GV_GRID_SMALL 1
 #endif
 #ifndef FT_GV_GRID_LARGE
 #define FT_GV_GRID_LARGE 2

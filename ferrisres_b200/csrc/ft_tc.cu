@@ -993,6 +993,30 @@ cudaError_t launch_prep(const PrepBatch& pb, int64_t slots, cudaLaunchConfig_t c
 #ifndef FT_MAX_NPAD
 #define FT_MAX_NPAD 128
 #endif
+
+// K splits of a launch of `tiles` (pass, tile) pairs whose longest weight has
+// `chunks` K chunks.  Split-K partials are combined with int32 atomics, so a
+// split pays 128 x npad atomics per item against the shorter per-CTA chunk
+// chain it buys; the split with the least modelled time wins (fewer splits on
+// near-ties).  The constants are measured on B200 with W[11008, 4096]: a CTA
+// takes ~400 cycles per chunk at npad <= 64 and ~640 at npad 128 (MMA-bound),
+// and the GPU completes ~100 int32 atomics per cycle.  With 86 tiles this
+// picks no split: split 4-14 ways the same launch ran 1.6-2.5x slower.
+int pick_ksplit(int64_t tiles, int64_t grid_target, int64_t chunks, int npad) {
+  const double chunk_cycles = npad >= 128 ? 640.0 : 400.0, atomics_per_cycle = 100.0;
+  double best = 0.0;
+  int best_ks = 1;
+  for (int ks = 1; ks <= 64 && ks <= chunks; ++ks) {
+    const double t = (double)ceil_div(tiles * ks, grid_target) *
+                         (double)ceil_div(chunks, (int64_t)ks) * chunk_cycles +
+                     (ks > 1 ? (double)(tiles * ks) * 128.0 * npad / atomics_per_cycle : 0.0);
+    if (ks == 1 || t < 0.97 * best) {
+      best = t;
+      best_ks = ks;
+    }
+  }
+  return best_ks;
+}
 // Column-pass width.  Wide problems use 128-column passes: two TMEM
 // accumulators then fit, so a tile's epilogue overlaps the next tile's MMAs.
 int pick_npad(int64_t ncols) {
@@ -1131,9 +1155,12 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
   // Two CTAs per SM when both fit in TMEM (each has its own MMA-issuing
   // thread, which is what limits a small-N launch); one otherwise.
   const int64_t grid_target = (int64_t)ctx->num_sms * (tmem_cols_for(npad) <= 256 ? 2 : 1);
-  int64_t tiles_total = 0;
-  for (int q = 0; q < nlive; ++q)
+  int64_t tiles_total = 0, max_chunks = 1;
+  for (int q = 0; q < nlive; ++q) {
     tiles_total += ws[live[q]]->n_tiles * ceil_div(src_seq[src_of[q]], tok_per_pass);
+    max_chunks = ws[live[q]]->n_chunks > max_chunks ? ws[live[q]]->n_chunks : max_chunks;
+  }
+  const int64_t ks_group = pick_ksplit(tiles_total, grid_target, max_chunks, npad);
   size_t zoff = 0;
   size_t acc_off[kMaxProblems], cnt_off[kMaxProblems];
   static thread_local TqBatch batch;  // host staging; the launch copies it as the parameter
@@ -1148,14 +1175,7 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
     const int j = src_of[q];
     const int64_t passes = ceil_div(src_seq[j], tok_per_pass);
     TqProblem& p = batch.p[q];
-    // Split K only when the group has too few tiles to give every CTA work
-    // (narrow passes: aim at ~4 items per CTA; wide passes, whose split-K
-    // partials are costly to combine: only when tiles are fewer than CTAs/2).
-    int64_t want = npad < 128 ? (4 * grid_target + tiles_total - 1) / tiles_total
-                   : (2 * tiles_total >= grid_target ? 1
-                                                     : (grid_target + tiles_total - 1) / tiles_total);
-    if (want < 1) want = 1;
-    if (want > w->n_chunks) want = w->n_chunks;
+    const int64_t want = ks_group < w->n_chunks ? ks_group : w->n_chunks;
     p.cps = (int)ceil_div(w->n_chunks, want);
     p.ksplit = (int)ceil_div(w->n_chunks, p.cps);
     p.codes = w->codes;
@@ -1347,9 +1367,7 @@ int launch_tc_noalloc(ft_ctx* ctx, const ft_weight* w, int64_t seq, const float*
   batch.bf16 = 0;
   const int64_t grid_target = (int64_t)ctx->num_sms * (tmem_cols_for(npad) <= 256 ? 2 : 1);
   TqProblem& p = batch.p[0];
-  int64_t want = (4 * grid_target + w->n_tiles - 1) / w->n_tiles;
-  if (want < 1) want = 1;
-  if (want > w->n_chunks) want = w->n_chunks;
+  const int64_t want = pick_ksplit(w->n_tiles, grid_target, w->n_chunks, npad);
   p.cps = (int)ceil_div(w->n_chunks, want);
   p.ksplit = (int)ceil_div(w->n_chunks, p.cps);
   p.codes = w->codes;
