@@ -490,6 +490,75 @@ def run_gemm(args, torch, dist, device, local, sub_steps, cpu_seconds):
     return res
 
 
+def run_midm(args, torch, dist, device, local, sub_steps, cpu_seconds):
+    """Mid-size activations on the cfg2 weight shape W[11008, 4096]: device time per matmul
+    call at each M (int8 and fp32 activations), CUDA-graph replay of 12 calls over 12
+    weight copies (135 MB > L2).  Covers the shapes between the decode GEMV (<= 16
+    activation columns) and the wide tensor-core passes (>= 128 columns), where the
+    engine's K-split choice decides the time.  Not part of the default line."""
+    from ferrisres_b200 import gpu
+    ctx = gpu.get_context(local)
+    g = torch.Generator(device=device)
+    weights = []
+    for i in range(12):
+        g.manual_seed(100 + i)
+        u = torch.rand(G_N * G_K, generator=g, device=device)
+        codes = torch.where(u < 0.25, 0, torch.where(u < 0.75, 1, 2)).to(torch.int64)
+        scales = (torch.rand(G_N, generator=g, device=device) * 0.09 + 0.01).contiguous()
+        weights.append(_upload_u32(gpu, torch, ctx, _words_from_codes(torch, codes), G_N, G_K,
+                                   scales, device))
+        del u, codes
+    stream = torch.cuda.Stream(device=device)
+
+    def graph_us(fn, reps=8):
+        with torch.cuda.stream(stream):
+            for i in range(12):
+                fn(i)  # grows the workspaces before capture
+            stream.synchronize()
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=stream):
+                for i in range(12):
+                    fn(i)
+            for _ in range(2):
+                gr.replay()
+            stream.synchronize()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(reps):
+                gr.replay()
+            e1.record(stream)
+            stream.synchronize()
+        del gr
+        return e0.elapsed_time(e1) / (reps * 12) * 1e3
+
+    wbytes = G_N * G_K // 4
+    rows = []
+    gen = torch.Generator(device=device)
+    gen.manual_seed(3)
+    for kind, ms in (("int8", (8, 16, 17, 24, 32, 48, 64, 96, 128, 256, 512)),
+                     ("fp32", (2, 3, 4, 8, 12, 16, 32, 64))):
+        for m in ms:
+            y = torch.empty(m, G_N, device=device)
+            if kind == "int8":
+                q = torch.randint(-127, 128, (m, G_K), dtype=torch.int8, device=device,
+                                  generator=gen)
+                sx = torch.rand(m, device=device, generator=gen) * 0.01
+                us = graph_us(lambda i: weights[i % 12].matmul_i8(q, sx, out=y, stream=stream))
+            else:
+                x = torch.randn(m, G_K, device=device, generator=gen)
+                us = graph_us(lambda i: weights[i % 12].matmul_f32(x, out=y, stream=stream))
+            rows.append({"act": kind, "M": m, "us": round(us, 2),
+                         "weight_GBps": round(wbytes / us / 1e3, 1),
+                         "TOPS": round(2 * m * G_N * G_K / us / 1e6, 1)})
+    for w in weights:
+        w.close()
+    return {"metric": "mid-size M ternary matmul time", "unit": "us per call",
+            "config": {"workload": "W[11008, 4096], M = 2..512, 12 weight copies > L2, "
+                                   "CUDA-graph replay"},
+            "rows": rows}
+
+
 def gemm_cpu_baseline(seconds):
     """Oracle restatement of ternary_matmul_parallel (over tokens) on int8 codes as f32,
     on all host cores, over a bounded sample of the 512 tokens."""
@@ -1082,7 +1151,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="headline CPU baseline sample (s); each sub-config uses a third")
     ap.add_argument("--workload", choices=["all", "gemv", "gemm_cfg2", "sparse_cfg3", "moe_cfg4",
-                                           "kv_cfg5"], default="all",
+                                           "kv_cfg5", "midm"], default="all",
                     help="all = the headline GEMV line with every config as a sub-object")
     ap.add_argument("--ep-micro", type=int, default=0,
                     help="MoE micro-batches per step (0: 1)")
@@ -1119,8 +1188,8 @@ def main():
         res = r if res is None else {**res, "moe_cfg4": _compact(r)}
     if ws == 1:
         for name, fn in (("gemm_cfg2", run_gemm), ("sparse_cfg3", run_sparse),
-                         ("kv_cfg5", run_kv)):
-            if w in ("all", name):
+                         ("kv_cfg5", run_kv), ("midm", run_midm)):
+            if w == name or (w == "all" and name != "midm"):
                 torch.cuda.empty_cache()
                 r = fn(args, torch, dist, device, local, sub_steps, sub_cpu)
                 res = r if res is None else {**res, name: _compact(r)}

@@ -254,6 +254,19 @@ __device__ __forceinline__ void mma_i8_ts(uint32_t d_tmem, uint32_t a_tmem, uint
       : "memory");
 }
 
+// elect.sync over the full warp: true in the one elected lane; `leader` receives
+// the elected lane id in every lane.
+__device__ __forceinline__ bool elect_one(uint32_t& leader) {
+  uint32_t e, l;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync %1|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(e), "=r"(l));
+  leader = l;
+  return e != 0;
+}
+
 // Arrive (once) on `bar` when all previously issued tcgen05 async ops of this
 // thread have completed.
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
