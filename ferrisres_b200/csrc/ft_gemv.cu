@@ -524,8 +524,10 @@ __global__ void __launch_bounds__(kThreads, GvCfg<NB>::CTAS)
   // One token at a time: its x quads stay in registers between the absmax
   // and the digit split (K up to 4 * kRQ * kThreads in one load).
   constexpr int kRQ = 4;
-  for (int t = 0; t < seq; ++t) {
+  // (int8 activations: four tokens per pass of this loop, see below)
+  for (int t = 0; t < seq; t += (D == 1 ? 4 : 1)) {
     int cs[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    const int ntok = D == 1 ? (seq - t < 4 ? seq - t : 4) : 1;
     if (D != 1) {
       float4 xr[kRQ];
       float am = 0.0f;
@@ -666,27 +668,55 @@ __global__ void __launch_bounds__(kThreads, GvCfg<NB>::CTAS)
       for (int q = tid + kRQ * kThreads; q < nquad; q += kThreads)
         split(load_xs4(S, P.xkind, t, 4 * (int64_t)q), q);
     } else {
-      const int8_t* xq = static_cast<const int8_t*>(S.x) + (int64_t)t * S.ldx;
-      for (int q = tid; q < nquad; q += kThreads) {
-        const int64_t k = 4 * (int64_t)q;
-        uint32_t wv = 0u;
-        if (k + 3 < S.K && (reinterpret_cast<uintptr_t>(xq + k) & 3) == 0) {
-          wv = __ldg(reinterpret_cast<const uint32_t*>(xq + k));
-        } else {
+      // int8: tokens t..t+ntok-1 together, the 16 words of four tokens x four
+      // quads loaded before any is used (a token at a time, each quad's load
+      // latency was paid in turn: ~1 us per token at K = 4096)
+      const int8_t* xq[4];
+      bool fast = (S.K & 3) == 0 && (S.ldx & 3) == 0;
 #pragma unroll
-          for (int e = 0; e < 4; ++e)
-            if (k + e < S.K) wv |= (uint32_t)(xq[k + e] & 0xFF) << (8 * e);
-        }
-        cs[0] = __dp4a((int)wv, 0x01010101, cs[0]);
-        frag[frag_word(q, t, NB)] = wv;
+      for (int tt = 0; tt < 4; ++tt) {
+        xq[tt] = static_cast<const int8_t*>(S.x) + (int64_t)(t + (tt < ntok ? tt : 0)) * S.ldx;
+        fast = fast && (reinterpret_cast<uintptr_t>(xq[tt]) & 3) == 0;
+      }
+      for (int q0 = tid; q0 < nquad; q0 += 4 * kThreads) {
+        uint32_t wv[4][4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+          for (int tt = 0; tt < 4; ++tt) {
+            const int q = q0 + j * kThreads;
+            const int64_t k = 4 * (int64_t)q;
+            uint32_t w = 0u;
+            if (q < nquad && tt < ntok) {
+              if (fast) {
+                if (k < S.K) w = __ldg(reinterpret_cast<const uint32_t*>(xq[tt] + k));
+              } else {
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                  if (k + e < S.K) w |= (uint32_t)(xq[tt][k + e] & 0xFF) << (8 * e);
+              }
+            }
+            wv[j][tt] = w;
+          }
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+          for (int tt = 0; tt < 4; ++tt) {
+            const int q = q0 + j * kThreads;
+            if (q < nquad && tt < ntok) {
+              cs[tt] = __dp4a((int)wv[j][tt], 0x01010101, cs[tt]);
+              frag[frag_word(q, t + tt, NB)] = wv[j][tt];
+            }
+          }
       }
     }
     // column sums: one warp-wide integer add per column, one shared atomic
     // per warp and column
     // (2:4 weights need none: their A operand is w itself, not w + 1)
+    // (int8: column t + d is token t + d's single digit)
 #pragma unroll
     for (int d = 0; d < 8; ++d) {
-      if (d < D && !SP) {
+      if (d < (D == 1 ? ntok : D) && !SP) {
         const int v = __reduce_add_sync(0xffffffffu, cs[d]);
         if (lane == 0) atomicAdd(&colsum[t * D + d], v);
       }

@@ -55,7 +55,8 @@ def test_cfg1_baseline_seed0(gpu):
     assert_fp32_close(y, ref, condition(t, x, rows, cols, 1, rs), what="cfg1 seed 0")
 
 
-@pytest.mark.parametrize("rows,cols,seq", SHAPES)
+@pytest.mark.parametrize("rows,cols,seq", SHAPES + [
+    (300, 1000, 16), (257, 4096, 12), (64, 4098, 15), (130, 1024, 6), (512, 2052, 8)])
 def test_i8_bit_exact(gpu, rows, cols, seq):
     rng = np.random.default_rng(rows + cols * 3 + seq)
     t = ternary_matrix(rng, rows, cols, p_zero=0.5)
