@@ -151,14 +151,6 @@ struct Cursor {
     if (item < b.total_items) it = decode_item(b, item);
   }
   __device__ __forceinline__ bool valid(const TqBatch& b) const { return item < b.total_items; }
-  // returns true when the item changed
-  __device__ __forceinline__ bool advance(const TqBatch& b) {
-    if (++chunk < it.nch) return false;
-    chunk = 0;
-    item += gridDim.x;
-    if (item < b.total_items) it = decode_item(b, item);
-    return true;
-  }
   // chunks in the super-stage that starts at `chunk` (never spans two items)
   __device__ __forceinline__ int ss_len() const {
     return it.nch - chunk < kSK ? it.nch - chunk : kSK;
@@ -453,27 +445,48 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
     }
   } else if (warp == kWarpLoadA) {
     // ------------------------------------------- weight-block producer --
-    if (lane == 0) {
+    // One super-stage (its one or two 4 KB blocks) per step: the whole warp
+    // waits for the free slots, then an elect.sync lane issues the copies back
+    // to back.  A wait issued right after a copy costs the copy's issue on
+    // B200 (several hundred cycles with the activation copies in flight): a
+    // wait-copy-wait-copy loop supplied one block per ~600 cycles, slower
+    // than the MMAs consume them.
+    {
       Cursor cs;
       cs.start(b);
       uint32_t gb = 0;
       while (cs.valid(b) && ok) {
         const TqProblem& p = b.p[cs.it.prob];
-        const uint32_t sa = gb % kSA;
-        if (gb >= kSA)
-          ok = tc::mbar_wait(tc::smem_u32(&bar_sa_empty[sa]), ((gb / kSA) + 1) & 1, b.err, 17);
+        const int n = cs.ss_len();
+#pragma unroll
+        for (int j = 0; j < kSK; ++j)
+          if (j < n && gb + j >= (uint32_t)kSA)
+            ok = ok && tc::mbar_wait(tc::smem_u32(&bar_sa_empty[(gb + j) % kSA]),
+                                     (((gb + j) / kSA) + 1) & 1, b.err, 17);
+        ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
-        const uint32_t bar = tc::smem_u32(&bar_sa_full[sa]);
-        tc::mbar_arrive_expect_tx(bar, kBlk);
-        const uint8_t* src = p.codes + (cs.it.tile * p.n_chunks + cs.it.c0 + cs.chunk) * kBlk;
-        tc::bulk_g2s(tc::smem_u32(smem_a + sa * kBlockBytes), src, kBlk, bar);
-        ++gb;
-        cs.advance(b);
+        uint32_t leader;
+        if (tc::elect_one(leader)) {
+          const uint8_t* src = p.codes + (cs.it.tile * p.n_chunks + cs.it.c0 + cs.chunk) * kBlk;
+#pragma unroll
+          for (int j = 0; j < kSK; ++j) {
+            if (j < n) {
+              const uint32_t sa = (gb + j) % kSA;
+              const uint32_t bar = tc::smem_u32(&bar_sa_full[sa]);
+              tc::mbar_arrive_expect_tx(bar, kBlk);
+              tc::bulk_g2s(tc::smem_u32(smem_a + sa * kBlockBytes), src + j * kBlk, kBlk, bar);
+            }
+          }
+        }
+        __syncwarp();
+        gb += (uint32_t)n;
+        cs.advance_ss(b);
       }
     }
   } else if (warp == kWarpLoadB) {
     // ------------------------------------------- B super-stage producer --
-    if (lane == 0) {
+    // (same form as the weight producer)
+    {
       tc::pdl_wait();  // B is written by the preceding prep kernel
       Cursor cs;
       cs.start(b);
@@ -484,13 +497,18 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
         const uint32_t sb = gs % kSBS;
         if (gs >= (uint32_t)kSBS)
           ok = tc::mbar_wait(tc::smem_u32(&bar_sb_empty[sb]), ((gs / kSBS) + 1) & 1, b.err, 12);
+        ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
-        const uint32_t bar = tc::smem_u32(&bar_sb_full[sb]);
-        tc::mbar_arrive_expect_tx(bar, n * kBStage);
-        // the super-stage's chunks are contiguous in the prepared operand
-        const int8_t* src =
-            p.bmat + ((int64_t)cs.it.pass * p.n_chunks + cs.it.c0 + cs.chunk) * kBStage;
-        tc::bulk_g2s(tc::smem_u32(smem_b + sb * kBSuper), src, n * kBStage, bar);
+        uint32_t leader;
+        if (tc::elect_one(leader)) {
+          const uint32_t bar = tc::smem_u32(&bar_sb_full[sb]);
+          tc::mbar_arrive_expect_tx(bar, n * kBStage);
+          // the super-stage's chunks are contiguous in the prepared operand
+          const int8_t* src =
+              p.bmat + ((int64_t)cs.it.pass * p.n_chunks + cs.it.c0 + cs.chunk) * kBStage;
+          tc::bulk_g2s(tc::smem_u32(smem_b + sb * kBSuper), src, n * kBStage, bar);
+        }
+        __syncwarp();
         ++gs;
         cs.advance_ss(b);
       }
