@@ -57,17 +57,8 @@ namespace {
 #ifndef FT_TC_BBUDGET
 #define FT_TC_BBUDGET 98304
 #endif
-constexpr int kSA = FT_TC_SA;  // smem ring of 4 KB weight blocks
 constexpr int kSK = 2;   // K chunks per super-stage: one barrier wait / commit per 8 KB of weights
 constexpr int kWarpLoadA = 4, kWarpLoadB = 5, kWarpMma = 6;  // warps 0-3 convert, 7-10 epilogue
-#ifndef FT_TC_CONV_GROUPS
-#define FT_TC_CONV_GROUPS 2
-#endif
-// Converter groups of 4 warps (one per TMEM sub-partition): group k converts
-// super-stages k, k + G, k + 2G, ...  A group's pass over a super-stage is a
-// long chain of waits and short latencies, so several groups work at once.
-constexpr int kConvGroups = FT_TC_CONV_GROUPS;
-constexpr int kThreads = (11 + 4 * (kConvGroups - 1)) * 32;  // extra groups are warps 11..
 constexpr int kMaxProblems = 64;
 
 struct TqProblem {
@@ -188,9 +179,37 @@ __host__ __device__ constexpr int b_ss_raw(int npad) {
 __host__ __device__ constexpr int b_ss_for(int npad) {
   return b_ss_raw(npad) < 2 ? 2 : b_ss_raw(npad) > 8 ? 8 : b_ss_raw(npad);
 }
-__host__ __device__ constexpr size_t smem_bytes_for(int npad) {
-  return (size_t)kSA * 4096 + (size_t)b_ss_for(npad) * kSK * npad * 128;
-}
+// Per kernel instance: converter groups of 4 warps (one per TMEM
+// sub-partition); group k converts super-stages k, k + G, k + 2G, ...  A
+// group's pass over a super-stage is a long chain of waits and short
+// latencies, so several groups work at once: three for the 2:4 kernel with
+// 128-column passes (its thread-per-row expansion is the slowest role, 70 ->
+// 61 us at cfg3 M=64), two otherwise.  A TMEM A stage is reused every SS
+// super-stages, a weight slot every SA / kSK and a B stage every SBS: all
+// three periods are multiples of G, so each stage and slot always returns to
+// the same group, which waited on its previous phase.  (Parity waits tell
+// only consecutive phases apart; with a stage shared between groups one could
+// pass a wait a phase early: a 3-group build with 4 A stages did, and a
+// 2-group build with 3 B stages relied on copies landing in issue order.)
+template <int NPAD, bool kSparse>
+struct TqCfg {
+  static constexpr int G = (kSparse && NPAD == 128) ? 3 : 2;
+  static constexpr int THREADS = (11 + 4 * (G - 1)) * 32;  // extra groups are warps 11..
+  static constexpr int SA = FT_TC_SA / (kSK * G) * (kSK * G);  // ring of 4 KB weight blocks
+  static constexpr int SS = a_ss_for(NPAD) / G * G;
+  // B stages: b_ss_for's count rounded up to a multiple of G when that stays
+  // within its budget (one CTA per SM: ~200 KB in all), else down
+  static constexpr int SBS_UP = (b_ss_for(NPAD) + G - 1) / G * G;
+  static constexpr int SBS =
+      (tmem_cols_for(NPAD) > 256 && (size_t)SA * 4096 + (size_t)SBS_UP * kSK * NPAD * 128 <= 200 * 1024)
+          ? SBS_UP
+          : b_ss_for(NPAD) / G * G;
+  static constexpr size_t SMEM = (size_t)SA * 4096 + (size_t)SBS * kSK * NPAD * 128;
+  static_assert(SS >= G && SA >= kSK * G && SBS >= G, "each converter group needs its own stages");
+  static_assert(SS % G == 0 && (SA / kSK) % G == 0 && SBS % G == 0,
+                "stage periods must be multiples of G");
+  static_assert(SMEM <= 220 * 1024, "shared memory");
+};
 
 __device__ __forceinline__ void named_sync_epilogue() {
   asm volatile("bar.sync 1, 128;" ::: "memory");
@@ -261,7 +280,10 @@ __device__ __forceinline__ void epilogue_group(const TqProblem& p, int digits, b
 }
 
 template <int NPAD, bool kSparse>
-__global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_constant__ TqBatch b) {
+__global__ void __launch_bounds__(TqCfg<NPAD, kSparse>::THREADS, 1)
+    tq_grouped_kernel(const __grid_constant__ TqBatch b) {
+  using Cfg = TqCfg<NPAD, kSparse>;
+  constexpr int kSA = Cfg::SA, kConvGroups = Cfg::G;
   // weight block bytes in HBM and in the smem ring (2:4 blocks use the first 3072 bytes)
   constexpr uint32_t kBlk = kSparse ? kSparseBlockBytes : kBlockBytes;
   // 2:4 group (metadata nibble << 2 | the two sign bits) -> four unsigned
@@ -271,8 +293,8 @@ __global__ void __launch_bounds__(kThreads, 1) tq_grouped_kernel(const __grid_co
   extern __shared__ __align__(1024) uint8_t smem_dyn[];
   constexpr uint32_t kBStage = NPAD * 128;       // B bytes per chunk
   constexpr uint32_t kBSuper = kSK * kBStage;    // B bytes per super-stage
-  constexpr int kSBS = b_ss_for(NPAD);
-  constexpr int kSS = a_ss_for(NPAD);
+  constexpr int kSBS = Cfg::SBS;
+  constexpr int kSS = Cfg::SS;
   uint8_t* const smem_a = smem_dyn;
   uint8_t* const smem_b = smem_dyn + kSA * kBlockBytes;
   __shared__ __align__(8) uint64_t bar_sa_full[kSA];    // weight block landed (tx)
@@ -1069,7 +1091,7 @@ int pick_npad(int64_t ncols) {
 
 template <int NPAD, bool kSparse = false>
 int launch_grouped_t(const TqBatch& batch, int64_t grid, cudaStream_t s) {
-  const size_t smem = smem_bytes_for(NPAD);
+  const size_t smem = TqCfg<NPAD, kSparse>::SMEM;
   static bool attr_set = false;  // per template instance
   if (!attr_set) {
     FT_CUDA(cudaFuncSetAttribute(tq_grouped_kernel<NPAD, kSparse>,
@@ -1078,7 +1100,7 @@ int launch_grouped_t(const TqBatch& batch, int64_t grid, cudaStream_t s) {
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid);
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(TqCfg<NPAD, kSparse>::THREADS);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
