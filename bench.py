@@ -134,7 +134,13 @@ class ClockSampler:
 
 class Timer:
     """Device time of work issued on `stream`, max over ranks (CUDA events,
-    a barrier and a synchronize on both sides)."""
+    a barrier and a synchronize on both sides).  A ~100 us spin kernel runs on
+    the stream just before the start event, outside the timed region: the GPU
+    is then still busy while the host submits the first timed launch, so the
+    host's submission latency (tens of us for a graph launch, 4% of a 20-step
+    GEMV region) is not counted as device time."""
+
+    LEAD_IN_CYCLES = 200_000
 
     def __init__(self, torch, dist, stream, device, ws):
         self.torch, self.dist, self.stream, self.device, self.ws = torch, dist, stream, device, ws
@@ -147,6 +153,8 @@ class Timer:
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with torch.cuda.stream(self.stream):
+            if hasattr(torch.cuda, "_sleep"):
+                torch.cuda._sleep(self.LEAD_IN_CYCLES)
             e0.record(self.stream)
             fn()
             e1.record(self.stream)

@@ -155,6 +155,94 @@ __global__ void quantize_i8_kernel(const void* __restrict__ x, bool bf16, int64_
   if (threadIdx.x == 0) sx[s] = __fdiv_rn(amax, 127.0f);
 }
 
+// Same arithmetic, 16-byte loads: a row of cols % (16 / element size) == 0 on
+// 16-byte aligned rows.  The first kKeep loads of a thread stay in registers
+// between the absmax and the rounding pass (all of them up to 8192 bf16 /
+// 4096 f32 columns), later ones are read again.  Each thread then stores its
+// codes as one 8-byte (bf16) or 4-byte (f32) word per load.
+template <bool kBf16>
+__global__ void quantize_i8_vec_kernel(const void* __restrict__ x, int64_t cols,
+                                       int8_t* __restrict__ q, float* __restrict__ sx) {
+  constexpr int V = kBf16 ? 8 : 4, kKeep = 4;
+  const int64_t s = blockIdx.x;
+  const uint4* xv =
+      reinterpret_cast<const uint4*>(static_cast<const char*>(x) + s * cols * (kBf16 ? 2 : 4));
+  const int64_t nv = cols / V;
+  auto unpack = [](const uint4 u, float (&f)[V]) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+    if (kBf16) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        f[2 * e] = __uint_as_float(w[e] << 16);
+        f[2 * e + 1] = __uint_as_float(w[e] & 0xffff0000u);
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < V; ++e) f[e] = __uint_as_float(w[e]);
+    }
+  };
+  uint4 keep[kKeep];
+  float amax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < kKeep; ++i) {
+    const int64_t j = threadIdx.x + (int64_t)i * blockDim.x;
+    keep[i] = j < nv ? __ldg(xv + j) : make_uint4(0u, 0u, 0u, 0u);
+  }
+#pragma unroll
+  for (int i = 0; i < kKeep; ++i) {
+    float f[V];
+    unpack(keep[i], f);
+#pragma unroll
+    for (int e = 0; e < V; ++e) amax = fmaxf(amax, fabsf(f[e]));
+  }
+  for (int64_t j = threadIdx.x + (int64_t)kKeep * blockDim.x; j < nv; j += blockDim.x) {
+    float f[V];
+    unpack(__ldg(xv + j), f);
+#pragma unroll
+    for (int e = 0; e < V; ++e) amax = fmaxf(amax, fabsf(f[e]));
+  }
+  __shared__ float red[32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  amax = red[0];
+  const bool zero = amax == 0.0f;
+  const float inv = zero ? 0.0f : 127.0f / amax;  // IEEE division (no fast-math in this build)
+  // codes of one load's elements (all zero for an all-zero row, as above)
+  auto store = [&](const uint4 u, int8_t* qr, int64_t j) {
+    float f[V];
+    unpack(u, f);
+    uint32_t w[2] = {0u, 0u};
+#pragma unroll
+    for (int g = 0; g < V / 4; ++g)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float r = roundf(__fmul_rn(f[4 * g + e], inv));
+        r = fminf(fmaxf(r, -127.0f), 127.0f);
+        w[g] |= zero ? 0u : (uint32_t)((int)r & 0xFF) << (8 * e);
+      }
+    if (kBf16) reinterpret_cast<uint2*>(qr)[j] = make_uint2(w[0], w[1]);
+    else reinterpret_cast<uint32_t*>(qr)[j] = w[0];
+  };
+  int8_t* qr = q + s * cols;
+#pragma unroll
+  for (int i = 0; i < kKeep; ++i) {
+    const int64_t j = threadIdx.x + (int64_t)i * blockDim.x;
+    if (j < nv) store(keep[i], qr, j);
+  }
+  for (int64_t j = threadIdx.x + (int64_t)kKeep * blockDim.x; j < nv; j += blockDim.x)
+    store(__ldg(xv + j), qr, j);
+  if (threadIdx.x == 0) sx[s] = zero ? 1.0f : __fdiv_rn(amax, 127.0f);
+}
+
 // ------------------------------------------------------------ WGSL op ------
 // One warp per (token, row) over the raw u32 layout; lanes take words
 // round-robin, then a shuffle reduction; result * scales[row].
@@ -325,7 +413,14 @@ int launch_repack_sparse_wgsl(const uint32_t* words, int64_t rows, int64_t cols,
 int launch_quantize_i8(const void* x, bool bf16, int64_t seq, int64_t cols, int8_t* q, float* sx,
                        cudaStream_t s) {
   if (seq == 0) return FT_OK;
-  quantize_i8_kernel<<<(unsigned)seq, 256, 0, s>>>(x, bf16, cols, q, sx);
+  const int V = bf16 ? 8 : 4;
+  if (cols % V == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(q) & (bf16 ? 7 : 3)) == 0 && (cols * (bf16 ? 2 : 4)) % 16 == 0) {
+    if (bf16) quantize_i8_vec_kernel<true><<<(unsigned)seq, 256, 0, s>>>(x, cols, q, sx);
+    else quantize_i8_vec_kernel<false><<<(unsigned)seq, 256, 0, s>>>(x, cols, q, sx);
+  } else {
+    quantize_i8_kernel<<<(unsigned)seq, 256, 0, s>>>(x, bf16, cols, q, sx);
+  }
   FT_LAUNCH_CHECK();
   return FT_OK;
 }

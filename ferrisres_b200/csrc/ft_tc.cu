@@ -1036,6 +1036,83 @@ __global__ void __launch_bounds__(kPrepThreads, W == 1 ? 3 : 1) prep_b_kernel(co
   if (W == 1) tc::pdl_launch_dependents();
 }
 
+// int8 activations (D = 1): the operand is a re-layout of the codes.  A block
+// takes 8 consecutive token slots of one (source, pass); lane (r, q) of warp w
+// moves the 16 bytes of token r at K groups 4 (w + 8 i) + q, so every warp
+// store writes four whole 128-byte core-matrix row groups (8 tokens x 16 bytes)
+// and every load reads 64 contiguous bytes of a token row.  (The general
+// kernel's 8-byte stores at the K-group stride took 6.9 us for cfg2's 2 MB.)
+__global__ void __launch_bounds__(kPrepThreads) prep_i8_kernel(const __grid_constant__ PrepBatch pb) {
+  tc::pdl_launch_dependents();
+  tc::pdl_wait();  // the previous matmul may still be reading bmat
+  __shared__ int red[kPrepWarps][8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = lane & 7, q = lane >> 3;
+  const int64_t slot0 = (int64_t)blockIdx.x * 8;
+  if (slot0 >= pb.block_begin[pb.nsrc]) return;  // uniform over the block
+  int lo = 0, hi = pb.nsrc - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (pb.block_begin[mid] <= slot0) lo = mid;
+    else hi = mid - 1;
+  }
+  const PrepSource& src = pb.s[lo];
+  const int64_t local = slot0 - pb.block_begin[lo];
+  const int64_t pass = local / pb.tok_per_pass;
+  const int lt = (int)(local % pb.tok_per_pass) + r;
+  const int64_t t = pass * pb.tok_per_pass + lt;
+  const bool live = t < src.seq;
+  const int64_t K = src.K, groups = src.n_chunks * 8;  // 16-byte K groups
+  const int8_t* row = static_cast<const int8_t*>(src.x) + (live ? t : 0) * src.ldx;
+  const bool fast = (K & 15) == 0 && (src.ldx & 15) == 0 &&
+                    (reinterpret_cast<uintptr_t>(src.x) & 15) == 0;
+  int cs = 0;
+  // eight K groups per thread at a time, every load issued before any store
+  constexpr int kStep = 4 * kPrepWarps, kU = 8;
+  for (int64_t kb = 4 * warp + q; kb < groups; kb += kU * kStep) {
+    uint4 v[kU];
+#pragma unroll
+    for (int i = 0; i < kU; ++i) {
+      const int64_t k0 = 16 * (kb + i * kStep);
+      v[i] = make_uint4(0u, 0u, 0u, 0u);
+      if (live && k0 < K) {
+        if (fast) {
+          v[i] = __ldg(reinterpret_cast<const uint4*>(row + k0));
+        } else {
+          uint32_t w[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            if (k0 + e < K) w[e >> 2] |= (uint32_t)(row[k0 + e] & 0xFF) << (8 * (e & 3));
+          v[i] = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kU; ++i) {
+      const int64_t kg = kb + i * kStep, k0 = 16 * kg;
+      if (kg < groups) {
+        cs = __dp4a((int)v[i].x, 0x01010101, cs);
+        cs = __dp4a((int)v[i].y, 0x01010101, cs);
+        cs = __dp4a((int)v[i].z, 0x01010101, cs);
+        cs = __dp4a((int)v[i].w, 0x01010101, cs);
+        *reinterpret_cast<uint4*>(src.bmat + b_offset(pass, k0 >> 7, lt, (int)(k0 & 127),
+                                                      pb.npad, src.n_chunks)) = v[i];
+      }
+    }
+  }
+  // column sums of the 8 tokens: lanes r, r + 8, r + 16, r + 24 of every warp
+  cs += __shfl_xor_sync(0xffffffffu, cs, 8);
+  cs += __shfl_xor_sync(0xffffffffu, cs, 16);
+  if (q == 0) red[warp][r] = cs;
+  __syncthreads();
+  if (threadIdx.x < 8) {  // lane r = threadIdx.x: lt is token r's slot
+    int v = 0;
+#pragma unroll
+    for (int w = 0; w < kPrepWarps; ++w) v += red[w][threadIdx.x];
+    src.colsum[pass * pb.npad + lt] = v;
+  }
+}
+
 // slots -> warps per slot: many slots use one warp each, few slots (long
 // rows, little parallelism) up to a block each
 int prep_warps(int64_t slots) {
@@ -1324,7 +1401,10 @@ int launch_tc_grouped(ft_ctx* ctx, int n, const ft_weight* const* ws, int64_t se
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (D == 1) FT_CUDA(launch_prep<1>(pb, blocks, cfg));
+    if (D == 1) {  // int8 codes: tok_per_pass = npad, a multiple of 8 slots per (source, pass)
+      cfg.gridDim = dim3((unsigned)(blocks / 8));
+      FT_CUDA(cudaLaunchKernelEx(&cfg, prep_i8_kernel, pb));
+    }
     else if (D == 4) FT_CUDA(launch_prep<4>(pb, blocks, cfg));
     else FT_CUDA(launch_prep<8>(pb, blocks, cfg));
     FT_LAUNCH_CHECK();
