@@ -68,6 +68,12 @@ namespace {
 #ifndef FT_GV_DEPTH2
 #define FT_GV_DEPTH2 8
 #endif
+// int8 activations of more tokens go to the tensor-core engine: at 9-16
+// tokens it measured 8.7-8.9 us per call on W[5632, 2048] and 13.5-13.7 us on
+// W[11008, 4096] against 10.8-13.2 and 15.2-18.1 us here
+#ifndef FT_GV_I8_MAX_TOKENS
+#define FT_GV_I8_MAX_TOKENS 8
+#endif
 #ifndef FT_GV_GRID_SMALL
 #define FT_GV_GRID_SMALL 1
 #endif
@@ -954,6 +960,7 @@ bool gemv_fits(const ft_weight* w, int64_t seq, int xkind, int digits) {
   const int64_t ncols = seq * gemv_digits(xkind, digits);
   // int32 bound: the k-step-3 accumulator grows by <= 128 * 128 * 32 per chunk
   if ((w->format != 0 && w->format != 1) || ncols > 16 || w->n_chunks > 2048) return false;
+  if (xkind == 2 && ncols > FT_GV_I8_MAX_TOKENS) return false;
   const int nb = ncols > 8 ? 2 : 1;
   return smem_for(nb, w->format == 1, false, w->n_chunks) <= (size_t)kGemvMaxSmem &&
          smem_for(nb, w->format == 1, true, w->n_chunks) <= (size_t)kGemvMaxSmem;

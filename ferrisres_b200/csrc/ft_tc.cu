@@ -1140,16 +1140,22 @@ cudaError_t launch_prep(const PrepBatch& pb, int64_t slots, cudaLaunchConfig_t c
 // near-ties).  The constants are measured on B200 with W[11008, 4096]: a CTA
 // takes ~400 cycles per chunk at npad <= 64 and ~640 at npad 128 (MMA-bound),
 // and the GPU completes ~100 int32 atomics per cycle.  With 86 tiles this
-// picks no split: split 4-14 ways the same launch ran 1.6-2.5x slower.
+// picks no split: split 4-14 ways the same launch ran 1.6-2.5x slower.  A
+// split must also beat the unsplit model by FT_TC_SPLIT_GAIN: the 2-way split
+// the model chose at 16 columns (86 or 44 tiles) measured slower than none.
+#ifndef FT_TC_SPLIT_GAIN
+#define FT_TC_SPLIT_GAIN 0.7
+#endif
 int pick_ksplit(int64_t tiles, int64_t grid_target, int64_t chunks, int npad) {
   const double chunk_cycles = npad >= 128 ? 640.0 : 400.0, atomics_per_cycle = 100.0;
-  double best = 0.0;
+  double best = 0.0, unsplit = 0.0;
   int best_ks = 1;
   for (int ks = 1; ks <= 64 && ks <= chunks; ++ks) {
     const double t = (double)ceil_div(tiles * ks, grid_target) *
                          (double)ceil_div(chunks, (int64_t)ks) * chunk_cycles +
                      (ks > 1 ? (double)(tiles * ks) * 128.0 * npad / atomics_per_cycle : 0.0);
-    if (ks == 1 || t < 0.97 * best) {
+    if (ks == 1) unsplit = t;
+    if (ks == 1 || (t < 0.97 * best && t < FT_TC_SPLIT_GAIN * unsplit)) {
       best = t;
       best_ks = ks;
     }
